@@ -1,0 +1,329 @@
+"""Benchmark of the quantized attention hot path.
+
+Workload (one "step"): SageAttention forward through the public API on
+B=2, H=24, S=4096, D=128 bf16 inputs, K carrying a per-channel offset
+~N(0, 4): K mean-smoothing, INT8 Q (per 128 rows) / K (per 64 rows), e4m3 P
+and per-channel e4m3 V -- the quantisation prologue kernels plus the tcgen05
+attention kernel.  Metric: attention TOPS = 4*B*H*S^2*D ops per step / time.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+With N > 1 (torchrun, one process per GPU) every rank runs its own replica of
+the workload (attention does not shard; no collective on the data path);
+value = N * ops / max-over-ranks time.  ``--impl reference`` times the CPU
+restatement of the reference algorithm (oracle) on a bounded sample on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+B, H, S, D = 2, 24, 4096, 128
+OPS_PER_STEP = 4 * B * H * S * S * D  # 412.3 G ops (2 for QK^T + 2 for PV per MAC pair)
+METRIC = "SageAttn TOPS (B2 H24 S4096 D128, INT8 QK + FP8 PV)"
+UNIT = "TOPS"
+# Measured DRAM traffic of one attention launch at this workload, from
+# profiles/attn_fwd_config2.md (ncu dram__bytes_read.sum + dram__bytes_write.sum); None until captured.
+ATTN_TRAFFIC_BYTES = None
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"bf16_tflops": d["bf16_tflops"], "hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_inputs(seed: int, device=None):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, H, S, D, generator=g, dtype=torch.float32).to(torch.bfloat16)
+    k = (torch.randn(B, H, S, D, generator=g) + 2.0 * torch.randn(D, generator=g)).to(torch.bfloat16)
+    v = torch.randn(B, H, S, D, generator=g, dtype=torch.float32).to(torch.bfloat16)
+    if device is not None:
+        q, k, v = q.to(device), k.to(device), v.to(device)
+    return q, k, v
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def cpu_baseline_sample(seconds_budget: float = 20.0) -> dict:
+    """Time the CPU restatement of the reference algorithm on a bounded sample."""
+    from oracle import attention as OA
+
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    heads, done_ops, t_total = 0, 0, 0.0
+    while t_total < seconds_budget and heads < B * H:
+        q = torch.randn(1, S, D, generator=g).to(torch.bfloat16)
+        k = (torch.randn(1, S, D, generator=g) + 2.0 * torch.randn(D, generator=g)).to(torch.bfloat16)
+        v = torch.randn(1, S, D, generator=g).to(torch.bfloat16)
+        t0 = time.perf_counter()
+        OA.attention_forward(q, k, v, sm_scale=1 / math.sqrt(D), qk_quant="int8", granularity="per_block",
+                             pv_quant="fp8_channel")
+        t_total += time.perf_counter() - t0
+        heads += 1
+        done_ops += 4 * S * S * D
+    return {"value": done_ops / t_total / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{heads} of {B * H} (b,h) heads at S={S}, oracle.attention.attention_forward "
+                      f"(torch CPU, {threads} threads), {t_total:.1f} s"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return 0
+    per_step = []
+    cb = None
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline_sample(seconds_budget=max(2.0, 60.0 / max(1, args.warmup + args.steps)))
+        if i >= args.warmup:
+            per_step.append(r["value"])
+        cb = r
+    val = statistics.mean(per_step) if per_step else cb["value"]
+    line = {
+        "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": OPS_PER_STEP / (val * 1e12) * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp8",
+        "data": "synthetic",
+        "config": {"workload": "config2_quantized_attention", "B": B, "H": H, "S": S, "D": D,
+                   "qk": "int8 per-block", "pv": "fp8 per-channel V, static P"},
+        "cpu_baseline": {**cb, "value": val},
+        "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, world, rank, local):
+    from futudiffu_b200 import _lib as L
+    from futudiffu_b200 import check_status
+    from futudiffu_b200 import sage_attention as SA
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    SA.configure_sage(smooth_k=True, qk_quant="int8", pv_quant="fp8", qk_granularity="per_block")
+    q, k, v = make_inputs(1234 + rank, dev)
+    BH = B * H
+    qf, kf, vf = (t.reshape(BH, S, D) for t in (q, k, v))
+    stream = torch.cuda.current_stream(dev)
+    sm = 1.0 / math.sqrt(D)
+
+    def step(ev_pair=None):
+        qz = SA.quantize_qkv(qf, kf, vf, sm, smooth_k=True, qk_quant="int8", granularity="per_block",
+                             pv_quant="fp8")
+        out = torch.empty_like(qf)
+        if ev_pair is not None:
+            ev_pair[0].record(stream)
+        L.call("fd_sage_attn_fwd", L.ptr(qz["q_codes"]), L.ptr(qz["q_desc"]), L.ptr(qz["k_codes"]),
+               L.ptr(qz["k_desc"]), L.ptr(qz["v_codes"]), L.ptr(qz["v_desc"]), None, 0, L.ptr(out), None,
+               BH, S, L.QK_INT8, L.GRAN_BLOCK, L.GRAN_BLOCK, L.PV_FP8, L.stream_ptr(dev))
+        if ev_pair is not None:
+            ev_pair[1].record(stream)
+        return out
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    check_status()
+
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else local) as clocks:
+        start.record(stream)
+        for i in range(args.steps):
+            step(kev[i])
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_local = start.elapsed_time(end) / args.steps
+    kernel_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+    ms = max_over_ranks(ms_local, world, dev)
+    kernel_ms = max_over_ranks(kernel_ms, world, dev)
+    value = world * OPS_PER_STEP / (ms * 1e-3) / 1e12
+    check_status()
+
+    # ---------------- end to end: pinned host inputs -> device -> public API -> host output
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    hout = torch.empty(B, H, S, D, dtype=torch.bfloat16).pin_memory()
+    h2d = 3 * q.numel() * q.element_size()
+    d2h = hout.numel() * hout.element_size()
+    e2e_steps = max(3, min(args.steps, 20))
+
+    def e2e_step():
+        dq, dk, dv = (t.to(dev, non_blocking=True) for t in (hq, hk, hv))
+        o = SA.sage_attn_forward(dq, dk, dv)
+        hout.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world, dev)
+    e2e_val = world * OPS_PER_STEP / (e2e_ms * 1e-3) / 1e12
+    check_status()
+
+    if rank == 0:
+        pk = peaks()
+        peak_tops = 2.0 * pk["bf16_tflops"]
+        achieved = OPS_PER_STEP / (kernel_ms * 1e-3) / 1e12
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8/fp8", "data": "synthetic",
+            "config": {"workload": "config2_quantized_attention", "B": B, "H": H, "S": S, "D": D,
+                       "qk": "int8 per-block (Q 128 rows, K 64 rows), K mean-smoothed",
+                       "pv": "fp8 e4m3 P (static scale), fp8 e4m3 V (per-channel)",
+                       "step": "quantisation prologue + tcgen05 attention",
+                       "l2": "inputs 151 MB bf16 > 126 MB L2; no explicit flush",
+                       "parallelism": f"replicas x{world}"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tops, "unit": "TOP/s",
+                         "frac": achieved / peak_tops, "traffic": ATTN_TRAFFIC_BYTES,
+                         "kernel": "attn_fwd_kernel<int8, block, fp8>",
+                         "kernel_ms": kernel_ms,
+                         "peak_source": f"2 x {pk['source']} bf16 dense ({pk['bf16_tflops']} TF/s): "
+                                        "int8/fp8 dense rate is twice bf16"},
+            "cpu_baseline": cpu_baseline_sample(15.0) if world == 1 else None,
+            "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms, "api": "futudiffu_b200.sage_attention.sage_attn_forward"},
+            "gpu_launches": 3 * args.steps,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    args = ap.parse_args(argv)
+    args.warmup = max(3, args.warmup)
+    world, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            return run_reference(args, world, rank)
+        return run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,543 @@
+// Quantized attention forward (A5/A6) on tcgen05.
+//
+// Reference semantics: _sage_attn_fwd_int8qk_bf16pv_masked_lse and siblings,
+// src/futudiffu/sage_kernels.py:1379-1477 (production), :592-798 (int8
+// unmasked), :107-315 (fp8 QK), :1037-1168 (fp8 PV).  Per query row:
+//   L[n]  = S[n] * q_desc * k_desc[n]            (log2 domain, sm_scale folded)
+//   online softmax over KV tiles: m, l, O with exp2, LSE = m + log2(l),
+//   out   = O / l.
+//
+// CTA = one 128-row Q tile of one (b, h); 6 warps:
+//   warps 0-3  softmax: thread = query row (TMEM lane).  Reads its S row
+//              from TMEM, scales, row max, exp2, row sum, writes P to shared
+//              memory; rescales its O row in TMEM when the running max moves.
+//   warp 4     TMA producer: Q once, then K (+ per-token K scales) and V
+//              tiles of 128 keys into a 2-stage ring.
+//   warp 5     MMA issuer: S = Q K^T (kind::i8 -> s32, or kind::f8f6f4 -> f32)
+//              and O += P V (kind::f8f6f4 e4m3, or kind::f16 bf16).
+// TMEM: S at columns [0,128), O at [128,256).  Two CTAs fit on one SM
+// (fp8 PV), so one CTA's softmax overlaps the other's MMAs; inside a CTA the
+// next S = Q K^T is issued as soon as the softmax has pulled S into registers.
+//
+// Running-max threshold: O is rescaled only when a row max grows by more
+// than TAU = 8 (log2 units) over the reference max used for exp2, so P <= 2^8.
+// With e4m3 P this is encoded as P8 = e4m3(p * 448 / 256) and undone in the
+// epilogue; bf16 P is stored as is.  Results equal the reference online
+// softmax up to fp32 rounding (exp2 is shift-exact in bf16 / e4m3 up to
+// rounding of the argument).
+#include "fd_common.cuh"
+#include "fd_host.h"
+
+namespace fd {
+namespace attn {
+
+constexpr int BQ = 128;   // query rows per CTA
+constexpr int BKV = 128;  // keys per KV tile
+constexpr int HD = 128;
+constexpr int KST = 2;    // K/V pipeline stages
+constexpr int NUM_THREADS = 192;
+constexpr float TAU = 8.0f;
+constexpr float P8_SCALE = 448.0f / 256.0f;
+
+template <int PV>
+struct Smem {
+  static constexpr uint32_t Q_BYTES = BQ * HD;                           // int8/e4m3 codes
+  static constexpr uint32_t K_BYTES = BKV * HD;
+  static constexpr uint32_t V_BYTES = BKV * HD * (PV == FD_PV_FP8 ? 1 : 2);
+  static constexpr uint32_t P_BYTES = BQ * BKV * (PV == FD_PV_FP8 ? 1 : 2);
+  static constexpr uint32_t OFF_Q = 0;
+  static constexpr uint32_t OFF_K = OFF_Q + Q_BYTES;
+  static constexpr uint32_t OFF_V = OFF_K + KST * K_BYTES;
+  static constexpr uint32_t OFF_P = OFF_V + KST * V_BYTES;
+  static constexpr uint32_t OFF_KD = OFF_P + P_BYTES;                    // KST x 128 f32
+  static constexpr uint32_t OFF_VD = OFF_KD + KST * 512;                 // 128 f32
+  static constexpr uint32_t OFF_BAR = OFF_VD + 512;
+  static constexpr uint32_t TOTAL = OFF_BAR + 256 + 1024;               // + barriers, align slack
+};
+
+struct Params {
+  const float* q_desc;
+  const float* k_desc;
+  const float* v_desc;
+  const uint8_t* mask;
+  int64_t mask_bh_stride;
+  __nv_bfloat16* out;
+  float* lse;
+  int N;
+  int n_kv_tiles;
+  int nkb64;       // ceil(N/64): mask columns
+  int q_gran;
+  int64_t q_desc_stride;
+  int64_t k_desc_stride;
+};
+
+FD_DEV void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+FD_DEV bool tile_valid(const Params& p, int bh, int qb, int j) {
+  if (!p.mask) return true;
+  const uint8_t* m = p.mask + (int64_t)bh * p.mask_bh_stride + (int64_t)qb * p.nkb64;
+  const uint8_t a = m[2 * j];
+  const uint8_t b = (2 * j + 1 < p.nkb64) ? m[2 * j + 1] : 0;
+  return (a | b) != 0;
+}
+
+FD_DEV void drain_wait(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > FD_WAIT_NS) {
+      atomicOr(&g_status, FD_STATUS_TIMEOUT);
+      return;
+    }
+  }
+}
+
+// QK: FD_QK_INT8 / FD_QK_FP8; KG: k granularity; PV: FD_PV_BF16 / FD_PV_FP8
+template <int QK, int KG, int PV>
+__global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using SM = Smem<PV>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + SM::OFF_Q;
+  uint8_t* sK = smem + SM::OFF_K;
+  uint8_t* sV = smem + SM::OFF_V;
+  uint8_t* sP = smem + SM::OFF_P;
+  float* sKd = reinterpret_cast<float*>(smem + SM::OFF_KD);
+  float* sVd = reinterpret_cast<float*>(smem + SM::OFF_VD);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::OFF_BAR);
+  uint64_t* bQ = bars + 0;
+  uint64_t* bKfull = bars + 1;            // [KST]
+  uint64_t* bVfull = bars + 1 + KST;      // [KST]
+  uint64_t* bKVempty = bars + 1 + 2 * KST;  // [KST]
+  uint64_t* bSfull = bars + 1 + 3 * KST;
+  uint64_t* bSfree = bSfull + 1;
+  uint64_t* bPfull = bSfull + 2;
+  uint64_t* bOready = bSfull + 3;
+  uint64_t* bDrain = bSfull + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bSfull + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id(), lane = lane_id();
+  const int qb = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int q0 = qb * BQ;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bQ, 1);
+    for (int s = 0; s < KST; ++s) {
+      mbar_init(&bKfull[s], 1);
+      mbar_init(&bVfull[s], 1);
+      mbar_init(&bKVempty[s], 1);
+    }
+    mbar_init(bSfull, 1);
+    mbar_init(bSfree, 4);
+    mbar_init(bPfull, 4);
+    mbar_init(bOready, 1);
+    mbar_init(bDrain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tS = tmem_base, tO = tmem_base + 128;
+
+  if (warp == 4) {
+    // ================================================================ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(bQ, SM::Q_BYTES);
+      tma_load_3d(sQ, &tmQ, bQ, 0, q0, bh);
+      uint32_t i = 0;
+      uint32_t issued = 0;
+      for (int j = 0; j < p.n_kv_tiles; ++j) {
+        if (!tile_valid(p, bh, qb, j)) continue;
+        const uint32_t s = i % KST, use = i / KST;
+        if (!mbar_wait(&bKVempty[s], (use & 1) ^ 1, abort_flag)) break;
+        const uint32_t kbytes = SM::K_BYTES + (KG == FD_GRAN_TOKEN ? 512u : 0u);
+        mbar_arrive_expect_tx(&bKfull[s], kbytes);
+        tma_load_3d(sK + s * SM::K_BYTES, &tmK, &bKfull[s], 0, j * BKV, bh);
+        if (KG == FD_GRAN_TOKEN)
+          bulk_load(sKd + s * 128, p.k_desc + (int64_t)bh * p.k_desc_stride + (int64_t)j * BKV, 512,
+                    &bKfull[s]);
+        mbar_arrive_expect_tx(&bVfull[s], SM::V_BYTES);
+        if (PV == FD_PV_FP8) {
+          tma_load_3d(sV + s * SM::V_BYTES, &tmV, &bVfull[s], 0, j * BKV, bh);
+        } else {
+          tma_load_3d(sV + s * SM::V_BYTES, &tmV, &bVfull[s], 0, j * BKV, bh);
+          tma_load_3d(sV + s * SM::V_BYTES + BKV * 128, &tmV, &bVfull[s], 64, j * BKV, bh);
+        }
+        ++i;
+        issued = i;
+      }
+      // drain: every stage's newest loads must have landed
+      drain_wait(bQ, 0);
+      for (uint32_t k = 0; k < (uint32_t)KST && k < issued; ++k) {
+        const uint32_t last = issued - 1 - k;
+        const uint32_t s = last % KST, ph = (last / KST) & 1;
+        drain_wait(&bKfull[s], ph);
+        drain_wait(&bVfull[s], ph);
+      }
+    }
+  } else if (warp == 5) {
+    // ================================================================ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk =
+          QK == FD_QK_INT8 ? make_idesc(/*S32*/ 2, /*S8*/ 1, 1, 0, 0, BQ, BKV)
+                           : make_idesc(/*F32*/ 1, /*E4M3*/ 0, 0, 0, 0, BQ, BKV);
+      constexpr uint32_t idesc_pv =
+          PV == FD_PV_FP8 ? make_idesc(1, /*E4M3*/ 0, 0, /*A K-major*/ 0, /*B MN-major*/ 1, BQ, HD)
+                          : make_idesc(1, /*BF16*/ 1, 1, 0, 1, BQ, HD);
+      const uint32_t aQ = smem_u32(sQ);
+      bool ok = mbar_wait(bQ, 0, abort_flag);
+      // list of valid tiles is re-derived here in the same order as the producer
+      int jcur = -1;
+      auto next_valid = [&](int from) {
+        for (int j = from; j < p.n_kv_tiles; ++j)
+          if (tile_valid(p, bh, qb, j)) return j;
+        return p.n_kv_tiles;
+      };
+      auto issue_qk = [&](uint32_t i) -> bool {
+        const uint32_t s = i % KST, use = i / KST;
+        if (!mbar_wait(&bKfull[s], use & 1, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t bK = smem_u32(sK + s * SM::K_BYTES);
+#pragma unroll
+        for (int k = 0; k < HD / 32; ++k) {
+          const uint64_t ad = make_sdesc_sw128(aQ + k * 32, 16, 1024);
+          const uint64_t bd = make_sdesc_sw128(bK + k * 32, 16, 1024);
+          if (QK == FD_QK_INT8) mma_i8_ss(tS, ad, bd, idesc_qk, k > 0);
+          else mma_f8f6f4_ss(tS, ad, bd, idesc_qk, k > 0);
+        }
+        tc_commit(bSfull);
+        return true;
+      };
+      uint32_t i = 0;
+      jcur = next_valid(0);
+      if (ok && jcur < p.n_kv_tiles) ok = issue_qk(0);
+      while (ok && jcur < p.n_kv_tiles) {
+        const int jn = next_valid(jcur + 1);
+        if (jn < p.n_kv_tiles) {
+          // S is free once the softmax has pulled S(i) into registers
+          if (!mbar_wait(bSfree, i & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          if (!issue_qk(i + 1)) { ok = false; break; }
+        }
+        const uint32_t s = i % KST, use = i / KST;
+        if (!mbar_wait(bPfull, i & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&bVfull[s], use & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t aP = smem_u32(sP);
+        const uint32_t bV = smem_u32(sV + s * SM::V_BYTES);
+        if (PV == FD_PV_FP8) {
+#pragma unroll
+          for (int k = 0; k < BKV / 32; ++k) {
+            const uint64_t ad = make_sdesc_sw128(aP + k * 32, 16, 1024);
+            const uint64_t bd = make_sdesc_sw128(bV + k * 32 * 128, 16, 1024);
+            mma_f8f6f4_ss(tO, ad, bd, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < BKV / 16; ++k) {
+            const uint64_t ad = make_sdesc_sw128(aP + (k >> 2) * (BQ * 128) + (k & 3) * 32, 16, 1024);
+            const uint64_t bd = make_sdesc_sw128(bV + k * 16 * 128, BKV * 128, 1024);
+            mma_f16_ss(tO, ad, bd, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
+          }
+        }
+        tc_commit(&bKVempty[s]);
+        tc_commit(bOready);
+        ++i;
+        jcur = jn;
+      }
+      tc_commit(bDrain);
+      drain_wait(bDrain, 0);
+    }
+  } else {
+    // ================================================================ softmax (warps 0-3)
+    const int row = warp * 32 + lane;          // TMEM lane == query row in the tile
+    const int qrow = q0 + row;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    if (PV == FD_PV_FP8) sVd[row] = p.v_desc[(int64_t)bh * HD + row];
+    named_bar_sync(1, 128);
+    const float qd = p.q_gran == FD_GRAN_TOKEN
+                         ? p.q_desc[(int64_t)bh * p.q_desc_stride + (qrow < p.N ? qrow : 0)]
+                         : p.q_desc[(int64_t)bh * p.q_desc_stride + qb];
+    float m_ref = -INFINITY, l = 0.f;
+    uint32_t i = 0;
+    bool ok = true;
+    for (int j = 0; j < p.n_kv_tiles && ok; ++j) {
+      if (!tile_valid(p, bh, qb, j)) continue;
+      const uint32_t s = i % KST, use = i / KST;
+      // per-column scale factors of this tile (times qd)
+      float c_lo, c_hi;  // per-block K: one factor per 64-column half
+      bool half_ok[2] = {true, true};
+      if (p.mask) {
+        const uint8_t* mr = p.mask + (int64_t)bh * p.mask_bh_stride + (int64_t)qb * p.nkb64;
+        half_ok[0] = mr[2 * j] != 0;
+        half_ok[1] = (2 * j + 1 < p.nkb64) ? (mr[2 * j + 1] != 0) : false;
+      }
+      if (KG == FD_GRAN_BLOCK) {
+        const float* kd = p.k_desc + (int64_t)bh * p.k_desc_stride + 2 * j;
+        c_lo = kd[0] * qd;
+        c_hi = (2 * j + 1 < p.nkb64) ? kd[1] * qd : 0.f;
+      }
+      if (!mbar_wait(bSfull, i & 1, abort_flag)) { ok = false; break; }
+      if (KG == FD_GRAN_TOKEN) {
+        if (!mbar_wait(&bKfull[s], use & 1, abort_flag)) { ok = false; break; }
+      }
+      tc_fence_after();
+      float x[128];
+      {
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(tS + lane_base + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            if (QK == FD_QK_INT8) x[c * 32 + e] = (float)(int)r[e];
+            else x[c * 32 + e] = __uint_as_float(r[e]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bSfree);
+
+      // scale to log2-domain logits, mask, row max
+      const int kv0 = j * BKV;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        float cf;
+        if (KG == FD_GRAN_TOKEN) cf = sKd[s * 128 + c];
+        else cf = c < 64 ? c_lo : c_hi;
+        float v;
+        if (KG == FD_GRAN_TOKEN) v = (x[c] * qd) * cf;  // reference order (s * q_desc) * k_desc
+        else v = x[c] * cf;
+        const bool valid = (kv0 + c < p.N) && half_ok[c >> 6];
+        v = valid ? v : -INFINITY;
+        x[c] = v;
+        mt = fmaxf(mt, v);
+      }
+      const bool need = mt > m_ref + TAU;
+      const float m_new = need ? mt : m_ref;
+      if (__any_sync(0xffffffffu, need)) {
+        const float alpha = (m_ref == -INFINITY) ? 0.f : ex2_approx(m_ref - m_new);
+        l *= alpha;
+        if (i > 0) {
+          // PV(i-1) must be complete before O is touched
+          if (!mbar_wait(bOready, (i - 1) & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          uint32_t r[16];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            tmem_ld16(tO + lane_base + c * 16, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+            tmem_st16(tO + lane_base + c * 16, r);
+          }
+          tmem_wait_st();
+        }
+        m_ref = m_new;
+      }
+      const float msafe = (m_ref == -INFINITY) ? 0.f : m_ref;
+      // P buffer is free once PV(i-1) has completed
+      if (i > 0) {
+        if (!mbar_wait(bOready, (i - 1) & 1, abort_flag)) { ok = false; break; }
+      }
+      float lsum = 0.f;
+      if (PV == FD_PV_FP8) {
+        uint8_t* prow = sP + row * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {  // 16-byte chunk c holds keys 16c .. 16c+15
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float p0 = ex2_approx(x[16 * c + 4 * e + 0] - msafe);
+            const float p1 = ex2_approx(x[16 * c + 4 * e + 1] - msafe);
+            const float p2 = ex2_approx(x[16 * c + 4 * e + 2] - msafe);
+            const float p3 = ex2_approx(x[16 * c + 4 * e + 3] - msafe);
+            lsum += (p0 + p1) + (p2 + p3);
+            w[e] = f32x2_to_e4m3x2(p0 * P8_SCALE, p1 * P8_SCALE) |
+                   (f32x2_to_e4m3x2(p2 * P8_SCALE, p3 * P8_SCALE) << 16);
+          }
+          *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {  // 16-byte chunk c holds keys 8c .. 8c+7
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float p0 = ex2_approx(x[8 * c + 2 * e] - msafe);
+            const float p1 = ex2_approx(x[8 * c + 2 * e + 1] - msafe);
+            lsum += p0 + p1;
+            w[e] = pack_bf16x2(p0, p1);
+          }
+          const int panel = c >> 3, cc = c & 7;
+          *reinterpret_cast<uint4*>(sP + panel * (BQ * 128) + row * 128 + ((cc ^ (row & 7)) << 4)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      l += lsum;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bPfull);
+      ++i;
+    }
+    // ---------------------------------------------------------------- epilogue
+    if (ok && i > 0) ok = mbar_wait(bOready, (i - 1) & 1, abort_flag);
+    if (ok) {
+      tc_fence_after();
+      const bool any = i > 0;
+      const float inv_l = any ? __fdividef(1.0f, l) : __int_as_float(0x7fc00000);
+      const float lse_v = any ? m_ref + __log2f(l) : -INFINITY;
+      const bool row_ok = qrow < p.N;
+      if (row_ok && p.lse) p.lse[(int64_t)bh * p.N + qrow] = lse_v;
+      __nv_bfloat16* orow = p.out + ((int64_t)bh * p.N + (row_ok ? qrow : 0)) * HD;
+      // tcgen05.ld is warp-collective: every lane loads, only valid rows store
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        if (any) {
+          tmem_ld32(tO + lane_base + c * 32, r);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = 0u;
+        }
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          float o0 = __uint_as_float(r[2 * e]);
+          float o1 = __uint_as_float(r[2 * e + 1]);
+          if (PV == FD_PV_FP8) {
+            o0 *= sVd[c * 32 + 2 * e] * (1.0f / P8_SCALE);
+            o1 *= sVd[c * 32 + 2 * e + 1] * (1.0f / P8_SCALE);
+          }
+          w[e] = pack_bf16x2(o0 * inv_l, o1 * inv_l);
+        }
+        if (row_ok) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
+          dst[3] = make_uint4(w[12], w[13], w[14], w[15]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 5) tmem_dealloc(tmem_base, 256);
+}
+
+template <int QK, int KG, int PV>
+static int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const Params& p,
+                  int BH, cudaStream_t st) {
+  auto kern = attn_fwd_kernel<QK, KG, PV>;
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem<PV>::TOTAL);
+    if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "attn smem attribute: %s", cudaGetErrorString(e));
+    attr_done = true;
+  }
+  dim3 grid((unsigned)((p.N + BQ - 1) / BQ), (unsigned)BH);
+  kern<<<grid, NUM_THREADS, Smem<PV>::TOTAL, st>>>(tq, tk, tv, p);
+  return check_launch("sage_attn_fwd");
+}
+
+}  // namespace attn
+}  // namespace fd
+
+using namespace fd;
+
+int64_t fd_desc_stride(int64_t N, int gran, int rows_per_block);
+
+extern "C" int fd_sage_attn_fwd(const void* q_codes, const float* q_desc, const void* k_codes,
+                                const float* k_desc, const void* v, const float* v_desc,
+                                const uint8_t* block_mask, int64_t mask_bh_stride, void* out,
+                                float* lse, int64_t BH, int64_t N, int qk_kind, int q_gran,
+                                int k_gran, int pv_kind, void* stream) {
+  FD_CHECK_ARG(BH > 0 && BH <= 65535 && N > 0 && N < (1ll << 30), "bad shape");
+  FD_CHECK_ARG(qk_kind == FD_QK_INT8 || qk_kind == FD_QK_FP8, "bad qk_kind");
+  FD_CHECK_ARG(q_gran == FD_GRAN_TOKEN || q_gran == FD_GRAN_BLOCK, "bad q_gran");
+  FD_CHECK_ARG(k_gran == FD_GRAN_TOKEN || k_gran == FD_GRAN_BLOCK, "bad k_gran");
+  FD_CHECK_ARG(pv_kind == FD_PV_BF16 || pv_kind == FD_PV_FP8, "bad pv_kind");
+  FD_CHECK_ARG(q_codes && q_desc && k_codes && k_desc && v && out, "null pointer");
+  FD_CHECK_ARG(pv_kind == FD_PV_BF16 || v_desc, "v_desc required for fp8 PV");
+  FD_CHECK_ARG(aligned16(q_codes) && aligned16(k_codes) && aligned16(v) && aligned16(out) &&
+                   aligned16(k_desc),
+               "q/k/v codes, out and k_desc must be 16-byte aligned");
+  CUtensorMap tq, tk, tv;
+  {
+    const uint64_t dims[3] = {128, (uint64_t)N, (uint64_t)BH};
+    const uint64_t strides[2] = {128, (uint64_t)N * 128};
+    const uint32_t box[3] = {128, 128, 1};
+    int rc = encode_tiled(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, q_codes, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = encode_tiled(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, k_codes, dims, strides, box,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    if (pv_kind == FD_PV_FP8) {
+      rc = encode_tiled(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, v, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+    } else {
+      const uint64_t vstr[2] = {256, (uint64_t)N * 256};
+      const uint32_t vbox[3] = {64, 128, 1};
+      rc = encode_tiled(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, v, dims, vstr, vbox,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    if (rc) return rc;
+  }
+  attn::Params p;
+  p.q_desc = q_desc;
+  p.k_desc = k_desc;
+  p.v_desc = v_desc;
+  p.mask = block_mask;
+  p.mask_bh_stride = mask_bh_stride;
+  p.out = (__nv_bfloat16*)out;
+  p.lse = lse;
+  p.N = (int)N;
+  p.n_kv_tiles = (int)((N + 127) / 128);
+  p.nkb64 = (int)((N + 63) / 64);
+  p.q_gran = q_gran;
+  p.q_desc_stride = fd_desc_stride(N, q_gran, 128);
+  p.k_desc_stride = fd_desc_stride(N, k_gran, 64);
+  cudaStream_t st = (cudaStream_t)stream;
+#define FD_ATTN(QKV, KGV, PVV) return attn::launch<QKV, KGV, PVV>(tq, tk, tv, p, (int)BH, st)
+  if (qk_kind == FD_QK_INT8) {
+    if (k_gran == FD_GRAN_TOKEN) {
+      if (pv_kind == FD_PV_FP8) FD_ATTN(FD_QK_INT8, FD_GRAN_TOKEN, FD_PV_FP8);
+      else FD_ATTN(FD_QK_INT8, FD_GRAN_TOKEN, FD_PV_BF16);
+    } else {
+      if (pv_kind == FD_PV_FP8) FD_ATTN(FD_QK_INT8, FD_GRAN_BLOCK, FD_PV_FP8);
+      else FD_ATTN(FD_QK_INT8, FD_GRAN_BLOCK, FD_PV_BF16);
+    }
+  } else {
+    if (k_gran == FD_GRAN_TOKEN) {
+      if (pv_kind == FD_PV_FP8) FD_ATTN(FD_QK_FP8, FD_GRAN_TOKEN, FD_PV_FP8);
+      else FD_ATTN(FD_QK_FP8, FD_GRAN_TOKEN, FD_PV_BF16);
+    } else {
+      if (pv_kind == FD_PV_FP8) FD_ATTN(FD_QK_FP8, FD_GRAN_BLOCK, FD_PV_FP8);
+      else FD_ATTN(FD_QK_FP8, FD_GRAN_BLOCK, FD_PV_BF16);
+    }
+  }
+#undef FD_ATTN
+}

@@ -1,0 +1,331 @@
+// Attention quantisation prologue (A1..A4): K mean-smoothing, INT8 / e4m3
+// quantisation of Q and K (per token or per block) and e4m3 quantisation of V
+// (one scale per (bh, d) over the sequence).
+//
+// Two launches, both deterministic (fixed reduction order, no atomics):
+//   1. colstats: per (bh, row chunk) partial column sums of K and column
+//      absmax of V -> workspace.
+//   2. quant: per (bh, 128-row block): reduce the partials in chunk order,
+//      round the K mean to bf16, smooth, quantise, write codes and scales.
+//
+// Reference arithmetic:
+//   _smooth_k          src/futudiffu/sage_attention.py:63-71 (bf16 mean, bf16 sub)
+//   INT8 Q/K per token src/futudiffu/sage_kernels.py:632-639, :656-663
+//   FP8 Q/K per token  src/futudiffu/sage_kernels.py:151-155, :176-179
+//   V e4m3 per channel src/futudiffu/sage_kernels.py:1146-1151 (here over the
+//                      whole sequence instead of one 64-row tile)
+#include "fd_common.cuh"
+#include "fd_host.h"
+
+namespace fd {
+
+constexpr int kChunkRows = 256;  // rows per colstats CTA
+
+FD_DEV void unpack8(const uint4& u, float (&v)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+// grid (nchunks, BH), 256 threads: thread t -> column group (t & 15) * 8,
+// row lane t >> 4 (16 row lanes).
+__global__ void __launch_bounds__(256) colstats_kernel(const __nv_bfloat16* __restrict__ k,
+                                                      const __nv_bfloat16* __restrict__ v,
+                                                      float* __restrict__ ws_sum,
+                                                      float* __restrict__ ws_amax, int64_t N,
+                                                      int nchunks, int do_k, int do_v) {
+  const int chunk = blockIdx.x;
+  const int64_t bh = blockIdx.y;
+  const int cg = threadIdx.x & 15, rl = threadIdx.x >> 4;
+  float s[8] = {0, 0, 0, 0, 0, 0, 0, 0}, a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  const int64_t r0 = (int64_t)chunk * kChunkRows;
+  for (int r = rl; r < kChunkRows; r += 16) {
+    const int64_t n = r0 + r;
+    if (n >= N) break;
+    const int64_t off = (bh * N + n) * 128 + cg * 8;
+    float x[8];
+    if (do_k) {
+      unpack8(__ldg(reinterpret_cast<const uint4*>(k + off)), x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s[e] += x[e];
+    }
+    if (do_v) {
+      unpack8(__ldg(reinterpret_cast<const uint4*>(v + off)), x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) a[e] = fmaxf(a[e], fabsf(x[e]));
+    }
+  }
+  __shared__ float sh_s[16][128];
+  __shared__ float sh_a[16][128];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    sh_s[rl][cg * 8 + e] = s[e];
+    sh_a[rl][cg * 8 + e] = a[e];
+  }
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    const int c = threadIdx.x;
+    float ts = 0.f, ta = 0.f;
+    for (int i = 0; i < 16; ++i) {
+      ts += sh_s[i][c];
+      ta = fmaxf(ta, sh_a[i][c]);
+    }
+    ws_sum[(bh * nchunks + chunk) * 128 + c] = ts;
+    ws_amax[(bh * nchunks + chunk) * 128 + c] = ta;
+  }
+}
+
+template <int QK>  // FD_QK_INT8 or FD_QK_FP8
+FD_DEV uint32_t quant_code(float x, float inv) {
+  const float y = x * inv;
+  if constexpr (QK == FD_QK_INT8) {
+    // .to(tl.int8) truncates toward zero (|y| <= 127 by construction)
+    return (uint32_t)(__float2int_rz(y) & 0xFF);
+  } else {
+    return f32x2_to_e4m3x2(y, 0.f) & 0xFF;
+  }
+}
+
+template <int QK>
+FD_DEV uint2 quant_row8(const float (&x)[8], float inv) {
+  uint32_t c[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) c[e] = quant_code<QK>(x[e], inv);
+  return make_uint2(c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24),
+                    c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24));
+}
+
+FD_DEV float amax8(const float (&v)[8]) {
+  float a = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a = fmaxf(a, fabsf(v[i]));
+  return a;
+}
+
+FD_DEV float half_max(float v) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// grid (ceil(N/128), BH), 256 threads.  Thread t handles column group
+// (t & 15) * 8 of rows (t >> 4) + 16 i, i = 0..7, of the 128-row block.
+template <int QK>
+__global__ void __launch_bounds__(256) quant_kernel(
+    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+    const __nv_bfloat16* __restrict__ v, int64_t N, int nchunks, int smooth_k, int q_gran,
+    int k_gran, int pv_fp8, float sm_scale_log2e, uint8_t* __restrict__ q_codes,
+    float* __restrict__ q_desc, uint8_t* __restrict__ k_codes, float* __restrict__ k_desc,
+    uint8_t* __restrict__ v_codes, float* __restrict__ v_desc, float* __restrict__ k_mean,
+    const float* __restrict__ ws_sum, const float* __restrict__ ws_amax, int64_t q_desc_stride,
+    int64_t k_desc_stride) {
+  const int blk = blockIdx.x;
+  const int64_t bh = blockIdx.y;
+  const int cg = threadIdx.x & 15, rl = threadIdx.x >> 4;
+  const int64_t r0 = (int64_t)blk * 128;
+  const float qmax = (QK == FD_QK_INT8) ? 127.0f : 448.0f;
+
+  __shared__ float sh_mean[128];
+  __shared__ float sh_vinv[128];
+  __shared__ float sh_red[8];
+  __shared__ float sh_red2[2][8];
+
+  if (threadIdx.x < 128) {
+    const int c = threadIdx.x;
+    if (smooth_k) {
+      float tot = 0.f;
+      for (int i = 0; i < nchunks; ++i) tot += ws_sum[(bh * nchunks + i) * 128 + c];
+      // torch bf16 mean: fp32 accumulate, times 1/N, round to bf16
+      const float mean = round_to_bf16(tot * (1.0f / (float)N));
+      sh_mean[c] = mean;
+      if (blk == 0 && k_mean) k_mean[bh * 128 + c] = mean;
+    } else {
+      sh_mean[c] = 0.f;
+    }
+    if (pv_fp8) {
+      float am = 0.f;
+      for (int i = 0; i < nchunks; ++i) am = fmaxf(am, ws_amax[(bh * nchunks + i) * 128 + c]);
+      sh_vinv[c] = __fdiv_rn(448.0f, fmaxf(am, 1e-12f));
+      if (blk == 0) v_desc[bh * 128 + c] = __fdiv_rn(am, 448.0f);
+    }
+  }
+  __syncthreads();
+
+  // ---------------- Q
+  {
+    float x[8][8];
+    float rowmax[8];
+    float blkmax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t n = r0 + rl + 16 * i;
+      if (n < N) unpack8(__ldg(reinterpret_cast<const uint4*>(q + (bh * N + n) * 128 + cg * 8)), x[i]);
+      else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[i][e] = 0.f;
+      }
+      rowmax[i] = half_max(amax8(x[i]));
+      blkmax = fmaxf(blkmax, rowmax[i]);
+    }
+    if (q_gran == FD_GRAN_BLOCK) {
+      blkmax = warp_max(blkmax);
+      if (lane_id() == 0) sh_red[warp_id()] = blkmax;
+      __syncthreads();
+      blkmax = sh_red[0];
+#pragma unroll
+      for (int w = 1; w < 8; ++w) blkmax = fmaxf(blkmax, sh_red[w]);
+      if (threadIdx.x == 0)
+        q_desc[bh * q_desc_stride + blk] = __fdiv_rn(blkmax, qmax) * sm_scale_log2e;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t n = r0 + rl + 16 * i;
+      const float am = (q_gran == FD_GRAN_BLOCK) ? blkmax : rowmax[i];
+      const float inv = __fdiv_rn(qmax, fmaxf(am, 1e-12f));
+      if (n < N) {
+        *reinterpret_cast<uint2*>(q_codes + (bh * N + n) * 128 + cg * 8) = quant_row8<QK>(x[i], inv);
+        if (q_gran == FD_GRAN_TOKEN && cg == 0)
+          q_desc[bh * q_desc_stride + n] = __fdiv_rn(am, qmax) * sm_scale_log2e;
+      } else if (q_gran == FD_GRAN_TOKEN && cg == 0 && n < q_desc_stride) {
+        q_desc[bh * q_desc_stride + n] = 0.f;
+      }
+    }
+  }
+
+  // ---------------- K (smoothed)
+  {
+    float x[8][8];
+    float rowmax[8];
+    float hmax[2] = {0.f, 0.f};  // rows 0..63 / 64..127 of the block
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t n = r0 + rl + 16 * i;
+      if (n < N) {
+        unpack8(__ldg(reinterpret_cast<const uint4*>(k + (bh * N + n) * 128 + cg * 8)), x[i]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[i][e] = round_to_bf16(x[i][e] - sh_mean[cg * 8 + e]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[i][e] = 0.f;
+      }
+      rowmax[i] = half_max(amax8(x[i]));
+      hmax[i >> 2] = fmaxf(hmax[i >> 2], rowmax[i]);  // row rl+16i < 64 iff i < 4
+    }
+    if (k_gran == FD_GRAN_BLOCK) {
+      hmax[0] = warp_max(hmax[0]);
+      hmax[1] = warp_max(hmax[1]);
+      if (lane_id() == 0) {
+        sh_red2[0][warp_id()] = hmax[0];
+        sh_red2[1][warp_id()] = hmax[1];
+      }
+      __syncthreads();
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float m = sh_red2[h][0];
+#pragma unroll
+        for (int w = 1; w < 8; ++w) m = fmaxf(m, sh_red2[h][w]);
+        hmax[h] = m;
+      }
+      if (threadIdx.x < 2) {
+        const int64_t kb = (int64_t)blk * 2 + threadIdx.x;
+        if (kb * 64 < N) k_desc[bh * k_desc_stride + kb] = __fdiv_rn(hmax[threadIdx.x], qmax);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t n = r0 + rl + 16 * i;
+      const float am = (k_gran == FD_GRAN_BLOCK) ? hmax[i >> 2] : rowmax[i];
+      const float inv = __fdiv_rn(qmax, fmaxf(am, 1e-12f));
+      if (n < N) {
+        *reinterpret_cast<uint2*>(k_codes + (bh * N + n) * 128 + cg * 8) = quant_row8<QK>(x[i], inv);
+        if (k_gran == FD_GRAN_TOKEN && cg == 0) k_desc[bh * k_desc_stride + n] = __fdiv_rn(am, qmax);
+      } else if (k_gran == FD_GRAN_TOKEN && cg == 0 && n < k_desc_stride) {
+        k_desc[bh * k_desc_stride + n] = 0.f;
+      }
+    }
+  }
+
+  // ---------------- V (e4m3, per channel)
+  if (pv_fp8) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t n = r0 + rl + 16 * i;
+      if (n < N) {
+        float x[8];
+        unpack8(__ldg(reinterpret_cast<const uint4*>(v + (bh * N + n) * 128 + cg * 8)), x);
+        uint32_t c[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float a = fminf(fmaxf(x[2 * e] * sh_vinv[cg * 8 + 2 * e], -448.f), 448.f);
+          const float b = fminf(fmaxf(x[2 * e + 1] * sh_vinv[cg * 8 + 2 * e + 1], -448.f), 448.f);
+          c[e] = f32x2_to_e4m3x2(a, b);
+        }
+        *reinterpret_cast<uint2*>(v_codes + (bh * N + n) * 128 + cg * 8) =
+            make_uint2(c[0] | (c[1] << 16), c[2] | (c[3] << 16));
+      }
+    }
+  }
+}
+
+}  // namespace fd
+
+using namespace fd;
+
+static int64_t n_chunks(int64_t N) { return (N + kChunkRows - 1) / kChunkRows; }
+
+extern "C" int64_t fd_attn_quant_workspace_floats(int64_t BH, int64_t N) {
+  return 2 * BH * n_chunks(N) * 128;
+}
+
+// Internal layouts of the descale arrays (shared with the attention kernel):
+//   per-token q/k: (BH, round_up(N, 128)), zero beyond N
+//   per-block q:   (BH, ceil(N/128)); per-block k: (BH, ceil(N/64))
+int64_t fd_desc_stride(int64_t N, int gran, int rows_per_block) {
+  return gran == FD_GRAN_TOKEN ? ((N + 127) / 128) * 128 : (N + rows_per_block - 1) / rows_per_block;
+}
+
+extern "C" int fd_attn_quant(const void* q, const void* k, const void* v, int64_t BH, int64_t N,
+                             int smooth_k, int qk_kind, int q_gran, int k_gran, int pv_kind,
+                             float sm_scale_log2e, void* q_codes, float* q_desc, void* k_codes,
+                             float* k_desc, void* v_codes, float* v_desc, float* k_mean,
+                             float* workspace, void* stream) {
+  FD_CHECK_ARG(BH > 0 && N > 0, "empty input");
+  FD_CHECK_ARG(BH <= 65535, "BH too large");
+  FD_CHECK_ARG(qk_kind == FD_QK_INT8 || qk_kind == FD_QK_FP8, "bad qk_kind");
+  FD_CHECK_ARG((q_gran == FD_GRAN_TOKEN || q_gran == FD_GRAN_BLOCK) &&
+                   (k_gran == FD_GRAN_TOKEN || k_gran == FD_GRAN_BLOCK),
+               "bad granularity");
+  FD_CHECK_ARG(pv_kind == FD_PV_BF16 || pv_kind == FD_PV_FP8, "bad pv_kind");
+  FD_CHECK_ARG(q && k && q_codes && q_desc && k_codes && k_desc && workspace, "null pointer");
+  FD_CHECK_ARG(pv_kind == FD_PV_BF16 || (v && v_codes && v_desc), "null V pointer");
+  FD_CHECK_ARG(aligned16(q) && aligned16(k) && (v == nullptr || aligned16(v)) &&
+                   aligned8(q_codes) && aligned8(k_codes) &&
+                   (v_codes == nullptr || aligned8(v_codes)),
+               "misaligned pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  const int nchunks = (int)n_chunks(N);
+  float* ws_sum = workspace;
+  float* ws_amax = workspace + BH * nchunks * 128;
+  const int pv_fp8 = pv_kind == FD_PV_FP8;
+  if (smooth_k || pv_fp8) {
+    colstats_kernel<<<dim3(nchunks, (unsigned)BH), 256, 0, st>>>(
+        (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, ws_sum, ws_amax, N, nchunks, smooth_k,
+        pv_fp8);
+    int rc = check_launch("attn_quant colstats");
+    if (rc) return rc;
+  }
+  const int64_t qs = fd_desc_stride(N, q_gran, 128), ks = fd_desc_stride(N, k_gran, 64);
+  dim3 grid((unsigned)((N + 127) / 128), (unsigned)BH);
+#define FD_Q_LAUNCH(QK)                                                                         \
+  quant_kernel<QK><<<grid, 256, 0, st>>>(                                                       \
+      (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, N, nchunks,   \
+      smooth_k, q_gran, k_gran, pv_fp8, sm_scale_log2e, (uint8_t*)q_codes, q_desc,              \
+      (uint8_t*)k_codes, k_desc, (uint8_t*)v_codes, v_desc, k_mean, ws_sum, ws_amax, qs, ks)
+  if (qk_kind == FD_QK_INT8) FD_Q_LAUNCH(FD_QK_INT8);
+  else FD_Q_LAUNCH(FD_QK_FP8);
+#undef FD_Q_LAUNCH
+  return check_launch("attn_quant");
+}

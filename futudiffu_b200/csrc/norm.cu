@@ -1,0 +1,246 @@
+// Fused RMSNorm prologues of the DiT block:
+//   P1 rms_norm_modulate    (src/futudiffu/fused_kernels.py:43-86)
+//   P2 rms_norm_gate_residual (src/futudiffu/fused_kernels.py:99-148)
+//   P3 qkv_postprocess       (src/futudiffu/fused_kernels.py:270-385)
+//
+// P1/P2: one warp per token row; the row is held in registers (dim <= 8192,
+// 16-byte vectors), so x is read exactly once and the output written once.
+// P3: one warp per (token, head): each lane owns two RoPE pairs (4 values)
+// of Q and K and 4 values of V.
+//
+// Arithmetic follows the Triton kernels: fp32 throughout, mean of squares
+// by a correctly rounded divide, rrms = 1 / sqrt.approx(mean + eps)
+// (Triton's tl.sqrt is the approximate square root, `1.0 / x` the IEEE
+// divide), products evaluated left to right.
+#include "fd_common.cuh"
+#include "fd_host.h"
+
+namespace fd {
+
+FD_DEV float sqrt_approx(float x) {
+  float y;
+  asm("sqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int DT>
+FD_DEV float load_elem(const void* p, int64_t i) {
+  if constexpr (DT == FD_DT_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  else if constexpr (DT == FD_DT_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  else return reinterpret_cast<const float*>(p)[i];
+}
+
+FD_DEV void unpack_bf16x8(const uint4& u, float (&v)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+FD_DEV uint4 pack_bf16x8(const float (&v)[8]) {
+  return make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                    pack_bf16x2(v[6], v[7]));
+}
+
+// Max 8192 / (32 lanes * 8) = 32 vectors per lane.
+constexpr int kMaxVecPerLane = 32;
+
+// MODE 0: P1 (modulate), MODE 1: P2 (gate + residual)
+template <int MODE, int WDT, int SDT, int NV>
+__global__ void __launch_bounds__(256) rms_row_kernel(const __nv_bfloat16* __restrict__ x,
+                                                     const void* __restrict__ w,
+                                                     const void* __restrict__ sg,
+                                                     const __nv_bfloat16* __restrict__ res,
+                                                     __nv_bfloat16* __restrict__ out,
+                                                     int64_t rows, int64_t S, int dim, float eps) {
+  const int lane = lane_id();
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int nvec = dim / 8;
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp_id(); row < rows;
+       row += warps) {
+    const int64_t b = row / S;
+    float v[NV][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = (lane + 32 * j);
+      if (c < nvec) {
+        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(x + row * dim) + c), v[j]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss += v[j][e] * v[j][e];
+      }
+    }
+    ss = warp_sum(ss);
+    const float mean_sq = __fdiv_rn(ss, (float)dim);
+    const float rrms = __fdiv_rn(1.0f, sqrt_approx(mean_sq + eps));
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = (lane + 32 * j);
+      if (c < nvec) {
+        float o[8];
+        float r[8];
+        if constexpr (MODE == 1)
+          unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(res + row * dim) + c), r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int col = c * 8 + e;
+          const float normed = (v[j][e] * rrms) * load_elem<WDT>(w, col);
+          const float sv = load_elem<SDT>(sg, b * dim + col);
+          if constexpr (MODE == 0) o[e] = normed * (1.0f + sv);
+          else o[e] = r[e] + tanhf(sv) * normed;
+        }
+        reinterpret_cast<uint4*>(out + row * dim)[c] = pack_bf16x8(o);
+      }
+    }
+  }
+}
+
+template <int MODE, int WDT, int SDT>
+static void launch_rms(const void* x, const void* w, const void* sg, const void* res, void* out,
+                       int64_t rows, int64_t S, int dim, float eps, cudaStream_t st) {
+  const int nvec = dim / 8;
+  int64_t grid = (rows + 7) / 8;
+  const int64_t cap = (int64_t)num_sms() * 16;
+  if (grid > cap) grid = cap;
+  if (grid < 1) grid = 1;
+#define FD_RMS_LAUNCH(NVV)                                                                  \
+  rms_row_kernel<MODE, WDT, SDT, NVV><<<(unsigned)grid, 256, 0, st>>>(                     \
+      (const __nv_bfloat16*)x, w, sg, (const __nv_bfloat16*)res, (__nv_bfloat16*)out, rows, S, \
+      dim, eps)
+  if (nvec <= 32 * 4) FD_RMS_LAUNCH(4);
+  else if (nvec <= 32 * 8) FD_RMS_LAUNCH(8);
+  else if (nvec <= 32 * 16) FD_RMS_LAUNCH(16);
+  else FD_RMS_LAUNCH(32);
+#undef FD_RMS_LAUNCH
+}
+
+template <int MODE>
+static int dispatch_rms(const void* x, const void* w, int wdt, const void* sg, int sdt,
+                        const void* res, void* out, int64_t rows, int64_t S, int dim, float eps,
+                        cudaStream_t st) {
+#define FD_RMS_W(WD)                                                                       \
+  switch (sdt) {                                                                           \
+    case FD_DT_BF16: launch_rms<MODE, WD, FD_DT_BF16>(x, w, sg, res, out, rows, S, dim, eps, st); break; \
+    case FD_DT_F16: launch_rms<MODE, WD, FD_DT_F16>(x, w, sg, res, out, rows, S, dim, eps, st); break;   \
+    case FD_DT_F32: launch_rms<MODE, WD, FD_DT_F32>(x, w, sg, res, out, rows, S, dim, eps, st); break;   \
+    default: return set_error(FD_ERR_ARG, "unsupported scale/gate dtype");                 \
+  }
+  switch (wdt) {
+    case FD_DT_BF16: FD_RMS_W(FD_DT_BF16); break;
+    case FD_DT_F16: FD_RMS_W(FD_DT_F16); break;
+    case FD_DT_F32: FD_RMS_W(FD_DT_F32); break;
+    default: return set_error(FD_ERR_ARG, "unsupported weight dtype");
+  }
+#undef FD_RMS_W
+  return check_launch(MODE == 0 ? "rms_norm_modulate" : "rms_norm_gate_residual");
+}
+
+// ---------------------------------------------------------------- P3
+// One warp per (token row, head); lane l owns elements 4l .. 4l+3 (pairs
+// 2l and 2l+1) of Q, K and V of that head.
+__global__ void __launch_bounds__(256) qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                                      const float* __restrict__ qw,
+                                                      const float* __restrict__ kw,
+                                                      const float* __restrict__ freqs,
+                                                      __nv_bfloat16* __restrict__ oq,
+                                                      __nv_bfloat16* __restrict__ ok,
+                                                      __nv_bfloat16* __restrict__ ov,
+                                                      int64_t rows, int64_t S, int H, float eps) {
+  constexpr int HD = 128;
+  const int lane = lane_id();
+  const int64_t items = rows * H;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int dim = H * HD;
+  const float4 wq = reinterpret_cast<const float4*>(qw)[lane];
+  const float4 wk = reinterpret_cast<const float4*>(kw)[lane];
+  for (int64_t it = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp_id(); it < items; it += warps) {
+    const int64_t row = it / H;
+    const int h = (int)(it % H);
+    const __nv_bfloat16* base = qkv + row * 3 * dim + h * HD + lane * 4;
+    const uint2 uq = *reinterpret_cast<const uint2*>(base);
+    const uint2 uk = *reinterpret_cast<const uint2*>(base + dim);
+    const uint2 uv = *reinterpret_cast<const uint2*>(base + 2 * dim);
+    float q[4] = {bf16_bits_to_f32(uq.x & 0xFFFF), bf16_bits_to_f32(uq.x >> 16),
+                  bf16_bits_to_f32(uq.y & 0xFFFF), bf16_bits_to_f32(uq.y >> 16)};
+    float k[4] = {bf16_bits_to_f32(uk.x & 0xFFFF), bf16_bits_to_f32(uk.x >> 16),
+                  bf16_bits_to_f32(uk.y & 0xFFFF), bf16_bits_to_f32(uk.y >> 16)};
+    float sq = q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3];
+    float sk = k[0] * k[0] + k[1] * k[1] + k[2] * k[2] + k[3] * k[3];
+    sq = warp_sum(sq);
+    sk = warp_sum(sk);
+    const float rq = __fdiv_rn(1.0f, sqrt_approx(__fdiv_rn(sq, (float)HD) + eps));
+    const float rk = __fdiv_rn(1.0f, sqrt_approx(__fdiv_rn(sk, (float)HD) + eps));
+    const float wqa[4] = {wq.x, wq.y, wq.z, wq.w};
+    const float wka[4] = {wk.x, wk.y, wk.z, wk.w};
+    float qo[4], ko[4];
+    // freqs (rows, 64, 2, 2): pair p at row*256 + p*4: [cos, -sin, sin, cos]
+    const float4* fr = reinterpret_cast<const float4*>(freqs + row * 256) + lane * 2;
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const float4 f = fr[p];
+      const float qe = (q[2 * p] * rq) * wqa[2 * p], qd = (q[2 * p + 1] * rq) * wqa[2 * p + 1];
+      const float ke = (k[2 * p] * rk) * wka[2 * p], kd = (k[2 * p + 1] * rk) * wka[2 * p + 1];
+      qo[2 * p] = f.x * qe + f.y * qd;
+      qo[2 * p + 1] = f.z * qe + f.x * qd;
+      ko[2 * p] = f.x * ke + f.y * kd;
+      ko[2 * p + 1] = f.z * ke + f.x * kd;
+    }
+    const int64_t b = row / S, s = row % S;
+    const int64_t o = ((b * H + h) * S + s) * HD + lane * 4;
+    *reinterpret_cast<uint2*>(oq + o) = make_uint2(pack_bf16x2(qo[0], qo[1]), pack_bf16x2(qo[2], qo[3]));
+    *reinterpret_cast<uint2*>(ok + o) = make_uint2(pack_bf16x2(ko[0], ko[1]), pack_bf16x2(ko[2], ko[3]));
+    *reinterpret_cast<uint2*>(ov + o) = uv;
+  }
+}
+
+}  // namespace fd
+
+using namespace fd;
+
+extern "C" int fd_rms_norm_modulate(const void* x, const void* w, int w_dtype, const void* scale,
+                                    int scale_dtype, void* out, int64_t B, int64_t S, int64_t dim,
+                                    float eps, void* stream) {
+  FD_CHECK_ARG(B >= 0 && S >= 0 && dim > 0 && dim % 8 == 0 && dim <= 8192,
+               "dim must be a multiple of 8 and at most 8192");
+  if (B * S == 0) return FD_OK;
+  FD_CHECK_ARG(x && w && scale && out, "null pointer");
+  FD_CHECK_ARG(aligned16(x) && aligned16(out), "x and out must be 16-byte aligned");
+  return dispatch_rms<0>(x, w, w_dtype, scale, scale_dtype, nullptr, out, B * S, S, (int)dim, eps,
+                         (cudaStream_t)stream);
+}
+
+extern "C" int fd_rms_norm_gate_residual(const void* x, const void* w, int w_dtype,
+                                         const void* gate, int gate_dtype, const void* residual,
+                                         void* out, int64_t B, int64_t S, int64_t dim, float eps,
+                                         void* stream) {
+  FD_CHECK_ARG(B >= 0 && S >= 0 && dim > 0 && dim % 8 == 0 && dim <= 8192,
+               "dim must be a multiple of 8 and at most 8192");
+  if (B * S == 0) return FD_OK;
+  FD_CHECK_ARG(x && w && gate && residual && out, "null pointer");
+  FD_CHECK_ARG(aligned16(x) && aligned16(out) && aligned16(residual),
+               "x, residual and out must be 16-byte aligned");
+  return dispatch_rms<1>(x, w, w_dtype, gate, gate_dtype, residual, out, B * S, S, (int)dim, eps,
+                         (cudaStream_t)stream);
+}
+
+extern "C" int fd_qkv_postprocess(const void* qkv, const float* qw, const float* kw,
+                                  const float* freqs, void* oq, void* ok, void* ov, int64_t B,
+                                  int64_t S, int64_t H, int64_t hd, float eps, void* stream) {
+  FD_CHECK_ARG(hd == 128, "head_dim must be 128");
+  FD_CHECK_ARG(B >= 0 && S >= 0 && H > 0, "bad shape");
+  if (B * S == 0) return FD_OK;
+  FD_CHECK_ARG(qkv && qw && kw && freqs && oq && ok && ov, "null pointer");
+  FD_CHECK_ARG(aligned16(qw) && aligned16(kw) && aligned16(freqs) && aligned8(qkv) &&
+                   aligned8(oq) && aligned8(ok) && aligned8(ov),
+               "misaligned pointer");
+  const int64_t items = B * S * H;
+  int64_t grid = (items + 7) / 8;
+  const int64_t cap = (int64_t)num_sms() * 16;
+  if (grid > cap) grid = cap;
+  qkv_post_kernel<<<(unsigned)grid, 256, 0, (cudaStream_t)stream>>>(
+      (const __nv_bfloat16*)qkv, qw, kw, freqs, (__nv_bfloat16*)oq, (__nv_bfloat16*)ok,
+      (__nv_bfloat16*)ov, B * S, S, (int)H, eps);
+  return check_launch("qkv_postprocess");
+}

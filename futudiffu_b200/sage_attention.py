@@ -1,0 +1,361 @@
+"""SageAttention API, B200 edition: drop-in for ``futudiffu.sage_attention``.
+
+Public names, signatures, config globals, assertions, output layouts and the
+``futudiffu::sage_attn`` / ``futudiffu::sage_attn_masked`` custom ops follow
+src/futudiffu/sage_attention.py.  Each call runs two sm_100a kernels:
+
+1. the quantisation prologue (``fd_attn_quant``): K mean-smoothing
+   (``_smooth_k``, :63-71), Q/K quantisation to INT8 (truncating) or e4m3 with
+   per-token or per-block scales, and optional e4m3 V with per-channel scales;
+2. the tcgen05 attention kernel (``fd_sage_attn_fwd``): QK^T on the INT8 or
+   FP8 tensor-core path, exp2 online softmax, PV on bf16 or e4m3, LSE.
+
+Dispatch mirrors the reference exactly (which kernel each entry point uses
+for each ``configure_sage`` setting) with one addition: ``qk_granularity``.
+``"per_token"`` (default) is the reference's quantisation; ``"per_block"``
+selects per-128-row Q / per-64-row K scales and honours ``pv_quant`` in every
+entry point (the INT8-QK + FP8-PV combination of the B200 headline config).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+from torch import Tensor
+
+from . import _lib as L
+
+_LOG2E = math.log2(math.e)
+
+_SAGE_SMOOTH_K = True
+_SAGE_QK_QUANT = "fp8"
+_SAGE_PV_QUANT = "bf16"
+_SAGE_QK_GRAN = "per_token"
+
+
+def configure_sage(
+    *,
+    smooth_k: bool = True,
+    qk_quant: str = "fp8",
+    pv_quant: str = "bf16",
+    qk_granularity: str = "per_token",
+) -> None:
+    """Select the SageAttention variant (reference sage_attention.py:37-60).
+
+    qk_granularity: "per_token" (reference) or "per_block" (Q per 128 rows,
+    K per 64 rows; also enables fp8 PV together with int8 QK).
+    """
+    global _SAGE_SMOOTH_K, _SAGE_QK_QUANT, _SAGE_PV_QUANT, _SAGE_QK_GRAN
+    if qk_quant not in ("fp8", "int8"):
+        raise ValueError(f"Unknown qk_quant: {qk_quant!r}")
+    if pv_quant not in ("bf16", "fp8"):
+        raise ValueError(f"Unknown pv_quant: {pv_quant!r}")
+    if qk_granularity not in ("per_token", "per_block"):
+        raise ValueError(f"Unknown qk_granularity: {qk_granularity!r}")
+    _SAGE_SMOOTH_K = smooth_k
+    _SAGE_QK_QUANT = qk_quant
+    _SAGE_PV_QUANT = pv_quant
+    _SAGE_QK_GRAN = qk_granularity
+
+
+def get_sage_config() -> dict:
+    return {
+        "smooth_k": _SAGE_SMOOTH_K,
+        "qk_quant": _SAGE_QK_QUANT,
+        "pv_quant": _SAGE_PV_QUANT,
+        "qk_granularity": _SAGE_QK_GRAN,
+    }
+
+
+def _smooth_k(k: Tensor) -> Tensor:
+    """k - k.mean(dim=2, keepdim=True) in k's dtype (reference :63-71).
+
+    Kept for API parity; the attention entry points fuse this into the
+    quantisation prologue kernel instead of calling it.
+    """
+    return k - k.mean(dim=2, keepdim=True)
+
+
+def _check_sm_capability() -> tuple[int, int]:
+    if not torch.cuda.is_available():
+        raise RuntimeError("SageAttention requires CUDA")
+    cap = torch.cuda.get_device_capability()
+    if cap < (10, 0):
+        raise RuntimeError(f"futudiffu_b200 SageAttention requires SM 10.0 (B200), got SM {cap[0]}.{cap[1]}")
+    return cap
+
+
+def _desc_stride(N: int, gran: int, rows: int) -> int:
+    return ((N + 127) // 128) * 128 if gran == L.GRAN_TOKEN else (N + rows - 1) // rows
+
+
+def quantize_qkv(
+    q: Tensor, k: Tensor, v: Tensor, sm_scale: float, *, smooth_k: bool, qk_quant: str,
+    granularity: str, pv_quant: str,
+) -> dict:
+    """Run the quantisation prologue on (BH, N, 128) bf16 Q/K/V; returns codes and scales.
+
+    Layouts: codes (BH, N, 128); per-token descales (BH, round_up(N, 128)),
+    per-block descales (BH, ceil(N/128)) for Q and (BH, ceil(N/64)) for K;
+    v_desc (BH, 128); k_mean (BH, 128) (bf16-rounded smoothing mean as f32).
+    """
+    BH, N, D = q.shape
+    dev = q.device
+    qk = L.QK_INT8 if qk_quant == "int8" else L.QK_FP8
+    gran = L.GRAN_TOKEN if granularity == "per_token" else L.GRAN_BLOCK
+    pv = L.PV_FP8 if pv_quant == "fp8" else L.PV_BF16
+    code_dt = torch.int8 if qk == L.QK_INT8 else torch.float8_e4m3fn
+    q_codes = torch.empty(BH, N, D, dtype=code_dt, device=dev)
+    k_codes = torch.empty(BH, N, D, dtype=code_dt, device=dev)
+    q_desc = torch.empty(BH, _desc_stride(N, gran, 128), dtype=torch.float32, device=dev)
+    k_desc = torch.empty(BH, _desc_stride(N, gran, 64), dtype=torch.float32, device=dev)
+    k_mean = torch.empty(BH, D, dtype=torch.float32, device=dev)
+    if pv == L.PV_FP8:
+        v_codes = torch.empty(BH, N, D, dtype=torch.float8_e4m3fn, device=dev)
+        v_desc = torch.empty(BH, D, dtype=torch.float32, device=dev)
+    else:
+        v_codes = None
+        v_desc = None
+    ws = torch.empty(int(L.lib().fd_attn_quant_workspace_floats(BH, N)), dtype=torch.float32, device=dev)
+    L.call(
+        "fd_attn_quant", L.ptr(q), L.ptr(k), L.ptr(v), BH, N, int(bool(smooth_k)), qk, gran, gran, pv,
+        float(sm_scale * _LOG2E), L.ptr(q_codes), L.ptr(q_desc), L.ptr(k_codes), L.ptr(k_desc),
+        L.ptr(v_codes), L.ptr(v_desc), L.ptr(k_mean), L.ptr(ws), L.stream_ptr(dev),
+    )
+    return {
+        "q_codes": q_codes, "q_desc": q_desc, "k_codes": k_codes, "k_desc": k_desc,
+        "v_codes": v_codes, "v_desc": v_desc, "k_mean": k_mean,
+        "qk": qk, "gran": gran, "pv": pv,
+    }
+
+
+def _normalize_mask(block_mask: Tensor | None, N: int) -> tuple[Tensor | None, int]:
+    if block_mask is None:
+        return None, 0
+    bm = block_mask.contiguous()
+    if bm.dtype != torch.uint8:
+        bm = bm.to(torch.uint8)
+    nq, nk = (N + 127) // 128, (N + 63) // 64
+    if bm.ndim == 2:
+        stride = 0
+    elif bm.ndim == 3:
+        stride = bm.shape[1] * bm.shape[2]
+    else:
+        raise ValueError(f"block_mask must be 2D or 3D, got {bm.ndim}D")
+    if tuple(bm.shape[-2:]) != (nq, nk):
+        raise ValueError(f"block_mask must have trailing shape ({nq}, {nk}), got {tuple(bm.shape)}")
+    return bm, stride
+
+
+def _attn_forward(
+    q: Tensor, k: Tensor, v: Tensor, sm_scale: float | None, *, block_mask: Tensor | None,
+    qk_quant: str, pv_quant: str, granularity: str, want_lse: bool,
+) -> tuple[Tensor, Tensor | None]:
+    B, H, N, D = q.shape
+    assert D == 128, f"SageAttention currently requires head_dim=128, got {D}"
+    assert q.dtype == torch.bfloat16, f"Expected BF16 input, got {q.dtype}"
+    L.require_cuda(q, k, v)
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    BH = B * H
+    qf = q.reshape(BH, N, D).contiguous()
+    kf = k.reshape(BH, N, D).contiguous()
+    vf = v.reshape(BH, N, D).contiguous()
+    bm, bm_stride = _normalize_mask(block_mask, N)
+    qz = quantize_qkv(qf, kf, vf, sm_scale, smooth_k=_SAGE_SMOOTH_K, qk_quant=qk_quant,
+                      granularity=granularity, pv_quant=pv_quant)
+    out = torch.empty_like(qf)
+    lse = torch.empty(BH, N, dtype=torch.float32, device=q.device) if want_lse else None
+    vsrc = qz["v_codes"] if qz["pv"] == L.PV_FP8 else vf
+    L.call(
+        "fd_sage_attn_fwd", L.ptr(qz["q_codes"]), L.ptr(qz["q_desc"]), L.ptr(qz["k_codes"]),
+        L.ptr(qz["k_desc"]), L.ptr(vsrc), L.ptr(qz["v_desc"]), L.ptr(bm), bm_stride, L.ptr(out),
+        L.ptr(lse), BH, N, qz["qk"], qz["gran"], qz["gran"], qz["pv"], L.stream_ptr(q.device),
+    )
+    return out.reshape(B, H, N, D), lse
+
+
+def _pv_for(default_pv: str) -> str:
+    return _SAGE_PV_QUANT if _SAGE_QK_GRAN == "per_block" else default_pv
+
+
+def sage_attn_forward(q: Tensor, k: Tensor, v: Tensor, sm_scale: float | None = None) -> Tensor:
+    """Attention forward without LSE (reference :121-180): qk_quant QK, bf16 PV."""
+    out, _ = _attn_forward(q, k, v, sm_scale, block_mask=None, qk_quant=_SAGE_QK_QUANT,
+                           pv_quant=_pv_for("bf16"), granularity=_SAGE_QK_GRAN, want_lse=False)
+    return out
+
+
+def sage_attn_forward_masked(
+    q: Tensor, k: Tensor, v: Tensor, block_mask: Tensor, sm_scale: float | None = None,
+) -> Tensor:
+    """Block-masked forward (reference :183-268); mask is (nq, nk64) or (BH, nq, nk64) uint8."""
+    out, _ = _attn_forward(q, k, v, sm_scale, block_mask=block_mask, qk_quant=_SAGE_QK_QUANT,
+                           pv_quant=_pv_for("bf16"), granularity=_SAGE_QK_GRAN, want_lse=False)
+    return out
+
+
+def sage_attn_forward_with_lse(
+    q: Tensor, k: Tensor, v: Tensor, sm_scale: float | None = None
+) -> tuple[Tensor, Tensor]:
+    """Forward returning (out, lse (BH, N) log2-domain) (reference :271-341).
+
+    Reference dispatch: pv_quant == "fp8" -> FP8 QK + FP8 PV; else qk_quant QK + bf16 PV.
+    """
+    if _SAGE_QK_GRAN == "per_block":
+        qk, pv = _SAGE_QK_QUANT, _SAGE_PV_QUANT
+    elif _SAGE_PV_QUANT == "fp8":
+        qk, pv = "fp8", "fp8"
+    else:
+        qk, pv = _SAGE_QK_QUANT, "bf16"
+    return _attn_forward(q, k, v, sm_scale, block_mask=None, qk_quant=qk, pv_quant=pv,
+                         granularity=_SAGE_QK_GRAN, want_lse=True)
+
+
+def sage_attn_forward_masked_with_lse(
+    q: Tensor, k: Tensor, v: Tensor, block_mask: Tensor, sm_scale: float | None = None,
+) -> tuple[Tensor, Tensor]:
+    """Masked forward with LSE; always INT8 QK + bf16 PV like the reference (:461-531)."""
+    return _attn_forward(q, k, v, sm_scale, block_mask=block_mask, qk_quant="int8",
+                         pv_quant=_pv_for("bf16"), granularity=_SAGE_QK_GRAN, want_lse=True)
+
+
+def _attn_backward(q, k, v, out, lse, dout, sm_scale, block_mask, qk_quant):
+    B, H, N, D = q.shape
+    BH = B * H
+    L.require_cuda(q, k, v, out, lse, dout)
+    qf = q.reshape(BH, N, D).contiguous()
+    kf = k.reshape(BH, N, D).contiguous()
+    vf = v.reshape(BH, N, D).contiguous()
+    of = out.reshape(BH, N, D).contiguous()
+    dof = dout.reshape(BH, N, D).contiguous().to(torch.bfloat16)
+    lse = lse.contiguous()
+    bm, bm_stride = _normalize_mask(block_mask, N)
+    # same per-token codes (and smoothed K) as the forward
+    qz = quantize_qkv(qf, kf, vf, sm_scale, smooth_k=_SAGE_SMOOTH_K, qk_quant=qk_quant,
+                      granularity="per_token", pv_quant="bf16")
+    delta = torch.empty(BH, N, dtype=torch.float32, device=q.device)
+    L.call("fd_sage_attn_bwd_prepass", L.ptr(dof), L.ptr(of), L.ptr(delta), BH, N, L.stream_ptr(q.device))
+    if _SAGE_SMOOTH_K:
+        ks = (kf - qz["k_mean"].to(torch.bfloat16).unsqueeze(1)).contiguous()
+    else:
+        ks = kf
+    dq = torch.empty_like(qf)
+    dk = torch.empty_like(qf)
+    dv = torch.empty_like(qf)
+    L.call(
+        "fd_sage_attn_bwd", L.ptr(qf), L.ptr(ks), L.ptr(vf), L.ptr(dof), L.ptr(lse), L.ptr(delta),
+        L.ptr(qz["q_codes"]), L.ptr(qz["q_desc"]), L.ptr(qz["k_codes"]), L.ptr(qz["k_desc"]),
+        L.ptr(bm), bm_stride, L.ptr(dq), L.ptr(dk), L.ptr(dv), BH, N, qz["qk"], float(sm_scale),
+        L.stream_ptr(q.device),
+    )
+    return dq.reshape(B, H, N, D), dk.reshape(B, H, N, D), dv.reshape(B, H, N, D)
+
+
+def sage_attn_backward(
+    q: Tensor, k: Tensor, v: Tensor, out: Tensor, lse: Tensor, dout: Tensor, sm_scale: float,
+) -> tuple[Tensor, Tensor, Tensor]:
+    """dQ, dK, dV with the forward's quantised P recomputation (reference :344-458)."""
+    return _attn_backward(q, k, v, out, lse, dout, sm_scale, None, _SAGE_QK_QUANT)
+
+
+def sage_attn_backward_masked(
+    q: Tensor, k: Tensor, v: Tensor, out: Tensor, lse: Tensor, dout: Tensor, block_mask: Tensor,
+    sm_scale: float,
+) -> tuple[Tensor, Tensor, Tensor]:
+    """Masked backward, INT8 recompute (reference :534-648)."""
+    return _attn_backward(q, k, v, out, lse, dout, sm_scale, block_mask, "int8")
+
+
+def smoke_test_fp8_dot(n: int = 128) -> dict:
+    """FP8 per-row quantised dot check on this GPU (reference :90-118).
+
+    Quantises two random (n, n) bf16 matrices per row with the G1 quantiser
+    (one 128-wide block per row) and multiplies them on the tcgen05 GEMM.
+    """
+    _check_sm_capability()
+    from .fp8_kernels import fp8_act_quant, fp8_gemm_blockwise
+
+    assert n % 128 == 0
+    a = torch.randn(n, n, dtype=torch.bfloat16, device="cuda")
+    b = torch.randn(n, n, dtype=torch.bfloat16, device="cuda")
+    a8, a_s = fp8_act_quant(a)
+    b8, b_s_rows = fp8_act_quant(b)
+    # per-row B scales act as rowwise weight scales when n == 128
+    from .fp8_kernels import fp8_gemm_rowwise
+
+    if n == 128:
+        c = fp8_gemm_rowwise(a8, a_s, b8, b_s_rows.reshape(-1).contiguous())
+    else:
+        c = fp8_gemm_blockwise(a8, a_s, b8, torch.ones(n // 128, n // 128, device="cuda"))
+    ref = a.float() @ b.float().T
+    c_f32 = c.float()
+    cos_sim = torch.nn.functional.cosine_similarity(c_f32.flatten().unsqueeze(0), ref.flatten().unsqueeze(0)).item()
+    return {"cosine_similarity": cos_sim, "max_error": (c_f32 - ref).abs().max().item()}
+
+
+# ---------------------------------------------------------------------------
+# custom ops (reference :650-807)
+# ---------------------------------------------------------------------------
+
+_USE_CUSTOM_OP = True
+_USE_MASKED_CUSTOM_OP = True
+
+
+@torch.library.custom_op("futudiffu::sage_attn", mutates_args=())
+def sage_attn_op(q: Tensor, k: Tensor, v: Tensor, sm_scale: float) -> tuple[Tensor, Tensor]:
+    """SageAttention forward: returns (output, lse) for backward."""
+    return sage_attn_forward_with_lse(q, k, v, sm_scale)
+
+
+@sage_attn_op.register_fake
+def _sage_attn_op_fake(q, k, v, sm_scale):
+    B, H, N, D = q.shape
+    return q.new_empty(B, H, N, D), q.new_empty(B * H, N, dtype=torch.float32)
+
+
+def _setup_context(ctx, inputs, output):
+    q, k, v, sm_scale = inputs
+    out, lse = output
+    ctx.save_for_backward(q, k, v, out, lse)
+    ctx.sm_scale = sm_scale
+
+
+def _backward(ctx, grad_out, grad_lse):
+    q, k, v, out, lse = ctx.saved_tensors
+    dq, dk, dv = sage_attn_backward(q, k, v, out, lse, grad_out, ctx.sm_scale)
+    return dq, dk, dv, None
+
+
+sage_attn_op.register_autograd(_backward, setup_context=_setup_context)
+
+
+@torch.library.custom_op("futudiffu::sage_attn_masked", mutates_args=())
+def sage_attn_masked_op(
+    q: Tensor, k: Tensor, v: Tensor, block_mask: Tensor, sm_scale: float
+) -> tuple[Tensor, Tensor]:
+    """Masked SageAttention forward: returns (output, lse) for backward."""
+    return sage_attn_forward_masked_with_lse(q, k, v, block_mask, sm_scale)
+
+
+@sage_attn_masked_op.register_fake
+def _sage_attn_masked_op_fake(q, k, v, block_mask, sm_scale):
+    B, H, N, D = q.shape
+    return q.new_empty(B, H, N, D), q.new_empty(B * H, N, dtype=torch.float32)
+
+
+def _masked_setup_context(ctx, inputs, output):
+    q, k, v, block_mask, sm_scale = inputs
+    out, lse = output
+    ctx.save_for_backward(q, k, v, out, lse, block_mask)
+    ctx.sm_scale = sm_scale
+
+
+def _masked_backward(ctx, grad_out, grad_lse):
+    q, k, v, out, lse, block_mask = ctx.saved_tensors
+    dq, dk, dv = sage_attn_backward_masked(q, k, v, out, lse, grad_out, block_mask, ctx.sm_scale)
+    return dq, dk, dv, None, None
+
+
+sage_attn_masked_op.register_autograd(_masked_backward, setup_context=_masked_setup_context)

@@ -1,0 +1,195 @@
+/*
+ * futudiffu_b200 C ABI.
+ *
+ * One shared library (futudiffu_b200/libfd_b200.so) exports these entry
+ * points.  Every function takes plain device pointers, sizes and a
+ * cudaStream_t passed as void*, launches asynchronously on that stream and
+ * returns an FD_* status code.  No function allocates device memory: the
+ * caller owns every buffer (the reference's Python wrappers allocate all
+ * outputs with torch before launching, and so does the Python layer here).
+ *
+ * Layouts and formulas follow the reference operator API of sqcu/futudiffu
+ * (cited per function as file:line in that project).  Tensors are
+ * row-major and contiguous unless a stride argument says otherwise.
+ *
+ * dtype codes follow the reference's custom-op encoding
+ * (src/futudiffu/fp8_kernels.py:1772-1776): 0 bf16, 1 f16, 2 f32, 3 e4m3.
+ */
+#ifndef FD_B200_H
+#define FD_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ---- status codes -------------------------------------------------------- */
+#define FD_OK 0
+#define FD_ERR_ARG 1         /* bad shape / alignment / null pointer          */
+#define FD_ERR_CUDA 2        /* a CUDA runtime or driver call failed          */
+#define FD_ERR_TIMEOUT 3     /* a device-side bounded wait expired            */
+#define FD_ERR_UNSUPPORTED 4 /* combination of options not built               */
+
+/* bits of the device-wide status word (fd_get_status) */
+#define FD_STATUS_TIMEOUT 1u
+#define FD_STATUS_BOUNDS 2u
+
+/* ---- dtype codes ---------------------------------------------------------- */
+#define FD_DT_BF16 0
+#define FD_DT_F16 1
+#define FD_DT_F32 2
+#define FD_DT_E4M3 3
+#define FD_DT_I8 4
+
+/* ---- attention option codes ------------------------------------------------ */
+#define FD_QK_INT8 0 /* INT8 codes, truncation toward zero (sage_kernels.py:632-639) */
+#define FD_QK_FP8 1  /* e4m3 codes, RNE (sage_kernels.py:151-155)                  */
+#define FD_GRAN_TOKEN 0 /* one scale per row (reference)                            */
+#define FD_GRAN_BLOCK 1 /* one scale per 128 Q rows / 64 K rows                      */
+#define FD_PV_BF16 0 /* bf16 P x bf16 V (sage_kernels.py:681-684)                     */
+#define FD_PV_FP8 1  /* e4m3 P (static scale) x e4m3 V (per-channel scale)            */
+
+/* Library version string and the last host-side error message (thread-local). */
+const char* fd_version(void);
+const char* fd_last_error(void);
+
+/* Read (and optionally clear) the device status word on the current device.
+ * Synchronises the device.  Returns FD_OK or FD_ERR_CUDA. */
+int fd_get_status(unsigned int* out, int clear);
+
+/* G1 -- fp8_act_quant (src/futudiffu/fp8_kernels.py:54-90).
+ * x (M, K) in x_dtype (bf16/f16/f32), K % block == 0, block == 128.
+ * y (M, K) e4m3; s (M, K/block) f32 with s = max(amax/448, 1e-12),
+ * y = e4m3_rne(clamp(x * (448 / max(amax, 1e-12)), -448, 448)). */
+int fd_fp8_act_quant(const void* x, int x_dtype, void* y, float* s, int64_t M, int64_t K,
+                     int block, void* stream);
+
+/* G6 -- quantize_fp8_blockwise (src/futudiffu/fp8.py:337-371).
+ * w (N, K) in w_dtype, N % block == 0, K % block == 0; y (N, K) e4m3;
+ * s (N/block, K/block) f32 holding 1 / (448 / max(amax, 1e-12)). */
+int fd_fp8_weight_quant(const void* w, int w_dtype, void* y, float* s, int64_t N, int64_t K,
+                        int block, void* stream);
+
+/* G6 -- dequantize_fp8_blockwise (src/futudiffu/fp8.py:452-480).
+ * out (N, K) in out_dtype = float(code) * s[n/block, k/block]. */
+int fd_fp8_dequant_blockwise(const void* w, const float* s, void* out, int out_dtype, int64_t N,
+                             int64_t K, int block, void* stream);
+
+/* G2 -- fp8_gemm_blockwise / fp8_addmm_blockwise / fp8_gemm_v1t
+ * (src/futudiffu/fp8_kernels.py:125-343, :1417-1699; op :1814-1841).
+ * a (M, K) e4m3, a_s (M, K/128) f32.
+ * b_layout 0: b (N, K) e4m3, b_s (ceil(N/128), K/128)   [fp8_gemm_blockwise]
+ * b_layout 1: b (K, N) e4m3, b_s (K/128, ceil(N/128))   [fp8_gemm_v1t]
+ * b_layout 2: b (N, K) e4m3, b_s (N,) per-row, applied after the K loop
+ *             [fp8_gemm_rowwise, fp8_kernels.py:349-414]
+ * c (M, N) in c_dtype (bf16/f16/f32) =
+ *   sum_k dot128(a, b)[m, n] * a_s[m, k] * b_s[n/128, k] (+ bias[n]).
+ * bias may be NULL; bias_dtype in {bf16, f16, f32}.  K % 128 == 0,
+ * N % 16 == 0.  Accumulation is fp32 with one promotion per 128-K slice. */
+int fd_fp8_gemm_blockwise(const void* a, const float* a_s, const void* b, const float* b_s,
+                          const void* bias, int bias_dtype, void* c, int c_dtype, int64_t M,
+                          int64_t N, int64_t K, int b_layout, void* stream);
+
+/* G4 -- fp8_silu_gate_quant (src/futudiffu/fp8_kernels.py:842-978).
+ * x (M, 2N) bf16 = [w1 | w3]; y (M, N) e4m3 = quant(silu(w1) * w3) per 1 x block,
+ * s (M, N/block) f32.  N % block == 0, block == 128. */
+int fd_fp8_silu_gate_quant(const void* x, void* y, float* s, int64_t M, int64_t N, int block,
+                           void* stream);
+
+/* GELU(tanh approximation) + 1 x block fp8 quantisation of a bf16 tensor
+ * (the MMDiT MLP activation; same quantiser formula as G1). */
+int fd_fp8_gelu_tanh_quant(const void* x, void* y, float* s, int64_t M, int64_t N, int block,
+                           void* stream);
+
+/* fp8_gelu (src/futudiffu/fp8_kernels.py:716-833): dequant -> erf-GELU -> requant.
+ * x (M, N) e4m3 with sx (M, N/block); y (M, N) e4m3 with sy (M, N/block). */
+int fd_fp8_gelu_requant(const void* x, const float* sx, void* y, float* sy, int64_t M, int64_t N,
+                        int block, void* stream);
+
+/* P1 -- fused_rms_norm_modulate (src/futudiffu/fused_kernels.py:43-86, :155-197).
+ * x (B, S, dim) bf16; w (dim) in w_dtype; scale (B, dim) in scale_dtype;
+ * out (B, S, dim) bf16 = rmsnorm(x) * w * (1 + scale[b]). */
+int fd_rms_norm_modulate(const void* x, const void* w, int w_dtype, const void* scale,
+                         int scale_dtype, void* out, int64_t B, int64_t S, int64_t dim, float eps,
+                         void* stream);
+
+/* P2 -- fused_rms_norm_gate_residual (src/futudiffu/fused_kernels.py:99-148, :200-247).
+ * out = residual + tanh(gate[b]) * rmsnorm(x) * w. */
+int fd_rms_norm_gate_residual(const void* x, const void* w, int w_dtype, const void* gate,
+                              int gate_dtype, const void* residual, void* out, int64_t B,
+                              int64_t S, int64_t dim, float eps, void* stream);
+
+/* P3 -- fused_qkv_postprocess (src/futudiffu/fused_kernels.py:270-471).
+ * qkv (B*S, 3*H*hd) bf16; qw, kw (hd) f32; freqs (B*S, hd/2, 2, 2) f32;
+ * oq, ok, ov (B, H, S, hd) bf16.  hd == 128. */
+int fd_qkv_postprocess(const void* qkv, const float* qw, const float* kw, const float* freqs,
+                       void* oq, void* ok, void* ov, int64_t B, int64_t S, int64_t H, int64_t hd,
+                       float eps, void* stream);
+
+/* A1..A4 -- attention quantisation prologue.
+ * Replaces _smooth_k (src/futudiffu/sage_attention.py:63-71) and the in-kernel
+ * Q/K quantisation of the attention kernels (sage_kernels.py:632-639,
+ * :656-663 int8; :151-155, :176-179 fp8) plus V quantisation (:1146-1151).
+ * q, k, v: (BH, N, 128) bf16.
+ *  smooth_k: subtract the bf16-rounded per-(bh, d) mean over N from K,
+ *            rounding the difference to bf16 (torch bf16 semantics).
+ *  qk_kind:  FD_QK_INT8 / FD_QK_FP8.
+ *  q_gran / k_gran: FD_GRAN_TOKEN (per row) or FD_GRAN_BLOCK (128 Q rows,
+ *            64 K rows).
+ *  pv_kind:  FD_PV_BF16 (v_codes/v_desc unused) or FD_PV_FP8 (V -> e4m3 with
+ *            one scale per (bh, d) over the whole sequence).
+ * Outputs: q_codes/k_codes (BH, N, 128) int8|e4m3; q_desc (BH, nq) f32 with
+ * sm_scale_log2e folded in (nq = N or ceil(N/128)); k_desc (BH, nk) f32
+ * (nk = N or ceil(N/64)); v_codes (BH, N, 128) e4m3; v_desc (BH, 128) f32;
+ * k_mean (BH, 128) f32 (the bf16-rounded mean, for inspection; may be NULL).
+ * workspace: f32 scratch of fd_attn_quant_workspace_floats(BH, N) elements. */
+int64_t fd_attn_quant_workspace_floats(int64_t BH, int64_t N);
+int fd_attn_quant(const void* q, const void* k, const void* v, int64_t BH, int64_t N,
+                  int smooth_k, int qk_kind, int q_gran, int k_gran, int pv_kind,
+                  float sm_scale_log2e, void* q_codes, float* q_desc, void* k_codes,
+                  float* k_desc, void* v_codes, float* v_desc, float* k_mean, float* workspace,
+                  void* stream);
+
+/* A5/A6 -- quantized attention forward
+ * (production kernel _sage_attn_fwd_int8qk_bf16pv_masked_lse,
+ *  src/futudiffu/sage_kernels.py:1379-1477, and its unmasked / fp8 siblings).
+ * Consumes the prologue outputs.  v is bf16 (BH, N, 128) when pv_kind ==
+ * FD_PV_BF16, else the e4m3 codes with v_desc.  block_mask: uint8
+ * (ceil(N/128), ceil(N/64)) per head at mask_bh_stride bytes (0 = broadcast),
+ * or NULL.  out (BH, N, 128) bf16; lse (BH, N) f32 in log2 units (may be NULL). */
+int fd_sage_attn_fwd(const void* q_codes, const float* q_desc, const void* k_codes,
+                     const float* k_desc, const void* v, const float* v_desc,
+                     const uint8_t* block_mask, int64_t mask_bh_stride, void* out, float* lse,
+                     int64_t BH, int64_t N, int qk_kind, int q_gran, int k_gran, int pv_kind,
+                     void* stream);
+
+/* A7 -- attention backward, Delta pre-pass (sage_kernels.py:322-349):
+ * delta (BH, N) f32 = rowsum(dO * O). */
+int fd_sage_attn_bwd_prepass(const void* dout, const void* out, float* delta, int64_t BH,
+                             int64_t N, void* stream);
+
+/* A7 -- attention backward (sage_kernels.py:805-1015 int8, :1491-1722 masked int8,
+ * :356-567 fp8).  Recomputes P = exp2(S - lse) from the same per-token Q/K
+ * codes the forward used, then dV = P^T dO, dS = P (dO V^T - delta),
+ * dK = sm_scale dS^T Q, dQ = sm_scale dS K, all with bf16 operands and fp32
+ * accumulation.  q, k (smoothed), v, dout: (BH, N, 128) bf16. */
+int fd_sage_attn_bwd(const void* q, const void* k, const void* v, const void* dout,
+                     const float* lse, const float* delta, const void* q_codes,
+                     const float* q_desc, const void* k_codes, const float* k_desc,
+                     const uint8_t* block_mask, int64_t mask_bh_stride, void* dq, void* dk,
+                     void* dv, int64_t BH, int64_t N, int qk_kind, float sm_scale, void* stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FD_B200_H */

@@ -1,0 +1,150 @@
+"""Generate the golden fixtures in this directory from the reference itself.
+
+Runs the reference project's (sqcu/futudiffu) own CPU-runnable code on seeded
+inputs and stores inputs and outputs as ``.pt`` files:
+
+  smooth_k.pt          futudiffu.sage_attention._smooth_k           (sage_attention.py:63-71)
+  block_mask.pt        src_ii.block_mask.build_block_mask            (block_mask.py:35-99)
+  dequant.pt           futudiffu.fp8.dequantize_fp8_blockwise        (fp8.py:452-480)
+  weight_quant.pt      futudiffu.fp8.quantize_fp8_blockwise          (fp8.py:337-371),
+                       its CUDA transfer replaced by an identity so it runs on the CPU
+  act_quant_scales.pt  futudiffu.fp8_kernels.fp8_act_quant (Triton kernel under the
+                       Triton CPU interpreter; only the scales are kept -- the
+                       interpreter's fp8 cast is not round-to-nearest-even)
+  silu_gate.pt         fp8_silu_gate_quant torch fallback            (fp8_kernels.py:1725-1747)
+  fused_norms.pt       fused_kernels torch fallbacks + _qkv_postprocess_reference
+                       (fused_kernels.py:479-541, :802-842) and attention.rope_embed
+
+Usage:  python tests/golden/make_golden.py --reference <path to the reference checkout>
+
+The reference is needed only to regenerate; tests read the stored files.
+Sections that need Triton blocked run in a child process of this script.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib.abc
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import torch
+
+HERE = Path(__file__).resolve().parent
+
+
+class _BlockTriton(importlib.abc.MetaPathFinder):
+    def find_spec(self, name, path, target=None):
+        if name == "triton" or name.startswith("triton."):
+            raise ImportError("triton blocked for fallback capture")
+        return None
+
+
+def _gen(seed: int) -> torch.Generator:
+    return torch.Generator().manual_seed(seed)
+
+
+def main_triton(ref: Path) -> None:
+    sys.path.insert(0, str(ref / "src"))
+    sys.path.insert(0, str(ref))
+    from futudiffu.sage_attention import _smooth_k
+    from futudiffu import fp8 as rfp8
+    from src_ii.block_mask import build_block_mask
+
+    # ---- smooth_k: bf16 K with a per-channel offset (std 2) over (B, H, N, D)
+    g = _gen(0)
+    k = torch.randn(2, 3, 200, 128, generator=g, dtype=torch.float32)
+    k = (k + 2.0 * torch.randn(128, generator=g)).to(torch.bfloat16)
+    torch.save({"k": k, "ks": _smooth_k(k)}, HERE / "smooth_k.pt")
+
+    # ---- block masks, including a padding tail that keeps document id 0
+    cases = [([128, 256, 64], None), ([100, 160, 40], None), ([4288], None), ([1000, 2000], 3100),
+             ([2144, 2144], 4288), ([96, 32, 200, 72], None)]
+    masks = [build_block_mask(seg, total_len=tl, device="cpu") for seg, tl in cases]
+    torch.save({"cases": cases, "masks": masks}, HERE / "block_mask.pt")
+
+    # ---- dequantize_fp8_blockwise on random codes / scales
+    g = _gen(1)
+    codes = (torch.randn(256, 384, generator=g) * 100).clamp(-448, 448).to(torch.float8_e4m3fn)
+    scales = torch.rand(2, 3, generator=g) * 0.01 + 1e-4
+    torch.save({"codes": codes, "scales": scales,
+                "out": rfp8.dequantize_fp8_blockwise(codes, scales)}, HERE / "dequant.pt")
+
+    # ---- quantize_fp8_blockwise with the device transfer made an identity
+    g = _gen(2)
+    w = (torch.randn(256, 384, generator=g) * 0.02).to(torch.bfloat16)
+    w[0:128, 128:256] = 0.0  # an all-zero tile exercises the 1e-12 clamp
+    saved = torch.Tensor.cuda
+    torch.Tensor.cuda = lambda self, *a, **kw: self  # type: ignore[assignment]
+    try:
+        q, s = rfp8.quantize_fp8_blockwise(w)
+    finally:
+        torch.Tensor.cuda = saved  # type: ignore[assignment]
+    torch.save({"w": w, "codes": q, "scales": s}, HERE / "weight_quant.pt")
+
+    # ---- fp8_act_quant Triton kernel in the CPU interpreter: scales only
+    env = dict(os.environ, TRITON_INTERPRET="1")
+    subprocess.run([sys.executable, __file__, "--reference", str(ref), "--section", "interp"],
+                   check=True, env=env)
+    # ---- torch fallbacks (Triton blocked)
+    subprocess.run([sys.executable, __file__, "--reference", str(ref), "--section", "fallback"],
+                   check=True)
+
+
+def main_interp(ref: Path) -> None:
+    sys.path.insert(0, str(ref / "src"))
+    from futudiffu.fp8_kernels import fp8_act_quant
+
+    g = _gen(3)
+    x = (torch.randn(16, 512, generator=g) * torch.rand(16, 1, generator=g) * 10).to(torch.bfloat16)
+    x[3, 128:256] = 0.0
+    _, s = fp8_act_quant(x)
+    torch.save({"x": x, "scales": s}, HERE / "act_quant_scales.pt")
+
+
+def main_fallback(ref: Path) -> None:
+    sys.meta_path.insert(0, _BlockTriton())
+    sys.path.insert(0, str(ref / "src"))
+    from futudiffu import fp8_kernels as rk
+    from futudiffu import fused_kernels as rf
+    from futudiffu.attention import rope_embed
+
+    assert not rk._HAS_TRITON and not rf._HAS_TRITON
+    g = _gen(4)
+    x = (torch.randn(8, 2 * 256, generator=g) * 2).to(torch.bfloat16)
+    y, s = rk.fp8_silu_gate_quant(x)
+    torch.save({"x": x, "codes": y, "scales": s}, HERE / "silu_gate.pt")
+
+    g = _gen(5)
+    B, S, H, hd = 2, 40, 4, 128
+    dim = H * hd
+    xn = torch.randn(B, S, dim, generator=g).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(dim, generator=g)).to(torch.bfloat16)
+    scale = (0.5 * torch.randn(B, dim, generator=g)).to(torch.bfloat16)
+    gate = torch.randn(B, dim, generator=g).to(torch.bfloat16)
+    res = torch.randn(B, S, dim, generator=g).to(torch.bfloat16)
+    mod = rf._fused_rms_norm_modulate_fallback(xn, w, scale, 1e-5)
+    gr = rf._fused_rms_norm_gate_residual_fallback(xn, w, gate, res, 1e-5)
+    qkv = torch.randn(B, S, 3 * dim, generator=g).to(torch.bfloat16)
+    qw = 1 + 0.1 * torch.randn(hd, generator=g)
+    kw = 1 + 0.1 * torch.randn(hd, generator=g)
+    pos = torch.zeros(S, 3)
+    pos[:, 0] = 1.0
+    pos[:, 1] = (torch.arange(S) % 7).float()
+    pos[:, 2] = (torch.arange(S) // 7).float()
+    freqs = torch.cat([rope_embed(pos[None, :, i], d, 256.0) for i, d in enumerate((32, 48, 48))], dim=-3)
+    freqs = freqs.expand(B, S, hd // 2, 2, 2).unsqueeze(2).contiguous()
+    q_ref, k_ref, v_ref = rf._qkv_postprocess_reference(qkv, qw, kw, freqs, H, hd, 1e-5)
+    torch.save({"x": xn, "w": w, "scale": scale, "gate": gate, "res": res, "modulate": mod,
+                "gate_residual": gr, "qkv": qkv, "qw": qw, "kw": kw, "freqs": freqs,
+                "q": q_ref, "k": k_ref, "v": v_ref, "H": H, "hd": hd}, HERE / "fused_norms.pt")
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, type=Path)
+    ap.add_argument("--section", default="main", choices=["main", "interp", "fallback"])
+    a = ap.parse_args()
+    {"main": main_triton, "interp": main_interp, "fallback": main_fallback}[a.section](a.reference)

@@ -1,0 +1,110 @@
+"""Host-side API behaviour that needs no GPU: config validation, error types,
+no-CPU-fallback guarantee, fake-tensor shapes of the custom ops (CPU only)."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+
+def test_configure_sage_validation():
+    from futudiffu_b200 import sage_attention as SA
+
+    with pytest.raises(ValueError):
+        SA.configure_sage(qk_quant="int4")
+    with pytest.raises(ValueError):
+        SA.configure_sage(pv_quant="fp16")
+    with pytest.raises(ValueError):
+        SA.configure_sage(qk_granularity="per_head")
+    SA.configure_sage(smooth_k=False, qk_quant="int8", pv_quant="fp8", qk_granularity="per_block")
+    assert SA.get_sage_config() == {"smooth_k": False, "qk_quant": "int8", "pv_quant": "fp8",
+                                    "qk_granularity": "per_block"}
+    SA.configure_sage()
+    assert SA.get_sage_config()["qk_quant"] == "fp8"
+
+
+def test_set_attention_backend_validation():
+    from futudiffu_b200 import attention as A
+
+    with pytest.raises(ValueError):
+        A.set_attention_backend("flash")
+    A.set_attention_backend("auto")
+    assert A.get_attention_backend() == "auto"
+    A.set_attention_backend("sdpa")
+
+
+def test_no_cpu_fallback():
+    from futudiffu_b200.fp8_kernels import fp8_act_quant, fp8_gemm_blockwise
+    from futudiffu_b200.fused_kernels import fused_rms_norm_modulate
+    from futudiffu_b200.sage_attention import sage_attn_forward
+
+    x = torch.zeros(4, 256, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        fp8_act_quant(x)
+    a8 = torch.zeros(4, 256, dtype=torch.float8_e4m3fn)
+    with pytest.raises(RuntimeError):
+        fp8_gemm_blockwise(a8, torch.ones(4, 2), torch.zeros(128, 256, dtype=torch.float8_e4m3fn), torch.ones(1, 2))
+    with pytest.raises(RuntimeError):
+        fused_rms_norm_modulate(torch.zeros(1, 2, 128, dtype=torch.bfloat16), torch.ones(128), torch.zeros(1, 128))
+    q = torch.zeros(1, 1, 128, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        sage_attn_forward(q, q, q)
+
+
+def test_sage_asserts_match_reference():
+    from futudiffu_b200.sage_attention import sage_attn_forward
+
+    with pytest.raises(AssertionError):
+        sage_attn_forward(*(torch.zeros(1, 1, 16, 64, dtype=torch.bfloat16),) * 3)
+    with pytest.raises(AssertionError):
+        sage_attn_forward(*(torch.zeros(1, 1, 16, 128, dtype=torch.float16),) * 3)
+
+
+def test_fake_tensor_shapes():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    import futudiffu_b200.fp8  # noqa: F401  (registers futudiffu::fp8_linear*)
+    import futudiffu_b200.fused_kernels  # noqa: F401
+    import futudiffu_b200.sage_attention  # noqa: F401
+
+    with FakeTensorMode():
+        q = torch.empty(2, 3, 256, 128, dtype=torch.bfloat16)
+        out, lse = torch.ops.futudiffu.sage_attn(q, q, q, 0.1)
+        assert out.shape == (2, 3, 256, 128) and lse.shape == (6, 256) and out.is_contiguous()
+        m = torch.empty(2, 4, dtype=torch.uint8)
+        out, lse = torch.ops.futudiffu.sage_attn_masked(q, q, q, m, 0.1)
+        assert out.shape == (2, 3, 256, 128)
+        x = torch.empty(2, 7, 512, dtype=torch.bfloat16)
+        w = torch.empty(1024, 512, dtype=torch.float8_e4m3fn)
+        ws = torch.empty(8, 4)
+        y = torch.ops.futudiffu.fp8_linear(x, w, ws, 128, 0)
+        assert y.shape == (2, 7, 1024) and y.dtype == torch.bfloat16
+        y = torch.ops.futudiffu.fp8_linear_bias(x, w, ws, torch.empty(1024), 128, 2)
+        assert y.dtype == torch.float32
+        g, s = torch.ops.futudiffu.fp8_silu_gate_quant(torch.empty(5, 512, dtype=torch.bfloat16), 128, 3)
+        assert g.shape == (5, 256) and s.shape == (5, 2)
+        qkv = torch.empty(2, 9, 3 * 4 * 128, dtype=torch.bfloat16)
+        oq, ok, ov = torch.ops.futudiffu.fused_qkv_postprocess(qkv, torch.empty(128), torch.empty(128),
+                                                              torch.empty(2, 9, 1, 64, 2, 2), 4, 128, 1e-5)
+        assert oq.shape == (2, 4, 9, 128)
+
+
+def test_block_mask_on_cpu_device():
+    from futudiffu_b200.block_mask import build_block_mask
+
+    m = build_block_mask([128, 128], device="cpu")
+    assert m.shape == (2, 4) and m.dtype == torch.uint8
+    assert m.tolist() == [[1, 1, 0, 0], [0, 0, 1, 1]]
+
+
+def test_fp8_linear_replacement_logic():
+    import torch.nn as nn
+
+    from futudiffu_b200.fp8 import FP8Linear, replace_linear_with_fp8
+
+    model = nn.Sequential(nn.Linear(256, 128), nn.Sequential(nn.Linear(128, 256)))
+    sd = {"0.weight": torch.zeros(128, 256, dtype=torch.float8_e4m3fn), "0.weight_scale": torch.ones(1, 2),
+          "1.0.weight": torch.zeros(256, 128)}
+    replace_linear_with_fp8(model, sd)
+    assert isinstance(model[0], FP8Linear) and isinstance(model[1][0], nn.Linear)
+    assert model[0].in_features == 256 and model[0].out_features == 128

@@ -1,0 +1,215 @@
+"""GPU parity: attention quantisation prologue (bit-exact) and tcgen05 attention vs the oracle."""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+from oracle import attention as OA
+from oracle import block_mask as OB
+from tests.conftest import gen
+from tests.helpers import cosine, e4m3_bits
+
+pytestmark = pytest.mark.gpu
+
+SM = 1.0 / math.sqrt(128)
+
+
+def qkv(BH, N, seed, koff=2.0):
+    g = gen(seed)
+    q = torch.randn(BH, N, 128, generator=g).to(torch.bfloat16)
+    k = (torch.randn(BH, N, 128, generator=g) + koff * torch.randn(128, generator=g)).to(torch.bfloat16)
+    v = torch.randn(BH, N, 128, generator=g).to(torch.bfloat16)
+    return q, k, v
+
+
+@pytest.fixture(autouse=True)
+def _reset_sage():
+    from futudiffu_b200 import sage_attention as SA
+
+    yield
+    SA.configure_sage()
+
+
+@pytest.mark.parametrize("qk", ["int8", "fp8"])
+@pytest.mark.parametrize("gran", ["per_token", "per_block"])
+@pytest.mark.parametrize("N", [64, 200, 1024, 4288])
+def test_prologue_codes_bit_exact(cuda_device, qk, gran, N):
+    from futudiffu_b200.sage_attention import quantize_qkv
+
+    q, k, v = qkv(3, N, N)
+    qz = quantize_qkv(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), SM, smooth_k=True,
+                      qk_quant=qk, granularity=gran, pv_quant="fp8")
+    # smoothing mean: bf16-rounded, within one bf16 ulp of torch's
+    km_ref = k.float().mean(dim=1).to(torch.bfloat16).float()
+    km = qz["k_mean"].cpu()
+    assert ((km - km_ref).abs() <= km_ref.abs() * 2**-7 + 1e-30).all()
+    # codes and scales bit-exact given the kernel's mean
+    ks = OA.smooth_k_with_mean(k, km.to(torch.bfloat16))
+    rq, rk = (1, 1) if gran == "per_token" else (128, 64)
+    qc, qd = OA.quant_rows(q, qk, rq, SM * OA.LOG2E)
+    kc, kd = OA.quant_rows(ks, qk, rk)
+    bits = (lambda t: t.cpu().view(torch.uint8)) if qk == "fp8" else (lambda t: t.cpu())
+    assert torch.equal(bits(qz["q_codes"]), bits(qc))
+    assert torch.equal(bits(qz["k_codes"]), bits(kc))
+    assert torch.equal(qz["q_desc"].cpu()[:, :qd.shape[1]], qd)
+    assert torch.equal(qz["k_desc"].cpu()[:, :kd.shape[1]], kd)
+    vc, vd = OA.quant_v_per_channel(v)
+    assert torch.equal(e4m3_bits(qz["v_codes"]), e4m3_bits(vc))
+    assert torch.equal(qz["v_desc"].cpu(), vd)
+
+
+def test_prologue_deterministic(cuda_device):
+    from futudiffu_b200.sage_attention import quantize_qkv
+
+    q, k, v = (t.to(cuda_device) for t in qkv(4, 3000, 1))
+    a = quantize_qkv(q, k, v, SM, smooth_k=True, qk_quant="int8", granularity="per_token", pv_quant="fp8")
+    b = quantize_qkv(q, k, v, SM, smooth_k=True, qk_quant="int8", granularity="per_token", pv_quant="fp8")
+    for key in ("q_codes", "k_codes", "q_desc", "k_desc", "v_desc", "k_mean"):
+        assert torch.equal(a[key], b[key]), key
+
+
+# (qk_quant, granularity, pv_quant for the API, oracle pv mode, min cosine vs oracle)
+MODES = [
+    ("int8", "per_token", "bf16", "bf16", 0.9995),
+    ("fp8", "per_token", "bf16", "bf16", 0.9995),
+    ("int8", "per_block", "bf16", "bf16", 0.9995),
+    ("int8", "per_block", "fp8", "fp8_channel", 0.9995),
+    ("fp8", "per_block", "fp8", "fp8_channel", 0.9995),
+]
+
+
+def _run(q, k, v, dev, qk, gran, pv, mask=None, lse=True):
+    from futudiffu_b200 import sage_attention as SA
+
+    SA.configure_sage(smooth_k=True, qk_quant=qk, pv_quant=pv, qk_granularity=gran)
+    d = lambda t: t.to(dev)  # noqa: E731
+    B = 1
+    q4, k4, v4 = (d(t).unsqueeze(0) for t in (q, k, v))
+    if mask is not None:
+        out, l = SA._attn_forward(q4, k4, v4, SM, block_mask=d(mask), qk_quant=qk, pv_quant=pv,
+                                  granularity=gran, want_lse=True)
+    else:
+        out, l = SA._attn_forward(q4, k4, v4, SM, block_mask=None, qk_quant=qk, pv_quant=pv,
+                                  granularity=gran, want_lse=True)
+    return out[0].cpu(), l.cpu()
+
+
+@pytest.mark.parametrize("mode", MODES, ids=lambda m: "-".join(m[:3]))
+@pytest.mark.parametrize("BH,N", [(2, 128), (3, 200), (2, 1024), (1, 4288)])
+def test_attention_vs_oracle(cuda_device, mode, BH, N):
+    qk, gran, pv, opv, tol = mode
+    q, k, v = qkv(BH, N, BH * N)
+    out, lse = _run(q, k, v, cuda_device, qk, gran, pv)
+    ref, rlse = OA.attention_forward(q, k, v, sm_scale=SM, qk_quant=qk, granularity=gran, pv_quant=opv)
+    assert torch.isfinite(out.float()).all()
+    c = cosine(out, ref)
+    assert c >= tol, c
+    err = (out.float() - ref.float()).abs().max().item()
+    assert err <= 0.05 * ref.float().abs().max().item() + 0.02, err
+    assert torch.allclose(lse, rlse, rtol=0, atol=2e-3 * max(1.0, rlse.abs().max().item()))
+
+
+def test_attention_fp8_pv_reference_tile_mode(cuda_device):
+    # reference A4 (per-64-key-tile P/V scales) vs this build's per-channel V: tolerance gate
+    q, k, v = qkv(2, 1024, 7)
+    out, _ = _run(q, k, v, cuda_device, "fp8", "per_token", "fp8")
+    ref, _ = OA.attention_forward(q, k, v, sm_scale=SM, qk_quant="fp8", pv_quant="fp8_tile")
+    assert cosine(out, ref) >= 0.999
+
+
+def test_attention_close_to_exact(cuda_device):
+    q, k, v = qkv(2, 2048, 3)
+    exact = OA.attention_exact(q, k, v, SM)
+    out, _ = _run(q, k, v, cuda_device, "int8", "per_block", "fp8")
+    assert cosine(out, exact) >= 0.998
+    out, _ = _run(q, k, v, cuda_device, "int8", "per_token", "bf16")
+    assert cosine(out, exact) >= 0.9995
+
+
+@pytest.mark.parametrize("segs,total", [([128, 256, 64], None), ([100, 160, 40], None), ([1000, 2000], 3100),
+                                        ([2144, 2144], 4288)])
+def test_attention_block_mask(cuda_device, segs, total):
+    N = total or sum(segs)
+    mask = torch.from_numpy(OB.build_block_mask(segs, total))
+    q, k, v = qkv(2, N, N)
+    for qk, gran, pv, opv, _ in (MODES[0], MODES[3]):
+        out, lse = _run(q, k, v, cuda_device, qk, gran, pv, mask=mask)
+        ref, rlse = OA.attention_forward(q, k, v, sm_scale=SM, qk_quant=qk, granularity=gran,
+                                         pv_quant=opv, block_mask=mask)
+        assert cosine(out, ref) >= 0.9995
+        assert torch.allclose(lse, rlse, atol=5e-3)
+
+
+def test_attention_mask_3d_and_fully_masked_rows(cuda_device):
+    N = 256
+    q, k, v = qkv(2, N, 11)
+    mask = torch.ones(2, 2, 4, dtype=torch.uint8)
+    mask[1, 1, :] = 0  # head 1, q block 1 sees nothing -> NaN output, -inf lse
+    mask[0, 0, 2:] = 0
+    out, lse = _run(q, k, v, cuda_device, "int8", "per_token", "bf16", mask=mask)
+    ref, rlse = OA.attention_forward(q, k, v, sm_scale=SM, qk_quant="int8", block_mask=mask)
+    assert torch.isnan(out[1, 128:].float()).all()
+    assert torch.isneginf(lse[1, 128:]).all()
+    good = torch.ones(2, N, dtype=torch.bool)
+    good[1, 128:] = False
+    assert cosine(out[good], ref[good]) >= 0.9995
+
+
+def test_attention_public_api(cuda_device):
+    from futudiffu_b200 import sage_attention as SA
+    from futudiffu_b200.attention import sdpa_attention, set_attention_backend
+
+    B, H, N = 2, 3, 256
+    g = gen(2)
+    q = torch.randn(B, H, N, 128, generator=g).to(torch.bfloat16).to(cuda_device)
+    k = torch.randn(B, H, N, 128, generator=g).to(torch.bfloat16).to(cuda_device)
+    v = torch.randn(B, H, N, 128, generator=g).to(torch.bfloat16).to(cuda_device)
+    SA.configure_sage(qk_quant="int8")
+    o1 = SA.sage_attn_forward(q, k, v)
+    o2, lse = SA.sage_attn_forward_with_lse(q, k, v)
+    o3, lse3 = SA.sage_attn_op(q, k, v, SM)
+    assert o1.shape == (B, H, N, 128) and lse.shape == (B * H, N)
+    assert torch.equal(o1, o2) and torch.equal(o2, o3) and torch.equal(lse, lse3)
+    set_attention_backend("sage")
+    try:
+        flat = sdpa_attention(q.transpose(1, 2).reshape(B, N, H * 128), k.transpose(1, 2).reshape(B, N, H * 128),
+                              v.transpose(1, 2).reshape(B, N, H * 128), heads=H)
+    finally:
+        set_attention_backend("sdpa")
+    assert torch.equal(flat, o3.transpose(1, 2).reshape(B, N, H * 128))
+
+
+def test_attention_deterministic(cuda_device):
+    q, k, v = qkv(4, 2048, 5)
+    a, la = _run(q, k, v, cuda_device, "int8", "per_block", "fp8")
+    b, lb = _run(q, k, v, cuda_device, "int8", "per_block", "fp8")
+    assert torch.equal(a, b) and torch.equal(la, lb)
+
+
+def test_attention_config2_full_size(cuda_device):
+    # B2 H24 S4096, K offset ~N(0, 4); all heads vs GPU fp32 softmax,
+    # two heads vs the CPU oracle
+    from futudiffu_b200 import sage_attention as SA
+
+    B, H, N = 2, 24, 4096
+    g = gen(2024)
+    q = torch.randn(B, H, N, 128, generator=g).to(torch.bfloat16)
+    k = (torch.randn(B, H, N, 128, generator=g) + 2.0 * torch.randn(128, generator=g)).to(torch.bfloat16)
+    v = torch.randn(B, H, N, 128, generator=g).to(torch.bfloat16)
+    SA.configure_sage(smooth_k=True, qk_quant="int8", pv_quant="fp8", qk_granularity="per_block")
+    out = SA.sage_attn_forward(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device))
+    qd, kd, vd = (t.to(cuda_device).float() for t in (q, k, v))
+    exact = torch.nn.functional.scaled_dot_product_attention(qd, kd, vd)
+    assert cosine(out, exact) >= 0.998
+    ref, _ = OA.attention_forward(q[0, :2].contiguous(), k[0, :2].contiguous(), v[0, :2].contiguous(),
+                                  sm_scale=SM, qk_quant="int8", granularity="per_block", pv_quant="fp8_channel")
+    assert cosine(out[0, :2].cpu(), ref) >= 0.9995
+
+
+def test_attention_status_clean(cuda_device):
+    from futudiffu_b200 import check_status
+
+    check_status()

@@ -1,0 +1,98 @@
+"""GPU parity: fused RMSNorm / adaLN / RoPE prologues vs the CPU oracle."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import fused as OF
+from tests.conftest import gen
+from tests.helpers import bf16_ulp_diff, cosine
+
+pytestmark = pytest.mark.gpu
+
+
+def _close(a, b):
+    # one rounding to bf16 in both; rsqrt/sum order may move the last bit
+    assert torch.allclose(a.float().cpu(), b.float(), rtol=2**-7, atol=2**-7)
+    assert cosine(a, b) > 0.99999
+
+
+@pytest.mark.parametrize("B,S,dim", [(1, 1, 128), (2, 40, 512), (1, 4608, 3072), (2, 4288, 3840), (3, 7, 8192)])
+@pytest.mark.parametrize("wdt", [torch.bfloat16, torch.float32])
+def test_rms_norm_modulate(cuda_device, B, S, dim, wdt):
+    from futudiffu_b200.fused_kernels import fused_rms_norm_modulate
+
+    g = gen(B * S + dim)
+    x = torch.randn(B, S, dim, generator=g).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(dim, generator=g)).to(wdt)
+    sc = (0.5 * torch.randn(B, dim, generator=g)).to(torch.bfloat16)
+    out = fused_rms_norm_modulate(x.to(cuda_device), w.to(cuda_device), sc.to(cuda_device), 1e-5)
+    _close(out, OF.rms_norm_modulate(x, w, sc))
+
+
+@pytest.mark.parametrize("B,S,dim", [(2, 40, 512), (1, 4608, 3072)])
+def test_rms_norm_gate_residual(cuda_device, B, S, dim):
+    from futudiffu_b200.fused_kernels import fused_rms_norm_gate_residual
+
+    g = gen(S)
+    x = torch.randn(B, S, dim, generator=g).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(dim, generator=g)).to(torch.bfloat16)
+    gt = torch.randn(B, dim, generator=g).to(torch.bfloat16)
+    r = torch.randn(B, S, dim, generator=g).to(torch.bfloat16)
+    d = lambda t: t.to(cuda_device)  # noqa: E731
+    out = fused_rms_norm_gate_residual(d(x), d(w), d(gt), d(r), 1e-5)
+    _close(out, OF.rms_norm_gate_residual(x, w, gt, r))
+
+
+def test_fused_golden(cuda_device, golden_dir):
+    from futudiffu_b200.fused_kernels import (
+        fused_qkv_postprocess,
+        fused_rms_norm_gate_residual,
+        fused_rms_norm_modulate,
+    )
+
+    d = torch.load(golden_dir / "fused_norms.pt")
+    c = lambda t: t.to(cuda_device)  # noqa: E731
+    mod = fused_rms_norm_modulate(c(d["x"]), c(d["w"]), c(d["scale"]), 1e-5)
+    assert bf16_ulp_diff(mod, d["modulate"]).max().item() <= 2
+    gr = fused_rms_norm_gate_residual(c(d["x"]), c(d["w"]), c(d["gate"]), c(d["res"]), 1e-5)
+    assert torch.allclose(gr.float().cpu(), d["gate_residual"].float(), rtol=2**-7, atol=2**-6)
+    q, k, v = fused_qkv_postprocess(c(d["qkv"]), c(d["qw"]), c(d["kw"]), c(d["freqs"]), d["H"], d["hd"], 1e-5)
+    assert torch.equal(v.cpu(), d["v"])
+    for a, b in ((q, d["q"]), (k, d["k"])):
+        for h in range(d["H"]):
+            assert cosine(a[:, h], b[:, h]) > 0.999
+
+
+@pytest.mark.parametrize("B,S,H", [(1, 3, 1), (2, 40, 4), (1, 4608, 24)])
+def test_qkv_postprocess(cuda_device, B, S, H):
+    from futudiffu_b200.attention import rope_embed
+    from futudiffu_b200.fused_kernels import fused_qkv_postprocess
+
+    hd = 128
+    g = gen(S * H)
+    qkv = torch.randn(B, S, 3 * H * hd, generator=g).to(torch.bfloat16)
+    qw = 1 + 0.1 * torch.randn(hd, generator=g)
+    kw = 1 + 0.1 * torch.randn(hd, generator=g)
+    pos = torch.stack([torch.zeros(S), (torch.arange(S) % 64).float(), (torch.arange(S) // 64).float()], -1)
+    freqs = torch.cat([rope_embed(pos[None, :, i], dd, 256.0) for i, dd in enumerate((32, 48, 48))], dim=-3)
+    freqs = freqs.expand(B, S, hd // 2, 2, 2).unsqueeze(2).contiguous()
+    c = lambda t: t.to(cuda_device)  # noqa: E731
+    q, k, v = fused_qkv_postprocess(c(qkv), c(qw), c(kw), c(freqs), H, hd, 1e-5)
+    rq, rk, rv = OF.qkv_postprocess(qkv, qw, kw, freqs, H, hd)
+    assert torch.equal(v.cpu(), rv)
+    _close(q, rq)
+    _close(k, rk)
+
+
+def test_fused_backward_runs(cuda_device):
+    from futudiffu_b200.fused_kernels import fused_rms_norm_modulate
+
+    x = torch.randn(1, 8, 256, device=cuda_device, dtype=torch.bfloat16, requires_grad=True)
+    w = torch.ones(256, device=cuda_device, dtype=torch.bfloat16)
+    s = torch.zeros(1, 256, device=cuda_device, dtype=torch.bfloat16)
+    fused_rms_norm_modulate(x, w, s).float().sum().backward()
+    ref_x = x.detach().float().requires_grad_(True)
+    (ref_x * torch.rsqrt((ref_x * ref_x).mean(-1, keepdim=True) + 1e-5)).sum().backward()
+    assert torch.allclose(x.grad.float(), ref_x.grad, rtol=2e-2, atol=2e-2)

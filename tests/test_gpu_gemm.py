@@ -1,0 +1,149 @@
+"""GPU parity: tcgen05 FP8 blockwise GEMM vs the CPU oracle (per-128-K promotion)."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import gemm as OG
+from oracle import quant as OQ
+from tests.conftest import gen
+from tests.helpers import cosine
+
+pytestmark = pytest.mark.gpu
+
+
+def _operands(M, N, K, seed, b_layout=0):
+    g = gen(seed)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+    a8, a_s = OQ.act_quant(x)
+    if b_layout == 2:
+        b8, bs = OQ.act_quant(w.reshape(-1, 128))  # per-row scale requires one group per row
+        b8 = b8.reshape(N, K)
+        bs = torch.rand(N, generator=g) * 1e-3 + 1e-4
+    else:
+        Np = (N + 127) // 128 * 128
+        wp = torch.nn.functional.pad(w.float(), (0, 0, 0, Np - N))
+        b8, bs = OQ.weight_quant(wp)
+        b8 = b8[:N].contiguous()
+        if b_layout == 1:
+            b8 = b8.t().contiguous()
+            bs = bs.t().contiguous()
+    return a8, a_s, b8, bs
+
+
+def _check(c, ref, tight=True):
+    cf, rf = c.float().cpu(), ref.float()
+    assert torch.isfinite(cf).all()
+    assert cosine(cf, rf) >= 0.99999
+    err = (cf - rf).abs().max().item()
+    bound = 2 ** -7 * rf.abs().max().item() + 1e-3
+    assert err <= bound, (err, bound)
+
+
+@pytest.mark.parametrize(
+    "M,N,K",
+    [(1, 128, 128), (128, 128, 128), (129, 256, 256), (100, 144, 384), (256, 3072, 3072),
+     (2048, 3072, 3072), (777, 1280, 1024), (4608, 512, 640)],
+)
+def test_gemm_blockwise(cuda_device, M, N, K):
+    from futudiffu_b200.fp8_kernels import fp8_gemm_blockwise
+
+    a8, a_s, b8, bs = _operands(M, N, K, M + N + K)
+    c = fp8_gemm_blockwise(a8.to(cuda_device), a_s.to(cuda_device), b8.to(cuda_device), bs.to(cuda_device))
+    assert c.dtype == torch.bfloat16 and c.shape == (M, N)
+    _check(c, OG.gemm_blockwise(a8, a_s, b8, bs))
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16])
+@pytest.mark.parametrize("bias_dtype", [None, torch.bfloat16, torch.float32])
+def test_addmm_dtypes(cuda_device, out_dtype, bias_dtype):
+    from futudiffu_b200.fp8_kernels import fp8_addmm_blockwise
+
+    M, N, K = 200, 384, 512
+    a8, a_s, b8, bs = _operands(M, N, K, 3)
+    bias = None if bias_dtype is None else torch.randn(N, generator=gen(4)).to(bias_dtype)
+    d = lambda t: None if t is None else t.to(cuda_device)  # noqa: E731
+    c = fp8_addmm_blockwise(d(a8), d(a_s), d(b8), d(bs), bias=d(bias), output_dtype=out_dtype)
+    assert c.dtype == out_dtype
+    _check(c, OG.gemm_blockwise(a8, a_s, b8, bs, bias=bias, out_dtype=torch.float32))
+
+
+def test_gemm_v1t_and_rowwise(cuda_device):
+    from futudiffu_b200.fp8_kernels import fp8_addmm_v1t, fp8_gemm_rowwise, fp8_gemm_v1t
+
+    M, N, K = 300, 512, 768
+    a8, a_s, b8, bs = _operands(M, N, K, 8, b_layout=1)
+    d = lambda t: t.to(cuda_device)  # noqa: E731
+    _check(fp8_gemm_v1t(d(a8), d(a_s), d(b8), d(bs)), OG.gemm_blockwise(a8, a_s, b8, bs, b_layout=1))
+    bias = torch.randn(N, generator=gen(2)).to(torch.bfloat16)
+    _check(fp8_addmm_v1t(d(a8), d(a_s), d(b8), d(bs), bias=d(bias)),
+           OG.gemm_blockwise(a8, a_s, b8, bs, bias=bias, b_layout=1))
+    a8, a_s, b8, bs = _operands(M, N, K, 9, b_layout=2)
+    _check(fp8_gemm_rowwise(d(a8), d(a_s), d(b8), d(bs)), OG.gemm_blockwise(a8, a_s, b8, bs, b_layout=2))
+
+
+def test_gemm_batched_input_and_quant(cuda_device):
+    from futudiffu_b200.fp8_kernels import fp8_act_quant, fp8_gemm_blockwise, fp8_gemm_quant
+
+    x = torch.randn(2, 65, 256, generator=gen(1)).to(torch.bfloat16).to(cuda_device)
+    w = (torch.randn(384, 256, generator=gen(2)) * 0.02)
+    b8, bs = OQ.weight_quant(w)
+    a8, a_s = fp8_act_quant(x)
+    c = fp8_gemm_blockwise(a8, a_s, b8.to(cuda_device), bs.to(cuda_device))
+    assert c.shape == (2, 65, 384)
+    ref = OG.gemm_blockwise(a8.cpu(), a_s.cpu(), b8, bs).reshape(2, 65, 384)
+    _check(c, ref)
+    q, qs = fp8_gemm_quant(a8, a_s, b8.to(cuda_device), bs.to(cuda_device))
+    assert q.shape == (2, 65, 384) and qs.shape == (2, 65, 3)
+    rq, rs = OQ.act_quant(OG.gemm_blockwise(a8.cpu(), a_s.cpu(), b8, bs, out_dtype=torch.float32))
+    assert cosine(q.float().cpu() * qs.cpu().repeat_interleave(128, -1), rq.float().reshape(2, 65, 384)
+                  * rs.reshape(2, 65, 3).repeat_interleave(128, -1)) > 0.999
+
+
+def test_fp8_linear_module(cuda_device):
+    from futudiffu_b200.fp8 import FP8Linear, quantize_fp8_blockwise_cuda
+
+    K, N = 512, 1024
+    w = (torch.randn(N, K, generator=gen(3)) * 0.02).to(cuda_device)
+    w8, ws = quantize_fp8_blockwise_cuda(w)
+    bias = torch.randn(N, generator=gen(4)).to(torch.bfloat16).to(cuda_device)
+    lin = FP8Linear(w8, ws, bias=bias)
+    x = torch.randn(2, 100, K, generator=gen(5)).to(torch.bfloat16).to(cuda_device)
+    out_op = lin(x)
+    out_eager = lin._forward_eager(x)
+    assert cosine(out_op, out_eager) > 0.9999  # reference test threshold (fp8.py:656)
+    assert torch.equal(out_op, out_eager)
+    ref = x.float() @ (w8.float() * ws.repeat_interleave(128, 0).repeat_interleave(128, 1)).T + bias.float()
+    assert cosine(out_op, ref) > 0.999
+    lin.transpose_weight()
+    assert cosine(lin(x), out_op) > 0.99999
+
+
+def test_fp8_linear_backward(cuda_device):
+    from futudiffu_b200.fp8 import FP8Linear, dequantize_fp8_blockwise, quantize_fp8_blockwise_cuda
+
+    w = (torch.randn(256, 384, generator=gen(6)) * 0.02).to(cuda_device)
+    w8, ws = quantize_fp8_blockwise_cuda(w)
+    lin = FP8Linear(w8, ws)
+    x = torch.randn(4, 384, generator=gen(7)).to(torch.bfloat16).to(cuda_device).requires_grad_(True)
+    lin(x).float().sum().backward()
+    expect = torch.ones(4, 256, device=cuda_device, dtype=torch.bfloat16) @ dequantize_fp8_blockwise(w8, ws)
+    assert torch.allclose(x.grad.float(), expect.float(), rtol=1e-2, atol=1e-2)
+
+
+def test_gemm_zero_rows(cuda_device):
+    from futudiffu_b200.fp8_kernels import fp8_gemm_blockwise
+
+    a8 = torch.zeros(0, 256, dtype=torch.float8_e4m3fn, device=cuda_device)
+    a_s = torch.zeros(0, 2, device=cuda_device)
+    b8 = torch.zeros(128, 256, dtype=torch.float8_e4m3fn, device=cuda_device)
+    bs = torch.ones(1, 2, device=cuda_device)
+    assert fp8_gemm_blockwise(a8, a_s, b8, bs).shape == (0, 128)
+
+
+def test_gemm_status_clean(cuda_device):
+    from futudiffu_b200 import check_status
+
+    check_status()
