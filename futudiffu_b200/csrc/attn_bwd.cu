@@ -26,6 +26,278 @@ __global__ void __launch_bounds__(256) prepass_kernel(const __nv_bfloat16* __res
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// dK / dV and dQ.  CUDA-core fp32 kernels over 64 x 64 tiles (the backward is
+// the QAT training path, outside the timed forward configs).  Per tile pair:
+//   S  = (Qc . Kc) * q_desc * k_desc            (codes exact, as the forward)
+//   P  = exp2(S - lse);  dP = dO . V^T;  dS = P * (dP - delta)
+//   dV += bf16(P)^T dO;  dK += bf16(dS * sm_scale)^T Q;  dQ += bf16(dS) K
+// with bf16-rounded operands where the reference casts (:896-907, :1007-1010).
+constexpr int TB = 64;     // tile rows / cols
+constexpr int LD = 129;    // padded row stride (floats) to avoid bank conflicts
+constexpr int LDT = 65;
+constexpr uint32_t BWD_SMEM = (5 * TB * LD + 2 * TB * LDT + 6 * TB) * 4;
+
+template <int QK>
+FD_DEV float code_val(const uint8_t* codes, int64_t i) {
+  if constexpr (QK == FD_QK_INT8) return (float)(int8_t)codes[i];
+  else {
+    __nv_fp8_e4m3 c;
+    c.__x = codes[i];
+    return float(c);
+  }
+}
+
+FD_DEV bool pair_valid(const uint8_t* mask, int64_t mstride, int nkb, int bh, int q0, int kblk) {
+  if (!mask) return true;
+  return mask[(int64_t)bh * mstride + (int64_t)(q0 / 128) * nkb + kblk] != 0;
+}
+
+// load a 64 x 128 tile of codes (row r0..r0+63) into smem as float, rows >= N as 0
+template <int QK>
+FD_DEV void load_codes(float* dst, const uint8_t* src, int64_t base_row, int r0, int N) {
+  for (int e = threadIdx.x; e < TB * 128; e += blockDim.x) {
+    const int r = e >> 7, d = e & 127;
+    dst[r * LD + d] = (r0 + r < N) ? code_val<QK>(src, (base_row + r0 + r) * 128 + d) : 0.f;
+  }
+}
+
+FD_DEV void load_bf16(float* dst, const __nv_bfloat16* src, int64_t base_row, int r0, int N) {
+  for (int e = threadIdx.x; e < TB * 128; e += blockDim.x) {
+    const int r = e >> 7, d = e & 127;
+    dst[r * LD + d] = (r0 + r < N) ? __bfloat162float(src[(base_row + r0 + r) * 128 + d]) : 0.f;
+  }
+}
+
+template <int QK>
+__global__ void __launch_bounds__(256) dkdv_kernel(
+    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ v,
+    const __nv_bfloat16* __restrict__ dout, const float* __restrict__ lse,
+    const float* __restrict__ delta, const uint8_t* __restrict__ qc, const float* __restrict__ qd,
+    const uint8_t* __restrict__ kc, const float* __restrict__ kd, const uint8_t* __restrict__ mask,
+    int64_t mstride, __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv, int N,
+    int64_t dstride, float sm_scale) {
+  extern __shared__ float sm[];
+  float* sK = sm;                 // [64][LD] K codes
+  float* sV = sK + TB * LD;       // [64][LD] V
+  float* sQc = sV + TB * LD;      // [64][LD] Q codes
+  float* sQ = sQc + TB * LD;      // [64][LD] Q bf16
+  float* sDO = sQ + TB * LD;      // [64][LD] dO
+  float* sPt = sDO + TB * LD;     // [64 k][LDT] bf16(P)^T
+  float* sDSt = sPt + TB * LDT;   // [64 k][LDT] bf16(dS * sm_scale)^T
+  float* sKd = sDSt + TB * LDT;   // [64]
+  float* sQd = sKd + TB;          // [64]
+  float* sL = sQd + TB;           // [64]
+  float* sDl = sL + TB;           // [64]
+  const int kblk = blockIdx.x, bh = blockIdx.y;
+  const int k0 = kblk * TB;
+  const int64_t row0 = (int64_t)bh * N;
+  const int t = threadIdx.x;
+  const int nkb = (N + 63) / 64;
+  load_codes<QK>(sK, kc, row0, k0, N);
+  load_bf16(sV, v, row0, k0, N);
+  if (t < TB) sKd[t] = (k0 + t < N) ? kd[(int64_t)bh * dstride + k0 + t] : 0.f;
+  // S^T / dP^T tile mapping: keys ty*4+i, queries tx*4+j
+  const int ty = t >> 4, tx = t & 15;
+  // dV / dK mapping: keys (t>>5)*8 + i, d (t&31)*4 + j
+  const int ak = (t >> 5) * 8, ad = (t & 31) * 4;
+  float accV[8][4], accK[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) accV[i][j] = accK[i][j] = 0.f;
+
+  for (int q0 = 0; q0 < N; q0 += TB) {
+    if (!pair_valid(mask, mstride, nkb, bh, q0, kblk)) continue;
+    __syncthreads();
+    load_codes<QK>(sQc, qc, row0, q0, N);
+    load_bf16(sQ, q, row0, q0, N);
+    load_bf16(sDO, dout, row0, q0, N);
+    if (t < TB) {
+      const bool ok = q0 + t < N;
+      sQd[t] = ok ? qd[(int64_t)bh * dstride + q0 + t] : 0.f;
+      sL[t] = ok ? lse[row0 + q0 + t] : 0.f;
+      sDl[t] = ok ? delta[row0 + q0 + t] : 0.f;
+    }
+    __syncthreads();
+    float s[4][4], dp[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[i][j] = dp[i][j] = 0.f;
+    for (int d = 0; d < 128; ++d) {
+      float kk[4], vv[4], qq[4], oo[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        kk[i] = sK[(ty * 4 + i) * LD + d];
+        vv[i] = sV[(ty * 4 + i) * LD + d];
+        qq[i] = sQc[(tx * 4 + i) * LD + d];
+        oo[i] = sDO[(tx * 4 + i) * LD + d];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          s[i][j] = fmaf(kk[i], qq[j], s[i][j]);
+          dp[i][j] = fmaf(vv[i], oo[j], dp[i][j]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int kr = ty * 4 + i;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int qr = tx * 4 + j;
+        float p = 0.f, ds = 0.f;
+        if (k0 + kr < N && q0 + qr < N) {
+          const float sc = (s[i][j] * sQd[qr]) * sKd[kr];
+          p = ex2_approx(sc - sL[qr]);
+          ds = p * (dp[i][j] - sDl[qr]);
+        }
+        sPt[kr * LDT + qr] = round_to_bf16(p);
+        sDSt[kr * LDT + qr] = round_to_bf16(ds * sm_scale);
+      }
+    }
+    __syncthreads();
+    for (int qi = 0; qi < TB; ++qi) {
+      float o[4], qv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        o[j] = sDO[qi * LD + ad + j];
+        qv[j] = sQ[qi * LD + ad + j];
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float pt = sPt[(ak + i) * LDT + qi];
+        const float dt = sDSt[(ak + i) * LDT + qi];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          accV[i][j] = fmaf(pt, o[j], accV[i][j]);
+          accK[i][j] = fmaf(dt, qv[j], accK[i][j]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int kr = k0 + ak + i;
+    if (kr < N) {
+      const int64_t o = (row0 + kr) * 128 + ad;
+      *reinterpret_cast<uint2*>(dv + o) = make_uint2(pack_bf16x2(accV[i][0], accV[i][1]), pack_bf16x2(accV[i][2], accV[i][3]));
+      *reinterpret_cast<uint2*>(dk + o) = make_uint2(pack_bf16x2(accK[i][0], accK[i][1]), pack_bf16x2(accK[i][2], accK[i][3]));
+    }
+  }
+}
+
+template <int QK>
+__global__ void __launch_bounds__(256) dq_kernel(
+    const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
+    const __nv_bfloat16* __restrict__ dout, const float* __restrict__ lse,
+    const float* __restrict__ delta, const uint8_t* __restrict__ qc, const float* __restrict__ qd,
+    const uint8_t* __restrict__ kc, const float* __restrict__ kd, const uint8_t* __restrict__ mask,
+    int64_t mstride, __nv_bfloat16* __restrict__ dq, int N, int64_t dstride, float sm_scale) {
+  extern __shared__ float sm[];
+  float* sQc = sm;                // [64 q][LD]
+  float* sDO = sQc + TB * LD;     // [64 q][LD]
+  float* sKc = sDO + TB * LD;     // [64 k][LD]
+  float* sV = sKc + TB * LD;      // [64 k][LD]
+  float* sK = sV + TB * LD;       // [64 k][LD] smoothed K bf16
+  float* sDS = sK + TB * LD;      // [64 q][LDT] bf16(dS)
+  float* sKd = sDS + 2 * TB * LDT;
+  float* sQd = sKd + TB;
+  float* sL = sQd + TB;
+  float* sDl = sL + TB;
+  const int qblk = blockIdx.x, bh = blockIdx.y;
+  const int q0 = qblk * TB;
+  const int64_t row0 = (int64_t)bh * N;
+  const int t = threadIdx.x;
+  const int nkb = (N + 63) / 64;
+  load_codes<QK>(sQc, qc, row0, q0, N);
+  load_bf16(sDO, dout, row0, q0, N);
+  if (t < TB) {
+    const bool ok = q0 + t < N;
+    sQd[t] = ok ? qd[(int64_t)bh * dstride + q0 + t] : 0.f;
+    sL[t] = ok ? lse[row0 + q0 + t] : 0.f;
+    sDl[t] = ok ? delta[row0 + q0 + t] : 0.f;
+  }
+  const int ty = t >> 4, tx = t & 15;           // S: queries ty*4+i, keys tx*4+j
+  const int aq = (t >> 5) * 8, ad = (t & 31) * 4;  // dQ: queries aq+i, d ad+j
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  for (int kb = 0; kb < nkb; ++kb) {
+    const int k0 = kb * TB;
+    if (!pair_valid(mask, mstride, nkb, bh, q0, kb)) continue;
+    __syncthreads();
+    load_codes<QK>(sKc, kc, row0, k0, N);
+    load_bf16(sV, v, row0, k0, N);
+    load_bf16(sK, k, row0, k0, N);
+    if (t < TB) sKd[t] = (k0 + t < N) ? kd[(int64_t)bh * dstride + k0 + t] : 0.f;
+    __syncthreads();
+    float s[4][4], dp[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[i][j] = dp[i][j] = 0.f;
+    for (int d = 0; d < 128; ++d) {
+      float qq[4], oo[4], kk[4], vv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        qq[i] = sQc[(ty * 4 + i) * LD + d];
+        oo[i] = sDO[(ty * 4 + i) * LD + d];
+        kk[i] = sKc[(tx * 4 + i) * LD + d];
+        vv[i] = sV[(tx * 4 + i) * LD + d];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          s[i][j] = fmaf(qq[i], kk[j], s[i][j]);
+          dp[i][j] = fmaf(oo[i], vv[j], dp[i][j]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int qr = ty * 4 + i;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int kr = tx * 4 + j;
+        float ds = 0.f;
+        if (k0 + kr < N && q0 + qr < N) {
+          const float p = ex2_approx((s[i][j] * sQd[qr]) * sKd[kr] - sL[qr]);
+          ds = p * (dp[i][j] - sDl[qr]);
+        }
+        sDS[qr * LDT + kr] = round_to_bf16(ds);
+      }
+    }
+    __syncthreads();
+    for (int ki = 0; ki < TB; ++ki) {
+      float kv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) kv[j] = sK[ki * LD + ad + j];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float dsv = sDS[(aq + i) * LDT + ki];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(dsv, kv[j], acc[i][j]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int qr = q0 + aq + i;
+    if (qr < N) {
+      const int64_t o = (row0 + qr) * 128 + ad;
+      *reinterpret_cast<uint2*>(dq + o) =
+          make_uint2(pack_bf16x2(acc[i][0] * sm_scale, acc[i][1] * sm_scale),
+                     pack_bf16x2(acc[i][2] * sm_scale, acc[i][3] * sm_scale));
+    }
+  }
+}
+
 }  // namespace attn_bwd
 }  // namespace fd
 
@@ -51,8 +323,34 @@ extern "C" int fd_sage_attn_bwd(const void* q, const void* k, const void* v, con
                                 const uint8_t* block_mask, int64_t mask_bh_stride, void* dq,
                                 void* dk, void* dv, int64_t BH, int64_t N, int qk_kind,
                                 float sm_scale, void* stream) {
-  (void)q; (void)k; (void)v; (void)dout; (void)lse; (void)delta; (void)q_codes; (void)q_desc;
-  (void)k_codes; (void)k_desc; (void)block_mask; (void)mask_bh_stride; (void)dq; (void)dk;
-  (void)dv; (void)BH; (void)N; (void)qk_kind; (void)sm_scale; (void)stream;
-  return set_error(FD_ERR_UNSUPPORTED, "fd_sage_attn_bwd: not built yet");
+  FD_CHECK_ARG(BH > 0 && BH <= 65535 && N > 0 && N < (1ll << 30), "bad shape");
+  FD_CHECK_ARG(qk_kind == FD_QK_INT8 || qk_kind == FD_QK_FP8, "bad qk_kind");
+  FD_CHECK_ARG(q && k && v && dout && lse && delta && q_codes && q_desc && k_codes && k_desc && dq &&
+                   dk && dv,
+               "null pointer");
+  FD_CHECK_ARG(aligned8(dq) && aligned8(dk) && aligned8(dv), "gradients must be 8-byte aligned");
+  const int64_t dstride = ((N + 127) / 128) * 128;  // per-token descale layout of fd_attn_quant
+  cudaStream_t st = (cudaStream_t)stream;
+  static bool attr_done[2] = {false, false};
+  const int kind = qk_kind == FD_QK_INT8 ? 0 : 1;
+  auto k_dkdv = kind == 0 ? attn_bwd::dkdv_kernel<FD_QK_INT8> : attn_bwd::dkdv_kernel<FD_QK_FP8>;
+  auto k_dq = kind == 0 ? attn_bwd::dq_kernel<FD_QK_INT8> : attn_bwd::dq_kernel<FD_QK_FP8>;
+  if (!attr_done[kind]) {
+    if (cudaFuncSetAttribute(k_dkdv, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_bwd::BWD_SMEM) != cudaSuccess ||
+        cudaFuncSetAttribute(k_dq, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_bwd::BWD_SMEM) != cudaSuccess)
+      return check_launch("sage_attn_bwd attributes");
+    attr_done[kind] = true;
+  }
+  dim3 grid((unsigned)((N + 63) / 64), (unsigned)BH);
+  k_dkdv<<<grid, 256, attn_bwd::BWD_SMEM, st>>>(
+      (const __nv_bfloat16*)q, (const __nv_bfloat16*)v, (const __nv_bfloat16*)dout, lse, delta,
+      (const uint8_t*)q_codes, q_desc, (const uint8_t*)k_codes, k_desc, block_mask, mask_bh_stride,
+      (__nv_bfloat16*)dk, (__nv_bfloat16*)dv, (int)N, dstride, sm_scale);
+  int rc = check_launch("sage_attn_bwd dkdv");
+  if (rc) return rc;
+  k_dq<<<grid, 256, attn_bwd::BWD_SMEM, st>>>(
+      (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, (const __nv_bfloat16*)dout, lse, delta,
+      (const uint8_t*)q_codes, q_desc, (const uint8_t*)k_codes, k_desc, block_mask, mask_bh_stride,
+      (__nv_bfloat16*)dq, (int)N, dstride, sm_scale);
+  return check_launch("sage_attn_bwd dq");
 }

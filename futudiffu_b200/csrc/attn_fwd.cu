@@ -20,9 +20,9 @@
 // next S = Q K^T is issued as soon as the softmax has pulled S into registers.
 //
 // Running-max threshold: O is rescaled only when a row max grows by more
-// than TAU = 8 (log2 units) over the reference max used for exp2, so P <= 2^8.
-// With e4m3 P this is encoded as P8 = e4m3(p * 448 / 256) and undone in the
-// epilogue; bf16 P is stored as is.  Results equal the reference online
+// than TAU (log2 units) over the reference max used for exp2, so P <= 2^TAU
+// (TAU = 8 for bf16 P, stored as is; TAU = 2 for e4m3 P, encoded as
+// P8 = e4m3(p * 448 / 4) and undone in the epilogue).  Results equal the reference online
 // softmax up to fp32 rounding (exp2 is shift-exact in bf16 / e4m3 up to
 // rounding of the argument).
 #include "fd_common.cuh"
@@ -36,8 +36,14 @@ constexpr int BKV = 128;  // keys per KV tile
 constexpr int HD = 128;
 constexpr int KST = 2;    // K/V pipeline stages
 constexpr int NUM_THREADS = 192;
-constexpr float TAU = 8.0f;
-constexpr float P8_SCALE = 448.0f / 256.0f;
+// Rescale threshold (log2 units): bf16 P keeps full relative precision at any
+// scale, so a wide threshold (O rescaled rarely) is free; e4m3 P must map
+// p <= 2^TAU onto 448, so a narrow one keeps small probabilities normal.
+template <int PV>
+struct PScale {
+  static constexpr float TAU = PV == FD_PV_FP8 ? 2.0f : 8.0f;
+  static constexpr float SCALE = PV == FD_PV_FP8 ? 448.0f / 4.0f : 1.0f;
+};
 
 template <int PV>
 struct Smem {
@@ -330,7 +336,7 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
         x[c] = v;
         mt = fmaxf(mt, v);
       }
-      const bool need = mt > m_ref + TAU;
+      const bool need = mt > m_ref + PScale<PV>::TAU;
       const float m_new = need ? mt : m_ref;
       if (__any_sync(0xffffffffu, need)) {
         const float alpha = (m_ref == -INFINITY) ? 0.f : ex2_approx(m_ref - m_new);
@@ -370,8 +376,8 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
             const float p2 = ex2_approx(x[16 * c + 4 * e + 2] - msafe);
             const float p3 = ex2_approx(x[16 * c + 4 * e + 3] - msafe);
             lsum += (p0 + p1) + (p2 + p3);
-            w[e] = f32x2_to_e4m3x2(p0 * P8_SCALE, p1 * P8_SCALE) |
-                   (f32x2_to_e4m3x2(p2 * P8_SCALE, p3 * P8_SCALE) << 16);
+            w[e] = f32x2_to_e4m3x2(p0 * PScale<PV>::SCALE, p1 * PScale<PV>::SCALE) |
+                   (f32x2_to_e4m3x2(p2 * PScale<PV>::SCALE, p3 * PScale<PV>::SCALE) << 16);
           }
           *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
@@ -425,8 +431,8 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
           float o0 = __uint_as_float(r[2 * e]);
           float o1 = __uint_as_float(r[2 * e + 1]);
           if (PV == FD_PV_FP8) {
-            o0 *= sVd[c * 32 + 2 * e] * (1.0f / P8_SCALE);
-            o1 *= sVd[c * 32 + 2 * e + 1] * (1.0f / P8_SCALE);
+            o0 *= sVd[c * 32 + 2 * e] * (1.0f / PScale<PV>::SCALE);
+            o1 *= sVd[c * 32 + 2 * e + 1] * (1.0f / PScale<PV>::SCALE);
           }
           w[e] = pack_bf16x2(o0 * inv_l, o1 * inv_l);
         }

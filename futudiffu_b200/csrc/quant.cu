@@ -97,7 +97,8 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const T* __restrict__ x,
 
 // ---------------------------------------------------------------- G6
 // quantize_fp8_blockwise, src/futudiffu/fp8.py:352-369: one CTA per
-// 128 x 128 tile, two passes over the (L2-resident) tile.
+// 128 x 128 tile, two passes over the (L2-resident) tile.  This reference
+// path is torch code, so its quotients follow torch's scalar / tensor rule.
 template <typename T>
 __global__ void __launch_bounds__(256) weight_quant_kernel(const T* __restrict__ w,
                                                           uint8_t* __restrict__ y,
@@ -120,13 +121,14 @@ __global__ void __launch_bounds__(256) weight_quant_kernel(const T* __restrict__
   amax = red[0];
 #pragma unroll
   for (int i = 1; i < 8; ++i) amax = fmaxf(amax, red[i]);
-  const float qs = quant_mult(amax);  // 448 / clamp_min(amax, 1e-12)
+  // torch evaluates `448 / t` as t.reciprocal() * 448: two correctly rounded steps
+  const float qs = __fmul_rn(__frcp_rn(fmaxf(amax, 1e-12f)), 448.0f);
   for (int r = threadIdx.x >> 4; r < 128; r += 16) {
     float v[8];
     load8<T>(w + (nb * 128 + r) * K + kb * 128 + col, v);
     *reinterpret_cast<uint2*>(y + (nb * 128 + r) * K + kb * 128 + col) = quant8(v, qs);
   }
-  if (threadIdx.x == 0) s[nb * kblocks + kb] = __fdiv_rn(1.0f, qs);
+  if (threadIdx.x == 0) s[nb * kblocks + kb] = __frcp_rn(qs);  // (1.0 / quant_scale).float()
 }
 
 // dequantize_fp8_blockwise, src/futudiffu/fp8.py:469-480.

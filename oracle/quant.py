@@ -20,6 +20,14 @@ def _f32(x):
     return x.detach().to("cpu", torch.float32)
 
 
+def div_ieee(a, b) -> torch.Tensor:
+    """Correctly rounded fp32 quotient (the quotient is formed in float64 and
+    rounded once; for division double rounding through 53 bits is exact)."""
+    a64 = torch.as_tensor(a, dtype=torch.float64)
+    b64 = torch.as_tensor(b, dtype=torch.float64)
+    return (a64 / b64).to(torch.float32)
+
+
 def quant_e4m3_groups(xf: torch.Tensor):
     """xf (..., G, 128) fp32 -> (codes e4m3, dequant scale (..., G)).
 
@@ -27,8 +35,8 @@ def quant_e4m3_groups(xf: torch.Tensor):
       scale = max(amax / 448, 1e-12); y = clamp(x * (448 / max(amax, 1e-12)), +-448)
     """
     amax = xf.abs().amax(dim=-1)
-    scale = torch.clamp(amax / FP8_MAX, min=1e-12)
-    qs = FP8_MAX / torch.clamp(amax, min=1e-12)
+    scale = torch.clamp(div_ieee(amax, FP8_MAX), min=1e-12)
+    qs = div_ieee(FP8_MAX, torch.clamp(amax, min=1e-12))
     y = (xf * qs.unsqueeze(-1)).clamp(-FP8_MAX, FP8_MAX).to(E4M3)
     return y, scale
 
@@ -46,6 +54,8 @@ def weight_quant(w: torch.Tensor, block: int = 128):
     """G6 quantize_fp8_blockwise (src/futudiffu/fp8.py:352-369): 128 x 128 tiles.
 
     Returns codes (N, K) e4m3 and the stored scale 1 / (448 / max(amax, 1e-12)).
+    Both quotients follow torch's ``scalar / tensor``, which evaluates
+    ``tensor.reciprocal() * scalar`` (two roundings), exactly as the reference.
     """
     t = _f32(w)
     N, K = t.shape
@@ -69,7 +79,7 @@ def silu_gate_quant(x: torch.Tensor, block: int = 128):
     xf = _f32(x)
     N = xf.shape[-1] // 2
     w1, w3 = xf[..., :N], xf[..., N:]
-    gated = (w1 * (1.0 / (1.0 + torch.exp(-w1)))) * w3
+    gated = (w1 * div_ieee(1.0, 1.0 + torch.exp(-w1))) * w3
     return act_quant(gated, block)
 
 
@@ -85,7 +95,7 @@ def gelu_requant(x8: torch.Tensor, sx: torch.Tensor, block: int = 128):
     K = xf.shape[-1]
     g = xf.reshape(*xf.shape[:-1], K // block, block) * sx.cpu().unsqueeze(-1)
     sqrt_2 = torch.tensor(1.41421356237, dtype=torch.float32)
-    ge = g * 0.5 * (1.0 + torch.erf(g / sqrt_2))
+    ge = g * 0.5 * (1.0 + torch.erf(div_ieee(g, sqrt_2)))
     y, s = quant_e4m3_groups(ge)
     return y.reshape(xf.shape), s
 

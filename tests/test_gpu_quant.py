@@ -14,7 +14,8 @@ pytestmark = pytest.mark.gpu
 
 def _x(shape, seed, scale=3.0, dtype=torch.bfloat16):
     g = gen(seed)
-    x = torch.randn(*shape, generator=g) * (torch.rand(shape[0], 1, generator=g) * scale + 1e-3)
+    row_scale = torch.rand(*shape[:-1], 1, generator=g) * scale + 1e-3
+    x = torch.randn(*shape, generator=g) * row_scale
     return x.to(dtype)
 
 
