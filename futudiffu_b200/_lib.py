@@ -61,6 +61,8 @@ _SIGS: dict[str, list] = {
     "fd_qkv_postprocess": [_P, _P, _P, _P, _P, _P, _P, _L, _L, _L, _L, _F, _P],
     "fd_attn_quant_workspace_floats": [_L, _L],
     "fd_attn_quant": [_P, _P, _P, _L, _L, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P, _P],
+    "fd_attn_quant_noalloc_max_floats": [],
+    "fd_attn_quant_noalloc": [_P, _P, _P, _L, _L, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P],
     "fd_sage_attn_fwd": [_P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _L, _L, _I, _I, _I, _I, _P],
     "fd_sage_attn_bwd_prepass": [_P, _P, _P, _L, _L, _P],
     "fd_sage_attn_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _P, _L, _L, _I, _F, _P],
@@ -69,6 +71,7 @@ _RESTYPES = {
     "fd_version": ctypes.c_char_p,
     "fd_last_error": ctypes.c_char_p,
     "fd_attn_quant_workspace_floats": ctypes.c_int64,
+    "fd_attn_quant_noalloc_max_floats": ctypes.c_int64,
 }
 
 _lib = None

@@ -14,12 +14,20 @@
 //   FP8 Q/K per token  src/futudiffu/sage_kernels.py:151-155, :176-179
 //   V e4m3 per channel src/futudiffu/sage_kernels.py:1146-1151 (here over the
 //                      whole sequence instead of one 64-row tile)
+#include <mutex>
+
 #include "fd_common.cuh"
 #include "fd_host.h"
 
 namespace fd {
 
 constexpr int kChunkRows = 256;  // rows per colstats CTA
+
+// Scratch of fd_attn_quant_noalloc: a fixed device array, so that entry point
+// never allocates.  FD_NOALLOC_WS_FLOATS floats (4 MiB) on every GPU that loads
+// the library, held until the process exits.
+constexpr int64_t kNoAllocWsFloats = FD_NOALLOC_WS_FLOATS;
+static __device__ __align__(256) float g_attn_quant_ws[kNoAllocWsFloats];
 
 FD_DEV void unpack8(const uint4& u, float (&v)[8]) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
@@ -328,4 +336,63 @@ extern "C" int fd_attn_quant(const void* q, const void* k, const void* v, int64_
   else FD_Q_LAUNCH(FD_QK_FP8);
 #undef FD_Q_LAUNCH
   return check_launch("attn_quant");
+}
+
+// ---------------------------------------------------------------------------
+// fd_attn_quant_noalloc: fd_attn_quant with its scratch in g_attn_quant_ws.
+//
+// For callers that cannot allocate device memory themselves -- hosts that hand
+// this library only their input and output buffers (a serving process that
+// carves all device memory from one arena planned at start-up, or a foreign
+// runtime calling through the C ABI with no allocator of its own), and code
+// paths where cudaMalloc's implicit synchronisation is not allowed.
+//
+// The host cannot use the array's name as a device address, so the address is
+// looked up once per device with cudaGetSymbolAddress, with that device
+// current, on the first call made on it; make that first call before any
+// stream capture.  The colstats launch writes every scratch element the
+// quantisation launch reads, so nothing needs clearing between calls; but all
+// calls share the one array, so calls that overlap on the GPU (different
+// streams, or different host threads, on one device) race on it.
+static std::mutex g_ws_mutex;
+static float* g_ws_addr[64] = {nullptr};
+
+static int noalloc_ws(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "fd_attn_quant_noalloc: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return set_error(FD_ERR_ARG, "fd_attn_quant_noalloc: device index %d unsupported", dev);
+  std::lock_guard<std::mutex> lock(g_ws_mutex);
+  if (!g_ws_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_quant_ws);
+    if (e != cudaSuccess || p == nullptr)
+      return set_error(FD_ERR_CUDA, "fd_attn_quant_noalloc: cudaGetSymbolAddress failed: %s",
+                       cudaGetErrorString(e));
+    g_ws_addr[dev] = static_cast<float*>(p);
+  }
+  *out = g_ws_addr[dev];
+  return FD_OK;
+}
+
+extern "C" int64_t fd_attn_quant_noalloc_max_floats(void) { return kNoAllocWsFloats; }
+
+extern "C" int fd_attn_quant_noalloc(const void* q, const void* k, const void* v, int64_t BH,
+                                     int64_t N, int smooth_k, int qk_kind, int q_gran, int k_gran,
+                                     int pv_kind, float sm_scale_log2e, void* q_codes,
+                                     float* q_desc, void* k_codes, float* k_desc, void* v_codes,
+                                     float* v_desc, float* k_mean, void* stream) {
+  FD_CHECK_ARG(BH > 0 && N > 0, "empty input");
+  const int64_t need = fd_attn_quant_workspace_floats(BH, N);
+  if (need > kNoAllocWsFloats)
+    return set_error(FD_ERR_ARG,
+                     "fd_attn_quant_noalloc: BH=%lld, N=%lld needs %lld scratch floats, above the "
+                     "built-in maximum of %lld (2 * BH * ceil(N / 256) * 128 must not exceed it); "
+                     "use fd_attn_quant with a caller-provided workspace",
+                     (long long)BH, (long long)N, (long long)need, (long long)kNoAllocWsFloats);
+  float* ws = nullptr;
+  const int rc = noalloc_ws(&ws);
+  if (rc) return rc;
+  return fd_attn_quant(q, k, v, BH, N, smooth_k, qk_kind, q_gran, k_gran, pv_kind, sm_scale_log2e,
+                       q_codes, q_desc, k_codes, k_desc, v_codes, v_desc, k_mean, ws, stream);
 }

@@ -155,6 +155,25 @@ int fd_attn_quant(const void* q, const void* k, const void* v, int64_t BH, int64
                   float* k_desc, void* v_codes, float* v_desc, float* k_mean, float* workspace,
                   void* stream);
 
+/* No counterpart in the reference.  fd_attn_quant with no workspace argument:
+ * the scratch lives in a fixed device array inside the library (one per GPU
+ * that loads it, FD_NOALLOC_WS_FLOATS floats = 4 MiB, held until exit), so
+ * this entry point allocates nothing.  Meant for callers that cannot allocate
+ * device memory (hosts that pass only their planned input/output buffers, or
+ * paths where cudaMalloc's synchronisation is not allowed).  Rejects shapes
+ * whose scratch, 2 * BH * ceil(N/256) * 128 floats, exceeds the array
+ * (FD_ERR_ARG).  The first call on a device looks up the array's device
+ * address; make it before any stream capture.  Calls share the array: calls
+ * that overlap on one GPU race.  fd_attn_quant_noalloc_max_floats() returns
+ * the array size. */
+#define FD_NOALLOC_WS_FLOATS 1048576
+int64_t fd_attn_quant_noalloc_max_floats(void);
+int fd_attn_quant_noalloc(const void* q, const void* k, const void* v, int64_t BH, int64_t N,
+                          int smooth_k, int qk_kind, int q_gran, int k_gran, int pv_kind,
+                          float sm_scale_log2e, void* q_codes, float* q_desc, void* k_codes,
+                          float* k_desc, void* v_codes, float* v_desc, float* k_mean,
+                          void* stream);
+
 /* A5/A6 -- quantized attention forward
  * (production kernel _sage_attn_fwd_int8qk_bf16pv_masked_lse,
  *  src/futudiffu/sage_kernels.py:1379-1477, and its unmasked / fp8 siblings).
