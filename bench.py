@@ -305,18 +305,83 @@ def run_ours(args, world, rank, local):
     return 0
 
 
+GEMM_SHAPES = {"config1": (2048, 3072, 3072), "ref_qkv": (8576, 11520, 3840), "ref_w2": (8576, 3840, 10240)}
+
+
+def run_gemm(args, world, rank, local):
+    """FP8 block-GEMM TFLOPS (or the reference's own Z-Image shapes)."""
+    from futudiffu_b200 import _lib as L
+    from futudiffu_b200 import check_status
+    from futudiffu_b200.fp8 import quantize_fp8_blockwise_cuda
+    from futudiffu_b200.fp8_kernels import fp8_act_quant
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    M, N, K = GEMM_SHAPES[args.gemm_shape]
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(dev)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(dev)
+    w8, ws = quantize_fp8_blockwise_cuda(w)
+    a8, a_s = fp8_act_quant(x)
+    c = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def gemm():
+        L.call("fd_fp8_gemm_blockwise", L.ptr(a8), L.ptr(a_s), L.ptr(w8), L.ptr(ws), None, 0, L.ptr(c),
+               L.DT_BF16, M, N, K, 0, L.stream_ptr(dev))
+
+    for _ in range(args.warmup):
+        gemm()
+    torch.cuda.synchronize()
+    times = []
+    with ClockSampler(local) as clocks:
+        for _ in range(args.steps):
+            flush.zero_()  # L2 flush between timed launches (operands < L2)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            gemm()
+            e1.record(stream)
+            times.append((e0, e1))
+        torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in times)
+    check_status()
+    flops = 2.0 * M * N * K
+    pk = peaks()
+    peak = 2.0 * pk["bf16_tflops"]
+    tf = flops / (ms * 1e-3) / 1e12
+    if rank == 0:
+        print(json.dumps({
+            "metric": "FP8 block-GEMM TFLOPS", "value": tf * world, "unit": "TFLOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp8 e4m3 (1x128 / 128x128 f32 scales)",
+            "data": "synthetic",
+            "config": {"workload": f"gemm_{args.gemm_shape}", "M": M, "N": N, "K": K, "l2": "flushed"},
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
+                         "frac": tf / peak, "traffic": None,
+                         "peak_source": f"2 x {pk['source']} bf16 dense: fp8 dense rate is twice bf16"},
+            "gpu_launches": args.steps, "clocks": clocks.summary(),
+        }), flush=True)
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["attention", "gemm"], default="attention",
+                    help="attention = BASELINE config 2 (headline); gemm = FP8 block GEMM")
+    ap.add_argument("--gemm-shape", choices=sorted(GEMM_SHAPES), default="config1")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
     world, rank, local = dist_setup()
     try:
         if args.impl == "reference":
             return run_reference(args, world, rank)
+        if args.workload == "gemm":
+            return run_gemm(args, world, rank, local)
         return run_ours(args, world, rank, local)
     finally:
         if world > 1:

@@ -49,6 +49,7 @@ _SIGS: dict[str, list] = {
     "fd_version": [],
     "fd_last_error": [],
     "fd_get_status": [ctypes.POINTER(ctypes.c_uint), _I],
+    "fd_div_full_f32": [_P, _P, _P, _L, _P],
     "fd_fp8_act_quant": [_P, _I, _P, _P, _L, _L, _I, _P],
     "fd_fp8_weight_quant": [_P, _I, _P, _P, _L, _L, _I, _P],
     "fd_fp8_dequant_blockwise": [_P, _P, _P, _I, _L, _L, _I, _P],
@@ -152,6 +153,22 @@ def get_status(clear: bool = True) -> int:
     out = ctypes.c_uint(0)
     call("fd_get_status", ctypes.byref(out), 1 if clear else 0)
     return int(out.value)
+
+
+def device_divide(a, b) -> torch.Tensor:
+    """a / b on the device with the quantisers' f32 divide (Triton's `/`, div.full.f32).
+
+    a, b: tensors or numbers (broadcast together); returns a CPU float32 tensor.
+    """
+    require_cuda()
+    at = torch.as_tensor(a, dtype=torch.float32)
+    bt = torch.as_tensor(b, dtype=torch.float32)
+    shape = torch.broadcast_shapes(at.shape, bt.shape)
+    ad = torch.broadcast_to(at.to("cuda"), shape).contiguous()
+    bd = torch.broadcast_to(bt.to("cuda"), shape).contiguous()
+    out = torch.empty_like(ad)
+    call("fd_div_full_f32", ptr(ad), ptr(bd), ptr(out), ad.numel(), stream_ptr(ad.device))
+    return out.cpu()
 
 
 def check_status() -> None:

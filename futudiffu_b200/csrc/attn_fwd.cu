@@ -7,13 +7,14 @@
 //   online softmax over KV tiles: m, l, O with exp2, LSE = m + log2(l),
 //   out   = O / l.
 //
-// CTA = one 128-row Q tile of one (b, h); 6 warps:
-//   warps 0-3  softmax: thread = query row (TMEM lane).  Reads its S row
-//              from TMEM, scales, row max, exp2, row sum, writes P to shared
-//              memory; rescales its O row in TMEM when the running max moves.
-//   warp 4     TMA producer: Q once, then K (+ per-token K scales) and V
+// CTA = one 128-row Q tile of one (b, h); 10 warps:
+//   warps 0-7  softmax: two threads per query row (TMEM lane), 64 keys each.
+//              Read S from TMEM, scale, row max (exchanged with the partner
+//              thread), exp2, row sum, write P to shared memory; rescale their
+//              half of the O row in TMEM when the running max moves.
+//   warp 8     TMA producer: Q once, then K (+ per-token K scales) and V
 //              tiles of 128 keys into a 2-stage ring.
-//   warp 5     MMA issuer: S = Q K^T (kind::i8 -> s32, or kind::f8f6f4 -> f32)
+//   warp 9     MMA issuer: S = Q K^T (kind::i8 -> s32, or kind::f8f6f4 -> f32)
 //              and O += P V (kind::f8f6f4 e4m3, or kind::f16 bf16).
 // TMEM: S at columns [0,128), O at [128,256).  Two CTAs fit on one SM
 // (fp8 PV), so one CTA's softmax overlaps the other's MMAs; inside a CTA the
@@ -35,7 +36,9 @@ constexpr int BQ = 128;   // query rows per CTA
 constexpr int BKV = 128;  // keys per KV tile
 constexpr int HD = 128;
 constexpr int KST = 2;    // K/V pipeline stages
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_SOFTMAX_WARPS = 8;  // two threads per query row, 64 keys each
+constexpr int WARP_TMA = 8, WARP_MMA = 9;
+constexpr int NUM_THREADS = 320;
 // Rescale threshold (log2 units): bf16 P keeps full relative precision at any
 // scale, so a wide threshold (O rescaled rarely) is free; e4m3 P must map
 // p <= 2^TAU onto 448, so a narrow one keeps small probabilities normal.
@@ -43,7 +46,51 @@ template <int PV>
 struct PScale {
   static constexpr float TAU = PV == FD_PV_FP8 ? 2.0f : 8.0f;
   static constexpr float SCALE = PV == FD_PV_FP8 ? 448.0f / 4.0f : 1.0f;
+  static constexpr float LOG2_SCALE = PV == FD_PV_FP8 ? 6.8073549220576041f : 0.0f;  // log2(112)
 };
+
+// packed f32x2 helpers (sm_100a FADD2 / FMUL2 / FFMA2)
+FD_DEV uint64_t pk(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+FD_DEV void unpk(uint64_t v, float& a, float& b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v)); }
+FD_DEV uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+FD_DEV uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+FD_DEV uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+FD_DEV float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// max of 64 consecutive values with four independent 3-input chains
+FD_DEV float max_reduce64(const float* x) {
+  float m0 = max3(x[0], x[1], x[2]), m1 = max3(x[3], x[4], x[5]);
+  float m2 = max3(x[6], x[7], x[8]), m3 = max3(x[9], x[10], x[11]);
+#pragma unroll
+  for (int c = 12; c < 60; c += 8) {
+    m0 = max3(m0, x[c], x[c + 1]);
+    m1 = max3(m1, x[c + 2], x[c + 3]);
+    m2 = max3(m2, x[c + 4], x[c + 5]);
+    m3 = max3(m3, x[c + 6], x[c + 7]);
+  }
+  m0 = max3(m0, x[60], x[61]);
+  m1 = max3(m1, x[62], x[63]);
+  return fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+}
 
 template <int PV>
 struct Smem {
@@ -57,7 +104,8 @@ struct Smem {
   static constexpr uint32_t OFF_P = OFF_V + KST * V_BYTES;
   static constexpr uint32_t OFF_KD = OFF_P + P_BYTES;                    // KST x 128 f32
   static constexpr uint32_t OFF_VD = OFF_KD + KST * 512;                 // 128 f32
-  static constexpr uint32_t OFF_BAR = OFF_VD + 512;
+  static constexpr uint32_t OFF_RED = OFF_VD + 512;                      // row max / sum exchange
+  static constexpr uint32_t OFF_BAR = OFF_RED + (2 * 2 * 128 + 2 * 128) * 4;
   static constexpr uint32_t TOTAL = OFF_BAR + 256 + 1024;               // + barriers, align slack
 };
 
@@ -97,6 +145,75 @@ FD_DEV void drain_wait(uint64_t* bar, uint32_t parity) {
       return;
     }
   }
+}
+
+// Row max of one thread's 64 logits.  Per-block K: x holds raw scores and the
+// 64 keys share the factor c >= 0; per-token K: x is already scaled.  The
+// partial variant first sets out-of-range / masked keys to -inf.
+template <int KG, bool FULL>
+FD_DEV float half_max(float (&x)[64], float c, int col0, int N, bool half_ok) {
+  if (!FULL) {
+#pragma unroll
+    for (int e = 0; e < 64; ++e)
+      if (!(half_ok && col0 + e < N)) x[e] = -INFINITY;
+  }
+  const float m = max_reduce64(x);
+  if (KG == FD_GRAN_BLOCK) return m == -INFINITY ? -INFINITY : m * c;
+  return m;
+}
+
+// P = exp2(L + nb) for one thread's 64 keys, written to the shared-memory P tile
+// in the 128-byte-swizzled K-major layout the PV MMA reads; returns the sum of P.
+template <int KG, int PV, bool FULL>
+FD_DEV float exp_store(const float (&x)[64], float c, float nb, uint8_t* sP, int row, int h) {
+  uint64_t acc = pk(0.f, 0.f);
+  auto pexp = [&](int e, float& p0, float& p1) {
+    uint64_t a;
+    if (KG == FD_GRAN_BLOCK) a = fma2(pk(x[e], x[e + 1]), pk(c, c), pk(nb, nb));
+    else a = add2(pk(x[e], x[e + 1]), pk(nb, nb));
+    float a0, a1;
+    unpk(a, a0, a1);
+    p0 = ex2_approx(a0);
+    p1 = ex2_approx(a1);
+    if (!FULL) {  // masked keys: -inf (times 0 for an all-zero K block would be NaN)
+      if (x[e] == -INFINITY) p0 = 0.f;
+      if (x[e + 1] == -INFINITY) p1 = 0.f;
+    }
+    acc = add2(acc, pk(p0, p1));
+  };
+  if (PV == FD_PV_FP8) {
+    // this thread's keys are the 16-byte chunks 4h .. 4h+3 of the 128-byte P row
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float p0, p1, p2, p3;
+        pexp(16 * ch + 4 * e, p0, p1);
+        pexp(16 * ch + 4 * e + 2, p2, p3);
+        w[e] = f32x2_to_e4m3x2(p0, p1) | (f32x2_to_e4m3x2(p2, p3) << 16);
+      }
+      *reinterpret_cast<uint4*>(sP + row * 128 + (((4 * h + ch) ^ (row & 7)) << 4)) =
+          make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+    // bf16: this thread's 64 keys are panel h (one 128-byte row of 8 chunks)
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float p0, p1;
+        pexp(8 * ch + 2 * e, p0, p1);
+        w[e] = pack_bf16x2(p0, p1);
+      }
+      *reinterpret_cast<uint4*>(sP + h * (BQ * 128) + row * 128 + ((ch ^ (row & 7)) << 4)) =
+          make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+  float s0, s1;
+  unpk(acc, s0, s1);
+  return s0 + s1;
 }
 
 // QK: FD_QK_INT8 / FD_QK_FP8; KG: k granularity; PV: FD_PV_BF16 / FD_PV_FP8
@@ -139,14 +256,14 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
       mbar_init(&bKVempty[s], 1);
     }
     mbar_init(bSfull, 1);
-    mbar_init(bSfree, 4);
-    mbar_init(bPfull, 4);
+    mbar_init(bSfree, NUM_SOFTMAX_WARPS);
+    mbar_init(bPfull, NUM_SOFTMAX_WARPS);
     mbar_init(bOready, 1);
     mbar_init(bDrain, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == WARP_MMA) {
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
@@ -156,7 +273,7 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t tS = tmem_base, tO = tmem_base + 128;
 
-  if (warp == 4) {
+  if (warp == WARP_TMA) {
     // ================================================================ producer
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
@@ -195,7 +312,7 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
         drain_wait(&bVfull[s], ph);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == WARP_MMA) {
     // ================================================================ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_qk =
@@ -269,73 +386,86 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
       drain_wait(bDrain, 0);
     }
   } else {
-    // ================================================================ softmax (warps 0-3)
-    const int row = warp * 32 + lane;          // TMEM lane == query row in the tile
+    // ================================================================ softmax (warps 0-7)
+    // Two threads per query row: warp w owns row (w & 3) * 32 + lane (its TMEM lane
+    // quadrant is w & 3) and key columns [64 h, 64 h + 64) of every tile, h = w >> 2.
+    // The partners exchange row maxima through shared memory once per tile.
+    const int quad = warp & 3, h = warp >> 2;
+    const int row = quad * 32 + lane;
     const int qrow = q0 + row;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    if (PV == FD_PV_FP8) sVd[row] = p.v_desc[(int64_t)bh * HD + row];
-    named_bar_sync(1, 128);
+    const int cb = h * 64;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    float* red_max = reinterpret_cast<float*>(smem + SM::OFF_RED);  // [parity][half][128]
+    float* red_l = red_max + 2 * 2 * 128;                           // [half][128]
+    if (PV == FD_PV_FP8 && h == 0) sVd[row] = p.v_desc[(int64_t)bh * HD + row];
+    named_bar_sync(1, NUM_SOFTMAX_WARPS * 32);
     const float qd = p.q_gran == FD_GRAN_TOKEN
                          ? p.q_desc[(int64_t)bh * p.q_desc_stride + (qrow < p.N ? qrow : 0)]
                          : p.q_desc[(int64_t)bh * p.q_desc_stride + qb];
+    // l accumulates this thread's share of P in its stored scale (x PScale::SCALE)
     float m_ref = -INFINITY, l = 0.f;
     uint32_t i = 0;
     bool ok = true;
     for (int j = 0; j < p.n_kv_tiles && ok; ++j) {
       if (!tile_valid(p, bh, qb, j)) continue;
       const uint32_t s = i % KST, use = i / KST;
-      // per-column scale factors of this tile (times qd)
-      float c_lo, c_hi;  // per-block K: one factor per 64-column half
-      bool half_ok[2] = {true, true};
+      const int col0 = j * BKV + cb;  // first key of this thread's half-tile
+      bool my_half_ok = true, other_half_ok = true;
       if (p.mask) {
         const uint8_t* mr = p.mask + (int64_t)bh * p.mask_bh_stride + (int64_t)qb * p.nkb64;
-        half_ok[0] = mr[2 * j] != 0;
-        half_ok[1] = (2 * j + 1 < p.nkb64) ? (mr[2 * j + 1] != 0) : false;
+        my_half_ok = (2 * j + h < p.nkb64) && mr[2 * j + h] != 0;
+        other_half_ok = (2 * j + (h ^ 1) < p.nkb64) && mr[2 * j + (h ^ 1)] != 0;
       }
+      // the whole half-tile is in range and unmasked: the common case, no selects
+      const bool full = (col0 + 64 <= p.N) && my_half_ok;
+      (void)other_half_ok;
+      float c = 0.f;  // per-block K: logit factor of this thread's 64 keys
       if (KG == FD_GRAN_BLOCK) {
-        const float* kd = p.k_desc + (int64_t)bh * p.k_desc_stride + 2 * j;
-        c_lo = kd[0] * qd;
-        c_hi = (2 * j + 1 < p.nkb64) ? kd[1] * qd : 0.f;
+        const int kb = 2 * j + h;
+        c = (kb < p.nkb64) ? p.k_desc[(int64_t)bh * p.k_desc_stride + kb] * qd : 0.f;
       }
       if (!mbar_wait(bSfull, i & 1, abort_flag)) { ok = false; break; }
       if (KG == FD_GRAN_TOKEN) {
         if (!mbar_wait(&bKfull[s], use & 1, abort_flag)) { ok = false; break; }
       }
       tc_fence_after();
-      float x[128];
+      float x[64];
       {
-        uint32_t r[32];
+        uint32_t r[2][32];
+        tmem_ld32(tS + lane_base + cb, r[0]);
+        tmem_ld32(tS + lane_base + cb + 32, r[1]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bSfree);  // the tensor core may overwrite S now
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(tS + lane_base + c * 32, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            if (QK == FD_QK_INT8) x[c * 32 + e] = (float)(int)r[e];
-            else x[c * 32 + e] = __uint_as_float(r[e]);
+        for (int e = 0; e < 64; e += 2) {
+          if (QK == FD_QK_INT8) {
+            // exact s32 -> f32: |s| <= 128*127*127 < 2^22, so adding the bit pattern
+            // of 1.5*2^23 and subtracting 1.5*2^23 is exact
+            const float a = __int_as_float((int)r[e >> 5][e & 31] + 0x4B400000);
+            const float b = __int_as_float((int)r[e >> 5][(e & 31) + 1] + 0x4B400000);
+            unpk(add2(pk(a, b), pk(-12582912.0f, -12582912.0f)), x[e], x[e + 1]);
+          } else {
+            x[e] = __uint_as_float(r[e >> 5][e & 31]);
+            x[e + 1] = __uint_as_float(r[e >> 5][(e & 31) + 1]);
           }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bSfree);
-
-      // scale to log2-domain logits, mask, row max
-      const int kv0 = j * BKV;
-      float mt = -INFINITY;
+      if (KG == FD_GRAN_TOKEN) {
+        // reference order: (s * q_desc) * k_desc, per key
+        const float* kd = sKd + s * 128 + cb;
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        float cf;
-        if (KG == FD_GRAN_TOKEN) cf = sKd[s * 128 + c];
-        else cf = c < 64 ? c_lo : c_hi;
-        float v;
-        if (KG == FD_GRAN_TOKEN) v = (x[c] * qd) * cf;  // reference order (s * q_desc) * k_desc
-        else v = x[c] * cf;
-        const bool valid = (kv0 + c < p.N) && half_ok[c >> 6];
-        v = valid ? v : -INFINITY;
-        x[c] = v;
-        mt = fmaxf(mt, v);
+        for (int e = 0; e < 64; e += 2)
+          unpk(mul2(mul2(pk(x[e], x[e + 1]), pk(qd, qd)), pk(kd[e], kd[e + 1])), x[e], x[e + 1]);
       }
+      const float mloc = full ? half_max<KG, true>(x, c, col0, p.N, my_half_ok)
+                              : half_max<KG, false>(x, c, col0, p.N, my_half_ok);
+      float* rm = red_max + (i & 1) * 256;
+      rm[h * 128 + row] = mloc;
+      named_bar_sync(2 + quad, 64);
+      const float mt = fmaxf(mloc, rm[(h ^ 1) * 128 + row]);
+      // both partners see the same mt and m_ref, so they take the same decisions
       const bool need = mt > m_ref + PScale<PV>::TAU;
       const float m_new = need ? mt : m_ref;
       if (__any_sync(0xffffffffu, need)) {
@@ -347,57 +477,25 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
           tc_fence_after();
           uint32_t r[16];
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            tmem_ld16(tO + lane_base + c * 16, r);
+          for (int cc = 0; cc < 4; ++cc) {
+            tmem_ld16(tO + lane_base + cb + cc * 16, r);
             tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-            tmem_st16(tO + lane_base + c * 16, r);
+            tmem_st16(tO + lane_base + cb + cc * 16, r);
           }
           tmem_wait_st();
         }
         m_ref = m_new;
       }
-      const float msafe = (m_ref == -INFINITY) ? 0.f : m_ref;
+      // exp2 argument: L - (m_ref - log2 SCALE), so ex2 yields P already in its stored scale
+      const float nb = (m_ref == -INFINITY) ? 0.f : -(m_ref - PScale<PV>::LOG2_SCALE);
       // P buffer is free once PV(i-1) has completed
       if (i > 0) {
         if (!mbar_wait(bOready, (i - 1) & 1, abort_flag)) { ok = false; break; }
       }
-      float lsum = 0.f;
-      if (PV == FD_PV_FP8) {
-        uint8_t* prow = sP + row * 128;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {  // 16-byte chunk c holds keys 16c .. 16c+15
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float p0 = ex2_approx(x[16 * c + 4 * e + 0] - msafe);
-            const float p1 = ex2_approx(x[16 * c + 4 * e + 1] - msafe);
-            const float p2 = ex2_approx(x[16 * c + 4 * e + 2] - msafe);
-            const float p3 = ex2_approx(x[16 * c + 4 * e + 3] - msafe);
-            lsum += (p0 + p1) + (p2 + p3);
-            w[e] = f32x2_to_e4m3x2(p0 * PScale<PV>::SCALE, p1 * PScale<PV>::SCALE) |
-                   (f32x2_to_e4m3x2(p2 * PScale<PV>::SCALE, p3 * PScale<PV>::SCALE) << 16);
-          }
-          *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {  // 16-byte chunk c holds keys 8c .. 8c+7
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float p0 = ex2_approx(x[8 * c + 2 * e] - msafe);
-            const float p1 = ex2_approx(x[8 * c + 2 * e + 1] - msafe);
-            lsum += p0 + p1;
-            w[e] = pack_bf16x2(p0, p1);
-          }
-          const int panel = c >> 3, cc = c & 7;
-          *reinterpret_cast<uint4*>(sP + panel * (BQ * 128) + row * 128 + ((cc ^ (row & 7)) << 4)) =
-              make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      }
-      l += lsum;
+      l += full ? exp_store<KG, PV, true>(x, c, nb, sP, row, h)
+                : exp_store<KG, PV, false>(x, c, nb, sP, row, h);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
@@ -406,20 +504,24 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
     }
     // ---------------------------------------------------------------- epilogue
     if (ok && i > 0) ok = mbar_wait(bOready, (i - 1) & 1, abort_flag);
+    red_l[h * 128 + row] = l;
+    named_bar_sync(2 + quad, 64);
+    const float l_tot = l + red_l[(h ^ 1) * 128 + row];
     if (ok) {
       tc_fence_after();
       const bool any = i > 0;
-      const float inv_l = any ? __fdividef(1.0f, l) : __int_as_float(0x7fc00000);
-      const float lse_v = any ? m_ref + __log2f(l) : -INFINITY;
+      // reference: LSE = m + log2(l) (tl.math.log2 == log2f), out = o / l (Triton f32 divide)
+      const float lse_v = any ? m_ref + (log2f(l_tot) - PScale<PV>::LOG2_SCALE) : -INFINITY;
+      const float l_div = any ? l_tot : 0.f;  // 0/0 -> NaN for rows that saw no key, as the reference
       const bool row_ok = qrow < p.N;
-      if (row_ok && p.lse) p.lse[(int64_t)bh * p.N + qrow] = lse_v;
-      __nv_bfloat16* orow = p.out + ((int64_t)bh * p.N + (row_ok ? qrow : 0)) * HD;
+      if (row_ok && h == 0 && p.lse) p.lse[(int64_t)bh * p.N + qrow] = lse_v;
+      __nv_bfloat16* orow = p.out + ((int64_t)bh * p.N + (row_ok ? qrow : 0)) * HD + cb;
       // tcgen05.ld is warp-collective: every lane loads, only valid rows store
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int cc = 0; cc < 2; ++cc) {
         uint32_t r[32];
         if (any) {
-          tmem_ld32(tO + lane_base + c * 32, r);
+          tmem_ld32(tO + lane_base + cb + cc * 32, r);
           tmem_wait_ld();
         } else {
 #pragma unroll
@@ -430,14 +532,14 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
         for (int e = 0; e < 16; ++e) {
           float o0 = __uint_as_float(r[2 * e]);
           float o1 = __uint_as_float(r[2 * e + 1]);
-          if (PV == FD_PV_FP8) {
-            o0 *= sVd[c * 32 + 2 * e] * (1.0f / PScale<PV>::SCALE);
-            o1 *= sVd[c * 32 + 2 * e + 1] * (1.0f / PScale<PV>::SCALE);
+          if (PV == FD_PV_FP8) {  // O and l both carry the P scale; V carries v_desc
+            o0 *= sVd[cb + cc * 32 + 2 * e];
+            o1 *= sVd[cb + cc * 32 + 2 * e + 1];
           }
-          w[e] = pack_bf16x2(o0 * inv_l, o1 * inv_l);
+          w[e] = pack_bf16x2(div_full(o0, l_div), div_full(o1, l_div));
         }
         if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+          uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
           dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
           dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
           dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
@@ -450,7 +552,7 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 5) tmem_dealloc(tmem_base, 256);
+  if (warp == WARP_MMA) tmem_dealloc(tmem_base, 256);
 }
 
 template <int QK, int KG, int PV>

@@ -8,6 +8,7 @@
 //   2. quant: per (bh, 128-row block): reduce the partials in chunk order,
 //      round the K mean to bf16, smooth, quantise, write codes and scales.
 //
+// Quotients use Triton's f32 divide (div.full.f32) like the reference kernels.
 // Reference arithmetic:
 //   _smooth_k          src/futudiffu/sage_attention.py:63-71 (bf16 mean, bf16 sub)
 //   INT8 Q/K per token src/futudiffu/sage_kernels.py:632-639, :656-663
@@ -156,8 +157,8 @@ __global__ void __launch_bounds__(256) quant_kernel(
     if (pv_fp8) {
       float am = 0.f;
       for (int i = 0; i < nchunks; ++i) am = fmaxf(am, ws_amax[(bh * nchunks + i) * 128 + c]);
-      sh_vinv[c] = __fdiv_rn(448.0f, fmaxf(am, 1e-12f));
-      if (blk == 0) v_desc[bh * 128 + c] = __fdiv_rn(am, 448.0f);
+      sh_vinv[c] = div_full(448.0f, fmaxf(am, 1e-12f));
+      if (blk == 0) v_desc[bh * 128 + c] = div_full(am, 448.0f);
     }
   }
   __syncthreads();
@@ -186,17 +187,17 @@ __global__ void __launch_bounds__(256) quant_kernel(
 #pragma unroll
       for (int w = 1; w < 8; ++w) blkmax = fmaxf(blkmax, sh_red[w]);
       if (threadIdx.x == 0)
-        q_desc[bh * q_desc_stride + blk] = __fdiv_rn(blkmax, qmax) * sm_scale_log2e;
+        q_desc[bh * q_desc_stride + blk] = div_full(blkmax, qmax) * sm_scale_log2e;
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int64_t n = r0 + rl + 16 * i;
       const float am = (q_gran == FD_GRAN_BLOCK) ? blkmax : rowmax[i];
-      const float inv = __fdiv_rn(qmax, fmaxf(am, 1e-12f));
+      const float inv = div_full(qmax, fmaxf(am, 1e-12f));
       if (n < N) {
         *reinterpret_cast<uint2*>(q_codes + (bh * N + n) * 128 + cg * 8) = quant_row8<QK>(x[i], inv);
         if (q_gran == FD_GRAN_TOKEN && cg == 0)
-          q_desc[bh * q_desc_stride + n] = __fdiv_rn(am, qmax) * sm_scale_log2e;
+          q_desc[bh * q_desc_stride + n] = div_full(am, qmax) * sm_scale_log2e;
       } else if (q_gran == FD_GRAN_TOKEN && cg == 0 && n < q_desc_stride) {
         q_desc[bh * q_desc_stride + n] = 0.f;
       }
@@ -239,17 +240,17 @@ __global__ void __launch_bounds__(256) quant_kernel(
       }
       if (threadIdx.x < 2) {
         const int64_t kb = (int64_t)blk * 2 + threadIdx.x;
-        if (kb * 64 < N) k_desc[bh * k_desc_stride + kb] = __fdiv_rn(hmax[threadIdx.x], qmax);
+        if (kb * 64 < N) k_desc[bh * k_desc_stride + kb] = div_full(hmax[threadIdx.x], qmax);
       }
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int64_t n = r0 + rl + 16 * i;
       const float am = (k_gran == FD_GRAN_BLOCK) ? hmax[i >> 2] : rowmax[i];
-      const float inv = __fdiv_rn(qmax, fmaxf(am, 1e-12f));
+      const float inv = div_full(qmax, fmaxf(am, 1e-12f));
       if (n < N) {
         *reinterpret_cast<uint2*>(k_codes + (bh * N + n) * 128 + cg * 8) = quant_row8<QK>(x[i], inv);
-        if (k_gran == FD_GRAN_TOKEN && cg == 0) k_desc[bh * k_desc_stride + n] = __fdiv_rn(am, qmax);
+        if (k_gran == FD_GRAN_TOKEN && cg == 0) k_desc[bh * k_desc_stride + n] = div_full(am, qmax);
       } else if (k_gran == FD_GRAN_TOKEN && cg == 0 && n < k_desc_stride) {
         k_desc[bh * k_desc_stride + n] = 0.f;
       }

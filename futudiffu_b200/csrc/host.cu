@@ -69,7 +69,24 @@ int encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void*
   return FD_OK;
 }
 
+__global__ void div_full_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                float* __restrict__ out, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = div_full(a[i], b[i]);
+}
+
 }  // namespace fd
+
+extern "C" int fd_div_full_f32(const float* a, const float* b, float* out, int64_t n, void* stream) {
+  FD_CHECK_ARG(n >= 0, "negative size");
+  if (n == 0) return FD_OK;
+  FD_CHECK_ARG(a && b && out, "null pointer");
+  int64_t grid = (n + 255) / 256;
+  if (grid > 4096) grid = 4096;
+  fd::div_full_kernel<<<(unsigned)grid, 256, 0, (cudaStream_t)stream>>>(a, b, out, n);
+  return fd::check_launch("div_full");
+}
 
 extern "C" const char* fd_version(void) { return "futudiffu_b200 0.1 sm_100a"; }
 

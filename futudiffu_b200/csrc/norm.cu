@@ -8,20 +8,13 @@
 // P3: one warp per (token, head): each lane owns two RoPE pairs (4 values)
 // of Q and K and 4 values of V.
 //
-// Arithmetic follows the Triton kernels: fp32 throughout, mean of squares
-// by a correctly rounded divide, rrms = 1 / sqrt.approx(mean + eps)
-// (Triton's tl.sqrt is the approximate square root, `1.0 / x` the IEEE
-// divide), products evaluated left to right.
+// Arithmetic follows the Triton kernels: fp32 throughout, mean of squares and
+// rrms = 1 / sqrt(mean + eps) with Triton's lowerings of `/` (div.full.f32) and
+// tl.sqrt (sqrt.approx.f32), products evaluated left to right.
 #include "fd_common.cuh"
 #include "fd_host.h"
 
 namespace fd {
-
-FD_DEV float sqrt_approx(float x) {
-  float y;
-  asm("sqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 
 template <int DT>
 FD_DEV float load_elem(const void* p, int64_t i) {
@@ -73,8 +66,8 @@ __global__ void __launch_bounds__(256) rms_row_kernel(const __nv_bfloat16* __res
       }
     }
     ss = warp_sum(ss);
-    const float mean_sq = __fdiv_rn(ss, (float)dim);
-    const float rrms = __fdiv_rn(1.0f, sqrt_approx(mean_sq + eps));
+    const float mean_sq = div_full(ss, (float)dim);
+    const float rrms = div_full(1.0f, sqrt_approx(mean_sq + eps));
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int c = (lane + 32 * j);
@@ -170,8 +163,8 @@ __global__ void __launch_bounds__(256) qkv_post_kernel(const __nv_bfloat16* __re
     float sk = k[0] * k[0] + k[1] * k[1] + k[2] * k[2] + k[3] * k[3];
     sq = warp_sum(sq);
     sk = warp_sum(sk);
-    const float rq = __fdiv_rn(1.0f, sqrt_approx(__fdiv_rn(sq, (float)HD) + eps));
-    const float rk = __fdiv_rn(1.0f, sqrt_approx(__fdiv_rn(sk, (float)HD) + eps));
+    const float rq = div_full(1.0f, sqrt_approx(div_full(sq, (float)HD) + eps));
+    const float rk = div_full(1.0f, sqrt_approx(div_full(sk, (float)HD) + eps));
     const float wqa[4] = {wq.x, wq.y, wq.z, wq.w};
     const float wka[4] = {wk.x, wk.y, wk.z, wk.w};
     float qo[4], ko[4];

@@ -11,10 +11,10 @@
 
 namespace fd {
 
-// IEEE-exact forms of the reference's divides (Triton and torch both lower
-// fp32 `/` to a correctly rounded divide).
-FD_DEV float quant_mult(float amax) { return __fdiv_rn(448.0f, fmaxf(amax, 1e-12f)); }
-FD_DEV float dequant_scale(float amax) { return fmaxf(__fdiv_rn(amax, 448.0f), 1e-12f); }
+// The reference quantisers are Triton code; their divides are Triton's f32 `/`
+// (div.full.f32, see fd_common.cuh).
+FD_DEV float quant_mult(float amax) { return div_full(448.0f, fmaxf(amax, 1e-12f)); }
+FD_DEV float dequant_scale(float amax) { return fmaxf(div_full(amax, 448.0f), 1e-12f); }
 
 // The reference clamps to +-448 before the cast; the saturating cvt would do
 // the same, the explicit clamp keeps NaN handling identical as well.
@@ -174,8 +174,8 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict_
 }
 
 // ---------------------------------------------------------------- G4
-// Triton lowers fp32 tl.exp(x) to ex2.approx.f32(x * log2(e)); the same
-// two instructions are used here.
+// Triton lowers fp32 tl.exp(x) to ex2.approx.f32(x * log2(e)) (measured: bit
+// identical); the same two instructions are used here.
 FD_DEV float exp_like_triton(float x) {
   float y;
   asm("{\n\t.reg .f32 t;\n\t"
@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(256) silu_gate_quant_kernel(const __nv_bfloat1
     load8<__nv_bfloat16>(x + m * 2 * N + N + nb * 128 + sub * 8, w3);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float sig = __fdiv_rn(1.0f, 1.0f + exp_like_triton(-w1[i]));
+      const float sig = div_full(1.0f, 1.0f + exp_like_triton(-w1[i]));
       v[i] = (w1[i] * sig) * w3[i];
     }
     const float amax = half_warp_max(amax8(v));
@@ -256,7 +256,7 @@ __global__ void __launch_bounds__(256) gelu_requant_kernel(const uint8_t* __rest
       __nv_fp8_e4m3 q;
       q.__x = (cw[j / 4] >> ((j % 4) * 8)) & 0xFF;
       const float a = float(q) * sc;
-      v[j] = a * 0.5f * (1.0f + erff(__fdiv_rn(a, 1.41421356237f)));
+      v[j] = a * 0.5f * (1.0f + erff(div_full(a, 1.41421356237f)));
     }
     const float amax = half_warp_max(amax8(v));
     const float qm = quant_mult(amax);

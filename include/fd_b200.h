@@ -62,6 +62,12 @@ const char* fd_last_error(void);
  * Synchronises the device.  Returns FD_OK or FD_ERR_CUDA. */
 int fd_get_status(unsigned int* out, int clear);
 
+/* Numerics hook; no counterpart in the reference.  out[i] = a[i] / b[i] with the
+ * f32 divide every quantiser here uses: PTX div.full.f32, which is what the
+ * reference's Triton kernels compile `/` to (measured bit-identical on the B200).
+ * Parity tests evaluate the CPU oracle's scale arithmetic with it. */
+int fd_div_full_f32(const float* a, const float* b, float* out, int64_t n, void* stream);
+
 /* G1 -- fp8_act_quant (src/futudiffu/fp8_kernels.py:54-90).
  * x (M, K) in x_dtype (bf16/f16/f32), K % block == 0, block == 128.
  * y (M, K) e4m3; s (M, K/block) f32 with s = max(amax/448, 1e-12),

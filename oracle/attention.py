@@ -19,7 +19,7 @@ import math
 
 import torch
 
-from .quant import div_ieee
+from .quant import triton_div
 
 LOG2E = math.log2(math.e)
 E4M3 = torch.float8_e4m3fn
@@ -51,11 +51,11 @@ def quant_rows(x: torch.Tensor, kind: str, rows_per_scale: int = 1, extra_scale:
     pad = nb * R - N
     xp = torch.nn.functional.pad(xf, (0, 0, 0, pad)) if pad else xf
     amax = xp.reshape(BH, nb, R * D).abs().amax(dim=-1)
-    inv = div_ieee(qmax, torch.clamp(amax, min=1e-12))
+    inv = triton_div(qmax, torch.clamp(amax, min=1e-12))
     inv_rows = inv.repeat_interleave(R, dim=1)[:, :N]
     y = xf * inv_rows.unsqueeze(-1)
     codes = y.to(torch.int8) if kind == "int8" else y.to(E4M3)
-    desc = div_ieee(amax, qmax) * torch.tensor(extra_scale, dtype=torch.float32)
+    desc = triton_div(amax, qmax) * torch.tensor(extra_scale, dtype=torch.float32)
     return codes, desc
 
 
@@ -63,9 +63,9 @@ def quant_v_per_channel(v: torch.Tensor):
     """V (BH, N, D) -> e4m3 codes with one scale per (bh, d) over the sequence."""
     vf = v.cpu().float()
     amax = vf.abs().amax(dim=1)  # (BH, D)
-    inv = div_ieee(448.0, torch.clamp(amax, min=1e-12))
+    inv = triton_div(448.0, torch.clamp(amax, min=1e-12))
     codes = (vf * inv.unsqueeze(1)).clamp(-448.0, 448.0).to(E4M3)
-    return codes, div_ieee(amax, 448.0)
+    return codes, triton_div(amax, 448.0)
 
 
 def _mask_rows(block_mask, BH: int, N: int, tile: int):
@@ -127,12 +127,12 @@ def attention_forward(
             pv = (p.to(torch.bfloat16).to(torch.float64) @ vb[:, n0:n1].to(torch.float64)).to(torch.float32)
         elif pv_quant == "fp8_tile":
             pam = p.abs().amax(dim=-1)
-            p8 = (p * div_ieee(448.0, torch.clamp(pam, min=1e-12)).unsqueeze(-1)).to(E4M3)
+            p8 = (p * triton_div(448.0, torch.clamp(pam, min=1e-12)).unsqueeze(-1)).to(E4M3)
             vt = vb[:, n0:n1].float()
             vam = vt.abs().amax(dim=1)
-            v8 = (vt * div_ieee(448.0, torch.clamp(vam, min=1e-12)).unsqueeze(1)).to(E4M3)
+            v8 = (vt * triton_div(448.0, torch.clamp(vam, min=1e-12)).unsqueeze(1)).to(E4M3)
             pv = (p8.to(torch.float64) @ v8.to(torch.float64)).to(torch.float32)
-            pv = (pv * div_ieee(pam, 448.0).unsqueeze(-1)) * div_ieee(vam, 448.0).unsqueeze(1)
+            pv = (pv * triton_div(pam, 448.0).unsqueeze(-1)) * triton_div(vam, 448.0).unsqueeze(1)
         elif pv_quant == "fp8_channel":
             p8 = (p * 448.0).clamp(max=448.0).to(E4M3)
             pv = (p8.to(torch.float64) @ vc[:, n0:n1].to(torch.float64)).to(torch.float32)

@@ -14,6 +14,16 @@ from tests.helpers import cosine, e4m3_bits
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(autouse=True)
+def _triton_division():
+    """Evaluate the oracle's Triton-kernel quotients with the device's div.full.f32."""
+    from futudiffu_b200._lib import device_divide
+    from oracle import quant as _OQ
+
+    with _OQ.division(device_divide):
+        yield
+
 SM = 1.0 / math.sqrt(128)
 
 

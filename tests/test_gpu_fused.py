@@ -12,6 +12,16 @@ from tests.helpers import bf16_ulp_diff, cosine
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def _triton_division():
+    """Evaluate the oracle's Triton-kernel quotients with the device's div.full.f32."""
+    from futudiffu_b200._lib import device_divide
+    from oracle import quant as _OQ
+
+    with _OQ.division(device_divide):
+        yield
+
+
 def _close(a, b):
     # one rounding to bf16 in both; rsqrt/sum order may move the last bit
     assert torch.allclose(a.float().cpu(), b.float(), rtol=2**-7, atol=2**-7)

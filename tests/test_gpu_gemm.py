@@ -13,6 +13,16 @@ from tests.helpers import cosine
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def _triton_division():
+    """Evaluate the oracle's Triton-kernel quotients with the device's div.full.f32."""
+    from futudiffu_b200._lib import device_divide
+    from oracle import quant as _OQ
+
+    with _OQ.division(device_divide):
+        yield
+
+
 def _operands(M, N, K, seed, b_layout=0):
     g = gen(seed)
     x = torch.randn(M, K, generator=g).to(torch.bfloat16)

@@ -12,6 +12,16 @@ from tests.helpers import e4m3_bits, e4m3_step_diff
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def _triton_division():
+    """Evaluate the oracle's Triton-kernel quotients with the device's div.full.f32."""
+    from futudiffu_b200._lib import device_divide
+    from oracle import quant as _OQ
+
+    with _OQ.division(device_divide):
+        yield
+
+
 def _x(shape, seed, scale=3.0, dtype=torch.bfloat16):
     g = gen(seed)
     row_scale = torch.rand(*shape[:-1], 1, generator=g) * scale + 1e-3
@@ -144,3 +154,16 @@ def test_quant_no_device_fault_status(cuda_device):
     from futudiffu_b200 import check_status
 
     check_status()
+
+
+def test_device_divide_within_two_ulp_of_ieee(cuda_device):
+    from futudiffu_b200._lib import device_divide
+
+    g = gen(123)
+    a = torch.rand(1 << 20, generator=g) * 500
+    b = torch.rand(1 << 20, generator=g) * 20 + 1e-6
+    got = device_divide(a, b)
+    ref = OQ.div_ieee(a, b)
+    ulp = (got.view(torch.int32) - ref.view(torch.int32)).abs()
+    assert ulp.max().item() <= 2
+    assert (device_divide(torch.tensor([448.0]), torch.tensor([448.0])) == 1.0).all()
