@@ -147,73 +147,158 @@ FD_DEV void drain_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
-// Row max of one thread's 64 logits.  Per-block K: x holds raw scores and the
-// 64 keys share the factor c >= 0; per-token K: x is already scaled.  The
-// partial variant first sets out-of-range / masked keys to -inf.
-template <int KG, bool FULL>
-FD_DEV float half_max(float (&x)[64], float c, int col0, int N, bool half_ok) {
-  if (!FULL) {
-#pragma unroll
-    for (int e = 0; e < 64; ++e)
-      if (!(half_ok && col0 + e < N)) x[e] = -INFINITY;
-  }
-  const float m = max_reduce64(x);
-  if (KG == FD_GRAN_BLOCK) return m == -INFINITY ? -INFINITY : m * c;
-  return m;
+// f16x2 helpers for the e4m3-P path: P only needs e4m3 precision (3 mantissa
+// bits), so its exp2 runs as one ex2.approx.f16x2 per key pair (two results per
+// MUFU issue) and converts straight to e4m3x2.
+FD_DEV uint32_t f32x2_to_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+FD_DEV uint32_t ex2_f16x2(uint32_t x) {
+  uint32_t r;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(x));
+  return r;
+}
+FD_DEV uint32_t f16x2_to_e4m3x2(uint32_t h) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(r) : "r"(h));
+  return r;
+}
+FD_DEV uint32_t hadd2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+FD_DEV float f16x2_sum_f32(uint32_t h) {
+  float lo, hi;
+  asm("{\n\t.reg .f16 l, u;\n\tmov.b32 {l, u}, %2;\n\tcvt.f32.f16 %0, l;\n\tcvt.f32.f16 %1, u;\n\t}"
+      : "=f"(lo), "=f"(hi)
+      : "r"(h));
+  return lo + hi;
 }
 
-// P = exp2(L + nb) for one thread's 64 keys, written to the shared-memory P tile
-// in the 128-byte-swizzled K-major layout the PV MMA reads; returns the sum of P.
-template <int KG, int PV, bool FULL>
-FD_DEV float exp_store(const float (&x)[64], float c, float nb, uint8_t* sP, int row, int h) {
-  uint64_t acc = pk(0.f, 0.f);
-  auto pexp = [&](int e, float& p0, float& p1) {
-    uint64_t a;
-    if (KG == FD_GRAN_BLOCK) a = fma2(pk(x[e], x[e + 1]), pk(c, c), pk(nb, nb));
-    else a = add2(pk(x[e], x[e + 1]), pk(nb, nb));
-    float a0, a1;
-    unpk(a, a0, a1);
-    p0 = ex2_approx(a0);
-    p1 = ex2_approx(a1);
-    if (!FULL) {  // masked keys: -inf (times 0 for an all-zero K block would be NaN)
-      if (x[e] == -INFINITY) p0 = 0.f;
-      if (x[e + 1] == -INFINITY) p1 = 0.f;
-    }
-    acc = add2(acc, pk(p0, p1));
-  };
-  if (PV == FD_PV_FP8) {
-    // this thread's keys are the 16-byte chunks 4h .. 4h+3 of the 128-byte P row
+// Exact s32 -> f32 of a pair of QK^T scores: |s| <= 128*127*127 < 2^22, so adding
+// the bit pattern of 1.5*2^23 and subtracting 1.5*2^23 is exact.
+FD_DEV uint64_t s32x2_to_f32x2(uint32_t a, uint32_t b) {
+  return add2(pk(__int_as_float((int)a + 0x4B400000), __int_as_float((int)b + 0x4B400000)),
+              pk(-12582912.0f, -12582912.0f));
+}
+
+// Pass 1 over one 32-key chunk: the maximum score.  Per-block K: maximum of the
+// raw scores (the 64 keys share one factor, applied by the caller); per-token K:
+// maximum of the scaled logits (s * q_desc) * k_desc (reference order).
+template <int QK, int KG, bool FULL>
+FD_DEV float chunk_max(const uint32_t (&r)[32], int col0, int N, bool half_ok, float qd, const float* kd) {
+  if (KG == FD_GRAN_BLOCK && QK == FD_QK_INT8) {
+    int m0 = INT_MIN, m1 = INT_MIN, m2 = INT_MIN, m3 = INT_MIN;
 #pragma unroll
-    for (int ch = 0; ch < 4; ++ch) {
-      uint32_t w[4];
+    for (int e = 0; e < 32; e += 4) {
+      int v[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float p0, p1, p2, p3;
-        pexp(16 * ch + 4 * e, p0, p1);
-        pexp(16 * ch + 4 * e + 2, p2, p3);
-        w[e] = f32x2_to_e4m3x2(p0, p1) | (f32x2_to_e4m3x2(p2, p3) << 16);
+      for (int u = 0; u < 4; ++u) {
+        v[u] = (int)r[e + u];
+        if (!FULL && !(half_ok && col0 + e + u < N)) v[u] = INT_MIN;
       }
-      *reinterpret_cast<uint4*>(sP + row * 128 + (((4 * h + ch) ^ (row & 7)) << 4)) =
-          make_uint4(w[0], w[1], w[2], w[3]);
+      m0 = max(m0, v[0]);
+      m1 = max(m1, v[1]);
+      m2 = max(m2, v[2]);
+      m3 = max(m3, v[3]);
     }
+    const int m = max(max(m0, m1), max(m2, m3));
+    return m == INT_MIN ? -INFINITY : (float)m;
   } else {
-    // bf16: this thread's 64 keys are panel h (one 128-byte row of 8 chunks)
+    float x[32];
 #pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
-      uint32_t w[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float p0, p1;
-        pexp(8 * ch + 2 * e, p0, p1);
-        w[e] = pack_bf16x2(p0, p1);
+    for (int e = 0; e < 32; e += 2) {
+      if (QK == FD_QK_INT8) {
+        unpk(s32x2_to_f32x2(r[e], r[e + 1]), x[e], x[e + 1]);
+      } else {
+        x[e] = __uint_as_float(r[e]);
+        x[e + 1] = __uint_as_float(r[e + 1]);
       }
-      *reinterpret_cast<uint4*>(sP + h * (BQ * 128) + row * 128 + ((ch ^ (row & 7)) << 4)) =
-          make_uint4(w[0], w[1], w[2], w[3]);
+      if (KG == FD_GRAN_TOKEN)
+        unpk(mul2(mul2(pk(x[e], x[e + 1]), pk(qd, qd)), pk(kd[e], kd[e + 1])), x[e], x[e + 1]);
+    }
+    if (!FULL) {
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        if (!(half_ok && col0 + e < N)) x[e] = -INFINITY;
+    }
+    float m0 = max3(x[0], x[1], x[2]), m1 = max3(x[3], x[4], x[5]);
+#pragma unroll
+    for (int e = 6; e < 30; e += 4) {
+      m0 = max3(m0, x[e], x[e + 1]);
+      m1 = max3(m1, x[e + 2], x[e + 3]);
+    }
+    return max3(m0, m1, fmaxf(x[30], x[31]));
+  }
+}
+
+// Pass 2 over one 32-key chunk: P = exp2(L + nb) written into the shared-memory
+// P tile (128-byte swizzled, K-major) at 32-key group g of the row; returns the
+// chunk's sum of P.  nb folds in -(m_ref - log2 SCALE).
+template <int QK, int KG, int PV, bool FULL>
+FD_DEV float chunk_exp_store(const uint32_t (&r)[32], int col0, int N, bool half_ok, float qd,
+                             const float* kd, float c, float nb, uint8_t* sP, int row, int g) {
+  float a[32];
+#pragma unroll
+  for (int e = 0; e < 32; e += 2) {
+    uint64_t v;
+    if (QK == FD_QK_INT8) v = s32x2_to_f32x2(r[e], r[e + 1]);
+    else v = pk(__uint_as_float(r[e]), __uint_as_float(r[e + 1]));
+    if (KG == FD_GRAN_BLOCK) {
+      v = fma2(v, pk(c, c), pk(nb, nb));
+    } else {
+      v = add2(mul2(mul2(v, pk(qd, qd)), pk(kd[e], kd[e + 1])), pk(nb, nb));
+    }
+    unpk(v, a[e], a[e + 1]);
+    if (!FULL) {
+      if (!(half_ok && col0 + e < N)) a[e] = -INFINITY;
+      if (!(half_ok && col0 + e + 1 < N)) a[e + 1] = -INFINITY;
     }
   }
-  float s0, s1;
-  unpk(acc, s0, s1);
-  return s0 + s1;
+  if (PV == FD_PV_FP8) {
+    uint32_t h[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) h[u] = ex2_f16x2(f32x2_to_f16x2(a[2 * u], a[2 * u + 1]));
+    // 32 keys = two 16-byte chunks (2g, 2g+1) of the 128-byte e4m3 P row
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        w[e] = f16x2_to_e4m3x2(h[8 * k + 2 * e]) | (f16x2_to_e4m3x2(h[8 * k + 2 * e + 1]) << 16);
+      *reinterpret_cast<uint4*>(sP + row * 128 + (((2 * g + k) ^ (row & 7)) << 4)) =
+          make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    // sum of P: f16 pairwise tree (partials <= 16 * 448) then f32
+#pragma unroll
+    for (int st = 1; st < 16; st <<= 1)
+#pragma unroll
+      for (int u = 0; u < 16; u += 2 * st) h[u] = hadd2(h[u], h[u + st]);
+    return f16x2_sum_f32(h[0]);
+  } else {
+    uint64_t acc = pk(0.f, 0.f);
+    uint32_t w[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const float p0 = ex2_approx(a[2 * u]), p1 = ex2_approx(a[2 * u + 1]);
+      acc = add2(acc, pk(p0, p1));
+      w[u] = pack_bf16x2(p0, p1);
+    }
+    // 32 keys = four 16-byte chunks of the 128-byte bf16 panel row (keys 64h..64h+63)
+    const int panel = g >> 1;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int ch = (g & 1) * 4 + k;
+      *reinterpret_cast<uint4*>(sP + panel * (BQ * 128) + row * 128 + ((ch ^ (row & 7)) << 4)) =
+          make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+    }
+    float s0, s1;
+    unpk(acc, s0, s1);
+    return s0 + s1;
+  }
 }
 
 // QK: FD_QK_INT8 / FD_QK_FP8; KG: k granularity; PV: FD_PV_BF16 / FD_PV_FP8
@@ -429,38 +514,18 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
         if (!mbar_wait(&bKfull[s], use & 1, abort_flag)) { ok = false; break; }
       }
       tc_fence_after();
-      float x[64];
-      {
-        uint32_t r[2][32];
-        tmem_ld32(tS + lane_base + cb, r[0]);
-        tmem_ld32(tS + lane_base + cb + 32, r[1]);
+      const float* kd = sKd + s * 128 + cb;  // per-token K scales of this thread's keys
+      // ---- pass 1: row max over this thread's 64 keys (two 32-key chunks from TMEM)
+      float mloc = -INFINITY;
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t r[32];
+        tmem_ld32(tS + lane_base + cb + 32 * cc, r);
         tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bSfree);  // the tensor core may overwrite S now
-#pragma unroll
-        for (int e = 0; e < 64; e += 2) {
-          if (QK == FD_QK_INT8) {
-            // exact s32 -> f32: |s| <= 128*127*127 < 2^22, so adding the bit pattern
-            // of 1.5*2^23 and subtracting 1.5*2^23 is exact
-            const float a = __int_as_float((int)r[e >> 5][e & 31] + 0x4B400000);
-            const float b = __int_as_float((int)r[e >> 5][(e & 31) + 1] + 0x4B400000);
-            unpk(add2(pk(a, b), pk(-12582912.0f, -12582912.0f)), x[e], x[e + 1]);
-          } else {
-            x[e] = __uint_as_float(r[e >> 5][e & 31]);
-            x[e + 1] = __uint_as_float(r[e >> 5][(e & 31) + 1]);
-          }
-        }
+        mloc = fmaxf(mloc, full ? chunk_max<QK, KG, true>(r, col0 + 32 * cc, p.N, my_half_ok, qd, kd + 32 * cc)
+                                : chunk_max<QK, KG, false>(r, col0 + 32 * cc, p.N, my_half_ok, qd, kd + 32 * cc));
       }
-      if (KG == FD_GRAN_TOKEN) {
-        // reference order: (s * q_desc) * k_desc, per key
-        const float* kd = sKd + s * 128 + cb;
-#pragma unroll
-        for (int e = 0; e < 64; e += 2)
-          unpk(mul2(mul2(pk(x[e], x[e + 1]), pk(qd, qd)), pk(kd[e], kd[e + 1])), x[e], x[e + 1]);
-      }
-      const float mloc = full ? half_max<KG, true>(x, c, col0, p.N, my_half_ok)
-                              : half_max<KG, false>(x, c, col0, p.N, my_half_ok);
+      if (KG == FD_GRAN_BLOCK) mloc = mloc == -INFINITY ? -INFINITY : mloc * c;  // c >= 0
       float* rm = red_max + (i & 1) * 256;
       rm[h * 128 + row] = mloc;
       named_bar_sync(2 + quad, 64);
@@ -494,8 +559,22 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
       if (i > 0) {
         if (!mbar_wait(bOready, (i - 1) & 1, abort_flag)) { ok = false; break; }
       }
-      l += full ? exp_store<KG, PV, true>(x, c, nb, sP, row, h)
-                : exp_store<KG, PV, false>(x, c, nb, sP, row, h);
+      // ---- pass 2: P = exp2(L + nb) into shared memory, row-sum into l
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t r[32];
+        tmem_ld32(tS + lane_base + cb + 32 * cc, r);
+        tmem_wait_ld();
+        if (cc == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bSfree);  // the tensor core may overwrite S now
+        }
+        l += full ? chunk_exp_store<QK, KG, PV, true>(r, col0 + 32 * cc, p.N, my_half_ok, qd, kd + 32 * cc, c,
+                                                      nb, sP, row, 2 * h + cc)
+                  : chunk_exp_store<QK, KG, PV, false>(r, col0 + 32 * cc, p.N, my_half_ok, qd, kd + 32 * cc, c,
+                                                       nb, sP, row, 2 * h + cc);
+      }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();

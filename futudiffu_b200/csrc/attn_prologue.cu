@@ -51,18 +51,24 @@ __global__ void __launch_bounds__(256) colstats_kernel(const __nv_bfloat16* __re
   const int cg = threadIdx.x & 15, rl = threadIdx.x >> 4;
   float s[8] = {0, 0, 0, 0, 0, 0, 0, 0}, a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   const int64_t r0 = (int64_t)chunk * kChunkRows;
-  for (int r = rl; r < kChunkRows; r += 16) {
-    const int64_t n = r0 + r;
-    if (n >= N) break;
-    const int64_t off = (bh * N + n) * 128 + cg * 8;
-    float x[8];
-    if (do_k) {
-      unpack8(__ldg(reinterpret_cast<const uint4*>(k + off)), x);
+  const int rows = (int)((N - r0) < kChunkRows ? (N - r0) : kChunkRows);
+  // four rows per lane per iteration: eight independent 16-byte loads in flight
+  for (int r = rl; r < rows; r += 64) {
+    uint4 kv[4], vv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const bool ok = r + 16 * u < rows;
+      const int64_t off = (bh * N + r0 + r + 16 * u) * 128 + cg * 8;
+      kv[u] = (do_k && ok) ? __ldg(reinterpret_cast<const uint4*>(k + off)) : make_uint4(0, 0, 0, 0);
+      vv[u] = (do_v && ok) ? __ldg(reinterpret_cast<const uint4*>(v + off)) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float x[8];
+      unpack8(kv[u], x);
 #pragma unroll
       for (int e = 0; e < 8; ++e) s[e] += x[e];
-    }
-    if (do_v) {
-      unpack8(__ldg(reinterpret_cast<const uint4*>(v + off)), x);
+      unpack8(vv[u], x);
 #pragma unroll
       for (int e = 0; e < 8; ++e) a[e] = fmaxf(a[e], fabsf(x[e]));
     }
@@ -120,8 +126,9 @@ FD_DEV float half_max(float v) {
   return v;
 }
 
-// grid (ceil(N/128), BH), 256 threads.  Thread t handles column group
-// (t & 15) * 8 of rows (t >> 4) + 16 i, i = 0..7, of the 128-row block.
+// grid (ceil(N/128), BH, 2 or 3), 256 threads; blockIdx.z selects Q, K or V, so
+// the three tensors are quantised by independent CTAs.  Thread t handles column
+// group (t & 15) * 8 of rows (t >> 4) + 16 i, i = 0..7, of the 128-row block.
 template <int QK>
 __global__ void __launch_bounds__(256) quant_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
@@ -133,6 +140,7 @@ __global__ void __launch_bounds__(256) quant_kernel(
     int64_t k_desc_stride) {
   const int blk = blockIdx.x;
   const int64_t bh = blockIdx.y;
+  const int which = blockIdx.z;  // 0 Q, 1 K, 2 V
   const int cg = threadIdx.x & 15, rl = threadIdx.x >> 4;
   const int64_t r0 = (int64_t)blk * 128;
   const float qmax = (QK == FD_QK_INT8) ? 127.0f : 448.0f;
@@ -142,9 +150,9 @@ __global__ void __launch_bounds__(256) quant_kernel(
   __shared__ float sh_red[8];
   __shared__ float sh_red2[2][8];
 
-  if (threadIdx.x < 128) {
+  if (threadIdx.x < 128 && which != 0) {
     const int c = threadIdx.x;
-    if (smooth_k) {
+    if (which == 1 && smooth_k) {
       float tot = 0.f;
       for (int i = 0; i < nchunks; ++i) tot += ws_sum[(bh * nchunks + i) * 128 + c];
       // torch bf16 mean: fp32 accumulate, times 1/N, round to bf16
@@ -154,7 +162,7 @@ __global__ void __launch_bounds__(256) quant_kernel(
     } else {
       sh_mean[c] = 0.f;
     }
-    if (pv_fp8) {
+    if (which == 2) {
       float am = 0.f;
       for (int i = 0; i < nchunks; ++i) am = fmaxf(am, ws_amax[(bh * nchunks + i) * 128 + c]);
       sh_vinv[c] = div_full(448.0f, fmaxf(am, 1e-12f));
@@ -164,7 +172,7 @@ __global__ void __launch_bounds__(256) quant_kernel(
   __syncthreads();
 
   // ---------------- Q
-  {
+  if (which == 0) {
     float x[8][8];
     float rowmax[8];
     float blkmax = 0.f;
@@ -205,7 +213,7 @@ __global__ void __launch_bounds__(256) quant_kernel(
   }
 
   // ---------------- K (smoothed)
-  {
+  if (which == 1) {
     float x[8][8];
     float rowmax[8];
     float hmax[2] = {0.f, 0.f};  // rows 0..63 / 64..127 of the block
@@ -258,7 +266,7 @@ __global__ void __launch_bounds__(256) quant_kernel(
   }
 
   // ---------------- V (e4m3, per channel)
-  if (pv_fp8) {
+  if (which == 2) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int64_t n = r0 + rl + 16 * i;
@@ -327,7 +335,7 @@ extern "C" int fd_attn_quant(const void* q, const void* k, const void* v, int64_
     if (rc) return rc;
   }
   const int64_t qs = fd_desc_stride(N, q_gran, 128), ks = fd_desc_stride(N, k_gran, 64);
-  dim3 grid((unsigned)((N + 127) / 128), (unsigned)BH);
+  dim3 grid((unsigned)((N + 127) / 128), (unsigned)BH, pv_fp8 ? 3u : 2u);
 #define FD_Q_LAUNCH(QK)                                                                         \
   quant_kernel<QK><<<grid, 256, 0, st>>>(                                                       \
       (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, N, nchunks,   \
