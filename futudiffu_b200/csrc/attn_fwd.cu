@@ -147,92 +147,49 @@ FD_DEV void drain_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
-// f16x2 helpers for the e4m3-P path: P only needs e4m3 precision (3 mantissa
-// bits), so its exp2 runs as one ex2.approx.f16x2 per key pair (two results per
-// MUFU issue) and converts straight to e4m3x2.
-FD_DEV uint32_t f32x2_to_f16x2(float lo, float hi) {
+// Four f32 -> four e4m3 in one word (keys in byte order), RNE with saturation.
+FD_DEV uint32_t f32x4_to_e4m3x4(float a, float b, float c, float d) {
   uint32_t r;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  asm("{\n\t.reg .b16 lo, hi;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 lo, %2, %1;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f32 hi, %4, %3;\n\t"
+      "mov.b32 %0, {lo, hi};\n\t}"
+      : "=r"(r)
+      : "f"(a), "f"(b), "f"(c), "f"(d));
   return r;
-}
-FD_DEV uint32_t ex2_f16x2(uint32_t x) {
-  uint32_t r;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(x));
-  return r;
-}
-FD_DEV uint32_t f16x2_to_e4m3x2(uint32_t h) {
-  uint16_t r;
-  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(r) : "r"(h));
-  return r;
-}
-FD_DEV uint32_t hadd2(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-FD_DEV float f16x2_sum_f32(uint32_t h) {
-  float lo, hi;
-  asm("{\n\t.reg .f16 l, u;\n\tmov.b32 {l, u}, %2;\n\tcvt.f32.f16 %0, l;\n\tcvt.f32.f16 %1, u;\n\t}"
-      : "=f"(lo), "=f"(hi)
-      : "r"(h));
-  return lo + hi;
 }
 
-// Exact s32 -> f32 of a pair of QK^T scores: |s| <= 128*127*127 < 2^22, so adding
-// the bit pattern of 1.5*2^23 and subtracting 1.5*2^23 is exact.
-FD_DEV uint64_t s32x2_to_f32x2(uint32_t a, uint32_t b) {
-  return add2(pk(__int_as_float((int)a + 0x4B400000), __int_as_float((int)b + 0x4B400000)),
-              pk(-12582912.0f, -12582912.0f));
-}
+// INT8 QK^T scores are accumulated on top of the bit pattern of 1.5*2^23
+// (S_BIAS_BITS, written into the S columns before every QK^T): |s| <= 128*127*127
+// < 2^22, so the s32 accumulator holds exactly the bits of the float 1.5*2^23 + s.
+// The softmax then reads scores as floats with no integer conversion: the row
+// max is a float max of biased values, and s = biased - 1.5*2^23 exactly.
+constexpr uint32_t S_BIAS_BITS = 0x4B400000u;
+constexpr float S_BIAS = 12582912.0f;  // 1.5 * 2^23
 
-// Pass 1 over one 32-key chunk: the maximum score.  Per-block K: maximum of the
-// raw scores (the 64 keys share one factor, applied by the caller); per-token K:
-// maximum of the scaled logits (s * q_desc) * k_desc (reference order).
+// Pass 1 over 64 keys (two 32-key chunks): the maximum score.  Per-block K:
+// the maximum of the raw scores (still biased for INT8; the 64 keys share one
+// factor, applied by the caller); per-token K: the maximum of the scaled logits
+// (s * q_desc) * k_desc (reference order).
 template <int QK, int KG, bool FULL>
-FD_DEV float chunk_max(const uint32_t (&r)[32], int col0, int N, bool half_ok, float qd, const float* kd) {
-  if (KG == FD_GRAN_BLOCK && QK == FD_QK_INT8) {
-    int m0 = INT_MIN, m1 = INT_MIN, m2 = INT_MIN, m3 = INT_MIN;
+FD_DEV float chunk_max(const uint32_t (&r)[64], int col0, int N, bool half_ok, float qd, const float* kd) {
+  float x[64];
 #pragma unroll
-    for (int e = 0; e < 32; e += 4) {
-      int v[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        v[u] = (int)r[e + u];
-        if (!FULL && !(half_ok && col0 + e + u < N)) v[u] = INT_MIN;
-      }
-      m0 = max(m0, v[0]);
-      m1 = max(m1, v[1]);
-      m2 = max(m2, v[2]);
-      m3 = max(m3, v[3]);
+  for (int e = 0; e < 64; e += 2) {
+    x[e] = __uint_as_float(r[e]);
+    x[e + 1] = __uint_as_float(r[e + 1]);
+    if (KG == FD_GRAN_TOKEN) {
+      uint64_t v = pk(x[e], x[e + 1]);
+      if (QK == FD_QK_INT8) v = add2(v, pk(-S_BIAS, -S_BIAS));
+      unpk(mul2(mul2(v, pk(qd, qd)), pk(kd[e], kd[e + 1])), x[e], x[e + 1]);
     }
-    const int m = max(max(m0, m1), max(m2, m3));
-    return m == INT_MIN ? -INFINITY : (float)m;
-  } else {
-    float x[32];
-#pragma unroll
-    for (int e = 0; e < 32; e += 2) {
-      if (QK == FD_QK_INT8) {
-        unpk(s32x2_to_f32x2(r[e], r[e + 1]), x[e], x[e + 1]);
-      } else {
-        x[e] = __uint_as_float(r[e]);
-        x[e + 1] = __uint_as_float(r[e + 1]);
-      }
-      if (KG == FD_GRAN_TOKEN)
-        unpk(mul2(mul2(pk(x[e], x[e + 1]), pk(qd, qd)), pk(kd[e], kd[e + 1])), x[e], x[e + 1]);
-    }
-    if (!FULL) {
-#pragma unroll
-      for (int e = 0; e < 32; ++e)
-        if (!(half_ok && col0 + e < N)) x[e] = -INFINITY;
-    }
-    float m0 = max3(x[0], x[1], x[2]), m1 = max3(x[3], x[4], x[5]);
-#pragma unroll
-    for (int e = 6; e < 30; e += 4) {
-      m0 = max3(m0, x[e], x[e + 1]);
-      m1 = max3(m1, x[e + 2], x[e + 3]);
-    }
-    return max3(m0, m1, fmaxf(x[30], x[31]));
   }
+  if (!FULL) {
+#pragma unroll
+    for (int e = 0; e < 64; ++e)
+      if (!(half_ok && col0 + e < N)) x[e] = -INFINITY;
+  }
+  return max_reduce64(x);
 }
 
 // Pass 2 over one 32-key chunk: P = exp2(L + nb) written into the shared-memory
@@ -244,12 +201,11 @@ FD_DEV float chunk_exp_store(const uint32_t (&r)[32], int col0, int N, bool half
   float a[32];
 #pragma unroll
   for (int e = 0; e < 32; e += 2) {
-    uint64_t v;
-    if (QK == FD_QK_INT8) v = s32x2_to_f32x2(r[e], r[e + 1]);
-    else v = pk(__uint_as_float(r[e]), __uint_as_float(r[e + 1]));
+    uint64_t v = pk(__uint_as_float(r[e]), __uint_as_float(r[e + 1]));
     if (KG == FD_GRAN_BLOCK) {
-      v = fma2(v, pk(c, c), pk(nb, nb));
+      v = fma2(v, pk(c, c), pk(nb, nb));  // nb carries -S_BIAS * c for INT8
     } else {
+      if (QK == FD_QK_INT8) v = add2(v, pk(-S_BIAS, -S_BIAS));
       v = add2(mul2(mul2(v, pk(qd, qd)), pk(kd[e], kd[e + 1])), pk(nb, nb));
     }
     unpk(v, a[e], a[e + 1]);
@@ -259,25 +215,31 @@ FD_DEV float chunk_exp_store(const uint32_t (&r)[32], int col0, int N, bool half
     }
   }
   if (PV == FD_PV_FP8) {
-    uint32_t h[16];
+    // f32 exp2 (one MUFU op per key; the f16x2 form costs the same MUFU work plus
+    // packing), sum in f32 pairs, e4m3 pairs packed four keys per word
+    float pv[32];
+    uint64_t acc = pk(0.f, 0.f);
 #pragma unroll
-    for (int u = 0; u < 16; ++u) h[u] = ex2_f16x2(f32x2_to_f16x2(a[2 * u], a[2 * u + 1]));
+    for (int e = 0; e < 32; e += 2) {
+      pv[e] = ex2_approx(a[e]);
+      pv[e + 1] = ex2_approx(a[e + 1]);
+      acc = add2(acc, pk(pv[e], pv[e + 1]));
+    }
     // 32 keys = two 16-byte chunks (2g, 2g+1) of the 128-byte e4m3 P row
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       uint32_t w[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e)
-        w[e] = f16x2_to_e4m3x2(h[8 * k + 2 * e]) | (f16x2_to_e4m3x2(h[8 * k + 2 * e + 1]) << 16);
+      for (int q = 0; q < 4; ++q) {
+        const int e = 16 * k + 4 * q;
+        w[q] = f32x4_to_e4m3x4(pv[e], pv[e + 1], pv[e + 2], pv[e + 3]);
+      }
       *reinterpret_cast<uint4*>(sP + row * 128 + (((2 * g + k) ^ (row & 7)) << 4)) =
           make_uint4(w[0], w[1], w[2], w[3]);
     }
-    // sum of P: f16 pairwise tree (partials <= 16 * 448) then f32
-#pragma unroll
-    for (int st = 1; st < 16; st <<= 1)
-#pragma unroll
-      for (int u = 0; u < 16; u += 2 * st) h[u] = hadd2(h[u], h[u + st]);
-    return f16x2_sum_f32(h[0]);
+    float s0, s1;
+    unpk(acc, s0, s1);
+    return s0 + s1;
   } else {
     uint64_t acc = pk(0.f, 0.f);
     uint32_t w[16];
@@ -424,7 +386,7 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
         for (int k = 0; k < HD / 32; ++k) {
           const uint64_t ad = make_sdesc_sw128(aQ + k * 32, 16, 1024);
           const uint64_t bd = make_sdesc_sw128(bK + k * 32, 16, 1024);
-          if (QK == FD_QK_INT8) mma_i8_ss(tS, ad, bd, idesc_qk, k > 0);
+          if (QK == FD_QK_INT8) mma_i8_ss(tS, ad, bd, idesc_qk, 1u);  // onto S_BIAS_BITS
           else mma_f8f6f4_ss(tS, ad, bd, idesc_qk, k > 0);
         }
         tc_commit(bSfull);
@@ -432,12 +394,17 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
       };
       uint32_t i = 0;
       jcur = next_valid(0);
-      if (ok && jcur < p.n_kv_tiles) ok = issue_qk(0);
+      // bSfree phase k completes when the softmax has refilled S for QK^T(k):
+      // phase 0 after the initial fill, phase i + 1 once S(i) is in registers.
+      if (ok && jcur < p.n_kv_tiles) ok = mbar_wait(bSfree, 0, abort_flag);
+      if (ok && jcur < p.n_kv_tiles) {
+        tc_fence_after();
+        ok = issue_qk(0);
+      }
       while (ok && jcur < p.n_kv_tiles) {
         const int jn = next_valid(jcur + 1);
         if (jn < p.n_kv_tiles) {
-          // S is free once the softmax has pulled S(i) into registers
-          if (!mbar_wait(bSfree, i & 1, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(bSfree, (i + 1) & 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
           if (!issue_qk(i + 1)) { ok = false; break; }
         }
@@ -483,6 +450,15 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
     float* red_max = reinterpret_cast<float*>(smem + SM::OFF_RED);  // [parity][half][128]
     float* red_l = red_max + 2 * 2 * 128;                           // [half][128]
     if (PV == FD_PV_FP8 && h == 0) sVd[row] = p.v_desc[(int64_t)bh * HD + row];
+    // initial fill of this thread's S columns; the arrival releases QK^T(0)
+    if (QK == FD_QK_INT8) {
+      tmem_fill32(tS + lane_base + cb, S_BIAS_BITS);
+      tmem_fill32(tS + lane_base + cb + 32, S_BIAS_BITS);
+      tmem_wait_st();
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bSfree);
     named_bar_sync(1, NUM_SOFTMAX_WARPS * 32);
     const float qd = p.q_gran == FD_GRAN_TOKEN
                          ? p.q_desc[(int64_t)bh * p.q_desc_stride + (qrow < p.N ? qrow : 0)]
@@ -516,16 +492,18 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
       tc_fence_after();
       const float* kd = sKd + s * 128 + cb;  // per-token K scales of this thread's keys
       // ---- pass 1: row max over this thread's 64 keys (two 32-key chunks from TMEM)
-      float mloc = -INFINITY;
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        uint32_t r[32];
-        tmem_ld32(tS + lane_base + cb + 32 * cc, r);
+      float mloc;
+      {
+        uint32_t r[64];
+        tmem_ld64(tS + lane_base + cb, r);
         tmem_wait_ld();
-        mloc = fmaxf(mloc, full ? chunk_max<QK, KG, true>(r, col0 + 32 * cc, p.N, my_half_ok, qd, kd + 32 * cc)
-                                : chunk_max<QK, KG, false>(r, col0 + 32 * cc, p.N, my_half_ok, qd, kd + 32 * cc));
+        mloc = full ? chunk_max<QK, KG, true>(r, col0, p.N, my_half_ok, qd, kd)
+                    : chunk_max<QK, KG, false>(r, col0, p.N, my_half_ok, qd, kd);
       }
-      if (KG == FD_GRAN_BLOCK) mloc = mloc == -INFINITY ? -INFINITY : mloc * c;  // c >= 0
+      if (KG == FD_GRAN_BLOCK) {
+        if (QK == FD_QK_INT8) mloc -= S_BIAS;  // exact; -inf stays -inf
+        mloc = mloc == -INFINITY ? -INFINITY : mloc * c;  // c >= 0
+      }
       float* rm = red_max + (i & 1) * 256;
       rm[h * 128 + row] = mloc;
       named_bar_sync(2 + quad, 64);
@@ -554,7 +532,9 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
         m_ref = m_new;
       }
       // exp2 argument: L - (m_ref - log2 SCALE), so ex2 yields P already in its stored scale
-      const float nb = (m_ref == -INFINITY) ? 0.f : -(m_ref - PScale<PV>::LOG2_SCALE);
+      const float nb0 = (m_ref == -INFINITY) ? 0.f : -(m_ref - PScale<PV>::LOG2_SCALE);
+      // per-block INT8: fold the score bias into the offset, L + nb0 = b * c + (nb0 - S_BIAS * c)
+      const float nb = (KG == FD_GRAN_BLOCK && QK == FD_QK_INT8) ? fmaf(-S_BIAS, c, nb0) : nb0;
       // P buffer is free once PV(i-1) has completed
       if (i > 0) {
         if (!mbar_wait(bOready, (i - 1) & 1, abort_flag)) { ok = false; break; }
@@ -565,7 +545,9 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
         uint32_t r[32];
         tmem_ld32(tS + lane_base + cb + 32 * cc, r);
         tmem_wait_ld();
+        if (QK == FD_QK_INT8) tmem_fill32(tS + lane_base + cb + 32 * cc, S_BIAS_BITS);
         if (cc == 1) {
+          if (QK == FD_QK_INT8) tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(bSfree);  // the tensor core may overwrite S now
