@@ -30,6 +30,7 @@ DT_BF16, DT_F16, DT_F32, DT_E4M3, DT_I8 = 0, 1, 2, 3, 4
 QK_INT8, QK_FP8 = 0, 1
 GRAN_TOKEN, GRAN_BLOCK = 0, 1
 PV_BF16, PV_FP8 = 0, 1
+ACT_NONE, ACT_GELU_TANH, ACT_SILU_GATE = 0, 1, 2
 
 _DT_CODE = {
     torch.bfloat16: DT_BF16,
@@ -54,6 +55,7 @@ _SIGS: dict[str, list] = {
     "fd_fp8_weight_quant": [_P, _I, _P, _P, _L, _L, _I, _P],
     "fd_fp8_dequant_blockwise": [_P, _P, _P, _I, _L, _L, _I, _P],
     "fd_fp8_gemm_blockwise": [_P, _P, _P, _P, _P, _I, _P, _I, _L, _L, _L, _I, _P],
+    "fd_fp8_gemm_quant": [_P, _P, _P, _P, _P, _I, _P, _P, _L, _L, _L, _I, _P],
     "fd_fp8_silu_gate_quant": [_P, _P, _P, _L, _L, _I, _P],
     "fd_fp8_gelu_tanh_quant": [_P, _P, _P, _L, _L, _I, _P],
     "fd_fp8_gelu_requant": [_P, _P, _P, _P, _L, _L, _I, _P],

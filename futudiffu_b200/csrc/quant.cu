@@ -6,19 +6,10 @@
 // iteration and every global access is a fully coalesced 512-byte warp
 // transaction.  Grids are sized to a multiple of the SM count and stride
 // over the work.
-#include "fd_common.cuh"
+#include "fd_act.cuh"
 #include "fd_host.h"
 
 namespace fd {
-
-// The reference quantisers are Triton code; their divides are Triton's f32 `/`
-// (div.full.f32, see fd_common.cuh).
-FD_DEV float quant_mult(float amax) { return div_full(448.0f, fmaxf(amax, 1e-12f)); }
-FD_DEV float dequant_scale(float amax) { return fmaxf(div_full(amax, 448.0f), 1e-12f); }
-
-// The reference clamps to +-448 before the cast; the saturating cvt would do
-// the same, the explicit clamp keeps NaN handling identical as well.
-FD_DEV float clamp448(float v) { return fminf(fmaxf(v, -448.0f), 448.0f); }
 
 template <typename T>
 FD_DEV void load8(const T* p, float (&v)[8]);
@@ -55,11 +46,7 @@ FD_DEV void load8<float>(const float* p, float (&v)[8]) {
 }
 
 FD_DEV uint2 quant8(const float (&v)[8], float qm) {
-  uint32_t c[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-    c[i] = f32x2_to_e4m3x2(clamp448(v[2 * i] * qm), clamp448(v[2 * i + 1] * qm));
-  return make_uint2(c[0] | (c[1] << 16), c[2] | (c[3] << 16));
+  return make_uint2(quant4(v[0], v[1], v[2], v[3], qm), quant4(v[4], v[5], v[6], v[7], qm));
 }
 
 // max over the 16 lanes of a half-warp
@@ -174,18 +161,6 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict_
 }
 
 // ---------------------------------------------------------------- G4
-// Triton lowers fp32 tl.exp(x) to ex2.approx.f32(x * log2(e)) (measured: bit
-// identical); the same two instructions are used here.
-FD_DEV float exp_like_triton(float x) {
-  float y;
-  asm("{\n\t.reg .f32 t;\n\t"
-      "mul.f32 t, %1, 0f3FB8AA3B;\n\t"
-      "ex2.approx.f32 %0, t;\n\t}"
-      : "=f"(y)
-      : "f"(x));
-  return y;
-}
-
 // fp8_silu_gate_quant_kernel, src/futudiffu/fp8_kernels.py:843-916.
 __global__ void __launch_bounds__(256) silu_gate_quant_kernel(const __nv_bfloat16* __restrict__ x,
                                                              uint8_t* __restrict__ y,
@@ -202,10 +177,7 @@ __global__ void __launch_bounds__(256) silu_gate_quant_kernel(const __nv_bfloat1
     load8<__nv_bfloat16>(x + m * 2 * N + nb * 128 + sub * 8, w1);
     load8<__nv_bfloat16>(x + m * 2 * N + N + nb * 128 + sub * 8, w3);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float sig = div_full(1.0f, 1.0f + exp_like_triton(-w1[i]));
-      v[i] = (w1[i] * sig) * w3[i];
-    }
+    for (int i = 0; i < 8; ++i) v[i] = silu_gate(w1[i], w3[i]);
     const float amax = half_warp_max(amax8(v));
     const float qm = quant_mult(amax);
     *reinterpret_cast<uint2*>(y + m * N + nb * 128 + sub * 8) = quant8(v, qm);
@@ -220,16 +192,12 @@ __global__ void __launch_bounds__(256) gelu_tanh_quant_kernel(const __nv_bfloat1
                                                              int64_t ngroups) {
   const int64_t half_warps = (int64_t)gridDim.x * (blockDim.x >> 4);
   const int sub = threadIdx.x & 15;
-  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
   for (int64_t g = (int64_t)blockIdx.x * (blockDim.x >> 4) + (threadIdx.x >> 4); g < ngroups;
        g += half_warps) {
     float v[8];
     load8<__nv_bfloat16>(x + g * 128 + sub * 8, v);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float a = v[i];
-      v[i] = 0.5f * a * (1.0f + tanhf(k0 * (a + k1 * a * a * a)));
-    }
+    for (int i = 0; i < 8; ++i) v[i] = gelu_tanh(v[i]);
     const float amax = half_warp_max(amax8(v));
     const float qm = quant_mult(amax);
     *reinterpret_cast<uint2*>(y + g * 128 + sub * 8) = quant8(v, qm);

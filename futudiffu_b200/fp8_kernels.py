@@ -20,7 +20,7 @@ There is no Triton and no CPU fallback: every function requires CUDA tensors.
 
 from __future__ import annotations
 
-from typing import Tuple
+from typing import Optional, Tuple
 
 import torch
 
@@ -234,7 +234,11 @@ def fp8_gemm_quant(
     out_block_size: int = 128,
     out_dtype: torch.dtype = torch.float8_e4m3fn,
 ) -> Tuple[torch.Tensor, torch.Tensor]:
-    """GEMM + 1 x out_block_size requantisation of the fp32 accumulator (reference :666-709)."""
+    """GEMM whose fp32 accumulator is requantised 1 x 128 in the epilogue (reference :666-709).
+
+    Returns the e4m3 output (batch shape of ``a``, N) and its dequant scales
+    (M, N / out_block_size), the layout of the reference.
+    """
     assert a.is_contiguous() and b.is_contiguous()
     assert a_s.is_contiguous() and b_s.is_contiguous()
     assert b.dim() == 2
@@ -243,13 +247,74 @@ def fp8_gemm_quant(
     N = b.shape[0]
     batch_shape = a.shape[:-1]
     assert N % out_block_size == 0
-    assert out_block_size == 128, "out_block_size must be 128"
-    acc = _gemm(a, a_s, b, b_s, None, torch.float32, 0, N)
-    c, c_s = fp8_act_quant(acc.reshape(M, N), out_block_size, out_dtype)
-    c = c.reshape(*batch_shape, N)
-    if len(batch_shape) > 0:
-        c_s = c_s.reshape(*batch_shape, N // out_block_size)
+    assert input_block_size == 128 and out_block_size == 128, "block sizes must be 128"
+    return _gemm_quant(a, a_s, b, b_s, None, L.ACT_NONE, M, N, K, batch_shape, out_dtype)
+
+
+def _gemm_quant(a, a_s, b, b_s, bias, act, M, N, K, batch_shape, out_dtype):
+    L.require_cuda(a, a_s, b, b_s, bias)
+    if out_dtype != torch.float8_e4m3fn:
+        raise ValueError("quantising GEMM epilogues produce float8_e4m3fn only")
+    c = a.new_empty(*batch_shape, N, dtype=out_dtype)
+    c_s = a.new_empty(M, N // 128, dtype=torch.float32)
+    if M == 0:
+        return c, c_s
+    if bias is not None:
+        bias = bias.contiguous()
+    L.call("fd_fp8_gemm_quant", L.ptr(a), L.ptr(a_s), L.ptr(b), L.ptr(b_s), L.ptr(bias),
+           L.dtype_code(bias.dtype) if bias is not None else 0, L.ptr(c), L.ptr(c_s), M, N, K, act,
+           L.stream_ptr(a.device))
     return c, c_s
+
+
+def fp8_gemm_gelu_tanh_quant(
+    a: torch.Tensor,
+    a_s: torch.Tensor,
+    b: torch.Tensor,
+    b_s: torch.Tensor,
+    bias: Optional[torch.Tensor] = None,
+    block_size: int = 128,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """``fp8_gelu_tanh_quant(fp8_addmm_blockwise(a, a_s, b, b_s, bias))`` in one kernel.
+
+    The GEMM output is rounded to bf16 (as the unfused pair stores it), passed
+    through GELU (tanh approximation) and quantised 1 x 128; codes and scales are
+    identical to the two-kernel path.  Scales have shape (M, N / 128).
+    """
+    assert a.is_contiguous() and b.is_contiguous()
+    assert a_s.is_contiguous() and b_s.is_contiguous()
+    assert b.dim() == 2 and block_size == 128
+    K = a.size(-1)
+    M = a.numel() // K
+    N = b.shape[0]
+    assert N % block_size == 0
+    return _gemm_quant(a, a_s, b, b_s, bias, L.ACT_GELU_TANH, M, N, K, a.shape[:-1], torch.float8_e4m3fn)
+
+
+def fp8_gemm_silu_gate_quant(
+    a: torch.Tensor,
+    a_s: torch.Tensor,
+    b13: torch.Tensor,
+    b13_s: torch.Tensor,
+    bias: Optional[torch.Tensor] = None,
+    block_size: int = 128,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """The FFN chain head in one kernel (reference src_ii/transformer.py:536-545).
+
+    ``b13`` is the fused w1w3 weight (2 H, K) with scales (2 H / 128, K / 128):
+    rows [0, H) are w1, rows [H, 2 H) are w3, the layout of the reference's
+    ``w1w3`` FP8Linear.  Equals ``fp8_silu_gate_quant(fp8_addmm_blockwise(a, a_s,
+    b13, b13_s, bias))`` code for code without materialising the bf16 (M, 2 H)
+    intermediate.  Returns (codes (..., H) e4m3, scales (M, H / 128)).
+    """
+    assert a.is_contiguous() and b13.is_contiguous()
+    assert a_s.is_contiguous() and b13_s.is_contiguous()
+    assert b13.dim() == 2 and b13.shape[0] % 2 == 0 and block_size == 128
+    K = a.size(-1)
+    M = a.numel() // K
+    H = b13.shape[0] // 2
+    assert H % block_size == 0
+    return _gemm_quant(a, a_s, b13, b13_s, bias, L.ACT_SILU_GATE, M, H, K, a.shape[:-1], torch.float8_e4m3fn)
 
 
 def fp8_gelu(

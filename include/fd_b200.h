@@ -104,6 +104,25 @@ int fd_fp8_gemm_blockwise(const void* a, const float* a_s, const void* b, const 
 /* G4 -- fp8_silu_gate_quant (src/futudiffu/fp8_kernels.py:842-978).
  * x (M, 2N) bf16 = [w1 | w3]; y (M, N) e4m3 = quant(silu(w1) * w3) per 1 x block,
  * s (M, N/block) f32.  N % block == 0, block == 128. */
+/* GEMM with a quantising epilogue: c (M, N) e4m3 codes and c_s (M, N/128) fp32
+ * dequant scales, 1 x 128 groups, from A (M, K) e4m3 + a_s and B e4m3 (K-major) + b_s
+ * (128 x 128 blocks), optional bias (added in fp32).  N and K multiples of 128.
+ *   act FD_ACT_NONE:      requantise the fp32 accumulator; replaces fp8_gemm_quant
+ *                         (src/futudiffu/fp8_kernels.py:573-709).
+ *   act FD_ACT_GELU_TANH: bf16(acc) -> GELU(tanh) -> quantise; replaces
+ *                         fp8_addmm_blockwise followed by the GELU-tanh quantiser.
+ *   act FD_ACT_SILU_GATE: B = [w1; w3] of shape (2 N, K), b_s (2 N/128, K/128), bias 2 N;
+ *                         silu(bf16(w1 acc)) * bf16(w3 acc) -> quantise; replaces the FFN
+ *                         chain head fp8_addmm -> fp8_silu_gate_quant
+ *                         (src_ii/transformer.py:536-545, fp8_kernels.py:842-978).
+ * Codes and scales equal those of the replaced kernel pair. */
+#define FD_ACT_NONE 0
+#define FD_ACT_GELU_TANH 1
+#define FD_ACT_SILU_GATE 2
+int fd_fp8_gemm_quant(const void* a, const float* a_s, const void* b, const float* b_s,
+                      const void* bias, int bias_dtype, void* c, float* c_s, int64_t M, int64_t N,
+                      int64_t K, int act, void* stream);
+
 int fd_fp8_silu_gate_quant(const void* x, void* y, float* s, int64_t M, int64_t N, int block,
                            void* stream);
 

@@ -157,3 +157,68 @@ def test_gemm_status_clean(cuda_device):
     from futudiffu_b200 import check_status
 
     check_status()
+
+
+# ------------------------------------------------------------------ fused quantising epilogues
+def _e4m3(t):
+    return t.view(torch.uint8).cpu()
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 128, 128), (129, 256, 384), (777, 1280, 1024), (2048, 3072, 3072)])
+def test_gemm_quant_epilogue(cuda_device, M, N, K):
+    """fp8_gemm_quant: the fp32 accumulator requantised in the epilogue equals the
+    f32 GEMM followed by the 1 x 128 quantiser, code for code."""
+    from futudiffu_b200 import fp8_kernels as FK
+
+    a8, a_s, b8, bs = (t.to(cuda_device) for t in _operands(M, N, K, seed=11))
+    c, c_s = FK.fp8_gemm_quant(a8, a_s, b8, bs)
+    acc = FK.fp8_gemm_blockwise(a8, a_s, b8, bs, output_dtype=torch.float32)
+    y, s = FK.fp8_act_quant(acc)
+    assert c_s.shape == (M, N // 128)
+    assert torch.equal(_e4m3(c), _e4m3(y))
+    assert torch.equal(c_s.cpu(), s.reshape(M, N // 128).cpu())
+    # and against the oracle: the oracle's fp32 accumulation order differs, so
+    # codes may move by one e4m3 step where the product sits on a rounding edge
+    ref_acc = OG.gemm_blockwise(a8.cpu(), a_s.cpu(), b8.cpu(), bs.cpu(), out_dtype=torch.float32)
+    ry, rs = OQ.act_quant(ref_acc)
+    from tests.helpers import e4m3_step_diff
+
+    assert e4m3_step_diff(c.cpu(), ry).max() <= 1
+    torch.testing.assert_close(c_s.cpu(), rs.reshape(M, N // 128), rtol=1e-5, atol=0)
+
+
+@pytest.mark.parametrize("bias", [False, True])
+@pytest.mark.parametrize("M,N,K", [(1, 128, 128), (300, 512, 384), (4608, 1024, 768)])
+def test_gemm_gelu_tanh_quant_epilogue(cuda_device, M, N, K, bias):
+    """GEMM -> bf16 -> GELU(tanh) -> 1 x 128 e4m3 fused equals fp8_addmm + fp8_gelu_tanh_quant."""
+    from futudiffu_b200 import fp8_kernels as FK
+
+    a8, a_s, b8, bs = (t.to(cuda_device) for t in _operands(M, N, K, seed=12))
+    bvec = (torch.randn(N, generator=gen(5)) * 0.1).to(torch.bfloat16).to(cuda_device) if bias else None
+    c, c_s = FK.fp8_gemm_gelu_tanh_quant(a8, a_s, b8, bs, bias=bvec)
+    h = FK.fp8_addmm_blockwise(a8, a_s, b8, bs, bias=bvec, output_dtype=torch.bfloat16)
+    y, s = FK.fp8_gelu_tanh_quant(h)
+    assert torch.equal(_e4m3(c), _e4m3(y))
+    assert torch.equal(c_s.cpu(), s.reshape(M, N // 128).cpu())
+
+
+@pytest.mark.parametrize("bias", [False, True])
+@pytest.mark.parametrize("M,H,K", [(1, 128, 128), (257, 384, 256), (2048, 1280, 1024), (4608, 1024, 3072)])
+def test_gemm_silu_gate_quant_epilogue(cuda_device, M, H, K, bias):
+    """FFN chain head fused: equals fp8_addmm (M, 2H) bf16 -> fp8_silu_gate_quant, code for code."""
+    from futudiffu_b200 import fp8_kernels as FK
+
+    a8, a_s, b8, bs = (t.to(cuda_device) for t in _operands(M, 2 * H, K, seed=13))
+    bvec = (torch.randn(2 * H, generator=gen(6)) * 0.1).to(torch.bfloat16).to(cuda_device) if bias else None
+    c, c_s = FK.fp8_gemm_silu_gate_quant(a8, a_s, b8, bs, bias=bvec)
+    w13 = FK.fp8_addmm_blockwise(a8, a_s, b8, bs, bias=bvec, output_dtype=torch.bfloat16)
+    y, s = FK.fp8_silu_gate_quant(w13)
+    assert c.shape == (M, H) and c_s.shape == (M, H // 128)
+    assert torch.equal(_e4m3(c), _e4m3(y))
+    assert torch.equal(c_s.cpu(), s.reshape(M, H // 128).cpu())
+    # the oracle's SiLU gate of the same bf16 intermediate (CPU exp: within one step)
+    from tests.helpers import e4m3_step_diff
+
+    ry, rs = OQ.silu_gate_quant(w13.cpu())
+    assert e4m3_step_diff(c.cpu(), ry).max().item() <= 1
+    torch.testing.assert_close(c_s.cpu(), rs.reshape(M, H // 128), rtol=2e-6, atol=0)
