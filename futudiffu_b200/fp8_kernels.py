@@ -237,7 +237,7 @@ def fp8_gemm_quant(
     """GEMM whose fp32 accumulator is requantised 1 x 128 in the epilogue (reference :666-709).
 
     Returns the e4m3 output (batch shape of ``a``, N) and its dequant scales
-    (M, N / out_block_size), the layout of the reference.
+    (batch shape of ``a``, N / out_block_size), the layout of the reference.
     """
     assert a.is_contiguous() and b.is_contiguous()
     assert a_s.is_contiguous() and b_s.is_contiguous()
@@ -264,6 +264,8 @@ def _gemm_quant(a, a_s, b, b_s, bias, act, M, N, K, batch_shape, out_dtype):
     L.call("fd_fp8_gemm_quant", L.ptr(a), L.ptr(a_s), L.ptr(b), L.ptr(b_s), L.ptr(bias),
            L.dtype_code(bias.dtype) if bias is not None else 0, L.ptr(c), L.ptr(c_s), M, N, K, act,
            L.stream_ptr(a.device))
+    if len(batch_shape) > 0:
+        c_s = c_s.reshape(*batch_shape, N // 128)
     return c, c_s
 
 
@@ -279,7 +281,7 @@ def fp8_gemm_gelu_tanh_quant(
 
     The GEMM output is rounded to bf16 (as the unfused pair stores it), passed
     through GELU (tanh approximation) and quantised 1 x 128; codes and scales are
-    identical to the two-kernel path.  Scales have shape (M, N / 128).
+    identical to the two-kernel path.  Scales have shape (batch shape, N / 128).
     """
     assert a.is_contiguous() and b.is_contiguous()
     assert a_s.is_contiguous() and b_s.is_contiguous()
@@ -305,7 +307,7 @@ def fp8_gemm_silu_gate_quant(
     rows [0, H) are w1, rows [H, 2 H) are w3, the layout of the reference's
     ``w1w3`` FP8Linear.  Equals ``fp8_silu_gate_quant(fp8_addmm_blockwise(a, a_s,
     b13, b13_s, bias))`` code for code without materialising the bf16 (M, 2 H)
-    intermediate.  Returns (codes (..., H) e4m3, scales (M, H / 128)).
+    intermediate.  Returns (codes (..., H) e4m3, scales (..., H / 128)).
     """
     assert a.is_contiguous() and b13.is_contiguous()
     assert a_s.is_contiguous() and b13_s.is_contiguous()
