@@ -1,0 +1,329 @@
+"""Diffusion-transformer workloads on the futudiffu_b200 kernels.
+
+The benchmark models of the quantized DiT hot path, built from random-init
+weights (no checkpoint is needed or read):
+
+* ``DoubleStreamBlock`` -- the MMDiT double-stream block: text and image
+  streams with their own weights, joint quantized attention over both.
+* ``SingleStreamBlock`` -- the single-stream block: one fused QKV + MLP-in
+  linear, attention and GELU(tanh) MLP in parallel, one fused output linear.
+* ``DiT`` + ``euler_denoise`` -- the 12B-class rectified-flow transformer
+  (19 double + 38 single blocks at hidden 3072) and its Euler sampler.
+
+Block anatomy follows the reference's Z-Image transformer
+(src_ii/transformer.py:459-475, :533-567, :680-702): adaLN from a timestep
+vector produces per-sublayer (scale, gate) pairs consumed by
+``fused_rms_norm_modulate`` (x -> rmsnorm(x) w (1 + scale)) and
+``fused_rms_norm_gate_residual`` (r + tanh(gate) rmsnorm(y) w); Q/K get a
+per-head RMSNorm and RoPE inside ``fused_qkv_postprocess``; every linear of the
+blocks is an FP8 128 x 128 block-scaled GEMM.  The FFN chain stays in FP8
+between its two GEMMs: the first GEMM's epilogue applies GELU(tanh) and the
+1 x 128 requantisation (``fp8_gemm_gelu_tanh_quant``), the second consumes the
+codes directly.  Small per-sample GEMMs (timestep MLP, adaLN, patch in/out
+projections) run in bf16 through torch; they are not on the hot path.
+
+Every hot op is one of the package's sm_100a kernels; nothing here has a CPU
+path (the CPU restatement used for checking lives with the test oracle).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+from torch import Tensor, nn
+
+from . import _lib as L
+from .attention import rope_embed
+from .fp8 import FP8Linear, quantize_fp8_blockwise_cuda
+from .fp8_kernels import (
+    fp8_act_quant,
+    fp8_addmm_blockwise,
+    fp8_gemm_blockwise,
+    fp8_gemm_gelu_tanh_quant,
+)
+from .fused_kernels import fused_qkv_postprocess, fused_rms_norm_gate_residual, fused_rms_norm_modulate
+from .sage_attention import _attn_forward
+
+HEAD_DIM = 128
+
+
+@dataclass
+class DiTConfig:
+    hidden: int = 3072
+    heads: int = 24
+    mlp_ratio: int = 4
+    n_double: int = 19
+    n_single: int = 38
+    txt_tokens: int = 512
+    img_grid: tuple[int, int] = (64, 64)  # token grid after 2x2 patching
+    patch_dim: int = 64                    # 16 latent channels x 2 x 2
+    time_dim: int = 256
+    rope_axes: tuple[int, int] = (64, 64)  # head_dim split over the (h, w) axes
+    rope_theta: float = 10000.0
+    eps: float = 1e-5
+    # quantized attention mode (the B200 throughput configuration)
+    qk_quant: str = "int8"
+    pv_quant: str = "fp8"
+    granularity: str = "per_block"
+
+    @property
+    def img_tokens(self) -> int:
+        return self.img_grid[0] * self.img_grid[1]
+
+    @property
+    def tokens(self) -> int:
+        return self.txt_tokens + self.img_tokens
+
+
+def random_fp8_linear(out_f: int, in_f: int, gen: torch.Generator, device, std: float = 0.02,
+                      bias: bool = False) -> FP8Linear:
+    """An FP8Linear whose weight is N(0, std) quantised 128 x 128 on the device."""
+    w = torch.randn(out_f, in_f, generator=gen, device=device, dtype=torch.float32).mul_(std)
+    w8, ws = quantize_fp8_blockwise_cuda(w.to(torch.bfloat16))
+    b = None
+    if bias:
+        b = (torch.randn(out_f, generator=gen, device=device) * std).to(torch.bfloat16)
+    return FP8Linear(w8, ws, b)
+
+
+def _rand(shape, gen, device, std, mean=0.0, dtype=torch.bfloat16) -> Tensor:
+    return (torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std + mean).to(dtype)
+
+
+def image_freqs(cfg: DiTConfig, device) -> Tensor:
+    """2-D RoPE rotations of the image tokens, (img_tokens, head_dim/2, 2, 2) fp32."""
+    gh, gw = cfg.img_grid
+    ys = torch.arange(gh, device=device).repeat_interleave(gw)
+    xs = torch.arange(gw, device=device).repeat(gh)
+    fy = rope_embed(ys, cfg.rope_axes[0], cfg.rope_theta)
+    fx = rope_embed(xs, cfg.rope_axes[1], cfg.rope_theta)
+    return torch.cat([fy, fx], dim=-3).contiguous()
+
+
+def batch_freqs(freqs: Tensor, B: int) -> Tensor:
+    """Per-sequence rotations (L, 64, 2, 2) repeated for a batch: (B, L, 64, 2, 2) contiguous."""
+    return freqs.unsqueeze(0).expand(B, *freqs.shape).contiguous()
+
+
+def text_freqs(cfg: DiTConfig, device) -> Tensor:
+    """Text tokens carry no positional rotation: identity matrices."""
+    eye = torch.eye(2, dtype=torch.float32, device=device)
+    return eye.expand(cfg.txt_tokens, HEAD_DIM // 2, 2, 2).contiguous()
+
+
+def linear_bf16(x: Tensor, lin: FP8Linear) -> Tensor:
+    """x (..., K) bf16 -> FP8 GEMM -> (..., N) bf16 (activation quantised 1 x 128)."""
+    a8, a_s = fp8_act_quant(x)
+    if lin.bias is not None:
+        return fp8_addmm_blockwise(a8, a_s, lin.weight, lin.weight_scale, bias=lin.bias,
+                                   output_dtype=torch.bfloat16)
+    return fp8_gemm_blockwise(a8, a_s, lin.weight, lin.weight_scale, output_dtype=torch.bfloat16)
+
+
+def mlp_fp8(x: Tensor, w_in: FP8Linear, w_out: FP8Linear) -> Tensor:
+    """GELU(tanh) MLP kept in FP8 between its GEMMs (fused GELU + requant epilogue)."""
+    a8, a_s = fp8_act_quant(x)
+    h8, h_s = fp8_gemm_gelu_tanh_quant(a8, a_s, w_in.weight, w_in.weight_scale, bias=w_in.bias)
+    return fp8_gemm_blockwise(h8, h_s, w_out.weight, w_out.weight_scale, output_dtype=torch.bfloat16)
+
+
+def joint_attention(q: Tensor, k: Tensor, v: Tensor, cfg: DiTConfig) -> Tensor:
+    """Quantized attention over (B, H, N, 128) -> (B, N, H * 128) bf16."""
+    o, _ = _attn_forward(q, k, v, None, block_mask=None, qk_quant=cfg.qk_quant, pv_quant=cfg.pv_quant,
+                         granularity=cfg.granularity, want_lse=False)
+    B, H, N, D = o.shape
+    return o.transpose(1, 2).reshape(B, N, H * D)
+
+
+class _Stream(nn.Module):
+    """Weights of one stream of a double-stream block."""
+
+    def __init__(self, cfg: DiTConfig, gen, device):
+        super().__init__()
+        D = cfg.hidden
+        self.adaln = nn.Linear(D, 4 * D, device=device, dtype=torch.bfloat16)
+        with torch.no_grad():
+            self.adaln.weight.copy_(_rand((4 * D, D), gen, device, 0.02))
+            self.adaln.bias.copy_(_rand((4 * D,), gen, device, 0.02))
+        self.norm_w = nn.ParameterList(
+            [nn.Parameter(_rand((D,), gen, device, 0.05, 1.0), requires_grad=False) for _ in range(4)])
+        self.q_norm = nn.Parameter(_rand((HEAD_DIM,), gen, device, 0.05, 1.0), requires_grad=False)
+        self.k_norm = nn.Parameter(_rand((HEAD_DIM,), gen, device, 0.05, 1.0), requires_grad=False)
+        self.qkv = random_fp8_linear(3 * D, D, gen, device)
+        self.proj = random_fp8_linear(D, D, gen, device)
+        self.mlp_in = random_fp8_linear(cfg.mlp_ratio * D, D, gen, device)
+        self.mlp_out = random_fp8_linear(D, cfg.mlp_ratio * D, gen, device)
+
+    def modulation(self, vec: Tensor) -> list[Tensor]:
+        # (scale_attn, gate_attn, scale_mlp, gate_mlp), each (B, D)
+        return list(self.adaln(torch.nn.functional.silu(vec)).chunk(4, dim=-1))
+
+
+class DoubleStreamBlock(nn.Module):
+    """MMDiT double-stream block: per-stream weights, joint attention."""
+
+    def __init__(self, cfg: DiTConfig, gen, device):
+        super().__init__()
+        self.cfg = cfg
+        self.txt = _Stream(cfg, gen, device)
+        self.img = _Stream(cfg, gen, device)
+
+    def forward(self, x_txt: Tensor, x_img: Tensor, vec: Tensor, freqs_txt: Tensor,
+                freqs_img: Tensor) -> tuple[Tensor, Tensor]:
+        """x_* (B, L_*, D) bf16; vec (B, D); freqs_* (B, L_*, 64, 2, 2) fp32 (see batch_freqs)."""
+        cfg = self.cfg
+        B = x_txt.shape[0]
+        mods, qs, ks, vs = [], [], [], []
+        for st, x, fr in ((self.txt, x_txt, freqs_txt), (self.img, x_img, freqs_img)):
+            m = st.modulation(vec)
+            mods.append(m)
+            h = fused_rms_norm_modulate(x, st.norm_w[0], m[0].contiguous(), cfg.eps)
+            qkv = linear_bf16(h, st.qkv)
+            q, k, v = fused_qkv_postprocess(qkv, st.q_norm, st.k_norm, fr, cfg.heads, HEAD_DIM, cfg.eps)
+            qs.append(q)
+            ks.append(k)
+            vs.append(v)
+        o = joint_attention(torch.cat(qs, dim=2), torch.cat(ks, dim=2), torch.cat(vs, dim=2), cfg)
+        o_txt, o_img = o.split([x_txt.shape[1], x_img.shape[1]], dim=1)
+        outs = []
+        for st, x, o_s, m in ((self.txt, x_txt, o_txt, mods[0]), (self.img, x_img, o_img, mods[1])):
+            a = linear_bf16(o_s.contiguous(), st.proj)
+            x = fused_rms_norm_gate_residual(a, st.norm_w[1], m[1].contiguous(), x, cfg.eps)
+            h = fused_rms_norm_modulate(x, st.norm_w[2], m[2].contiguous(), cfg.eps)
+            f = mlp_fp8(h, st.mlp_in, st.mlp_out)
+            x = fused_rms_norm_gate_residual(f, st.norm_w[3], m[3].contiguous(), x, cfg.eps)
+            outs.append(x)
+        return outs[0], outs[1]
+
+
+class SingleStreamBlock(nn.Module):
+    """Single-stream block over the joint sequence: one linear (D -> 3D + rD)
+    feeding attention and the MLP, one linear (D + rD -> D) for both outputs."""
+
+    def __init__(self, cfg: DiTConfig, gen, device):
+        super().__init__()
+        self.cfg = cfg
+        D, R = cfg.hidden, cfg.mlp_ratio
+        self.adaln = nn.Linear(D, 2 * D, device=device, dtype=torch.bfloat16)
+        with torch.no_grad():
+            self.adaln.weight.copy_(_rand((2 * D, D), gen, device, 0.02))
+            self.adaln.bias.copy_(_rand((2 * D,), gen, device, 0.02))
+        self.norm_w = nn.ParameterList(
+            [nn.Parameter(_rand((D,), gen, device, 0.05, 1.0), requires_grad=False) for _ in range(2)])
+        self.q_norm = nn.Parameter(_rand((HEAD_DIM,), gen, device, 0.05, 1.0), requires_grad=False)
+        self.k_norm = nn.Parameter(_rand((HEAD_DIM,), gen, device, 0.05, 1.0), requires_grad=False)
+        # linear1 rows: [qkv (3D) | mlp_in (R D)]; linear2 columns: [attn (D) | mlp (R D)]
+        self.linear1 = random_fp8_linear(3 * D + R * D, D, gen, device)
+        self.linear2 = random_fp8_linear(D, D + R * D, gen, device)
+
+    def forward(self, x: Tensor, vec: Tensor, freqs: Tensor) -> Tensor:
+        """x (B, L, D) bf16; vec (B, D); freqs (B, L, 64, 2, 2) fp32."""
+        cfg = self.cfg
+        B, N, D = x.shape
+        scale, gate = self.adaln(torch.nn.functional.silu(vec)).chunk(2, dim=-1)
+        h = fused_rms_norm_modulate(x, self.norm_w[0], scale.contiguous(), cfg.eps)
+        a8, a_s = fp8_act_quant(h)
+        w, ws = self.linear1.weight, self.linear1.weight_scale
+        n_qkv = 3 * D
+        qkv = fp8_gemm_blockwise(a8, a_s, w[:n_qkv], ws[: n_qkv // 128], output_dtype=torch.bfloat16)
+        m8, m_s = fp8_gemm_gelu_tanh_quant(a8, a_s, w[n_qkv:], ws[n_qkv // 128:])
+        q, k, v = fused_qkv_postprocess(qkv, self.q_norm, self.k_norm, freqs, cfg.heads, HEAD_DIM, cfg.eps)
+        o = joint_attention(q, k, v, cfg)
+        o8, o_s = fp8_act_quant(o)
+        # the 1 x 128 blocks of both halves concatenate along K: one GEMM for linear2
+        cat8 = torch.cat([o8.view(torch.uint8), m8.view(torch.uint8)], dim=-1).view(torch.float8_e4m3fn)
+        cat_s = torch.cat([o_s, m_s], dim=-1)
+        y = fp8_gemm_blockwise(cat8, cat_s, self.linear2.weight, self.linear2.weight_scale,
+                               output_dtype=torch.bfloat16)
+        return fused_rms_norm_gate_residual(y, self.norm_w[1], gate.contiguous(), x, cfg.eps)
+
+
+def timestep_embedding(t: Tensor, dim: int, max_period: float = 10000.0) -> Tensor:
+    """Sinusoidal embedding of t in [0, 1] (scaled by 1000), (B, dim) fp32."""
+    half = dim // 2
+    freqs = torch.exp(-math.log(max_period) * torch.arange(half, dtype=torch.float32, device=t.device) / half)
+    args = (t.float() * 1000.0)[:, None] * freqs[None]
+    return torch.cat([torch.cos(args), torch.sin(args)], dim=-1)
+
+
+class DiT(nn.Module):
+    """Rectified-flow DiT: patch tokens + text tokens -> velocity of the patch tokens."""
+
+    def __init__(self, cfg: DiTConfig, seed: int = 0, device="cuda"):
+        super().__init__()
+        self.cfg = cfg
+        dev = torch.device(device)
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        D = cfg.hidden
+        if D != HEAD_DIM * cfg.heads:
+            raise ValueError(f"hidden {D} must equal heads x {HEAD_DIM}")
+        self.img_in = nn.Linear(cfg.patch_dim, D, device=dev, dtype=torch.bfloat16)
+        self.time_in1 = nn.Linear(cfg.time_dim, D, device=dev, dtype=torch.bfloat16)
+        self.time_in2 = nn.Linear(D, D, device=dev, dtype=torch.bfloat16)
+        self.final_adaln = nn.Linear(D, D, device=dev, dtype=torch.bfloat16)
+        self.final_out = nn.Linear(D, cfg.patch_dim, device=dev, dtype=torch.bfloat16)
+        with torch.no_grad():
+            for lin in (self.img_in, self.time_in1, self.time_in2, self.final_adaln, self.final_out):
+                lin.weight.copy_(_rand(tuple(lin.weight.shape), gen, dev, 0.02))
+                lin.bias.zero_()
+        self.final_norm = nn.Parameter(_rand((D,), gen, dev, 0.05, 1.0), requires_grad=False)
+        self.double_blocks = nn.ModuleList([DoubleStreamBlock(cfg, gen, dev) for _ in range(cfg.n_double)])
+        self.single_blocks = nn.ModuleList([SingleStreamBlock(cfg, gen, dev) for _ in range(cfg.n_single)])
+        self.register_buffer("freqs_img", image_freqs(cfg, dev), persistent=False)
+        self.register_buffer("freqs_txt", text_freqs(cfg, dev), persistent=False)
+        self.register_buffer("freqs_all", torch.cat([self.freqs_txt, self.freqs_img], dim=0), persistent=False)
+        self._freqs_cache: dict[int, tuple[Tensor, Tensor, Tensor]] = {}
+
+    @torch.no_grad()
+    def forward(self, img: Tensor, txt: Tensor, t: Tensor) -> Tensor:
+        """img (B, img_tokens, patch_dim) bf16, txt (B, txt_tokens, hidden) bf16, t (B,) in [0, 1]."""
+        cfg = self.cfg
+        vec = self.time_in2(torch.nn.functional.silu(self.time_in1(
+            timestep_embedding(t, cfg.time_dim).to(torch.bfloat16))))
+        x_img = self.img_in(img).contiguous()
+        x_txt = txt.contiguous()
+        B = img.shape[0]
+        if B not in self._freqs_cache:
+            self._freqs_cache[B] = tuple(batch_freqs(f, B) for f in (self.freqs_txt, self.freqs_img, self.freqs_all))
+        f_txt, f_img, f_all = self._freqs_cache[B]
+        for blk in self.double_blocks:
+            x_txt, x_img = blk(x_txt, x_img, vec, f_txt, f_img)
+        x = torch.cat([x_txt, x_img], dim=1)
+        for blk in self.single_blocks:
+            x = blk(x, vec, f_all)
+        x_img = x[:, cfg.txt_tokens:].contiguous()
+        scale = self.final_adaln(torch.nn.functional.silu(vec)).contiguous()
+        h = fused_rms_norm_modulate(x_img, self.final_norm, scale, cfg.eps)
+        return self.final_out(h)
+
+
+@torch.no_grad()
+def euler_step(model: DiT, x: Tensor, txt: Tensor, sigma: float, sigma_next: float) -> Tensor:
+    """One rectified-flow Euler step: x + (sigma_next - sigma) * v(x, sigma)."""
+    t = torch.full((x.shape[0],), sigma, device=x.device, dtype=torch.float32)
+    v = model(x, txt, t)
+    return (x.float() + (sigma_next - sigma) * v.float()).to(x.dtype)
+
+
+def sigmas(steps: int) -> list[float]:
+    """Linear flow-matching schedule from 1 (noise) to 0 (data)."""
+    return [1.0 - i / steps for i in range(steps + 1)]
+
+
+@torch.no_grad()
+def euler_denoise(model: DiT, x: Tensor, txt: Tensor, steps: int = 28) -> Tensor:
+    s = sigmas(steps)
+    for i in range(steps):
+        x = euler_step(model, x, txt, s[i], s[i + 1])
+    return x
+
+
+def flops_per_sample_step(cfg: DiTConfig) -> float:
+    """Algorithmic FLOPs of one forward of one sample: block linears + attention."""
+    D, R, N = cfg.hidden, cfg.mlp_ratio, cfg.tokens
+    lin_double = 2 * (3 + 1 + 2 * R) * D * D * N      # both streams together cover N tokens
+    lin_single = 2 * ((3 + R) * D * D + (1 + R) * D * D) * N
+    attn = 4 * N * N * D
+    return cfg.n_double * (lin_double + attn) + cfg.n_single * (lin_single + attn)

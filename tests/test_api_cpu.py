@@ -108,3 +108,21 @@ def test_fp8_linear_replacement_logic():
     replace_linear_with_fp8(model, sd)
     assert isinstance(model[0], FP8Linear) and isinstance(model[1][0], nn.Linear)
     assert model[0].in_features == 256 and model[0].out_features == 128
+
+
+def test_dit_config_arithmetic():
+    """Config-4 shapes and FLOP accounting (no GPU needed)."""
+    from futudiffu_b200.dit import DiTConfig, batch_freqs, flops_per_sample_step, image_freqs, sigmas, text_freqs
+
+    cfg = DiTConfig()
+    assert cfg.tokens == 4608 and cfg.img_tokens == 4096 and cfg.hidden == 24 * 128
+    assert abs(flops_per_sample_step(cfg) / 1e12 - 74.36) < 0.05
+    s = sigmas(28)
+    assert len(s) == 29 and s[0] == 1.0 and s[-1] == 0.0
+    small = DiTConfig(hidden=256, heads=2, txt_tokens=4, img_grid=(2, 3))
+    fi = image_freqs(small, "cpu")
+    assert fi.shape == (6, 64, 2, 2)
+    assert torch.allclose(fi[0], torch.eye(2).expand(64, 2, 2))  # position (0, 0): identity
+    ft = text_freqs(small, "cpu")
+    assert torch.equal(ft, torch.eye(2).expand(4, 64, 2, 2))
+    assert batch_freqs(fi, 3).shape == (3, 6, 64, 2, 2)
