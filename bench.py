@@ -1,17 +1,21 @@
-"""Benchmark of the quantized attention hot path.
-
-Workload (one "step"): SageAttention forward through the public API on
-B=2, H=24, S=4096, D=128 bf16 inputs, K carrying a per-channel offset
-~N(0, 4): K mean-smoothing, INT8 Q (per 128 rows) / K (per 64 rows), e4m3 P
-and per-channel e4m3 V -- the quantisation prologue kernels plus the tcgen05
-attention kernel.  Metric: attention TOPS = 4*B*H*S^2*D ops per step / time.
+"""Benchmarks of the quantized DiT hot path on B200.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload dit|attention|gemm]
 
-With N > 1 (torchrun, one process per GPU) every rank runs its own replica of
-the workload (attention does not shard; no collective on the data path);
-value = N * ops / max-over-ranks time.  ``--impl reference`` times the CPU
-restatement of the reference algorithm (oracle) on a bounded sample on rank 0.
+Workloads (one "step" each):
+  dit (default, BASELINE config 4, the headline metric "DiT denoise steps/s"):
+      one rectified-flow Euler step of the 12B-class DiT (19 double + 38
+      single blocks, hidden 3072, 4096 image + 512 text tokens) over the whole
+      batch of 8, random-init FP8 weights.  The batch is sharded by sample:
+      8/N samples per rank, no collective on the data path (strong scaling);
+      value = batch-8 steps per second = 1 / max-over-ranks step time.
+  attention: quantisation prologue + tcgen05 attention on
+      B=2, H=24, S=4096, D=128 (int8 per-block QK, e4m3 P/V); replicas per rank.
+  gemm (or the reference's Z-Image shapes): one FP8 block GEMM.
+
+``--impl reference`` times the CPU restatement of the reference algorithm (the
+oracle) on a bounded sample on rank 0; the other ranks exit without work.
 """
 
 from __future__ import annotations
@@ -46,8 +50,9 @@ def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"bf16_tflops": d["bf16_tflops"], "hbm_gbs": d["hbm_gbs"], "source": "measured"}
-    return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "source": "fallback"}
+        return {"bf16_tflops": d["bf16_tflops"], "hbm_gbs": d["hbm_gbs"], "source": "measured",
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"])}
+    return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "source": "fallback", "bf16_tflops_sustained": 1400.0}
 
 
 class ClockSampler:
@@ -305,6 +310,227 @@ def run_ours(args, world, rank, local):
     return 0
 
 
+# ------------------------------------------------------------------ config 4: DiT denoise
+DIT_BATCH = 8
+DIT_METRIC = "DiT denoise steps/s (12B-class, 19 double + 38 single blocks, 4096+512 tokens, batch 8)"
+KERNELS_PER_CALL = {"fd_attn_quant": 2, "fd_attn_quant_noalloc": 2}
+
+
+class LaunchRecorder:
+    """Counts this library's kernel launches and times every GEMM / attention
+    launch with CUDA events on the launching stream while ``active``."""
+
+    GEMMS = ("fd_fp8_gemm_blockwise", "fd_fp8_gemm_quant")
+
+    def __init__(self):
+        from futudiffu_b200 import _lib as L
+
+        self.L = L
+        self.orig = L.call
+        self.active = False
+        self.launches = 0
+        self.pending = []  # (kind, work, e0, e1)
+        L.call = self._call
+
+    def _call(self, name, *args):
+        if not self.active:
+            return self.orig(name, *args)
+        self.launches += KERNELS_PER_CALL.get(name, 1)
+        kind = work = None
+        if name in self.GEMMS:
+            M, N, K = args[8], args[9], args[10]
+            mult = 2 if (name == "fd_fp8_gemm_quant" and args[11] == self.L.ACT_SILU_GATE) else 1
+            kind, work = "gemm", 2.0 * M * N * K * mult
+        elif name == "fd_sage_attn_fwd":
+            BH, N = args[10], args[11]
+            kind, work = "attn", 4.0 * BH * N * N * 128
+        if kind is None:
+            return self.orig(name, *args)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        r = self.orig(name, *args)
+        e1.record()
+        self.pending.append((kind, work, e0, e1))
+        return r
+
+    def summary(self, kind):
+        ms = sum(a.elapsed_time(b) for k, _, a, b in self.pending if k == kind)
+        work = sum(w for k, w, _, _ in self.pending if k == kind)
+        n = sum(1 for k, *_ in self.pending if k == kind)
+        return work, ms, n
+
+    def close(self):
+        self.L.call = self.orig
+
+
+_DIT_CPU_BLOCKS: dict = {}
+
+
+def dit_cpu_sample(img_tokens: int = 1024) -> dict:
+    """One config-3 double-stream block through the oracle on the host cores
+    (CPU-built weights), at 512 text + ``img_tokens`` image tokens, extrapolated
+    to batch-8 steps/s by FLOPs."""
+    from futudiffu_b200.dit import DiTConfig, flops_per_sample_step
+    from oracle import dit as OD
+
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    torch.set_num_threads(threads)
+    full = DiTConfig()
+    cfg = DiTConfig(img_grid=(img_tokens // 64, 64))
+    if img_tokens not in _DIT_CPU_BLOCKS:
+        _DIT_CPU_BLOCKS[img_tokens] = OD.random_double_block(cfg, seed=0)
+    blk = _DIT_CPU_BLOCKS[img_tokens]
+    cg = torch.Generator().manual_seed(1)
+    x_txt = torch.randn(1, cfg.txt_tokens, cfg.hidden, generator=cg).to(torch.bfloat16)
+    x_img = torch.randn(1, cfg.img_tokens, cfg.hidden, generator=cg).to(torch.bfloat16)
+    vec = torch.randn(1, cfg.hidden, generator=cg).to(torch.bfloat16)
+    from futudiffu_b200.dit import image_freqs, text_freqs
+
+    ft = text_freqs(cfg, "cpu").unsqueeze(0)
+    fi = image_freqs(cfg, "cpu").unsqueeze(0)
+    t0 = time.perf_counter()
+    OD.double_block(blk, x_txt, x_img, vec, ft, fi)
+    dt = time.perf_counter() - t0
+    D, R, N = cfg.hidden, cfg.mlp_ratio, cfg.tokens
+    blk_flops = 2 * (3 + 1 + 2 * R) * D * D * N + 4 * N * N * D
+    step_s = dt * (flops_per_sample_step(full) / blk_flops) * DIT_BATCH
+    return {"value": 1.0 / step_s, "unit": "steps/s", "cores": threads, "kind": "port",
+            "sample": f"one double-stream block at {cfg.txt_tokens}+{cfg.img_tokens} tokens through "
+                      f"oracle.dit.double_block ({dt:.1f} s, {threads} threads), extrapolated to a "
+                      f"batch-{DIT_BATCH} Euler step by FLOP ratio ({step_s:.0f} s/step)"}
+
+
+def run_dit_reference(args, world, rank):
+    if rank != 0:
+        return 0
+    vals, cb = [], None
+    for i in range(args.warmup + args.steps):
+        cb = dit_cpu_sample(img_tokens=256)
+        if i >= args.warmup:
+            vals.append(cb["value"])
+    val = statistics.mean(vals)
+    print(json.dumps({
+        "impl": "reference", "metric": DIT_METRIC, "value": val, "unit": "steps/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / val, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp8/int8", "data": "synthetic",
+        "config": {"workload": "config4_dit_denoise", "batch": DIT_BATCH, "tokens": 4608},
+        "cpu_baseline": {**cb, "value": val},
+        "e2e": {"value": val, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+    return 0
+
+
+def run_dit(args, world, rank, local):
+    from futudiffu_b200 import check_status
+    from futudiffu_b200.dit import DiT, DiTConfig, euler_step, flops_per_sample_step, sigmas
+
+    if DIT_BATCH % world:
+        raise SystemExit(f"batch {DIT_BATCH} does not shard over {world} GPUs")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = DiTConfig()
+    model = DiT(cfg, seed=0, device=dev)  # identical weights on every rank
+    bl = DIT_BATCH // world
+    g = torch.Generator().manual_seed(100 + rank)  # this rank's samples
+    img = torch.randn(bl, cfg.img_tokens, cfg.patch_dim, generator=g).to(torch.bfloat16)
+    txt = torch.randn(bl, cfg.txt_tokens, cfg.hidden, generator=g).to(torch.bfloat16)
+    d_img, d_txt = img.to(dev), txt.to(dev)
+    sig = sigmas(28)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i, x):
+        return euler_step(model, x, d_txt, sig[i % 28], sig[i % 28 + 1])
+
+    x = d_img
+    for i in range(args.warmup):
+        x = step(i, x)
+    torch.cuda.synchronize()
+    check_status()
+    rec = LaunchRecorder()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else local) as clocks:
+        rec.active = True
+        start.record(stream)
+        for i in range(args.steps):
+            x = step(i, x)
+        end.record(stream)
+        rec.active = False
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_local = start.elapsed_time(end) / args.steps
+    ms = max_over_ranks(ms_local, world, dev)
+    gemm_work, gemm_ms, n_gemm = rec.summary("gemm")
+    attn_work, attn_ms, n_attn = rec.summary("attn")
+    launches = rec.launches
+    rec.close()
+    check_status()
+    value = 1e3 / ms
+
+    # ---------------- end to end: pinned host latents + text -> device -> Euler step -> host
+    h_img, h_txt = img.pin_memory(), txt.pin_memory()
+    h_out = torch.empty_like(img).pin_memory()
+    h2d = (img.numel() + txt.numel()) * 2
+    d2h = img.numel() * 2
+
+    def e2e_step(i):
+        xi = h_img.to(dev, non_blocking=True)
+        ti = h_txt.to(dev, non_blocking=True)
+        y = euler_step(model, xi, ti, sig[i], sig[i + 1])
+        h_out.copy_(y, non_blocking=True)
+
+    e2e_step(0)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_n = 3
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(e2e_n):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_n, world, dev)
+    check_status()
+
+    if rank == 0:
+        pk = peaks()
+        peak = 2.0 * pk["bf16_tflops_sustained"]
+        gemm_tf = gemm_work / (gemm_ms * 1e-3) / 1e12
+        step_flops = flops_per_sample_step(cfg) * DIT_BATCH
+        line = {
+            "metric": DIT_METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp8/int8", "data": "synthetic (random-init weights, N(0,1) latents/text)",
+            "config": {"workload": "config4_dit_denoise", "batch": DIT_BATCH, "per_gpu_batch": bl,
+                       "blocks": "19 double + 38 single", "hidden": cfg.hidden, "heads": cfg.heads,
+                       "tokens": f"{cfg.img_tokens} image + {cfg.txt_tokens} text", "euler_steps": 28,
+                       "linears": "fp8 e4m3 1x128 act / 128x128 weight scales (tcgen05)",
+                       "attention": "int8 per-block QK, e4m3 P/V (tcgen05)",
+                       "l2": "weights 11 GB and activations >> 126 MB L2; no explicit flush",
+                       "parallelism": f"batch sharded by sample x{world}, no collective",
+                       "model_tflop_per_step": step_flops / 1e12,
+                       "model_tflops": step_flops / (ms * 1e-3) / 1e12,
+                       "attention_kernel_tops": attn_work / (attn_ms * 1e-3) / 1e12 if attn_ms else None,
+                       "time_share": {"gemm": gemm_ms / args.steps / ms_local, "attention": attn_ms / args.steps / ms_local}},
+            "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": peak, "unit": "TFLOP/s",
+                         "frac": gemm_tf / peak, "traffic": None,
+                         "kernel": f"gemm_fp8_kernel (all {n_gemm // max(1, args.steps)} GEMM launches of a step, "
+                                   "flop-weighted)",
+                         "peak_source": f"2 x {pk['source']} sustained bf16 dense "
+                                        f"({pk['bf16_tflops_sustained']} TF/s, kernels inside a long step): "
+                                        "fp8 dense rate is twice bf16"},
+            "cpu_baseline": dit_cpu_sample() if world == 1 else None,
+            "e2e": {"value": 1e3 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms,
+                    "api": "futudiffu_b200.dit.euler_step"},
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 GEMM_SHAPES = {"config1": (2048, 3072, 3072), "ref_qkv": (8576, 11520, 3840), "ref_w2": (8576, 3840, 10240)}
 
 
@@ -368,16 +594,22 @@ def run_gemm(args, world, rank, local):
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default: 10 dit, 50 otherwise)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["attention", "gemm"], default="attention",
-                    help="attention = BASELINE config 2 (headline); gemm = FP8 block GEMM")
+    ap.add_argument("--workload", choices=["dit", "attention", "gemm"], default="dit",
+                    help="dit = BASELINE config 4 (headline); attention = config 2; gemm = config 1")
     ap.add_argument("--gemm-shape", choices=sorted(GEMM_SHAPES), default="config1")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
+    if args.steps is None:
+        args.steps = 10 if args.workload == "dit" else 50
     world, rank, local = dist_setup()
     try:
+        if args.workload == "dit":
+            if args.impl == "reference":
+                return run_dit_reference(args, world, rank)
+            return run_dit(args, world, rank, local)
         if args.impl == "reference":
             return run_reference(args, world, rank)
         if args.workload == "gemm":

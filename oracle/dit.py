@@ -128,3 +128,29 @@ def dit_forward(model, img, txt, t):
     scale = _torch_linear(torch.nn.functional.silu(vec.float()).to(torch.bfloat16), model.final_adaln)
     h = OF.rms_norm_modulate(x_img, _cpu(model.final_norm), scale, cfg.eps)
     return _torch_linear(h, model.final_out)
+
+
+def random_double_block(cfg, seed: int = 0):
+    """Weights of one double-stream block built on the CPU alone (oracle weight
+    quantiser), with the attribute layout of futudiffu_b200.dit.DoubleStreamBlock."""
+    from types import SimpleNamespace
+
+    g = torch.Generator().manual_seed(seed)
+    D, R = cfg.hidden, cfg.mlp_ratio
+
+    def rand(shape, std, mean=0.0):
+        return (torch.randn(shape, generator=g) * std + mean).to(torch.bfloat16)
+
+    def fp8_linear(n, k):
+        w8, ws = OQ.weight_quant(torch.randn(n, k, generator=g) * 0.02)
+        return SimpleNamespace(weight=w8, weight_scale=ws, bias=None)
+
+    def stream():
+        return SimpleNamespace(
+            adaln=SimpleNamespace(weight=rand((4 * D, D), 0.02), bias=rand((4 * D,), 0.02)),
+            norm_w=[rand((D,), 0.05, 1.0) for _ in range(4)],
+            q_norm=rand((128,), 0.05, 1.0), k_norm=rand((128,), 0.05, 1.0),
+            qkv=fp8_linear(3 * D, D), proj=fp8_linear(D, D),
+            mlp_in=fp8_linear(R * D, D), mlp_out=fp8_linear(D, R * D))
+
+    return SimpleNamespace(cfg=cfg, txt=stream(), img=stream())
