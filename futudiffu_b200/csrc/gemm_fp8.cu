@@ -5,56 +5,44 @@
 // fp8_gemm_v1t (B stored K x N), :1417-1525.
 //
 // Design (one persistent CTA per SM, warp specialised, 10 warps):
-//   warp 0      TMA producer: 128x128 A and B tiles per 128-K slice into a
-//               6-stage shared-memory ring (128-byte swizzle, no multicast).
-//   warp 1      MMA issuer: 4 x tcgen05.mma.kind::f8f6f4 (M128 N128 K32) per
-//               slice into one of 4 TMEM slice buffers (4 x 128 fp32 columns),
+//   warp 0      TMA producer: a 128 x 128 A tile and a 256 x 128 B tile per
+//               128-K slice into a 4-stage shared-memory ring (128-byte
+//               swizzle, no multicast).
+//   warp 1      MMA issuer: 4 x tcgen05.mma.kind::f8f6f4 (M128 N256 K32) per
+//               slice into one of 2 TMEM slice buffers (2 x 256 fp32 columns),
 //               then tcgen05.commit to free the smem stage and to publish the
 //               slice.
-//   warps 2..9  promotion / epilogue: each thread owns one output row and 64
-//               columns; per slice it tcgen05.ld's its 64 partial sums, frees
-//               the TMEM buffer and does acc += partial * (a_s * b_s) in fp32
-//               registers (the per-128-K-slice promotion of the reference).
-//               At the end of a tile it adds the bias and stores the row.
-// The 4-deep TMEM ring lets the tensor core run up to 3 slices ahead of the
-// promotion, so MMA and promotion overlap.
-//
-// Fused epilogues (EPI), each replacing a GEMM + quantiser pair of the
-// reference and producing its exact codes and scales:
-//   EPI_STORE      C = acc (+ bias) in bf16 / f16 / f32.
-//   EPI_QUANT      fp8_gemm_quant (fp8_kernels.py:573-709): the fp32
-//                  accumulator quantised 1 x 128 to e4m3 + fp32 dequant scales.
-//   EPI_GELU_TANH  GEMM -> bf16 -> GELU(tanh) -> 1 x 128 e4m3 (the MMDiT MLP:
-//                  replaces fp8_addmm + fp8_gelu_tanh_quant).
-//   EPI_SILU_GATE  the FFN chain head (transformer.py:536-545): B = [w1; w3]
-//                  (2 H x K); a CTA computes the w1 tile and then the matching
-//                  w3 tile of the same rows, parks w1 as bf16 in shared memory
-//                  and emits silu(w1) * w3 quantised 1 x 128 (replaces
-//                  fp8_addmm -> bf16 (M, 2H) -> fp8_silu_gate_quant).
-// The two threads that hold the halves of a 128-column group exchange their
-// maxima through shared memory (named barrier of the quadrant's two warps).
+//   warps 2..9  promotion / epilogue: each thread owns one output row and 128
+//               columns (one 1 x 128 output group); per slice it tcgen05.ld's
+//               its partial sums, frees the TMEM buffer and does
+//               acc += partial * (a_s * b_s) in fp32 registers (the
+//               per-128-K-slice promotion of the reference).
+// Why N = 256: an M128 N128 K32 MMA reads 8 KiB of operands from shared memory
+// in its 64 cycles, the SM's whole shared-memory bandwidth, and the TMA writes
+// of the next slice compete for the same bandwidth; at N = 256 each staged
+// byte feeds twice the MMA work (48 KiB per 512 MMA cycles instead of 32 KiB
+// per 256).  Tiles are visited in groups of GROUP_M row tiles so that the
+// tiles running at the same time share their A and B tiles in L2.
 #include "fd_act.cuh"
 #include "fd_host.h"
 
 namespace fd {
 namespace gemm {
 
-constexpr int BM = 128, BN = 128, BK = 128;
-constexpr int NTBUF = 4;
+constexpr int BM = 128, BN = 256, BK = 128;  // BN: MMA / TMEM columns per tile
+constexpr int NTBUF = 2;                       // TMEM slice buffers (2 x 256 columns)
+constexpr int STAGES = 4;
 constexpr int NUM_THREADS = 320;
 constexpr int EPI_WARPS = 8;
-constexpr uint32_t STAGE_BYTES = BM * BK + BN * BK;  // 32 KiB
+constexpr int GROUP_M = 16;                    // row tiles per rasterisation group
+constexpr uint32_t A_BYTES = BM * BK;          // 16 KiB
+constexpr uint32_t STAGE_BYTES = BM * BK + BN * BK;  // 48 KiB
 
 enum { EPI_STORE = 0, EPI_QUANT = 1, EPI_GELU_TANH = 2, EPI_SILU_GATE = 3 };
 
-template <int EPI>
 struct Layout {
-  static constexpr int STAGES = EPI == EPI_SILU_GATE ? 5 : 6;
-  static constexpr uint32_t OFF_STASH = STAGES * STAGE_BYTES;                  // w1 tile, bf16
-  static constexpr uint32_t STASH_BYTES = EPI == EPI_SILU_GATE ? BM * BN * 2 : 0;
-  static constexpr uint32_t OFF_RED = OFF_STASH + STASH_BYTES;                 // [2][2][128] f32
-  static constexpr uint32_t RED_BYTES = EPI == EPI_STORE ? 0 : 2 * 2 * 128 * 4;
-  static constexpr uint32_t OFF_BAR = OFF_RED + RED_BYTES;
+  static constexpr uint32_t OFF_RED = STAGES * STAGE_BYTES;  // [2][2][128] f32 (SiLU-gate max exchange)
+  static constexpr uint32_t OFF_BAR = OFF_RED + 2 * 2 * 128 * 4;
   static constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 /*barriers*/ + 1024 /*align*/;
 };
 
@@ -65,9 +53,21 @@ struct Params {
   void* c;
   float* c_s;      // quantising epilogues: 1 x 128 dequant scales (M, N_out / 128)
   int M, N, K;     // N: columns of the output (for EPI_SILU_GATE: H, B has 2 H rows)
-  int ntm, ntn, ntiles;
+  int ntm, ntn, ntiles;  // ntn: output column tiles (256 wide; 128 wide for EPI_SILU_GATE)
   int kblocks;
+  int nbs;         // rows of b_s (BMODE 0: ceil(rows of B / 128)); BMODE 1: its columns
 };
+
+// Tile t -> (row tile, column tile), GROUP_M row tiles at a time so that the
+// CTAs running together reuse their A and B tiles from L2.
+FD_DEV void tile_coords(const Params& p, int t, int& mb, int& nb) {
+  const int per_group = GROUP_M * p.ntn;
+  const int g = t / per_group, r = t % per_group;
+  const int m0 = g * GROUP_M;
+  const int gm = min(GROUP_M, p.ntm - m0);
+  mb = m0 + r % gm;
+  nb = r / gm;
+}
 
 template <int CDT>
 FD_DEV void store_row64(void* c, int64_t row_off, int n_start, int N, const float (&v)[64]) {
@@ -126,13 +126,10 @@ template <int BMODE, int CDT, int BDT, int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const Params p) {
-  using LY = Layout<EPI>;
-  constexpr int STAGES = LY::STAGES;
-  constexpr int NSUB = EPI == EPI_SILU_GATE ? 2 : 1;  // GEMM tiles per output tile
+  using LY = Layout;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * BM * BK;
+  // stage s: A tile at s * STAGE_BYTES, B tile (256 rows) right after it
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::OFF_BAR);
   uint64_t* full = bars;                   // [STAGES]
   uint64_t* empty = bars + STAGES;         // [STAGES]
@@ -178,18 +175,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       uint32_t issued_mask = 0;  // stages with a load issued
       for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x) {
-        const int mb = tile % p.ntm, nbo = tile / p.ntm;
-        for (int sub = 0; sub < NSUB && ok; ++sub) {
-          const int nb = nbo + sub * p.ntn;  // EPI_SILU_GATE: w3 rows follow the H w1 rows
-          for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
-            const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
-            if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
-            mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-            tma_load_2d(sA + s * (BM * BK), &tmA, &full[s], kb * BK, mb * BM);
-            if (B_MN) tma_load_2d(sB + s * (BN * BK), &tmB, &full[s], nb * BN, kb * BK);
-            else tma_load_2d(sB + s * (BN * BK), &tmB, &full[s], kb * BK, nb * BN);
-            issued_mask |= 1u << s;
+        int mb, nb;
+        tile_coords(p, tile, mb, nb);
+        for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
+          const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+          uint8_t* sa = smem + s * STAGE_BYTES;
+          uint8_t* sb = sa + A_BYTES;
+          mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+          tma_load_2d(sa, &tmA, &full[s], kb * BK, mb * BM);
+          if (EPI == EPI_SILU_GATE) {
+            // B rows [w1 block nb | w3 block nb]: the w3 rows start H rows further
+            tma_load_2d(sb, &tmB, &full[s], kb * BK, nb * 128);
+            tma_load_2d(sb + 128 * BK, &tmB, &full[s], kb * BK, p.N + nb * 128);
+          } else if (B_MN) {
+            // (K, N) storage: two 128-column panels of the 256-wide tile
+            tma_load_2d(sb, &tmB, &full[s], nb * BN, kb * BK);
+            tma_load_2d(sb + 128 * BK, &tmB, &full[s], nb * BN + 128, kb * BK);
+          } else {
+            tma_load_2d(sb, &tmB, &full[s], kb * BK, nb * BN);
           }
+          issued_mask |= 1u << s;
         }
       }
       // Drain: the newest load of every stage must have landed before exit.
@@ -206,22 +212,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       constexpr uint32_t idesc = make_idesc(/*c F32*/ 1, /*E4M3*/ 0, 0, /*a K-major*/ 0, B_MN, BM, BN);
       uint32_t it = 0;
       bool ok = true;
-      // GEMM tiles in the producer's order: per output tile, NSUB sub-tiles
-      const int ngemm = ((p.ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * NSUB;
-      for (int g = 0; g < ngemm && ok; ++g) {
+      for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x) {
         for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
           const uint32_t tb = it % NTBUF, tph = (it / NTBUF) & 1;
           if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
           if (!mbar_wait(&tempty[tb], tph ^ 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + s * (BM * BK));
-          const uint32_t b0 = smem_u32(sB + s * (BN * BK));
+          const uint32_t a0 = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t b0 = a0 + A_BYTES;
           const uint32_t d = tmem_base + tb * BN;
 #pragma unroll
           for (int k4 = 0; k4 < BK / 32; ++k4) {
             const uint64_t ad = make_sdesc_sw128(a0 + k4 * 32, 16, 1024);
-            const uint64_t bd = B_MN ? make_sdesc_sw128(b0 + k4 * 32 * 128, 16, 1024)
+            // MN-major B: 128-column panels 128 x BK bytes apart (LBO), 8 K rows per 1 KiB
+            const uint64_t bd = B_MN ? make_sdesc_sw128(b0 + k4 * 32 * 128, 128 * BK, 1024)
                                      : make_sdesc_sw128(b0 + k4 * 32, 16, 1024);
             mma_f8f6f4_ss(d, ad, bd, idesc, k4 > 0 ? 1u : 0u);
           }
@@ -234,115 +239,130 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ promotion + epilogue
+    // Thread (q, h): row q * 32 + lane; TMEM columns [128 h, 128 h + 128) of the
+    // 256-column accumulator (EPI_SILU_GATE: w1 columns [64 h, 64 h + 64) and the
+    // matching w3 columns 128 + [64 h, 64 h + 64)).
     const int q = warp & 3;             // TMEM lane quadrant this warp may access
-    const int h = (warp - 2) >> 2;      // column half: 0 -> cols 0..63, 1 -> 64..127
+    const int h = (warp - 2) >> 2;      // column half
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const int r = q * 32 + lane;        // row within the tile
-    const int et = h * 128 + r;         // epilogue thread index 0..255
-    uint4* stash = reinterpret_cast<uint4*>(smem + LY::OFF_STASH);  // [8][256] x 16 B
-    float* red = reinterpret_cast<float*>(smem + LY::OFF_RED);      // [parity][half][128]
+    float* red = reinterpret_cast<float*>(smem + LY::OFF_RED);  // [parity][half][128]
     uint32_t it = 0, nt = 0;
     bool ok = true;
     // A thread whose wait timed out keeps walking the tiles (skipping the work)
     // so its partner is never left at the max-exchange barrier.
     for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++nt) {
-      const int mb = tile % p.ntm, nbo = tile / p.ntm;
+      int mb, nb;
+      tile_coords(p, tile, mb, nb);
       const int m = mb * BM + r;
       const bool row_ok = m < p.M;
       const float* as_row = p.a_s + (int64_t)(row_ok ? m : 0) * p.kblocks;
-      for (int sub = 0; sub < NSUB; ++sub) {
-        const int nb = nbo + sub * p.ntn;
-        float acc[64];
+      // GEMM columns (rows of B) of acc[0..63] and acc[64..127]
+      const int n_lo = EPI == EPI_SILU_GATE ? nb * 128 + h * 64 : nb * BN + h * 128;
+      const int n_hi = EPI == EPI_SILU_GATE ? p.N + nb * 128 + h * 64 : n_lo + 64;
+      const uint32_t col_lo = EPI == EPI_SILU_GATE ? h * 64 : h * 128;
+      const uint32_t col_hi = col_lo + (EPI == EPI_SILU_GATE ? 128 : 64);
+      float acc[128];
 #pragma unroll
-        for (int i = 0; i < 64; ++i) acc[i] = 0.f;
-        for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
-          const uint32_t tb = it % NTBUF, tph = (it / NTBUF) & 1;
-          const float bs = BMODE == 1   ? __ldg(p.b_s + (int64_t)kb * (p.ntn * NSUB) + nb)
-                           : BMODE == 0 ? __ldg(p.b_s + (int64_t)nb * p.kblocks + kb)
-                                        : 1.0f;
-          const float sc = (row_ok ? __ldg(as_row + kb) : 0.f) * bs;
-          ok = ok && mbar_wait(&tfull[tb], tph, abort_flag);
-          ok = __all_sync(0xffffffffu, ok);
-          if (!ok) continue;
-          tc_fence_after();
-          uint32_t r0[32], r1[32];
-          const uint32_t taddr = tmem_base + lane_base + tb * BN + h * 64;
-          tmem_ld32(taddr, r0);
-          tmem_ld32(taddr + 32, r1);
-          tmem_wait_ld();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[tb]);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            acc[i] = fmaf(__uint_as_float(r0[i]), sc, acc[i]);
-            acc[32 + i] = fmaf(__uint_as_float(r1[i]), sc, acc[32 + i]);
-          }
-        }
-        const int n0 = nb * BN + h * 64;  // column of acc[0] in the GEMM output
-        if (BMODE == 2) {
-          // fp8_gemm_rowwise_kernel: accumulator *= b_s[n] after the K loop (:407-408)
-#pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            const int n = n0 + i;
-            acc[i] *= (n < p.N) ? __ldg(p.b_s + n) : 0.f;
-          }
-        }
-        if (BDT >= 0 && p.bias) {
-#pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            const int n = n0 + i;
-            if (EPI == EPI_SILU_GATE || n < p.N) acc[i] += load_bias<BDT < 0 ? FD_DT_F32 : BDT>(p.bias, n);
-          }
-        }
-        if constexpr (EPI == EPI_STORE) {
-          if (ok && row_ok) store_row64<CDT>(p.c, (int64_t)m * p.N, n0, p.N, acc);
+      for (int i = 0; i < 128; ++i) acc[i] = 0.f;
+      for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
+        const uint32_t tb = it % NTBUF, tph = (it / NTBUF) & 1;
+        float bs_lo, bs_hi;
+        // (columns past the end of B read the last block's scale; they are never stored)
+        const int blo = min(n_lo / 128, p.nbs - 1), bhi = min(n_hi / 128, p.nbs - 1);
+        if (BMODE == 1) {
+          bs_lo = __ldg(p.b_s + (int64_t)kb * p.nbs + blo);
+          bs_hi = __ldg(p.b_s + (int64_t)kb * p.nbs + bhi);
+        } else if (BMODE == 0) {
+          bs_lo = __ldg(p.b_s + (int64_t)blo * p.kblocks + kb);
+          bs_hi = __ldg(p.b_s + (int64_t)bhi * p.kblocks + kb);
         } else {
-          if (EPI == EPI_SILU_GATE && sub == 0) {
-            // w1 tile: the reference rounds the w1w3 GEMM output to bf16; park it
+          bs_lo = bs_hi = 1.0f;
+        }
+        const float as = row_ok ? __ldg(as_row + kb) : 0.f;
+        const float sc_lo = as * bs_lo, sc_hi = as * bs_hi;
+        ok = ok && mbar_wait(&tfull[tb], tph, abort_flag);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) continue;
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + lane_base + tb * BN;
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-              stash[k * 256 + et] =
-                  make_uint4(pack_bf16x2(acc[8 * k], acc[8 * k + 1]), pack_bf16x2(acc[8 * k + 2], acc[8 * k + 3]),
-                             pack_bf16x2(acc[8 * k + 4], acc[8 * k + 5]), pack_bf16x2(acc[8 * k + 6], acc[8 * k + 7]));
-            continue;
+        for (int c = 0; c < 8; ++c) {
+          uint32_t r0[16];
+          tmem_ld16(taddr + (c < 4 ? col_lo : col_hi) + (c & 3) * 16, r0);
+          tmem_wait_ld();
+          if (c == 7) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[tb]);
           }
-          if (EPI == EPI_GELU_TANH) {
+          const float sc = c < 4 ? sc_lo : sc_hi;
 #pragma unroll
-            for (int i = 0; i < 64; ++i) acc[i] = gelu_tanh(round_to_bf16(acc[i]));
-          } else if (EPI == EPI_SILU_GATE) {
+          for (int i = 0; i < 16; ++i) acc[16 * c + i] = fmaf(__uint_as_float(r0[i]), sc, acc[16 * c + i]);
+        }
+      }
+      if (BMODE == 2) {
+        // fp8_gemm_rowwise_kernel: accumulator *= b_s[n] after the K loop (:407-408)
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const uint4 w = stash[k * 256 + et];
-              const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+        for (int i = 0; i < 128; ++i) {
+          const int n = n_lo + i;
+          acc[i] *= (n < p.N) ? __ldg(p.b_s + n) : 0.f;
+        }
+      }
+      if (BDT >= 0 && p.bias) {
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                acc[8 * k + 2 * e] = silu_gate(__uint_as_float(ww[e] << 16), round_to_bf16(acc[8 * k + 2 * e]));
-                acc[8 * k + 2 * e + 1] =
-                    silu_gate(__uint_as_float(ww[e] & 0xFFFF0000u), round_to_bf16(acc[8 * k + 2 * e + 1]));
-              }
-            }
-          }
-          // 1 x 128 group = this thread's 64 columns and its partner's
-          float amax = 0.f;
+        for (int i = 0; i < 128; ++i) {
+          const int n = (i < 64 ? n_lo : n_hi) + (i & 63);
+          if (EPI == EPI_SILU_GATE || n < p.N) acc[i] += load_bias<BDT < 0 ? FD_DT_F32 : BDT>(p.bias, n);
+        }
+      }
+      if constexpr (EPI == EPI_STORE) {
+        if (ok && row_ok) {
+          store_row64<CDT>(p.c, (int64_t)m * p.N, n_lo, p.N, *reinterpret_cast<float(*)[64]>(acc));
+          store_row64<CDT>(p.c, (int64_t)m * p.N, n_lo + 64, p.N, *reinterpret_cast<float(*)[64]>(acc + 64));
+        }
+      } else if constexpr (EPI == EPI_SILU_GATE) {
+        // the reference rounds the w1w3 GEMM output to bf16 before the gate
 #pragma unroll
-          for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(acc[i]));
-          float* rd = red + (nt & 1) * 256;
-          rd[h * 128 + r] = amax;
-          named_bar_sync(1 + q, 64);
-          amax = fmaxf(amax, rd[(h ^ 1) * 128 + r]);
-          if (ok && row_ok) {
-            const float qm = quant_mult(amax);
-            const int c0 = nbo * BN + h * 64;  // output column of acc[0]
-            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.c) + (int64_t)m * p.N + c0);
+        for (int i = 0; i < 64; ++i) acc[i] = silu_gate(round_to_bf16(acc[i]), round_to_bf16(acc[64 + i]));
+        // 1 x 128 group = this thread's 64 gate columns and its partner's
+        float amax = 0.f;
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              dst[k] = make_uint4(quant4(acc[16 * k], acc[16 * k + 1], acc[16 * k + 2], acc[16 * k + 3], qm),
-                                  quant4(acc[16 * k + 4], acc[16 * k + 5], acc[16 * k + 6], acc[16 * k + 7], qm),
-                                  quant4(acc[16 * k + 8], acc[16 * k + 9], acc[16 * k + 10], acc[16 * k + 11], qm),
-                                  quant4(acc[16 * k + 12], acc[16 * k + 13], acc[16 * k + 14], acc[16 * k + 15], qm));
-            if (h == 0) p.c_s[(int64_t)m * (p.N / BN) + nbo] = dequant_scale(amax);
-          }
+        for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(acc[i]));
+        float* rd = red + (nt & 1) * 256;
+        rd[h * 128 + r] = amax;
+        named_bar_sync(1 + q, 64);
+        amax = fmaxf(amax, rd[(h ^ 1) * 128 + r]);
+        if (ok && row_ok) {
+          const float qm = quant_mult(amax);
+          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.c) + (int64_t)m * p.N + nb * 128 + h * 64);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            dst[k] = make_uint4(quant4(acc[16 * k], acc[16 * k + 1], acc[16 * k + 2], acc[16 * k + 3], qm),
+                                quant4(acc[16 * k + 4], acc[16 * k + 5], acc[16 * k + 6], acc[16 * k + 7], qm),
+                                quant4(acc[16 * k + 8], acc[16 * k + 9], acc[16 * k + 10], acc[16 * k + 11], qm),
+                                quant4(acc[16 * k + 12], acc[16 * k + 13], acc[16 * k + 14], acc[16 * k + 15], qm));
+          if (h == 0) p.c_s[(int64_t)m * (p.N / 128) + nb] = dequant_scale(amax);
+        }
+      } else {
+        // EPI_QUANT / EPI_GELU_TANH: this thread's 128 columns are one whole output group
+        if (EPI == EPI_GELU_TANH) {
+#pragma unroll
+          for (int i = 0; i < 128; ++i) acc[i] = gelu_tanh(round_to_bf16(acc[i]));
+        }
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 128; ++i) amax = fmaxf(amax, fabsf(acc[i]));
+        if (ok && row_ok && n_lo < p.N) {
+          const float qm = quant_mult(amax);
+          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.c) + (int64_t)m * p.N + n_lo);
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            dst[k] = make_uint4(quant4(acc[16 * k], acc[16 * k + 1], acc[16 * k + 2], acc[16 * k + 3], qm),
+                                quant4(acc[16 * k + 4], acc[16 * k + 5], acc[16 * k + 6], acc[16 * k + 7], qm),
+                                quant4(acc[16 * k + 8], acc[16 * k + 9], acc[16 * k + 10], acc[16 * k + 11], qm),
+                                quant4(acc[16 * k + 12], acc[16 * k + 13], acc[16 * k + 14], acc[16 * k + 15], qm));
+          p.c_s[(int64_t)m * (p.N / 128) + n_lo / 128] = dequant_scale(amax);
         }
       }
     }
@@ -357,7 +377,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 template <int BMODE, int CDT, int BDT, int EPI = EPI_STORE>
 static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t st) {
   auto kern = gemm_fp8_kernel<BMODE, CDT, BDT, EPI>;
-  constexpr uint32_t smem_bytes = Layout<EPI>::SMEM_BYTES;
+  constexpr uint32_t smem_bytes = Layout::SMEM_BYTES;
   static bool attr_done = false;  // per instantiation
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
@@ -434,7 +454,7 @@ extern "C" int fd_fp8_gemm_blockwise(const void* a, const float* a_s, const void
   if (b_layout != 1) {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
     const uint64_t strides[1] = {(uint64_t)K};
-    const uint32_t box[2] = {128, 128};
+    const uint32_t box[2] = {128, 256};
     int rc = encode_tiled(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, b, dims, strides, box,
                           CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
@@ -456,7 +476,8 @@ extern "C" int fd_fp8_gemm_blockwise(const void* a, const float* a_s, const void
   p.N = (int)N;
   p.K = (int)K;
   p.ntm = (int)((M + 127) / 128);
-  p.ntn = (int)((N + 127) / 128);
+  p.ntn = (int)((N + 255) / 256);
+  p.nbs = (int)((N + 127) / 128);
   p.ntiles = p.ntm * p.ntn;
   p.kblocks = (int)(K / 128);
   cudaStream_t st = (cudaStream_t)stream;
@@ -492,7 +513,8 @@ extern "C" int fd_fp8_gemm_quant(const void* a, const float* a_s, const void* b,
   {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)nb_rows};
     const uint64_t strides[1] = {(uint64_t)K};
-    const uint32_t box[2] = {128, 128};
+    // SiLU gate: two 128-row boxes (w1 block, w3 block) per B tile
+    const uint32_t box[2] = {128, act == FD_ACT_SILU_GATE ? 128u : 256u};
     int rc = encode_tiled(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, b, dims, strides, box,
                           CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
@@ -507,7 +529,8 @@ extern "C" int fd_fp8_gemm_quant(const void* a, const float* a_s, const void* b,
   p.N = (int)N;
   p.K = (int)K;
   p.ntm = (int)((M + 127) / 128);
-  p.ntn = (int)(N / 128);
+  p.ntn = act == FD_ACT_SILU_GATE ? (int)(N / 128) : (int)((N + 255) / 256);
+  p.nbs = (int)(nb_rows / 128);
   p.ntiles = p.ntm * p.ntn;
   p.kblocks = (int)(K / 128);
   cudaStream_t st = (cudaStream_t)stream;
