@@ -341,7 +341,7 @@ class LaunchRecorder:
             M, N, K = args[8], args[9], args[10]
             mult = 2 if (name == "fd_fp8_gemm_quant" and args[11] == self.L.ACT_SILU_GATE) else 1
             kind, work = "gemm", 2.0 * M * N * K * mult
-        elif name == "fd_sage_attn_fwd":
+        elif name in ("fd_sage_attn_fwd", "fd_sage_attn_fwd_bnhd"):
             BH, N = args[10], args[11]
             kind, work = "attn", 4.0 * BH * N * N * 128
         if kind is None:
@@ -452,9 +452,14 @@ def run_dit(args, world, rank, local):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else local) as clocks:
         rec.active = True
+        if args.profile:
+            torch.cuda.cudart().cudaProfilerStart()
         start.record(stream)
         for i in range(args.steps):
             x = step(i, x)
+            if args.profile and i == 0:
+                torch.cuda.synchronize()
+                torch.cuda.cudart().cudaProfilerStop()
         end.record(stream)
         rec.active = False
         torch.cuda.synchronize()
@@ -600,6 +605,9 @@ def main(argv=None) -> int:
     ap.add_argument("--workload", choices=["dit", "attention", "gemm"], default="dit",
                     help="dit = BASELINE config 4 (headline); attention = config 2; gemm = config 1")
     ap.add_argument("--gemm-shape", choices=sorted(GEMM_SHAPES), default="config1")
+    ap.add_argument("--profile", action="store_true",
+                    help="dit: bracket the first timed step with cudaProfilerStart/Stop "
+                         "(for ncu --profile-from-start off); timing of that run is not a result")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
     if args.steps is None:

@@ -60,13 +60,16 @@ _SIGS: dict[str, list] = {
     "fd_fp8_gelu_tanh_quant": [_P, _P, _P, _L, _L, _I, _P],
     "fd_fp8_gelu_requant": [_P, _P, _P, _P, _L, _L, _I, _P],
     "fd_rms_norm_modulate": [_P, _P, _I, _P, _I, _P, _L, _L, _L, _F, _P],
+    "fd_rms_norm_modulate_quant": [_P, _P, _I, _P, _I, _P, _P, _L, _L, _L, _F, _P],
     "fd_rms_norm_gate_residual": [_P, _P, _I, _P, _I, _P, _P, _L, _L, _L, _F, _P],
     "fd_qkv_postprocess": [_P, _P, _P, _P, _P, _P, _P, _L, _L, _L, _L, _F, _P],
+    "fd_qkv_postprocess_into": [_P, _P, _P, _P, _P, _P, _P, _L, _L, _L, _L, _F, _L, _L, _P],
     "fd_attn_quant_workspace_floats": [_L, _L],
     "fd_attn_quant": [_P, _P, _P, _L, _L, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P, _P],
     "fd_attn_quant_noalloc_max_floats": [],
     "fd_attn_quant_noalloc": [_P, _P, _P, _L, _L, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P],
     "fd_sage_attn_fwd": [_P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _L, _L, _I, _I, _I, _I, _P],
+    "fd_sage_attn_fwd_bnhd": [_P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _L, _L, _L, _I, _I, _I, _I, _P],
     "fd_sage_attn_bwd_prepass": [_P, _P, _P, _L, _L, _P],
     "fd_sage_attn_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _P, _L, _L, _I, _F, _P],
 }

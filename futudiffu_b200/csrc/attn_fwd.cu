@@ -123,6 +123,7 @@ struct Params {
   int q_gran;
   int64_t q_desc_stride;
   int64_t k_desc_stride;
+  int64_t out_heads;  // 0: out is (BH, N, 128); H > 0: out is (BH / H, N, H, 128)
 };
 
 FD_DEV void named_bar_sync(int id, int nthreads) {
@@ -576,7 +577,11 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
       const float l_div = any ? l_tot : 0.f;  // 0/0 -> NaN for rows that saw no key, as the reference
       const bool row_ok = qrow < p.N;
       if (row_ok && h == 0 && p.lse) p.lse[(int64_t)bh * p.N + qrow] = lse_v;
-      __nv_bfloat16* orow = p.out + ((int64_t)bh * p.N + (row_ok ? qrow : 0)) * HD + cb;
+      const int64_t orow_idx = p.out_heads == 0
+                                   ? (int64_t)bh * p.N + (row_ok ? qrow : 0)
+                                   : ((int64_t)(bh / p.out_heads) * p.N + (row_ok ? qrow : 0)) * p.out_heads +
+                                         bh % p.out_heads;
+      __nv_bfloat16* orow = p.out + orow_idx * HD + cb;
       // tcgen05.ld is warp-collective: every lane loads, only valid rows store
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
@@ -638,11 +643,11 @@ using namespace fd;
 
 int64_t fd_desc_stride(int64_t N, int gran, int rows_per_block);
 
-extern "C" int fd_sage_attn_fwd(const void* q_codes, const float* q_desc, const void* k_codes,
+static int sage_attn_fwd_impl(const void* q_codes, const float* q_desc, const void* k_codes,
                                 const float* k_desc, const void* v, const float* v_desc,
                                 const uint8_t* block_mask, int64_t mask_bh_stride, void* out,
                                 float* lse, int64_t BH, int64_t N, int qk_kind, int q_gran,
-                                int k_gran, int pv_kind, void* stream) {
+                                int k_gran, int pv_kind, int64_t out_heads, void* stream) {
   FD_CHECK_ARG(BH > 0 && BH <= 65535 && N > 0 && N < (1ll << 30), "bad shape");
   FD_CHECK_ARG(qk_kind == FD_QK_INT8 || qk_kind == FD_QK_FP8, "bad qk_kind");
   FD_CHECK_ARG(q_gran == FD_GRAN_TOKEN || q_gran == FD_GRAN_BLOCK, "bad q_gran");
@@ -683,6 +688,7 @@ extern "C" int fd_sage_attn_fwd(const void* q_codes, const float* q_desc, const 
   p.mask_bh_stride = mask_bh_stride;
   p.out = (__nv_bfloat16*)out;
   p.lse = lse;
+  p.out_heads = out_heads;
   p.N = (int)N;
   p.n_kv_tiles = (int)((N + 127) / 128);
   p.nkb64 = (int)((N + 63) / 64);
@@ -709,4 +715,23 @@ extern "C" int fd_sage_attn_fwd(const void* q_codes, const float* q_desc, const 
     }
   }
 #undef FD_ATTN
+}
+
+extern "C" int fd_sage_attn_fwd(const void* q_codes, const float* q_desc, const void* k_codes,
+                                const float* k_desc, const void* v, const float* v_desc,
+                                const uint8_t* block_mask, int64_t mask_bh_stride, void* out,
+                                float* lse, int64_t BH, int64_t N, int qk_kind, int q_gran,
+                                int k_gran, int pv_kind, void* stream) {
+  return sage_attn_fwd_impl(q_codes, q_desc, k_codes, k_desc, v, v_desc, block_mask, mask_bh_stride, out,
+                            lse, BH, N, qk_kind, q_gran, k_gran, pv_kind, 0, stream);
+}
+
+extern "C" int fd_sage_attn_fwd_bnhd(const void* q_codes, const float* q_desc, const void* k_codes,
+                                     const float* k_desc, const void* v, const float* v_desc,
+                                     const uint8_t* block_mask, int64_t mask_bh_stride, void* out,
+                                     float* lse, int64_t BH, int64_t N, int64_t H, int qk_kind,
+                                     int q_gran, int k_gran, int pv_kind, void* stream) {
+  FD_CHECK_ARG(H > 0 && BH % H == 0, "H must divide BH");
+  return sage_attn_fwd_impl(q_codes, q_desc, k_codes, k_desc, v, v_desc, block_mask, mask_bh_stride, out,
+                            lse, BH, N, qk_kind, q_gran, k_gran, pv_kind, H, stream);
 }

@@ -7,7 +7,7 @@
 // Design (one persistent CTA per SM, warp specialised, 10 warps):
 //   warp 0      TMA producer: a 128 x 128 A tile and a 256 x 128 B tile per
 //               128-K slice into a 4-stage shared-memory ring (128-byte
-//               swizzle, no multicast).
+//               swizzle, one plain TMA copy per tile).
 //   warp 1      MMA issuer: 4 x tcgen05.mma.kind::f8f6f4 (M128 N256 K32) per
 //               slice into one of 2 TMEM slice buffers (2 x 256 fp32 columns),
 //               then tcgen05.commit to free the smem stage and to publish the

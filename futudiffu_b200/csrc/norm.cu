@@ -2,6 +2,9 @@
 //   P1 rms_norm_modulate    (src/futudiffu/fused_kernels.py:43-86)
 //   P2 rms_norm_gate_residual (src/futudiffu/fused_kernels.py:99-148)
 //   P3 qkv_postprocess       (src/futudiffu/fused_kernels.py:270-385)
+//   P1 + G1 rms_norm_modulate_quant: P1's bf16 row quantised 1 x 128 to e4m3 in
+//      the same pass (the input of the next FP8 GEMM), equal to P1 followed by
+//      fp8_act_quant (src/futudiffu/fp8_kernels.py:54-90) code for code.
 //
 // P1/P2: one warp per token row; the row is held in registers (dim <= 8192,
 // 16-byte vectors), so x is read exactly once and the output written once.
@@ -11,7 +14,7 @@
 // Arithmetic follows the Triton kernels: fp32 throughout, mean of squares and
 // rrms = 1 / sqrt(mean + eps) with Triton's lowerings of `/` (div.full.f32) and
 // tl.sqrt (sqrt.approx.f32), products evaluated left to right.
-#include "fd_common.cuh"
+#include "fd_act.cuh"
 #include "fd_host.h"
 
 namespace fd {
@@ -40,29 +43,48 @@ FD_DEV uint4 pack_bf16x8(const float (&v)[8]) {
 // Max 8192 / (32 lanes * 8) = 32 vectors per lane.
 constexpr int kMaxVecPerLane = 32;
 
-// MODE 0: P1 (modulate), MODE 1: P2 (gate + residual)
+// MODE 0: P1 (modulate), MODE 1: P2 (gate + residual), MODE 2: P1 + 1 x 128 e4m3
+// quantisation (out holds the codes, qs the dequant scales).  A 128-column group
+// is 16 consecutive 8-column vectors, i.e. one half-warp for a given j.
+//
+// Grid (CTAs per sample, B): a CTA serves rows of one sample b, so the
+// per-column factors -- the norm weight and (1 + scale[b]) or tanh(gate[b]),
+// which the reference evaluates per element -- are computed once per CTA into
+// shared memory (fp32, dim <= 8192) and read back as 16-byte vectors.
 template <int MODE, int WDT, int SDT, int NV>
 __global__ void __launch_bounds__(256) rms_row_kernel(const __nv_bfloat16* __restrict__ x,
                                                      const void* __restrict__ w,
                                                      const void* __restrict__ sg,
                                                      const __nv_bfloat16* __restrict__ res,
                                                      __nv_bfloat16* __restrict__ out,
+                                                     float* __restrict__ qs,
                                                      int64_t rows, int64_t S, int dim, float eps) {
+  extern __shared__ float4 norm_smem[];
+  float* s_w = reinterpret_cast<float*>(norm_smem);  // [dim] weight
+  float* s_f = s_w + dim;                             // [dim] 1 + scale  or  tanh(gate)
   const int lane = lane_id();
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t b = blockIdx.y;
+  for (int col = threadIdx.x; col < dim; col += blockDim.x) {
+    s_w[col] = load_elem<WDT>(w, col);
+    const float sv = load_elem<SDT>(sg, b * dim + col);
+    s_f[col] = MODE == 1 ? tanhf(sv) : 1.0f + sv;
+  }
+  __syncthreads();
   const int nvec = dim / 8;
-  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp_id(); row < rows;
-       row += warps) {
-    const int64_t b = row / S;
-    float v[NV][8];
+  const int64_t wpb = (int64_t)gridDim.x * (blockDim.x >> 5);  // warps serving this sample
+  for (int64_t sr = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp_id(); sr < S; sr += wpb) {
+    const int64_t row = b * S + sr;
+    uint4 xr[NV];  // the row, still packed bf16 (half the registers of fp32)
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int c = (lane + 32 * j);
       if (c < nvec) {
-        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(x + row * dim) + c), v[j]);
+        xr[j] = __ldg(reinterpret_cast<const uint4*>(x + row * dim) + c);
+        float t[8];
+        unpack_bf16x8(xr[j], t);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) ss += v[j][e] * v[j][e];
+        for (int e = 0; e < 8; ++e) ss += t[e] * t[e];
       }
     }
     ss = warp_sum(ss);
@@ -71,18 +93,50 @@ __global__ void __launch_bounds__(256) rms_row_kernel(const __nv_bfloat16* __res
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int c = (lane + 32 * j);
-      if (c < nvec) {
+      if constexpr (MODE == 2) {
+        if (32 * j >= nvec) break;  // warp-uniform
+        // the unfused pair stores P1's row in bf16 and quantises those values
+        float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (c < nvec) {
+          const float4* w4 = reinterpret_cast<const float4*>(s_w + c * 8);
+          const float4* f4 = reinterpret_cast<const float4*>(s_f + c * 8);
+          const float4 wa = w4[0], wb = w4[1], fa = f4[0], fb = f4[1];
+          const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+          const float fv[8] = {fa.x, fa.y, fa.z, fa.w, fb.x, fb.y, fb.z, fb.w};
+          float xv[8];
+          unpack_bf16x8(xr[j], xv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[e] = round_to_bf16(((xv[e] * rrms) * wv[e]) * fv[e]);
+        }
+        float amax = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(o[e]));
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        if (c < nvec) {
+          const float qm = quant_mult(amax);
+          uint8_t* codes = reinterpret_cast<uint8_t*>(out);
+          *reinterpret_cast<uint2*>(codes + row * dim + c * 8) =
+              make_uint2(quant4(o[0], o[1], o[2], o[3], qm), quant4(o[4], o[5], o[6], o[7], qm));
+          if ((lane & 15) == 0) qs[row * (dim / 128) + c / 16] = dequant_scale(amax);
+        }
+      } else if (c < nvec) {
         float o[8];
         float r[8];
         if constexpr (MODE == 1)
           unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(res + row * dim) + c), r);
+        const float4* w4 = reinterpret_cast<const float4*>(s_w + c * 8);
+        const float4* f4 = reinterpret_cast<const float4*>(s_f + c * 8);
+        const float4 wa = w4[0], wb = w4[1], fa = f4[0], fb = f4[1];
+        const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        const float fv[8] = {fa.x, fa.y, fa.z, fa.w, fb.x, fb.y, fb.z, fb.w};
+        float xv[8];
+        unpack_bf16x8(xr[j], xv);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const int col = c * 8 + e;
-          const float normed = (v[j][e] * rrms) * load_elem<WDT>(w, col);
-          const float sv = load_elem<SDT>(sg, b * dim + col);
-          if constexpr (MODE == 0) o[e] = normed * (1.0f + sv);
-          else o[e] = r[e] + tanhf(sv) * normed;
+          const float normed = (xv[e] * rrms) * wv[e];
+          if constexpr (MODE == 1) o[e] = r[e] + fv[e] * normed;
+          else o[e] = normed * fv[e];
         }
         reinterpret_cast<uint4*>(out + row * dim)[c] = pack_bf16x8(o);
       }
@@ -92,19 +146,33 @@ __global__ void __launch_bounds__(256) rms_row_kernel(const __nv_bfloat16* __res
 
 template <int MODE, int WDT, int SDT>
 static void launch_rms(const void* x, const void* w, const void* sg, const void* res, void* out,
-                       int64_t rows, int64_t S, int dim, float eps, cudaStream_t st) {
+                       float* qs, int64_t rows, int64_t S, int dim, float eps, cudaStream_t st) {
   const int nvec = dim / 8;
-  int64_t grid = (rows + 7) / 8;
-  const int64_t cap = (int64_t)num_sms() * 16;
-  if (grid > cap) grid = cap;
-  if (grid < 1) grid = 1;
+  const int64_t B = rows / S;
+  // about 8 CTAs (64 warps) per SM in total, spread over the samples
+  int64_t per_b = ((int64_t)num_sms() * 8 + B - 1) / B;
+  const int64_t need = (S + 7) / 8;
+  if (per_b > need) per_b = need;
+  if (per_b < 1) per_b = 1;
+  const dim3 grid((unsigned)per_b, (unsigned)B);
+  const size_t smem = 2 * (size_t)dim * sizeof(float);
 #define FD_RMS_LAUNCH(NVV)                                                                  \
-  rms_row_kernel<MODE, WDT, SDT, NVV><<<(unsigned)grid, 256, 0, st>>>(                     \
-      (const __nv_bfloat16*)x, w, sg, (const __nv_bfloat16*)res, (__nv_bfloat16*)out, rows, S, \
-      dim, eps)
+  do {                                                                                      \
+    auto kern = rms_row_kernel<MODE, WDT, SDT, NVV>;                                        \
+    static bool attr_done = false;                                                          \
+    if (!attr_done) {                                                                       \
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 8192 * 4); \
+      attr_done = true;                                                                     \
+    }                                                                                       \
+    kern<<<grid, 256, smem, st>>>((const __nv_bfloat16*)x, w, sg, (const __nv_bfloat16*)res, \
+                                  (__nv_bfloat16*)out, qs, rows, S, dim, eps);              \
+  } while (0)
+  // the row lives in registers: the smallest vector count that holds it
   if (nvec <= 32 * 4) FD_RMS_LAUNCH(4);
   else if (nvec <= 32 * 8) FD_RMS_LAUNCH(8);
+  else if (nvec <= 32 * 12) FD_RMS_LAUNCH(12);  // dim 3072
   else if (nvec <= 32 * 16) FD_RMS_LAUNCH(16);
+  else if (nvec <= 32 * 20) FD_RMS_LAUNCH(20);  // dim 5120
   else FD_RMS_LAUNCH(32);
 #undef FD_RMS_LAUNCH
 }
@@ -112,12 +180,12 @@ static void launch_rms(const void* x, const void* w, const void* sg, const void*
 template <int MODE>
 static int dispatch_rms(const void* x, const void* w, int wdt, const void* sg, int sdt,
                         const void* res, void* out, int64_t rows, int64_t S, int dim, float eps,
-                        cudaStream_t st) {
+                        cudaStream_t st, float* qs = nullptr) {
 #define FD_RMS_W(WD)                                                                       \
   switch (sdt) {                                                                           \
-    case FD_DT_BF16: launch_rms<MODE, WD, FD_DT_BF16>(x, w, sg, res, out, rows, S, dim, eps, st); break; \
-    case FD_DT_F16: launch_rms<MODE, WD, FD_DT_F16>(x, w, sg, res, out, rows, S, dim, eps, st); break;   \
-    case FD_DT_F32: launch_rms<MODE, WD, FD_DT_F32>(x, w, sg, res, out, rows, S, dim, eps, st); break;   \
+    case FD_DT_BF16: launch_rms<MODE, WD, FD_DT_BF16>(x, w, sg, res, out, qs, rows, S, dim, eps, st); break; \
+    case FD_DT_F16: launch_rms<MODE, WD, FD_DT_F16>(x, w, sg, res, out, qs, rows, S, dim, eps, st); break;   \
+    case FD_DT_F32: launch_rms<MODE, WD, FD_DT_F32>(x, w, sg, res, out, qs, rows, S, dim, eps, st); break;   \
     default: return set_error(FD_ERR_ARG, "unsupported scale/gate dtype");                 \
   }
   switch (wdt) {
@@ -127,7 +195,7 @@ static int dispatch_rms(const void* x, const void* w, int wdt, const void* sg, i
     default: return set_error(FD_ERR_ARG, "unsupported weight dtype");
   }
 #undef FD_RMS_W
-  return check_launch(MODE == 0 ? "rms_norm_modulate" : "rms_norm_gate_residual");
+  return check_launch(MODE == 0 ? "rms_norm_modulate" : MODE == 1 ? "rms_norm_gate_residual" : "rms_norm_modulate_quant");
 }
 
 // ---------------------------------------------------------------- P3
@@ -140,7 +208,8 @@ __global__ void __launch_bounds__(256) qkv_post_kernel(const __nv_bfloat16* __re
                                                       __nv_bfloat16* __restrict__ oq,
                                                       __nv_bfloat16* __restrict__ ok,
                                                       __nv_bfloat16* __restrict__ ov,
-                                                      int64_t rows, int64_t S, int H, float eps) {
+                                                      int64_t rows, int64_t S, int H, float eps,
+                                                      int64_t S_out, int64_t s_off) {
   constexpr int HD = 128;
   const int lane = lane_id();
   const int64_t items = rows * H;
@@ -181,7 +250,7 @@ __global__ void __launch_bounds__(256) qkv_post_kernel(const __nv_bfloat16* __re
       ko[2 * p + 1] = f.z * ke + f.x * kd;
     }
     const int64_t b = row / S, s = row % S;
-    const int64_t o = ((b * H + h) * S + s) * HD + lane * 4;
+    const int64_t o = ((b * H + h) * S_out + s_off + s) * HD + lane * 4;
     *reinterpret_cast<uint2*>(oq + o) = make_uint2(pack_bf16x2(qo[0], qo[1]), pack_bf16x2(qo[2], qo[3]));
     *reinterpret_cast<uint2*>(ok + o) = make_uint2(pack_bf16x2(ko[0], ko[1]), pack_bf16x2(ko[2], ko[3]));
     *reinterpret_cast<uint2*>(ov + o) = uv;
@@ -204,6 +273,18 @@ extern "C" int fd_rms_norm_modulate(const void* x, const void* w, int w_dtype, c
                          (cudaStream_t)stream);
 }
 
+extern "C" int fd_rms_norm_modulate_quant(const void* x, const void* w, int w_dtype, const void* scale,
+                                          int scale_dtype, void* y, float* y_s, int64_t B, int64_t S,
+                                          int64_t dim, float eps, void* stream) {
+  FD_CHECK_ARG(B >= 0 && S >= 0 && dim > 0 && dim % 128 == 0 && dim <= 8192,
+               "dim must be a multiple of 128 and at most 8192");
+  if (B * S == 0) return FD_OK;
+  FD_CHECK_ARG(x && w && scale && y && y_s, "null pointer");
+  FD_CHECK_ARG(aligned16(x) && aligned16(y), "x and y must be 16-byte aligned");
+  return dispatch_rms<2>(x, w, w_dtype, scale, scale_dtype, nullptr, y, B * S, S, (int)dim, eps,
+                         (cudaStream_t)stream, y_s);
+}
+
 extern "C" int fd_rms_norm_gate_residual(const void* x, const void* w, int w_dtype,
                                          const void* gate, int gate_dtype, const void* residual,
                                          void* out, int64_t B, int64_t S, int64_t dim, float eps,
@@ -218,11 +299,13 @@ extern "C" int fd_rms_norm_gate_residual(const void* x, const void* w, int w_dty
                          (cudaStream_t)stream);
 }
 
-extern "C" int fd_qkv_postprocess(const void* qkv, const float* qw, const float* kw,
-                                  const float* freqs, void* oq, void* ok, void* ov, int64_t B,
-                                  int64_t S, int64_t H, int64_t hd, float eps, void* stream) {
+extern "C" int fd_qkv_postprocess_into(const void* qkv, const float* qw, const float* kw,
+                                       const float* freqs, void* oq, void* ok, void* ov, int64_t B,
+                                       int64_t S, int64_t H, int64_t hd, float eps, int64_t S_out,
+                                       int64_t s_off, void* stream) {
   FD_CHECK_ARG(hd == 128, "head_dim must be 128");
   FD_CHECK_ARG(B >= 0 && S >= 0 && H > 0, "bad shape");
+  FD_CHECK_ARG(s_off >= 0 && S_out >= s_off + S, "S_out must hold rows [s_off, s_off + S)");
   if (B * S == 0) return FD_OK;
   FD_CHECK_ARG(qkv && qw && kw && freqs && oq && ok && ov, "null pointer");
   FD_CHECK_ARG(aligned16(qw) && aligned16(kw) && aligned16(freqs) && aligned8(qkv) &&
@@ -234,6 +317,12 @@ extern "C" int fd_qkv_postprocess(const void* qkv, const float* qw, const float*
   if (grid > cap) grid = cap;
   qkv_post_kernel<<<(unsigned)grid, 256, 0, (cudaStream_t)stream>>>(
       (const __nv_bfloat16*)qkv, qw, kw, freqs, (__nv_bfloat16*)oq, (__nv_bfloat16*)ok,
-      (__nv_bfloat16*)ov, B * S, S, (int)H, eps);
+      (__nv_bfloat16*)ov, B * S, S, (int)H, eps, S_out, s_off);
   return check_launch("qkv_postprocess");
+}
+
+extern "C" int fd_qkv_postprocess(const void* qkv, const float* qw, const float* kw,
+                                  const float* freqs, void* oq, void* ok, void* ov, int64_t B,
+                                  int64_t S, int64_t H, int64_t hd, float eps, void* stream) {
+  return fd_qkv_postprocess_into(qkv, qw, kw, freqs, oq, ok, ov, B, S, H, hd, eps, S, 0, stream);
 }

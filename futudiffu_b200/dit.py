@@ -43,7 +43,13 @@ from .fp8_kernels import (
     fp8_gemm_blockwise,
     fp8_gemm_gelu_tanh_quant,
 )
-from .fused_kernels import fused_qkv_postprocess, fused_rms_norm_gate_residual, fused_rms_norm_modulate
+from .fused_kernels import (
+    fused_qkv_postprocess,
+    fused_rms_norm_gate_residual,
+    fused_rms_norm_modulate,
+    fused_rms_norm_modulate_quant,
+    qkv_postprocess_into,
+)
 from .sage_attention import _attn_forward
 
 HEAD_DIM = 128
@@ -122,6 +128,20 @@ def linear_bf16(x: Tensor, lin: FP8Linear) -> Tensor:
     return fp8_gemm_blockwise(a8, a_s, lin.weight, lin.weight_scale, output_dtype=torch.bfloat16)
 
 
+def gemm_bf16(a8: Tensor, a_s: Tensor, lin: FP8Linear) -> Tensor:
+    """Quantised activation (codes, 1 x 128 scales) -> FP8 GEMM -> bf16."""
+    if lin.bias is not None:
+        return fp8_addmm_blockwise(a8, a_s, lin.weight, lin.weight_scale, bias=lin.bias,
+                                   output_dtype=torch.bfloat16)
+    return fp8_gemm_blockwise(a8, a_s, lin.weight, lin.weight_scale, output_dtype=torch.bfloat16)
+
+
+def mlp_fp8_q(a8: Tensor, a_s: Tensor, w_in: FP8Linear, w_out: FP8Linear) -> Tensor:
+    """GELU(tanh) MLP on a quantised input, kept in FP8 between its GEMMs."""
+    h8, h_s = fp8_gemm_gelu_tanh_quant(a8, a_s, w_in.weight, w_in.weight_scale, bias=w_in.bias)
+    return fp8_gemm_blockwise(h8, h_s, w_out.weight, w_out.weight_scale, output_dtype=torch.bfloat16)
+
+
 def mlp_fp8(x: Tensor, w_in: FP8Linear, w_out: FP8Linear) -> Tensor:
     """GELU(tanh) MLP kept in FP8 between its GEMMs (fused GELU + requant epilogue)."""
     a8, a_s = fp8_act_quant(x)
@@ -130,11 +150,11 @@ def mlp_fp8(x: Tensor, w_in: FP8Linear, w_out: FP8Linear) -> Tensor:
 
 
 def joint_attention(q: Tensor, k: Tensor, v: Tensor, cfg: DiTConfig) -> Tensor:
-    """Quantized attention over (B, H, N, 128) -> (B, N, H * 128) bf16."""
+    """Quantized attention over (B, H, N, 128) -> (B, N, H * 128) bf16, written in
+    that layout by the kernel (no transpose)."""
     o, _ = _attn_forward(q, k, v, None, block_mask=None, qk_quant=cfg.qk_quant, pv_quant=cfg.pv_quant,
-                         granularity=cfg.granularity, want_lse=False)
-    B, H, N, D = o.shape
-    return o.transpose(1, 2).reshape(B, N, H * D)
+                         granularity=cfg.granularity, want_lse=False, out_bnhd=True)
+    return o
 
 
 class _Stream(nn.Module):
@@ -174,25 +194,27 @@ class DoubleStreamBlock(nn.Module):
                 freqs_img: Tensor) -> tuple[Tensor, Tensor]:
         """x_* (B, L_*, D) bf16; vec (B, D); freqs_* (B, L_*, 64, 2, 2) fp32 (see batch_freqs)."""
         cfg = self.cfg
-        B = x_txt.shape[0]
-        mods, qs, ks, vs = [], [], [], []
-        for st, x, fr in ((self.txt, x_txt, freqs_txt), (self.img, x_img, freqs_img)):
+        B, Nt = x_txt.shape[0], x_txt.shape[1]
+        N = Nt + x_img.shape[1]
+        # joint Q/K/V: each stream's post-processing writes its rows in place
+        q, k, v = (torch.empty(B, cfg.heads, N, HEAD_DIM, dtype=torch.bfloat16, device=x_txt.device)
+                   for _ in range(3))
+        mods = []
+        for st, x, fr, off in ((self.txt, x_txt, freqs_txt, 0), (self.img, x_img, freqs_img, Nt)):
             m = st.modulation(vec)
             mods.append(m)
-            h = fused_rms_norm_modulate(x, st.norm_w[0], m[0].contiguous(), cfg.eps)
-            qkv = linear_bf16(h, st.qkv)
-            q, k, v = fused_qkv_postprocess(qkv, st.q_norm, st.k_norm, fr, cfg.heads, HEAD_DIM, cfg.eps)
-            qs.append(q)
-            ks.append(k)
-            vs.append(v)
-        o = joint_attention(torch.cat(qs, dim=2), torch.cat(ks, dim=2), torch.cat(vs, dim=2), cfg)
+            # norm + 1 x 128 quant in one pass, straight into the QKV GEMM
+            h8, h_s = fused_rms_norm_modulate_quant(x, st.norm_w[0], m[0].contiguous(), cfg.eps)
+            qkv = gemm_bf16(h8, h_s, st.qkv)
+            qkv_postprocess_into(qkv, st.q_norm, st.k_norm, fr, q, k, v, off, cfg.eps)
+        o = joint_attention(q, k, v, cfg)
         o_txt, o_img = o.split([x_txt.shape[1], x_img.shape[1]], dim=1)
         outs = []
         for st, x, o_s, m in ((self.txt, x_txt, o_txt, mods[0]), (self.img, x_img, o_img, mods[1])):
             a = linear_bf16(o_s.contiguous(), st.proj)
             x = fused_rms_norm_gate_residual(a, st.norm_w[1], m[1].contiguous(), x, cfg.eps)
-            h = fused_rms_norm_modulate(x, st.norm_w[2], m[2].contiguous(), cfg.eps)
-            f = mlp_fp8(h, st.mlp_in, st.mlp_out)
+            h8, h_s = fused_rms_norm_modulate_quant(x, st.norm_w[2], m[2].contiguous(), cfg.eps)
+            f = mlp_fp8_q(h8, h_s, st.mlp_in, st.mlp_out)
             x = fused_rms_norm_gate_residual(f, st.norm_w[3], m[3].contiguous(), x, cfg.eps)
             outs.append(x)
         return outs[0], outs[1]
@@ -223,8 +245,7 @@ class SingleStreamBlock(nn.Module):
         cfg = self.cfg
         B, N, D = x.shape
         scale, gate = self.adaln(torch.nn.functional.silu(vec)).chunk(2, dim=-1)
-        h = fused_rms_norm_modulate(x, self.norm_w[0], scale.contiguous(), cfg.eps)
-        a8, a_s = fp8_act_quant(h)
+        a8, a_s = fused_rms_norm_modulate_quant(x, self.norm_w[0], scale.contiguous(), cfg.eps)
         w, ws = self.linear1.weight, self.linear1.weight_scale
         n_qkv = 3 * D
         qkv = fp8_gemm_blockwise(a8, a_s, w[:n_qkv], ws[: n_qkv // 128], output_dtype=torch.bfloat16)

@@ -36,6 +36,44 @@ def _fused_rms_norm_modulate_cuda(x, weight, scale, eps=1e-5):
     return out
 
 
+def fused_rms_norm_modulate_quant(x, weight, scale, eps=1e-5):
+    """``fp8_act_quant(fused_rms_norm_modulate(x, weight, scale, eps))`` in one pass.
+
+    Returns e4m3 codes (B, seq, dim) and fp32 dequant scales (B, seq, dim / 128),
+    code for code equal to the two-kernel path, without the bf16 intermediate.
+    (No single reference op: the reference runs the norm and the quantiser
+    separately, fused_kernels.py:43-86 and fp8_kernels.py:54-90.)
+    """
+    assert x.ndim == 3, f"Expected x to be 3D (B, seq, dim), got {x.ndim}D"
+    assert x.is_contiguous() and weight.is_contiguous() and scale.is_contiguous()
+    B, seq_len, dim = x.shape
+    assert weight.shape == (dim,) and scale.shape == (B, dim)
+    assert x.dtype == torch.bfloat16, "x must be bf16"
+    assert dim % 128 == 0, "dim must be a multiple of 128"
+    L.require_cuda(x, weight, scale)
+    y = torch.empty(B, seq_len, dim, dtype=torch.float8_e4m3fn, device=x.device)
+    y_s = torch.empty(B, seq_len, dim // 128, dtype=torch.float32, device=x.device)
+    L.call("fd_rms_norm_modulate_quant", L.ptr(x), L.ptr(weight), L.dtype_code(weight.dtype), L.ptr(scale),
+           L.dtype_code(scale.dtype), L.ptr(y), L.ptr(y_s), B, seq_len, dim, float(eps), L.stream_ptr(x.device))
+    return y, y_s
+
+
+def qkv_postprocess_into(qkv, q_norm_weight, k_norm_weight, freqs_cis, q_out, k_out, v_out, seq_offset,
+                         norm_eps=1e-5):
+    """``fused_qkv_postprocess`` writing rows [seq_offset, seq_offset + S) of
+    preallocated (B, H, S_total, 128) outputs (the streams of a joint attention
+    share one buffer).  ``freqs_cis`` is (B, S, 64, 2, 2) fp32 contiguous."""
+    B, S, three_dim = qkv.shape
+    _, H, S_total, hd = q_out.shape
+    assert hd == 128 and three_dim == 3 * H * hd
+    assert qkv.is_contiguous() and q_out.is_contiguous() and k_out.is_contiguous() and v_out.is_contiguous()
+    assert freqs_cis.dtype == torch.float32 and freqs_cis.is_contiguous()
+    L.require_cuda(qkv, q_out)
+    L.call("fd_qkv_postprocess_into", L.ptr(qkv), L.ptr(q_norm_weight.float().contiguous()),
+           L.ptr(k_norm_weight.float().contiguous()), L.ptr(freqs_cis), L.ptr(q_out), L.ptr(k_out), L.ptr(v_out),
+           B, S, H, hd, float(norm_eps), S_total, seq_offset, L.stream_ptr(qkv.device))
+
+
 def _fused_rms_norm_gate_residual_cuda(x, weight, gate, residual, eps=1e-5):
     assert x.ndim == 3, f"Expected x to be 3D (B, seq, dim), got {x.ndim}D"
     assert x.is_contiguous(), "Input x must be contiguous"

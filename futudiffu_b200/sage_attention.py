@@ -150,8 +150,9 @@ def _normalize_mask(block_mask: Tensor | None, N: int) -> tuple[Tensor | None, i
 
 def _attn_forward(
     q: Tensor, k: Tensor, v: Tensor, sm_scale: float | None, *, block_mask: Tensor | None,
-    qk_quant: str, pv_quant: str, granularity: str, want_lse: bool,
+    qk_quant: str, pv_quant: str, granularity: str, want_lse: bool, out_bnhd: bool = False,
 ) -> tuple[Tensor, Tensor | None]:
+    """(B, H, N, 128) bf16 -> out (B, H, N, 128), or (B, N, H * 128) when ``out_bnhd``."""
     B, H, N, D = q.shape
     assert D == 128, f"SageAttention currently requires head_dim=128, got {D}"
     assert q.dtype == torch.bfloat16, f"Expected BF16 input, got {q.dtype}"
@@ -165,14 +166,16 @@ def _attn_forward(
     bm, bm_stride = _normalize_mask(block_mask, N)
     qz = quantize_qkv(qf, kf, vf, sm_scale, smooth_k=_SAGE_SMOOTH_K, qk_quant=qk_quant,
                       granularity=granularity, pv_quant=pv_quant)
-    out = torch.empty_like(qf)
+    out = torch.empty(B, N, H * D, dtype=q.dtype, device=q.device) if out_bnhd else torch.empty_like(qf)
     lse = torch.empty(BH, N, dtype=torch.float32, device=q.device) if want_lse else None
     vsrc = qz["v_codes"] if qz["pv"] == L.PV_FP8 else vf
-    L.call(
-        "fd_sage_attn_fwd", L.ptr(qz["q_codes"]), L.ptr(qz["q_desc"]), L.ptr(qz["k_codes"]),
-        L.ptr(qz["k_desc"]), L.ptr(vsrc), L.ptr(qz["v_desc"]), L.ptr(bm), bm_stride, L.ptr(out),
-        L.ptr(lse), BH, N, qz["qk"], qz["gran"], qz["gran"], qz["pv"], L.stream_ptr(q.device),
-    )
+    common = (L.ptr(qz["q_codes"]), L.ptr(qz["q_desc"]), L.ptr(qz["k_codes"]), L.ptr(qz["k_desc"]),
+              L.ptr(vsrc), L.ptr(qz["v_desc"]), L.ptr(bm), bm_stride, L.ptr(out), L.ptr(lse), BH, N)
+    kinds = (qz["qk"], qz["gran"], qz["gran"], qz["pv"], L.stream_ptr(q.device))
+    if out_bnhd:
+        L.call("fd_sage_attn_fwd_bnhd", *common, H, *kinds)
+        return out, lse
+    L.call("fd_sage_attn_fwd", *common, *kinds)
     return out.reshape(B, H, N, D), lse
 
 

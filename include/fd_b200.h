@@ -145,6 +145,16 @@ int fd_rms_norm_modulate(const void* x, const void* w, int w_dtype, const void* 
 
 /* P2 -- fused_rms_norm_gate_residual (src/futudiffu/fused_kernels.py:99-148, :200-247).
  * out = residual + tanh(gate[b]) * rmsnorm(x) * w. */
+/* RMSNorm-modulate (as fd_rms_norm_modulate) with the 1 x 128 e4m3 activation
+ * quantiser fused into the same pass: y (B, S, dim) e4m3 codes, y_s (B, S, dim/128)
+ * fp32 dequant scales, equal to fd_rms_norm_modulate followed by fd_fp8_act_quant
+ * code for code.  No single counterpart in the reference (it runs the pair
+ * fused_rms_norm_modulate -> fp8_act_quant, fused_kernels.py:43-86 and
+ * fp8_kernels.py:54-90); dim a multiple of 128. */
+int fd_rms_norm_modulate_quant(const void* x, const void* w, int w_dtype, const void* scale,
+                               int scale_dtype, void* y, float* y_s, int64_t B, int64_t S,
+                               int64_t dim, float eps, void* stream);
+
 int fd_rms_norm_gate_residual(const void* x, const void* w, int w_dtype, const void* gate,
                               int gate_dtype, const void* residual, void* out, int64_t B,
                               int64_t S, int64_t dim, float eps, void* stream);
@@ -155,6 +165,12 @@ int fd_rms_norm_gate_residual(const void* x, const void* w, int w_dtype, const v
 int fd_qkv_postprocess(const void* qkv, const float* qw, const float* kw, const float* freqs,
                        void* oq, void* ok, void* ov, int64_t B, int64_t S, int64_t H, int64_t hd,
                        float eps, void* stream);
+/* fd_qkv_postprocess writing Q, K, V rows [s_off, s_off + S) of (B, H, S_out, 128)
+ * buffers, so the streams of a joint attention land in one buffer without a copy.
+ * No counterpart in the reference. */
+int fd_qkv_postprocess_into(const void* qkv, const float* qw, const float* kw, const float* freqs,
+                            void* oq, void* ok, void* ov, int64_t B, int64_t S, int64_t H,
+                            int64_t hd, float eps, int64_t S_out, int64_t s_off, void* stream);
 
 /* A1..A4 -- attention quantisation prologue.
  * Replaces _smooth_k (src/futudiffu/sage_attention.py:63-71) and the in-kernel
@@ -211,6 +227,14 @@ int fd_sage_attn_fwd(const void* q_codes, const float* q_desc, const void* k_cod
                      const uint8_t* block_mask, int64_t mask_bh_stride, void* out, float* lse,
                      int64_t BH, int64_t N, int qk_kind, int q_gran, int k_gran, int pv_kind,
                      void* stream);
+/* fd_sage_attn_fwd with out laid out (BH / H, N, H, 128), i.e. (B, N, H * 128): the
+ * input layout of the output projection, so no transpose follows the kernel.
+ * No counterpart in the reference. */
+int fd_sage_attn_fwd_bnhd(const void* q_codes, const float* q_desc, const void* k_codes,
+                          const float* k_desc, const void* v, const float* v_desc,
+                          const uint8_t* block_mask, int64_t mask_bh_stride, void* out, float* lse,
+                          int64_t BH, int64_t N, int64_t H, int qk_kind, int q_gran, int k_gran,
+                          int pv_kind, void* stream);
 
 /* A7 -- attention backward, Delta pre-pass (sage_kernels.py:322-349):
  * delta (BH, N) f32 = rowsum(dO * O). */

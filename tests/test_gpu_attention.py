@@ -285,3 +285,19 @@ def test_sage_op_autograd(cuda_device):
     # reference test threshold: backward vs SDPA cosine > 0.95 (test_sage_backward.py:91-93)
     for a, b in ((q.grad, qr.grad), (k.grad, kr.grad), (v.grad, vr.grad)):
         assert cosine(a, b) > 0.95
+
+
+def test_attention_bnhd_output_layout(cuda_device):
+    """The (B, N, H*128) output layout holds exactly the transposed (B, H, N, 128) result."""
+    from futudiffu_b200.sage_attention import _attn_forward
+
+    g = gen(91)
+    B, H, N = 2, 3, 300
+    q, k, v = (torch.randn(B, H, N, 128, generator=g).to(torch.bfloat16).to(cuda_device) for _ in range(3))
+    for qk, pv, gran in (("int8", "fp8", "per_block"), ("int8", "bf16", "per_token"), ("fp8", "bf16", "per_token")):
+        a, _ = _attn_forward(q, k, v, None, block_mask=None, qk_quant=qk, pv_quant=pv, granularity=gran,
+                             want_lse=False)
+        b, _ = _attn_forward(q, k, v, None, block_mask=None, qk_quant=qk, pv_quant=pv, granularity=gran,
+                             want_lse=False, out_bnhd=True)
+        assert b.shape == (B, N, H * 128)
+        assert torch.equal(b.cpu(), a.transpose(1, 2).reshape(B, N, H * 128).cpu())

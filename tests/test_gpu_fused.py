@@ -106,3 +106,46 @@ def test_fused_backward_runs(cuda_device):
     ref_x = x.detach().float().requires_grad_(True)
     (ref_x * torch.rsqrt((ref_x * ref_x).mean(-1, keepdim=True) + 1e-5)).sum().backward()
     assert torch.allclose(x.grad.float(), ref_x.grad, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("B,S,dim,wdt", [(1, 1, 128, torch.bfloat16), (2, 37, 384, torch.float32),
+                                         (1, 4608, 3072, torch.bfloat16), (3, 5, 5120, torch.bfloat16)])
+def test_rms_norm_modulate_quant(cuda_device, B, S, dim, wdt):
+    """Norm + 1 x 128 quant in one pass equals the norm followed by the quantiser, code for code."""
+    from futudiffu_b200.fp8_kernels import fp8_act_quant
+    from futudiffu_b200.fused_kernels import fused_rms_norm_modulate, fused_rms_norm_modulate_quant
+
+    g = gen(B * S + dim)
+    x = (torch.randn(B, S, dim, generator=g) * 3).to(torch.bfloat16).to(cuda_device)
+    w = (1 + 0.1 * torch.randn(dim, generator=g)).to(wdt).to(cuda_device)
+    sc = (0.2 * torch.randn(B, dim, generator=g)).to(torch.bfloat16).to(cuda_device)
+    y8, ys = fused_rms_norm_modulate_quant(x, w, sc)
+    r8, rs = fp8_act_quant(fused_rms_norm_modulate(x, w, sc))
+    assert y8.shape == (B, S, dim) and ys.shape == (B, S, dim // 128)
+    assert torch.equal(y8.view(torch.uint8).cpu(), r8.view(torch.uint8).cpu())
+    assert torch.equal(ys.cpu(), rs.reshape(B, S, dim // 128).cpu())
+
+
+def test_qkv_postprocess_into_joint_buffer(cuda_device):
+    """Writing two streams into one joint buffer equals concatenating their outputs."""
+    from futudiffu_b200.fused_kernels import fused_qkv_postprocess, qkv_postprocess_into
+
+    B, H = 2, 3
+    g = gen(77)
+    parts = []
+    for S in (5, 131):
+        qkv = torch.randn(B, S, 3 * H * 128, generator=g).to(torch.bfloat16).to(cuda_device)
+        fr = torch.randn(B, S, 64, 2, 2, generator=g).to(cuda_device)
+        parts.append((qkv, fr))
+    qw = (1 + 0.1 * torch.randn(128, generator=g)).to(cuda_device)
+    kw = (1 + 0.1 * torch.randn(128, generator=g)).to(cuda_device)
+    N = 5 + 131
+    q, k, v = (torch.empty(B, H, N, 128, dtype=torch.bfloat16, device=cuda_device) for _ in range(3))
+    off = 0
+    refs = []
+    for qkv, fr in parts:
+        qkv_postprocess_into(qkv, qw, kw, fr, q, k, v, off)
+        refs.append(fused_qkv_postprocess(qkv, qw, kw, fr, H, 128))
+        off += qkv.shape[1]
+    for i, t in enumerate((q, k, v)):
+        assert torch.equal(t.cpu(), torch.cat([r[i] for r in refs], dim=2).cpu())
