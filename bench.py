@@ -536,6 +536,100 @@ def run_dit(args, world, rank, local):
     return 0
 
 
+# ------------------------------------------------------------------ config 5: video DiT, Ulysses
+VIDEO_METRIC = "video DiT denoise steps/s (14B-class, 40 blocks, 32760 video + 512 text tokens, Ulysses)"
+
+
+def run_video(args, world, rank, local):
+    import torch.distributed as dist
+
+    from futudiffu_b200 import check_status
+    from futudiffu_b200.dit import VideoDiT, VideoDiTConfig, sigmas, video_flops_per_step
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = VideoDiTConfig()
+    model = VideoDiT(cfg, seed=0, device=dev, group=None)
+    Ls = model.local_tokens
+    g = torch.Generator().manual_seed(200)  # the whole sample, sliced per rank
+    lat = torch.randn(1, cfg.tokens, cfg.patch_dim, generator=g).to(torch.bfloat16)
+    txt = torch.randn(1, cfg.txt_tokens, cfg.hidden, generator=g).to(torch.bfloat16).to(dev)
+    x = lat[:, rank * Ls:(rank + 1) * Ls].contiguous().to(dev)
+    sig = sigmas(28)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i, x):
+        t = torch.full((1,), sig[i % 28], device=dev)
+        v = model(x, txt, t)
+        return (x.float() + (sig[i % 28 + 1] - sig[i % 28]) * v.float()).to(x.dtype)
+
+    for i in range(args.warmup):
+        x = step(i, x)
+    torch.cuda.synchronize()
+    check_status()
+    rec = LaunchRecorder()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else local) as clocks:
+        rec.active = True
+        start.record(stream)
+        for i in range(args.steps):
+            x = step(i, x)
+        end.record(stream)
+        rec.active = False
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_local = start.elapsed_time(end) / args.steps
+    ms = max_over_ranks(ms_local, world, dev)
+    gemm_work, gemm_ms, _ = rec.summary("gemm")
+    attn_work, attn_ms, _ = rec.summary("attn")
+    launches = rec.launches
+    rec.close()
+    check_status()
+    # ---------------- end to end: host latent shard -> device -> step -> host
+    h_x = lat[:, rank * Ls:(rank + 1) * Ls].contiguous().pin_memory()
+    h_out = torch.empty_like(h_x).pin_memory()
+    step(0, h_x.to(dev, non_blocking=True))
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(2):
+        h_out.copy_(step(i, h_x.to(dev, non_blocking=True)), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / 2, world, dev)
+    if rank == 0:
+        pk = peaks()
+        peak = 2.0 * pk["bf16_tflops_sustained"]
+        gemm_tf = gemm_work / (gemm_ms * 1e-3) / 1e12
+        fl = video_flops_per_step(cfg)
+        print(json.dumps({
+            "metric": VIDEO_METRIC, "value": 1e3 / ms, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp8/int8", "data": "synthetic (random-init weights, N(0,1) latents/text)",
+            "config": {"workload": "config5_video_dit_ulysses", "tokens": cfg.tokens, "text_tokens": cfg.txt_tokens,
+                       "hidden": cfg.hidden, "heads": cfg.heads, "ffn": cfg.ffn, "blocks": cfg.n_blocks,
+                       "parallelism": f"Ulysses sequence parallel x{world} (NCCL all_to_all_single)",
+                       "model_pflop_per_step": fl / 1e15, "model_tflops": fl / (ms * 1e-3) / 1e12,
+                       "attention_kernel_tops_per_gpu": attn_work / (attn_ms * 1e-3) / 1e12 if attn_ms else None,
+                       "time_share": {"gemm": gemm_ms / args.steps / ms_local,
+                                      "attention": attn_ms / args.steps / ms_local},
+                       "cross_attention": "bf16 torch SDPA (512 text keys, <1% of FLOPs)",
+                       "l2": "weights 14 GB, activations >> L2"},
+            "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": peak, "unit": "TFLOP/s",
+                         "frac": gemm_tf / peak, "traffic": None, "kernel": "gemm_fp8_kernel (flop-weighted, rank 0)",
+                         "peak_source": f"2 x {pk['source']} sustained bf16 dense ({pk['bf16_tflops_sustained']} TF/s)"},
+            "cpu_baseline": None,
+            "e2e": {"value": 1e3 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h_x.numel() * 2 * world,
+                    "d2h_bytes_per_step": h_x.numel() * 2 * world, "ms_per_step": e2e_ms,
+                    "api": "futudiffu_b200.dit.VideoDiT"},
+            "gpu_launches": launches, "clocks": clocks.summary(),
+        }), flush=True)
+    return 0
+
+
 GEMM_SHAPES = {"config1": (2048, 3072, 3072), "ref_qkv": (8576, 11520, 3840), "ref_w2": (8576, 3840, 10240)}
 
 
@@ -602,8 +696,9 @@ def main(argv=None) -> int:
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default: 10 dit, 50 otherwise)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["dit", "attention", "gemm"], default="dit",
-                    help="dit = BASELINE config 4 (headline); attention = config 2; gemm = config 1")
+    ap.add_argument("--workload", choices=["dit", "video", "attention", "gemm"], default="dit",
+                    help="dit = BASELINE config 4 (headline); video = config 5 (Ulysses); "
+                         "attention = config 2; gemm = config 1")
     ap.add_argument("--gemm-shape", choices=sorted(GEMM_SHAPES), default="config1")
     ap.add_argument("--profile", action="store_true",
                     help="dit: bracket the first timed step with cudaProfilerStart/Stop "
@@ -611,13 +706,20 @@ def main(argv=None) -> int:
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
     if args.steps is None:
-        args.steps = 10 if args.workload == "dit" else 50
+        args.steps = {"dit": 10, "video": 3}.get(args.workload, 50)
     world, rank, local = dist_setup()
     try:
         if args.workload == "dit":
             if args.impl == "reference":
                 return run_dit_reference(args, world, rank)
             return run_dit(args, world, rank, local)
+        if args.workload == "video":
+            if args.impl == "reference":
+                if rank == 0:
+                    print(json.dumps({"impl": "reference", "unavailable": "config 5 has no CPU reference arm: "
+                                      "a 1.7 PFLOP step; see the dit workload's CPU baseline"}), flush=True)
+                return 0
+            return run_video(args, world, rank, local)
         if args.impl == "reference":
             return run_reference(args, world, rank)
         if args.workload == "gemm":

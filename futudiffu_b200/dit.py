@@ -348,3 +348,153 @@ def flops_per_sample_step(cfg: DiTConfig) -> float:
     lin_single = 2 * ((3 + R) * D * D + (1 + R) * D * D) * N
     attn = 4 * N * N * D
     return cfg.n_double * (lin_double + attn) + cfg.n_single * (lin_single + attn)
+
+
+# ------------------------------------------------------------------ video DiT (Ulysses)
+@dataclass
+class VideoDiTConfig:
+    hidden: int = 5120
+    heads: int = 40
+    ffn: int = 13824
+    n_blocks: int = 40
+    grid: tuple[int, int, int] = (21, 30, 52)   # latent frames x patch rows x patch cols
+    patch_dim: int = 64                         # 16 latent channels x 1 x 2 x 2
+    txt_tokens: int = 512
+    time_dim: int = 256
+    rope_axes: tuple[int, int, int] = (44, 42, 42)
+    rope_theta: float = 10000.0
+    eps: float = 1e-5
+    qk_quant: str = "int8"
+    pv_quant: str = "fp8"
+    granularity: str = "per_block"
+
+    @property
+    def tokens(self) -> int:
+        t, h, w = self.grid
+        return t * h * w
+
+
+def video_freqs(cfg: VideoDiTConfig, device, start: int = 0, count: int | None = None) -> Tensor:
+    """3-D RoPE rotations of video tokens [start, start + count) of the (t, h, w)
+    grid, (count, head_dim/2, 2, 2) fp32."""
+    t, h, w = cfg.grid
+    count = cfg.tokens - start if count is None else count
+    idx = torch.arange(start, start + count, device=device)
+    pos = (idx // (h * w), (idx // w) % h, idx % w)
+    parts = [rope_embed(p, d, cfg.rope_theta) for p, d in zip(pos, cfg.rope_axes)]
+    return torch.cat(parts, dim=-3).contiguous()
+
+
+class VideoBlock(nn.Module):
+    """Video DiT block: self-attention over the (sequence-sharded) video tokens,
+    cross-attention to the text tokens, GELU(tanh) FFN; every linear FP8."""
+
+    def __init__(self, cfg: VideoDiTConfig, gen, device):
+        super().__init__()
+        self.cfg = cfg
+        D = cfg.hidden
+        self.adaln = nn.Linear(D, 4 * D, device=device, dtype=torch.bfloat16)
+        with torch.no_grad():
+            self.adaln.weight.copy_(_rand((4 * D, D), gen, device, 0.02))
+            self.adaln.bias.copy_(_rand((4 * D,), gen, device, 0.02))
+        self.norm_w = nn.ParameterList(
+            [nn.Parameter(_rand((D,), gen, device, 0.05, 1.0), requires_grad=False) for _ in range(6)])
+        self.cross_gate = nn.Parameter(_rand((1, D), gen, device, 0.5), requires_grad=False)
+        self.q_norm = nn.Parameter(_rand((HEAD_DIM,), gen, device, 0.05, 1.0), requires_grad=False)
+        self.k_norm = nn.Parameter(_rand((HEAD_DIM,), gen, device, 0.05, 1.0), requires_grad=False)
+        self.qkv = random_fp8_linear(3 * D, D, gen, device)
+        self.proj = random_fp8_linear(D, D, gen, device)
+        self.cq = random_fp8_linear(D, D, gen, device)
+        self.ckv = random_fp8_linear(2 * D, D, gen, device)
+        self.co = random_fp8_linear(D, D, gen, device)
+        self.ffn_in = random_fp8_linear(cfg.ffn, D, gen, device)
+        self.ffn_out = random_fp8_linear(D, cfg.ffn, gen, device)
+
+    def forward(self, x: Tensor, vec: Tensor, txt: Tensor, freqs: Tensor, group=None) -> Tensor:
+        """x (1, L/P, D) bf16: this rank's tokens; vec (1, D); txt (1, 512, D); freqs (1, L/P, 64, 2, 2)."""
+        from .ulysses import ulysses_attention
+
+        cfg = self.cfg
+        _, Ls, D = x.shape
+        H = cfg.heads
+        m = [c.contiguous() for c in self.adaln(torch.nn.functional.silu(vec)).chunk(4, dim=-1)]
+        # ---- self-attention (Ulysses: sequence -> head all-to-all around the kernel)
+        h8, h_s = fused_rms_norm_modulate_quant(x, self.norm_w[0], m[0], cfg.eps)
+        qkv = gemm_bf16(h8, h_s, self.qkv)
+        q, k, v = fused_qkv_postprocess(qkv, self.q_norm, self.k_norm, freqs, H, HEAD_DIM, cfg.eps)
+
+        def attn(qh, kh, vh):
+            o, _ = _attn_forward(qh, kh, vh, None, block_mask=None, qk_quant=cfg.qk_quant,
+                                 pv_quant=cfg.pv_quant, granularity=cfg.granularity, want_lse=False)
+            return o
+
+        o = ulysses_attention(q[0], k[0], v[0], attn, group)            # (L/P, D)
+        a = linear_bf16(o.unsqueeze(0), self.proj)
+        x = fused_rms_norm_gate_residual(a, self.norm_w[1], m[1], x, cfg.eps)
+        # ---- cross-attention to the text (replicated on every rank; 512 keys, bf16 SDPA)
+        zero = torch.zeros_like(m[0])
+        c8, c_s = fused_rms_norm_modulate_quant(x, self.norm_w[2], zero, cfg.eps)
+        qc = gemm_bf16(c8, c_s, self.cq).view(1, Ls, H, HEAD_DIM).transpose(1, 2)
+        kv = linear_bf16(txt, self.ckv).view(1, -1, 2, H, HEAD_DIM)
+        kc, vc = kv[:, :, 0].transpose(1, 2), kv[:, :, 1].transpose(1, 2)
+        oc = torch.nn.functional.scaled_dot_product_attention(qc, kc, vc)
+        ac = linear_bf16(oc.transpose(1, 2).reshape(1, Ls, D).contiguous(), self.co)
+        x = fused_rms_norm_gate_residual(ac, self.norm_w[3], self.cross_gate.expand(1, D).contiguous(), x, cfg.eps)
+        # ---- FFN
+        f8, f_s = fused_rms_norm_modulate_quant(x, self.norm_w[4], m[2], cfg.eps)
+        f = mlp_fp8_q(f8, f_s, self.ffn_in, self.ffn_out)
+        return fused_rms_norm_gate_residual(f, self.norm_w[5], m[3], x, cfg.eps)
+
+
+class VideoDiT(nn.Module):
+    """14B-class video DiT, sequence-parallel over a process group (Ulysses)."""
+
+    def __init__(self, cfg: VideoDiTConfig, seed: int = 0, device="cuda", group=None):
+        super().__init__()
+        import torch.distributed as dist
+
+        self.cfg = cfg
+        self.group = group
+        dev = torch.device(device)
+        gen = torch.Generator(device=dev).manual_seed(seed)   # identical weights on every rank
+        D = cfg.hidden
+        if D != HEAD_DIM * cfg.heads:
+            raise ValueError(f"hidden {D} must equal heads x {HEAD_DIM}")
+        P = dist.get_world_size(group) if dist.is_initialized() else 1
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if cfg.tokens % P or cfg.heads % P:
+            raise ValueError(f"{cfg.tokens} tokens / {cfg.heads} heads do not split over {P} ranks")
+        self.P, self.rank = P, rank
+        self.local_tokens = cfg.tokens // P
+        self.img_in = nn.Linear(cfg.patch_dim, D, device=dev, dtype=torch.bfloat16)
+        self.time_in1 = nn.Linear(cfg.time_dim, D, device=dev, dtype=torch.bfloat16)
+        self.time_in2 = nn.Linear(D, D, device=dev, dtype=torch.bfloat16)
+        self.final_adaln = nn.Linear(D, D, device=dev, dtype=torch.bfloat16)
+        self.final_out = nn.Linear(D, cfg.patch_dim, device=dev, dtype=torch.bfloat16)
+        with torch.no_grad():
+            for lin in (self.img_in, self.time_in1, self.time_in2, self.final_adaln, self.final_out):
+                lin.weight.copy_(_rand(tuple(lin.weight.shape), gen, dev, 0.02))
+                lin.bias.zero_()
+        self.final_norm = nn.Parameter(_rand((D,), gen, dev, 0.05, 1.0), requires_grad=False)
+        self.blocks = nn.ModuleList([VideoBlock(cfg, gen, dev) for _ in range(cfg.n_blocks)])
+        f = video_freqs(cfg, dev, rank * self.local_tokens, self.local_tokens)
+        self.register_buffer("freqs_local", f.unsqueeze(0).contiguous(), persistent=False)
+
+    @torch.no_grad()
+    def forward(self, x_local: Tensor, txt: Tensor, t: Tensor) -> Tensor:
+        """x_local (1, L/P, patch_dim): this rank's latent tokens; txt (1, 512, D); t (1,)."""
+        cfg = self.cfg
+        vec = self.time_in2(torch.nn.functional.silu(self.time_in1(
+            timestep_embedding(t, cfg.time_dim).to(torch.bfloat16))))
+        x = self.img_in(x_local).contiguous()
+        for blk in self.blocks:
+            x = blk(x, vec, txt, self.freqs_local, self.group)
+        scale = self.final_adaln(torch.nn.functional.silu(vec)).contiguous()
+        return self.final_out(fused_rms_norm_modulate(x, self.final_norm, scale, cfg.eps))
+
+
+def video_flops_per_step(cfg: VideoDiTConfig) -> float:
+    """Algorithmic FLOPs of one forward (one sample): linears, self- and cross-attention."""
+    D, F, L, T = cfg.hidden, cfg.ffn, cfg.tokens, cfg.txt_tokens
+    lin = 2 * L * (4 * D * D + 2 * D * D + 2 * D * F) + 2 * T * 2 * D * D
+    return cfg.n_blocks * (lin + 4 * L * L * D + 4 * L * T * D)

@@ -154,3 +154,27 @@ def random_double_block(cfg, seed: int = 0):
             mlp_in=fp8_linear(R * D, D), mlp_out=fp8_linear(D, R * D))
 
     return SimpleNamespace(cfg=cfg, txt=stream(), img=stream())
+
+
+def video_block(blk, x, vec, txt, freqs):
+    """futudiffu_b200.dit.VideoBlock on the CPU, single rank (the whole sequence)."""
+    cfg = blk.cfg
+    x, vec, txt = _cpu(x), _cpu(vec), _cpu(txt)
+    _, L, D = x.shape
+    H = cfg.heads
+    m = _torch_linear(torch.nn.functional.silu(vec.float()).to(torch.bfloat16), blk.adaln).chunk(4, dim=-1)
+    h = OF.rms_norm_modulate(x, _cpu(blk.norm_w[0]), m[0], cfg.eps)
+    qkv = linear(h, blk.qkv)
+    q, k, v = OF.qkv_postprocess(qkv, _cpu(blk.q_norm), _cpu(blk.k_norm), _cpu(freqs), H, 128, cfg.eps)
+    o = attention(q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16), cfg)
+    x = OF.rms_norm_gate_residual(linear(o, blk.proj), _cpu(blk.norm_w[1]), m[1], x, cfg.eps)
+    hc = OF.rms_norm_modulate(x, _cpu(blk.norm_w[2]), torch.zeros_like(m[0]), cfg.eps)
+    qc = linear(hc, blk.cq).view(1, L, H, 128).transpose(1, 2).float()
+    kv = linear(txt, blk.ckv).view(1, -1, 2, H, 128).float()
+    kc, vc = kv[:, :, 0].transpose(1, 2), kv[:, :, 1].transpose(1, 2)
+    oc = torch.nn.functional.scaled_dot_product_attention(qc, kc, vc).to(torch.bfloat16)
+    ac = linear(oc.transpose(1, 2).reshape(1, L, D), blk.co)
+    x = OF.rms_norm_gate_residual(ac, _cpu(blk.norm_w[3]), _cpu(blk.cross_gate), x, cfg.eps)
+    hf = OF.rms_norm_modulate(x, _cpu(blk.norm_w[4]), m[2], cfg.eps)
+    f = mlp(hf, blk.ffn_in, blk.ffn_out)
+    return OF.rms_norm_gate_residual(f, _cpu(blk.norm_w[5]), m[3], x, cfg.eps)

@@ -92,3 +92,37 @@ def test_dit_forward_and_euler(cuda_device):
     _close(v, OD.dit_forward(model, img, txt, t), cos_min=0.995)
     x1 = euler_step(model, img.to(cuda_device), txt.to(cuda_device), 1.0, 0.5)
     assert torch.isfinite(x1.float()).all() and x1.shape == img.shape
+
+
+def test_video_block_single_rank(cuda_device):
+    """Video DiT block (Ulysses path at P = 1) against the CPU composition of the oracle ops."""
+    from futudiffu_b200.dit import VideoBlock, VideoDiTConfig, video_freqs
+
+    cfg = VideoDiTConfig(hidden=256, heads=2, ffn=512, n_blocks=1, grid=(2, 4, 24), txt_tokens=64,
+                         rope_axes=(44, 42, 42))
+    g = torch.Generator(device=cuda_device).manual_seed(9)
+    blk = VideoBlock(cfg, g, cuda_device)
+    cg = gen(10)
+    L = cfg.tokens
+    x = torch.randn(1, L, cfg.hidden, generator=cg).to(torch.bfloat16)
+    vec = torch.randn(1, cfg.hidden, generator=cg).to(torch.bfloat16)
+    txt = torch.randn(1, cfg.txt_tokens, cfg.hidden, generator=cg).to(torch.bfloat16)
+    fr = video_freqs(cfg, cuda_device).unsqueeze(0).contiguous()
+    with torch.no_grad():
+        o = blk(x.to(cuda_device), vec.to(cuda_device), txt.to(cuda_device), fr)
+        r = OD.video_block(blk, x, vec, txt, fr)
+    _close(o, r)
+
+
+def test_video_dit_forward(cuda_device):
+    from futudiffu_b200.dit import VideoDiT, VideoDiTConfig
+
+    cfg = VideoDiTConfig(hidden=256, heads=2, ffn=512, n_blocks=2, grid=(2, 4, 8), txt_tokens=32)
+    model = VideoDiT(cfg, seed=3, device=cuda_device)
+    cg = gen(11)
+    x = torch.randn(1, cfg.tokens, cfg.patch_dim, generator=cg).to(torch.bfloat16).to(cuda_device)
+    txt = torch.randn(1, cfg.txt_tokens, cfg.hidden, generator=cg).to(torch.bfloat16).to(cuda_device)
+    v1 = model(x, txt, torch.tensor([0.5], device=cuda_device))
+    v2 = model(x, txt, torch.tensor([0.5], device=cuda_device))
+    assert v1.shape == (1, cfg.tokens, cfg.patch_dim) and torch.isfinite(v1.float()).all()
+    assert torch.equal(v1, v2)

@@ -1,0 +1,66 @@
+"""Ulysses sequence parallelism on CPU: world_size 2 over gloo, exact attention
+as the per-rank kernel; the sharded result must equal full attention."""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _exact(q, k, v):
+    s = torch.einsum("bhqd,bhkd->bhqk", q.float(), k.float()) / q.shape[-1] ** 0.5
+    return torch.einsum("bhqk,bhkd->bhqd", s.softmax(-1), v.float())
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, H, L, D, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from futudiffu_b200.ulysses import head_to_seq, seq_to_head, ulysses_attention
+
+        g = torch.Generator().manual_seed(0)
+        q, k, v = (torch.randn(H, L, D, generator=g) for _ in range(3))
+        Ls = L // world
+        sl = slice(rank * Ls, (rank + 1) * Ls)
+        # the exchange itself: sequence -> head -> sequence is the identity
+        qh = seq_to_head(q[:, sl].contiguous())
+        assert torch.equal(qh, q[rank * H // world:(rank + 1) * H // world])
+        back = head_to_seq(qh)
+        assert torch.equal(back, q[:, sl].transpose(0, 1).reshape(Ls, H * D))
+        o = ulysses_attention(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), _exact)
+        ref = _exact(q[None], k[None], v[None])[0][:, sl].transpose(0, 1).reshape(Ls, H * D)
+        out[rank] = float((o - ref).abs().max())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,H,L", [(2, 4, 12), (2, 6, 10)])
+def test_ulysses_attention_world2(world, H, L):
+    ctx = mp.get_context("spawn")
+    mgr = ctx.Manager()
+    out = mgr.dict()
+    mp.start_processes(_worker, args=(world, _free_port(), H, L, 8, out), nprocs=world, join=True,
+                       start_method="spawn")
+    assert len(out) == world
+    assert max(out.values()) < 1e-5
+
+
+def test_ulysses_single_rank_is_plain_attention():
+    from futudiffu_b200.ulysses import ulysses_attention
+
+    g = torch.Generator().manual_seed(1)
+    q, k, v = (torch.randn(3, 7, 8, generator=g) for _ in range(3))
+    o = ulysses_attention(q, k, v, _exact)
+    assert torch.allclose(o, _exact(q[None], k[None], v[None])[0].transpose(0, 1).reshape(7, 24), atol=1e-6)
