@@ -41,9 +41,11 @@ B, H, S, D = 2, 24, 4096, 128
 OPS_PER_STEP = 4 * B * H * S * S * D  # 412.3 G ops (2 for QK^T + 2 for PV per MAC pair)
 METRIC = "SageAttn TOPS (B2 H24 S4096 D128, INT8 QK + FP8 PV)"
 UNIT = "TOPS"
-# Measured DRAM traffic of one attention launch at this workload, from
-# profiles/attn_fwd_config2.md (ncu dram__bytes_read.sum + dram__bytes_write.sum); None until captured.
-ATTN_TRAFFIC_BYTES = None
+# Measured DRAM traffic of one attention launch at this workload (ncu
+# dram__bytes_read.sum + dram__bytes_write.sum of attn_fwd_kernel): 75.6 + 16.1 MB.
+ATTN_TRAFFIC_BYTES = 91.7e6
+# Same for one GEMM launch at the reference QKV shape (M 8576, N 11520, K 3840).
+GEMM_TRAFFIC_BYTES = {"ref_qkv": 352.5e6}
 
 
 def peaks() -> dict:
@@ -683,7 +685,7 @@ def run_gemm(args, world, rank, local):
             "data": "synthetic",
             "config": {"workload": f"gemm_{args.gemm_shape}", "M": M, "N": N, "K": K, "l2": "flushed"},
             "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
-                         "frac": tf / peak, "traffic": None,
+                         "frac": tf / peak, "traffic": GEMM_TRAFFIC_BYTES.get(args.gemm_shape),
                          "peak_source": f"2 x {pk['source']} bf16 dense: fp8 dense rate is twice bf16"},
             "gpu_launches": args.steps, "clocks": clocks.summary(),
         }), flush=True)
