@@ -93,6 +93,51 @@ __global__ void __launch_bounds__(256) colstats_kernel(const __nv_bfloat16* __re
   }
 }
 
+// One CTA per head: reduces the per-chunk column partials into the final
+// smoothing mean (bf16-rounded, as torch's bf16 mean) and the V inverse scale,
+// once per head instead of once per quantisation CTA.  The partials are summed
+// in chunk order (loads batched, additions sequential), and the results go to
+// chunk 0's slot of the workspace, where quant_kernel reads them.
+__global__ void __launch_bounds__(128) colstats_final_kernel(float* __restrict__ ws_sum,
+                                                            float* __restrict__ ws_amax, int64_t N,
+                                                            int nchunks, int do_k, int do_v,
+                                                            float* __restrict__ k_mean,
+                                                            float* __restrict__ v_desc) {
+  const int64_t bh = blockIdx.x;
+  const int c = threadIdx.x;
+  const int64_t base = bh * nchunks * 128 + c;
+  if (do_k) {
+    float tot = 0.f;
+    int i = 0;
+    for (; i + 8 <= nchunks; i += 8) {
+      float t[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) t[u] = ws_sum[base + (int64_t)(i + u) * 128];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) tot += t[u];
+    }
+    for (; i < nchunks; ++i) tot += ws_sum[base + (int64_t)i * 128];
+    // torch bf16 mean: fp32 accumulate, times 1/N, round to bf16
+    const float mean = round_to_bf16(tot * (1.0f / (float)N));
+    ws_sum[base] = mean;
+    if (k_mean) k_mean[bh * 128 + c] = mean;
+  }
+  if (do_v) {
+    float am = 0.f;
+    int i = 0;
+    for (; i + 8 <= nchunks; i += 8) {
+      float t[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) t[u] = ws_amax[base + (int64_t)(i + u) * 128];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) am = fmaxf(am, t[u]);
+    }
+    for (; i < nchunks; ++i) am = fmaxf(am, ws_amax[base + (int64_t)i * 128]);
+    ws_amax[base] = div_full(448.0f, fmaxf(am, 1e-12f));
+    v_desc[bh * 128 + c] = div_full(am, 448.0f);
+  }
+}
+
 template <int QK>  // FD_QK_INT8 or FD_QK_FP8
 FD_DEV uint32_t quant_code(float x, float inv) {
   const float y = x * inv;
@@ -151,23 +196,10 @@ __global__ void __launch_bounds__(256) quant_kernel(
   __shared__ float sh_red2[2][8];
 
   if (threadIdx.x < 128 && which != 0) {
+    // final per-head statistics from colstats_final_kernel (chunk 0's slot)
     const int c = threadIdx.x;
-    if (which == 1 && smooth_k) {
-      float tot = 0.f;
-      for (int i = 0; i < nchunks; ++i) tot += ws_sum[(bh * nchunks + i) * 128 + c];
-      // torch bf16 mean: fp32 accumulate, times 1/N, round to bf16
-      const float mean = round_to_bf16(tot * (1.0f / (float)N));
-      sh_mean[c] = mean;
-      if (blk == 0 && k_mean) k_mean[bh * 128 + c] = mean;
-    } else {
-      sh_mean[c] = 0.f;
-    }
-    if (which == 2) {
-      float am = 0.f;
-      for (int i = 0; i < nchunks; ++i) am = fmaxf(am, ws_amax[(bh * nchunks + i) * 128 + c]);
-      sh_vinv[c] = div_full(448.0f, fmaxf(am, 1e-12f));
-      if (blk == 0) v_desc[bh * 128 + c] = div_full(am, 448.0f);
-    }
+    sh_mean[c] = (which == 1 && smooth_k) ? ws_sum[bh * nchunks * 128 + c] : 0.f;
+    if (which == 2) sh_vinv[c] = ws_amax[bh * nchunks * 128 + c];
   }
   __syncthreads();
 
@@ -332,6 +364,10 @@ extern "C" int fd_attn_quant(const void* q, const void* k, const void* v, int64_
         (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, ws_sum, ws_amax, N, nchunks, smooth_k,
         pv_fp8);
     int rc = check_launch("attn_quant colstats");
+    if (rc) return rc;
+    colstats_final_kernel<<<(unsigned)BH, 128, 0, st>>>(ws_sum, ws_amax, N, nchunks, smooth_k, pv_fp8,
+                                                        k_mean, v_desc);
+    rc = check_launch("attn_quant colstats final");
     if (rc) return rc;
   }
   const int64_t qs = fd_desc_stride(N, q_gran, 128), ks = fd_desc_stride(N, k_gran, 64);

@@ -23,6 +23,29 @@
 // byte feeds twice the MMA work (48 KiB per 512 MMA cycles instead of 32 KiB
 // per 256).  Tiles are visited in groups of GROUP_M row tiles so that the
 // tiles running at the same time share their A and B tiles in L2.
+//
+// Fused epilogues (EPI), each replacing a GEMM + quantiser pair of the
+// reference and producing its exact codes and scales:
+//   EPI_STORE      C = acc (+ bias) in bf16 / f16 / f32.
+//   EPI_QUANT      fp8_gemm_quant (fp8_kernels.py:573-709): the fp32
+//                  accumulator quantised 1 x 128 to e4m3 + fp32 dequant scales.
+//   EPI_GELU_TANH  GEMM -> bf16 -> GELU(tanh) -> 1 x 128 e4m3 (the MMDiT MLP:
+//                  replaces fp8_addmm + the GELU-tanh quantiser).
+//   EPI_SILU_GATE  the FFN chain head (src_ii/transformer.py:536-545): B = [w1; w3]
+//                  (2 H x K); the B tile holds w1 block nb and w3 block nb, so one
+//                  accumulator holds both halves of a gate group; emits
+//                  silu(bf16 w1) * bf16 w3 quantised 1 x 128 (replaces
+//                  fp8_addmm -> bf16 (M, 2H) -> fp8_silu_gate_quant).
+// For EPI_QUANT / EPI_GELU_TANH a thread's 128 columns are one output group; for
+// EPI_SILU_GATE the two threads holding the halves of a group exchange their
+// maxima through shared memory (named barrier of the quadrant's two warps).
+//
+// Multi-LoRA (EPI_STORE): the adapter delta sum_j s_j (x A_j^T) B_j^T of the
+// reference's MultiLoRALinear (src_ii/multi_lora.py:231-325, lora_kernels.py:55-157)
+// enters as extra 64-wide K slices after the FP8 slices: A = the per-token
+// scaled mid activations h (M, K_lora) bf16, B = [B_1 | B_2 | ...] (N, K_lora)
+// bf16, one tcgen05 kind::f16 MMA group per slice, promoted with scale 1, so
+// the delta is added to the fp32 accumulator before the single output rounding.
 #include "fd_act.cuh"
 #include "fd_host.h"
 
@@ -56,6 +79,7 @@ struct Params {
   int ntm, ntn, ntiles;  // ntn: output column tiles (256 wide; 128 wide for EPI_SILU_GATE)
   int kblocks;
   int nbs;         // rows of b_s (BMODE 0: ceil(rows of B / 128)); BMODE 1: its columns
+  int lora_slices; // 64-column bf16 LoRA slices after the FP8 slices (EPI_STORE, BMODE 0)
 };
 
 // Tile t -> (row tile, column tile), GROUP_M row tiles at a time so that the
@@ -125,6 +149,7 @@ FD_DEV void named_bar_sync(int id, int nthreads) {
 template <int BMODE, int CDT, int BDT, int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmLB,
                     const Params p) {
   using LY = Layout;
   extern __shared__ uint8_t smem_raw[];
@@ -197,6 +222,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           issued_mask |= 1u << s;
         }
+        for (int ls = 0; ls < p.lora_slices && ok; ++ls, ++it) {
+          // bf16 LoRA slice: 128 x 64 of h and 256 x 64 of B_cat (128-byte rows, same layout)
+          const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+          uint8_t* sa = smem + s * STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+          tma_load_2d(sa, &tmLA, &full[s], ls * 64, mb * BM);
+          tma_load_2d(sa + A_BYTES, &tmLB, &full[s], ls * 64, nb * BN);
+          issued_mask |= 1u << s;
+        }
       }
       // Drain: the newest load of every stage must have landed before exit.
       for (uint32_t s = 0; s < (uint32_t)STAGES; ++s) {
@@ -210,10 +245,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc(/*c F32*/ 1, /*E4M3*/ 0, 0, /*a K-major*/ 0, B_MN, BM, BN);
+      constexpr uint32_t idesc_lora = make_idesc(/*c F32*/ 1, /*BF16*/ 1, 1, 0, 0, BM, BN);
       uint32_t it = 0;
       bool ok = true;
+      const int nslices = p.kblocks + p.lora_slices;
       for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x) {
-        for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
+        for (int kb = 0; kb < nslices; ++kb, ++it) {
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
           const uint32_t tb = it % NTBUF, tph = (it / NTBUF) & 1;
           if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
@@ -222,13 +259,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t a0 = smem_u32(smem + s * STAGE_BYTES);
           const uint32_t b0 = a0 + A_BYTES;
           const uint32_t d = tmem_base + tb * BN;
+          if (kb < p.kblocks) {
 #pragma unroll
-          for (int k4 = 0; k4 < BK / 32; ++k4) {
-            const uint64_t ad = make_sdesc_sw128(a0 + k4 * 32, 16, 1024);
-            // MN-major B: 128-column panels 128 x BK bytes apart (LBO), 8 K rows per 1 KiB
-            const uint64_t bd = B_MN ? make_sdesc_sw128(b0 + k4 * 32 * 128, 128 * BK, 1024)
-                                     : make_sdesc_sw128(b0 + k4 * 32, 16, 1024);
-            mma_f8f6f4_ss(d, ad, bd, idesc, k4 > 0 ? 1u : 0u);
+            for (int k4 = 0; k4 < BK / 32; ++k4) {
+              const uint64_t ad = make_sdesc_sw128(a0 + k4 * 32, 16, 1024);
+              // MN-major B: 128-column panels 128 x BK bytes apart (LBO), 8 K rows per 1 KiB
+              const uint64_t bd = B_MN ? make_sdesc_sw128(b0 + k4 * 32 * 128, 128 * BK, 1024)
+                                       : make_sdesc_sw128(b0 + k4 * 32, 16, 1024);
+              mma_f8f6f4_ss(d, ad, bd, idesc, k4 > 0 ? 1u : 0u);
+            }
+          } else {
+            // LoRA slice: 64 bf16 columns = 4 x K16, 32 bytes per step as for e4m3 K32
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4) {
+              const uint64_t ad = make_sdesc_sw128(a0 + k4 * 32, 16, 1024);
+              const uint64_t bd = make_sdesc_sw128(b0 + k4 * 32, 16, 1024);
+              mma_f16_ss(d, ad, bd, idesc_lora, k4 > 0 ? 1u : 0u);
+            }
           }
           tc_commit(&empty[s]);
           tc_commit(&tfull[tb]);
@@ -265,22 +312,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       float acc[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.f;
-      for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
+      const int nslices = p.kblocks + p.lora_slices;
+      for (int kb = 0; kb < nslices; ++kb, ++it) {
         const uint32_t tb = it % NTBUF, tph = (it / NTBUF) & 1;
-        float bs_lo, bs_hi;
-        // (columns past the end of B read the last block's scale; they are never stored)
-        const int blo = min(n_lo / 128, p.nbs - 1), bhi = min(n_hi / 128, p.nbs - 1);
-        if (BMODE == 1) {
-          bs_lo = __ldg(p.b_s + (int64_t)kb * p.nbs + blo);
-          bs_hi = __ldg(p.b_s + (int64_t)kb * p.nbs + bhi);
-        } else if (BMODE == 0) {
-          bs_lo = __ldg(p.b_s + (int64_t)blo * p.kblocks + kb);
-          bs_hi = __ldg(p.b_s + (int64_t)bhi * p.kblocks + kb);
-        } else {
-          bs_lo = bs_hi = 1.0f;
+        const bool lora = kb >= p.kblocks;  // LoRA slices: the bf16 operands carry their scales
+        float sc_lo = 1.0f, sc_hi = 1.0f;
+        if (!lora) {
+          // (columns past the end of B read the last block's scale; they are never stored)
+          const int blo = min(n_lo / 128, p.nbs - 1), bhi = min(n_hi / 128, p.nbs - 1);
+          float bs_lo = 1.0f, bs_hi = 1.0f;
+          if (BMODE == 1) {
+            bs_lo = __ldg(p.b_s + (int64_t)kb * p.nbs + blo);
+            bs_hi = __ldg(p.b_s + (int64_t)kb * p.nbs + bhi);
+          } else if (BMODE == 0) {
+            bs_lo = __ldg(p.b_s + (int64_t)blo * p.kblocks + kb);
+            bs_hi = __ldg(p.b_s + (int64_t)bhi * p.kblocks + kb);
+          }
+          const float as = row_ok ? __ldg(as_row + kb) : 0.f;
+          sc_lo = as * bs_lo;
+          sc_hi = as * bs_hi;
         }
-        const float as = row_ok ? __ldg(as_row + kb) : 0.f;
-        const float sc_lo = as * bs_lo, sc_hi = as * bs_hi;
         ok = ok && mbar_wait(&tfull[tb], tph, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) continue;
@@ -375,7 +426,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 }
 
 template <int BMODE, int CDT, int BDT, int EPI = EPI_STORE>
-static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t st) {
+static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t st,
+                  const CUtensorMap* tla = nullptr, const CUtensorMap* tlb = nullptr) {
   auto kern = gemm_fp8_kernel<BMODE, CDT, BDT, EPI>;
   constexpr uint32_t smem_bytes = Layout::SMEM_BYTES;
   static bool attr_done = false;  // per instantiation
@@ -385,7 +437,7 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
     attr_done = true;
   }
   const int grid = p.ntiles < num_sms() ? p.ntiles : num_sms();
-  kern<<<grid, NUM_THREADS, smem_bytes, st>>>(ta, tb, p);
+  kern<<<grid, NUM_THREADS, smem_bytes, st>>>(ta, tb, tla ? *tla : ta, tlb ? *tlb : tb, p);
   return check_launch("fp8_gemm_blockwise");
 }
 
@@ -403,23 +455,23 @@ static int launch_quant(int bdt, const CUtensorMap& ta, const CUtensorMap& tb, c
 
 template <int BMODE, int CDT>
 static int launch_bias(int bdt, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
-                       cudaStream_t st) {
-  if (!p.bias) return launch<BMODE, CDT, -1>(ta, tb, p, st);
+                       cudaStream_t st, const CUtensorMap* tla = nullptr, const CUtensorMap* tlb = nullptr) {
+  if (!p.bias) return launch<BMODE, CDT, -1>(ta, tb, p, st, tla, tlb);
   switch (bdt) {
-    case FD_DT_BF16: return launch<BMODE, CDT, FD_DT_BF16>(ta, tb, p, st);
-    case FD_DT_F16: return launch<BMODE, CDT, FD_DT_F16>(ta, tb, p, st);
-    case FD_DT_F32: return launch<BMODE, CDT, FD_DT_F32>(ta, tb, p, st);
+    case FD_DT_BF16: return launch<BMODE, CDT, FD_DT_BF16>(ta, tb, p, st, tla, tlb);
+    case FD_DT_F16: return launch<BMODE, CDT, FD_DT_F16>(ta, tb, p, st, tla, tlb);
+    case FD_DT_F32: return launch<BMODE, CDT, FD_DT_F32>(ta, tb, p, st, tla, tlb);
     default: return set_error(FD_ERR_ARG, "unsupported bias dtype");
   }
 }
 
 template <int BMODE>
 static int launch_c(int cdt, int bdt, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
-                    cudaStream_t st) {
+                    cudaStream_t st, const CUtensorMap* tla = nullptr, const CUtensorMap* tlb = nullptr) {
   switch (cdt) {
-    case FD_DT_BF16: return launch_bias<BMODE, FD_DT_BF16>(bdt, ta, tb, p, st);
-    case FD_DT_F16: return launch_bias<BMODE, FD_DT_F16>(bdt, ta, tb, p, st);
-    case FD_DT_F32: return launch_bias<BMODE, FD_DT_F32>(bdt, ta, tb, p, st);
+    case FD_DT_BF16: return launch_bias<BMODE, FD_DT_BF16>(bdt, ta, tb, p, st, tla, tlb);
+    case FD_DT_F16: return launch_bias<BMODE, FD_DT_F16>(bdt, ta, tb, p, st, tla, tlb);
+    case FD_DT_F32: return launch_bias<BMODE, FD_DT_F32>(bdt, ta, tb, p, st, tla, tlb);
     default: return set_error(FD_ERR_ARG, "unsupported output dtype");
   }
 }
@@ -472,6 +524,7 @@ extern "C" int fd_fp8_gemm_blockwise(const void* a, const float* a_s, const void
   p.bias = bias;
   p.c = c;
   p.c_s = nullptr;
+  p.lora_slices = 0;
   p.M = (int)M;
   p.N = (int)N;
   p.K = (int)K;
@@ -531,10 +584,81 @@ extern "C" int fd_fp8_gemm_quant(const void* a, const float* a_s, const void* b,
   p.ntm = (int)((M + 127) / 128);
   p.ntn = act == FD_ACT_SILU_GATE ? (int)(N / 128) : (int)((N + 255) / 256);
   p.nbs = (int)(nb_rows / 128);
+  p.lora_slices = 0;
   p.ntiles = p.ntm * p.ntn;
   p.kblocks = (int)(K / 128);
   cudaStream_t st = (cudaStream_t)stream;
   if (act == FD_ACT_NONE) return gemm::launch_quant<gemm::EPI_QUANT>(bias_dtype, ta, tb, p, st);
   if (act == FD_ACT_GELU_TANH) return gemm::launch_quant<gemm::EPI_GELU_TANH>(bias_dtype, ta, tb, p, st);
   return gemm::launch_quant<gemm::EPI_SILU_GATE>(bias_dtype, ta, tb, p, st);
+}
+
+// FP8 block GEMM (b_layout 0) plus the multi-LoRA delta lora_a @ lora_b^T in the same
+// accumulator: lora_a (M, lora_k) bf16 = per-token scaled mid activations, lora_b
+// (N, lora_k) bf16 = the adapters' B matrices side by side; lora_k a positive
+// multiple of 64 (zero-padded).  K may be 0 (delta only: a, a_s, b, b_s unused).
+extern "C" int fd_fp8_gemm_blockwise_lora(const void* a, const float* a_s, const void* b,
+                                          const float* b_s, const void* bias, int bias_dtype, void* c,
+                                          int c_dtype, int64_t M, int64_t N, int64_t K,
+                                          const void* lora_a, const void* lora_b, int64_t lora_k,
+                                          void* stream) {
+  FD_CHECK_ARG(M >= 0 && N > 0 && K >= 0, "bad shape");
+  FD_CHECK_ARG(K % 128 == 0, "K must be a multiple of 128");
+  FD_CHECK_ARG(N % 16 == 0, "N must be a multiple of 16");
+  FD_CHECK_ARG(lora_k > 0 && lora_k % 64 == 0 && lora_k <= 65536, "lora_k must be a positive multiple of 64");
+  FD_CHECK_ARG(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "dimension too large");
+  if (M == 0) return FD_OK;
+  FD_CHECK_ARG(lora_a && lora_b && c, "null pointer");
+  FD_CHECK_ARG(K == 0 || (a && a_s && b && b_s), "null FP8 operand");
+  FD_CHECK_ARG(aligned16(lora_a) && aligned16(lora_b) && aligned16(c) && (K == 0 || (aligned16(a) && aligned16(b))),
+               "operands must be 16-byte aligned");
+  CUtensorMap ta, tb, tla, tlb;
+  {
+    const uint64_t dims[2] = {(uint64_t)lora_k, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)lora_k * 2};
+    const uint32_t box[2] = {64, 128};
+    int rc = encode_tiled(&tla, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, lora_a, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)lora_k, (uint64_t)N};
+    const uint64_t strides[1] = {(uint64_t)lora_k * 2};
+    const uint32_t box[2] = {64, 256};
+    int rc = encode_tiled(&tlb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, lora_b, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  if (K > 0) {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)K};
+    const uint32_t box[2] = {128, 128};
+    int rc = encode_tiled(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    const uint64_t bdims[2] = {(uint64_t)K, (uint64_t)N};
+    const uint32_t bbox[2] = {128, 256};
+    rc = encode_tiled(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, b, bdims, strides, bbox,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  } else {
+    ta = tla;  // never read: no FP8 slices
+    tb = tlb;
+  }
+  gemm::Params p;
+  p.a_s = a_s;
+  p.b_s = b_s;
+  p.bias = bias;
+  p.c = c;
+  p.c_s = nullptr;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.ntm = (int)((M + 127) / 128);
+  p.ntn = (int)((N + 255) / 256);
+  p.nbs = (int)((N + 127) / 128);
+  p.ntiles = p.ntm * p.ntn;
+  p.kblocks = (int)(K / 128);
+  p.lora_slices = (int)(lora_k / 64);
+  return gemm::launch_c<0>(c_dtype, bias_dtype, ta, tb, p, (cudaStream_t)stream, &tla, &tlb);
 }

@@ -104,6 +104,19 @@ int fd_fp8_gemm_blockwise(const void* a, const float* a_s, const void* b, const 
 /* G4 -- fp8_silu_gate_quant (src/futudiffu/fp8_kernels.py:842-978).
  * x (M, 2N) bf16 = [w1 | w3]; y (M, N) e4m3 = quant(silu(w1) * w3) per 1 x block,
  * s (M, N/block) f32.  N % block == 0, block == 128. */
+/* FP8 block GEMM (B stored (N, K)) plus a multi-LoRA delta in the same fp32
+ * accumulator: C = A8 B8^T (block-scaled, as fd_fp8_gemm_blockwise) + lora_a lora_b^T
+ * (+ bias), one rounding to c_dtype.  lora_a (M, lora_k) bf16 holds the per-token
+ * scaled mid activations s_j (x A_j^T) of every adapter j side by side, lora_b
+ * (N, lora_k) bf16 the adapters' B_j side by side; lora_k a positive multiple of 64
+ * (zero-padded).  K may be 0 (delta only).  Replaces the base linear + the adapter
+ * loop of MultiLoRALinear (src_ii/multi_lora.py:231-325) and the Triton
+ * _multi_lora_kernel (src/futudiffu/lora_kernels.py:55-157). */
+int fd_fp8_gemm_blockwise_lora(const void* a, const float* a_s, const void* b, const float* b_s,
+                               const void* bias, int bias_dtype, void* c, int c_dtype, int64_t M,
+                               int64_t N, int64_t K, const void* lora_a, const void* lora_b,
+                               int64_t lora_k, void* stream);
+
 /* GEMM with a quantising epilogue: c (M, N) e4m3 codes and c_s (M, N/128) fp32
  * dequant scales, 1 x 128 groups, from A (M, K) e4m3 + a_s and B e4m3 (K-major) + b_s
  * (128 x 128 blocks), optional bias (added in fp32).  N and K multiples of 128.

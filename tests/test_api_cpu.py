@@ -126,3 +126,33 @@ def test_dit_config_arithmetic():
     ft = text_freqs(small, "cpu")
     assert torch.equal(ft, torch.eye(2).expand(4, 64, 2, 2))
     assert batch_freqs(fi, 3).shape == (3, 6, 64, 2, 2)
+
+
+def test_multi_lora_slot_api():
+    """Slot bookkeeping of MultiLoRALinear (no GPU work)."""
+    from futudiffu_b200.multi_lora import MultiLoRALinear
+
+    base = torch.nn.Linear(256, 128, bias=False)
+    lin = MultiLoRALinear(base, max_adapters=2, max_rank=8, device="cpu")
+    lin.assign_adapter(0, "a", rank=4, alpha=8.0)
+    assert float(lin._lora_scalings[0]) == 2.0 and float(lin._slot_active[0]) == 1.0
+    assert torch.count_nonzero(lin.lora_A[0][4:]) == 0 and torch.count_nonzero(lin.lora_A[0][:4]) > 0
+    with pytest.raises(ValueError):
+        lin.assign_adapter(1, "a", rank=4, alpha=1.0)
+    with pytest.raises(ValueError):
+        lin.assign_adapter(1, "b", rank=16, alpha=1.0)
+    with pytest.raises(IndexError):
+        lin.assign_adapter(2, "b", rank=4, alpha=1.0)
+    lin.release_adapter(0)
+    assert lin._slot_names == [None, None] and float(lin._lora_scalings[0]) == 0.0
+    assert lin.in_features == 256 and lin.out_features_val == 128
+    eff = lin._effective_scales(5, torch.tensor([[1.0, 2.0], [3.0, 4.0]]), torch.tensor([0, 1, -1, 1, 0]))
+    assert eff.shape == (5, 2)
+
+
+def test_lora_operand_padding():
+    from futudiffu_b200.lora_kernels import lora_operands
+
+    h, b, kp = lora_operands(torch.ones(3, 40), torch.ones(5, 40))
+    assert kp == 64 and h.shape == (3, 64) and b.shape == (5, 64)
+    assert h[:, 40:].abs().sum() == 0
