@@ -146,7 +146,7 @@ FD_DEV void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-template <int BMODE, int CDT, int BDT, int EPI>
+template <int BMODE, int CDT, int BDT, int EPI, bool LORA>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmLB,
@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           issued_mask |= 1u << s;
         }
-        for (int ls = 0; ls < p.lora_slices && ok; ++ls, ++it) {
+        for (int ls = 0; LORA && ls < p.lora_slices && ok; ++ls, ++it) {
           // bf16 LoRA slice: 128 x 64 of h and 256 x 64 of B_cat (128-byte rows, same layout)
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
@@ -248,7 +248,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       constexpr uint32_t idesc_lora = make_idesc(/*c F32*/ 1, /*BF16*/ 1, 1, 0, 0, BM, BN);
       uint32_t it = 0;
       bool ok = true;
-      const int nslices = p.kblocks + p.lora_slices;
+      const int nslices = p.kblocks + (LORA ? p.lora_slices : 0);
       for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x) {
         for (int kb = 0; kb < nslices; ++kb, ++it) {
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t a0 = smem_u32(smem + s * STAGE_BYTES);
           const uint32_t b0 = a0 + A_BYTES;
           const uint32_t d = tmem_base + tb * BN;
-          if (kb < p.kblocks) {
+          if (!LORA || kb < p.kblocks) {
 #pragma unroll
             for (int k4 = 0; k4 < BK / 32; ++k4) {
               const uint64_t ad = make_sdesc_sw128(a0 + k4 * 32, 16, 1024);
@@ -312,10 +312,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       float acc[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.f;
-      const int nslices = p.kblocks + p.lora_slices;
+      const int nslices = p.kblocks + (LORA ? p.lora_slices : 0);
       for (int kb = 0; kb < nslices; ++kb, ++it) {
         const uint32_t tb = it % NTBUF, tph = (it / NTBUF) & 1;
-        const bool lora = kb >= p.kblocks;  // LoRA slices: the bf16 operands carry their scales
+        const bool lora = LORA && kb >= p.kblocks;  // LoRA slices: the bf16 operands carry their scales
         float sc_lo = 1.0f, sc_hi = 1.0f;
         if (!lora) {
           // (columns past the end of B read the last block's scale; they are never stored)
@@ -425,10 +425,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) tmem_dealloc(tmem_base, 512);
 }
 
-template <int BMODE, int CDT, int BDT, int EPI = EPI_STORE>
+template <int BMODE, int CDT, int BDT, int EPI = EPI_STORE, bool LORA = false>
 static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t st,
                   const CUtensorMap* tla = nullptr, const CUtensorMap* tlb = nullptr) {
-  auto kern = gemm_fp8_kernel<BMODE, CDT, BDT, EPI>;
+  auto kern = gemm_fp8_kernel<BMODE, CDT, BDT, EPI, LORA>;
   constexpr uint32_t smem_bytes = Layout::SMEM_BYTES;
   static bool attr_done = false;  // per instantiation
   if (!attr_done) {
@@ -453,25 +453,25 @@ static int launch_quant(int bdt, const CUtensorMap& ta, const CUtensorMap& tb, c
   }
 }
 
-template <int BMODE, int CDT>
+template <int BMODE, int CDT, bool LORA = false>
 static int launch_bias(int bdt, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
                        cudaStream_t st, const CUtensorMap* tla = nullptr, const CUtensorMap* tlb = nullptr) {
-  if (!p.bias) return launch<BMODE, CDT, -1>(ta, tb, p, st, tla, tlb);
+  if (!p.bias) return launch<BMODE, CDT, -1, EPI_STORE, LORA>(ta, tb, p, st, tla, tlb);
   switch (bdt) {
-    case FD_DT_BF16: return launch<BMODE, CDT, FD_DT_BF16>(ta, tb, p, st, tla, tlb);
-    case FD_DT_F16: return launch<BMODE, CDT, FD_DT_F16>(ta, tb, p, st, tla, tlb);
-    case FD_DT_F32: return launch<BMODE, CDT, FD_DT_F32>(ta, tb, p, st, tla, tlb);
+    case FD_DT_BF16: return launch<BMODE, CDT, FD_DT_BF16, EPI_STORE, LORA>(ta, tb, p, st, tla, tlb);
+    case FD_DT_F16: return launch<BMODE, CDT, FD_DT_F16, EPI_STORE, LORA>(ta, tb, p, st, tla, tlb);
+    case FD_DT_F32: return launch<BMODE, CDT, FD_DT_F32, EPI_STORE, LORA>(ta, tb, p, st, tla, tlb);
     default: return set_error(FD_ERR_ARG, "unsupported bias dtype");
   }
 }
 
-template <int BMODE>
+template <int BMODE, bool LORA = false>
 static int launch_c(int cdt, int bdt, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
                     cudaStream_t st, const CUtensorMap* tla = nullptr, const CUtensorMap* tlb = nullptr) {
   switch (cdt) {
-    case FD_DT_BF16: return launch_bias<BMODE, FD_DT_BF16>(bdt, ta, tb, p, st, tla, tlb);
-    case FD_DT_F16: return launch_bias<BMODE, FD_DT_F16>(bdt, ta, tb, p, st, tla, tlb);
-    case FD_DT_F32: return launch_bias<BMODE, FD_DT_F32>(bdt, ta, tb, p, st, tla, tlb);
+    case FD_DT_BF16: return launch_bias<BMODE, FD_DT_BF16, LORA>(bdt, ta, tb, p, st, tla, tlb);
+    case FD_DT_F16: return launch_bias<BMODE, FD_DT_F16, LORA>(bdt, ta, tb, p, st, tla, tlb);
+    case FD_DT_F32: return launch_bias<BMODE, FD_DT_F32, LORA>(bdt, ta, tb, p, st, tla, tlb);
     default: return set_error(FD_ERR_ARG, "unsupported output dtype");
   }
 }
@@ -660,5 +660,5 @@ extern "C" int fd_fp8_gemm_blockwise_lora(const void* a, const float* a_s, const
   p.ntiles = p.ntm * p.ntn;
   p.kblocks = (int)(K / 128);
   p.lora_slices = (int)(lora_k / 64);
-  return gemm::launch_c<0>(c_dtype, bias_dtype, ta, tb, p, (cudaStream_t)stream, &tla, &tlb);
+  return gemm::launch_c<0, true>(c_dtype, bias_dtype, ta, tb, p, (cudaStream_t)stream, &tla, &tlb);
 }
