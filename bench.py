@@ -1,7 +1,7 @@
 """Benchmarks of the quantized DiT hot path on B200.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload dit|attention|gemm]
+                  [--workload dit|video|attention|gemm|packed]
 
 Workloads (one "step" each):
   dit (default, BASELINE config 4, the headline metric "DiT denoise steps/s"):
@@ -13,6 +13,11 @@ Workloads (one "step" each):
   attention: quantisation prologue + tcgen05 attention on
       B=2, H=24, S=4096, D=128 (int8 per-block QK, e4m3 P/V); replicas per rank.
   gemm (or the reference's Z-Image shapes): one FP8 block GEMM.
+  video: one denoise step of the 14B-class video DiT with
+      Ulysses sequence parallelism (NCCL all-to-all around the attention).
+  packed (the reference's production shape): a bin of the bin packer (two
+      images + captions in 4288 tokens) through 30 Z-Image-class
+      JointTransformerBlocks with per-image adaLN and the block mask.
 
 ``--impl reference`` times the CPU restatement of the reference algorithm (the
 oracle) on a bounded sample on rank 0; the other ranks exit without work.
@@ -635,6 +640,127 @@ def run_video(args, world, rank, local):
 GEMM_SHAPES = {"config1": (2048, 3072, 3072), "ref_qkv": (8576, 11520, 3840), "ref_w2": (8576, 3840, 10240)}
 
 
+PACKED_METRIC = "packed multi-image forward tokens/s (Z-Image-class blocks, 3840 hidden, 30 heads, 4288-token bin)"
+
+
+def run_packed(args, world, rank, local):
+    """The reference's production shape: one bin of the bin packer (two images of
+    different resolution with their captions, padded to REFERENCE_TOTAL_LEN = 4288
+    tokens) through ``--layers`` JointTransformerBlocks with per-image adaLN and
+    the block-diagonal mask; one step = one forward of the layer stack."""
+    from futudiffu_b200 import check_status
+    from futudiffu_b200.bin_packer import REFERENCE_TOTAL_LEN, BinPackScheduler
+    from futudiffu_b200.block_mask import build_block_mask_from_packing_info
+    from futudiffu_b200.forward_packed import _pad_plan_to_fixed_len
+    from futudiffu_b200.transformer import PackedTrunk, build_packed_rope, build_packed_sequence, row_ranges
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dim, heads = 3840, 30
+    plan = [{"width": 1024, "height": 768, "cap_tokens": 50}, {"width": 512, "height": 512, "cap_tokens": 50}]
+    bins = BinPackScheduler().pack_generation_plan(plan)
+    assert len(bins) == 1
+    g = torch.Generator().manual_seed(7 + rank)
+    caps = [torch.randn(1, it["cap_tokens"], dim, generator=g).to(torch.bfloat16) for it in bins[0]]
+    grids = [(it["height"] // 16, it["width"] // 16) for it in bins[0]]
+    imgs = [torch.randn(1, h * w, dim, generator=g).to(torch.bfloat16) for h, w in grids]
+    pad = torch.zeros(dim, dtype=torch.bfloat16)
+    packed, info = build_packed_sequence(caps, imgs, grids, [it["cap_tokens"] for it in bins[0]], 32, pad, pad)
+    natural = info.total_len
+    info, rope = _pad_plan_to_fixed_len(info, build_packed_rope(info, device="cpu"), REFERENCE_TOTAL_LEN)
+    host_x = torch.cat([packed, packed.new_zeros(1, REFERENCE_TOTAL_LEN - natural, dim)], 1).contiguous()
+    x0 = host_x.to(dev)
+    rope = rope.to(dev)
+    mask = build_block_mask_from_packing_info(info, device=dev)
+    mask_density = float(mask.float().mean())
+    ranges = row_ranges(info.document_id, n_params=info.n_images, device=dev)
+    adaln = torch.randn(info.n_images, 256, generator=g).to(torch.bfloat16).to(dev)
+    trunk = PackedTrunk(args.layers, dim, heads, seed=0, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return trunk(x0, adaln, ranges, mask, rope)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    check_status()
+    rec = LaunchRecorder()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else local) as clocks:
+        rec.active = True
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        rec.active = False
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_local = start.elapsed_time(end) / args.steps
+    ms = max_over_ranks(ms_local, world, dev)
+    gemm_work, gemm_ms, n_gemm = rec.summary("gemm")
+    attn_work, attn_ms, n_attn = rec.summary("attn")
+    launches = rec.launches
+    rec.close()
+    check_status()
+
+    # end to end: the packed bin from pinned host memory, the output back to the host
+    h_x = host_x.pin_memory()
+    h_out = torch.empty_like(host_x).pin_memory()
+
+    def e2e_step():
+        xi = h_x.to(dev, non_blocking=True)
+        h_out.copy_(trunk(xi, adaln, ranges, mask, rope), non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(3):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / 3, world, dev)
+    check_status()
+    if rank == 0:
+        pk = peaks()
+        peak = 2.0 * pk["bf16_tflops_sustained"]
+        gemm_tf = gemm_work / (gemm_ms * 1e-3) / 1e12
+        toks = REFERENCE_TOTAL_LEN * world
+        line = {
+            "metric": PACKED_METRIC, "value": toks / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp8/int8",
+            "data": "synthetic (random-init weights, N(0,1) captions/patches)",
+            "config": {"workload": "packed_zimage_trunk", "layers": args.layers, "hidden": dim, "heads": heads,
+                       "ffn_hidden": 10240, "bin": [(it["width"], it["height"], it["cap_tokens"]) for it in bins[0]],
+                       "tokens": f"{natural} packed + {REFERENCE_TOTAL_LEN - natural} padding",
+                       "adaln": "per image (row ranges)", "attention": "int8 per-token QK, bf16 PV, block mask",
+                       "l2": "weights and activations exceed the 126 MB L2; no explicit flush",
+                       "parallelism": f"one bin per GPU x{world}, no collective",
+                       # the mask skips tiles that mix images: count the computed tiles only
+                       "attention_mask_density": mask_density,
+                       "attention_kernel_tops": (attn_work * mask_density / (attn_ms * 1e-3) / 1e12
+                                                 if attn_ms else None),
+                       "time_share": {"gemm": gemm_ms / args.steps / ms_local,
+                                      "attention": attn_ms / args.steps / ms_local}},
+            "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": peak, "unit": "TFLOP/s",
+                         "frac": gemm_tf / peak, "traffic": None,
+                         "kernel": f"gemm_fp8_kernel ({n_gemm // max(1, args.steps)} launches per step, flop-weighted)",
+                         "peak_source": f"2 x {pk['source']} sustained bf16 dense ({pk['bf16_tflops_sustained']} TF/s)"},
+            "cpu_baseline": None,
+            "e2e": {"value": toks / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": host_x.numel() * 2 * world, "d2h_bytes_per_step": host_x.numel() * 2 * world,
+                    "ms_per_step": e2e_ms, "api": "futudiffu_b200.transformer.PackedTrunk"},
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_gemm(args, world, rank, local):
     """FP8 block-GEMM TFLOPS (or the reference's own Z-Image shapes)."""
     from futudiffu_b200 import _lib as L
@@ -698,17 +824,19 @@ def main(argv=None) -> int:
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default: 10 dit, 50 otherwise)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["dit", "video", "attention", "gemm"], default="dit",
+    ap.add_argument("--workload", choices=["dit", "video", "attention", "gemm", "packed"], default="dit",
                     help="dit = BASELINE config 4 (headline); video = config 5 (Ulysses); "
-                         "attention = config 2; gemm = config 1")
+                         "attention = config 2; gemm = config 1; packed = the reference's packed "
+                         "4288-token bin through Z-Image-class JointTransformerBlocks")
     ap.add_argument("--gemm-shape", choices=sorted(GEMM_SHAPES), default="config1")
+    ap.add_argument("--layers", type=int, default=30, help="packed: JointTransformerBlocks in the stack")
     ap.add_argument("--profile", action="store_true",
                     help="dit: bracket the first timed step with cudaProfilerStart/Stop "
                          "(for ncu --profile-from-start off); timing of that run is not a result")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
     if args.steps is None:
-        args.steps = {"dit": 10, "video": 3}.get(args.workload, 50)
+        args.steps = {"dit": 10, "video": 3, "packed": 10}.get(args.workload, 50)
     world, rank, local = dist_setup()
     try:
         if args.workload == "dit":
@@ -722,6 +850,13 @@ def main(argv=None) -> int:
                                       "a 1.7 PFLOP step; see the dit workload's CPU baseline"}), flush=True)
                 return 0
             return run_video(args, world, rank, local)
+        if args.workload == "packed":
+            if args.impl == "reference":
+                if rank == 0:
+                    print(json.dumps({"impl": "reference", "unavailable": "the packed workload has no CPU "
+                                      "reference arm; see the dit workload's CPU baseline"}), flush=True)
+                return 0
+            return run_packed(args, world, rank, local)
         if args.impl == "reference":
             return run_reference(args, world, rank)
         if args.workload == "gemm":

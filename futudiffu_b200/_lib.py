@@ -63,6 +63,9 @@ _SIGS: dict[str, list] = {
     "fd_rms_norm_modulate": [_P, _P, _I, _P, _I, _P, _L, _L, _L, _F, _P],
     "fd_rms_norm_modulate_quant": [_P, _P, _I, _P, _I, _P, _P, _L, _L, _L, _F, _P],
     "fd_rms_norm_gate_residual": [_P, _P, _I, _P, _I, _P, _P, _L, _L, _L, _F, _P],
+    "fd_rms_norm_modulate_ranges": [_P, _P, _I, _P, _I, _P, _L, _L, _F, _P, _P, _L, _L, _P],
+    "fd_rms_norm_modulate_quant_ranges": [_P, _P, _I, _P, _I, _P, _P, _L, _L, _F, _P, _P, _L, _L, _P],
+    "fd_rms_norm_gate_residual_ranges": [_P, _P, _I, _P, _I, _P, _P, _L, _L, _F, _P, _P, _L, _L, _P],
     "fd_qkv_postprocess": [_P, _P, _P, _P, _P, _P, _P, _L, _L, _L, _L, _F, _P],
     "fd_qkv_postprocess_into": [_P, _P, _P, _P, _P, _P, _P, _L, _L, _L, _L, _F, _L, _L, _P],
     "fd_attn_quant_workspace_floats": [_L, _L],

@@ -47,10 +47,16 @@ constexpr int kMaxVecPerLane = 32;
 // quantisation (out holds the codes, qs the dequant scales).  A 128-column group
 // is 16 consecutive 8-column vectors, i.e. one half-warp for a given j.
 //
-// Grid (CTAs per sample, B): a CTA serves rows of one sample b, so the
+// Grid (B, CTAs per sample): a CTA serves rows of one sample b, so the
 // per-column factors -- the norm weight and (1 + scale[b]) or tanh(gate[b]),
 // which the reference evaluates per element -- are computed once per CTA into
 // shared memory (fp32, dim <= 8192) and read back as 16-byte vectors.
+//
+// Row ranges (packed multi-image sequences, per-token adaLN): with `ranges`
+// set, "sample" b is the row range [ranges[b], ranges[b + 1]) and its factors
+// come from parameter row rparam[b] of scale / gate (n_params rows), so a
+// packed sequence's per-image modulation is applied without materialising a
+// (tokens, dim) tensor.  Ranges or parameter rows out of bounds are skipped.
 template <int MODE, int WDT, int SDT, int NV>
 __global__ void __launch_bounds__(256) rms_row_kernel(const __nv_bfloat16* __restrict__ x,
                                                      const void* __restrict__ w,
@@ -58,22 +64,32 @@ __global__ void __launch_bounds__(256) rms_row_kernel(const __nv_bfloat16* __res
                                                      const __nv_bfloat16* __restrict__ res,
                                                      __nv_bfloat16* __restrict__ out,
                                                      float* __restrict__ qs,
-                                                     int64_t rows, int64_t S, int dim, float eps) {
+                                                     int64_t rows, int64_t S, int dim, float eps,
+                                                     const int* __restrict__ ranges,
+                                                     const int* __restrict__ rparam, int64_t n_params) {
   extern __shared__ float4 norm_smem[];
   float* s_w = reinterpret_cast<float*>(norm_smem);  // [dim] weight
   float* s_f = s_w + dim;                             // [dim] 1 + scale  or  tanh(gate)
   const int lane = lane_id();
-  const int64_t b = blockIdx.y;
+  const int64_t b = blockIdx.x;
+  int64_t prow = b, row0 = b * S, nrows = S;
+  if (ranges) {
+    prow = rparam[b];
+    row0 = ranges[b];
+    nrows = (int64_t)ranges[b + 1] - row0;
+    if (prow < 0 || prow >= n_params || row0 < 0 || nrows < 0 || row0 + nrows > rows) return;
+  }
+  if ((int64_t)blockIdx.y * (blockDim.x >> 5) >= nrows) return;  // no row for this CTA
   for (int col = threadIdx.x; col < dim; col += blockDim.x) {
     s_w[col] = load_elem<WDT>(w, col);
-    const float sv = load_elem<SDT>(sg, b * dim + col);
+    const float sv = load_elem<SDT>(sg, prow * dim + col);
     s_f[col] = MODE == 1 ? tanhf(sv) : 1.0f + sv;
   }
   __syncthreads();
   const int nvec = dim / 8;
-  const int64_t wpb = (int64_t)gridDim.x * (blockDim.x >> 5);  // warps serving this sample
-  for (int64_t sr = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp_id(); sr < S; sr += wpb) {
-    const int64_t row = b * S + sr;
+  const int64_t wpb = (int64_t)gridDim.y * (blockDim.x >> 5);  // warps serving this sample
+  for (int64_t sr = (int64_t)blockIdx.y * (blockDim.x >> 5) + warp_id(); sr < nrows; sr += wpb) {
+    const int64_t row = row0 + sr;
     uint4 xr[NV];  // the row, still packed bf16 (half the registers of fp32)
     float ss = 0.f;
 #pragma unroll
@@ -146,15 +162,16 @@ __global__ void __launch_bounds__(256) rms_row_kernel(const __nv_bfloat16* __res
 
 template <int MODE, int WDT, int SDT>
 static void launch_rms(const void* x, const void* w, const void* sg, const void* res, void* out,
-                       float* qs, int64_t rows, int64_t S, int dim, float eps, cudaStream_t st) {
+                       float* qs, int64_t rows, int64_t S, int dim, float eps, cudaStream_t st,
+                       const int* ranges, const int* rparam, int64_t n_ranges, int64_t n_params) {
   const int nvec = dim / 8;
-  const int64_t B = rows / S;
-  // about 8 CTAs (64 warps) per SM in total, spread over the samples
+  const int64_t B = ranges ? n_ranges : rows / S;
+  // about 8 CTAs (64 warps) per SM in total, spread over the samples (ranges)
   int64_t per_b = ((int64_t)num_sms() * 8 + B - 1) / B;
-  const int64_t need = (S + 7) / 8;
+  const int64_t need = ((ranges ? rows : S) + 7) / 8;
   if (per_b > need) per_b = need;
   if (per_b < 1) per_b = 1;
-  const dim3 grid((unsigned)per_b, (unsigned)B);
+  const dim3 grid((unsigned)B, (unsigned)per_b);
   const size_t smem = 2 * (size_t)dim * sizeof(float);
 #define FD_RMS_LAUNCH(NVV)                                                                  \
   do {                                                                                      \
@@ -165,7 +182,8 @@ static void launch_rms(const void* x, const void* w, const void* sg, const void*
       attr_done = true;                                                                     \
     }                                                                                       \
     kern<<<grid, 256, smem, st>>>((const __nv_bfloat16*)x, w, sg, (const __nv_bfloat16*)res, \
-                                  (__nv_bfloat16*)out, qs, rows, S, dim, eps);              \
+                                  (__nv_bfloat16*)out, qs, rows, S, dim, eps, ranges, rparam, \
+                                  n_params);                                                \
   } while (0)
   // the row lives in registers: the smallest vector count that holds it
   if (nvec <= 32 * 4) FD_RMS_LAUNCH(4);
@@ -180,12 +198,14 @@ static void launch_rms(const void* x, const void* w, const void* sg, const void*
 template <int MODE>
 static int dispatch_rms(const void* x, const void* w, int wdt, const void* sg, int sdt,
                         const void* res, void* out, int64_t rows, int64_t S, int dim, float eps,
-                        cudaStream_t st, float* qs = nullptr) {
+                        cudaStream_t st, float* qs = nullptr, const int* ranges = nullptr,
+                        const int* rparam = nullptr, int64_t n_ranges = 0, int64_t n_params = 0) {
+#define FD_RMS_ARGS x, w, sg, res, out, qs, rows, S, dim, eps, st, ranges, rparam, n_ranges, n_params
 #define FD_RMS_W(WD)                                                                       \
   switch (sdt) {                                                                           \
-    case FD_DT_BF16: launch_rms<MODE, WD, FD_DT_BF16>(x, w, sg, res, out, qs, rows, S, dim, eps, st); break; \
-    case FD_DT_F16: launch_rms<MODE, WD, FD_DT_F16>(x, w, sg, res, out, qs, rows, S, dim, eps, st); break;   \
-    case FD_DT_F32: launch_rms<MODE, WD, FD_DT_F32>(x, w, sg, res, out, qs, rows, S, dim, eps, st); break;   \
+    case FD_DT_BF16: launch_rms<MODE, WD, FD_DT_BF16>(FD_RMS_ARGS); break;                 \
+    case FD_DT_F16: launch_rms<MODE, WD, FD_DT_F16>(FD_RMS_ARGS); break;                   \
+    case FD_DT_F32: launch_rms<MODE, WD, FD_DT_F32>(FD_RMS_ARGS); break;                   \
     default: return set_error(FD_ERR_ARG, "unsupported scale/gate dtype");                 \
   }
   switch (wdt) {
@@ -195,6 +215,7 @@ static int dispatch_rms(const void* x, const void* w, int wdt, const void* sg, i
     default: return set_error(FD_ERR_ARG, "unsupported weight dtype");
   }
 #undef FD_RMS_W
+#undef FD_RMS_ARGS
   return check_launch(MODE == 0 ? "rms_norm_modulate" : MODE == 1 ? "rms_norm_gate_residual" : "rms_norm_modulate_quant");
 }
 
@@ -298,6 +319,56 @@ extern "C" int fd_rms_norm_gate_residual(const void* x, const void* w, int w_dty
   return dispatch_rms<1>(x, w, w_dtype, gate, gate_dtype, residual, out, B * S, S, (int)dim, eps,
                          (cudaStream_t)stream);
 }
+
+// Row-range variants (packed sequences with per-image adaLN): rows
+// [range_rows[i], range_rows[i + 1]) use parameter row range_param[i] of
+// scale / gate (n_params x dim).  range_rows (n_ranges + 1) and range_param
+// (n_ranges) are int32 DEVICE arrays; rows outside every range are not written.
+#define FD_RANGE_CHECKS                                                                     \
+  FD_CHECK_ARG(rows >= 0 && dim > 0 && dim <= 8192 && n_ranges >= 0 && n_params > 0, "bad shape"); \
+  FD_CHECK_ARG(rows < (1ll << 31) && n_ranges < (1ll << 31), "too many rows");             \
+  if (rows == 0 || n_ranges == 0) return FD_OK;                                             \
+  FD_CHECK_ARG(range_rows && range_param, "null range arrays")
+
+extern "C" int fd_rms_norm_modulate_ranges(const void* x, const void* w, int w_dtype, const void* scale,
+                                           int scale_dtype, void* out, int64_t rows, int64_t dim, float eps,
+                                           const int32_t* range_rows, const int32_t* range_param,
+                                           int64_t n_ranges, int64_t n_params, void* stream) {
+  FD_RANGE_CHECKS;
+  FD_CHECK_ARG(dim % 8 == 0, "dim must be a multiple of 8");
+  FD_CHECK_ARG(x && w && scale && out, "null pointer");
+  FD_CHECK_ARG(aligned16(x) && aligned16(out), "x and out must be 16-byte aligned");
+  return dispatch_rms<0>(x, w, w_dtype, scale, scale_dtype, nullptr, out, rows, rows, (int)dim, eps,
+                         (cudaStream_t)stream, nullptr, range_rows, range_param, n_ranges, n_params);
+}
+
+extern "C" int fd_rms_norm_modulate_quant_ranges(const void* x, const void* w, int w_dtype,
+                                                 const void* scale, int scale_dtype, void* y, float* y_s,
+                                                 int64_t rows, int64_t dim, float eps,
+                                                 const int32_t* range_rows, const int32_t* range_param,
+                                                 int64_t n_ranges, int64_t n_params, void* stream) {
+  FD_RANGE_CHECKS;
+  FD_CHECK_ARG(dim % 128 == 0, "dim must be a multiple of 128");
+  FD_CHECK_ARG(x && w && scale && y && y_s, "null pointer");
+  FD_CHECK_ARG(aligned16(x) && aligned16(y), "x and y must be 16-byte aligned");
+  return dispatch_rms<2>(x, w, w_dtype, scale, scale_dtype, nullptr, y, rows, rows, (int)dim, eps,
+                         (cudaStream_t)stream, y_s, range_rows, range_param, n_ranges, n_params);
+}
+
+extern "C" int fd_rms_norm_gate_residual_ranges(const void* x, const void* w, int w_dtype, const void* gate,
+                                                int gate_dtype, const void* residual, void* out, int64_t rows,
+                                                int64_t dim, float eps, const int32_t* range_rows,
+                                                const int32_t* range_param, int64_t n_ranges,
+                                                int64_t n_params, void* stream) {
+  FD_RANGE_CHECKS;
+  FD_CHECK_ARG(dim % 8 == 0, "dim must be a multiple of 8");
+  FD_CHECK_ARG(x && w && gate && residual && out, "null pointer");
+  FD_CHECK_ARG(aligned16(x) && aligned16(out) && aligned16(residual),
+               "x, residual and out must be 16-byte aligned");
+  return dispatch_rms<1>(x, w, w_dtype, gate, gate_dtype, residual, out, rows, rows, (int)dim, eps,
+                         (cudaStream_t)stream, nullptr, range_rows, range_param, n_ranges, n_params);
+}
+#undef FD_RANGE_CHECKS
 
 extern "C" int fd_qkv_postprocess_into(const void* qkv, const float* qw, const float* kw,
                                        const float* freqs, void* oq, void* ok, void* ov, int64_t B,

@@ -74,6 +74,57 @@ def qkv_postprocess_into(qkv, q_norm_weight, k_norm_weight, freqs_cis, q_out, k_
            B, S, H, hd, float(norm_eps), S_total, seq_offset, L.stream_ptr(qkv.device))
 
 
+def _range_args(x, params, range_rows, range_param):
+    dim = x.shape[-1]
+    assert x.is_contiguous() and x.dtype == torch.bfloat16, "x must be contiguous bf16"
+    assert params.ndim == 2 and params.shape[1] == dim and params.is_contiguous(), "params must be (n, dim)"
+    assert range_rows.dtype == torch.int32 and range_param.dtype == torch.int32
+    assert range_rows.numel() == range_param.numel() + 1, "range_rows needs one more entry than range_param"
+    L.require_cuda(x, params, range_rows, range_param)
+    return x.numel() // dim, dim, range_param.numel(), params.shape[0]
+
+
+def rms_norm_modulate_ranges(x, weight, scale, range_rows, range_param, eps=1e-5):
+    """P1 over a packed sequence: rows [range_rows[i], range_rows[i + 1]) of x
+    (..., dim) are modulated by (1 + scale[range_param[i]]), scale (n_images, dim).
+
+    The per-token path of the reference block (src_ii/transformer.py:656-677)
+    with the per-image rows it scatters by document_id
+    (src_ii/zimage_model.py:496-512) left unscattered.  Rows in no range are
+    not written."""
+    rows, dim, n, n_params = _range_args(x, scale, range_rows, range_param)
+    out = torch.empty_like(x)
+    L.call("fd_rms_norm_modulate_ranges", L.ptr(x), L.ptr(weight), L.dtype_code(weight.dtype), L.ptr(scale),
+           L.dtype_code(scale.dtype), L.ptr(out), rows, dim, float(eps), L.ptr(range_rows), L.ptr(range_param),
+           n, n_params, L.stream_ptr(x.device))
+    return out
+
+
+def rms_norm_modulate_quant_ranges(x, weight, scale, range_rows, range_param, eps=1e-5):
+    """``rms_norm_modulate_ranges`` quantised 1 x 128 to e4m3 in the same pass:
+    codes (..., dim) and fp32 dequant scales (..., dim / 128)."""
+    rows, dim, n, n_params = _range_args(x, scale, range_rows, range_param)
+    assert dim % 128 == 0, "dim must be a multiple of 128"
+    y = torch.empty(x.shape, dtype=torch.float8_e4m3fn, device=x.device)
+    y_s = torch.empty(*x.shape[:-1], dim // 128, dtype=torch.float32, device=x.device)
+    L.call("fd_rms_norm_modulate_quant_ranges", L.ptr(x), L.ptr(weight), L.dtype_code(weight.dtype),
+           L.ptr(scale), L.dtype_code(scale.dtype), L.ptr(y), L.ptr(y_s), rows, dim, float(eps),
+           L.ptr(range_rows), L.ptr(range_param), n, n_params, L.stream_ptr(x.device))
+    return y, y_s
+
+
+def rms_norm_gate_residual_ranges(x, weight, gate, residual, range_rows, range_param, eps=1e-5):
+    """P2 over a packed sequence: residual + tanh(gate[range_param[i]]) *
+    rmsnorm(x) * w on the rows of range i."""
+    rows, dim, n, n_params = _range_args(x, gate, range_rows, range_param)
+    assert residual.shape == x.shape and residual.is_contiguous() and residual.dtype == torch.bfloat16
+    out = torch.empty_like(x)
+    L.call("fd_rms_norm_gate_residual_ranges", L.ptr(x), L.ptr(weight), L.dtype_code(weight.dtype), L.ptr(gate),
+           L.dtype_code(gate.dtype), L.ptr(residual), L.ptr(out), rows, dim, float(eps), L.ptr(range_rows),
+           L.ptr(range_param), n, n_params, L.stream_ptr(x.device))
+    return out
+
+
 def _fused_rms_norm_gate_residual_cuda(x, weight, gate, residual, eps=1e-5):
     assert x.ndim == 3, f"Expected x to be 3D (B, seq, dim), got {x.ndim}D"
     assert x.is_contiguous(), "Input x must be contiguous"

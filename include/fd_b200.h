@@ -156,8 +156,6 @@ int fd_rms_norm_modulate(const void* x, const void* w, int w_dtype, const void* 
                          int scale_dtype, void* out, int64_t B, int64_t S, int64_t dim, float eps,
                          void* stream);
 
-/* P2 -- fused_rms_norm_gate_residual (src/futudiffu/fused_kernels.py:99-148, :200-247).
- * out = residual + tanh(gate[b]) * rmsnorm(x) * w. */
 /* RMSNorm-modulate (as fd_rms_norm_modulate) with the 1 x 128 e4m3 activation
  * quantiser fused into the same pass: y (B, S, dim) e4m3 codes, y_s (B, S, dim/128)
  * fp32 dequant scales, equal to fd_rms_norm_modulate followed by fd_fp8_act_quant
@@ -168,9 +166,35 @@ int fd_rms_norm_modulate_quant(const void* x, const void* w, int w_dtype, const 
                                int scale_dtype, void* y, float* y_s, int64_t B, int64_t S,
                                int64_t dim, float eps, void* stream);
 
+/* P2 -- fused_rms_norm_gate_residual (src/futudiffu/fused_kernels.py:99-148, :200-247).
+ * out = residual + tanh(gate[b]) * rmsnorm(x) * w. */
 int fd_rms_norm_gate_residual(const void* x, const void* w, int w_dtype, const void* gate,
                               int gate_dtype, const void* residual, void* out, int64_t B,
                               int64_t S, int64_t dim, float eps, void* stream);
+
+/* P1 / P1 + G1 / P2 for a packed multi-image sequence with per-image adaLN
+ * (P4: the per-token path of JointTransformerBlock.forward,
+ * src_ii/transformer.py:656-677, whose per-token scale / gate rows are the
+ * per-image rows scattered by document_id, src_ii/zimage_model.py:496-512).
+ * x, residual, out: (rows, dim); scale / gate: (n_params, dim).  Rows
+ * [range_rows[i], range_rows[i + 1]) use parameter row range_param[i];
+ * range_rows (n_ranges + 1) and range_param (n_ranges) are int32 device arrays.
+ * Ranges that leave [0, rows) or name a row outside [0, n_params) are skipped;
+ * rows covered by no range are not written.  The reference runs this path
+ * unfused in torch bf16. */
+int fd_rms_norm_modulate_ranges(const void* x, const void* w, int w_dtype, const void* scale,
+                                int scale_dtype, void* out, int64_t rows, int64_t dim, float eps,
+                                const int32_t* range_rows, const int32_t* range_param,
+                                int64_t n_ranges, int64_t n_params, void* stream);
+int fd_rms_norm_modulate_quant_ranges(const void* x, const void* w, int w_dtype, const void* scale,
+                                      int scale_dtype, void* y, float* y_s, int64_t rows, int64_t dim,
+                                      float eps, const int32_t* range_rows, const int32_t* range_param,
+                                      int64_t n_ranges, int64_t n_params, void* stream);
+int fd_rms_norm_gate_residual_ranges(const void* x, const void* w, int w_dtype, const void* gate,
+                                     int gate_dtype, const void* residual, void* out, int64_t rows,
+                                     int64_t dim, float eps, const int32_t* range_rows,
+                                     const int32_t* range_param, int64_t n_ranges, int64_t n_params,
+                                     void* stream);
 
 /* P3 -- fused_qkv_postprocess (src/futudiffu/fused_kernels.py:270-471).
  * qkv (B*S, 3*H*hd) bf16; qw, kw (hd) f32; freqs (B*S, hd/2, 2, 2) f32;

@@ -14,6 +14,11 @@ inputs and stores inputs and outputs as ``.pt`` files:
   silu_gate.pt         fp8_silu_gate_quant torch fallback            (fp8_kernels.py:1725-1747)
   fused_norms.pt       fused_kernels torch fallbacks + _qkv_postprocess_reference
                        (fused_kernels.py:479-541, :802-842) and attention.rope_embed
+  packing.pt           src_ii.bin_packer (BinPackScheduler on seeded item lists and
+                       plans, estimate_efficiency, the length constants),
+                       src_ii.transformer.build_packed_sequence / build_packed_rope
+                       / EmbedND, src_ii.forward_packed._pad_plan_to_fixed_len and
+                       the Euler update of src_ii.triumphant_future_reduction_ops
 
 Usage:  python tests/golden/make_golden.py --reference <path to the reference checkout>
 
@@ -84,6 +89,8 @@ def main_triton(ref: Path) -> None:
         torch.Tensor.cuda = saved  # type: ignore[assignment]
     torch.save({"w": w, "codes": q, "scales": s}, HERE / "weight_quant.pt")
 
+    main_packing(ref)
+
     # ---- fp8_act_quant Triton kernel in the CPU interpreter: scales only
     env = dict(os.environ, TRITON_INTERPRET="1")
     subprocess.run([sys.executable, __file__, "--reference", str(ref), "--section", "interp"],
@@ -91,6 +98,56 @@ def main_triton(ref: Path) -> None:
     # ---- torch fallbacks (Triton blocked)
     subprocess.run([sys.executable, __file__, "--reference", str(ref), "--section", "fallback"],
                    check=True)
+
+
+def main_packing(ref: Path) -> None:
+    import random
+
+    from src_ii import bin_packer as rbp
+    from src_ii import forward_packed as rfp
+    from src_ii import transformer as rt
+    from src_ii import triumphant_future_reduction_ops as rops
+
+    rng = random.Random(7)
+    item_lists = []
+    for n in (1, 5, 17, 40):
+        item_lists.append([{"id": i, "seq_len": rng.choice([96, 640, 1088, 2144, 4288, 5000, rng.randint(32, 4288)])}
+                           for i in range(n)])
+    sched = rbp.BinPackScheduler()
+    packs = [[[it["id"] for it in b] for b in sched.pack(items)] for items in item_lists]
+    effs = [sched.estimate_efficiency(sched.pack(items)) for items in item_lists]
+    sizes = [(1280, 832), (832, 1280), (1024, 1024), (512, 512), (640, 384), (256, 256), (320, 192), (448, 576)]
+    plan = [{"id": i, "width": w, "height": h, **({"cap_tokens": rng.randint(20, 200)} if i % 3 else {})}
+            for i, (w, h) in enumerate(rng.choice(sizes) for _ in range(23))]
+    plan_bins = [[(it["id"], it["seq_len"], it["img_seq_len"], it["cap_tokens"]) for it in b]
+                 for b in rbp.BinPackScheduler(max_seq_len=6000).pack_generation_plan(plan)]
+    training_items = [(i, f"s{i}", w, h) for i, (w, h) in enumerate(rng.choice(sizes) for _ in range(11))]
+    training = rbp.BinPackScheduler().pack_for_training(training_items)
+
+    g = _gen(6)
+    caps = [torch.randn(1, n, 16, generator=g) for n in (40, 113, 7)]
+    grids = [(12, 16), (8, 8), (4, 6)]
+    imgs = [torch.randn(1, h * w, 16, generator=g) for h, w in grids]
+    cap_pad, x_pad = torch.randn(16, generator=g), torch.randn(16, generator=g)
+    packed, info = rt.build_packed_sequence(caps, imgs, grids, [40, 113, 7], 32, cap_pad, x_pad)
+    rope = rt.build_packed_rope(info, rt.EmbedND(128, 256.0, [32, 48, 48]), 32, torch.device("cpu"))
+    seg_doc = info.document_id.clone()
+    info_p, rope_p = rfp._pad_plan_to_fixed_len(info, rope, 768)
+
+    x = torch.randn(2, 16, 8, 8, generator=g)
+    guided = torch.randn(2, 16, 8, 8, generator=g)
+    euler = rops.euler_step(x, guided, torch.tensor(0.7), torch.tensor(0.55))
+    denoised = rops.denoise_all([x, guided], [guided, x], [torch.tensor(0.3), torch.tensor(0.9)])
+
+    torch.save({
+        "constants": (rbp.REFERENCE_SEQ_LEN, rbp.DEFAULT_CAP_TOKENS, rbp.REFERENCE_TOTAL_LEN),
+        "item_lists": item_lists, "packs": packs, "effs": effs,
+        "plan": plan, "plan_bins": plan_bins, "training_items": training_items, "training": training,
+        "caps": caps, "imgs": imgs, "grids": grids, "cap_pad": cap_pad, "x_pad": x_pad,
+        "packed": packed, "segments": info.segments, "document_id": seg_doc, "rope": rope,
+        "doc_padded": info_p.document_id, "rope_padded_shape": tuple(rope_p.shape),
+        "x": x, "guided": guided, "euler": euler, "denoised": denoised,
+    }, HERE / "packing.pt")
 
 
 def main_interp(ref: Path) -> None:
