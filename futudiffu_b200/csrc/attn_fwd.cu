@@ -13,12 +13,15 @@
 //              thread), exp2, row sum, write P to shared memory; rescale their
 //              half of the O row in TMEM when the running max moves.
 //   warp 8     TMA producer: Q once, then K (+ per-token K scales) and V
-//              tiles of 128 keys into a 2-stage ring.
+//              tiles of 128 keys into K and V rings (2 stages each for e4m3 V,
+//              1 each for bf16 V); a K stage is released when its QK^T is
+//              done, a V stage when its PV is done.
 //   warp 9     MMA issuer: S = Q K^T (kind::i8 -> s32, or kind::f8f6f4 -> f32)
 //              and O += P V (kind::f8f6f4 e4m3, or kind::f16 bf16).
-// TMEM: S at columns [0,128), O at [128,256).  Two CTAs fit on one SM
-// (fp8 PV), so one CTA's softmax overlaps the other's MMAs; inside a CTA the
-// next S = Q K^T is issued as soon as the softmax has pulled S into registers.
+// TMEM: S at columns [0,128), O at [128,256).  Two CTAs fit on one SM (the
+// bf16-V variant by keeping one K and one V stage: 102 KiB of shared memory), so
+// one CTA's softmax overlaps the other's MMAs; inside a CTA the next S = Q K^T is
+// issued as soon as the softmax has pulled S into registers.
 //
 // Running-max threshold: O is rescaled only when a row max grows by more
 // than TAU (log2 units) over the reference max used for exp2, so P <= 2^TAU
@@ -35,7 +38,14 @@ namespace attn {
 constexpr int BQ = 128;   // query rows per CTA
 constexpr int BKV = 128;  // keys per KV tile
 constexpr int HD = 128;
-constexpr int KST = 2;    // K/V pipeline stages
+// K and V pipeline stages: 2 with e4m3 V (16 KiB per V tile); 1 with bf16 V
+// (32 KiB) so that two CTAs still fit on one SM.
+constexpr int kv_stages(int pv) { return pv == FD_PV_FP8 ? 2 : 1; }
+// Per-token K scale slots: tile i uses slot i % (stages + 2).  The K stage of tile
+// i is free once QK^T(i - stages) is done, which was issued after the softmax of
+// tile i - stages - 1 released S, i.e. after the softmax of tile i - stages - 2
+// (the previous user of the slot) had finished reading its scales.
+constexpr int kd_slots(int pv) { return kv_stages(pv) + 2; }
 constexpr int NUM_SOFTMAX_WARPS = 8;  // two threads per query row, 64 keys each
 constexpr int WARP_TMA = 8, WARP_MMA = 9;
 constexpr int NUM_THREADS = 320;
@@ -94,6 +104,8 @@ FD_DEV float max_reduce64(const float* x) {
 
 template <int PV>
 struct Smem {
+  static constexpr int KST = kv_stages(PV);
+  static constexpr int KDS = kd_slots(PV);
   static constexpr uint32_t Q_BYTES = BQ * HD;                           // int8/e4m3 codes
   static constexpr uint32_t K_BYTES = BKV * HD;
   static constexpr uint32_t V_BYTES = BKV * HD * (PV == FD_PV_FP8 ? 1 : 2);
@@ -102,8 +114,8 @@ struct Smem {
   static constexpr uint32_t OFF_K = OFF_Q + Q_BYTES;
   static constexpr uint32_t OFF_V = OFF_K + KST * K_BYTES;
   static constexpr uint32_t OFF_P = OFF_V + KST * V_BYTES;
-  static constexpr uint32_t OFF_KD = OFF_P + P_BYTES;                    // KST x 128 f32
-  static constexpr uint32_t OFF_VD = OFF_KD + KST * 512;                 // 128 f32
+  static constexpr uint32_t OFF_KD = OFF_P + P_BYTES;                    // KDS x 128 f32 (per-token K)
+  static constexpr uint32_t OFF_VD = OFF_KD + KDS * 512;                 // 128 f32
   static constexpr uint32_t OFF_RED = OFF_VD + 512;                      // row max / sum exchange
   static constexpr uint32_t OFF_BAR = OFF_RED + (2 * 2 * 128 + 2 * 128) * 4;
   static constexpr uint32_t TOTAL = OFF_BAR + 256 + 1024;               // + barriers, align slack
@@ -266,10 +278,11 @@ FD_DEV float chunk_exp_store(const uint32_t (&r)[32], int col0, int N, bool half
 
 // QK: FD_QK_INT8 / FD_QK_FP8; KG: k granularity; PV: FD_PV_BF16 / FD_PV_FP8
 template <int QK, int KG, int PV>
-__global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
+__global__ void __launch_bounds__(NUM_THREADS, 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const Params p) {
   using SM = Smem<PV>;
+  constexpr int KST = SM::KST, KDS = SM::KDS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + SM::OFF_Q;
@@ -282,8 +295,10 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
   uint64_t* bQ = bars + 0;
   uint64_t* bKfull = bars + 1;            // [KST]
   uint64_t* bVfull = bars + 1 + KST;      // [KST]
-  uint64_t* bKVempty = bars + 1 + 2 * KST;  // [KST]
-  uint64_t* bSfull = bars + 1 + 3 * KST;
+  uint64_t* bKempty = bars + 1 + 2 * KST; // [KST] QK^T done with the K stage
+  uint64_t* bVempty = bars + 1 + 3 * KST; // [KST] PV done with the V stage
+  uint64_t* bKdfull = bars + 1 + 4 * KST; // [KDS] per-token K scales of tile i in slot i % KDS
+  uint64_t* bSfull = bKdfull + KDS;
   uint64_t* bSfree = bSfull + 1;
   uint64_t* bPfull = bSfull + 2;
   uint64_t* bOready = bSfull + 3;
@@ -301,8 +316,10 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
     for (int s = 0; s < KST; ++s) {
       mbar_init(&bKfull[s], 1);
       mbar_init(&bVfull[s], 1);
-      mbar_init(&bKVempty[s], 1);
+      mbar_init(&bKempty[s], 1);
+      mbar_init(&bVempty[s], 1);
     }
+    for (int s = 0; s < KDS; ++s) mbar_init(&bKdfull[s], 1);
     mbar_init(bSfull, 1);
     mbar_init(bSfree, NUM_SOFTMAX_WARPS);
     mbar_init(bPfull, NUM_SOFTMAX_WARPS);
@@ -330,17 +347,22 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
       mbar_arrive_expect_tx(bQ, SM::Q_BYTES);
       tma_load_3d(sQ, &tmQ, bQ, 0, q0, bh);
       uint32_t i = 0;
-      uint32_t issued = 0;
+      uint32_t issued = 0, v_issued = 0;  // tiles whose K / V copies were issued
       for (int j = 0; j < p.n_kv_tiles; ++j) {
         if (!tile_valid(p, bh, qb, j)) continue;
         const uint32_t s = i % KST, use = i / KST;
-        if (!mbar_wait(&bKVempty[s], (use & 1) ^ 1, abort_flag)) break;
-        const uint32_t kbytes = SM::K_BYTES + (KG == FD_GRAN_TOKEN ? 512u : 0u);
-        mbar_arrive_expect_tx(&bKfull[s], kbytes);
+        if (!mbar_wait(&bKempty[s], (use & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&bKfull[s], SM::K_BYTES);
         tma_load_3d(sK + s * SM::K_BYTES, &tmK, &bKfull[s], 0, j * BKV, bh);
-        if (KG == FD_GRAN_TOKEN)
-          bulk_load(sKd + s * 128, p.k_desc + (int64_t)bh * p.k_desc_stride + (int64_t)j * BKV, 512,
-                    &bKfull[s]);
+        if (KG == FD_GRAN_TOKEN) {
+          const uint32_t ks = i % KDS;  // free: see kd_slots
+          mbar_arrive_expect_tx(&bKdfull[ks], 512);
+          bulk_load(sKd + ks * 128, p.k_desc + (int64_t)bh * p.k_desc_stride + (int64_t)j * BKV, 512,
+                    &bKdfull[ks]);
+        }
+        ++i;
+        issued = i;
+        if (!mbar_wait(&bVempty[s], (use & 1) ^ 1, abort_flag)) break;
         mbar_arrive_expect_tx(&bVfull[s], SM::V_BYTES);
         if (PV == FD_PV_FP8) {
           tma_load_3d(sV + s * SM::V_BYTES, &tmV, &bVfull[s], 0, j * BKV, bh);
@@ -348,16 +370,20 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
           tma_load_3d(sV + s * SM::V_BYTES, &tmV, &bVfull[s], 0, j * BKV, bh);
           tma_load_3d(sV + s * SM::V_BYTES + BKV * 128, &tmV, &bVfull[s], 64, j * BKV, bh);
         }
-        ++i;
-        issued = i;
+        v_issued = i;
       }
-      // drain: every stage's newest loads must have landed
+      // drain: every stage's newest loads must have landed (the last tile's V
+      // may not have been issued if its wait gave up)
       drain_wait(bQ, 0);
       for (uint32_t k = 0; k < (uint32_t)KST && k < issued; ++k) {
         const uint32_t last = issued - 1 - k;
         const uint32_t s = last % KST, ph = (last / KST) & 1;
         drain_wait(&bKfull[s], ph);
-        drain_wait(&bVfull[s], ph);
+        if (v_issued > last) drain_wait(&bVfull[s], ph);
+      }
+      for (uint32_t k = 0; KG == FD_GRAN_TOKEN && k < (uint32_t)KDS && k < issued; ++k) {
+        const uint32_t last = issued - 1 - k;
+        drain_wait(&bKdfull[last % KDS], (last / KDS) & 1);
       }
     }
   } else if (warp == WARP_MMA) {
@@ -390,6 +416,7 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
           if (QK == FD_QK_INT8) mma_i8_ss(tS, ad, bd, idesc_qk, 1u);  // onto S_BIAS_BITS
           else mma_f8f6f4_ss(tS, ad, bd, idesc_qk, k > 0);
         }
+        tc_commit(&bKempty[s]);  // the K stage is free once these MMAs are done
         tc_commit(bSfull);
         return true;
       };
@@ -430,7 +457,7 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
             mma_f16_ss(tO, ad, bd, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
           }
         }
-        tc_commit(&bKVempty[s]);
+        tc_commit(&bVempty[s]);
         tc_commit(bOready);
         ++i;
         jcur = jn;
@@ -470,7 +497,6 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
     bool ok = true;
     for (int j = 0; j < p.n_kv_tiles && ok; ++j) {
       if (!tile_valid(p, bh, qb, j)) continue;
-      const uint32_t s = i % KST, use = i / KST;
       const int col0 = j * BKV + cb;  // first key of this thread's half-tile
       bool my_half_ok = true, other_half_ok = true;
       if (p.mask) {
@@ -488,10 +514,10 @@ __global__ void __launch_bounds__(NUM_THREADS, (PV == FD_PV_FP8 ? 2 : 1))
       }
       if (!mbar_wait(bSfull, i & 1, abort_flag)) { ok = false; break; }
       if (KG == FD_GRAN_TOKEN) {
-        if (!mbar_wait(&bKfull[s], use & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&bKdfull[i % KDS], (i / KDS) & 1, abort_flag)) { ok = false; break; }
       }
       tc_fence_after();
-      const float* kd = sKd + s * 128 + cb;  // per-token K scales of this thread's keys
+      const float* kd = sKd + (i % KDS) * 128 + cb;  // per-token K scales of this thread's keys
       // ---- pass 1: row max over this thread's 64 keys (two 32-key chunks from TMEM)
       float mloc;
       {
