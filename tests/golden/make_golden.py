@@ -14,6 +14,8 @@ inputs and stores inputs and outputs as ``.pt`` files:
   silu_gate.pt         fp8_silu_gate_quant torch fallback            (fp8_kernels.py:1725-1747)
   fused_norms.pt       fused_kernels torch fallbacks + _qkv_postprocess_reference
                        (fused_kernels.py:479-541, :802-842) and attention.rope_embed
+  checkpoint.pt        futudiffu.fp8.quantize_model on a small safetensors state dict
+                       (device transfer made an identity): every output tensor
   packing.pt           src_ii.bin_packer (BinPackScheduler on seeded item lists and
                        plans, estimate_efficiency, the length constants),
                        src_ii.transformer.build_packed_sequence / build_packed_rope
@@ -90,6 +92,7 @@ def main_triton(ref: Path) -> None:
     torch.save({"w": w, "codes": q, "scales": s}, HERE / "weight_quant.pt")
 
     main_packing(ref)
+    main_checkpoint(ref)
 
     # ---- fp8_act_quant Triton kernel in the CPU interpreter: scales only
     env = dict(os.environ, TRITON_INTERPRET="1")
@@ -98,6 +101,36 @@ def main_triton(ref: Path) -> None:
     # ---- torch fallbacks (Triton blocked)
     subprocess.run([sys.executable, __file__, "--reference", str(ref), "--section", "fallback"],
                    check=True)
+
+
+def main_checkpoint(ref: Path) -> None:
+    import tempfile
+
+    from safetensors.torch import load_file, save_file
+
+    from futudiffu import fp8 as rfp8
+
+    g = _gen(8)
+    sd = {
+        "blocks.0.attn.qkv.weight": (torch.randn(384, 128, generator=g) * 0.02).to(torch.bfloat16),
+        "blocks.0.attn.out.weight": (torch.randn(128, 128, generator=g) * 0.02).to(torch.float16),
+        "blocks.0.attn.out.bias": torch.randn(128, generator=g).to(torch.bfloat16),
+        "blocks.0.mlp.w2.weight": torch.randn(128, 256, generator=g) * 0.05,
+        "blocks.0.odd.weight": (torch.randn(200, 128, generator=g) * 0.02).to(torch.bfloat16),
+        "blocks.0.small.weight": (torch.randn(16, 128, generator=g)).to(torch.bfloat16),
+        "blocks.0.steps": torch.arange(7, dtype=torch.int64),
+    }
+    saved = torch.Tensor.cuda
+    torch.Tensor.cuda = lambda self, *a, **kw: self  # type: ignore[assignment]
+    try:
+        with tempfile.TemporaryDirectory() as d:
+            src, dst = f"{d}/in.safetensors", f"{d}/out.safetensors"
+            save_file(sd, src)
+            stats = rfp8.quantize_model(src, dst)
+            out = load_file(dst)
+    finally:
+        torch.Tensor.cuda = saved  # type: ignore[assignment]
+    torch.save({"input": sd, "output": dict(out), "stats": stats}, HERE / "checkpoint.pt")
 
 
 def main_packing(ref: Path) -> None:
