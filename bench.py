@@ -320,14 +320,14 @@ def run_ours(args, world, rank, local):
 # ------------------------------------------------------------------ config 4: DiT denoise
 DIT_BATCH = 8
 DIT_METRIC = "DiT denoise steps/s (12B-class, 19 double + 38 single blocks, 4096+512 tokens, batch 8)"
-KERNELS_PER_CALL = {"fd_attn_quant": 2, "fd_attn_quant_noalloc": 2}
+KERNELS_PER_CALL = {"fd_attn_quant": 3, "fd_attn_quant_noalloc": 3}
 
 
 class LaunchRecorder:
     """Counts this library's kernel launches and times every GEMM / attention
     launch with CUDA events on the launching stream while ``active``."""
 
-    GEMMS = ("fd_fp8_gemm_blockwise", "fd_fp8_gemm_quant")
+    GEMMS = ("fd_fp8_gemm_blockwise", "fd_fp8_gemm_quant", "fd_fp8_gemm_quant_ld")
 
     def __init__(self):
         from futudiffu_b200 import _lib as L
@@ -350,6 +350,9 @@ class LaunchRecorder:
             kind, work = "gemm", 2.0 * M * N * K * mult
         elif name in ("fd_sage_attn_fwd", "fd_sage_attn_fwd_bnhd"):
             BH, N = args[10], args[11]
+            kind, work = "attn", 4.0 * BH * N * N * 128
+        elif name == "fd_sage_attn_fwd_quant_out":
+            BH, N = args[9], args[10]
             kind, work = "attn", 4.0 * BH * N * N * 128
         if kind is None:
             return self.orig(name, *args)

@@ -56,6 +56,7 @@ _SIGS: dict[str, list] = {
     "fd_fp8_dequant_blockwise": [_P, _P, _P, _I, _L, _L, _I, _P],
     "fd_fp8_gemm_blockwise": [_P, _P, _P, _P, _P, _I, _P, _I, _L, _L, _L, _I, _P],
     "fd_fp8_gemm_quant": [_P, _P, _P, _P, _P, _I, _P, _P, _L, _L, _L, _I, _P],
+    "fd_fp8_gemm_quant_ld": [_P, _P, _P, _P, _P, _I, _P, _P, _L, _L, _L, _I, _L, _L, _P],
     "fd_fp8_gemm_blockwise_lora": [_P, _P, _P, _P, _P, _I, _P, _I, _L, _L, _L, _P, _P, _L, _P],
     "fd_fp8_silu_gate_quant": [_P, _P, _P, _L, _L, _I, _P],
     "fd_fp8_gelu_tanh_quant": [_P, _P, _P, _L, _L, _I, _P],
@@ -74,6 +75,8 @@ _SIGS: dict[str, list] = {
     "fd_attn_quant_noalloc": [_P, _P, _P, _L, _L, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P],
     "fd_sage_attn_fwd": [_P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _L, _L, _I, _I, _I, _I, _P],
     "fd_sage_attn_fwd_bnhd": [_P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _L, _L, _L, _I, _I, _I, _I, _P],
+    "fd_sage_attn_fwd_quant_out": [_P, _P, _P, _P, _P, _P, _P, _L, _P, _L, _L, _L, _I, _I, _I, _I,
+                                   _P, _P, _L, _L, _P, _P, _L, _L, _L, _P],
     "fd_sage_attn_bwd_prepass": [_P, _P, _P, _L, _L, _P],
     "fd_sage_attn_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _P, _L, _L, _I, _F, _P],
 }

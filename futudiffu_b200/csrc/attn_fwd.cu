@@ -29,7 +29,7 @@
 // P8 = e4m3(p * 448 / 4) and undone in the epilogue).  Results equal the reference online
 // softmax up to fp32 rounding (exp2 is shift-exact in bf16 / e4m3 up to
 // rounding of the argument).
-#include "fd_common.cuh"
+#include "fd_act.cuh"
 #include "fd_host.h"
 
 namespace fd {
@@ -136,6 +136,16 @@ struct Params {
   int64_t q_desc_stride;
   int64_t k_desc_stride;
   int64_t out_heads;  // 0: out is (BH, N, 128); H > 0: out is (BH / H, N, H, 128)
+  // Quantised output (qout != nullptr, out_heads = H): each row's 128 head values
+  // are one 1 x 128 group of the output linear's input, written as e4m3 codes +
+  // an fp32 dequant scale.  Rows n < split go to region 0, rows n >= split to
+  // region 1; in region r, sample b's row n sits at row b * rows_r + (n - start_r)
+  // with `qstride[r]` code bytes and `sstride[r]` scales per row.
+  uint8_t* qout[2];
+  float* qscale[2];
+  int64_t qstride[2];
+  int64_t sstride[2];
+  int split;
 };
 
 FD_DEV void named_bar_sync(int id, int nthreads) {
@@ -595,14 +605,75 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     red_l[h * 128 + row] = l;
     named_bar_sync(2 + quad, 64);
     const float l_tot = l + red_l[(h ^ 1) * 128 + row];
-    if (ok) {
-      tc_fence_after();
-      const bool any = i > 0;
-      // reference: LSE = m + log2(l) (tl.math.log2 == log2f), out = o / l (Triton f32 divide)
-      const float lse_v = any ? m_ref + (log2f(l_tot) - PScale<PV>::LOG2_SCALE) : -INFINITY;
-      const float l_div = any ? l_tot : 0.f;  // 0/0 -> NaN for rows that saw no key, as the reference
-      const bool row_ok = qrow < p.N;
-      if (row_ok && h == 0 && p.lse) p.lse[(int64_t)bh * p.N + qrow] = lse_v;
+    if (ok) tc_fence_after();
+    const bool any = i > 0;
+    // reference: LSE = m + log2(l) (tl.math.log2 == log2f), out = o / l (Triton f32 divide)
+    const float lse_v = any ? m_ref + (log2f(l_tot) - PScale<PV>::LOG2_SCALE) : -INFINITY;
+    const float l_div = any ? l_tot : 0.f;  // 0/0 -> NaN for rows that saw no key, as the reference
+    const bool row_ok = qrow < p.N;
+    if (ok && row_ok && h == 0 && p.lse) p.lse[(int64_t)bh * p.N + qrow] = lse_v;
+    // this thread's 64 output values of chunk cc (32 each), O / l, as fp32
+    auto load_out = [&](int cc, float (&o)[32]) {
+      uint32_t r[32];
+      if (any) {
+        tmem_ld32(tO + lane_base + cb + cc * 32, r);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) r[e] = 0u;
+      }
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        float v = __uint_as_float(r[e]);
+        if (PV == FD_PV_FP8) v *= sVd[cb + cc * 32 + e];  // O and l carry the P scale; V carries v_desc
+        o[e] = div_full(v, l_div);
+      }
+    };
+    if (p.qout[0]) {
+      // Quantised output: O / l rounded to bf16 (the values the bf16 store would
+      // hold), then the 1 x 128 quantiser over the row's 128 head values, which
+      // two threads hold: codes and scale equal fp8_act_quant of the bf16 output.
+      // Two TMEM passes (amax, then codes) keep the register count down; the
+      // partner exchange runs whether or not this thread's waits succeeded.
+      const int64_t b = bh / p.out_heads, hh = bh % p.out_heads;
+      const int n = row_ok ? qrow : 0;
+      const int rg = n < p.split ? 0 : 1;
+      const int64_t rows_r = rg == 0 ? p.split : p.N - p.split;
+      const int64_t qr = b * rows_r + (rg == 0 ? n : n - p.split);
+      float amax = 0.f;
+      if (ok) {
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          float o[32];
+          load_out(cc, o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(round_to_bf16(o[e])));
+        }
+      }
+      red_max[h * 128 + row] = amax;
+      named_bar_sync(2 + quad, 64);
+      amax = fmaxf(amax, red_max[(h ^ 1) * 128 + row]);
+      if (ok) {
+        const float qm = quant_mult(amax);
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          float o[32];
+          load_out(cc, o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = round_to_bf16(o[e]);
+          if (row_ok) {
+            uint4* dst = reinterpret_cast<uint4*>(p.qout[rg] + qr * p.qstride[rg] + hh * HD + cb + cc * 32);
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+              dst[k] = make_uint4(quant4(o[16 * k], o[16 * k + 1], o[16 * k + 2], o[16 * k + 3], qm),
+                                  quant4(o[16 * k + 4], o[16 * k + 5], o[16 * k + 6], o[16 * k + 7], qm),
+                                  quant4(o[16 * k + 8], o[16 * k + 9], o[16 * k + 10], o[16 * k + 11], qm),
+                                  quant4(o[16 * k + 12], o[16 * k + 13], o[16 * k + 14], o[16 * k + 15], qm));
+          }
+        }
+        if (row_ok && h == 0) p.qscale[rg][qr * p.sstride[rg] + hh] = dequant_scale(amax);
+      }
+    } else if (ok) {
       const int64_t orow_idx = p.out_heads == 0
                                    ? (int64_t)bh * p.N + (row_ok ? qrow : 0)
                                    : ((int64_t)(bh / p.out_heads) * p.N + (row_ok ? qrow : 0)) * p.out_heads +
@@ -611,26 +682,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       // tcgen05.ld is warp-collective: every lane loads, only valid rows store
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
-        uint32_t r[32];
-        if (any) {
-          tmem_ld32(tO + lane_base + cb + cc * 32, r);
-          tmem_wait_ld();
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) r[e] = 0u;
-        }
-        uint32_t w[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float o0 = __uint_as_float(r[2 * e]);
-          float o1 = __uint_as_float(r[2 * e + 1]);
-          if (PV == FD_PV_FP8) {  // O and l both carry the P scale; V carries v_desc
-            o0 *= sVd[cb + cc * 32 + 2 * e];
-            o1 *= sVd[cb + cc * 32 + 2 * e + 1];
-          }
-          w[e] = pack_bf16x2(div_full(o0, l_div), div_full(o1, l_div));
-        }
+        float o[32];
+        load_out(cc, o);
         if (row_ok) {
+          uint32_t w[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) w[e] = pack_bf16x2(o[2 * e], o[2 * e + 1]);
           uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
           dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
           dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
@@ -669,19 +726,28 @@ using namespace fd;
 
 int64_t fd_desc_stride(int64_t N, int gran, int rows_per_block);
 
+struct QuantOut {
+  void* codes[2];
+  float* scales[2];
+  int64_t code_stride[2];
+  int64_t scale_stride[2];
+  int64_t split;
+};
+
 static int sage_attn_fwd_impl(const void* q_codes, const float* q_desc, const void* k_codes,
                                 const float* k_desc, const void* v, const float* v_desc,
                                 const uint8_t* block_mask, int64_t mask_bh_stride, void* out,
                                 float* lse, int64_t BH, int64_t N, int qk_kind, int q_gran,
-                                int k_gran, int pv_kind, int64_t out_heads, void* stream) {
+                                int k_gran, int pv_kind, int64_t out_heads, void* stream,
+                                const QuantOut* qo = nullptr) {
   FD_CHECK_ARG(BH > 0 && BH <= 65535 && N > 0 && N < (1ll << 30), "bad shape");
   FD_CHECK_ARG(qk_kind == FD_QK_INT8 || qk_kind == FD_QK_FP8, "bad qk_kind");
   FD_CHECK_ARG(q_gran == FD_GRAN_TOKEN || q_gran == FD_GRAN_BLOCK, "bad q_gran");
   FD_CHECK_ARG(k_gran == FD_GRAN_TOKEN || k_gran == FD_GRAN_BLOCK, "bad k_gran");
   FD_CHECK_ARG(pv_kind == FD_PV_BF16 || pv_kind == FD_PV_FP8, "bad pv_kind");
-  FD_CHECK_ARG(q_codes && q_desc && k_codes && k_desc && v && out, "null pointer");
+  FD_CHECK_ARG(q_codes && q_desc && k_codes && k_desc && v && (out || qo), "null pointer");
   FD_CHECK_ARG(pv_kind == FD_PV_BF16 || v_desc, "v_desc required for fp8 PV");
-  FD_CHECK_ARG(aligned16(q_codes) && aligned16(k_codes) && aligned16(v) && aligned16(out) &&
+  FD_CHECK_ARG(aligned16(q_codes) && aligned16(k_codes) && aligned16(v) && (qo || aligned16(out)) &&
                    aligned16(k_desc),
                "q/k/v codes, out and k_desc must be 16-byte aligned");
   CUtensorMap tq, tk, tv;
@@ -715,6 +781,26 @@ static int sage_attn_fwd_impl(const void* q_codes, const float* q_desc, const vo
   p.out = (__nv_bfloat16*)out;
   p.lse = lse;
   p.out_heads = out_heads;
+  p.qout[0] = p.qout[1] = nullptr;
+  p.qscale[0] = p.qscale[1] = nullptr;
+  p.qstride[0] = p.qstride[1] = p.sstride[0] = p.sstride[1] = 0;
+  p.split = (int)N;
+  if (qo) {
+    FD_CHECK_ARG(out_heads > 0 && BH % out_heads == 0, "quantised output needs H dividing BH");
+    FD_CHECK_ARG(qo->split >= 1 && qo->split <= N, "split must be in [1, N]");
+    for (int r = 0; r < (qo->split < N ? 2 : 1); ++r) {
+      FD_CHECK_ARG(qo->codes[r] && qo->scales[r], "null quantised-output pointer");
+      FD_CHECK_ARG(aligned16(qo->codes[r]) && qo->code_stride[r] % 16 == 0 &&
+                       qo->code_stride[r] >= out_heads * 128 && qo->scale_stride[r] >= out_heads,
+                   "codes must be 16-byte aligned with a row stride >= H * 128 (multiple of 16), "
+                   "scale row stride >= H");
+      p.qout[r] = (uint8_t*)qo->codes[r];
+      p.qscale[r] = qo->scales[r];
+      p.qstride[r] = qo->code_stride[r];
+      p.sstride[r] = qo->scale_stride[r];
+    }
+    p.split = (int)qo->split;
+  }
   p.N = (int)N;
   p.n_kv_tiles = (int)((N + 127) / 128);
   p.nkb64 = (int)((N + 63) / 64);
@@ -760,4 +846,32 @@ extern "C" int fd_sage_attn_fwd_bnhd(const void* q_codes, const float* q_desc, c
   FD_CHECK_ARG(H > 0 && BH % H == 0, "H must divide BH");
   return sage_attn_fwd_impl(q_codes, q_desc, k_codes, k_desc, v, v_desc, block_mask, mask_bh_stride, out,
                             lse, BH, N, qk_kind, q_gran, k_gran, pv_kind, H, stream);
+}
+
+// Attention whose output is written as the e4m3 1 x 128 codes + fp32 scales of the
+// output linear's input: row (b, n) of head h is the group [h * 128, h * 128 + 128)
+// of output row n.  Rows n < split go to (codes0, scales0), rows n >= split to
+// (codes1, scales1) (each region holds its rows of every sample contiguously),
+// with the given row strides (code bytes, scales).
+extern "C" int fd_sage_attn_fwd_quant_out(const void* q_codes, const float* q_desc, const void* k_codes,
+                                          const float* k_desc, const void* v, const float* v_desc,
+                                          const uint8_t* block_mask, int64_t mask_bh_stride, float* lse,
+                                          int64_t BH, int64_t N, int64_t H, int qk_kind, int q_gran,
+                                          int k_gran, int pv_kind, void* codes0, float* scales0,
+                                          int64_t code_stride0, int64_t scale_stride0, void* codes1,
+                                          float* scales1, int64_t code_stride1, int64_t scale_stride1,
+                                          int64_t split, void* stream) {
+  QuantOut qo;
+  qo.codes[0] = codes0;
+  qo.codes[1] = codes1;
+  qo.scales[0] = scales0;
+  qo.scales[1] = scales1;
+  qo.code_stride[0] = code_stride0;
+  qo.code_stride[1] = code_stride1;
+  qo.scale_stride[0] = scale_stride0;
+  qo.scale_stride[1] = scale_stride1;
+  qo.split = split;
+  FD_CHECK_ARG(H > 0, "H must be positive");
+  return sage_attn_fwd_impl(q_codes, q_desc, k_codes, k_desc, v, v_desc, block_mask, mask_bh_stride, nullptr,
+                            lse, BH, N, qk_kind, q_gran, k_gran, pv_kind, H, stream, &qo);
 }

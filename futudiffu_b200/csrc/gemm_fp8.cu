@@ -80,6 +80,8 @@ struct Params {
   int kblocks;
   int nbs;         // rows of b_s (BMODE 0: ceil(rows of B / 128)); BMODE 1: its columns
   int lora_slices; // 64-column bf16 LoRA slices after the FP8 slices (EPI_STORE, BMODE 0)
+  int64_t ldc;     // row stride of c in elements (N unless the output is a column window)
+  int64_t ldcs;    // row stride of c_s in scales (N / 128 likewise)
 };
 
 // Tile t -> (row tile, column tile), GROUP_M row tiles at a time so that the
@@ -369,8 +371,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       if constexpr (EPI == EPI_STORE) {
         if (ok && row_ok) {
-          store_row64<CDT>(p.c, (int64_t)m * p.N, n_lo, p.N, *reinterpret_cast<float(*)[64]>(acc));
-          store_row64<CDT>(p.c, (int64_t)m * p.N, n_lo + 64, p.N, *reinterpret_cast<float(*)[64]>(acc + 64));
+          store_row64<CDT>(p.c, (int64_t)m * p.ldc, n_lo, p.N, *reinterpret_cast<float(*)[64]>(acc));
+          store_row64<CDT>(p.c, (int64_t)m * p.ldc, n_lo + 64, p.N, *reinterpret_cast<float(*)[64]>(acc + 64));
         }
       } else if constexpr (EPI == EPI_SILU_GATE) {
         // the reference rounds the w1w3 GEMM output to bf16 before the gate
@@ -386,14 +388,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         amax = fmaxf(amax, rd[(h ^ 1) * 128 + r]);
         if (ok && row_ok) {
           const float qm = quant_mult(amax);
-          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.c) + (int64_t)m * p.N + nb * 128 + h * 64);
+          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.c) + (int64_t)m * p.ldc + nb * 128 + h * 64);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             dst[k] = make_uint4(quant4(acc[16 * k], acc[16 * k + 1], acc[16 * k + 2], acc[16 * k + 3], qm),
                                 quant4(acc[16 * k + 4], acc[16 * k + 5], acc[16 * k + 6], acc[16 * k + 7], qm),
                                 quant4(acc[16 * k + 8], acc[16 * k + 9], acc[16 * k + 10], acc[16 * k + 11], qm),
                                 quant4(acc[16 * k + 12], acc[16 * k + 13], acc[16 * k + 14], acc[16 * k + 15], qm));
-          if (h == 0) p.c_s[(int64_t)m * (p.N / 128) + nb] = dequant_scale(amax);
+          if (h == 0) p.c_s[(int64_t)m * p.ldcs + nb] = dequant_scale(amax);
         }
       } else {
         // EPI_QUANT / EPI_GELU_TANH: this thread's 128 columns are one whole output group
@@ -406,14 +408,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int i = 0; i < 128; ++i) amax = fmaxf(amax, fabsf(acc[i]));
         if (ok && row_ok && n_lo < p.N) {
           const float qm = quant_mult(amax);
-          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.c) + (int64_t)m * p.N + n_lo);
+          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.c) + (int64_t)m * p.ldc + n_lo);
 #pragma unroll
           for (int k = 0; k < 8; ++k)
             dst[k] = make_uint4(quant4(acc[16 * k], acc[16 * k + 1], acc[16 * k + 2], acc[16 * k + 3], qm),
                                 quant4(acc[16 * k + 4], acc[16 * k + 5], acc[16 * k + 6], acc[16 * k + 7], qm),
                                 quant4(acc[16 * k + 8], acc[16 * k + 9], acc[16 * k + 10], acc[16 * k + 11], qm),
                                 quant4(acc[16 * k + 12], acc[16 * k + 13], acc[16 * k + 14], acc[16 * k + 15], qm));
-          p.c_s[(int64_t)m * (p.N / 128) + n_lo / 128] = dequant_scale(amax);
+          p.c_s[(int64_t)m * p.ldcs + n_lo / 128] = dequant_scale(amax);
         }
       }
     }
@@ -525,6 +527,8 @@ extern "C" int fd_fp8_gemm_blockwise(const void* a, const float* a_s, const void
   p.c = c;
   p.c_s = nullptr;
   p.lora_slices = 0;
+  p.ldc = N;
+  p.ldcs = N / 128;
   p.M = (int)M;
   p.N = (int)N;
   p.K = (int)K;
@@ -542,9 +546,9 @@ extern "C" int fd_fp8_gemm_blockwise(const void* a, const float* a_s, const void
 // GEMM with a quantising epilogue (see the header of this file): act 0 requantises
 // the fp32 accumulator (fp8_gemm_quant), 1 applies GELU(tanh) to the bf16 GEMM
 // output first, 2 is the SiLU gate with b = [w1; w3] of shape (2 N, K).
-extern "C" int fd_fp8_gemm_quant(const void* a, const float* a_s, const void* b, const float* b_s,
-                                 const void* bias, int bias_dtype, void* c, float* c_s, int64_t M,
-                                 int64_t N, int64_t K, int act, void* stream) {
+static int gemm_quant_impl(const void* a, const float* a_s, const void* b, const float* b_s, const void* bias,
+                           int bias_dtype, void* c, float* c_s, int64_t M, int64_t N, int64_t K, int act,
+                           int64_t ldc, int64_t ldcs, void* stream) {
   FD_CHECK_ARG(M >= 0 && N > 0 && K > 0, "bad shape");
   FD_CHECK_ARG(K % 128 == 0, "K must be a multiple of 128");
   FD_CHECK_ARG(N % 128 == 0, "N must be a multiple of 128 (1 x 128 output groups)");
@@ -585,12 +589,31 @@ extern "C" int fd_fp8_gemm_quant(const void* a, const float* a_s, const void* b,
   p.ntn = act == FD_ACT_SILU_GATE ? (int)(N / 128) : (int)((N + 255) / 256);
   p.nbs = (int)(nb_rows / 128);
   p.lora_slices = 0;
+  p.ldc = ldc;
+  p.ldcs = ldcs;
   p.ntiles = p.ntm * p.ntn;
   p.kblocks = (int)(K / 128);
   cudaStream_t st = (cudaStream_t)stream;
   if (act == FD_ACT_NONE) return gemm::launch_quant<gemm::EPI_QUANT>(bias_dtype, ta, tb, p, st);
   if (act == FD_ACT_GELU_TANH) return gemm::launch_quant<gemm::EPI_GELU_TANH>(bias_dtype, ta, tb, p, st);
   return gemm::launch_quant<gemm::EPI_SILU_GATE>(bias_dtype, ta, tb, p, st);
+}
+
+extern "C" int fd_fp8_gemm_quant(const void* a, const float* a_s, const void* b, const float* b_s,
+                                 const void* bias, int bias_dtype, void* c, float* c_s, int64_t M,
+                                 int64_t N, int64_t K, int act, void* stream) {
+  return gemm_quant_impl(a, a_s, b, b_s, bias, bias_dtype, c, c_s, M, N, K, act, N, N / 128, stream);
+}
+
+// fd_fp8_gemm_quant writing into a column window of wider code / scale rows:
+// row m of the output starts at c + m * ldc (codes) and c_s + m * ldcs (scales),
+// e.g. the second half of the [attention | MLP] input of a fused output linear.
+extern "C" int fd_fp8_gemm_quant_ld(const void* a, const float* a_s, const void* b, const float* b_s,
+                                    const void* bias, int bias_dtype, void* c, float* c_s, int64_t M,
+                                    int64_t N, int64_t K, int act, int64_t ldc, int64_t ldcs, void* stream) {
+  FD_CHECK_ARG(ldc >= N && ldc % 16 == 0 && ldcs >= N / 128, "ldc must be >= N and a multiple of 16, ldcs >= N / 128");
+  FD_CHECK_ARG(aligned16(c), "c must be 16-byte aligned");
+  return gemm_quant_impl(a, a_s, b, b_s, bias, bias_dtype, c, c_s, M, N, K, act, ldc, ldcs, stream);
 }
 
 // FP8 block GEMM (b_layout 0) plus the multi-LoRA delta lora_a @ lora_b^T in the same
@@ -660,5 +683,7 @@ extern "C" int fd_fp8_gemm_blockwise_lora(const void* a, const float* a_s, const
   p.ntiles = p.ntm * p.ntn;
   p.kblocks = (int)(K / 128);
   p.lora_slices = (int)(lora_k / 64);
+  p.ldc = N;
+  p.ldcs = N / 128;
   return gemm::launch_c<0, true>(c_dtype, bias_dtype, ta, tb, p, (cudaStream_t)stream, &tla, &tlb);
 }

@@ -50,7 +50,7 @@ from .fused_kernels import (
     fused_rms_norm_modulate_quant,
     qkv_postprocess_into,
 )
-from .sage_attention import _attn_forward
+from .sage_attention import _attn_forward, attn_forward_quant_out
 
 HEAD_DIM = 128
 
@@ -157,6 +157,13 @@ def joint_attention(q: Tensor, k: Tensor, v: Tensor, cfg: DiTConfig) -> Tensor:
     return o
 
 
+def joint_attention_codes(q: Tensor, k: Tensor, v: Tensor, cfg: DiTConfig, regions, split=None) -> None:
+    """Quantized attention written straight as the output linears' 1 x 128 e4m3
+    input (codes + scales) into ``regions`` (see attn_forward_quant_out)."""
+    attn_forward_quant_out(q, k, v, None, block_mask=None, qk_quant=cfg.qk_quant, pv_quant=cfg.pv_quant,
+                           granularity=cfg.granularity, regions=regions, split=split)
+
+
 class _Stream(nn.Module):
     """Weights of one stream of a double-stream block."""
 
@@ -207,11 +214,15 @@ class DoubleStreamBlock(nn.Module):
             h8, h_s = fused_rms_norm_modulate_quant(x, st.norm_w[0], m[0].contiguous(), cfg.eps)
             qkv = gemm_bf16(h8, h_s, st.qkv)
             qkv_postprocess_into(qkv, st.q_norm, st.k_norm, fr, q, k, v, off, cfg.eps)
-        o = joint_attention(q, k, v, cfg)
-        o_txt, o_img = o.split([x_txt.shape[1], x_img.shape[1]], dim=1)
+        # attention output as each stream's out-projection input: text rows to one
+        # code buffer, image rows to the other (no split copy, no separate quantiser)
+        dev, D = x_txt.device, cfg.hidden
+        codes = [(torch.empty(B, n, D, dtype=torch.float8_e4m3fn, device=dev),
+                  torch.empty(B, n, D // 128, dtype=torch.float32, device=dev)) for n in (Nt, N - Nt)]
+        joint_attention_codes(q, k, v, cfg, codes, split=Nt)
         outs = []
-        for st, x, o_s, m in ((self.txt, x_txt, o_txt, mods[0]), (self.img, x_img, o_img, mods[1])):
-            a = linear_bf16(o_s.contiguous(), st.proj)
+        for st, x, (o8, o_sc), m in ((self.txt, x_txt, codes[0], mods[0]), (self.img, x_img, codes[1], mods[1])):
+            a = gemm_bf16(o8, o_sc, st.proj)
             x = fused_rms_norm_gate_residual(a, st.norm_w[1], m[1].contiguous(), x, cfg.eps)
             h8, h_s = fused_rms_norm_modulate_quant(x, st.norm_w[2], m[2].contiguous(), cfg.eps)
             f = mlp_fp8_q(h8, h_s, st.mlp_in, st.mlp_out)
@@ -249,13 +260,14 @@ class SingleStreamBlock(nn.Module):
         w, ws = self.linear1.weight, self.linear1.weight_scale
         n_qkv = 3 * D
         qkv = fp8_gemm_blockwise(a8, a_s, w[:n_qkv], ws[: n_qkv // 128], output_dtype=torch.bfloat16)
-        m8, m_s = fp8_gemm_gelu_tanh_quant(a8, a_s, w[n_qkv:], ws[n_qkv // 128:])
+        # linear2's input [attention | MLP] as 1 x 128 codes: the GELU GEMM and the
+        # attention write their halves of the same rows in place
+        W = self.linear2.weight.shape[1]
+        cat8 = torch.empty(B, N, W, dtype=torch.float8_e4m3fn, device=x.device)
+        cat_s = torch.empty(B, N, W // 128, dtype=torch.float32, device=x.device)
+        fp8_gemm_gelu_tanh_quant(a8, a_s, w[n_qkv:], ws[n_qkv // 128:], out=(cat8[..., D:], cat_s[..., D // 128:]))
         q, k, v = fused_qkv_postprocess(qkv, self.q_norm, self.k_norm, freqs, cfg.heads, HEAD_DIM, cfg.eps)
-        o = joint_attention(q, k, v, cfg)
-        o8, o_s = fp8_act_quant(o)
-        # the 1 x 128 blocks of both halves concatenate along K: one GEMM for linear2
-        cat8 = torch.cat([o8.view(torch.uint8), m8.view(torch.uint8)], dim=-1).view(torch.float8_e4m3fn)
-        cat_s = torch.cat([o_s, m_s], dim=-1)
+        joint_attention_codes(q, k, v, cfg, [(cat8[..., :D], cat_s[..., :D // 128])])
         y = fp8_gemm_blockwise(cat8, cat_s, self.linear2.weight, self.linear2.weight_scale,
                                output_dtype=torch.bfloat16)
         return fused_rms_norm_gate_residual(y, self.norm_w[1], gate.contiguous(), x, cfg.eps)

@@ -251,19 +251,28 @@ def fp8_gemm_quant(
     return _gemm_quant(a, a_s, b, b_s, None, L.ACT_NONE, M, N, K, batch_shape, out_dtype)
 
 
-def _gemm_quant(a, a_s, b, b_s, bias, act, M, N, K, batch_shape, out_dtype):
+def _gemm_quant(a, a_s, b, b_s, bias, act, M, N, K, batch_shape, out_dtype, out=None):
     L.require_cuda(a, a_s, b, b_s, bias)
     if out_dtype != torch.float8_e4m3fn:
         raise ValueError("quantising GEMM epilogues produce float8_e4m3fn only")
+    if bias is not None:
+        bias = bias.contiguous()
+    bias_args = (L.ptr(bias), L.dtype_code(bias.dtype) if bias is not None else 0)
+    if out is not None:
+        # a column window of wider row-major code / scale buffers (views)
+        c, c_s = out
+        assert c.stride(-1) == 1 and c_s.stride(-1) == 1 and c.shape[-1] == N and c_s.shape[-1] == N // 128
+        assert c.numel() // N == M and c_s.numel() // (N // 128) == M
+        if M:
+            L.call("fd_fp8_gemm_quant_ld", L.ptr(a), L.ptr(a_s), L.ptr(b), L.ptr(b_s), *bias_args, L.ptr(c),
+                   L.ptr(c_s), M, N, K, act, c.stride(-2), c_s.stride(-2), L.stream_ptr(a.device))
+        return c, c_s
     c = a.new_empty(*batch_shape, N, dtype=out_dtype)
     c_s = a.new_empty(M, N // 128, dtype=torch.float32)
     if M == 0:
         return c, c_s
-    if bias is not None:
-        bias = bias.contiguous()
-    L.call("fd_fp8_gemm_quant", L.ptr(a), L.ptr(a_s), L.ptr(b), L.ptr(b_s), L.ptr(bias),
-           L.dtype_code(bias.dtype) if bias is not None else 0, L.ptr(c), L.ptr(c_s), M, N, K, act,
-           L.stream_ptr(a.device))
+    L.call("fd_fp8_gemm_quant", L.ptr(a), L.ptr(a_s), L.ptr(b), L.ptr(b_s), *bias_args, L.ptr(c), L.ptr(c_s),
+           M, N, K, act, L.stream_ptr(a.device))
     if len(batch_shape) > 0:
         c_s = c_s.reshape(*batch_shape, N // 128)
     return c, c_s
@@ -276,12 +285,15 @@ def fp8_gemm_gelu_tanh_quant(
     b_s: torch.Tensor,
     bias: Optional[torch.Tensor] = None,
     block_size: int = 128,
+    out: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
 ) -> Tuple[torch.Tensor, torch.Tensor]:
     """``fp8_gelu_tanh_quant(fp8_addmm_blockwise(a, a_s, b, b_s, bias))`` in one kernel.
 
     The GEMM output is rounded to bf16 (as the unfused pair stores it), passed
     through GELU (tanh approximation) and quantised 1 x 128; codes and scales are
     identical to the two-kernel path.  Scales have shape (batch shape, N / 128).
+    ``out``: optional (codes, scales) views with N and N / 128 columns whose rows
+    may be wider (a column window of a larger buffer); written in place.
     """
     assert a.is_contiguous() and b.is_contiguous()
     assert a_s.is_contiguous() and b_s.is_contiguous()
@@ -290,7 +302,7 @@ def fp8_gemm_gelu_tanh_quant(
     M = a.numel() // K
     N = b.shape[0]
     assert N % block_size == 0
-    return _gemm_quant(a, a_s, b, b_s, bias, L.ACT_GELU_TANH, M, N, K, a.shape[:-1], torch.float8_e4m3fn)
+    return _gemm_quant(a, a_s, b, b_s, bias, L.ACT_GELU_TANH, M, N, K, a.shape[:-1], torch.float8_e4m3fn, out)
 
 
 def fp8_gemm_silu_gate_quant(

@@ -179,6 +179,46 @@ def _attn_forward(
     return out.reshape(B, H, N, D), lse
 
 
+def attn_forward_quant_out(
+    q: Tensor, k: Tensor, v: Tensor, sm_scale: float | None, *, block_mask: Tensor | None, qk_quant: str,
+    pv_quant: str, granularity: str, regions: list[tuple[Tensor, Tensor]], split: int | None = None,
+) -> None:
+    """(B, H, N, 128) bf16 attention whose output is written as the 1 x 128 e4m3
+    codes + fp32 scales of the output linear's input (one group per token row and
+    head), code for code equal to ``fp8_act_quant`` of the (B, N, H * 128) bf16
+    output.  ``regions``: one or two (codes (rows, >= H * 128), scales (rows, >= H))
+    row-major views (row strides may exceed the width, e.g. a column window of a
+    wider buffer); rows n < split of every sample go to region 0 (B * split rows),
+    the rest to region 1."""
+    B, H, N, D = q.shape
+    assert D == 128 and q.dtype == torch.bfloat16
+    L.require_cuda(q, k, v)
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    split = N if split is None else split
+    assert 1 <= split <= N and len(regions) == (1 if split == N else 2)
+    BH = B * H
+    qf = q.reshape(BH, N, D).contiguous()
+    kf = k.reshape(BH, N, D).contiguous()
+    vf = v.reshape(BH, N, D).contiguous()
+    bm, bm_stride = _normalize_mask(block_mask, N)
+    qz = quantize_qkv(qf, kf, vf, sm_scale, smooth_k=_SAGE_SMOOTH_K, qk_quant=qk_quant,
+                      granularity=granularity, pv_quant=pv_quant)
+    vsrc = qz["v_codes"] if qz["pv"] == L.PV_FP8 else vf
+    reg = []
+    for i, (c, sc) in enumerate(regions):
+        rows = B * (split if i == 0 else N - split)
+        assert c.dtype in (torch.float8_e4m3fn, torch.uint8) and sc.dtype == torch.float32
+        assert c.stride(-1) == 1 and sc.stride(-1) == 1
+        assert c.numel() // c.shape[-1] >= rows and c.shape[-1] >= H * D and sc.shape[-1] >= H
+        reg.append((L.ptr(c), L.ptr(sc), c.stride(-2), sc.stride(-2)))
+    if len(reg) == 1:
+        reg.append((None, None, 0, 0))
+    L.call("fd_sage_attn_fwd_quant_out", L.ptr(qz["q_codes"]), L.ptr(qz["q_desc"]), L.ptr(qz["k_codes"]),
+           L.ptr(qz["k_desc"]), L.ptr(vsrc), L.ptr(qz["v_desc"]), L.ptr(bm), bm_stride, None, BH, N, H,
+           qz["qk"], qz["gran"], qz["gran"], qz["pv"], *reg[0], *reg[1], split, L.stream_ptr(q.device))
+
+
 def _pv_for(default_pv: str) -> str:
     return _SAGE_PV_QUANT if _SAGE_QK_GRAN == "per_block" else default_pv
 

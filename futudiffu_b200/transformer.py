@@ -49,7 +49,7 @@ from .fused_kernels import (
     rms_norm_modulate_quant_ranges,
     rms_norm_modulate_ranges,
 )
-from .sage_attention import _attn_forward, _pv_for, get_sage_config
+from .sage_attention import _attn_forward, _pv_for, attn_forward_quant_out, get_sage_config
 
 HEAD_DIM = 128
 
@@ -256,17 +256,32 @@ class JointAttention(nn.Module):
         self.out = _fp8(self.out)
         return self
 
+    def _qkv(self, qkv: Tensor, freqs_cis: Tensor):
+        return fused_qkv_postprocess(qkv, self.q_norm.weight, self.k_norm.weight, freqs_cis,
+                                     self.n_local_heads, self.head_dim, self.q_norm.eps)
+
     def core(self, qkv: Tensor, freqs_cis: Tensor, block_mask: Tensor) -> Tensor:
         """(B, L, 3 dim) bf16 -> attention output (B, L, dim) bf16 in the row layout
         of the output linear (the reference's transpose + reshape, :466)."""
-        xq, xk, xv = fused_qkv_postprocess(qkv, self.q_norm.weight, self.k_norm.weight, freqs_cis,
-                                           self.n_local_heads, self.head_dim, self.q_norm.eps)
+        xq, xk, xv = self._qkv(qkv, freqs_cis)
         # sage_attn_masked_op: INT8 QK, bf16 PV (or the per-block variant)
         cfg = get_sage_config()
         o, _ = _attn_forward(xq, xk, xv, 1.0 / (self.head_dim ** 0.5), block_mask=block_mask, qk_quant="int8",
                              pv_quant=_pv_for("bf16"), granularity=cfg["qk_granularity"], want_lse=False,
                              out_bnhd=True)
         return o
+
+    def core_codes(self, qkv: Tensor, freqs_cis: Tensor, block_mask: Tensor) -> tuple[Tensor, Tensor]:
+        """``core`` with the output written as the output linear's 1 x 128 e4m3 input
+        (codes (B, L, dim), scales (B, L, dim / 128)), equal to fp8_act_quant(core(...))."""
+        xq, xk, xv = self._qkv(qkv, freqs_cis)
+        B, Lq, dim = qkv.shape[0], qkv.shape[1], qkv.shape[2] // 3
+        o8 = torch.empty(B, Lq, dim, dtype=torch.float8_e4m3fn, device=qkv.device)
+        o_s = torch.empty(B, Lq, dim // 128, dtype=torch.float32, device=qkv.device)
+        cfg = get_sage_config()
+        attn_forward_quant_out(xq, xk, xv, 1.0 / (self.head_dim ** 0.5), block_mask=block_mask, qk_quant="int8",
+                               pv_quant=_pv_for("bf16"), granularity=cfg["qk_granularity"], regions=[(o8, o_s)])
+        return o8, o_s
 
     def forward(self, x: Tensor, x_mask: Tensor | None, freqs_cis: Tensor, block_mask=None,
                 adapter_scales: Tensor | None = None, token_to_image: Tensor | None = None) -> Tensor:
@@ -286,8 +301,9 @@ class JointAttention(nn.Module):
         if block_mask is None:
             raise RuntimeError("JointAttention requires a block mask")
         qkv = _linear_codes(a8, a_s, self.qkv)
-        o = self.core(qkv, freqs_cis, block_mask)
-        return self.out(o)
+        if _is_plain_fp8(self.out):
+            return _linear_codes(*self.core_codes(qkv, freqs_cis, block_mask), self.out)
+        return self.out(self.core(qkv, freqs_cis, block_mask))
 
 
 class FeedForward(nn.Module):

@@ -135,6 +135,11 @@ int fd_fp8_gemm_blockwise_lora(const void* a, const float* a_s, const void* b, c
 int fd_fp8_gemm_quant(const void* a, const float* a_s, const void* b, const float* b_s,
                       const void* bias, int bias_dtype, void* c, float* c_s, int64_t M, int64_t N,
                       int64_t K, int act, void* stream);
+/* fd_fp8_gemm_quant writing into a column window of wider rows: output row m
+ * starts at c + m * ldc (codes, ldc a multiple of 16) and c_s + m * ldcs. */
+int fd_fp8_gemm_quant_ld(const void* a, const float* a_s, const void* b, const float* b_s,
+                         const void* bias, int bias_dtype, void* c, float* c_s, int64_t M, int64_t N,
+                         int64_t K, int act, int64_t ldc, int64_t ldcs, void* stream);
 
 int fd_fp8_silu_gate_quant(const void* x, void* y, float* s, int64_t M, int64_t N, int block,
                            void* stream);
@@ -272,6 +277,24 @@ int fd_sage_attn_fwd_bnhd(const void* q_codes, const float* q_desc, const void* 
                           const uint8_t* block_mask, int64_t mask_bh_stride, void* out, float* lse,
                           int64_t BH, int64_t N, int64_t H, int qk_kind, int q_gran, int k_gran,
                           int pv_kind, void* stream);
+
+/* fd_sage_attn_fwd_bnhd whose output is the output linear's quantised input:
+ * every (token row, head) of the (B, N, H * 128) output is one 1 x 128 group,
+ * written as e4m3 codes + an fp32 dequant scale, equal to fd_fp8_act_quant of
+ * the bf16 output code for code.  Rows n < split go to region 0, rows n >= split
+ * to region 1 (e.g. the text and image streams of a joint attention); region r
+ * holds its rows of every sample consecutively, row stride code_stride_r bytes
+ * (a multiple of 16, >= H * 128) and scale_stride_r floats (>= H).  split == N
+ * leaves region 1 unused.  Replaces sage_attn_masked_op -> reshape ->
+ * fp8_act_quant (src_ii/transformer.py:462-470, fp8.py:64); no counterpart
+ * kernel in the reference. */
+int fd_sage_attn_fwd_quant_out(const void* q_codes, const float* q_desc, const void* k_codes,
+                               const float* k_desc, const void* v, const float* v_desc,
+                               const uint8_t* block_mask, int64_t mask_bh_stride, float* lse, int64_t BH,
+                               int64_t N, int64_t H, int qk_kind, int q_gran, int k_gran, int pv_kind,
+                               void* codes0, float* scales0, int64_t code_stride0, int64_t scale_stride0,
+                               void* codes1, float* scales1, int64_t code_stride1, int64_t scale_stride1,
+                               int64_t split, void* stream);
 
 /* A7 -- attention backward, Delta pre-pass (sage_kernels.py:322-349):
  * delta (BH, N) f32 = rowsum(dO * O). */

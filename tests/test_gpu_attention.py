@@ -301,3 +301,42 @@ def test_attention_bnhd_output_layout(cuda_device):
                              want_lse=False, out_bnhd=True)
         assert b.shape == (B, N, H * 128)
         assert torch.equal(b.cpu(), a.transpose(1, 2).reshape(B, N, H * 128).cpu())
+
+
+@pytest.mark.parametrize("masked", [False, True])
+def test_attention_quantised_output(cuda_device, masked):
+    """The quantised-output epilogue writes exactly fp8_act_quant of the bf16
+    (B, N, H*128) output, split into two row regions or into a column window of
+    wider rows."""
+    from futudiffu_b200.block_mask import build_block_mask
+    from futudiffu_b200.fp8_kernels import fp8_act_quant
+    from futudiffu_b200.sage_attention import _attn_forward, attn_forward_quant_out
+
+    g = gen(93)
+    B, H, N = 2, 3, 300
+    D = H * 128
+    q, k, v = (torch.randn(B, H, N, 128, generator=g).to(torch.bfloat16).to(cuda_device) for _ in range(3))
+    mask = build_block_mask([100, 200], device=cuda_device) if masked else None
+    split = 77
+    modes = [("int8", "fp8", "per_block"), ("int8", "bf16", "per_token"), ("fp8", "bf16", "per_token")]
+    for qk, pv, gran in modes:
+        o, _ = _attn_forward(q, k, v, None, block_mask=mask, qk_quant=qk, pv_quant=pv, granularity=gran,
+                             want_lse=False, out_bnhd=True)
+        r8, rs = fp8_act_quant(o)
+        r8 = r8.view(torch.uint8)
+        # two regions: rows n < split and n >= split of every sample
+        regions = [(torch.empty(B, n, D, dtype=torch.float8_e4m3fn, device=cuda_device),
+                    torch.empty(B, n, D // 128, dtype=torch.float32, device=cuda_device)) for n in (split, N - split)]
+        attn_forward_quant_out(q, k, v, None, block_mask=mask, qk_quant=qk, pv_quant=pv, granularity=gran,
+                               regions=regions, split=split)
+        assert torch.equal(regions[0][0].view(torch.uint8), r8[:, :split])
+        assert torch.equal(regions[1][0].view(torch.uint8), r8[:, split:])
+        assert torch.equal(regions[0][1], rs[:, :split]) and torch.equal(regions[1][1], rs[:, split:])
+        # one region: a column window of wider rows (the [attention | MLP] input of a fused linear)
+        W = D + 256
+        buf = torch.zeros(B, N, W, dtype=torch.uint8, device=cuda_device)
+        sbuf = torch.zeros(B, N, W // 128, dtype=torch.float32, device=cuda_device)
+        attn_forward_quant_out(q, k, v, None, block_mask=mask, qk_quant=qk, pv_quant=pv, granularity=gran,
+                               regions=[(buf[..., :D], sbuf[..., :D // 128])])
+        assert torch.equal(buf[..., :D], r8) and not buf[..., D:].any()
+        assert torch.equal(sbuf[..., :D // 128], rs) and not sbuf[..., D // 128:].any()

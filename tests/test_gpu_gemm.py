@@ -222,3 +222,20 @@ def test_gemm_silu_gate_quant_epilogue(cuda_device, M, H, K, bias):
     ry, rs = OQ.silu_gate_quant(w13.cpu())
     assert e4m3_step_diff(c.cpu(), ry).max().item() <= 1
     torch.testing.assert_close(c_s.cpu(), rs.reshape(M, H // 128), rtol=2e-6, atol=0)
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 512, 384), (4608, 1024, 768)])
+def test_gemm_quant_into_column_window(cuda_device, M, N, K):
+    """The quantising epilogue writes into a column window of wider code / scale
+    rows exactly what it writes into a buffer of its own, and nothing outside it."""
+    from futudiffu_b200 import fp8_kernels as FK
+
+    a8, a_s, b8, bs = (t.to(cuda_device) for t in _operands(M, N, K, seed=14))
+    c, c_s = FK.fp8_gemm_gelu_tanh_quant(a8, a_s, b8, bs)
+    off, W = 384, N + 640
+    buf = torch.zeros(M, W, dtype=torch.uint8, device=cuda_device)
+    sbuf = torch.zeros(M, W // 128, dtype=torch.float32, device=cuda_device)
+    FK.fp8_gemm_gelu_tanh_quant(a8, a_s, b8, bs, out=(buf[:, off:off + N], sbuf[:, off // 128:off // 128 + N // 128]))
+    assert torch.equal(buf[:, off:off + N], c.view(torch.uint8))
+    assert torch.equal(sbuf[:, off // 128:off // 128 + N // 128], c_s)
+    assert not buf[:, :off].any() and not buf[:, off + N:].any()
