@@ -550,6 +550,60 @@ def run_dit(args, world, rank, local):
 VIDEO_METRIC = "video DiT denoise steps/s (14B-class, 40 blocks, 32760 video + 512 text tokens, Ulysses)"
 
 
+_VIDEO_CPU_BLOCKS: dict = {}
+
+
+def video_cpu_sample(tokens: int = 1024) -> dict:
+    """One config-5 video block through the oracle on the host cores (CPU-built
+    weights) with ``tokens`` video tokens and the 512 text tokens, extrapolated to
+    the 40-block step over 32760 tokens by FLOPs."""
+    from futudiffu_b200.dit import VideoDiTConfig, video_flops_per_step, video_freqs
+    from oracle import dit as OD
+
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    torch.set_num_threads(threads)
+    cfg = VideoDiTConfig()
+    if "blk" not in _VIDEO_CPU_BLOCKS:
+        _VIDEO_CPU_BLOCKS["blk"] = OD.random_video_block(cfg, seed=0)
+    blk = _VIDEO_CPU_BLOCKS["blk"]
+    cg = torch.Generator().manual_seed(3)
+    D, F, T = cfg.hidden, cfg.ffn, cfg.txt_tokens
+    x = torch.randn(1, tokens, D, generator=cg).to(torch.bfloat16)
+    txt = torch.randn(1, T, D, generator=cg).to(torch.bfloat16)
+    vec = torch.randn(1, D, generator=cg).to(torch.bfloat16)
+    freqs = video_freqs(cfg, "cpu", 0, tokens).unsqueeze(0)
+    t0 = time.perf_counter()
+    OD.video_block(blk, x, vec, txt, freqs)
+    dt = time.perf_counter() - t0
+    L = tokens
+    blk_flops = 2 * L * (4 * D * D + 2 * D * D + 2 * D * F) + 2 * T * 2 * D * D + 4 * L * L * D + 4 * L * T * D
+    step_s = dt * video_flops_per_step(cfg) / blk_flops
+    return {"value": 1.0 / step_s, "unit": "steps/s", "cores": threads, "kind": "port",
+            "sample": f"one video block at {tokens} video + {T} text tokens through oracle.dit.video_block "
+                      f"({dt:.1f} s, {threads} threads), extrapolated to the {cfg.n_blocks}-block step over "
+                      f"{cfg.tokens} tokens by FLOP ratio ({step_s:.0f} s/step)"}
+
+
+def run_video_reference(args, world, rank):
+    if rank != 0:
+        return 0
+    vals, cb = [], None
+    for i in range(args.warmup + args.steps):
+        cb = video_cpu_sample()
+        if i >= args.warmup:
+            vals.append(cb["value"])
+    val = statistics.mean(vals)
+    print(json.dumps({
+        "impl": "reference", "metric": VIDEO_METRIC, "value": val, "unit": "steps/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / val, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp8/int8", "data": "synthetic",
+        "config": {"workload": "config5_video_dit_ulysses"},
+        "cpu_baseline": {**cb, "value": val},
+        "e2e": {"value": val, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+    return 0
+
+
 def run_video(args, world, rank, local):
     import torch.distributed as dist
 
@@ -631,7 +685,7 @@ def run_video(args, world, rank, local):
             "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": peak, "unit": "TFLOP/s",
                          "frac": gemm_tf / peak, "traffic": None, "kernel": "gemm_fp8_kernel (flop-weighted, rank 0)",
                          "peak_source": f"2 x {pk['source']} sustained bf16 dense ({pk['bf16_tflops_sustained']} TF/s)"},
-            "cpu_baseline": None,
+            "cpu_baseline": video_cpu_sample() if world == 1 else None,
             "e2e": {"value": 1e3 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h_x.numel() * 2 * world,
                     "d2h_bytes_per_step": h_x.numel() * 2 * world, "ms_per_step": e2e_ms,
                     "api": "futudiffu_b200.dit.VideoDiT"},
@@ -644,6 +698,68 @@ GEMM_SHAPES = {"config1": (2048, 3072, 3072), "ref_qkv": (8576, 11520, 3840), "r
 
 
 PACKED_METRIC = "packed multi-image forward tokens/s (Z-Image-class blocks, 3840 hidden, 30 heads, 4288-token bin)"
+
+
+_PACKED_CPU_BLOCKS: dict = {}
+
+
+def packed_cpu_sample(tokens: int = 1024, layers: int = 30) -> dict:
+    """One Z-Image-class JointTransformerBlock through the oracle on the host cores
+    (CPU-built weights) on a one-image sequence of ``tokens`` tokens, extrapolated
+    to the packed 30-layer forward of a 4288-token bin by FLOPs."""
+    from futudiffu_b200 import transformer as T
+    from futudiffu_b200.bin_packer import REFERENCE_TOTAL_LEN
+    from futudiffu_b200.block_mask import build_block_mask
+    from oracle import transformer as OT
+
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    torch.set_num_threads(threads)
+    dim, heads, hidden = 3840, 30, 10240
+    if "blk" not in _PACKED_CPU_BLOCKS:
+        _PACKED_CPU_BLOCKS["blk"] = OT.random_joint_block(dim, heads, hidden, seed=0)
+    blk = _PACKED_CPU_BLOCKS["blk"]
+    cg = torch.Generator().manual_seed(2)
+    cap = 64
+    grid = (tokens - cap) // 16
+    _, info = T.build_packed_sequence([torch.zeros(1, cap, 1)], [torch.zeros(1, grid * 16, 1)], [(grid, 16)],
+                                      [cap], 32, torch.zeros(1), torch.zeros(1))
+    rope = T.build_packed_rope(info, device="cpu")
+    n = info.total_len
+    x = torch.randn(1, n, dim, generator=cg).to(torch.bfloat16)
+    scales = tuple((0.1 * torch.randn(1, dim, generator=cg)).to(torch.bfloat16) for _ in range(4))
+    mask = build_block_mask([n], device="cpu")
+    t0 = time.perf_counter()
+    OT.block_forward(blk, x, rope, scales, mask)
+    dt = time.perf_counter() - t0
+    lin = 2 * (3 * dim * dim + dim * dim + 2 * hidden * dim + hidden * dim)
+    sample_flops = lin * n + 4 * n * n * dim
+    full_flops = layers * (lin * REFERENCE_TOTAL_LEN + 4 * 0.63 * REFERENCE_TOTAL_LEN ** 2 * dim)
+    step_s = dt * full_flops / sample_flops
+    return {"value": REFERENCE_TOTAL_LEN / step_s, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"one JointTransformerBlock (3840 hidden, 30 heads, FFN 10240) on {n} tokens through "
+                      f"oracle.transformer.block_forward ({dt:.1f} s, {threads} threads), extrapolated to the "
+                      f"{layers}-layer forward of a {REFERENCE_TOTAL_LEN}-token bin (mask density 0.63) by FLOP "
+                      f"ratio ({step_s:.0f} s/forward)"}
+
+
+def run_packed_reference(args, world, rank):
+    if rank != 0:
+        return 0
+    vals, cb = [], None
+    for i in range(args.warmup + args.steps):
+        cb = packed_cpu_sample(layers=args.layers)
+        if i >= args.warmup:
+            vals.append(cb["value"])
+    val = statistics.mean(vals)
+    print(json.dumps({
+        "impl": "reference", "metric": PACKED_METRIC, "value": val, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 4288 / val * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp8/int8", "data": "synthetic",
+        "config": {"workload": "packed_zimage_trunk", "layers": args.layers, "hidden": 3840, "heads": 30},
+        "cpu_baseline": {**cb, "value": val},
+        "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+    return 0
 
 
 def run_packed(args, world, rank, local):
@@ -753,7 +869,7 @@ def run_packed(args, world, rank, local):
                          "frac": gemm_tf / peak, "traffic": None,
                          "kernel": f"gemm_fp8_kernel ({n_gemm // max(1, args.steps)} launches per step, flop-weighted)",
                          "peak_source": f"2 x {pk['source']} sustained bf16 dense ({pk['bf16_tflops_sustained']} TF/s)"},
-            "cpu_baseline": None,
+            "cpu_baseline": packed_cpu_sample(layers=args.layers) if world == 1 else None,
             "e2e": {"value": toks / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": host_x.numel() * 2 * world, "d2h_bytes_per_step": host_x.numel() * 2 * world,
                     "ms_per_step": e2e_ms, "api": "futudiffu_b200.transformer.PackedTrunk"},
@@ -848,17 +964,11 @@ def main(argv=None) -> int:
             return run_dit(args, world, rank, local)
         if args.workload == "video":
             if args.impl == "reference":
-                if rank == 0:
-                    print(json.dumps({"impl": "reference", "unavailable": "config 5 has no CPU reference arm: "
-                                      "a 1.7 PFLOP step; see the dit workload's CPU baseline"}), flush=True)
-                return 0
+                return run_video_reference(args, world, rank)
             return run_video(args, world, rank, local)
         if args.workload == "packed":
             if args.impl == "reference":
-                if rank == 0:
-                    print(json.dumps({"impl": "reference", "unavailable": "the packed workload has no CPU "
-                                      "reference arm; see the dit workload's CPU baseline"}), flush=True)
-                return 0
+                return run_packed_reference(args, world, rank)
             return run_packed(args, world, rank, local)
         if args.impl == "reference":
             return run_reference(args, world, rank)

@@ -156,6 +156,29 @@ def random_double_block(cfg, seed: int = 0):
     return SimpleNamespace(cfg=cfg, txt=stream(), img=stream())
 
 
+def random_video_block(cfg, seed: int = 0):
+    """Weights of one video block built on the CPU alone, with the attribute layout
+    of futudiffu_b200.dit.VideoBlock."""
+    from types import SimpleNamespace
+
+    g = torch.Generator().manual_seed(seed)
+    D = cfg.hidden
+
+    def rand(shape, std, mean=0.0):
+        return (torch.randn(shape, generator=g) * std + mean).to(torch.bfloat16)
+
+    def fp8_linear(n, k):
+        w8, ws = OQ.weight_quant(torch.randn(n, k, generator=g) * 0.02)
+        return SimpleNamespace(weight=w8, weight_scale=ws, bias=None)
+
+    return SimpleNamespace(
+        cfg=cfg, adaln=SimpleNamespace(weight=rand((4 * D, D), 0.02), bias=rand((4 * D,), 0.02)),
+        norm_w=[rand((D,), 0.05, 1.0) for _ in range(6)], cross_gate=rand((1, D), 0.5),
+        q_norm=rand((128,), 0.05, 1.0), k_norm=rand((128,), 0.05, 1.0),
+        qkv=fp8_linear(3 * D, D), proj=fp8_linear(D, D), cq=fp8_linear(D, D), ckv=fp8_linear(2 * D, D),
+        co=fp8_linear(D, D), ffn_in=fp8_linear(cfg.ffn, D), ffn_out=fp8_linear(D, cfg.ffn))
+
+
 def video_block(blk, x, vec, txt, freqs):
     """futudiffu_b200.dit.VideoBlock on the CPU, single rank (the whole sequence)."""
     cfg = blk.cfg

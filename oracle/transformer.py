@@ -83,3 +83,26 @@ def block_forward(blk, x, freqs, scales, block_mask):
     ffn_in = OF.rms_norm_modulate(x, _cpu(f1.weight), scale_mlp, f1.eps)
     ffn_out = feed_forward(blk.feed_forward, ffn_in)
     return OF.rms_norm_gate_residual(ffn_out, _cpu(f2.weight), gate_mlp, x, f2.eps)
+
+
+def random_joint_block(dim: int, heads: int, hidden: int, seed: int = 0):
+    """Weights of one JointTransformerBlock built on the CPU alone (oracle weight
+    quantiser), with the attribute layout ``block_forward`` reads."""
+    from types import SimpleNamespace
+
+    from oracle import quant as OQ
+
+    g = torch.Generator().manual_seed(seed)
+
+    def norm(n):
+        return SimpleNamespace(weight=(1 + 0.05 * torch.randn(n, generator=g)).to(torch.bfloat16), eps=1e-5)
+
+    def fp8_linear(n, k):
+        w8, ws = OQ.weight_quant(torch.randn(n, k, generator=g) * (k ** -0.5))
+        return SimpleNamespace(weight=w8, weight_scale=ws, bias=None)
+
+    att = SimpleNamespace(n_local_heads=heads, qkv=fp8_linear(3 * dim, dim), out=fp8_linear(dim, dim),
+                          q_norm=norm(128), k_norm=norm(128))
+    ffn = SimpleNamespace(w1w3=fp8_linear(2 * hidden, dim), w2=fp8_linear(dim, hidden))
+    return SimpleNamespace(attention=att, feed_forward=ffn, attention_norm1=norm(dim), attention_norm2=norm(dim),
+                           ffn_norm1=norm(dim), ffn_norm2=norm(dim))
