@@ -424,7 +424,7 @@ class VideoBlock(nn.Module):
 
     def forward(self, x: Tensor, vec: Tensor, txt: Tensor, freqs: Tensor, group=None) -> Tensor:
         """x (1, L/P, D) bf16: this rank's tokens; vec (1, D); txt (1, 512, D); freqs (1, L/P, 64, 2, 2)."""
-        from .ulysses import ulysses_attention
+        from .ulysses import ulysses_attention_codes
 
         cfg = self.cfg
         _, Ls, D = x.shape
@@ -435,13 +435,17 @@ class VideoBlock(nn.Module):
         qkv = gemm_bf16(h8, h_s, self.qkv)
         q, k, v = fused_qkv_postprocess(qkv, self.q_norm, self.k_norm, freqs, H, HEAD_DIM, cfg.eps)
 
-        def attn(qh, kh, vh):
-            o, _ = _attn_forward(qh, kh, vh, None, block_mask=None, qk_quant=cfg.qk_quant,
-                                 pv_quant=cfg.pv_quant, granularity=cfg.granularity, want_lse=False)
-            return o
+        def attn_codes(qh, kh, vh):
+            # the output projection's 1 x 128 e4m3 input, written by the attention kernel
+            _, Hl, L, _ = qh.shape
+            c8 = torch.empty(L, Hl * HEAD_DIM, dtype=torch.uint8, device=qh.device)
+            cs = torch.empty(L, Hl, dtype=torch.float32, device=qh.device)
+            attn_forward_quant_out(qh, kh, vh, None, block_mask=None, qk_quant=cfg.qk_quant,
+                                   pv_quant=cfg.pv_quant, granularity=cfg.granularity, regions=[(c8, cs)])
+            return c8, cs
 
-        o = ulysses_attention(q[0], k[0], v[0], attn, group)            # (L/P, D)
-        a = linear_bf16(o.unsqueeze(0), self.proj)
+        o8, o_s = ulysses_attention_codes(q[0], k[0], v[0], attn_codes, group)   # (L/P, D), (L/P, D/128)
+        a = gemm_bf16(o8.view(torch.float8_e4m3fn).unsqueeze(0), o_s.unsqueeze(0), self.proj)
         x = fused_rms_norm_gate_residual(a, self.norm_w[1], m[1], x, cfg.eps)
         # ---- cross-attention to the text (replicated on every rank; 512 keys, bf16 SDPA)
         zero = torch.zeros_like(m[0])

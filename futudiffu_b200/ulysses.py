@@ -58,6 +58,34 @@ def head_to_seq(o: Tensor, group=None) -> Tensor:
     return recv.permute(2, 0, 1, 3).reshape(Ls, P * Hp * D)
 
 
+def head_to_seq_rows(x: Tensor, group=None) -> Tensor:
+    """(L, H/P * W) token-major rows of this rank's heads -> (L/P, H * W): this rank's
+    token shard with every head, in head_to_seq's column order.  W is any per-head
+    width: 128 e4m3 codes of the quantised attention output, or its one scale, so
+    the output projection's input crosses NVLink as 1 x 128 codes + scales
+    (1 + 4/128 bytes per value instead of 2)."""
+    P = _world(group)
+    L, C = x.shape
+    if P == 1:
+        return x
+    if L % P:
+        raise ValueError(f"sequence {L} does not split over {P} ranks")
+    send = x.contiguous()                        # rows [p L/P, (p+1) L/P) go to rank p
+    recv = torch.empty_like(send)                # (P_src, L/P, C)
+    dist.all_to_all_single(recv, send, group=group)
+    return recv.view(P, L // P, C).transpose(0, 1).reshape(L // P, P * C)
+
+
+def ulysses_attention_codes(q: Tensor, k: Tensor, v: Tensor, attn_codes_fn, group=None) -> tuple[Tensor, Tensor]:
+    """Sequence-sharded (H, L/P, D) Q/K/V -> attention -> the output projection's
+    quantised input for this rank's tokens: codes (L/P, H * 128) uint8 and scales
+    (L/P, H).  ``attn_codes_fn(q, k, v)`` runs on (1, H/P, L, D) and returns codes
+    (L, H/P * 128) uint8 and scales (L, H/P) fp32."""
+    qh, kh, vh = (seq_to_head(t, group) for t in (q, k, v))
+    codes, scales = attn_codes_fn(qh.unsqueeze(0), kh.unsqueeze(0), vh.unsqueeze(0))
+    return head_to_seq_rows(codes.view(torch.uint8), group), head_to_seq_rows(scales, group)
+
+
 def ulysses_attention(q: Tensor, k: Tensor, v: Tensor, attn_fn, group=None) -> Tensor:
     """Sequence-sharded (H, L/P, D) Q/K/V -> attention -> (L/P, H * D).
 

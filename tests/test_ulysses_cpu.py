@@ -28,7 +28,7 @@ def _worker(rank, world, port, H, L, D, out):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        from futudiffu_b200.ulysses import head_to_seq, seq_to_head, ulysses_attention
+        from futudiffu_b200.ulysses import head_to_seq, head_to_seq_rows, seq_to_head, ulysses_attention
 
         g = torch.Generator().manual_seed(0)
         q, k, v = (torch.randn(H, L, D, generator=g) for _ in range(3))
@@ -39,6 +39,14 @@ def _worker(rank, world, port, H, L, D, out):
         assert torch.equal(qh, q[rank * H // world:(rank + 1) * H // world])
         back = head_to_seq(qh)
         assert torch.equal(back, q[:, sl].transpose(0, 1).reshape(Ls, H * D))
+        # token-major rows of this rank's heads (codes / scales of the quantised output)
+        # land in head_to_seq's layout
+        rows = qh.transpose(0, 1).reshape(L, (H // world) * D)
+        assert torch.equal(head_to_seq_rows(rows), back)
+        codes = torch.randint(0, 256, (L, (H // world) * 128), generator=g, dtype=torch.uint8)
+        got = head_to_seq_rows(codes)
+        want = head_to_seq(codes.view(L, H // world, 128).transpose(0, 1).contiguous())
+        assert torch.equal(got, want)
         o = ulysses_attention(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), _exact)
         ref = _exact(q[None], k[None], v[None])[0][:, sl].transpose(0, 1).reshape(Ls, H * D)
         out[rank] = float((o - ref).abs().max())
