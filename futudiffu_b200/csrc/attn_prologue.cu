@@ -174,8 +174,11 @@ FD_DEV float half_max(float v) {
 // grid (ceil(N/128), BH, 2 or 3), 256 threads; blockIdx.z selects Q, K or V, so
 // the three tensors are quantised by independent CTAs.  Thread t handles column
 // group (t & 15) * 8 of rows (t >> 4) + 16 i, i = 0..7, of the 128-row block.
+// The 64 values a thread holds between its amax pass and its quantise pass stay
+// packed as bf16 (K after smoothing is bf16-rounded too), so three CTAs fit per
+// SM and their loads overlap each other's reductions.
 template <int QK>
-__global__ void __launch_bounds__(256) quant_kernel(
+__global__ void __launch_bounds__(256, 3) quant_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
     const __nv_bfloat16* __restrict__ v, int64_t N, int nchunks, int smooth_k, int q_gran,
     int k_gran, int pv_fp8, float sm_scale_log2e, uint8_t* __restrict__ q_codes,
@@ -205,18 +208,19 @@ __global__ void __launch_bounds__(256) quant_kernel(
 
   // ---------------- Q
   if (which == 0) {
-    float x[8][8];
+    uint4 xr[8];
     float rowmax[8];
     float blkmax = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int64_t n = r0 + rl + 16 * i;
-      if (n < N) unpack8(__ldg(reinterpret_cast<const uint4*>(q + (bh * N + n) * 128 + cg * 8)), x[i]);
-      else {
+      xr[i] = n < N ? __ldg(reinterpret_cast<const uint4*>(q + (bh * N + n) * 128 + cg * 8)) : make_uint4(0, 0, 0, 0);
+    }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) x[i][e] = 0.f;
-      }
-      rowmax[i] = half_max(amax8(x[i]));
+    for (int i = 0; i < 8; ++i) {
+      float x[8];
+      unpack8(xr[i], x);
+      rowmax[i] = half_max(amax8(x));
       blkmax = fmaxf(blkmax, rowmax[i]);
     }
     if (q_gran == FD_GRAN_BLOCK) {
@@ -235,7 +239,9 @@ __global__ void __launch_bounds__(256) quant_kernel(
       const float am = (q_gran == FD_GRAN_BLOCK) ? blkmax : rowmax[i];
       const float inv = div_full(qmax, fmaxf(am, 1e-12f));
       if (n < N) {
-        *reinterpret_cast<uint2*>(q_codes + (bh * N + n) * 128 + cg * 8) = quant_row8<QK>(x[i], inv);
+        float x[8];
+        unpack8(xr[i], x);
+        *reinterpret_cast<uint2*>(q_codes + (bh * N + n) * 128 + cg * 8) = quant_row8<QK>(x, inv);
         if (q_gran == FD_GRAN_TOKEN && cg == 0)
           q_desc[bh * q_desc_stride + n] = div_full(am, qmax) * sm_scale_log2e;
       } else if (q_gran == FD_GRAN_TOKEN && cg == 0 && n < q_desc_stride) {
@@ -246,21 +252,27 @@ __global__ void __launch_bounds__(256) quant_kernel(
 
   // ---------------- K (smoothed)
   if (which == 1) {
-    float x[8][8];
+    uint4 xr[8];
     float rowmax[8];
     float hmax[2] = {0.f, 0.f};  // rows 0..63 / 64..127 of the block
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int64_t n = r0 + rl + 16 * i;
+      xr[i] = n < N ? __ldg(reinterpret_cast<const uint4*>(k + (bh * N + n) * 128 + cg * 8)) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t n = r0 + rl + 16 * i;
+      float x[8];
+      unpack8(xr[i], x);
       if (n < N) {
-        unpack8(__ldg(reinterpret_cast<const uint4*>(k + (bh * N + n) * 128 + cg * 8)), x[i]);
+        // torch bf16 subtraction: the difference rounded to bf16 (exact in packed form)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) x[i][e] = round_to_bf16(x[i][e] - sh_mean[cg * 8 + e]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) x[i][e] = 0.f;
+        for (int e = 0; e < 8; ++e) x[e] = round_to_bf16(x[e] - sh_mean[cg * 8 + e]);
+        xr[i] = make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]), pack_bf16x2(x[4], x[5]),
+                           pack_bf16x2(x[6], x[7]));
       }
-      rowmax[i] = half_max(amax8(x[i]));
+      rowmax[i] = half_max(amax8(x));
       hmax[i >> 2] = fmaxf(hmax[i >> 2], rowmax[i]);  // row rl+16i < 64 iff i < 4
     }
     if (k_gran == FD_GRAN_BLOCK) {
@@ -289,7 +301,9 @@ __global__ void __launch_bounds__(256) quant_kernel(
       const float am = (k_gran == FD_GRAN_BLOCK) ? hmax[i >> 2] : rowmax[i];
       const float inv = div_full(qmax, fmaxf(am, 1e-12f));
       if (n < N) {
-        *reinterpret_cast<uint2*>(k_codes + (bh * N + n) * 128 + cg * 8) = quant_row8<QK>(x[i], inv);
+        float x[8];
+        unpack8(xr[i], x);
+        *reinterpret_cast<uint2*>(k_codes + (bh * N + n) * 128 + cg * 8) = quant_row8<QK>(x, inv);
         if (k_gran == FD_GRAN_TOKEN && cg == 0) k_desc[bh * k_desc_stride + n] = div_full(am, qmax);
       } else if (k_gran == FD_GRAN_TOKEN && cg == 0 && n < k_desc_stride) {
         k_desc[bh * k_desc_stride + n] = 0.f;
