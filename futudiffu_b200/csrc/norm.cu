@@ -40,6 +40,31 @@ FD_DEV uint4 pack_bf16x8(const float (&v)[8]) {
                     pack_bf16x2(v[6], v[7]));
 }
 
+// Eight consecutive elements of a DT array as floats; p + i must be 16-byte
+// aligned (one 16-byte load for bf16 / f16, two for f32).
+template <int DT>
+FD_DEV void load8(const void* p, int64_t i, float (&v)[8]) {
+  if constexpr (DT == FD_DT_F32) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p) + i));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if constexpr (DT == FD_DT_BF16) {
+        v[2 * k] = __uint_as_float(w[k] << 16);
+        v[2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+      } else {
+        const __half2 h = *reinterpret_cast<const __half2*>(&w[k]);
+        v[2 * k] = __low2float(h);
+        v[2 * k + 1] = __high2float(h);
+      }
+    }
+  }
+}
+
 // Max 8192 / (32 lanes * 8) = 32 vectors per lane.
 constexpr int kMaxVecPerLane = 32;
 
@@ -57,8 +82,10 @@ constexpr int kMaxVecPerLane = 32;
 // come from parameter row rparam[b] of scale / gate (n_params rows), so a
 // packed sequence's per-image modulation is applied without materialising a
 // (tokens, dim) tensor.  Ranges or parameter rows out of bounds are skipped.
+// Registers: the row (NV 16-byte vectors per lane) dominates; rows of up to 3072
+// values (NV <= 12) fit three CTAs per SM, wider rows two.
 template <int MODE, int WDT, int SDT, int NV>
-__global__ void __launch_bounds__(256) rms_row_kernel(const __nv_bfloat16* __restrict__ x,
+__global__ void __launch_bounds__(256, (NV <= 12 ? 3 : 2)) rms_row_kernel(const __nv_bfloat16* __restrict__ x,
                                                      const void* __restrict__ w,
                                                      const void* __restrict__ sg,
                                                      const __nv_bfloat16* __restrict__ res,
@@ -80,10 +107,31 @@ __global__ void __launch_bounds__(256) rms_row_kernel(const __nv_bfloat16* __res
     if (prow < 0 || prow >= n_params || row0 < 0 || nrows < 0 || row0 + nrows > rows) return;
   }
   if ((int64_t)blockIdx.y * (blockDim.x >> 5) >= nrows) return;  // no row for this CTA
-  for (int col = threadIdx.x; col < dim; col += blockDim.x) {
-    s_w[col] = load_elem<WDT>(w, col);
-    const float sv = load_elem<SDT>(sg, prow * dim + col);
-    s_f[col] = MODE == 1 ? tanhf(sv) : 1.0f + sv;
+  // Stage the factors: 16-byte loads, at most four per thread (dim <= 8192), all
+  // independent, so the CTA pays about one memory latency before its rows.
+  const size_t sb = SDT == FD_DT_F32 ? 4 : 2;
+  const bool vec_ok =
+      ((reinterpret_cast<uintptr_t>(w) | (reinterpret_cast<uintptr_t>(sg) + (size_t)prow * dim * sb)) & 15) == 0;
+  if (vec_ok) {
+#pragma unroll 4
+    for (int c8 = threadIdx.x; c8 < dim / 8; c8 += blockDim.x) {
+      float wv[8], sv[8];
+      load8<WDT>(w, (int64_t)c8 * 8, wv);
+      load8<SDT>(sg, prow * dim + (int64_t)c8 * 8, sv);
+      float fv[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) fv[e] = MODE == 1 ? tanhf(sv[e]) : 1.0f + sv[e];
+      reinterpret_cast<float4*>(s_w)[2 * c8] = make_float4(wv[0], wv[1], wv[2], wv[3]);
+      reinterpret_cast<float4*>(s_w)[2 * c8 + 1] = make_float4(wv[4], wv[5], wv[6], wv[7]);
+      reinterpret_cast<float4*>(s_f)[2 * c8] = make_float4(fv[0], fv[1], fv[2], fv[3]);
+      reinterpret_cast<float4*>(s_f)[2 * c8 + 1] = make_float4(fv[4], fv[5], fv[6], fv[7]);
+    }
+  } else {
+    for (int col = threadIdx.x; col < dim; col += blockDim.x) {
+      s_w[col] = load_elem<WDT>(w, col);
+      const float sv = load_elem<SDT>(sg, prow * dim + col);
+      s_f[col] = MODE == 1 ? tanhf(sv) : 1.0f + sv;
+    }
   }
   __syncthreads();
   const int nvec = dim / 8;
