@@ -215,11 +215,11 @@ static void launch_rms(const void* x, const void* w, const void* sg, const void*
   const int nvec = dim / 8;
   const int64_t B = ranges ? n_ranges : rows / S;
   // about 8 CTAs (64 warps) per SM in total, spread over the samples (ranges),
-  // but at least ~4 rows per warp: each CTA first stages dim weights and dim
-  // modulation factors in shared memory, which must be amortised over its rows.
-  // (Ranges: sized by the total row count, since one range may hold most rows.)
+  // and no more CTAs than one row per warp needs (ranges: sized by the total row
+  // count, since one range may hold most rows).  The per-CTA staging of the
+  // factors is one round of 16-byte loads, cheap next to a warp's rows.
   int64_t per_b = ((int64_t)num_sms() * 8 + B - 1) / B;
-  const int64_t need = ((ranges ? rows : S) + 31) / 32;
+  const int64_t need = ((ranges ? rows : S) + 7) / 8;
   if (per_b > need) per_b = need;
   if (per_b < 1) per_b = 1;
   const dim3 grid((unsigned)B, (unsigned)per_b);
