@@ -70,6 +70,9 @@ _SIGS: dict[str, list] = {
     "fd_qkv_postprocess": [_P, _P, _P, _P, _P, _P, _P, _L, _L, _L, _L, _F, _P],
     "fd_qkv_postprocess_into": [_P, _P, _P, _P, _P, _P, _P, _L, _L, _L, _L, _F, _L, _L, _P],
     "fd_attn_quant_workspace_floats": [_L, _L],
+    "fd_qkv_quant_workspace_floats": [_L, _L],
+    "fd_qkv_postprocess_quant": [_P, _P, _P, _P, _L, _L, _L, _F, _L, _L, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P],
+    "fd_attn_quant_kv": [_P, _P, _L, _L, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P],
     "fd_attn_quant": [_P, _P, _P, _L, _L, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P, _P],
     "fd_attn_quant_noalloc_max_floats": [],
     "fd_attn_quant_noalloc": [_P, _P, _P, _L, _L, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P, _P],
@@ -84,6 +87,7 @@ _RESTYPES = {
     "fd_version": ctypes.c_char_p,
     "fd_last_error": ctypes.c_char_p,
     "fd_attn_quant_workspace_floats": ctypes.c_int64,
+    "fd_qkv_quant_workspace_floats": ctypes.c_int64,
     "fd_attn_quant_noalloc_max_floats": ctypes.c_int64,
 }
 

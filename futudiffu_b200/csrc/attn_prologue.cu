@@ -185,10 +185,10 @@ __global__ void __launch_bounds__(256, 3) quant_kernel(
     float* __restrict__ q_desc, uint8_t* __restrict__ k_codes, float* __restrict__ k_desc,
     uint8_t* __restrict__ v_codes, float* __restrict__ v_desc, float* __restrict__ k_mean,
     const float* __restrict__ ws_sum, const float* __restrict__ ws_amax, int64_t q_desc_stride,
-    int64_t k_desc_stride) {
+    int64_t k_desc_stride, int z0) {
   const int blk = blockIdx.x;
   const int64_t bh = blockIdx.y;
-  const int which = blockIdx.z;  // 0 Q, 1 K, 2 V
+  const int which = blockIdx.z + z0;  // 0 Q, 1 K, 2 V
   const int cg = threadIdx.x & 15, rl = threadIdx.x >> 4;
   const int64_t r0 = (int64_t)blk * 128;
   const float qmax = (QK == FD_QK_INT8) ? 127.0f : 448.0f;
@@ -333,6 +333,150 @@ __global__ void __launch_bounds__(256, 3) quant_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// Fused P3 + attention prologue, first pass (one launch per stream of a joint
+// attention).  CTA = one 128-row block of one head of one sample; warp w takes
+// rows w, w + 8, ... of the block, lane l columns 4l .. 4l + 3 of the head.
+// Per row: the P3 arithmetic of qkv_post_kernel (per-head RMSNorm of Q and K,
+// RoPE, bf16 rounding of the stored values), then
+//   Q -> INT8 / e4m3 codes + descale, exactly as quant_kernel would quantise
+//        the bf16 Q P3 stores (per token: at once; per 128-row block: after the
+//        CTA has the block's absmax);
+//   K, V -> stored in bf16 (K still needs the sequence mean, V its column
+//        absmax, before they can be quantised), with this block's K column sums
+//        and V column absmax written to the workspace slot of its joint chunk.
+// Q / K / V rows are rows s_off + s of the joint (B, H, N, 128) layout; the
+// caller guarantees s_off % 128 == 0 and that every stream but the last has a
+// multiple of 128 rows, so a chunk never spans two launches.
+template <int QK>
+__global__ void __launch_bounds__(256, 3) qkv_quant_kernel(
+    const __nv_bfloat16* __restrict__ qkv, const float* __restrict__ qw, const float* __restrict__ kw,
+    const float* __restrict__ freqs, int64_t S, int H, float eps, int64_t N, int64_t s_off, int q_gran,
+    float sm_scale_log2e, uint8_t* __restrict__ q_codes, float* __restrict__ q_desc, int64_t q_desc_stride,
+    __nv_bfloat16* __restrict__ k_out, __nv_bfloat16* __restrict__ v_out, float* __restrict__ ws_sum,
+    float* __restrict__ ws_amax, int nchunks, int do_v) {
+  constexpr int HD = 128;
+  const int blk = blockIdx.x, h = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int64_t bh = b * H + h;
+  const int warp = warp_id(), lane = lane_id();
+  const int dim = H * HD;
+  const float qmax = (QK == FD_QK_INT8) ? 127.0f : 448.0f;
+  const int chunk = (int)((s_off + (int64_t)blk * 128) / 128);
+  const float4 wq = reinterpret_cast<const float4*>(qw)[lane];
+  const float4 wk = reinterpret_cast<const float4*>(kw)[lane];
+  const float wqa[4] = {wq.x, wq.y, wq.z, wq.w};
+  const float wka[4] = {wk.x, wk.y, wk.z, wk.w};
+  __shared__ float sh_k[8][128];
+  __shared__ float sh_v[8][128];
+  __shared__ float sh_q[8];
+  __shared__ uint2 sh_qkeep[128][32];  // per-block Q: the block's bf16 Q rows until its absmax is known
+  float ksum[4] = {0.f, 0.f, 0.f, 0.f}, vmax[4] = {0.f, 0.f, 0.f, 0.f};
+  float bmax = 0.f;
+#pragma unroll 2
+  for (int i = 0; i < 16; ++i) {
+    const int r = warp + 8 * i;  // row within the block
+    const int64_t s = (int64_t)blk * 128 + r;
+    const int64_t n = s_off + s;  // joint row
+    if (s >= S) {
+      if (q_gran == FD_GRAN_TOKEN && lane == 0 && n < q_desc_stride && s_off + S == N)
+        q_desc[bh * q_desc_stride + n] = 0.f;
+      continue;
+    }
+    const int64_t row = b * S + s;
+    const __nv_bfloat16* base = qkv + row * 3 * dim + h * HD + lane * 4;
+    const uint2 uq = *reinterpret_cast<const uint2*>(base);
+    const uint2 uk = *reinterpret_cast<const uint2*>(base + dim);
+    const uint2 uv = *reinterpret_cast<const uint2*>(base + 2 * dim);
+    float q[4] = {bf16_bits_to_f32(uq.x & 0xFFFF), bf16_bits_to_f32(uq.x >> 16),
+                  bf16_bits_to_f32(uq.y & 0xFFFF), bf16_bits_to_f32(uq.y >> 16)};
+    float k[4] = {bf16_bits_to_f32(uk.x & 0xFFFF), bf16_bits_to_f32(uk.x >> 16),
+                  bf16_bits_to_f32(uk.y & 0xFFFF), bf16_bits_to_f32(uk.y >> 16)};
+    float sq = q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3];
+    float sk = k[0] * k[0] + k[1] * k[1] + k[2] * k[2] + k[3] * k[3];
+    sq = warp_sum(sq);
+    sk = warp_sum(sk);
+    const float rq = div_full(1.0f, sqrt_approx(div_full(sq, (float)HD) + eps));
+    const float rk = div_full(1.0f, sqrt_approx(div_full(sk, (float)HD) + eps));
+    float qo[4], ko[4];
+    const float4* fr = reinterpret_cast<const float4*>(freqs + row * 256) + lane * 2;
+#pragma unroll
+    for (int pp = 0; pp < 2; ++pp) {
+      const float4 f = fr[pp];
+      const float qe = (q[2 * pp] * rq) * wqa[2 * pp], qd = (q[2 * pp + 1] * rq) * wqa[2 * pp + 1];
+      const float ke = (k[2 * pp] * rk) * wka[2 * pp], kd = (k[2 * pp + 1] * rk) * wka[2 * pp + 1];
+      qo[2 * pp] = round_to_bf16(f.x * qe + f.y * qd);
+      qo[2 * pp + 1] = round_to_bf16(f.z * qe + f.x * qd);
+      ko[2 * pp] = round_to_bf16(f.x * ke + f.y * kd);
+      ko[2 * pp + 1] = round_to_bf16(f.z * ke + f.x * kd);
+    }
+    const int64_t o = (bh * N + n) * HD + lane * 4;
+    *reinterpret_cast<uint2*>(k_out + o) = make_uint2(pack_bf16x2(ko[0], ko[1]), pack_bf16x2(ko[2], ko[3]));
+    *reinterpret_cast<uint2*>(v_out + o) = uv;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ksum[e] += ko[e];
+    if (do_v) {
+      const float v[4] = {bf16_bits_to_f32(uv.x & 0xFFFF), bf16_bits_to_f32(uv.x >> 16),
+                          bf16_bits_to_f32(uv.y & 0xFFFF), bf16_bits_to_f32(uv.y >> 16)};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) vmax[e] = fmaxf(vmax[e], fabsf(v[e]));
+    }
+    const float qa = fmaxf(fmaxf(fabsf(qo[0]), fabsf(qo[1])), fmaxf(fabsf(qo[2]), fabsf(qo[3])));
+    if (q_gran == FD_GRAN_TOKEN) {
+      const float am = warp_max(qa);
+      const float inv = div_full(qmax, fmaxf(am, 1e-12f));
+      const uint32_t c = quant_code<QK>(qo[0], inv) | (quant_code<QK>(qo[1], inv) << 8) |
+                         (quant_code<QK>(qo[2], inv) << 16) | (quant_code<QK>(qo[3], inv) << 24);
+      *reinterpret_cast<uint32_t*>(q_codes + (bh * N + n) * HD + lane * 4) = c;
+      if (lane == 0) q_desc[bh * q_desc_stride + n] = div_full(am, qmax) * sm_scale_log2e;
+    } else {
+      bmax = fmaxf(bmax, qa);
+      sh_qkeep[r][lane] = make_uint2(pack_bf16x2(qo[0], qo[1]), pack_bf16x2(qo[2], qo[3]));
+    }
+  }
+  // K column sums and V column absmax of this block -> workspace slot (bh, chunk)
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    sh_k[warp][lane * 4 + e] = ksum[e];
+    sh_v[warp][lane * 4 + e] = vmax[e];
+  }
+  if (q_gran == FD_GRAN_BLOCK) {
+    bmax = warp_max(bmax);
+    if (lane == 0) sh_q[warp] = bmax;
+  }
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    const int c = threadIdx.x;
+    float t = 0.f, a = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      t += sh_k[w][c];
+      a = fmaxf(a, sh_v[w][c]);
+    }
+    ws_sum[(bh * nchunks + chunk) * 128 + c] = t;
+    if (do_v) ws_amax[(bh * nchunks + chunk) * 128 + c] = a;
+  }
+  if (q_gran == FD_GRAN_BLOCK) {
+    float m = sh_q[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, sh_q[w]);
+    if (threadIdx.x == 0) q_desc[bh * q_desc_stride + chunk] = div_full(m, qmax) * sm_scale_log2e;
+    const float inv = div_full(qmax, fmaxf(m, 1e-12f));
+#pragma unroll 4
+    for (int i = 0; i < 16; ++i) {
+      const int r = warp + 8 * i;
+      const int64_t s = (int64_t)blk * 128 + r;
+      if (s >= S) continue;
+      const uint2 u = sh_qkeep[r][lane];  // written by this same thread
+      const float v4[4] = {__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                           __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u)};
+      const uint32_t c = quant_code<QK>(v4[0], inv) | (quant_code<QK>(v4[1], inv) << 8) |
+                         (quant_code<QK>(v4[2], inv) << 16) | (quant_code<QK>(v4[3], inv) << 24);
+      *reinterpret_cast<uint32_t*>(q_codes + (bh * N + s_off + s) * HD + lane * 4) = c;
+    }
+  }
+}
+
 }  // namespace fd
 
 using namespace fd;
@@ -390,7 +534,7 @@ extern "C" int fd_attn_quant(const void* q, const void* k, const void* v, int64_
   quant_kernel<QK><<<grid, 256, 0, st>>>(                                                       \
       (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, N, nchunks,   \
       smooth_k, q_gran, k_gran, pv_fp8, sm_scale_log2e, (uint8_t*)q_codes, q_desc,              \
-      (uint8_t*)k_codes, k_desc, (uint8_t*)v_codes, v_desc, k_mean, ws_sum, ws_amax, qs, ks)
+      (uint8_t*)k_codes, k_desc, (uint8_t*)v_codes, v_desc, k_mean, ws_sum, ws_amax, qs, ks, 0)
   if (qk_kind == FD_QK_INT8) FD_Q_LAUNCH(FD_QK_INT8);
   else FD_Q_LAUNCH(FD_QK_FP8);
 #undef FD_Q_LAUNCH
@@ -454,4 +598,77 @@ extern "C" int fd_attn_quant_noalloc(const void* q, const void* k, const void* v
   if (rc) return rc;
   return fd_attn_quant(q, k, v, BH, N, smooth_k, qk_kind, q_gran, k_gran, pv_kind, sm_scale_log2e,
                        q_codes, q_desc, k_codes, k_desc, v_codes, v_desc, k_mean, ws, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Fused P3 + prologue: fd_qkv_postprocess_quant once per stream, then
+// fd_attn_quant_kv once.  Workspace: fd_qkv_quant_workspace_floats(BH, N) floats.
+extern "C" int64_t fd_qkv_quant_workspace_floats(int64_t BH, int64_t N) { return 2 * BH * ((N + 127) / 128) * 128; }
+
+extern "C" int fd_qkv_postprocess_quant(const void* qkv, const float* qw, const float* kw, const float* freqs,
+                                        int64_t B, int64_t S, int64_t H, float eps, int64_t N, int64_t s_off,
+                                        int qk_kind, int q_gran, int pv_kind, float sm_scale_log2e,
+                                        void* q_codes, float* q_desc, void* k_out, void* v_out,
+                                        float* workspace, void* stream) {
+  FD_CHECK_ARG(B > 0 && S > 0 && H > 0 && B <= 65535 && H <= 65535, "bad shape");
+  FD_CHECK_ARG(s_off >= 0 && s_off % 128 == 0 && s_off + S <= N, "s_off must be a multiple of 128 inside N");
+  FD_CHECK_ARG(S % 128 == 0 || s_off + S == N, "only the last stream may end mid-block");
+  FD_CHECK_ARG(qk_kind == FD_QK_INT8 || qk_kind == FD_QK_FP8, "bad qk_kind");
+  FD_CHECK_ARG(q_gran == FD_GRAN_TOKEN || q_gran == FD_GRAN_BLOCK, "bad q_gran");
+  FD_CHECK_ARG(qkv && qw && kw && freqs && q_codes && q_desc && k_out && v_out && workspace, "null pointer");
+  FD_CHECK_ARG(aligned8(qkv) && aligned16(qw) && aligned16(kw) && aligned16(freqs) && aligned8(k_out) &&
+                   aligned8(v_out) && (reinterpret_cast<uintptr_t>(q_codes) & 3) == 0,
+               "misaligned pointer");
+  const int nchunks = (int)((N + 127) / 128);
+  float* ws_sum = workspace;
+  float* ws_amax = workspace + B * H * nchunks * 128;
+  const int64_t qs = fd_desc_stride(N, q_gran, 128);
+  dim3 grid((unsigned)((S + 127) / 128), (unsigned)H, (unsigned)B);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int do_v = pv_kind == FD_PV_FP8;
+#define FD_QQ(QK)                                                                                         \
+  qkv_quant_kernel<QK><<<grid, 256, 0, st>>>((const __nv_bfloat16*)qkv, qw, kw, freqs, S, (int)H, eps, N, \
+                                             s_off, q_gran, sm_scale_log2e, (uint8_t*)q_codes, q_desc, qs, \
+                                             (__nv_bfloat16*)k_out, (__nv_bfloat16*)v_out, ws_sum, ws_amax,  \
+                                             nchunks, do_v)
+  if (qk_kind == FD_QK_INT8) FD_QQ(FD_QK_INT8);
+  else FD_QQ(FD_QK_FP8);
+#undef FD_QQ
+  return check_launch("qkv_postprocess_quant");
+}
+
+extern "C" int fd_attn_quant_kv(const void* k, const void* v, int64_t BH, int64_t N, int smooth_k, int qk_kind,
+                                int k_gran, int pv_kind, void* k_codes, float* k_desc, void* v_codes,
+                                float* v_desc, float* k_mean, float* workspace, void* stream) {
+  FD_CHECK_ARG(BH > 0 && N > 0 && BH <= 65535, "bad shape");
+  FD_CHECK_ARG(qk_kind == FD_QK_INT8 || qk_kind == FD_QK_FP8, "bad qk_kind");
+  FD_CHECK_ARG(k_gran == FD_GRAN_TOKEN || k_gran == FD_GRAN_BLOCK, "bad granularity");
+  FD_CHECK_ARG(pv_kind == FD_PV_BF16 || pv_kind == FD_PV_FP8, "bad pv_kind");
+  FD_CHECK_ARG(k && k_codes && k_desc && workspace, "null pointer");
+  FD_CHECK_ARG(pv_kind == FD_PV_BF16 || (v && v_codes && v_desc), "null V pointer");
+  FD_CHECK_ARG(aligned16(k) && (v == nullptr || aligned16(v)) && aligned8(k_codes) &&
+                   (v_codes == nullptr || aligned8(v_codes)),
+               "misaligned pointer");
+  const int nchunks = (int)((N + 127) / 128);
+  float* ws_sum = workspace;
+  float* ws_amax = workspace + BH * nchunks * 128;
+  const int pv_fp8 = pv_kind == FD_PV_FP8;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (smooth_k || pv_fp8) {
+    colstats_final_kernel<<<(unsigned)BH, 128, 0, st>>>(ws_sum, ws_amax, N, nchunks, smooth_k, pv_fp8, k_mean,
+                                                        v_desc);
+    const int rc = check_launch("attn_quant_kv final");
+    if (rc) return rc;
+  }
+  const int64_t ks = fd_desc_stride(N, k_gran, 64);
+  dim3 grid((unsigned)((N + 127) / 128), (unsigned)BH, pv_fp8 ? 2u : 1u);
+#define FD_KV(QK)                                                                                         \
+  quant_kernel<QK><<<grid, 256, 0, st>>>(nullptr, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, N,    \
+                                         nchunks, smooth_k, FD_GRAN_TOKEN, k_gran, pv_fp8, 1.0f, nullptr, \
+                                         nullptr, (uint8_t*)k_codes, k_desc, (uint8_t*)v_codes, v_desc,   \
+                                         k_mean, ws_sum, ws_amax, 0, ks, 1)
+  if (qk_kind == FD_QK_INT8) FD_KV(FD_QK_INT8);
+  else FD_KV(FD_QK_FP8);
+#undef FD_KV
+  return check_launch("attn_quant_kv");
 }

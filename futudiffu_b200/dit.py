@@ -50,7 +50,7 @@ from .fused_kernels import (
     fused_rms_norm_modulate_quant,
     qkv_postprocess_into,
 )
-from .sage_attention import _attn_forward, attn_forward_quant_out
+from .sage_attention import _attn_forward, attn_forward_quant_out, attn_quant_out_from_streams, fused_prologue_ok
 
 HEAD_DIM = 128
 
@@ -157,6 +157,23 @@ def joint_attention(q: Tensor, k: Tensor, v: Tensor, cfg: DiTConfig) -> Tensor:
     return o
 
 
+def joint_prologue_attention(streams, cfg: DiTConfig, N: int, regions, split=None) -> None:
+    """Attention straight from the QKV linear outputs of the streams of a joint
+    attention: P3 fused with the quantisation prologue when the streams are
+    128-row aligned (else P3 into joint Q/K/V buffers and the separate prologue),
+    output written as the out-projections' 1 x 128 e4m3 input into ``regions``."""
+    if fused_prologue_ok([st[0].shape[1] for st in streams]):
+        attn_quant_out_from_streams(streams, cfg.heads, N, None, block_mask=None, qk_quant=cfg.qk_quant,
+                                    pv_quant=cfg.pv_quant, granularity=cfg.granularity, regions=regions,
+                                    split=split)
+        return
+    B, dev = streams[0][0].shape[0], streams[0][0].device
+    q, k, v = (torch.empty(B, cfg.heads, N, HEAD_DIM, dtype=torch.bfloat16, device=dev) for _ in range(3))
+    for qkv, qn, kn, fr, off, eps in streams:
+        qkv_postprocess_into(qkv, qn, kn, fr, q, k, v, off, eps)
+    joint_attention_codes(q, k, v, cfg, regions, split)
+
+
 def joint_attention_codes(q: Tensor, k: Tensor, v: Tensor, cfg: DiTConfig, regions, split=None) -> None:
     """Quantized attention written straight as the output linears' 1 x 128 e4m3
     input (codes + scales) into ``regions`` (see attn_forward_quant_out)."""
@@ -203,23 +220,21 @@ class DoubleStreamBlock(nn.Module):
         cfg = self.cfg
         B, Nt = x_txt.shape[0], x_txt.shape[1]
         N = Nt + x_img.shape[1]
-        # joint Q/K/V: each stream's post-processing writes its rows in place
-        q, k, v = (torch.empty(B, cfg.heads, N, HEAD_DIM, dtype=torch.bfloat16, device=x_txt.device)
-                   for _ in range(3))
-        mods = []
-        for st, x, fr, off in ((self.txt, x_txt, freqs_txt, 0), (self.img, x_img, freqs_img, Nt)):
+        mods, qkvs = [], []
+        for st, x in ((self.txt, x_txt), (self.img, x_img)):
             m = st.modulation(vec)
             mods.append(m)
             # norm + 1 x 128 quant in one pass, straight into the QKV GEMM
             h8, h_s = fused_rms_norm_modulate_quant(x, st.norm_w[0], m[0].contiguous(), cfg.eps)
-            qkv = gemm_bf16(h8, h_s, st.qkv)
-            qkv_postprocess_into(qkv, st.q_norm, st.k_norm, fr, q, k, v, off, cfg.eps)
+            qkvs.append(gemm_bf16(h8, h_s, st.qkv))
         # attention output as each stream's out-projection input: text rows to one
         # code buffer, image rows to the other (no split copy, no separate quantiser)
         dev, D = x_txt.device, cfg.hidden
         codes = [(torch.empty(B, n, D, dtype=torch.float8_e4m3fn, device=dev),
                   torch.empty(B, n, D // 128, dtype=torch.float32, device=dev)) for n in (Nt, N - Nt)]
-        joint_attention_codes(q, k, v, cfg, codes, split=Nt)
+        streams = [(qkvs[0], self.txt.q_norm, self.txt.k_norm, freqs_txt, 0, cfg.eps),
+                   (qkvs[1], self.img.q_norm, self.img.k_norm, freqs_img, Nt, cfg.eps)]
+        joint_prologue_attention(streams, cfg, N, codes, split=Nt)
         outs = []
         for st, x, (o8, o_sc), m in ((self.txt, x_txt, codes[0], mods[0]), (self.img, x_img, codes[1], mods[1])):
             a = gemm_bf16(o8, o_sc, st.proj)
@@ -266,8 +281,8 @@ class SingleStreamBlock(nn.Module):
         cat8 = torch.empty(B, N, W, dtype=torch.float8_e4m3fn, device=x.device)
         cat_s = torch.empty(B, N, W // 128, dtype=torch.float32, device=x.device)
         fp8_gemm_gelu_tanh_quant(a8, a_s, w[n_qkv:], ws[n_qkv // 128:], out=(cat8[..., D:], cat_s[..., D // 128:]))
-        q, k, v = fused_qkv_postprocess(qkv, self.q_norm, self.k_norm, freqs, cfg.heads, HEAD_DIM, cfg.eps)
-        joint_attention_codes(q, k, v, cfg, [(cat8[..., :D], cat_s[..., :D // 128])])
+        joint_prologue_attention([(qkv, self.q_norm, self.k_norm, freqs, 0, cfg.eps)], cfg, N,
+                                 [(cat8[..., :D], cat_s[..., :D // 128])])
         y = fp8_gemm_blockwise(cat8, cat_s, self.linear2.weight, self.linear2.weight_scale,
                                output_dtype=torch.bfloat16)
         return fused_rms_norm_gate_residual(y, self.norm_w[1], gate.contiguous(), x, cfg.eps)

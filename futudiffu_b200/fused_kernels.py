@@ -69,8 +69,12 @@ def qkv_postprocess_into(qkv, q_norm_weight, k_norm_weight, freqs_cis, q_out, k_
     assert qkv.is_contiguous() and q_out.is_contiguous() and k_out.is_contiguous() and v_out.is_contiguous()
     assert freqs_cis.dtype == torch.float32 and freqs_cis.is_contiguous()
     L.require_cuda(qkv, q_out)
-    L.call("fd_qkv_postprocess_into", L.ptr(qkv), L.ptr(q_norm_weight.float().contiguous()),
-           L.ptr(k_norm_weight.float().contiguous()), L.ptr(freqs_cis), L.ptr(q_out), L.ptr(k_out), L.ptr(v_out),
+    # the fp32 copies must stay referenced until the launch: a temporary freed
+    # inside the argument list could hand its block to the next one
+    qw = q_norm_weight.float().contiguous()
+    kw = k_norm_weight.float().contiguous()
+    L.call("fd_qkv_postprocess_into", L.ptr(qkv), L.ptr(qw),
+           L.ptr(kw), L.ptr(freqs_cis), L.ptr(q_out), L.ptr(k_out), L.ptr(v_out),
            B, S, H, hd, float(norm_eps), S_total, seq_offset, L.stream_ptr(qkv.device))
 
 

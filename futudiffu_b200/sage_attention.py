@@ -179,6 +179,103 @@ def _attn_forward(
     return out.reshape(B, H, N, D), lse
 
 
+def _freqs_rows(freqs: Tensor, B: int, S: int) -> Tensor:
+    """(B, S, [1,] 64, 2, 2) RoPE rotations as contiguous fp32 rows."""
+    if freqs.ndim == 6:
+        assert freqs.shape[2] == 1
+        freqs = freqs.squeeze(2)
+    return freqs.reshape(B * S, 64, 2, 2).to(torch.float32).contiguous()
+
+
+def fused_prologue_ok(stream_lengths: list[int]) -> bool:
+    """Streams laid out back to back qualify for the fused P3 + prologue when every
+    stream but the last holds a multiple of 128 rows (blocks never straddle)."""
+    return all(n % 128 == 0 for n in stream_lengths[:-1])
+
+
+def quantize_qkv_streams(
+    streams: list[tuple], H: int, N: int, sm_scale: float | None, *, smooth_k: bool, qk_quant: str,
+    granularity: str, pv_quant: str,
+) -> dict:
+    """P3 (per-head Q/K RMSNorm + RoPE) fused with the attention prologue, for
+    attention inputs straight from the QKV linear(s).  ``streams``: one
+    (qkv (B, S, 3 H 128) bf16, q_norm_w, k_norm_w, freqs (B, S, [1,] 64, 2, 2), s_off,
+    eps) per stream of a joint attention, rows [s_off, s_off + S) of the N joint
+    rows (see fused_prologue_ok).  Returns quantize_qkv's dict plus the bf16 K and
+    V ("k", "v", (B H, N, 128)); codes and scales equal fused_qkv_postprocess /
+    qkv_postprocess_into followed by quantize_qkv."""
+    qkv0 = streams[0][0]
+    B, dev = qkv0.shape[0], qkv0.device
+    BH = B * H
+    D = 128
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    qk = L.QK_INT8 if qk_quant == "int8" else L.QK_FP8
+    gran = L.GRAN_TOKEN if granularity == "per_token" else L.GRAN_BLOCK
+    pv = L.PV_FP8 if pv_quant == "fp8" else L.PV_BF16
+    code_dt = torch.int8 if qk == L.QK_INT8 else torch.float8_e4m3fn
+    q_codes = torch.empty(BH, N, D, dtype=code_dt, device=dev)
+    q_desc = torch.empty(BH, _desc_stride(N, gran, 128), dtype=torch.float32, device=dev)
+    k = torch.empty(BH, N, D, dtype=torch.bfloat16, device=dev)
+    v = torch.empty(BH, N, D, dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(int(L.lib().fd_qkv_quant_workspace_floats(BH, N)), dtype=torch.float32, device=dev)
+    stream_ptr = L.stream_ptr(dev)
+    for qkv, qw, kw, freqs, s_off, eps in streams:
+        Bq, S, C = qkv.shape
+        assert Bq == B and C == 3 * H * D and qkv.dtype == torch.bfloat16 and qkv.is_contiguous()
+        fr = _freqs_rows(freqs, B, S)
+        # keep the fp32 copies referenced until the launch (a temporary freed inside
+        # the argument list could hand its memory to the next one)
+        qw32, kw32 = qw.float().contiguous(), kw.float().contiguous()
+        L.call("fd_qkv_postprocess_quant", L.ptr(qkv), L.ptr(qw32), L.ptr(kw32),
+               L.ptr(fr), B, S, H, float(eps), N, s_off, qk, gran, pv, float(sm_scale * _LOG2E), L.ptr(q_codes),
+               L.ptr(q_desc), L.ptr(k), L.ptr(v), L.ptr(ws), stream_ptr)
+    k_codes = torch.empty(BH, N, D, dtype=code_dt, device=dev)
+    k_desc = torch.empty(BH, _desc_stride(N, gran, 64), dtype=torch.float32, device=dev)
+    k_mean = torch.empty(BH, D, dtype=torch.float32, device=dev)
+    v_codes = torch.empty(BH, N, D, dtype=torch.float8_e4m3fn, device=dev) if pv == L.PV_FP8 else None
+    v_desc = torch.empty(BH, D, dtype=torch.float32, device=dev) if pv == L.PV_FP8 else None
+    L.call("fd_attn_quant_kv", L.ptr(k), L.ptr(v), BH, N, int(bool(smooth_k)), qk, gran, pv, L.ptr(k_codes),
+           L.ptr(k_desc), L.ptr(v_codes), L.ptr(v_desc), L.ptr(k_mean), L.ptr(ws), stream_ptr)
+    return {
+        "q_codes": q_codes, "q_desc": q_desc, "k_codes": k_codes, "k_desc": k_desc,
+        "v_codes": v_codes, "v_desc": v_desc, "k_mean": k_mean, "qk": qk, "gran": gran, "pv": pv,
+        "k": k, "v": v, "B": B, "H": H, "N": N,
+    }
+
+
+def _quant_out_call(qz: dict, vsrc: Tensor, B: int, H: int, N: int, block_mask: Tensor | None,
+                    regions: list[tuple[Tensor, Tensor]], split: int | None, dev) -> None:
+    D = 128
+    split = N if split is None else split
+    assert 1 <= split <= N and len(regions) == (1 if split == N else 2)
+    bm, bm_stride = _normalize_mask(block_mask, N)
+    reg = []
+    for i, (c, sc) in enumerate(regions):
+        rows = B * (split if i == 0 else N - split)
+        assert c.dtype in (torch.float8_e4m3fn, torch.uint8) and sc.dtype == torch.float32
+        assert c.stride(-1) == 1 and sc.stride(-1) == 1
+        assert c.numel() // c.shape[-1] >= rows and c.shape[-1] >= H * D and sc.shape[-1] >= H
+        reg.append((L.ptr(c), L.ptr(sc), c.stride(-2), sc.stride(-2)))
+    if len(reg) == 1:
+        reg.append((None, None, 0, 0))
+    L.call("fd_sage_attn_fwd_quant_out", L.ptr(qz["q_codes"]), L.ptr(qz["q_desc"]), L.ptr(qz["k_codes"]),
+           L.ptr(qz["k_desc"]), L.ptr(vsrc), L.ptr(qz["v_desc"]), L.ptr(bm), bm_stride, None, B * H, N, H,
+           qz["qk"], qz["gran"], qz["gran"], qz["pv"], *reg[0], *reg[1], split, L.stream_ptr(dev))
+
+
+def attn_quant_out_from_streams(
+    streams: list[tuple], H: int, N: int, sm_scale: float | None, *, block_mask: Tensor | None, qk_quant: str,
+    pv_quant: str, granularity: str, regions: list[tuple[Tensor, Tensor]], split: int | None = None,
+) -> None:
+    """quantize_qkv_streams + the quantised-output attention (attn_forward_quant_out)
+    for attention inputs straight from the QKV linear(s)."""
+    qz = quantize_qkv_streams(streams, H, N, sm_scale, smooth_k=_SAGE_SMOOTH_K, qk_quant=qk_quant,
+                              granularity=granularity, pv_quant=pv_quant)
+    vsrc = qz["v_codes"] if qz["pv"] == L.PV_FP8 else qz["v"]
+    _quant_out_call(qz, vsrc, qz["B"], H, N, block_mask, regions, split, qz["k"].device)
+
+
 def attn_forward_quant_out(
     q: Tensor, k: Tensor, v: Tensor, sm_scale: float | None, *, block_mask: Tensor | None, qk_quant: str,
     pv_quant: str, granularity: str, regions: list[tuple[Tensor, Tensor]], split: int | None = None,
@@ -195,28 +292,14 @@ def attn_forward_quant_out(
     L.require_cuda(q, k, v)
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
-    split = N if split is None else split
-    assert 1 <= split <= N and len(regions) == (1 if split == N else 2)
     BH = B * H
     qf = q.reshape(BH, N, D).contiguous()
     kf = k.reshape(BH, N, D).contiguous()
     vf = v.reshape(BH, N, D).contiguous()
-    bm, bm_stride = _normalize_mask(block_mask, N)
     qz = quantize_qkv(qf, kf, vf, sm_scale, smooth_k=_SAGE_SMOOTH_K, qk_quant=qk_quant,
                       granularity=granularity, pv_quant=pv_quant)
     vsrc = qz["v_codes"] if qz["pv"] == L.PV_FP8 else vf
-    reg = []
-    for i, (c, sc) in enumerate(regions):
-        rows = B * (split if i == 0 else N - split)
-        assert c.dtype in (torch.float8_e4m3fn, torch.uint8) and sc.dtype == torch.float32
-        assert c.stride(-1) == 1 and sc.stride(-1) == 1
-        assert c.numel() // c.shape[-1] >= rows and c.shape[-1] >= H * D and sc.shape[-1] >= H
-        reg.append((L.ptr(c), L.ptr(sc), c.stride(-2), sc.stride(-2)))
-    if len(reg) == 1:
-        reg.append((None, None, 0, 0))
-    L.call("fd_sage_attn_fwd_quant_out", L.ptr(qz["q_codes"]), L.ptr(qz["q_desc"]), L.ptr(qz["k_codes"]),
-           L.ptr(qz["k_desc"]), L.ptr(vsrc), L.ptr(qz["v_desc"]), L.ptr(bm), bm_stride, None, BH, N, H,
-           qz["qk"], qz["gran"], qz["gran"], qz["pv"], *reg[0], *reg[1], split, L.stream_ptr(q.device))
+    _quant_out_call(qz, vsrc, B, H, N, block_mask, regions, split, q.device)
 
 
 def _pv_for(default_pv: str) -> str:

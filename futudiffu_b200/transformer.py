@@ -49,7 +49,7 @@ from .fused_kernels import (
     rms_norm_modulate_quant_ranges,
     rms_norm_modulate_ranges,
 )
-from .sage_attention import _attn_forward, _pv_for, attn_forward_quant_out, get_sage_config
+from .sage_attention import _attn_forward, _pv_for, attn_quant_out_from_streams, get_sage_config
 
 HEAD_DIM = 128
 
@@ -274,13 +274,15 @@ class JointAttention(nn.Module):
     def core_codes(self, qkv: Tensor, freqs_cis: Tensor, block_mask: Tensor) -> tuple[Tensor, Tensor]:
         """``core`` with the output written as the output linear's 1 x 128 e4m3 input
         (codes (B, L, dim), scales (B, L, dim / 128)), equal to fp8_act_quant(core(...))."""
-        xq, xk, xv = self._qkv(qkv, freqs_cis)
         B, Lq, dim = qkv.shape[0], qkv.shape[1], qkv.shape[2] // 3
         o8 = torch.empty(B, Lq, dim, dtype=torch.float8_e4m3fn, device=qkv.device)
         o_s = torch.empty(B, Lq, dim // 128, dtype=torch.float32, device=qkv.device)
         cfg = get_sage_config()
-        attn_forward_quant_out(xq, xk, xv, 1.0 / (self.head_dim ** 0.5), block_mask=block_mask, qk_quant="int8",
-                               pv_quant=_pv_for("bf16"), granularity=cfg["qk_granularity"], regions=[(o8, o_s)])
+        # P3 fused with the quantisation prologue, then the quantised-output attention
+        attn_quant_out_from_streams([(qkv.contiguous(), self.q_norm.weight, self.k_norm.weight, freqs_cis, 0,
+                                      self.q_norm.eps)], self.n_local_heads, Lq, 1.0 / (self.head_dim ** 0.5),
+                                    block_mask=block_mask, qk_quant="int8", pv_quant=_pv_for("bf16"),
+                                    granularity=cfg["qk_granularity"], regions=[(o8, o_s)])
         return o8, o_s
 
     def forward(self, x: Tensor, x_mask: Tensor | None, freqs_cis: Tensor, block_mask=None,

@@ -238,6 +238,31 @@ int fd_attn_quant(const void* q, const void* k, const void* v, int64_t BH, int64
                   float* k_desc, void* v_codes, float* v_desc, float* k_mean, float* workspace,
                   void* stream);
 
+/* P3 fused with the attention prologue, for (joint) attention inputs straight
+ * from the QKV linear.  No single counterpart in the reference, which runs
+ * fused_qkv_postprocess (fused_kernels.py:270-471) and then quantises Q/K/V
+ * inside every attention kernel (sage_kernels.py:632-663 and siblings); the
+ * codes and scales equal fd_qkv_postprocess_into followed by fd_attn_quant
+ * (the K smoothing mean is summed in another order, so it may differ from
+ * fd_attn_quant's by one bf16 rounding in rare columns).
+ *  fd_qkv_postprocess_quant, once per stream: qkv (B, S, 3 H 128) bf16 ->
+ *    Q codes (B H, N, 128) + q_desc (as fd_attn_quant's), K and V bf16 into
+ *    rows [s_off, s_off + S) of the joint (B, H, N, 128) buffers, and this
+ *    stream's K column sums / V column absmax (V only for FD_PV_FP8) into the
+ *    workspace.  s_off must be a multiple of 128 and every stream but the one
+ *    ending at N must hold a multiple of 128 rows.
+ *  fd_attn_quant_kv, once after every stream: K smoothing mean, K codes +
+ *    k_desc, and for FD_PV_FP8 the e4m3 V codes + v_desc (as fd_attn_quant).
+ * workspace: fd_qkv_quant_workspace_floats(B H, N) floats shared by both. */
+int64_t fd_qkv_quant_workspace_floats(int64_t BH, int64_t N);
+int fd_qkv_postprocess_quant(const void* qkv, const float* qw, const float* kw, const float* freqs, int64_t B,
+                             int64_t S, int64_t H, float eps, int64_t N, int64_t s_off, int qk_kind, int q_gran,
+                             int pv_kind, float sm_scale_log2e, void* q_codes, float* q_desc, void* k_out,
+                             void* v_out, float* workspace, void* stream);
+int fd_attn_quant_kv(const void* k, const void* v, int64_t BH, int64_t N, int smooth_k, int qk_kind, int k_gran,
+                     int pv_kind, void* k_codes, float* k_desc, void* v_codes, float* v_desc, float* k_mean,
+                     float* workspace, void* stream);
+
 /* No counterpart in the reference.  fd_attn_quant with no workspace argument:
  * the scratch lives in a fixed device array inside the library (one per GPU
  * that loads it, FD_NOALLOC_WS_FLOATS floats = 4 MiB, held until exit), so

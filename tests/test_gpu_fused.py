@@ -126,8 +126,11 @@ def test_rms_norm_modulate_quant(cuda_device, B, S, dim, wdt):
     assert torch.equal(ys.cpu(), rs.reshape(B, S, dim // 128).cpu())
 
 
-def test_qkv_postprocess_into_joint_buffer(cuda_device):
-    """Writing two streams into one joint buffer equals concatenating their outputs."""
+@pytest.mark.parametrize("wdt", [torch.float32, torch.bfloat16])
+def test_qkv_postprocess_into_joint_buffer(cuda_device, wdt):
+    """Writing two streams into one joint buffer equals concatenating their outputs
+    (bf16 norm weights: the wrapper's fp32 copies of Q's and K's weights must stay
+    distinct until the launch)."""
     from futudiffu_b200.fused_kernels import fused_qkv_postprocess, qkv_postprocess_into
 
     B, H = 2, 3
@@ -137,8 +140,8 @@ def test_qkv_postprocess_into_joint_buffer(cuda_device):
         qkv = torch.randn(B, S, 3 * H * 128, generator=g).to(torch.bfloat16).to(cuda_device)
         fr = torch.randn(B, S, 64, 2, 2, generator=g).to(cuda_device)
         parts.append((qkv, fr))
-    qw = (1 + 0.1 * torch.randn(128, generator=g)).to(cuda_device)
-    kw = (1 + 0.1 * torch.randn(128, generator=g)).to(cuda_device)
+    qw = (1 + 0.1 * torch.randn(128, generator=g)).to(wdt).to(cuda_device)
+    kw = (1 + 0.1 * torch.randn(128, generator=g)).to(wdt).to(cuda_device)
     N = 5 + 131
     q, k, v = (torch.empty(B, H, N, 128, dtype=torch.bfloat16, device=cuda_device) for _ in range(3))
     off = 0
@@ -149,3 +152,53 @@ def test_qkv_postprocess_into_joint_buffer(cuda_device):
         off += qkv.shape[1]
     for i, t in enumerate((q, k, v)):
         assert torch.equal(t.cpu(), torch.cat([r[i] for r in refs], dim=2).cpu())
+
+
+@pytest.mark.parametrize("qk,gran,pv", [("int8", "per_block", "fp8"), ("int8", "per_token", "bf16"),
+                                        ("fp8", "per_token", "fp8"), ("fp8", "per_block", "bf16")])
+def test_fused_qkv_prologue_matches_unfused(cuda_device, qk, gran, pv):
+    """P3 fused with the quantisation prologue (two streams of a joint attention)
+    gives the Q codes and scales, the bf16 K / V and the V codes of P3 followed by
+    the separate prologue; the K mean (summed in another order) within one bf16
+    rounding, the K codes wherever the means agree."""
+    import math
+
+    from futudiffu_b200.attention import rope_embed
+    from futudiffu_b200.fused_kernels import fused_qkv_postprocess
+    from futudiffu_b200.sage_attention import quantize_qkv, quantize_qkv_streams
+
+    g = gen(71)
+    B, H, S1, S2 = 2, 3, 256, 300
+    N = S1 + S2
+    d = lambda t: t.to(cuda_device)  # noqa: E731
+    qkvs = [d(torch.randn(B, S, 3 * H * 128, generator=g).to(torch.bfloat16)) for S in (S1, S2)]
+    qkvs[0][..., H * 128:2 * H * 128] += 2.0  # a K offset for the smoothing to remove
+    frs = []
+    for S in (S1, S2):
+        pos = torch.arange(S).float()
+        f = torch.cat([rope_embed(pos, 64, 256.0), rope_embed(pos * 0.5, 64, 256.0)], dim=-3)
+        frs.append(d(f.unsqueeze(0).expand(B, S, 64, 2, 2).contiguous()))
+    # bf16 norm weights as the models hold them; the reference P3 is the fused op
+    qw = d((1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16))
+    kw = d((1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16))
+    parts = [fused_qkv_postprocess(qkvs[i], qw, kw, frs[i], H, 128) for i in range(2)]
+    q, k, v = (torch.cat([parts[0][j], parts[1][j]], dim=2) for j in range(3))
+    sm = 1 / math.sqrt(128)
+    BH = B * H
+    ref = quantize_qkv(q.reshape(BH, N, 128), k.reshape(BH, N, 128), v.reshape(BH, N, 128), sm, smooth_k=True,
+                       qk_quant=qk, granularity=gran, pv_quant=pv)
+    got = quantize_qkv_streams([(qkvs[0], qw, kw, frs[0], 0, 1e-5), (qkvs[1], qw, kw, frs[1], S1, 1e-5)], H, N, sm,
+                               smooth_k=True, qk_quant=qk, granularity=gran, pv_quant=pv)
+    assert torch.equal(got["k"], k.reshape(BH, N, 128)) and torch.equal(got["v"], v.reshape(BH, N, 128))
+    assert torch.equal(got["q_codes"].view(torch.uint8), ref["q_codes"].view(torch.uint8))
+    assert torch.equal(got["q_desc"], ref["q_desc"])
+    if pv == "fp8":
+        assert torch.equal(got["v_codes"].view(torch.uint8), ref["v_codes"].view(torch.uint8))
+        assert torch.equal(got["v_desc"], ref["v_desc"])
+    dm = (got["k_mean"] - ref["k_mean"]).abs()
+    assert (dm <= ref["k_mean"].abs() * 2 ** -7 + 1e-30).all()
+    same = (dm == 0).all(dim=1)  # heads whose means agree exactly
+    assert same.float().mean() >= 0.5
+    kc_g, kc_r = got["k_codes"].view(torch.uint8)[same], ref["k_codes"].view(torch.uint8)[same]
+    assert torch.equal(kc_g, kc_r)
+    assert torch.equal(got["k_desc"][same], ref["k_desc"][same])
