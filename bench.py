@@ -432,7 +432,7 @@ def run_dit_reference(args, world, rank):
 
 def run_dit(args, world, rank, local):
     from futudiffu_b200 import check_status
-    from futudiffu_b200.dit import DiT, DiTConfig, euler_step, flops_per_sample_step, sigmas
+    from futudiffu_b200.dit import DiT, DiTConfig, EulerStepGraph, euler_step, flops_per_sample_step, sigmas
 
     if DIT_BATCH % world:
         raise SystemExit(f"batch {DIT_BATCH} does not shard over {world} GPUs")
@@ -456,30 +456,42 @@ def run_dit(args, world, rank, local):
         x = step(i, x)
     torch.cuda.synchronize()
     check_status()
+    # Kernel accounting (not timed as the result): two eager steps with CUDA events
+    # around every GEMM / attention launch and the launch count of one step.
     rec = LaunchRecorder()
+    rec.active = True
+    n_rec = 2
+    for i in range(n_rec):
+        x = step(i, x)
+    rec.active = False
+    torch.cuda.synchronize()
+    gemm_work, gemm_ms, n_gemm = rec.summary("gemm")
+    attn_work, attn_ms, n_attn = rec.summary("attn")
+    launches_per_step = rec.launches // n_rec
+    rec.close()
+    # The timed steps replay the step captured as one CUDA graph (EulerStepGraph).
+    graph = EulerStepGraph(model, x, d_txt)
+    for i in range(2):
+        x = graph(x, d_txt, sig[i % 28], sig[i % 28 + 1])
+    torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else local) as clocks:
-        rec.active = True
         if args.profile:
             torch.cuda.cudart().cudaProfilerStart()
         start.record(stream)
         for i in range(args.steps):
-            x = step(i, x)
+            x = graph(x, d_txt, sig[i % 28], sig[i % 28 + 1])
             if args.profile and i == 0:
                 torch.cuda.synchronize()
                 torch.cuda.cudart().cudaProfilerStop()
         end.record(stream)
-        rec.active = False
         torch.cuda.synchronize()
     barrier(world)
     ms_local = start.elapsed_time(end) / args.steps
     ms = max_over_ranks(ms_local, world, dev)
-    gemm_work, gemm_ms, n_gemm = rec.summary("gemm")
-    attn_work, attn_ms, n_attn = rec.summary("attn")
-    launches = rec.launches
-    rec.close()
+    launches = launches_per_step * args.steps
     check_status()
     value = 1e3 / ms
 
@@ -490,9 +502,7 @@ def run_dit(args, world, rank, local):
     d2h = img.numel() * 2
 
     def e2e_step(i):
-        xi = h_img.to(dev, non_blocking=True)
-        ti = h_txt.to(dev, non_blocking=True)
-        y = euler_step(model, xi, ti, sig[i], sig[i + 1])
+        y = graph(h_img.to(dev, non_blocking=True), h_txt.to(dev, non_blocking=True), sig[i], sig[i + 1])
         h_out.copy_(y, non_blocking=True)
 
     e2e_step(0)
@@ -527,18 +537,19 @@ def run_dit(args, world, rank, local):
                        "model_tflop_per_step": step_flops / 1e12,
                        "model_tflops": step_flops / (ms * 1e-3) / 1e12,
                        "attention_kernel_tops": attn_work / (attn_ms * 1e-3) / 1e12 if attn_ms else None,
-                       "time_share": {"gemm": gemm_ms / args.steps / ms_local, "attention": attn_ms / args.steps / ms_local}},
+                       "time_share": {"gemm": gemm_ms / n_rec / ms_local, "attention": attn_ms / n_rec / ms_local},
+                       "launch": "each timed step replays the step's ~1350 kernels as one captured CUDA graph"},
             "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": peak, "unit": "TFLOP/s",
                          "frac": gemm_tf / peak, "traffic": None,
-                         "kernel": f"gemm_fp8_kernel (all {n_gemm // max(1, args.steps)} GEMM launches of a step, "
-                                   "flop-weighted)",
+                         "kernel": f"gemm_fp8_kernel (all {n_gemm // n_rec} GEMM launches of a step, "
+                                   "flop-weighted, CUDA events per launch over two eager steps)",
                          "peak_source": f"2 x {pk['source']} sustained bf16 dense "
                                         f"({pk['bf16_tflops_sustained']} TF/s, kernels inside a long step): "
                                         "fp8 dense rate is twice bf16"},
             "cpu_baseline": dit_cpu_sample() if world == 1 else None,
             "e2e": {"value": 1e3 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms,
-                    "api": "futudiffu_b200.dit.euler_step"},
+                    "api": "futudiffu_b200.dit.EulerStepGraph (pinned host inputs copied in, result copied out)"},
             "gpu_launches": launches,
             "clocks": clocks.summary(),
         }

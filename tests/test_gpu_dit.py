@@ -94,6 +94,26 @@ def test_dit_forward_and_euler(cuda_device):
     assert torch.isfinite(x1.float()).all() and x1.shape == img.shape
 
 
+def test_euler_step_graph_matches_eager(cuda_device):
+    """The CUDA-graph replay of an Euler step gives the eager step's output bit for
+    bit, step after step (new inputs and sigmas each call)."""
+    from futudiffu_b200.dit import DiT, EulerStepGraph, euler_denoise, euler_step, sigmas
+
+    cfg = _small_cfg(n_double=1, n_single=2, img_grid=(8, 8))
+    model = DiT(cfg, seed=3, device=cuda_device)
+    cg = gen(12)
+    img = torch.randn(2, cfg.img_tokens, cfg.patch_dim, generator=cg).to(torch.bfloat16).to(cuda_device)
+    txt = torch.randn(2, cfg.txt_tokens, cfg.hidden, generator=cg).to(torch.bfloat16).to(cuda_device)
+    g = EulerStepGraph(model, img, txt)
+    s = sigmas(4)
+    xe, xg = img, img
+    for i in range(4):
+        xe = euler_step(model, xe, txt, s[i], s[i + 1])
+        xg = g(xg, txt, s[i], s[i + 1]).clone()
+        assert torch.equal(xe, xg), i
+    assert torch.equal(euler_denoise(model, img, txt, steps=4, graph=True), xe)
+
+
 def test_video_block_single_rank(cuda_device):
     """Video DiT block (Ulysses path at P = 1) against the CPU composition of the oracle ops."""
     from futudiffu_b200.dit import VideoBlock, VideoDiTConfig, video_freqs
