@@ -27,6 +27,14 @@ FD_STATUS_TIMEOUT = 1
 FD_STATUS_BOUNDS = 2
 
 DT_BF16, DT_F16, DT_F32, DT_E4M3, DT_I8 = 0, 1, 2, 3, 4
+GEMM_STORE_BF16 = -1
+
+
+class GemmProblem(ctypes.Structure):
+    """fd_gemm_problem (include/fd_b200.h)."""
+    _fields_ = [("a", ctypes.c_void_p), ("a_s", ctypes.c_void_p), ("b", ctypes.c_void_p), ("b_s", ctypes.c_void_p),
+                ("bias", ctypes.c_void_p), ("c", ctypes.c_void_p), ("c_s", ctypes.c_void_p),
+                ("M", ctypes.c_int64), ("N", ctypes.c_int64), ("K", ctypes.c_int64)]
 QK_INT8, QK_FP8 = 0, 1
 GRAN_TOKEN, GRAN_BLOCK = 0, 1
 PV_BF16, PV_FP8 = 0, 1
@@ -57,6 +65,7 @@ _SIGS: dict[str, list] = {
     "fd_fp8_gemm_blockwise": [_P, _P, _P, _P, _P, _I, _P, _I, _L, _L, _L, _I, _P],
     "fd_fp8_gemm_quant": [_P, _P, _P, _P, _P, _I, _P, _P, _L, _L, _L, _I, _P],
     "fd_fp8_gemm_quant_ld": [_P, _P, _P, _P, _P, _I, _P, _P, _L, _L, _L, _I, _L, _L, _P],
+    "fd_fp8_gemm_grouped2": [_P, _P, _I, _I, _P],
     "fd_fp8_gemm_blockwise_lora": [_P, _P, _P, _P, _P, _I, _P, _I, _L, _L, _L, _P, _P, _L, _P],
     "fd_fp8_silu_gate_quant": [_P, _P, _P, _L, _L, _I, _P],
     "fd_fp8_gelu_tanh_quant": [_P, _P, _P, _L, _L, _I, _P],

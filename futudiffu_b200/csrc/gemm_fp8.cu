@@ -148,11 +148,16 @@ FD_DEV void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-template <int BMODE, int CDT, int BDT, int EPI, bool LORA>
+// GROUPED: two independent problems (p0 with tmA / tmB, p1 with tmLA / tmLB) in one
+// persistent launch; tiles [0, p0.ntiles) belong to p0, the rest to p1, so a small
+// problem (a 512-row text stream) fills the SMs the large one leaves idle.
+template <int BMODE, int CDT, int BDT, int EPI, bool LORA, bool GROUPED>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmLB,
-                    const Params p) {
+                    const Params p0, const Params p1) {
+  static_assert(!(LORA && GROUPED), "LoRA slices and grouped problems share the second tensor maps");
+  const int total_tiles = p0.ntiles + (GROUPED ? p1.ntiles : 0);
   using LY = Layout;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -201,26 +206,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t it = 0;
       bool ok = true;
       uint32_t issued_mask = 0;  // stages with a load issued
-      for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x) {
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        const bool g1 = GROUPED && tile >= p0.ntiles;
+        const Params& p = g1 ? p1 : p0;
+        const CUtensorMap* mA = g1 ? &tmLA : &tmA;
+        const CUtensorMap* mB = g1 ? &tmLB : &tmB;
         int mb, nb;
-        tile_coords(p, tile, mb, nb);
+        tile_coords(p, g1 ? tile - p0.ntiles : tile, mb, nb);
         for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
           uint8_t* sa = smem + s * STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
           mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-          tma_load_2d(sa, &tmA, &full[s], kb * BK, mb * BM);
+          tma_load_2d(sa, mA, &full[s], kb * BK, mb * BM);
           if (EPI == EPI_SILU_GATE) {
             // B rows [w1 block nb | w3 block nb]: the w3 rows start H rows further
-            tma_load_2d(sb, &tmB, &full[s], kb * BK, nb * 128);
-            tma_load_2d(sb + 128 * BK, &tmB, &full[s], kb * BK, p.N + nb * 128);
+            tma_load_2d(sb, mB, &full[s], kb * BK, nb * 128);
+            tma_load_2d(sb + 128 * BK, mB, &full[s], kb * BK, p.N + nb * 128);
           } else if (B_MN) {
             // (K, N) storage: two 128-column panels of the 256-wide tile
-            tma_load_2d(sb, &tmB, &full[s], nb * BN, kb * BK);
-            tma_load_2d(sb + 128 * BK, &tmB, &full[s], nb * BN + 128, kb * BK);
+            tma_load_2d(sb, mB, &full[s], nb * BN, kb * BK);
+            tma_load_2d(sb + 128 * BK, mB, &full[s], nb * BN + 128, kb * BK);
           } else {
-            tma_load_2d(sb, &tmB, &full[s], kb * BK, nb * BN);
+            tma_load_2d(sb, mB, &full[s], kb * BK, nb * BN);
           }
           issued_mask |= 1u << s;
         }
@@ -250,8 +259,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       constexpr uint32_t idesc_lora = make_idesc(/*c F32*/ 1, /*BF16*/ 1, 1, 0, 0, BM, BN);
       uint32_t it = 0;
       bool ok = true;
-      const int nslices = p.kblocks + (LORA ? p.lora_slices : 0);
-      for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x) {
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        const Params& p = (GROUPED && tile >= p0.ntiles) ? p1 : p0;
+        const int nslices = p.kblocks + (LORA ? p.lora_slices : 0);
         for (int kb = 0; kb < nslices; ++kb, ++it) {
           const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
           const uint32_t tb = it % NTBUF, tph = (it / NTBUF) & 1;
@@ -300,9 +310,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     bool ok = true;
     // A thread whose wait timed out keeps walking the tiles (skipping the work)
     // so its partner is never left at the max-exchange barrier.
-    for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++nt) {
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++nt) {
+      const bool g1 = GROUPED && tile >= p0.ntiles;
+      const Params& p = g1 ? p1 : p0;
       int mb, nb;
-      tile_coords(p, tile, mb, nb);
+      tile_coords(p, g1 ? tile - p0.ntiles : tile, mb, nb);
       const int m = mb * BM + r;
       const bool row_ok = m < p.M;
       const float* as_row = p.a_s + (int64_t)(row_ok ? m : 0) * p.kblocks;
@@ -427,10 +439,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) tmem_dealloc(tmem_base, 512);
 }
 
-template <int BMODE, int CDT, int BDT, int EPI = EPI_STORE, bool LORA = false>
+template <int BMODE, int CDT, int BDT, int EPI = EPI_STORE, bool LORA = false, bool GROUPED = false>
 static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t st,
-                  const CUtensorMap* tla = nullptr, const CUtensorMap* tlb = nullptr) {
-  auto kern = gemm_fp8_kernel<BMODE, CDT, BDT, EPI, LORA>;
+                  const CUtensorMap* tla = nullptr, const CUtensorMap* tlb = nullptr, const Params* p1 = nullptr) {
+  auto kern = gemm_fp8_kernel<BMODE, CDT, BDT, EPI, LORA, GROUPED>;
   constexpr uint32_t smem_bytes = Layout::SMEM_BYTES;
   static bool attr_done = false;  // per instantiation
   if (!attr_done) {
@@ -438,8 +450,9 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
     if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "gemm smem attribute: %s", cudaGetErrorString(e));
     attr_done = true;
   }
-  const int grid = p.ntiles < num_sms() ? p.ntiles : num_sms();
-  kern<<<grid, NUM_THREADS, smem_bytes, st>>>(ta, tb, tla ? *tla : ta, tlb ? *tlb : tb, p);
+  const int total = p.ntiles + (GROUPED ? p1->ntiles : 0);
+  const int grid = total < num_sms() ? total : num_sms();
+  kern<<<grid, NUM_THREADS, smem_bytes, st>>>(ta, tb, tla ? *tla : ta, tlb ? *tlb : tb, p, p1 ? *p1 : p);
   return check_launch("fp8_gemm_blockwise");
 }
 
@@ -686,4 +699,83 @@ extern "C" int fd_fp8_gemm_blockwise_lora(const void* a, const float* a_s, const
   p.ldc = N;
   p.ldcs = N / 128;
   return gemm::launch_c<0, true>(c_dtype, bias_dtype, ta, tb, p, (cudaStream_t)stream, &tla, &tlb);
+}
+
+// ---------------------------------------------------------------------------
+// Two problems in one persistent launch (e.g. the text and image streams of a
+// double-stream block, same epilogue): act FD_GEMM_STORE_BF16 stores bf16
+// (+ bias), FD_ACT_* quantise as fd_fp8_gemm_quant.  B stored (N, K); bias
+// FD_DT_BF16 or none.
+static int grouped_problem(const fd_gemm_problem& q, int act, CUtensorMap& ta, CUtensorMap& tb, gemm::Params& p) {
+  const bool quant = act != FD_GEMM_STORE_BF16;
+  FD_CHECK_ARG(q.M > 0 && q.N > 0 && q.K > 0 && q.K % 128 == 0, "bad shape");
+  FD_CHECK_ARG(quant ? q.N % 128 == 0 : q.N % 16 == 0, "bad N");
+  const int64_t nb_rows = act == FD_ACT_SILU_GATE ? 2 * q.N : q.N;
+  FD_CHECK_ARG(q.M < (1ll << 31) && nb_rows < (1ll << 31) && q.K < (1ll << 31), "dimension too large");
+  FD_CHECK_ARG(q.a && q.a_s && q.b && q.b_s && q.c && (!quant || q.c_s), "null pointer");
+  FD_CHECK_ARG(aligned16(q.a) && aligned16(q.b) && aligned16(q.c), "a, b, c must be 16-byte aligned");
+  {
+    const uint64_t dims[2] = {(uint64_t)q.K, (uint64_t)q.M};
+    const uint64_t strides[1] = {(uint64_t)q.K};
+    const uint32_t box[2] = {128, 128};
+    int rc = encode_tiled(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q.a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)q.K, (uint64_t)nb_rows};
+    const uint64_t strides[1] = {(uint64_t)q.K};
+    const uint32_t box[2] = {128, act == FD_ACT_SILU_GATE ? 128u : 256u};
+    int rc = encode_tiled(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q.b, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  p.a_s = q.a_s;
+  p.b_s = q.b_s;
+  p.bias = q.bias;
+  p.c = q.c;
+  p.c_s = q.c_s;
+  p.M = (int)q.M;
+  p.N = (int)q.N;
+  p.K = (int)q.K;
+  p.ntm = (int)((q.M + 127) / 128);
+  p.ntn = act == FD_ACT_SILU_GATE ? (int)(q.N / 128) : (int)((q.N + 255) / 256);
+  p.nbs = (int)((nb_rows + 127) / 128);
+  p.ntiles = p.ntm * p.ntn;
+  p.kblocks = (int)(q.K / 128);
+  p.lora_slices = 0;
+  p.ldc = q.N;
+  p.ldcs = q.N / 128;
+  return FD_OK;
+}
+
+extern "C" int fd_fp8_gemm_grouped2(const fd_gemm_problem* q0, const fd_gemm_problem* q1, int bias_dtype, int act,
+                                    void* stream) {
+  FD_CHECK_ARG(q0 && q1, "null problem");
+  FD_CHECK_ARG(act == FD_GEMM_STORE_BF16 || (act >= FD_ACT_NONE && act <= FD_ACT_SILU_GATE), "bad act");
+  FD_CHECK_ARG((q0->bias == nullptr) == (q1->bias == nullptr), "both problems or neither take a bias");
+  FD_CHECK_ARG(q0->bias == nullptr || bias_dtype == FD_DT_BF16, "grouped GEMM bias must be bf16");
+  CUtensorMap ta0, tb0, ta1, tb1;
+  gemm::Params p0, p1;
+  int rc = grouped_problem(*q0, act, ta0, tb0, p0);
+  if (rc) return rc;
+  rc = grouped_problem(*q1, act, ta1, tb1, p1);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool bias = q0->bias != nullptr;
+  using namespace gemm;
+#define FD_G2(CD, BD, E) return launch<0, CD, BD, E, false, true>(ta0, tb0, p0, st, &ta1, &tb1, &p1)
+  if (act == FD_GEMM_STORE_BF16) {
+    if (bias) FD_G2(FD_DT_BF16, FD_DT_BF16, EPI_STORE);
+    FD_G2(FD_DT_BF16, -1, EPI_STORE);
+  }
+  if (act == FD_ACT_NONE) {
+    if (bias) FD_G2(-1, FD_DT_BF16, EPI_QUANT);
+    FD_G2(-1, -1, EPI_QUANT);
+  }
+  if (act == FD_ACT_GELU_TANH) {
+    if (bias) FD_G2(-1, FD_DT_BF16, EPI_GELU_TANH);
+    FD_G2(-1, -1, EPI_GELU_TANH);
+  }
+  if (bias) FD_G2(-1, FD_DT_BF16, EPI_SILU_GATE);
+  FD_G2(-1, -1, EPI_SILU_GATE);
+#undef FD_G2
 }

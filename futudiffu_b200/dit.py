@@ -42,6 +42,7 @@ from .fp8_kernels import (
     fp8_addmm_blockwise,
     fp8_gemm_blockwise,
     fp8_gemm_gelu_tanh_quant,
+    fp8_gemm_grouped2,
 )
 from .fused_kernels import (
     fused_qkv_postprocess,
@@ -220,13 +221,19 @@ class DoubleStreamBlock(nn.Module):
         cfg = self.cfg
         B, Nt = x_txt.shape[0], x_txt.shape[1]
         N = Nt + x_img.shape[1]
-        mods, qkvs = [], []
-        for st, x in ((self.txt, x_txt), (self.img, x_img)):
-            m = st.modulation(vec)
-            mods.append(m)
-            # norm + 1 x 128 quant in one pass, straight into the QKV GEMM
-            h8, h_s = fused_rms_norm_modulate_quant(x, st.norm_w[0], m[0].contiguous(), cfg.eps)
-            qkvs.append(gemm_bf16(h8, h_s, st.qkv))
+        sts, xs = (self.txt, self.img), [x_txt, x_img]
+        mods = [st.modulation(vec) for st in sts]
+
+        def both(lin_of, ins, act=None):
+            # the two streams' linears as one grouped GEMM launch (the 512-row text
+            # stream alone would leave most SMs idle at small batch)
+            return fp8_gemm_grouped2([(a8, a_s, lin_of(st).weight, lin_of(st).weight_scale, lin_of(st).bias)
+                                      for st, (a8, a_s) in zip(sts, ins)], act=act)
+
+        # norm + 1 x 128 quant in one pass, straight into the QKV GEMMs
+        hs = [fused_rms_norm_modulate_quant(x, st.norm_w[0], m[0].contiguous(), cfg.eps)
+              for st, x, m in zip(sts, xs, mods)]
+        qkvs = both(lambda st: st.qkv, hs)
         # attention output as each stream's out-projection input: text rows to one
         # code buffer, image rows to the other (no split copy, no separate quantiser)
         dev, D = x_txt.device, cfg.hidden
@@ -235,14 +242,15 @@ class DoubleStreamBlock(nn.Module):
         streams = [(qkvs[0], self.txt.q_norm, self.txt.k_norm, freqs_txt, 0, cfg.eps),
                    (qkvs[1], self.img.q_norm, self.img.k_norm, freqs_img, Nt, cfg.eps)]
         joint_prologue_attention(streams, cfg, N, codes, split=Nt)
-        outs = []
-        for st, x, (o8, o_sc), m in ((self.txt, x_txt, codes[0], mods[0]), (self.img, x_img, codes[1], mods[1])):
-            a = gemm_bf16(o8, o_sc, st.proj)
-            x = fused_rms_norm_gate_residual(a, st.norm_w[1], m[1].contiguous(), x, cfg.eps)
-            h8, h_s = fused_rms_norm_modulate_quant(x, st.norm_w[2], m[2].contiguous(), cfg.eps)
-            f = mlp_fp8_q(h8, h_s, st.mlp_in, st.mlp_out)
-            x = fused_rms_norm_gate_residual(f, st.norm_w[3], m[3].contiguous(), x, cfg.eps)
-            outs.append(x)
+        attn = both(lambda st: st.proj, codes)
+        xs = [fused_rms_norm_gate_residual(a, st.norm_w[1], m[1].contiguous(), x, cfg.eps)
+              for st, a, x, m in zip(sts, attn, xs, mods)]
+        hs = [fused_rms_norm_modulate_quant(x, st.norm_w[2], m[2].contiguous(), cfg.eps)
+              for st, x, m in zip(sts, xs, mods)]
+        gs = both(lambda st: st.mlp_in, hs, act=L.ACT_GELU_TANH)   # GELU(tanh) + requant epilogue
+        fs = both(lambda st: st.mlp_out, gs)
+        outs = [fused_rms_norm_gate_residual(f, st.norm_w[3], m[3].contiguous(), x, cfg.eps)
+                for st, f, x, m in zip(sts, fs, xs, mods)]
         return outs[0], outs[1]
 
 

@@ -20,6 +20,7 @@ There is no Triton and no CPU fallback: every function requires CUDA tensors.
 
 from __future__ import annotations
 
+import ctypes
 from typing import Optional, Tuple
 
 import torch
@@ -276,6 +277,41 @@ def _gemm_quant(a, a_s, b, b_s, bias, act, M, N, K, batch_shape, out_dtype, out=
     if len(batch_shape) > 0:
         c_s = c_s.reshape(*batch_shape, N // 128)
     return c, c_s
+
+
+def fp8_gemm_grouped2(problems, act: Optional[int] = None):
+    """Two FP8 block GEMMs with the same epilogue in one launch (``fd_fp8_gemm_grouped2``).
+
+    ``problems``: two (a8 (..., K) e4m3, a_s (..., K / 128), b8 (N, K), b_s, bias or
+    None) tuples.  ``act`` None -> bf16 outputs (..., N); else an ``L.ACT_*``
+    quantising epilogue -> (codes, scales) per problem, as fp8_gemm_quant /
+    fp8_gemm_gelu_tanh_quant / fp8_gemm_silu_gate_quant produce them.
+    """
+    assert len(problems) == 2
+    structs, outs, keep = [], [], []
+    for a, a_s, b, b_s, bias in problems:
+        assert a.is_contiguous() and a_s.is_contiguous() and b.is_contiguous() and b_s.is_contiguous()
+        L.require_cuda(a, a_s, b, b_s, bias)
+        K = a.shape[-1]
+        M = a.numel() // K
+        N = b.shape[0] // (2 if act == L.ACT_SILU_GATE else 1)
+        if bias is not None:
+            bias = bias.contiguous()
+            assert bias.dtype == torch.bfloat16
+        if act is None:
+            c, c_s = a.new_empty(*a.shape[:-1], N, dtype=torch.bfloat16), None
+            outs.append(c)
+        else:
+            c = a.new_empty(*a.shape[:-1], N, dtype=torch.float8_e4m3fn)
+            c_s = a.new_empty(*a.shape[:-1], N // 128, dtype=torch.float32)
+            outs.append((c, c_s))
+        keep += [bias, c, c_s]
+        structs.append(L.GemmProblem(L.ptr(a), L.ptr(a_s), L.ptr(b), L.ptr(b_s), L.ptr(bias), L.ptr(c), L.ptr(c_s),
+                                     M, N, K))
+    has_bias = problems[0][4] is not None
+    L.call("fd_fp8_gemm_grouped2", ctypes.addressof(structs[0]), ctypes.addressof(structs[1]),
+           L.DT_BF16 if has_bias else 0, L.GEMM_STORE_BF16 if act is None else act, L.stream_ptr(problems[0][0].device))
+    return outs
 
 
 def fp8_gemm_gelu_tanh_quant(

@@ -135,6 +135,27 @@ int fd_fp8_gemm_blockwise_lora(const void* a, const float* a_s, const void* b, c
 int fd_fp8_gemm_quant(const void* a, const float* a_s, const void* b, const float* b_s,
                       const void* bias, int bias_dtype, void* c, float* c_s, int64_t M, int64_t N,
                       int64_t K, int act, void* stream);
+/* Two FP8 block GEMMs with the same epilogue in one persistent launch (each
+ * problem C = A B^T as fd_fp8_gemm_blockwise with b_layout 0, or quantised as
+ * fd_fp8_gemm_quant): the tiles of both are scheduled together, so a small
+ * problem (the text stream of a double-stream block, M = 512 per sample) does
+ * not leave most SMs idle.  act: FD_GEMM_STORE_BF16 (bf16 C) or FD_ACT_*
+ * (1 x 128 e4m3 C + c_s).  bias: both or neither, bf16.  No counterpart in the
+ * reference (one GEMM launch per linear). */
+#define FD_GEMM_STORE_BF16 (-1)
+typedef struct fd_gemm_problem {
+  const void* a;     /* (M, K) e4m3 */
+  const float* a_s;  /* (M, K / 128) */
+  const void* b;     /* (N, K) e4m3 ((2 N, K) for FD_ACT_SILU_GATE) */
+  const float* b_s;  /* (N / 128, K / 128) */
+  const void* bias;  /* (N,) bf16 or NULL */
+  void* c;           /* (M, N) bf16, or e4m3 codes */
+  float* c_s;        /* (M, N / 128) when quantising */
+  int64_t M, N, K;
+} fd_gemm_problem;
+int fd_fp8_gemm_grouped2(const fd_gemm_problem* p0, const fd_gemm_problem* p1, int bias_dtype, int act,
+                         void* stream);
+
 /* fd_fp8_gemm_quant writing into a column window of wider rows: output row m
  * starts at c + m * ldc (codes, ldc a multiple of 16) and c_s + m * ldcs. */
 int fd_fp8_gemm_quant_ld(const void* a, const float* a_s, const void* b, const float* b_s,

@@ -239,3 +239,30 @@ def test_gemm_quant_into_column_window(cuda_device, M, N, K):
     assert torch.equal(buf[:, off:off + N], c.view(torch.uint8))
     assert torch.equal(sbuf[:, off // 128:off // 128 + N // 128], c_s)
     assert not buf[:, :off].any() and not buf[:, off + N:].any()
+
+
+@pytest.mark.parametrize("act", [None, "quant", "gelu", "silu"])
+def test_gemm_grouped2_equals_separate_launches(cuda_device, act):
+    """Two problems in one grouped launch give exactly what two separate launches give."""
+    from futudiffu_b200 import _lib as L
+    from futudiffu_b200 import fp8_kernels as FK
+
+    probs = []
+    for (M, N, K), seed in (((512, 384, 256), 31), ((1300, 256, 384), 32)):
+        Nb = 2 * N if act == "silu" else N
+        a8, a_s, b8, bs = (t.to(cuda_device) for t in _operands(M, Nb, K, seed=seed))
+        probs.append((a8, a_s, b8, bs, None))
+    code = {None: None, "quant": L.ACT_NONE, "gelu": L.ACT_GELU_TANH, "silu": L.ACT_SILU_GATE}[act]
+    got = FK.fp8_gemm_grouped2(probs, act=code)
+    for (a8, a_s, b8, bs, _), g in zip(probs, got):
+        if act is None:
+            assert torch.equal(g, FK.fp8_gemm_blockwise(a8, a_s, b8, bs, output_dtype=torch.bfloat16))
+            continue
+        if act == "quant":
+            ref = FK.fp8_gemm_quant(a8, a_s, b8, bs)
+        elif act == "gelu":
+            ref = FK.fp8_gemm_gelu_tanh_quant(a8, a_s, b8, bs)
+        else:
+            ref = FK.fp8_gemm_silu_gate_quant(a8, a_s, b8, bs)
+        assert torch.equal(g[0].view(torch.uint8), ref[0].view(torch.uint8))
+        assert torch.equal(g[1].reshape(ref[1].shape), ref[1])
