@@ -298,6 +298,58 @@ __global__ void __launch_bounds__(256) dq_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core backward, elementwise step.  The products of the backward run as
+// batched library GEMMs on a chunk of heads and query rows:
+//   S  = Qc Kc^T (codes, exact for INT8), dP = dO V^T          (fp32 out)
+// then this kernel, per (query row i, key j) of the chunk:
+//   p  = exp2((S_ij q_desc_i) k_desc_j - lse_i), 0 on masked (128 x 64) tiles
+//   dS = p (dP_ij - Delta_i)
+//   P16 = bf16(p), dSs16 = bf16(dS * sm_scale), dS16 = bf16(dS)
+// exactly the per-element arithmetic of the CUDA-core kernels above (and of the
+// reference, sage_kernels.py:896-907, :1007-1010); the GEMMs dV = P16^T dO,
+// dK = dSs16^T Q, dQ = dS16 Ks (x sm_scale) follow.  Eight keys per thread.
+__global__ void __launch_bounds__(256) bwd_elementwise_kernel(
+    const float* __restrict__ S, const float* __restrict__ dP, const float* __restrict__ qd,
+    const float* __restrict__ kd, const float* __restrict__ lse, const float* __restrict__ delta,
+    const uint8_t* __restrict__ mask, int64_t mstride, __nv_bfloat16* __restrict__ P16,
+    __nv_bfloat16* __restrict__ dSs16, __nv_bfloat16* __restrict__ dS16, int HC, int R, int r0, int N,
+    int64_t dstride, int bh0, float sm_scale) {
+  const int nv = N / 8;                       // 8-key vectors per row (N % 8 == 0)
+  const int64_t items = (int64_t)HC * R * nv;
+  const int nkb = (N + 63) / 64;
+  for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < items; it += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = it / nv;              // chunk row: head hc * R + local row
+    const int j0 = (int)(it % nv) * 8;
+    const int hc = (int)(row / R);
+    const int i = r0 + (int)(row % R);        // query row in the head
+    const int bh = bh0 + hc;
+    const float q_d = qd[(int64_t)bh * dstride + i];
+    const float l = lse[(int64_t)bh * N + i];
+    const float dl = delta[(int64_t)bh * N + i];
+    const bool valid = !mask || mask[(int64_t)bh * mstride + (int64_t)(i / 128) * nkb + j0 / 64] != 0;
+    const float4* s4 = reinterpret_cast<const float4*>(S + row * N + j0);
+    const float4* d4 = reinterpret_cast<const float4*>(dP + row * N + j0);
+    const float4 sa = s4[0], sb = s4[1], da = d4[0], db = d4[1];
+    const float sv[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+    const float dv[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
+    float p[8], ds[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      p[e] = valid ? ex2_approx((sv[e] * q_d) * kd[(int64_t)bh * dstride + j0 + e] - l) : 0.f;
+      ds[e] = p[e] * (dv[e] - dl);
+    }
+    const int64_t o = row * N + j0;
+    *reinterpret_cast<uint4*>(P16 + o) = make_uint4(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]),
+                                                    pack_bf16x2(p[4], p[5]), pack_bf16x2(p[6], p[7]));
+    *reinterpret_cast<uint4*>(dSs16 + o) =
+        make_uint4(pack_bf16x2(ds[0] * sm_scale, ds[1] * sm_scale), pack_bf16x2(ds[2] * sm_scale, ds[3] * sm_scale),
+                   pack_bf16x2(ds[4] * sm_scale, ds[5] * sm_scale), pack_bf16x2(ds[6] * sm_scale, ds[7] * sm_scale));
+    *reinterpret_cast<uint4*>(dS16 + o) = make_uint4(pack_bf16x2(ds[0], ds[1]), pack_bf16x2(ds[2], ds[3]),
+                                                     pack_bf16x2(ds[4], ds[5]), pack_bf16x2(ds[6], ds[7]));
+  }
+}
+
 }  // namespace attn_bwd
 }  // namespace fd
 
@@ -353,4 +405,30 @@ extern "C" int fd_sage_attn_bwd(const void* q, const void* k, const void* v, con
       (const uint8_t*)q_codes, q_desc, (const uint8_t*)k_codes, k_desc, block_mask, mask_bh_stride,
       (__nv_bfloat16*)dq, (int)N, dstride, sm_scale);
   return check_launch("sage_attn_bwd dq");
+}
+
+// Elementwise step of the tensor-core backward for a chunk of HC heads (bh0 ..
+// bh0 + HC - 1) and query rows [r0, r0 + R): S, dP (HC, R, N) fp32 in; P16,
+// dSs16, dS16 (HC, R, N) bf16 out.  q_desc / k_desc are the per-token descales
+// of fd_attn_quant (row stride round_up(N, 128)); lse, delta (BH, N).  N % 8 == 0.
+extern "C" int fd_sage_attn_bwd_elementwise(const float* S, const float* dP, const float* q_desc, const float* k_desc,
+                                            const float* lse, const float* delta, const uint8_t* block_mask,
+                                            int64_t mask_bh_stride, void* P16, void* dSs16, void* dS16, int64_t HC,
+                                            int64_t R, int64_t r0, int64_t N, int64_t bh0, float sm_scale,
+                                            void* stream) {
+  FD_CHECK_ARG(HC > 0 && R > 0 && N > 0 && N % 8 == 0 && r0 >= 0 && r0 + R <= N && bh0 >= 0, "bad shape");
+  FD_CHECK_ARG(N < (1ll << 31) && HC * R * N < (1ll << 40), "chunk too large");
+  FD_CHECK_ARG(S && dP && q_desc && k_desc && lse && delta && P16 && dSs16 && dS16, "null pointer");
+  FD_CHECK_ARG(aligned16(S) && aligned16(dP) && aligned16(k_desc) && aligned16(P16) && aligned16(dSs16) &&
+                   aligned16(dS16),
+               "misaligned pointer");
+  const int64_t dstride = ((N + 127) / 128) * 128;
+  const int64_t items = HC * R * (N / 8);
+  int64_t grid = (items + 255) / 256;
+  const int64_t cap = (int64_t)num_sms() * 16;
+  if (grid > cap) grid = cap;
+  attn_bwd::bwd_elementwise_kernel<<<(unsigned)grid, 256, 0, (cudaStream_t)stream>>>(
+      S, dP, q_desc, k_desc, lse, delta, block_mask, mask_bh_stride, (__nv_bfloat16*)P16, (__nv_bfloat16*)dSs16,
+      (__nv_bfloat16*)dS16, (int)HC, (int)R, (int)r0, (int)N, dstride, (int)bh0, sm_scale);
+  return check_launch("sage_attn_bwd_elementwise");
 }

@@ -358,6 +358,18 @@ int fd_sage_attn_bwd(const void* q, const void* k, const void* v, const void* do
                      const uint8_t* block_mask, int64_t mask_bh_stride, void* dq, void* dk,
                      void* dv, int64_t BH, int64_t N, int qk_kind, float sm_scale, void* stream);
 
+/* Elementwise step of the tensor-core backward (the products S = Qc Kc^T,
+ * dP = dO V^T, dV = P^T dO, dK = dS^T Q, dQ = dS Ks run as batched library GEMMs
+ * with fp32 output on a chunk of HC heads bh0 .. and query rows [r0, r0 + R)):
+ * S, dP (HC, R, N) fp32 -> P16 = bf16(p), dSs16 = bf16(dS * sm_scale),
+ * dS16 = bf16(dS), with p = exp2((S q_desc) k_desc - lse) (0 on masked tiles) and
+ * dS = p (dP - Delta), the per-element arithmetic of the reference's backward
+ * (sage_kernels.py:896-907, :1007-1010).  N % 8 == 0. */
+int fd_sage_attn_bwd_elementwise(const float* S, const float* dP, const float* q_desc, const float* k_desc,
+                                 const float* lse, const float* delta, const uint8_t* block_mask,
+                                 int64_t mask_bh_stride, void* P16, void* dSs16, void* dS16, int64_t HC, int64_t R,
+                                 int64_t r0, int64_t N, int64_t bh0, float sm_scale, void* stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

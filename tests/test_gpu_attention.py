@@ -242,8 +242,10 @@ def test_attention_status_clean(cuda_device):
 
 
 @pytest.mark.parametrize("qk", ["int8", "fp8"])
-@pytest.mark.parametrize("N,masked", [(256, False), (200, False), (384, True)])
+@pytest.mark.parametrize("N,masked", [(256, False), (200, False), (201, False), (384, True)])
 def test_attention_backward_vs_oracle(cuda_device, qk, N, masked):
+    """N % 8 == 0: the tensor-core backward (library GEMMs + elementwise kernel);
+    N = 201: the CUDA-core kernels."""
     from futudiffu_b200 import sage_attention as SA
 
     BH = 2
@@ -340,3 +342,29 @@ def test_attention_quantised_output(cuda_device, masked):
                                regions=[(buf[..., :D], sbuf[..., :D // 128])])
         assert torch.equal(buf[..., :D], r8) and not buf[..., D:].any()
         assert torch.equal(sbuf[..., :D // 128], rs) and not sbuf[..., D // 128:].any()
+
+
+
+@pytest.mark.parametrize("masked", [False, True])
+def test_backward_chunking_invariant(cuda_device, masked, monkeypatch):
+    """The tensor-core backward gives the same gradients whether a head is done in
+    one chunk or in 128-row query blocks (dK / dV accumulated in fp32 across them)."""
+    from futudiffu_b200 import sage_attention as SA
+
+    BH, N = 3, 512
+    q, k, v = (t.to(cuda_device).unsqueeze(0) for t in qkv(BH, N, 41))
+    dout = torch.randn(1, BH, N, 128, generator=gen(42)).to(torch.bfloat16).to(cuda_device)
+    mask = torch.from_numpy(OB.build_block_mask([200, N - 200])).to(cuda_device) if masked else None
+    SA.configure_sage(smooth_k=True, qk_quant="int8", pv_quant="bf16")
+    if masked:
+        out, lse = SA.sage_attn_forward_masked_with_lse(q, k, v, mask, SM)
+        run = lambda: SA.sage_attn_backward_masked(q, k, v, out, lse, dout, mask, SM)  # noqa: E731
+    else:
+        out, lse = SA.sage_attn_forward_with_lse(q, k, v, SM)
+        run = lambda: SA.sage_attn_backward(q, k, v, out, lse, dout, SM)  # noqa: E731
+    whole = run()
+    monkeypatch.setattr(SA, "_BWD_CHUNK_BYTES", SA._BWD_BYTES_PER_PAIR * N * 128)
+    blocks = run()
+    for a, b in zip(whole, blocks):
+        assert cosine(a.cpu(), b.cpu()) > 0.99999
+        assert (a.float() - b.float()).abs().max().item() <= 2 ** -6 * b.float().abs().max().item()
