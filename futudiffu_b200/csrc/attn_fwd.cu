@@ -192,8 +192,9 @@ constexpr float S_BIAS = 12582912.0f;  // 1.5 * 2^23
 
 // Pass 1 over 64 keys (two 32-key chunks): the maximum score.  Per-block K:
 // the maximum of the raw scores (still biased for INT8; the 64 keys share one
-// factor, applied by the caller); per-token K: the maximum of the scaled logits
-// (s * q_desc) * k_desc (reference order).
+// factor, applied by the caller); per-token K: max_n(s * k_desc[n]), times
+// q_desc by the caller (q_desc > 0).  The row maximum only sets the exp2 offset
+// (the lazy-rescale reference), so its last-bit rounding does not reach P.
 template <int QK, int KG, bool FULL>
 FD_DEV float chunk_max(const uint32_t (&r)[64], int col0, int N, bool half_ok, float qd, const float* kd) {
   float x[64];
@@ -204,7 +205,7 @@ FD_DEV float chunk_max(const uint32_t (&r)[64], int col0, int N, bool half_ok, f
     if (KG == FD_GRAN_TOKEN) {
       uint64_t v = pk(x[e], x[e + 1]);
       if (QK == FD_QK_INT8) v = add2(v, pk(-S_BIAS, -S_BIAS));
-      unpk(mul2(mul2(v, pk(qd, qd)), pk(kd[e], kd[e + 1])), x[e], x[e + 1]);
+      unpk(mul2(v, pk(kd[e], kd[e + 1])), x[e], x[e + 1]);
     }
   }
   if (!FULL) {
@@ -228,8 +229,9 @@ FD_DEV float chunk_exp_store(const uint32_t (&r)[32], int col0, int N, bool half
     if (KG == FD_GRAN_BLOCK) {
       v = fma2(v, pk(c, c), pk(nb, nb));  // nb carries -S_BIAS * c for INT8
     } else {
+      // ((s * q_desc) * k_desc) + nb with the last two steps fused
       if (QK == FD_QK_INT8) v = add2(v, pk(-S_BIAS, -S_BIAS));
-      v = add2(mul2(mul2(v, pk(qd, qd)), pk(kd[e], kd[e + 1])), pk(nb, nb));
+      v = fma2(mul2(v, pk(qd, qd)), pk(kd[e], kd[e + 1]), pk(nb, nb));
     }
     unpk(v, a[e], a[e + 1]);
     if (!FULL) {
@@ -540,6 +542,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       if (KG == FD_GRAN_BLOCK) {
         if (QK == FD_QK_INT8) mloc -= S_BIAS;  // exact; -inf stays -inf
         mloc = mloc == -INFINITY ? -INFINITY : mloc * c;  // c >= 0
+      } else {
+        mloc = mloc == -INFINITY ? -INFINITY : mloc * qd;  // q_desc >= 0
       }
       float* rm = red_max + (i & 1) * 256;
       rm[h * 128 + row] = mloc;
