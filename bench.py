@@ -1,7 +1,7 @@
 """Benchmarks of the quantized DiT hot path on B200.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload dit|video|attention|gemm|packed]
+                  [--workload dit|video|attention|gemm|packed|block]
 
 Workloads (one "step" each):
   dit (default, BASELINE config 4, the headline metric "DiT denoise steps/s"):
@@ -13,6 +13,8 @@ Workloads (one "step" each):
   attention: quantisation prologue + tcgen05 attention on
       B=2, H=24, S=4096, D=128 (int8 per-block QK, e4m3 P/V); replicas per rank.
   gemm (or the reference's Z-Image shapes): one FP8 block GEMM.
+  block: one MMDiT double-stream block forward at batch 1
+      (512 text + 4096 image tokens), replayed as a CUDA graph; replicas per rank.
   video: one denoise step of the 14B-class video DiT with
       Ulysses sequence parallelism (NCCL all-to-all around the attention).
   packed (the reference's production shape): a bin of the bin packer (two
@@ -320,7 +322,7 @@ def run_ours(args, world, rank, local):
 # ------------------------------------------------------------------ config 4: DiT denoise
 DIT_BATCH = 8
 DIT_METRIC = "DiT denoise steps/s (12B-class, 19 double + 38 single blocks, 4096+512 tokens, batch 8)"
-KERNELS_PER_CALL = {"fd_attn_quant": 3, "fd_attn_quant_noalloc": 3}
+KERNELS_PER_CALL = {"fd_attn_quant": 3, "fd_attn_quant_noalloc": 3, "fd_attn_quant_kv": 2}
 
 
 class LaunchRecorder:
@@ -348,6 +350,10 @@ class LaunchRecorder:
             M, N, K = args[8], args[9], args[10]
             mult = 2 if (name == "fd_fp8_gemm_quant" and args[11] == self.L.ACT_SILU_GATE) else 1
             kind, work = "gemm", 2.0 * M * N * K * mult
+        elif name == "fd_fp8_gemm_grouped2":
+            probs = [self.L.GemmProblem.from_address(a) for a in args[:2]]
+            mult = 2 if args[3] == self.L.ACT_SILU_GATE else 1
+            kind, work = "gemm", sum(2.0 * q.M * q.N * q.K * mult for q in probs)
         elif name in ("fd_sage_attn_fwd", "fd_sage_attn_fwd_bnhd"):
             BH, N = args[10], args[11]
             kind, work = "attn", 4.0 * BH * N * N * 128
@@ -554,6 +560,179 @@ def run_dit(args, world, rank, local):
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ config 3: one MMDiT double-stream block
+BLOCK_METRIC = "MMDiT double-stream block TFLOP/s (hidden 3072, 24 heads, 512 text + 4096 image tokens, batch 1)"
+
+
+def block_flops(cfg) -> float:
+    """Algorithmic FLOPs of one double-stream block forward of one sample."""
+    D, R, N = cfg.hidden, cfg.mlp_ratio, cfg.tokens
+    return 2 * (3 + 1 + 2 * R) * D * D * N + 4 * N * N * D
+
+
+def block_cpu_sample(img_tokens: int = 1024) -> dict:
+    """The oracle's double-stream block on the host cores at 512 text +
+    ``img_tokens`` image tokens (dit_cpu_sample), as a FLOP rate."""
+    from futudiffu_b200.dit import DiTConfig, flops_per_sample_step
+
+    cb = dit_cpu_sample(img_tokens=img_tokens)
+    val = cb["value"] * flops_per_sample_step(DiTConfig()) * DIT_BATCH / 1e12  # batch-8 steps/s -> FLOP/s
+    sample = cb["sample"].split(", extrapolated")[0] + "; its FLOP rate stands for the full block's"
+    return {**cb, "value": val, "unit": "TFLOPS", "sample": sample}
+
+
+def run_block_reference(args, world, rank):
+    if rank != 0:
+        return 0
+    from futudiffu_b200.dit import DiTConfig
+
+    full = block_flops(DiTConfig())
+    vals, cb = [], None
+    for i in range(args.warmup + args.steps):
+        cb = block_cpu_sample(img_tokens=256)
+        if i >= args.warmup:
+            vals.append(cb["value"])
+    val = statistics.mean(vals)
+    print(json.dumps({
+        "impl": "reference", "metric": BLOCK_METRIC, "value": val, "unit": "TFLOPS", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": full / (val * 1e12) * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp8/int8",
+        "data": "synthetic", "config": {"workload": "config3_mmdit_block", "batch": 1, "tokens": "512+4096"},
+        "cpu_baseline": {**cb, "value": val},
+        "e2e": {"value": val, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+    return 0
+
+
+def run_block(args, world, rank, local):
+    """one double-stream block forward (B 1, 512 + 4096 tokens),
+    replicated per rank.  Each step is the block replayed as a captured CUDA graph."""
+    from futudiffu_b200 import check_status
+    from futudiffu_b200.dit import DiTConfig, DoubleStreamBlock, batch_freqs, image_freqs, text_freqs
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = DiTConfig()
+    gen = torch.Generator(device=dev).manual_seed(0)
+    blk = DoubleStreamBlock(cfg, gen, dev)
+    g = torch.Generator().manual_seed(100 + rank)
+    h_txt = torch.randn(1, cfg.txt_tokens, cfg.hidden, generator=g).to(torch.bfloat16).pin_memory()
+    h_img = torch.randn(1, cfg.img_tokens, cfg.hidden, generator=g).to(torch.bfloat16).pin_memory()
+    h_vec = torch.randn(1, cfg.hidden, generator=g).to(torch.bfloat16).pin_memory()
+    d_txt, d_img, d_vec = (t.to(dev) for t in (h_txt, h_img, h_vec))
+    f_txt, f_img = batch_freqs(text_freqs(cfg, dev), 1), batch_freqs(image_freqs(cfg, dev), 1)
+    stream = torch.cuda.current_stream(dev)
+    flops = block_flops(cfg)
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            blk(d_txt, d_img, d_vec, f_txt, f_img)
+        torch.cuda.synchronize()
+        check_status()
+        rec = LaunchRecorder()
+        rec.active = True
+        n_rec = 3
+        for _ in range(n_rec):
+            blk(d_txt, d_img, d_vec, f_txt, f_img)
+        rec.active = False
+        torch.cuda.synchronize()
+        gemm_work, gemm_ms, n_gemm = rec.summary("gemm")
+        attn_work, attn_ms, _ = rec.summary("attn")
+        launches_per_step = rec.launches // n_rec
+        rec.close()
+        # capture the block (inputs stay at the static d_* addresses)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                blk(d_txt, d_img, d_vec, f_txt, f_img)
+        stream.wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            o_txt, o_img = blk(d_txt, d_img, d_vec, f_txt, f_img)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else local) as clocks:
+        for n, (e0, e1) in enumerate(ev):
+            if args.profile and n == 0:
+                torch.cuda.cudart().cudaProfilerStart()
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+            if args.profile and n == 0:
+                torch.cuda.synchronize()
+                torch.cuda.cudart().cudaProfilerStop()
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_local = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    ms = max_over_ranks(ms_local, world, dev)
+    check_status()
+    # end to end: pinned host activations + vec -> device -> block -> both outputs to host
+    o_h = [torch.empty_like(o_txt, device="cpu").pin_memory(), torch.empty_like(o_img, device="cpu").pin_memory()]
+
+    def e2e_step():
+        d_txt.copy_(h_txt, non_blocking=True)
+        d_img.copy_(h_img, non_blocking=True)
+        d_vec.copy_(h_vec, non_blocking=True)
+        graph.replay()
+        o_h[0].copy_(o_txt, non_blocking=True)
+        o_h[1].copy_(o_img, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_n = 10
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_n):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_n, world, dev)
+    check_status()
+    h2d = (h_txt.numel() + h_img.numel() + h_vec.numel()) * 2
+    d2h = (o_txt.numel() + o_img.numel()) * 2
+    if rank == 0:
+        pk = peaks()
+        peak = 2.0 * pk["bf16_tflops"]
+        gemm_tf = gemm_work / (gemm_ms * 1e-3) / 1e12
+        tf = flops / (ms * 1e-3) / 1e12
+        print(json.dumps({
+            "metric": BLOCK_METRIC, "value": tf * world, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp8/int8", "data": "synthetic (random-init weights, N(0,1) activations)",
+            "config": {"workload": "config3_mmdit_block", "batch": 1, "hidden": cfg.hidden, "heads": cfg.heads,
+                       "tokens": f"{cfg.txt_tokens} text + {cfg.img_tokens} image", "mlp": "ratio 4, GELU-tanh",
+                       "linears": "fp8 e4m3 1x128 act / 128x128 weight scales (tcgen05), the two streams' "
+                                  "linears as grouped launches",
+                       "attention": "fused RMSNorm/RoPE/quant prologue, int8 per-block QK, e4m3 P/V (tcgen05)",
+                       "block_tflop": flops / 1e12,
+                       "l2": "block weights 226 MB fp8 > 126 MB L2; no explicit flush",
+                       "parallelism": f"replica per GPU x{world}",
+                       "time_share": {"gemm": gemm_ms / n_rec / ms_local, "attention": attn_ms / n_rec / ms_local},
+                       "attention_kernel_tops": attn_work / (attn_ms * 1e-3) / 1e12 if attn_ms else None,
+                       "launch": f"each step replays the block's {launches_per_step} kernels as one CUDA graph"},
+            "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": peak, "unit": "TFLOP/s",
+                         "frac": gemm_tf / peak, "traffic": None,
+                         "kernel": f"gemm_fp8_kernel (the {n_gemm // n_rec} GEMM launches of a block, flop-weighted, "
+                                   "CUDA events per launch over three eager forwards)",
+                         "peak_source": f"2 x {pk['source']} burst bf16 dense ({pk['bf16_tflops']} TF/s): "
+                                        "fp8 dense rate is twice bf16"},
+            "cpu_baseline": block_cpu_sample() if world == 1 else None,
+            "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12 * world, "unit": "TFLOPS", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                    "api": "futudiffu_b200.dit.DoubleStreamBlock captured as a CUDA graph (pinned host inputs "
+                           "copied in, both stream outputs copied out)"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks.summary(),
+        }), flush=True)
     return 0
 
 
@@ -954,14 +1133,15 @@ def main(argv=None) -> int:
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default: 10 dit, 50 otherwise)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["dit", "video", "attention", "gemm", "packed"], default="dit",
+    ap.add_argument("--workload", choices=["dit", "video", "attention", "gemm", "packed", "block"], default="dit",
                     help="dit = BASELINE config 4 (headline); video = config 5 (Ulysses); "
+                         "block = config 3 (one double-stream block); "
                          "attention = config 2; gemm = config 1; packed = the reference's packed "
                          "4288-token bin through Z-Image-class JointTransformerBlocks")
     ap.add_argument("--gemm-shape", choices=sorted(GEMM_SHAPES), default="config1")
     ap.add_argument("--layers", type=int, default=30, help="packed: JointTransformerBlocks in the stack")
     ap.add_argument("--profile", action="store_true",
-                    help="dit: bracket the first timed step with cudaProfilerStart/Stop "
+                    help="dit, block: bracket the first timed step with cudaProfilerStart/Stop "
                          "(for ncu --profile-from-start off); timing of that run is not a result")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
@@ -977,6 +1157,10 @@ def main(argv=None) -> int:
             if args.impl == "reference":
                 return run_video_reference(args, world, rank)
             return run_video(args, world, rank, local)
+        if args.workload == "block":
+            if args.impl == "reference":
+                return run_block_reference(args, world, rank)
+            return run_block(args, world, rank, local)
         if args.workload == "packed":
             if args.impl == "reference":
                 return run_packed_reference(args, world, rank)
