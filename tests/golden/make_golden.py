@@ -11,6 +11,12 @@ inputs and stores inputs and outputs as ``.pt`` files:
   act_quant_scales.pt  futudiffu.fp8_kernels.fp8_act_quant (Triton kernel under the
                        Triton CPU interpreter; only the scales are kept -- the
                        interpreter's fp8 cast is not round-to-nearest-even)
+  ref_kernels.pt       the reference's Triton kernels (act quant, blockwise GEMM / addmm,
+                       GEMM + requant, GELU requant, SiLU-gate quant, RMSNorm+modulate,
+                       QKV postprocess, attention forward and backward in every QK / PV
+                       mode, masked and not) in the Triton CPU interpreter, with its
+                       float downcasts made round-to-nearest-even and its dot made an
+                       exact f32 dot (see _install_interpreter_fixes)
   silu_gate.pt         fp8_silu_gate_quant torch fallback            (fp8_kernels.py:1725-1747)
   fused_norms.pt       fused_kernels torch fallbacks + _qkv_postprocess_reference
                        (fused_kernels.py:479-541, :802-842) and attention.rope_embed
@@ -97,6 +103,9 @@ def main_triton(ref: Path) -> None:
     # ---- fp8_act_quant Triton kernel in the CPU interpreter: scales only
     env = dict(os.environ, TRITON_INTERPRET="1")
     subprocess.run([sys.executable, __file__, "--reference", str(ref), "--section", "interp"],
+                   check=True, env=env)
+    # ---- the reference's kernels in the interpreter with RNE casts and an exact dot
+    subprocess.run([sys.executable, __file__, "--reference", str(ref), "--section", "kernels"],
                    check=True, env=env)
     # ---- torch fallbacks (Triton blocked)
     subprocess.run([sys.executable, __file__, "--reference", str(ref), "--section", "fallback"],
@@ -194,6 +203,145 @@ def main_interp(ref: Path) -> None:
     torch.save({"x": x, "scales": s}, HERE / "act_quant_scales.pt")
 
 
+def _install_interpreter_fixes() -> None:
+    """Make the Triton CPU interpreter compute what the compiled kernels compute.
+
+    Two defects of the interpreter (triton/runtime/interpreter.py) would
+    otherwise make the reference's kernels disagree with their own GPU builds:
+      * float downcasts (f32 -> bf16 in ``cast_impl``, f32 -> e4m3 / bf16 / f16
+        in ``create_fp_to_fp``) go through ``_convert_float``, which truncates the
+        significand (or rounds ties away from zero) instead of rounding to nearest
+        even as the GPU's ``cvt.rn`` does;
+      * ``create_dot`` multiplies bf16 operands as their raw uint16 bit patterns.
+    The replacement downcast rounds to nearest even through torch's own
+    conversions; the replacement dot widens float operands exactly to f32 and
+    accumulates in f32 (integer operands keep the int32 matmul).  Divides,
+    exp2 / log2 and sqrt stay numpy's correctly rounded versions, so the fixtures
+    pin the reference's formulas with IEEE arithmetic (the oracle's CPU default).
+    """
+    import numpy as np
+    import triton.language as tl
+    from triton.runtime import interpreter as TI
+
+    orig = TI._convert_float
+    narrow = {tl.bfloat16: (torch.bfloat16, torch.int16, np.uint16), tl.float16: (torch.float16, torch.int16, np.uint16),
+              tl.float8e4nv: (torch.float8_e4m3fn, torch.uint8, np.uint8),
+              tl.float8e5: (torch.float8_e5m2, torch.uint8, np.uint8)}
+
+    def widen(data, dtype):
+        if dtype == tl.float32:
+            return data.astype(np.float32, copy=False)
+        return orig(data, dtype, tl.float32, None).view(np.float32)  # exact: upcasts only shift bits
+
+    def convert(data, src, dst, rounding_mode):
+        if src.primitive_bitwidth > dst.primitive_bitwidth and dst in narrow:
+            td, view, nd = narrow[dst]
+            f = torch.from_numpy(np.ascontiguousarray(widen(data, src)))
+            return f.to(td).view(view).numpy().view(nd)
+        return orig(data, src, dst, rounding_mode)
+
+    def dot(self, a, b, d, input_precision, max_num_imprecise_acc):
+        ad = widen(a.data, a.dtype) if a.dtype.is_floating() else a.data
+        bd = widen(b.data, b.dtype) if b.dtype.is_floating() else b.data
+        return TI.TensorHandle(np.matmul(ad, bd, dtype=d.data.dtype) + d.data, d.dtype.scalar)
+
+    TI._convert_float = convert
+    TI.InterpreterBuilder.create_dot = dot
+
+
+def main_kernels(ref: Path) -> None:
+    """ref_kernels.pt: the reference's own Triton kernels run in the CPU
+    interpreter (TRITON_INTERPRET=1, set by the parent) with the fixes above.
+
+    act quant (fp8_kernels.py:54-90), blockwise GEMM / addmm kernels (:125-343,
+    launched with one of their autotune configs, BLOCK_SIZE_M 64, as the
+    autotuner cannot time on the CPU), fp8_gemm_quant (:573-709), fp8_gelu
+    (:716-833), fp8_silu_gate_quant (:842-978), the fused RMSNorm+modulate and
+    QKV-postprocess kernels (fused_kernels.py:43-86, :270-471; the gate+residual
+    kernel calls libdevice tanh, which the interpreter lacks), and the attention
+    forward / backward entry points of sage_attention.py (:121-341, :344-458,
+    :461-648) in their INT8 / FP8 QK and bf16 / FP8 PV modes, masked and not.
+    """
+    _install_interpreter_fixes()
+    sys.path.insert(0, str(ref / "src"))
+    sys.path.insert(0, str(ref))
+    from futudiffu import fp8_kernels as rk
+    from futudiffu import fused_kernels as rf
+    from futudiffu import sage_attention as rsa
+
+    out = {}
+    # ---- G1 act quant: codes and scales
+    g = _gen(3)
+    x = (torch.randn(16, 512, generator=g) * torch.rand(16, 1, generator=g) * 10).to(torch.bfloat16)
+    x[3, 128:256] = 0.0
+    y, s = rk.fp8_act_quant(x)
+    out["act"] = {"x": x, "codes": y, "scales": s}
+
+    # ---- G2 GEMM / addmm (bf16 and f32 outputs), G2+requant, GELU requant
+    g = _gen(6)
+    M, N, K = 72, 256, 384
+    xa = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+    a8, a_s = rk.fp8_act_quant(xa)
+    saved = torch.Tensor.cuda
+    torch.Tensor.cuda = lambda self, *a, **kw: self  # type: ignore[assignment]
+    try:
+        from futudiffu.fp8 import quantize_fp8_blockwise
+
+        b8, b_s = quantize_fp8_blockwise(w)
+    finally:
+        torch.Tensor.cuda = saved  # type: ignore[assignment]
+    bias = torch.randn(N, generator=g).to(torch.bfloat16)
+    grid = ((M + 63) // 64, N // 128)
+    gemm = {"a8": a8, "a_s": a_s, "b8": b8, "b_s": b_s, "bias": bias}
+    for name, dt in (("bf16", torch.bfloat16), ("f32", torch.float32)):
+        c = torch.empty(M, N, dtype=dt)
+        rk.fp8_gemm_blockwise_kernel.fn[grid](a8, b8, c, a_s, b_s, M, N, K, 128,
+                                              BLOCK_SIZE_M=64, BLOCK_SIZE_N=128, BLOCK_SIZE_K=128)
+        cb = torch.empty(M, N, dtype=dt)
+        rk.fp8_addmm_blockwise_kernel.fn[grid](a8, b8, cb, bias, a_s, b_s, M, N, K, 128, BLOCK_SIZE_M=64,
+                                               BLOCK_SIZE_N=128, BLOCK_SIZE_K=128, HAS_BIAS=True)
+        gemm[f"c_{name}"], gemm[f"c_bias_{name}"] = c, cb
+    gemm["quant"] = rk.fp8_gemm_quant(a8, a_s, b8, b_s)
+    gemm["gelu"] = rk.fp8_gelu(a8, a_s)
+    out["gemm"] = gemm
+    g = _gen(7)
+    xs = (torch.randn(40, 2 * 256, generator=g) * 2).to(torch.bfloat16)
+    out["silu_gate"] = {"x": xs, "out": rk.fp8_silu_gate_quant(xs)}
+
+    # ---- P1 / P3 Triton kernels on the inputs stored in fused_norms.pt
+    fz = torch.load(HERE / "fused_norms.pt", weights_only=False)
+    out["norms"] = {
+        "modulate": rf._fused_rms_norm_modulate_triton(fz["x"], fz["w"], fz["scale"], 1e-5),
+        "qkv": rf._fused_qkv_postprocess_triton(fz["qkv"], fz["qw"], fz["kw"], fz["freqs"], fz["H"], fz["hd"], 1e-5),
+    }
+
+    # ---- attention: ragged N (two Q blocks, three 64-key tiles), a mask with skipped tiles
+    g = _gen(8)
+    B, H, Na = 1, 2, 136
+    q = torch.randn(B, H, Na, 128, generator=g).to(torch.bfloat16)
+    k = (torch.randn(B, H, Na, 128, generator=g) + 2.0 * torch.randn(128, generator=g)).to(torch.bfloat16)
+    v = torch.randn(B, H, Na, 128, generator=g).to(torch.bfloat16)
+    do = torch.randn(B, H, Na, 128, generator=g).to(torch.bfloat16)
+    mask = torch.tensor([[1, 0, 1], [1, 1, 0]], dtype=torch.uint8)
+    sm = 1.0 / 128 ** 0.5
+    att = {"q": q, "k": k, "v": v, "dout": do, "mask": mask, "sm_scale": sm, "fwd": {}, "bwd": {}}
+    for qk in ("int8", "fp8"):
+        rsa.configure_sage(smooth_k=True, qk_quant=qk, pv_quant="bf16")
+        o, lse = rsa.sage_attn_forward_with_lse(q, k, v)
+        att["fwd"][f"{qk}_bf16"] = (o, lse)
+        att["fwd"][f"{qk}_bf16_masked"] = (rsa.sage_attn_forward_masked(q, k, v, mask), None)
+        att["bwd"][qk] = rsa.sage_attn_backward(q, k, v, o, lse, do, sm)
+    rsa.configure_sage(smooth_k=True, qk_quant="fp8", pv_quant="fp8")
+    att["fwd"]["fp8_fp8tile"] = rsa.sage_attn_forward_with_lse(q, k, v)
+    rsa.configure_sage(smooth_k=True, qk_quant="int8", pv_quant="bf16")
+    o, lse = rsa.sage_attn_forward_masked_with_lse(q, k, v, mask)
+    att["fwd"]["int8_bf16_masked_lse"] = (o, lse)
+    att["bwd"]["int8_masked"] = rsa.sage_attn_backward_masked(q, k, v, o, lse, do, mask, sm)
+    out["attention"] = att
+    torch.save(out, HERE / "ref_kernels.pt")
+
+
 def main_fallback(ref: Path) -> None:
     sys.meta_path.insert(0, _BlockTriton())
     sys.path.insert(0, str(ref / "src"))
@@ -235,6 +383,7 @@ def main_fallback(ref: Path) -> None:
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
-    ap.add_argument("--section", default="main", choices=["main", "interp", "fallback"])
+    ap.add_argument("--section", default="main", choices=["main", "interp", "kernels", "fallback"])
     a = ap.parse_args()
-    {"main": main_triton, "interp": main_interp, "fallback": main_fallback}[a.section](a.reference)
+    {"main": main_triton, "interp": main_interp, "kernels": main_kernels,
+     "fallback": main_fallback}[a.section](a.reference)

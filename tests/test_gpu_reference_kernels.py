@@ -1,0 +1,136 @@
+"""The CUDA path, called through the reference-named API, against the outputs of
+the reference's own Triton kernels (tests/golden/ref_kernels.pt, made by
+tests/golden/make_golden.py in the Triton CPU interpreter with round-to-nearest-
+even casts and an exact f32 dot).
+
+The interpreter divides, takes exp2 and square roots correctly rounded; the GPU
+kernels here reproduce the compiled reference (div.full.f32, ex2.approx,
+sqrt.approx), so a scale may move by up to 2 fp32 ulp and a code by one e4m3
+step where it sits on a rounding edge.  Float results carry the tolerances
+written beside each check.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from tests.helpers import bf16_ulp_diff, cosine, e4m3_step_diff
+
+pytestmark = pytest.mark.gpu
+
+SCALE_RTOL = 2.5e-7  # two fp32 ulp: div.full.f32 vs the correctly rounded quotient
+
+
+@pytest.fixture(scope="module")
+def R(golden_dir):
+    return torch.load(golden_dir / "ref_kernels.pt", weights_only=False)
+
+
+def _codes_close(got, want, max_frac=0.01):
+    d = e4m3_step_diff(got.cpu(), want)
+    assert d.max().item() <= 1
+    assert (d > 0).float().mean().item() <= max_frac
+
+
+def test_fp8_act_quant(cuda_device, R):
+    from futudiffu_b200.fp8_kernels import fp8_act_quant
+
+    d = R["act"]
+    y, s = fp8_act_quant(d["x"].to(cuda_device))
+    torch.testing.assert_close(s.cpu(), d["scales"], rtol=SCALE_RTOL, atol=0)
+    _codes_close(y, d["codes"])
+
+
+def test_fp8_gemm_and_addmm(cuda_device, R):
+    from futudiffu_b200.fp8_kernels import fp8_addmm_blockwise, fp8_gemm_blockwise
+
+    g = R["gemm"]
+    a8, a_s, b8, b_s, bias = (g[k].to(cuda_device) for k in ("a8", "a_s", "b8", "b_s", "bias"))
+    for out_dtype, key in ((torch.bfloat16, "bf16"), (torch.float32, "f32")):
+        c = fp8_gemm_blockwise(a8, a_s, b8, b_s, output_dtype=out_dtype).cpu()
+        cb = fp8_addmm_blockwise(a8, a_s, b8, b_s, bias=bias, output_dtype=out_dtype).cpu()
+        for got, want in ((c, g[f"c_{key}"]), (cb, g[f"c_bias_{key}"])):
+            if key == "bf16":
+                # tensor-core sums in another order: at most one bf16 ulp, rarely
+                d = bf16_ulp_diff(got, want)
+                assert d.max().item() <= 1 and (d > 0).float().mean().item() <= 0.01
+            else:
+                tol = 8 * torch.finfo(torch.float32).eps * want.abs().amax()
+                assert (got - want).abs().max() <= tol
+
+
+def test_fp8_gemm_quant_gelu_and_silu_gate(cuda_device, R):
+    from futudiffu_b200.fp8_kernels import fp8_gelu, fp8_gemm_quant, fp8_silu_gate_quant
+
+    g = R["gemm"]
+    a8, a_s, b8, b_s = (g[k].to(cuda_device) for k in ("a8", "a_s", "b8", "b_s"))
+    for (y, s), (wy, ws) in ((fp8_gemm_quant(a8, a_s, b8, b_s), g["quant"]), (fp8_gelu(a8, a_s), g["gelu"])):
+        torch.testing.assert_close(s.cpu(), ws, rtol=1e-6, atol=0)
+        _codes_close(y, wy)
+    d = R["silu_gate"]
+    y, s = fp8_silu_gate_quant(d["x"].to(cuda_device))
+    torch.testing.assert_close(s.cpu(), d["out"][1], rtol=1e-6, atol=0)
+    _codes_close(y, d["out"][0])
+
+
+def test_fused_norm_and_qkv_postprocess(cuda_device, golden_dir, R):
+    from futudiffu_b200.fused_kernels import fused_qkv_postprocess, fused_rms_norm_modulate
+
+    fz = torch.load(golden_dir / "fused_norms.pt", weights_only=False)
+    n = R["norms"]
+    y = fused_rms_norm_modulate(*(fz[k].to(cuda_device) for k in ("x", "w", "scale")))
+    d = bf16_ulp_diff(y.cpu(), n["modulate"])  # rsqrt.approx vs a correctly rounded 1/sqrt
+    assert d.max().item() <= 1 and (d > 0).float().mean().item() <= 0.01
+    got = fused_qkv_postprocess(*(fz[k].to(cuda_device) for k in ("qkv", "qw", "kw", "freqs")), fz["H"], fz["hd"])
+    for a, b in zip(got, n["qkv"]):
+        d = bf16_ulp_diff(a.cpu(), b)
+        assert d.max().item() <= 2 and (d > 0).float().mean().item() <= 0.01
+
+
+@pytest.mark.parametrize("qk", ["int8", "fp8"])
+def test_sage_forward_and_backward(cuda_device, R, qk):
+    from futudiffu_b200 import sage_attention as SA
+
+    a = R["attention"]
+    q, k, v, do, mask = (a[x].to(cuda_device) for x in ("q", "k", "v", "dout", "mask"))
+    SA.configure_sage(smooth_k=True, qk_quant=qk, pv_quant="bf16")
+    try:
+        o, lse = SA.sage_attn_forward_with_lse(q, k, v)
+        ro, rlse = a["fwd"][f"{qk}_bf16"]
+        # P rounded to bf16 from ex2.approx: reference tolerance of the INT8 / FP8 modes
+        assert cosine(o.cpu(), ro) >= (0.9999 if qk == "int8" else 0.9995)
+        assert (lse.cpu() - rlse).abs().max().item() <= 2e-3
+        om = SA.sage_attn_forward_masked(q, k, v, mask)
+        assert cosine(om.cpu(), a["fwd"][f"{qk}_bf16_masked"][0]) >= (0.9999 if qk == "int8" else 0.9995)
+        dq, dk, dv = SA.sage_attn_backward(q, k, v, o, lse, do, a["sm_scale"])
+        for x, w in zip((dq, dk, dv), a["bwd"][qk]):
+            assert cosine(x.cpu(), w) >= 0.999
+        if qk == "int8":
+            o2, l2 = SA.sage_attn_forward_masked_with_lse(q, k, v, mask)
+            ro2, rl2 = a["fwd"]["int8_bf16_masked_lse"]
+            assert cosine(o2.cpu(), ro2) >= 0.9999
+            assert (l2.cpu() - rl2).abs().max().item() <= 2e-3
+            grads = SA.sage_attn_backward_masked(q, k, v, o2, l2, do, mask, a["sm_scale"])
+            for x, w in zip(grads, a["bwd"]["int8_masked"]):
+                assert cosine(x.cpu(), w) >= 0.999
+    finally:
+        SA.configure_sage()
+
+
+def test_sage_forward_fp8_pv(cuda_device, R):
+    """FP8 PV: the reference scales P per row and V per column over each 64-key
+    tile; this build uses per-channel V and a static P scale (two valid
+    roundings of ~3 % element noise), so the gate is a cosine."""
+    from futudiffu_b200 import sage_attention as SA
+
+    a = R["attention"]
+    q, k, v = (a[x].to(cuda_device) for x in ("q", "k", "v"))
+    SA.configure_sage(smooth_k=True, qk_quant="fp8", pv_quant="fp8")
+    try:
+        o, lse = SA.sage_attn_forward_with_lse(q, k, v)
+    finally:
+        SA.configure_sage()
+    ro, rlse = a["fwd"]["fp8_fp8tile"]
+    assert cosine(o.cpu(), ro) >= 0.998
+    assert (lse.cpu() - rlse).abs().max().item() <= 2e-3

@@ -132,3 +132,110 @@ def test_oracle_attention_close_to_exact():
             assert torch.isfinite(lse).all()
     out, _ = OA.attention_forward(q, k, v, qk_quant="int8", granularity="per_block", pv_quant="fp8_channel")
     assert cosine(out, exact) > 0.995
+
+
+# ---------------------------------------------------------------- the reference's own Triton kernels
+# tests/golden/ref_kernels.pt holds the reference's kernels run in the Triton CPU
+# interpreter (round-to-nearest-even casts, exact f32 dot; make_golden.py).  The
+# interpreter evaluates divides, exp2 and sqrt correctly rounded, the oracle's CPU
+# default, so quantised codes and scales must agree bit for bit; fp32 sums may
+# differ in order (the interpreter's matmul vs the oracle's float64 tile sums), so
+# GEMM accumulators agree to 2 fp32 ulp and attention outputs in all but a few
+# elements, each within a few bf16 ulp.
+
+import pytest  # noqa: E402
+
+from oracle import gemm as OG  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def ref_kernels(golden_dir):
+    return torch.load(golden_dir / "ref_kernels.pt", weights_only=False)
+
+
+def test_act_quant_matches_reference_kernel(ref_kernels):
+    d = ref_kernels["act"]
+    y, s = OQ.act_quant(d["x"])
+    assert torch.equal(e4m3_bits(y), e4m3_bits(d["codes"]))
+    assert torch.equal(s, d["scales"])
+
+
+def test_gemm_matches_reference_kernel(ref_kernels):
+    g = ref_kernels["gemm"]
+    args = (g["a8"], g["a_s"], g["b8"], g["b_s"])
+    for bias, key in ((None, "c"), (g["bias"], "c_bias")):
+        acc = OG.gemm_blockwise(*args, bias=bias, out_dtype=torch.float32)
+        want = g[f"{key}_f32"]
+        tol = 2 * torch.finfo(torch.float32).eps * want.abs().amax()
+        assert (acc - want).abs().max() <= tol
+        out = OG.gemm_blockwise(*args, bias=bias, out_dtype=torch.bfloat16)
+        assert torch.equal(out.view(torch.int16), g[f"{key}_bf16"].view(torch.int16))
+
+
+def test_gemm_requant_epilogues_match_reference_kernels(ref_kernels):
+    g = ref_kernels["gemm"]
+    acc = OG.gemm_blockwise(g["a8"], g["a_s"], g["b8"], g["b_s"], out_dtype=torch.float32)
+    y, s = OQ.act_quant(acc)
+    c, cs = g["quant"]
+    assert torch.equal(e4m3_bits(y), e4m3_bits(c))
+    torch.testing.assert_close(s, cs, rtol=4e-7, atol=0)  # amax of an accumulator: one fp32 ulp
+    y, s = OQ.gelu_requant(g["a8"], g["a_s"])
+    c, cs = g["gelu"]
+    assert torch.equal(e4m3_bits(y), e4m3_bits(c))
+    torch.testing.assert_close(s, cs, rtol=4e-7, atol=0)
+    d = ref_kernels["silu_gate"]
+    y, s = OQ.silu_gate_quant(d["x"])
+    assert torch.equal(e4m3_bits(y), e4m3_bits(d["out"][0]))
+    assert torch.equal(s, d["out"][1])
+
+
+def test_fused_prologues_match_reference_kernels(golden_dir, ref_kernels):
+    fz = torch.load(golden_dir / "fused_norms.pt", weights_only=False)
+    n = ref_kernels["norms"]
+    y = OF.rms_norm_modulate(fz["x"], fz["w"], fz["scale"], 1e-5)
+    assert torch.equal(y.view(torch.int16), n["modulate"].view(torch.int16))
+    got = OF.qkv_postprocess(fz["qkv"], fz["qw"], fz["kw"], fz["freqs"], fz["H"], fz["hd"])
+    for a, b in zip(got, n["qkv"]):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+_ATTN_MODES = {  # fixture key -> (qk_quant, pv_quant, masked)
+    "int8_bf16": ("int8", "bf16", False),
+    "int8_bf16_masked": ("int8", "bf16", True),
+    "int8_bf16_masked_lse": ("int8", "bf16", True),
+    "fp8_bf16": ("fp8", "bf16", False),
+    "fp8_bf16_masked": ("fp8", "bf16", True),
+    "fp8_fp8tile": ("fp8", "fp8_tile", False),
+}
+
+
+def _close_bf16(got, want, max_frac=2e-3, max_abs=4e-3):
+    differ = got.view(torch.int16) != want.view(torch.int16)
+    assert differ.float().mean().item() <= max_frac
+    assert (got.float() - want.float()).abs().max().item() <= max_abs
+
+
+@pytest.mark.parametrize("mode", sorted(_ATTN_MODES))
+def test_attention_forward_matches_reference_kernels(ref_kernels, mode):
+    a = ref_kernels["attention"]
+    qk, pv, masked = _ATTN_MODES[mode]
+    f = lambda t: t.reshape(-1, t.shape[-2], 128)  # noqa: E731
+    out, lse = OA.attention_forward(f(a["q"]), f(a["k"]), f(a["v"]), qk_quant=qk, granularity="per_token",
+                                    pv_quant=pv, block_mask=a["mask"] if masked else None)
+    ref_out, ref_lse = a["fwd"][mode]
+    _close_bf16(out, f(ref_out))
+    if ref_lse is not None:
+        assert (lse - ref_lse).abs().max().item() <= 4e-6
+
+
+@pytest.mark.parametrize("mode", ["int8", "fp8", "int8_masked"])
+def test_attention_backward_matches_reference_kernels(ref_kernels, mode):
+    a = ref_kernels["attention"]
+    f = lambda t: t.reshape(-1, t.shape[-2], 128)  # noqa: E731
+    qk = mode.split("_")[0]
+    masked = mode.endswith("masked")
+    o, lse = a["fwd"]["int8_bf16_masked_lse" if masked else f"{qk}_bf16"]
+    got = OA.attention_backward(f(a["q"]), f(a["k"]), f(a["v"]), f(o), lse, f(a["dout"]), sm_scale=a["sm_scale"],
+                                qk_quant=qk, block_mask=a["mask"] if masked else None)
+    for g, w in zip(got[:3], a["bwd"][mode]):
+        _close_bf16(g, f(w))
