@@ -302,6 +302,23 @@ def main_kernels(ref: Path) -> None:
         rk.fp8_addmm_blockwise_kernel.fn[grid](a8, b8, cb, bias, a_s, b_s, M, N, K, 128, BLOCK_SIZE_M=64,
                                                BLOCK_SIZE_N=128, BLOCK_SIZE_K=128, HAS_BIAS=True)
         gemm[f"c_{name}"], gemm[f"c_bias_{name}"] = c, cb
+    # rowwise (per-output-row weight scale), v1t (B pre-transposed to (K, N)),
+    # v2 (bf16 A quantised per 128-K slice inside the kernel), each with one of
+    # its autotune configs
+    b_row = (torch.rand(N, generator=g) * 1e-3 + 1e-4).float()
+    c = torch.empty(M, N, dtype=torch.float32)
+    rk.fp8_gemm_rowwise_kernel.fn[grid](a8, b8, c, a_s, b_row, M, N, K, 128,
+                                        BLOCK_SIZE_M=64, BLOCK_SIZE_N=128, BLOCK_SIZE_K=128)
+    gemm["b_row"], gemm["c_rowwise_f32"] = b_row, c
+    bt, bst = b8.t().contiguous(), b_s.t().contiguous()
+    c = torch.empty(M, N, dtype=torch.float32)
+    rk.fp8_gemm_v1t_kernel.fn[(grid[0], N // 128)](a8, bt, c, a_s, bst, M, N, K, 128,
+                                                   BLOCK_SIZE_M=64, BLOCK_SIZE_N=128, BLOCK_SIZE_K=128)
+    gemm["c_v1t_f32"] = c
+    c = torch.empty(M, N, dtype=torch.float32)
+    rk.fp8_gemm_v2_kernel.fn[(grid[0], N // 128)](xa, bt, c, bst, M, N, K, 128,
+                                                  BLOCK_SIZE_M=64, BLOCK_SIZE_N=128, FP8_MAX=448.0)
+    gemm["xa"], gemm["c_v2_f32"] = xa, c
     gemm["quant"] = rk.fp8_gemm_quant(a8, a_s, b8, b_s)
     gemm["gelu"] = rk.fp8_gelu(a8, a_s)
     out["gemm"] = gemm

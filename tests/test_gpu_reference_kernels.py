@@ -66,6 +66,25 @@ def test_fp8_gemm_and_addmm(cuda_device, R):
                 assert (got - want).abs().max() <= tol
 
 
+def test_fp8_gemm_rowwise_v1t_v2(cuda_device, R):
+    from futudiffu_b200.fp8_kernels import fp8_gemm_rowwise, fp8_gemm_v1t, fp8_gemm_v2
+
+    g = R["gemm"]
+    a8, a_s, b8, b_s, b_row, xa = (g[k].to(cuda_device) for k in ("a8", "a_s", "b8", "b_s", "b_row", "xa"))
+    bt, bst = b8.t().contiguous(), b_s.t().contiguous()
+    f32 = torch.float32
+    for got, want in ((fp8_gemm_rowwise(a8, a_s, b8, b_row, output_dtype=f32), g["c_rowwise_f32"]),
+                      (fp8_gemm_v1t(a8, a_s, bt, bst, output_dtype=f32), g["c_v1t_f32"])):
+        assert (got.cpu() - want).abs().max() <= 8 * torch.finfo(f32).eps * want.abs().amax()
+    # v2 quantises A inside the kernel with div.full, so a code on a rounding edge
+    # may move by one e4m3 step (the fixture divides correctly rounded): the rows
+    # it feeds move by up to ~1e-2 relative, all others stay within 8 fp32 eps
+    got, want = fp8_gemm_v2(xa, bt, bst, output_dtype=f32).cpu(), g["c_v2_f32"]
+    off = (got - want).abs() > 8 * torch.finfo(f32).eps * want.abs().amax()
+    assert off.float().mean().item() <= 0.02
+    assert cosine(got, want) >= 0.99999
+
+
 def test_fp8_gemm_quant_gelu_and_silu_gate(cuda_device, R):
     from futudiffu_b200.fp8_kernels import fp8_gelu, fp8_gemm_quant, fp8_silu_gate_quant
 

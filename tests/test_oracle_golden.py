@@ -170,6 +170,15 @@ def test_gemm_matches_reference_kernel(ref_kernels):
         assert (acc - want).abs().max() <= tol
         out = OG.gemm_blockwise(*args, bias=bias, out_dtype=torch.bfloat16)
         assert torch.equal(out.view(torch.int16), g[f"{key}_bf16"].view(torch.int16))
+    # rowwise, v1t (B as (K, N)) and v2 (bf16 A quantised per K slice in the kernel)
+    bt, bst = g["b8"].t().contiguous(), g["b_s"].t().contiguous()
+    a8, a_s = OQ.act_quant(g["xa"])
+    for got, want in (
+            (OG.gemm_blockwise(g["a8"], g["a_s"], g["b8"], g["b_row"], out_dtype=torch.float32, b_layout=2),
+             g["c_rowwise_f32"]),
+            (OG.gemm_blockwise(g["a8"], g["a_s"], bt, bst, out_dtype=torch.float32, b_layout=1), g["c_v1t_f32"]),
+            (OG.gemm_blockwise(a8, a_s, bt, bst, out_dtype=torch.float32, b_layout=1), g["c_v2_f32"])):
+        assert (got - want).abs().max() <= 2 * torch.finfo(torch.float32).eps * want.abs().amax()
 
 
 def test_gemm_requant_epilogues_match_reference_kernels(ref_kernels):
