@@ -12,11 +12,13 @@ inputs and stores inputs and outputs as ``.pt`` files:
                        Triton CPU interpreter; only the scales are kept -- the
                        interpreter's fp8 cast is not round-to-nearest-even)
   ref_kernels.pt       the reference's Triton kernels (act quant, blockwise GEMM / addmm,
-                       GEMM + requant, GELU requant, SiLU-gate quant, RMSNorm+modulate,
-                       QKV postprocess, attention forward and backward in every QK / PV
-                       mode, masked and not) in the Triton CPU interpreter, with its
-                       float downcasts made round-to-nearest-even and its dot made an
-                       exact f32 dot (see _install_interpreter_fixes)
+                       rowwise / v1t / v2 GEMMs, GEMM + requant, GELU requant, SiLU-gate
+                       quant, RMSNorm+modulate, QKV postprocess, attention forward and
+                       backward in every QK / PV mode, masked and not, multi-LoRA) in
+                       the Triton CPU interpreter, with its float downcasts made
+                       round-to-nearest-even and its dot made an exact f32 dot (see
+                       _install_interpreter_fixes); and src_ii.multi_lora
+                       MultiLoRALinear (torch) on an nn.Linear base
   silu_gate.pt         fp8_silu_gate_quant torch fallback            (fp8_kernels.py:1725-1747)
   fused_norms.pt       fused_kernels torch fallbacks + _qkv_postprocess_reference
                        (fused_kernels.py:479-541, :802-842) and attention.rope_embed
@@ -356,6 +358,40 @@ def main_kernels(ref: Path) -> None:
     att["fwd"]["int8_bf16_masked_lse"] = (o, lse)
     att["bwd"]["int8_masked"] = rsa.sage_attn_backward_masked(q, k, v, o, lse, do, mask, sm)
     out["attention"] = att
+
+    # ---- multi-LoRA: src_ii MultiLoRALinear (torch, the production path) on an
+    # nn.Linear base, and the Triton _multi_lora_kernel (lora_kernels.py:55-157)
+    from futudiffu.lora_kernels import multi_lora_forward
+    from src_ii.multi_lora import MultiLoRALinear
+
+    g = _gen(9)
+    IN, OUT, S = 256, 384, 40
+    base = torch.nn.Linear(IN, OUT, bias=True).to(torch.bfloat16)
+    with torch.no_grad():
+        base.weight.copy_(torch.randn(OUT, IN, generator=g) * 0.05)
+        base.bias.copy_(torch.randn(OUT, generator=g) * 0.1)
+    m = MultiLoRALinear(base, max_adapters=3, max_rank=16)
+    m.assign_adapter(0, "a", rank=8, alpha=16.0, init_a="zeros")
+    m.assign_adapter(2, "c", rank=16, alpha=8.0, init_a="zeros")
+    with torch.no_grad():
+        for j, r in ((0, 8), (2, 16)):
+            m.lora_A[j][:r].copy_(torch.randn(r, IN, generator=g) * 0.05)
+            m.lora_B[j][:, :r].copy_(torch.randn(OUT, r, generator=g) * 0.05)
+    xl = torch.randn(2, S, IN, generator=g).to(torch.bfloat16)
+    scales = torch.rand(2, 3, generator=g) * 2.0
+    t2i = torch.tensor([0] * 16 + [1] * 20 + [-1] * 4)  # per position, repeated per sample
+    with torch.no_grad():
+        lora = {"base_w": base.weight.detach().clone(), "base_b": base.bias.detach().clone(),
+                "A": [p.detach().clone() for p in m.lora_A], "B": [p.detach().clone() for p in m.lora_B],
+                "scalings": m._lora_scalings.clone(), "active": m._slot_active.clone(),
+                "x": xl, "scales": scales, "token_to_image": t2i,
+                "delta": m.adapter_delta(xl, scales, t2i), "out": m(xl, scales, t2i)}
+        A_all = torch.stack(lora["A"])
+        B_all = torch.stack(lora["B"])
+        scale_all = scales * (m._lora_scalings * m._slot_active)[None, :]
+        lora["kernel"] = {"A_all": A_all, "B_all": B_all, "scale_all": scale_all,
+                          "out": multi_lora_forward(xl, A_all, B_all, scale_all)}
+    out["lora"] = lora
     torch.save(out, HERE / "ref_kernels.pt")
 
 

@@ -159,3 +159,36 @@ def test_sage_forward_fp8_pv(cuda_device, R):
     ro, rlse = a["fwd"]["fp8_fp8tile"]
     assert cosine(o.cpu(), ro) >= 0.998
     _lse_close(lse, rlse)
+
+
+def _lora_close(got, want):
+    # this build folds the per-token scale into the bf16 mid activations and sums
+    # all adapters in one fp32 accumulator; the reference rounds per adapter
+    assert cosine(got.cpu(), want) >= 0.9999
+    assert (got.cpu().float() - want.float()).abs().max().item() <= 0.02 * want.float().abs().max().item()
+
+
+def test_multi_lora(cuda_device, R):
+    from futudiffu_b200.lora_kernels import multi_lora_forward
+    from futudiffu_b200.multi_lora import MultiLoRALinear
+
+    lo = R["lora"]
+    OUT, IN = lo["base_w"].shape
+    base = torch.nn.Linear(IN, OUT, bias=True, device=cuda_device, dtype=torch.bfloat16)
+    with torch.no_grad():
+        base.weight.copy_(lo["base_w"])
+        base.bias.copy_(lo["base_b"])
+    m = MultiLoRALinear(base, max_adapters=len(lo["A"]), max_rank=lo["A"][0].shape[0])
+    for j in range(len(lo["A"])):
+        if lo["active"][j] > 0:
+            m.assign_adapter(j, f"s{j}", rank=lo["A"][0].shape[0], alpha=1.0, init_a="zeros")
+            with torch.no_grad():
+                m.lora_A[j].copy_(lo["A"][j])
+                m.lora_B[j].copy_(lo["B"][j])
+    m._lora_scalings.copy_(lo["scalings"])
+    x, sc, t2i = lo["x"].to(cuda_device), lo["scales"].to(cuda_device), lo["token_to_image"].to(cuda_device)
+    _lora_close(m.adapter_delta(x, sc, t2i), lo["delta"])
+    _lora_close(m(x, sc, t2i), lo["out"])
+    k = lo["kernel"]
+    got = multi_lora_forward(x, k["A_all"].to(cuda_device), k["B_all"].to(cuda_device), k["scale_all"].to(cuda_device))
+    _lora_close(got, k["out"])

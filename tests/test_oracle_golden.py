@@ -248,3 +248,27 @@ def test_attention_backward_matches_reference_kernels(ref_kernels, mode):
                                 qk_quant=qk, block_mask=a["mask"] if masked else None)
     for g, w in zip(got[:3], a["bwd"][mode]):
         _close_bf16(g, f(w))
+
+
+def test_multi_lora_delta_matches_reference(ref_kernels):
+    """src_ii MultiLoRALinear.adapter_delta (per-image scales, token routing with
+    padding sentinels, an empty slot) equals the oracle bit for bit."""
+    from oracle import lora as OL
+
+    lo = ref_kernels["lora"]
+    x2 = lo["x"].reshape(-1, lo["x"].shape[-1])
+    eff = OL.effective_scales(x2.shape[0], lo["scales"], lo["token_to_image"], lo["scalings"], lo["active"])
+    d = OL.adapter_delta(x2, lo["A"], lo["B"], eff)
+    assert torch.equal(d.view(torch.int16), lo["delta"].reshape(d.shape).view(torch.int16))
+
+
+def test_multi_lora_kernel_restated(ref_kernels):
+    """_multi_lora_kernel (lora_kernels.py:100-157): mid rounded to bf16 per adapter,
+    s * (mid @ B^T) summed in fp32 over adapters, one bf16 rounding."""
+    k = ref_kernels["lora"]["kernel"]
+    x = ref_kernels["lora"]["x"]
+    acc = torch.zeros(*x.shape[:-1], k["B_all"].shape[1])
+    for i in range(k["A_all"].shape[0]):
+        mid = (x.float() @ k["A_all"][i].float().t()).to(torch.bfloat16).float()
+        acc += k["scale_all"][:, i].view(-1, 1, 1) * (mid @ k["B_all"][i].float().t())
+    assert torch.equal(acc.to(torch.bfloat16).view(torch.int16), k["out"].view(torch.int16))
