@@ -476,12 +476,15 @@ class PackedTrunk(nn.Module):
                  ffn_dim_multiplier: float | None = 8.0 / 3.0, norm_eps: float = 1e-5, seed: int = 0,
                  device=None):
         super().__init__()
-        torch.manual_seed(seed)
-        self.layers = nn.ModuleList([
-            JointTransformerBlock(i, dim, n_heads, None, multiple_of, ffn_dim_multiplier, norm_eps, qk_norm=True,
-                                  modulation=True, z_image_modulation=True, device=device,
-                                  dtype=torch.bfloat16).to_fp8()
-            for i in range(n_layers)])
+        dev = torch.device(device) if device is not None else torch.device("cpu")
+        # seeded random init without disturbing the caller's RNG streams
+        with torch.random.fork_rng(devices=[dev] if dev.type == "cuda" else []):
+            torch.manual_seed(seed)
+            self.layers = nn.ModuleList([
+                JointTransformerBlock(i, dim, n_heads, None, multiple_of, ffn_dim_multiplier, norm_eps,
+                                      qk_norm=True, modulation=True, z_image_modulation=True, device=device,
+                                      dtype=torch.bfloat16).to_fp8()
+                for i in range(n_layers)])
         self.dim = dim
         self._adaln_w: Tensor | None = None
         self._adaln_b: Tensor | None = None
