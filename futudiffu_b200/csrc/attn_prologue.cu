@@ -177,8 +177,8 @@ FD_DEV float half_max(float v) {
 // The 64 values a thread holds between its amax pass and its quantise pass stay
 // packed as bf16 (K after smoothing is bf16-rounded too), so three CTAs fit per
 // SM and their loads overlap each other's reductions.
-template <int QK>
-__global__ void __launch_bounds__(256, 3) quant_kernel(
+template <int QK, bool KV_ONLY>
+__global__ void __launch_bounds__(256, KV_ONLY ? 4 : 3) quant_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
     const __nv_bfloat16* __restrict__ v, int64_t N, int nchunks, int smooth_k, int q_gran,
     int k_gran, int pv_fp8, float sm_scale_log2e, uint8_t* __restrict__ q_codes,
@@ -188,7 +188,9 @@ __global__ void __launch_bounds__(256, 3) quant_kernel(
     int64_t k_desc_stride, int z0) {
   const int blk = blockIdx.x;
   const int64_t bh = blockIdx.y;
-  const int which = blockIdx.z + z0;  // 0 Q, 1 K, 2 V
+  // 0 Q, 1 K, 2 V; the K / V-only instantiation (the second pass of the fused
+  // prologue) carries no Q code
+  const int which = KV_ONLY ? (int)blockIdx.z + 1 : (int)blockIdx.z + z0;
   const int cg = threadIdx.x & 15, rl = threadIdx.x >> 4;
   const int64_t r0 = (int64_t)blk * 128;
   const float qmax = (QK == FD_QK_INT8) ? 127.0f : 448.0f;
@@ -207,7 +209,7 @@ __global__ void __launch_bounds__(256, 3) quant_kernel(
   __syncthreads();
 
   // ---------------- Q
-  if (which == 0) {
+  if (!KV_ONLY && which == 0) {
     uint4 xr[8];
     float rowmax[8];
     float blkmax = 0.f;
@@ -313,12 +315,19 @@ __global__ void __launch_bounds__(256, 3) quant_kernel(
 
   // ---------------- V (e4m3, per channel)
   if (which == 2) {
+    // all eight rows' loads issued before any conversion: 128 bytes in flight per thread
+    uint4 xr[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t n = r0 + rl + 16 * i;
+      xr[i] = n < N ? __ldg(reinterpret_cast<const uint4*>(v + (bh * N + n) * 128 + cg * 8)) : make_uint4(0, 0, 0, 0);
+    }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int64_t n = r0 + rl + 16 * i;
       if (n < N) {
         float x[8];
-        unpack8(__ldg(reinterpret_cast<const uint4*>(v + (bh * N + n) * 128 + cg * 8)), x);
+        unpack8(xr[i], x);
         uint32_t c[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -531,7 +540,7 @@ extern "C" int fd_attn_quant(const void* q, const void* k, const void* v, int64_
   const int64_t qs = fd_desc_stride(N, q_gran, 128), ks = fd_desc_stride(N, k_gran, 64);
   dim3 grid((unsigned)((N + 127) / 128), (unsigned)BH, pv_fp8 ? 3u : 2u);
 #define FD_Q_LAUNCH(QK)                                                                         \
-  quant_kernel<QK><<<grid, 256, 0, st>>>(                                                       \
+  quant_kernel<QK, false><<<grid, 256, 0, st>>>(                                                \
       (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, N, nchunks,   \
       smooth_k, q_gran, k_gran, pv_fp8, sm_scale_log2e, (uint8_t*)q_codes, q_desc,              \
       (uint8_t*)k_codes, k_desc, (uint8_t*)v_codes, v_desc, k_mean, ws_sum, ws_amax, qs, ks, 0)
@@ -663,7 +672,7 @@ extern "C" int fd_attn_quant_kv(const void* k, const void* v, int64_t BH, int64_
   const int64_t ks = fd_desc_stride(N, k_gran, 64);
   dim3 grid((unsigned)((N + 127) / 128), (unsigned)BH, pv_fp8 ? 2u : 1u);
 #define FD_KV(QK)                                                                                         \
-  quant_kernel<QK><<<grid, 256, 0, st>>>(nullptr, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, N,    \
+  quant_kernel<QK, true><<<grid, 256, 0, st>>>(nullptr, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, N, \
                                          nchunks, smooth_k, FD_GRAN_TOKEN, k_gran, pv_fp8, 1.0f, nullptr, \
                                          nullptr, (uint8_t*)k_codes, k_desc, (uint8_t*)v_codes, v_desc,   \
                                          k_mean, ws_sum, ws_amax, 0, ks, 1)
