@@ -1001,8 +1001,13 @@ def run_packed(args, world, rank, local):
     with ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else local) as clocks:
         rec.active = True
         start.record(stream)
-        for _ in range(args.steps):
+        for n in range(args.steps):
+            if args.profile and n == 0:
+                torch.cuda.cudart().cudaProfilerStart()
             step()
+            if args.profile and n == 0:
+                torch.cuda.synchronize()
+                torch.cuda.cudart().cudaProfilerStop()
         end.record(stream)
         rec.active = False
         torch.cuda.synchronize()
@@ -1141,7 +1146,7 @@ def main(argv=None) -> int:
     ap.add_argument("--gemm-shape", choices=sorted(GEMM_SHAPES), default="config1")
     ap.add_argument("--layers", type=int, default=30, help="packed: JointTransformerBlocks in the stack")
     ap.add_argument("--profile", action="store_true",
-                    help="dit, block: bracket the first timed step with cudaProfilerStart/Stop "
+                    help="dit, block, packed: bracket the first timed step with cudaProfilerStart/Stop "
                          "(for ncu --profile-from-start off); timing of that run is not a result")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
