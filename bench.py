@@ -4,18 +4,18 @@
                   [--workload dit|video|attention|gemm|packed|block]
 
 Workloads (one "step" each):
-  dit (default, BASELINE config 4, the headline metric "DiT denoise steps/s"):
+  dit (default, benchmark config 4, the headline metric "DiT denoise steps/s"):
       one rectified-flow Euler step of the 12B-class DiT (19 double + 38
       single blocks, hidden 3072, 4096 image + 512 text tokens) over the whole
       batch of 8, random-init FP8 weights.  The batch is sharded by sample:
       8/N samples per rank, no collective on the data path (strong scaling);
       value = batch-8 steps per second = 1 / max-over-ranks step time.
-  attention: quantisation prologue + tcgen05 attention on
+  attention (benchmark config 2): quantisation prologue + tcgen05 attention on
       B=2, H=24, S=4096, D=128 (int8 per-block QK, e4m3 P/V); replicas per rank.
-  gemm (or the reference's Z-Image shapes): one FP8 block GEMM.
-  block: one MMDiT double-stream block forward at batch 1
+  gemm (benchmark config 1, or the reference's Z-Image shapes): one FP8 block GEMM.
+  block (benchmark config 3): one MMDiT double-stream block forward at batch 1
       (512 text + 4096 image tokens), replayed as a CUDA graph; replicas per rank.
-  video: one denoise step of the 14B-class video DiT with
+  video (benchmark config 5): one denoise step of the 14B-class video DiT with
       Ulysses sequence parallelism (NCCL all-to-all around the attention).
   packed (the reference's production shape): a bin of the bin packer (two
       images + captions in 4288 tokens) through 30 Z-Image-class
@@ -608,7 +608,7 @@ def run_block_reference(args, world, rank):
 
 
 def run_block(args, world, rank, local):
-    """one double-stream block forward (B 1, 512 + 4096 tokens),
+    """benchmark config 3: one double-stream block forward (B 1, 512 + 4096 tokens),
     replicated per rank.  Each step is the block replayed as a captured CUDA graph."""
     from futudiffu_b200 import check_status
     from futudiffu_b200.dit import DiTConfig, DoubleStreamBlock, batch_freqs, image_freqs, text_freqs
@@ -1076,7 +1076,7 @@ def run_packed(args, world, rank, local):
 
 
 def run_gemm(args, world, rank, local):
-    """FP8 block-GEMM TFLOPS (or the reference's own Z-Image shapes)."""
+    """FP8 block-GEMM TFLOPS (benchmark config 1, or the reference's own Z-Image shapes)."""
     from futudiffu_b200 import _lib as L
     from futudiffu_b200 import check_status
     from futudiffu_b200.fp8 import quantize_fp8_blockwise_cuda
@@ -1139,7 +1139,7 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["dit", "video", "attention", "gemm", "packed", "block"], default="dit",
-                    help="dit = BASELINE config 4 (headline); video = config 5 (Ulysses); "
+                    help="dit = benchmark config 4 (headline); video = config 5 (Ulysses); "
                          "block = config 3 (one double-stream block); "
                          "attention = config 2; gemm = config 1; packed = the reference's packed "
                          "4288-token bin through Z-Image-class JointTransformerBlocks")

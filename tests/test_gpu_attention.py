@@ -215,7 +215,7 @@ def test_attention_deterministic(cuda_device):
 
 
 def test_attention_config2_full_size(cuda_device):
-    # B2 H24 S4096, K offset ~N(0, 4); all heads vs GPU fp32 softmax,
+    # benchmark config 2: B2 H24 S4096, K offset ~N(0, 4); all heads vs GPU fp32 softmax,
     # two heads vs the CPU oracle
     from futudiffu_b200 import sage_attention as SA
 
