@@ -229,9 +229,16 @@ FD_DEV float chunk_exp_store(const uint32_t (&r)[32], int col0, int N, bool half
     if (KG == FD_GRAN_BLOCK) {
       v = fma2(v, pk(c, c), pk(nb, nb));  // nb carries -S_BIAS * c for INT8
     } else {
-      // ((s * q_desc) * k_desc) + nb with the last two steps fused
-      if (QK == FD_QK_INT8) v = add2(v, pk(-S_BIAS, -S_BIAS));
-      v = fma2(mul2(v, pk(qd, qd)), pk(kd[e], kd[e + 1]), pk(nb, nb));
+      // ((s * q_desc) * k_desc) + nb with the last two steps fused.  INT8: the
+      // score bias is removed inside the first FMA, (s + B) * q_desc - B * q_desc:
+      // the product is exact inside the FMA, so the only added error is the
+      // rounding of B * q_desc (about q_desc / 4, against scores of order 10^3 q_desc)
+      if (QK == FD_QK_INT8) {
+        const float nbq = -S_BIAS * qd;
+        v = fma2(fma2(v, pk(qd, qd), pk(nbq, nbq)), pk(kd[e], kd[e + 1]), pk(nb, nb));
+      } else {
+        v = fma2(mul2(v, pk(qd, qd)), pk(kd[e], kd[e + 1]), pk(nb, nb));
+      }
     }
     unpk(v, a[e], a[e + 1]);
     if (!FULL) {
