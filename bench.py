@@ -382,58 +382,228 @@ class LaunchRecorder:
 _DIT_CPU_BLOCKS: dict = {}
 
 
-def dit_cpu_sample(img_tokens: int = 1024) -> dict:
-    """One config-3 double-stream block through the oracle on the host cores
-    (CPU-built weights), at 512 text + ``img_tokens`` image tokens, extrapolated
-    to batch-8 steps/s by FLOPs."""
-    from futudiffu_b200.dit import DiTConfig, flops_per_sample_step
-    from oracle import dit as OD
-
+def _cpu_threads() -> int:
     threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
     torch.set_num_threads(threads)
-    full = DiTConfig()
-    cfg = DiTConfig(img_grid=(img_tokens // 64, 64))
-    if img_tokens not in _DIT_CPU_BLOCKS:
-        _DIT_CPU_BLOCKS[img_tokens] = OD.random_double_block(cfg, seed=0)
-    blk = _DIT_CPU_BLOCKS[img_tokens]
-    cg = torch.Generator().manual_seed(1)
-    x_txt = torch.randn(1, cfg.txt_tokens, cfg.hidden, generator=cg).to(torch.bfloat16)
-    x_img = torch.randn(1, cfg.img_tokens, cfg.hidden, generator=cg).to(torch.bfloat16)
-    vec = torch.randn(1, cfg.hidden, generator=cg).to(torch.bfloat16)
-    from futudiffu_b200.dit import image_freqs, text_freqs
+    return threads
 
-    ft = text_freqs(cfg, "cpu").unsqueeze(0)
-    fi = image_freqs(cfg, "cpu").unsqueeze(0)
-    t0 = time.perf_counter()
-    OD.double_block(blk, x_txt, x_img, vec, ft, fi)
-    dt = time.perf_counter() - t0
-    D, R, N = cfg.hidden, cfg.mlp_ratio, cfg.tokens
-    blk_flops = 2 * (3 + 1 + 2 * R) * D * D * N + 4 * N * N * D
-    step_s = dt * (flops_per_sample_step(full) / blk_flops) * DIT_BATCH
+
+def dit_cpu_block_seconds(kind: str, img_tokens: int = 4096) -> float:
+    """Seconds for one config-4 block ("double" or "single") of one sample at 512
+    text + ``img_tokens`` image tokens through the oracle on the host cores, in the
+    reference's torch-eager dequantize-and-compute formulation (CPU-built weights)."""
+    from futudiffu_b200.dit import DiTConfig, image_freqs, text_freqs
+    from oracle import dit as OD
+
+    cfg = DiTConfig(img_grid=(img_tokens // 64, 64))
+    key = (kind, img_tokens)
+    if key not in _DIT_CPU_BLOCKS:
+        blk = OD.random_double_block(cfg, seed=0) if kind == "double" else OD.random_single_block(cfg, seed=1)
+        cg = torch.Generator().manual_seed(1)
+        x_txt = torch.randn(1, cfg.txt_tokens, cfg.hidden, generator=cg).to(torch.bfloat16)
+        x_img = torch.randn(1, cfg.img_tokens, cfg.hidden, generator=cg).to(torch.bfloat16)
+        vec = torch.randn(1, cfg.hidden, generator=cg).to(torch.bfloat16)
+        ft = text_freqs(cfg, "cpu").unsqueeze(0)
+        fi = image_freqs(cfg, "cpu").unsqueeze(0)
+        _DIT_CPU_BLOCKS[key] = (blk, x_txt, x_img, vec, ft, fi)
+    blk, x_txt, x_img, vec, ft, fi = _DIT_CPU_BLOCKS[key]
+    with OD.eager_cpu_timing():
+        t0 = time.perf_counter()
+        if kind == "double":
+            OD.double_block(blk, x_txt, x_img, vec, ft, fi)
+        else:
+            OD.single_block(blk, torch.cat([x_txt, x_img], 1), vec, torch.cat([ft, fi], 1))
+        return time.perf_counter() - t0
+
+
+def dit_cpu_step_seconds(t_double: float, t_single: float) -> float:
+    """A batch-8 Euler step of config 4 from per-block times: linear in the block
+    counts and the batch (every block of every sample does the same work)."""
+    from futudiffu_b200.dit import DiTConfig
+
+    cfg = DiTConfig()
+    return DIT_BATCH * (cfg.n_double * t_double + cfg.n_single * t_single)
+
+
+def dit_cpu_sample() -> dict:
+    """cpu_baseline of the config-4 line: one full-size double-stream and one
+    single-stream block (512 text + 4096 image tokens) on the host cores,
+    extrapolated over block count x batch."""
+    threads = _cpu_threads()
+    td = dit_cpu_block_seconds("double")
+    ts = dit_cpu_block_seconds("single")
+    step_s = dit_cpu_step_seconds(td, ts)
     return {"value": 1.0 / step_s, "unit": "steps/s", "cores": threads, "kind": "port",
-            "sample": f"one double-stream block at {cfg.txt_tokens}+{cfg.img_tokens} tokens through "
-                      f"oracle.dit.double_block ({dt:.1f} s, {threads} threads), extrapolated to a "
-                      f"batch-{DIT_BATCH} Euler step by FLOP ratio ({step_s:.0f} s/step)"}
+            "extrapolated": True,
+            "sample": f"one double-stream ({td:.2f} s) and one single-stream ({ts:.2f} s) block at 512 text + "
+                      f"4096 image tokens through oracle.dit (torch-eager dequantize-and-compute: fp32 matmuls "
+                      f"of dequantised fp8 operands, restated int8/fp8 attention; {threads} threads), times "
+                      f"batch 8 x (19 double + 38 single) blocks ({step_s:.0f} s/step)"}
+
+
+def dit_config(cfg, gpus: int) -> dict:
+    """The config-4 workload description, identical in both arms."""
+    return {"workload": "config4_dit_denoise", "batch": DIT_BATCH, "per_gpu_batch": DIT_BATCH // gpus,
+            "blocks": f"{cfg.n_double} double + {cfg.n_single} single", "hidden": cfg.hidden, "heads": cfg.heads,
+            "tokens": f"{cfg.img_tokens} image + {cfg.txt_tokens} text", "euler_steps": 28,
+            "linears": "fp8 e4m3, 1x128 activation / 128x128 weight fp32 scales",
+            "attention": f"{cfg.qk_quant} {cfg.granularity.replace('_', '-')} QK (K mean-smoothed), "
+                         f"{cfg.pv_quant} P and V",
+            "l2": "weights 11 GB and activations >> 126 MB L2; no explicit flush",
+            "parallelism": f"batch sharded by sample x{gpus}, no collective"}
 
 
 def run_dit_reference(args, world, rank):
+    """The reference arm: the oracle's CPU formulation on rank 0.  Each warm-up step
+    is a small block (512 + 256 tokens); each timed step is one full-size block,
+    double and single alternating (a pair when one step is asked for); the value
+    is extrapolated over block count x batch from the mean block times."""
     if rank != 0:
         return 0
-    vals, cb = [], None
-    for i in range(args.warmup + args.steps):
-        cb = dit_cpu_sample(img_tokens=256)
-        if i >= args.warmup:
-            vals.append(cb["value"])
-    val = statistics.mean(vals)
+    from futudiffu_b200.dit import DiTConfig
+
+    threads = _cpu_threads()
+    for i in range(args.warmup):
+        dit_cpu_block_seconds("double" if i % 2 == 0 else "single", img_tokens=256)
+    times = {"double": [], "single": []}
+    for i in range(args.steps):
+        kinds = ("double", "single") if args.steps == 1 else (("double",) if i % 2 == 0 else ("single",))
+        for kind in kinds:
+            times[kind].append(dit_cpu_block_seconds(kind))
+    td, ts = statistics.mean(times["double"]), statistics.mean(times["single"])
+    step_s = dit_cpu_step_seconds(td, ts)
+    val = 1.0 / step_s
+    timed_s = sum(times["double"]) + sum(times["single"])
+    cb = {"value": val, "unit": "steps/s", "cores": threads, "kind": "port", "extrapolated": True,
+          "sample": f"{len(times['double'])} double-stream and {len(times['single'])} single-stream blocks at "
+                    f"512 text + 4096 image tokens through oracle.dit (torch-eager dequantize-and-compute; "
+                    f"{threads} threads; mean {td:.2f} s / {ts:.2f} s per block), times batch 8 x "
+                    f"(19 double + 38 single) blocks ({step_s:.0f} s/step)"}
     print(json.dumps({
         "impl": "reference", "metric": DIT_METRIC, "value": val, "unit": "steps/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / val, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "fp8/int8", "data": "synthetic",
-        "config": {"workload": "config4_dit_denoise", "batch": DIT_BATCH, "tokens": 4608},
-        "cpu_baseline": {**cb, "value": val},
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": timed_s / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp8/int8",
+        "data": "synthetic (random-init weights, N(0,1) activations)",
+        "config": dit_config(DiTConfig(), args.gpus),
+        "extrapolated": True,
+        "extrapolation": "each timed step is one full-size block (ms_per_step is its CPU time); value = 1 / "
+                         "(8 samples x (19 x mean double-block s + 38 x mean single-block s))",
+        "cpu_baseline": cb,
         "e2e": {"value": val, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
     return 0
+
+
+def time_gemm(dev, shape: str, steps: int, warmup: int) -> list[float]:
+    """CUDA-event durations (ms) of ``steps`` FP8 block-GEMM launches at one of
+    GEMM_SHAPES (bf16 output), with a 256 MiB write between launches so that every
+    launch reads its operands from HBM (the operands are smaller than L2)."""
+    from futudiffu_b200 import _lib as L
+    from futudiffu_b200.fp8 import quantize_fp8_blockwise_cuda
+    from futudiffu_b200.fp8_kernels import fp8_act_quant
+
+    M, N, K = GEMM_SHAPES[shape]
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(dev)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(dev)
+    w8, ws = quantize_fp8_blockwise_cuda(w)
+    a8, a_s = fp8_act_quant(x)
+    c = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def gemm():
+        L.call("fd_fp8_gemm_blockwise", L.ptr(a8), L.ptr(a_s), L.ptr(w8), L.ptr(ws), None, 0, L.ptr(c),
+               L.DT_BF16, M, N, K, 0, L.stream_ptr(dev))
+
+    for _ in range(warmup):
+        gemm()
+    torch.cuda.synchronize()
+    ev = []
+    for _ in range(steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        gemm()
+        e1.record(stream)
+        ev.append((e0, e1))
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in ev]
+
+
+def time_attention(dev, pv: str, steps: int, warmup: int, seed: int = 1234) -> tuple[list[float], list[float]]:
+    """Config 2 (B2 H24 S4096 D128, INT8 per-block Q/K, ``pv`` P and V): CUDA-event
+    durations (ms) of the attention kernel alone and of the whole public call
+    (``sage_attn_forward``: quantisation prologue + attention kernel)."""
+    from futudiffu_b200 import _lib as L
+    from futudiffu_b200 import sage_attention as SA
+
+    q, k, v = make_inputs(seed, dev)
+    BH = B * H
+    qf, kf, vf = (t.reshape(BH, S, D) for t in (q, k, v))
+    stream = torch.cuda.current_stream(dev)
+    pvk = L.PV_FP8 if pv == "fp8" else L.PV_BF16
+    qz = SA.quantize_qkv(qf, kf, vf, 1.0 / math.sqrt(D), smooth_k=True, qk_quant="int8", granularity="per_block",
+                         pv_quant=pv)
+    vsrc = qz["v_codes"] if pv == "fp8" else vf
+    out = torch.empty_like(qf)
+
+    def kernel():
+        L.call("fd_sage_attn_fwd", L.ptr(qz["q_codes"]), L.ptr(qz["q_desc"]), L.ptr(qz["k_codes"]),
+               L.ptr(qz["k_desc"]), L.ptr(vsrc), L.ptr(qz["v_desc"]), None, 0, L.ptr(out), None,
+               BH, S, L.QK_INT8, L.GRAN_BLOCK, L.GRAN_BLOCK, pvk, L.stream_ptr(dev))
+
+    SA.configure_sage(smooth_k=True, qk_quant="int8", pv_quant=pv, qk_granularity="per_block")
+    try:
+        res = []
+        for fn in (kernel, lambda: SA.sage_attn_forward(q, k, v)):
+            for _ in range(warmup):
+                fn()
+            torch.cuda.synchronize()
+            ev = []
+            for _ in range(steps):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                fn()
+                e1.record(stream)
+                ev.append((e0, e1))
+            torch.cuda.synchronize()
+            res.append([a.elapsed_time(b) for a, b in ev])
+    finally:
+        SA.configure_sage()
+    return res[0], res[1]
+
+
+def sub_entries(dev, world: int, local: int) -> dict:
+    """BASELINE.json's other two metrics, measured in the same process on every
+    rank (replicas; max over ranks): FP8 block-GEMM TFLOPS at config 1 and at the
+    reference's QKV shape, SageAttn TOPS at config 2."""
+    pk = peaks()
+    out = {}
+    with ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else local) as clocks:
+        for shape in ("config1", "ref_qkv"):
+            M, N, K = GEMM_SHAPES[shape]
+            ms = max_over_ranks(statistics.mean(time_gemm(dev, shape, 30, 5)), world, dev)
+            tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+            out[f"gemm_{shape}"] = {
+                "metric": "FP8 block-GEMM TFLOPS", "value": tf * world, "unit": "TFLOPS", "per_gpu": tf,
+                "ms": ms, "shape": {"M": M, "N": N, "K": K}, "l2": "flushed between launches",
+                "frac_of_2x_burst_bf16": tf / (2.0 * pk["bf16_tflops"])}
+        for pv in ("fp8", "bf16"):
+            kms, sms = time_attention(dev, pv, 20, 5)
+            kms = max_over_ranks(statistics.mean(kms), world, dev)
+            sms = max_over_ranks(statistics.mean(sms), world, dev)
+            kt, st = OPS_PER_STEP / (kms * 1e-3) / 1e12, OPS_PER_STEP / (sms * 1e-3) / 1e12
+            out[f"attention_config2_{pv}_pv"] = {
+                "metric": "SageAttn TOPS", "value": st * world, "unit": "TOPS", "per_gpu": st,
+                "ms": sms, "kernel_ms": kms, "kernel_tops": kt,
+                "mode": f"int8 per-block QK (K mean-smoothed), {'e4m3 P and per-channel V' if pv == 'fp8' else 'bf16 P and V'}",
+                "timed": "sage_attn_forward (quantisation prologue + attention kernel); kernel_* the attention "
+                         "kernel alone",
+                "frac_of_2x_burst_bf16": kt / (2.0 * pk["bf16_tflops"])}
+    for v in out.values():
+        v["clocks"] = clocks.summary()
+    return out
 
 
 def run_dit(args, world, rank, local):
@@ -480,6 +650,16 @@ def run_dit(args, world, rank, local):
     for i in range(2):
         x = graph(x, d_txt, sig[i % 28], sig[i % 28 + 1])
     torch.cuda.synchronize()
+    # settle: untimed replays for 3 s, so that the timed steps run at the clock the
+    # GPU holds under this load (power-capped) whatever the per-GPU batch
+    t_settle = time.perf_counter()
+    n_settle = 0
+    while time.perf_counter() - t_settle < 3.0:
+        x = graph(x, d_txt, sig[n_settle % 28], sig[n_settle % 28 + 1])
+        n_settle += 1
+        if n_settle % 4 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -524,27 +704,30 @@ def run_dit(args, world, rank, local):
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_n, world, dev)
     check_status()
 
+    subs = sub_entries(dev, world, local) if not args.no_sub else {}
+    check_status()
+
     if rank == 0:
         pk = peaks()
         peak = 2.0 * pk["bf16_tflops_sustained"]
         gemm_tf = gemm_work / (gemm_ms * 1e-3) / 1e12
         step_flops = flops_per_sample_step(cfg) * DIT_BATCH
+        clk = clocks.summary()
         line = {
             "metric": DIT_METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "fp8/int8", "data": "synthetic (random-init weights, N(0,1) latents/text)",
-            "config": {"workload": "config4_dit_denoise", "batch": DIT_BATCH, "per_gpu_batch": bl,
-                       "blocks": "19 double + 38 single", "hidden": cfg.hidden, "heads": cfg.heads,
-                       "tokens": f"{cfg.img_tokens} image + {cfg.txt_tokens} text", "euler_steps": 28,
-                       "linears": "fp8 e4m3 1x128 act / 128x128 weight scales (tcgen05)",
-                       "attention": "int8 per-block QK, e4m3 P/V (tcgen05)",
-                       "l2": "weights 11 GB and activations >> 126 MB L2; no explicit flush",
-                       "parallelism": f"batch sharded by sample x{world}, no collective",
-                       "model_tflop_per_step": step_flops / 1e12,
+            "config": dit_config(cfg, world),
+            "detail": {"model_tflop_per_step": step_flops / 1e12,
                        "model_tflops": step_flops / (ms * 1e-3) / 1e12,
                        "attention_kernel_tops": attn_work / (attn_ms * 1e-3) / 1e12 if attn_ms else None,
                        "time_share": {"gemm": gemm_ms / n_rec / ms_local, "attention": attn_ms / n_rec / ms_local},
-                       "launch": "each timed step replays the step's ~1350 kernels as one captured CUDA graph"},
+                       "launch": f"each timed step replays the step's {launches_per_step} kernels as one "
+                                 "captured CUDA graph",
+                       "settle": f"{n_settle} untimed replays (3 s) before the timed steps"},
+            "clock_normalised": {"sm_mhz_median": clk.get("sm_mhz"),
+                                 "ms_x_mhz": ms * clk["sm_mhz"] if clk.get("sm_mhz") else None,
+                                 "note": "step time x median SM clock under load; compare across N"},
             "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": peak, "unit": "TFLOP/s",
                          "frac": gemm_tf / peak, "traffic": None,
                          "kernel": f"gemm_fp8_kernel (all {n_gemm // n_rec} GEMM launches of a step, "
@@ -557,7 +740,8 @@ def run_dit(args, world, rank, local):
                     "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms,
                     "api": "futudiffu_b200.dit.EulerStepGraph (pinned host inputs copied in, result copied out)"},
             "gpu_launches": launches,
-            "clocks": clocks.summary(),
+            "clocks": clk,
+            "sub": subs,
         }
         print(json.dumps(line), flush=True)
     return 0
@@ -573,15 +757,17 @@ def block_flops(cfg) -> float:
     return 2 * (3 + 1 + 2 * R) * D * D * N + 4 * N * N * D
 
 
-def block_cpu_sample(img_tokens: int = 1024) -> dict:
-    """The oracle's double-stream block on the host cores at 512 text +
-    ``img_tokens`` image tokens (dit_cpu_sample), as a FLOP rate."""
-    from futudiffu_b200.dit import DiTConfig, flops_per_sample_step
+def block_cpu_sample() -> dict:
+    """The oracle's double-stream block at its full size (512 text + 4096 image
+    tokens) on the host cores, in the torch-eager dequantize-and-compute
+    formulation, as a FLOP rate."""
+    from futudiffu_b200.dit import DiTConfig
 
-    cb = dit_cpu_sample(img_tokens=img_tokens)
-    val = cb["value"] * flops_per_sample_step(DiTConfig()) * DIT_BATCH / 1e12  # batch-8 steps/s -> FLOP/s
-    sample = cb["sample"].split(", extrapolated")[0] + "; its FLOP rate stands for the full block's"
-    return {**cb, "value": val, "unit": "TFLOPS", "sample": sample}
+    threads = _cpu_threads()
+    td = dit_cpu_block_seconds("double")
+    return {"value": block_flops(DiTConfig()) / td / 1e12, "unit": "TFLOPS", "cores": threads, "kind": "port",
+            "sample": f"one double-stream block at 512 text + 4096 image tokens through oracle.dit.double_block "
+                      f"(torch-eager dequantize-and-compute, {threads} threads): {td:.2f} s"}
 
 
 def run_block_reference(args, world, rank):
@@ -589,22 +775,37 @@ def run_block_reference(args, world, rank):
         return 0
     from futudiffu_b200.dit import DiTConfig
 
+    threads = _cpu_threads()
     full = block_flops(DiTConfig())
-    vals, cb = [], None
-    for i in range(args.warmup + args.steps):
-        cb = block_cpu_sample(img_tokens=256)
-        if i >= args.warmup:
-            vals.append(cb["value"])
-    val = statistics.mean(vals)
+    for _ in range(args.warmup):
+        dit_cpu_block_seconds("double", img_tokens=256)
+    times = [dit_cpu_block_seconds("double") for _ in range(args.steps)]
+    td = statistics.mean(times)
+    val = full / td / 1e12
+    cb = {"value": val, "unit": "TFLOPS", "cores": threads, "kind": "port",
+          "sample": f"{len(times)} double-stream blocks at 512 text + 4096 image tokens through "
+                    f"oracle.dit.double_block (torch-eager dequantize-and-compute, {threads} threads), "
+                    f"mean {td:.2f} s"}
     print(json.dumps({
         "impl": "reference", "metric": BLOCK_METRIC, "value": val, "unit": "TFLOPS", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": full / (val * 1e12) * 1e3,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": td * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp8/int8",
-        "data": "synthetic", "config": {"workload": "config3_mmdit_block", "batch": 1, "tokens": "512+4096"},
-        "cpu_baseline": {**cb, "value": val},
+        "data": "synthetic (random-init weights, N(0,1) activations)", "config": block_config(DiTConfig(), args.gpus),
+        "cpu_baseline": cb,
         "e2e": {"value": val, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
     return 0
+
+
+def block_config(cfg, gpus: int) -> dict:
+    """The config-3 workload description, identical in both arms."""
+    return {"workload": "config3_mmdit_block", "batch": 1, "hidden": cfg.hidden, "heads": cfg.heads,
+            "tokens": f"{cfg.txt_tokens} text + {cfg.img_tokens} image", "mlp": "ratio 4, GELU-tanh",
+            "linears": "fp8 e4m3, 1x128 activation / 128x128 weight fp32 scales",
+            "attention": f"{cfg.qk_quant} {cfg.granularity.replace('_', '-')} QK (K mean-smoothed), "
+                         f"{cfg.pv_quant} P and V",
+            "l2": "block weights 226 MB fp8 > 126 MB L2; no explicit flush",
+            "parallelism": f"replica per GPU x{gpus}"}
 
 
 def run_block(args, world, rank, local):
@@ -708,14 +909,10 @@ def run_block(args, world, rank, local):
             "metric": BLOCK_METRIC, "value": tf * world, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp8/int8", "data": "synthetic (random-init weights, N(0,1) activations)",
-            "config": {"workload": "config3_mmdit_block", "batch": 1, "hidden": cfg.hidden, "heads": cfg.heads,
-                       "tokens": f"{cfg.txt_tokens} text + {cfg.img_tokens} image", "mlp": "ratio 4, GELU-tanh",
-                       "linears": "fp8 e4m3 1x128 act / 128x128 weight scales (tcgen05), the two streams' "
-                                  "linears as grouped launches",
-                       "attention": "fused RMSNorm/RoPE/quant prologue, int8 per-block QK, e4m3 P/V (tcgen05)",
-                       "block_tflop": flops / 1e12,
-                       "l2": "block weights 226 MB fp8 > 126 MB L2; no explicit flush",
-                       "parallelism": f"replica per GPU x{world}",
+            "config": block_config(cfg, world),
+            "detail": {"block_tflop": flops / 1e12,
+                       "linears": "the two streams' linears as grouped launches",
+                       "attention": "fused RMSNorm/RoPE/quant prologue, then the tcgen05 attention kernel",
                        "time_share": {"gemm": gemm_ms / n_rec / ms_local, "attention": attn_ms / n_rec / ms_local},
                        "attention_kernel_tops": attn_work / (attn_ms * 1e-3) / 1e12 if attn_ms else None,
                        "launch": f"each step replays the block's {launches_per_step} kernels as one CUDA graph"},
@@ -1076,42 +1273,15 @@ def run_packed(args, world, rank, local):
 
 
 def run_gemm(args, world, rank, local):
-    """FP8 block-GEMM TFLOPS (benchmark config 1, or the reference's own Z-Image shapes)."""
-    from futudiffu_b200 import _lib as L
+    """FP8 block-GEMM TFLOPS (benchmark config 1, or the reference's Z-Image shapes)."""
     from futudiffu_b200 import check_status
-    from futudiffu_b200.fp8 import quantize_fp8_blockwise_cuda
-    from futudiffu_b200.fp8_kernels import fp8_act_quant
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     M, N, K = GEMM_SHAPES[args.gemm_shape]
-    g = torch.Generator().manual_seed(0)
-    x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(dev)
-    w = (torch.randn(N, K, generator=g) * 0.02).to(dev)
-    w8, ws = quantize_fp8_blockwise_cuda(w)
-    a8, a_s = fp8_act_quant(x)
-    c = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
-    stream = torch.cuda.current_stream(dev)
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
-
-    def gemm():
-        L.call("fd_fp8_gemm_blockwise", L.ptr(a8), L.ptr(a_s), L.ptr(w8), L.ptr(ws), None, 0, L.ptr(c),
-               L.DT_BF16, M, N, K, 0, L.stream_ptr(dev))
-
-    for _ in range(args.warmup):
-        gemm()
-    torch.cuda.synchronize()
-    times = []
     with ClockSampler(local) as clocks:
-        for _ in range(args.steps):
-            flush.zero_()  # L2 flush between timed launches (operands < L2)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            gemm()
-            e1.record(stream)
-            times.append((e0, e1))
-        torch.cuda.synchronize()
-    ms = statistics.mean(a.elapsed_time(b) for a, b in times)
+        times = time_gemm(dev, args.gemm_shape, args.steps, args.warmup)
+    ms = max_over_ranks(statistics.mean(times), world, dev)
     check_status()
     flops = 2.0 * M * N * K
     pk = peaks()
@@ -1145,6 +1315,8 @@ def main(argv=None) -> int:
                          "4288-token bin through Z-Image-class JointTransformerBlocks")
     ap.add_argument("--gemm-shape", choices=sorted(GEMM_SHAPES), default="config1")
     ap.add_argument("--layers", type=int, default=30, help="packed: JointTransformerBlocks in the stack")
+    ap.add_argument("--no-sub", action="store_true",
+                    help="dit: skip the config-1 GEMM / config-2 attention sub-measurements")
     ap.add_argument("--profile", action="store_true",
                     help="dit, block, packed: bracket the first timed step with cudaProfilerStart/Stop "
                          "(for ncu --profile-from-start off); timing of that run is not a result")

@@ -347,7 +347,23 @@ def sage_attn_forward_masked_with_lse(
                          pv_quant=_pv_for("bf16"), granularity=_SAGE_QK_GRAN, want_lse=True)
 
 
-def _attn_backward(q, k, v, out, lse, dout, sm_scale, block_mask, qk_quant):
+def _per_token_descales(qz: dict, N: int) -> tuple[Tensor, Tensor]:
+    """Q / K descales in the per-token layout (BH, round_up(N, 128)) that the
+    backward kernels index by row.  Per-block scales (one per 128 Q rows, one per
+    64 K rows) are repeated over their rows; the padding tail is zero."""
+    if qz["gran"] == L.GRAN_TOKEN:
+        return qz["q_desc"], qz["k_desc"]
+    width = _desc_stride(N, L.GRAN_TOKEN, 1)
+    qd = qz["q_desc"].repeat_interleave(128, dim=1)[:, :width]
+    kd = qz["k_desc"].repeat_interleave(64, dim=1)[:, :width]
+    qt = torch.zeros(qd.shape[0], width, dtype=torch.float32, device=qd.device)
+    kt = torch.zeros_like(qt)
+    qt[:, :N] = qd[:, :N]
+    kt[:, :N] = kd[:, :N]
+    return qt, kt
+
+
+def _attn_backward(q, k, v, out, lse, dout, sm_scale, block_mask, qk_quant, granularity):
     B, H, N, D = q.shape
     BH = B * H
     L.require_cuda(q, k, v, out, lse, dout)
@@ -358,9 +374,11 @@ def _attn_backward(q, k, v, out, lse, dout, sm_scale, block_mask, qk_quant):
     dof = dout.reshape(BH, N, D).contiguous().to(torch.bfloat16)
     lse = lse.contiguous()
     bm, bm_stride = _normalize_mask(block_mask, N)
-    # same per-token codes (and smoothed K) as the forward
+    # the forward's codes, scales and smoothed K: P = exp2(S - LSE) is only the
+    # forward's P when S is recomputed at the forward's quantisation granularity
     qz = quantize_qkv(qf, kf, vf, sm_scale, smooth_k=_SAGE_SMOOTH_K, qk_quant=qk_quant,
-                      granularity="per_token", pv_quant="bf16")
+                      granularity=granularity, pv_quant="bf16")
+    qz["q_desc"], qz["k_desc"] = _per_token_descales(qz, N)
     delta = torch.empty(BH, N, dtype=torch.float32, device=q.device)
     L.call("fd_sage_attn_bwd_prepass", L.ptr(dof), L.ptr(of), L.ptr(delta), BH, N, L.stream_ptr(q.device))
     if _SAGE_SMOOTH_K:
@@ -439,16 +457,21 @@ def _attn_backward_tc(qf, ks, vf, dof, lse, delta, qz, bm, bm_stride, sm_scale):
 def sage_attn_backward(
     q: Tensor, k: Tensor, v: Tensor, out: Tensor, lse: Tensor, dout: Tensor, sm_scale: float,
 ) -> tuple[Tensor, Tensor, Tensor]:
-    """dQ, dK, dV with the forward's quantised P recomputation (reference :344-458)."""
-    return _attn_backward(q, k, v, out, lse, dout, sm_scale, None, _SAGE_QK_QUANT)
+    """dQ, dK, dV with the forward's quantised P recomputation (reference :344-458).
+
+    P is recomputed with the Q/K quantisation that the forward entry points use
+    under the current ``configure_sage`` setting (per-token, or per-block when
+    ``qk_granularity="per_block"``), so it equals the forward's P."""
+    return _attn_backward(q, k, v, out, lse, dout, sm_scale, None, _SAGE_QK_QUANT, _SAGE_QK_GRAN)
 
 
 def sage_attn_backward_masked(
     q: Tensor, k: Tensor, v: Tensor, out: Tensor, lse: Tensor, dout: Tensor, block_mask: Tensor,
     sm_scale: float,
 ) -> tuple[Tensor, Tensor, Tensor]:
-    """Masked backward, INT8 recompute (reference :534-648)."""
-    return _attn_backward(q, k, v, out, lse, dout, sm_scale, block_mask, "int8")
+    """Masked backward, INT8 recompute (reference :534-648), at the forward's
+    quantisation granularity."""
+    return _attn_backward(q, k, v, out, lse, dout, sm_scale, block_mask, "int8", _SAGE_QK_GRAN)
 
 
 def smoke_test_fp8_dot(n: int = 128) -> dict:

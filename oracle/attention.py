@@ -15,6 +15,7 @@ static-P fp8 PV variant apply the same formulas at the stated granularity.
 
 from __future__ import annotations
 
+import contextlib
 import math
 
 import torch
@@ -23,6 +24,22 @@ from .quant import triton_div
 
 LOG2E = math.log2(math.e)
 E4M3 = torch.float8_e4m3fn
+# Matmul type of the restatement: float64 (exact INT8 dot products, one rounding
+# of each fp8 / bf16 dot product) for parity; bench.py's CPU-baseline timing
+# evaluates the same formulas in fp32 (matmul_dtype(torch.float32)), as a torch
+# eager CPU implementation would.
+_MM = torch.float64
+
+
+@contextlib.contextmanager
+def matmul_dtype(dt):
+    global _MM
+    old = _MM
+    _MM = dt
+    try:
+        yield
+    finally:
+        _MM = old
 
 
 def smooth_k(k: torch.Tensor) -> torch.Tensor:
@@ -105,8 +122,8 @@ def attention_forward(
     kc, kd = quant_rows(ks, qk_quant, rk)
     qd_rows = qd.repeat_interleave(rq, dim=1)[:, :N]
     kd_rows = kd.repeat_interleave(rk, dim=1)[:, :N]
-    qf = qc.to(torch.float64)
-    kf = kc.to(torch.float64)
+    qf = qc.to(_MM)
+    kf = kc.to(_MM)
     vb = v.cpu()
     if pv_quant == "fp8_channel":
         vc, vdesc = quant_v_per_channel(vb)
@@ -124,18 +141,18 @@ def attention_forward(
         p = torch.exp2(s - m_new.unsqueeze(-1))
         l_new = alpha * l + p.sum(dim=-1)
         if pv_quant == "bf16":
-            pv = (p.to(torch.bfloat16).to(torch.float64) @ vb[:, n0:n1].to(torch.float64)).to(torch.float32)
+            pv = (p.to(torch.bfloat16).to(_MM) @ vb[:, n0:n1].to(_MM)).to(torch.float32)
         elif pv_quant == "fp8_tile":
             pam = p.abs().amax(dim=-1)
             p8 = (p * triton_div(448.0, torch.clamp(pam, min=1e-12)).unsqueeze(-1)).to(E4M3)
             vt = vb[:, n0:n1].float()
             vam = vt.abs().amax(dim=1)
             v8 = (vt * triton_div(448.0, torch.clamp(vam, min=1e-12)).unsqueeze(1)).to(E4M3)
-            pv = (p8.to(torch.float64) @ v8.to(torch.float64)).to(torch.float32)
+            pv = (p8.to(_MM) @ v8.to(_MM)).to(torch.float32)
             pv = (pv * triton_div(pam, 448.0).unsqueeze(-1)) * triton_div(vam, 448.0).unsqueeze(1)
         elif pv_quant == "fp8_channel":
             p8 = (p * 448.0).clamp(max=448.0).to(E4M3)
-            pv = (p8.to(torch.float64) @ vc[:, n0:n1].to(torch.float64)).to(torch.float32)
+            pv = (p8.to(_MM) @ vc[:, n0:n1].to(_MM)).to(torch.float32)
             pv = pv * (vdesc.unsqueeze(1) / 448.0)
         else:
             raise ValueError(pv_quant)
@@ -161,18 +178,23 @@ def attention_exact(q, k, v, sm_scale: float | None = None):
 
 
 def attention_backward(q, k, v, out, lse, dout, *, sm_scale: float, qk_quant: str = "int8",
-                       smooth: bool = True, block_mask=None, k_mean=None):
-    """dQ, dK, dV with the forward's per-token quantised P (reference :322-349, :805-1015).
+                       smooth: bool = True, block_mask=None, k_mean=None, granularity: str = "per_token"):
+    """dQ, dK, dV with the forward's quantised P (reference :322-349, :805-1015).
 
-    Block-masked pairs (128-row Q block x 64-key tile) contribute nothing (:1491-1722).
+    P is recomputed from the saved LSE with the forward's Q/K quantisation: per
+    token (the reference) or per block (128 Q rows, 64 K rows).  Block-masked
+    pairs (128-row Q block x 64-key tile) contribute nothing (:1491-1722).
     """
     BH, N, D = q.shape
     sl2e = sm_scale * LOG2E
     ks = k.cpu()
     if smooth:
         ks = smooth_k(ks) if k_mean is None else smooth_k_with_mean(ks, k_mean)
-    qc, qd = quant_rows(q, qk_quant, 1, sl2e)
-    kc, kd = quant_rows(ks, qk_quant, 1)
+    rq, rk = (1, 1) if granularity == "per_token" else (128, 64)
+    qc, qd = quant_rows(q, qk_quant, rq, sl2e)
+    kc, kd = quant_rows(ks, qk_quant, rk)
+    qd = qd.repeat_interleave(rq, dim=1)[:, :N]
+    kd = kd.repeat_interleave(rk, dim=1)[:, :N]
     s = (qc.to(torch.float64) @ kc.to(torch.float64).transpose(1, 2)).to(torch.float32)
     s = (s * qd.unsqueeze(-1)) * kd.unsqueeze(1)
     p = torch.exp2(s - lse.cpu().unsqueeze(-1))

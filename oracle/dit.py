@@ -13,6 +13,8 @@ fused_kernels.py:43-247, QKV :270-471, attention sage_kernels.py:1379-1477.
 
 from __future__ import annotations
 
+import contextlib
+
 import torch
 
 from oracle import attention as OA
@@ -154,6 +156,38 @@ def random_double_block(cfg, seed: int = 0):
             mlp_in=fp8_linear(R * D, D), mlp_out=fp8_linear(D, R * D))
 
     return SimpleNamespace(cfg=cfg, txt=stream(), img=stream())
+
+
+def random_single_block(cfg, seed: int = 0):
+    """Weights of one single-stream block built on the CPU alone, with the
+    attribute layout of futudiffu_b200.dit.SingleStreamBlock."""
+    from types import SimpleNamespace
+
+    g = torch.Generator().manual_seed(seed)
+    D, R = cfg.hidden, cfg.mlp_ratio
+
+    def rand(shape, std, mean=0.0):
+        return (torch.randn(shape, generator=g) * std + mean).to(torch.bfloat16)
+
+    def fp8_linear(n, k):
+        w8, ws = OQ.weight_quant(torch.randn(n, k, generator=g) * 0.02)
+        return SimpleNamespace(weight=w8, weight_scale=ws, bias=None)
+
+    return SimpleNamespace(
+        cfg=cfg, adaln=SimpleNamespace(weight=rand((2 * D, D), 0.02), bias=rand((2 * D,), 0.02)),
+        norm_w=[rand((D,), 0.05, 1.0) for _ in range(2)],
+        q_norm=rand((128,), 0.05, 1.0), k_norm=rand((128,), 0.05, 1.0),
+        linear1=fp8_linear(3 * D + R * D, D), linear2=fp8_linear(D, D + R * D))
+
+
+@contextlib.contextmanager
+def eager_cpu_timing():
+    """The reference's torch-eager dequantize-and-compute CPU formulation, used
+    only to time the CPU baseline: linears as dequantised operands in one fp32
+    matmul (oracle.gemm.dequant_compute), attention matmuls in fp32.  Quantisers,
+    norms and the online softmax are the same restatements as in parity mode."""
+    with OG.dequant_compute(), OA.matmul_dtype(torch.float32):
+        yield
 
 
 def random_video_block(cfg, seed: int = 0):

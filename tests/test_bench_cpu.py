@@ -7,6 +7,7 @@ import json
 import os
 import subprocess
 import sys
+import time
 
 import pytest
 
@@ -21,16 +22,18 @@ def _json_lines(out: str) -> list[dict]:
 
 
 def _env():
-    env = dict(os.environ, MASTER_ADDR="127.0.0.1", OMP_NUM_THREADS="2")
+    env = dict(os.environ, MASTER_ADDR="127.0.0.1", OMP_NUM_THREADS="4")
     env.pop("CUDA_VISIBLE_DEVICES", None)
     return env
 
 
 @pytest.mark.parametrize("workload", ["dit", "block"])
 def test_reference_arm_json(workload):
+    t0 = time.perf_counter()
     r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--workload", workload,
                         "--steps", "1", "--warmup", "3"], capture_output=True, text=True, timeout=600, env=_env(),
                        cwd=ROOT)
+    wall = time.perf_counter() - t0
     assert r.returncode == 0, r.stderr[-2000:]
     lines = _json_lines(r.stdout)
     assert len(lines) == 1
@@ -40,6 +43,8 @@ def test_reference_arm_json(workload):
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     assert d["e2e"]["value"] == d["value"] and d["e2e"]["unit"] == d["unit"]
+    # the line claims only the work it timed: steps x ms_per_step fits inside the run
+    assert d["steps"] * d["ms_per_step"] / 1e3 <= wall
 
 
 def test_reference_arm_two_ranks_prints_once():

@@ -241,11 +241,13 @@ def test_attention_status_clean(cuda_device):
     check_status()
 
 
+@pytest.mark.parametrize("gran", ["per_token", "per_block"])
 @pytest.mark.parametrize("qk", ["int8", "fp8"])
 @pytest.mark.parametrize("N,masked", [(256, False), (200, False), (201, False), (384, True)])
-def test_attention_backward_vs_oracle(cuda_device, qk, N, masked):
+def test_attention_backward_vs_oracle(cuda_device, qk, N, masked, gran):
     """N % 8 == 0: the tensor-core backward (library GEMMs + elementwise kernel);
-    N = 201: the CUDA-core kernels."""
+    N = 201: the CUDA-core kernels.  Both granularities: the backward recomputes
+    P with the forward's Q/K scales (bf16 PV, so the forward is the oracle's)."""
     from futudiffu_b200 import sage_attention as SA
 
     BH = 2
@@ -255,22 +257,52 @@ def test_attention_backward_vs_oracle(cuda_device, qk, N, masked):
     mask = None
     if masked:
         mask = torch.from_numpy(OB.build_block_mask([128, N - 128]))
-    SA.configure_sage(smooth_k=True, qk_quant=qk, pv_quant="bf16")
+    SA.configure_sage(smooth_k=True, qk_quant=qk, pv_quant="bf16", qk_granularity=gran)
     d = lambda t: t.to(cuda_device).unsqueeze(0)  # noqa: E731
     if masked:
         out, lse = SA.sage_attn_forward_masked_with_lse(d(q), d(k), d(v), mask.to(cuda_device), SM)
         dq, dk, dv = SA.sage_attn_backward_masked(d(q), d(k), d(v), out, lse, d(dout), mask.to(cuda_device), SM)
         qkr = "int8"
     else:
-        SA.configure_sage(smooth_k=True, qk_quant=qk, pv_quant="bf16")
         out, lse = SA.sage_attn_forward_with_lse(d(q), d(k), d(v), SM)
         dq, dk, dv = SA.sage_attn_backward(d(q), d(k), d(v), out, lse, d(dout), SM)
         qkr = qk
-    km = None
+    # the forward's LSE normalises the oracle's P at the same granularity: rows sum to 1
+    ks = OA.smooth_k(k)
+    rq, rk = (1, 1) if gran == "per_token" else (128, 64)
+    qc, qd = OA.quant_rows(q, qkr, rq, SM * OA.LOG2E)
+    kc, kd = OA.quant_rows(ks, qkr, rk)
+    s = (qc.double() @ kc.double().transpose(1, 2)).float()
+    s = (s * qd.repeat_interleave(rq, 1)[:, :N, None]) * kd.repeat_interleave(rk, 1)[:, None, :N]
+    p = torch.exp2(s - lse.cpu().unsqueeze(-1))
+    if masked:
+        full = mask.bool().repeat_interleave(128, 0)[:N].repeat_interleave(64, 1)[:, :N]
+        p = p * full
+    assert torch.allclose(p.sum(-1), torch.ones(BH, N), atol=5e-3), p.sum(-1)
     rdq, rdk, rdv, _ = OA.attention_backward(q, k, v, out[0].cpu(), lse.cpu(), dout, sm_scale=SM, qk_quant=qkr,
-                                             block_mask=mask, k_mean=km)
+                                             block_mask=mask, granularity=gran)
     for a, b in ((dq, rdq), (dk, rdk), (dv, rdv)):
         assert torch.isfinite(a.float()).all()
+        assert cosine(a[0].cpu(), b) >= 0.999
+
+
+@pytest.mark.parametrize("pv", ["bf16", "fp8"])
+def test_sage_op_autograd_per_block(cuda_device, pv):
+    """configure_sage(qk_granularity="per_block") through the autograd op: the
+    gradients equal the oracle's backward at per-block granularity."""
+    from futudiffu_b200 import sage_attention as SA
+
+    BH, N = 2, 384
+    q, k, v = qkv(BH, N, 55)
+    w = torch.linspace(-1, 1, 128)
+    SA.configure_sage(smooth_k=True, qk_quant="int8", pv_quant=pv, qk_granularity="per_block")
+    qg, kg, vg = (t.to(cuda_device).unsqueeze(0).requires_grad_(True) for t in (q, k, v))
+    out, lse = SA.sage_attn_op(qg, kg, vg, SM)
+    (out.float() * w.to(cuda_device)).sum().backward()
+    dout = (torch.ones(BH, N, 128) * w).to(torch.bfloat16)
+    rdq, rdk, rdv, _ = OA.attention_backward(q, k, v, out[0].detach().cpu(), lse.detach().cpu(), dout,
+                                             sm_scale=SM, qk_quant="int8", granularity="per_block")
+    for a, b in ((qg.grad, rdq), (kg.grad, rdk), (vg.grad, rdv)):
         assert cosine(a[0].cpu(), b) >= 0.999
 
 
