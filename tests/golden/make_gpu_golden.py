@@ -132,7 +132,7 @@ def run(ref: Path, out_path: Path, timing_path: Path | None, skip_timing: bool) 
         x, w = C.gemm_inputs(name)
         x, w = x.to(DEV), w.to(DEV)
         a8, a_s = rk.fp8_act_quant(x)
-        b8, b_s = rfp8.quantize_fp8_blockwise(w)
+        b8, b_s = (t.to(DEV) for t in rfp8.quantize_fp8_blockwise(w))  # returned on the CPU (fp8.py:371)
         c = rk.fp8_gemm_blockwise(a8, a_s, b8, b_s, output_dtype=torch.bfloat16)
         rows = C.row_sample(M, C.GEMM_SAMPLE_ROWS[name])
         d = {"a_codes": C.digest(a8), "a_scales": C.digest(a_s), "b_codes": C.digest(b8), "b_scales": C.digest(b_s),
@@ -159,7 +159,7 @@ def run(ref: Path, out_path: Path, timing_path: Path | None, skip_timing: bool) 
             x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(DEV)
             w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
             a8, a_s = rk.fp8_act_quant(x)
-            b8, b_s = rfp8.quantize_fp8_blockwise(w)
+            b8, b_s = (t.to(DEV) for t in rfp8.quantize_fp8_blockwise(w))
             record(f"fp8_gemm_blockwise {M}x{N}x{K}", 2.0 * M * N * K, "TFLOP/s",
                    lambda: rk.fp8_gemm_blockwise(a8, a_s, b8, b_s, output_dtype=torch.bfloat16),
                    lambda: ok.fp8_gemm_blockwise(a8, a_s, b8, b_s, output_dtype=torch.bfloat16))
