@@ -1302,13 +1302,54 @@ def run_gemm(args, world, rank, local):
     return 0
 
 
+def run_tmem_probe(args, world, rank, local):
+    """TMEM -> register load throughput (fd_probe_tmem_ld): bytes per clock per SM
+    for load widths, loads per wait and warp counts, pure loads and with the FP8
+    GEMM's promotion arithmetic.  One JSON line with the table (rank 0)."""
+    from futudiffu_b200 import _lib as L
+    from futudiffu_b200 import check_status
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    nsm = torch.cuda.get_device_properties(dev).multi_processor_count
+    cycles = torch.zeros(nsm * 12, dtype=torch.int64, device=dev)
+    sink = torch.zeros(1, dtype=torch.float32, device=dev)
+    iters = 2048
+    rows = []
+    cases = [(w, l, n, 0) for (w, l) in ((16, 1), (16, 2), (16, 4), (32, 1), (32, 2), (32, 4), (64, 1), (64, 2))
+             for n in (4, 8, 12)]
+    cases += [(w, l, n, 1) for (w, l) in ((16, 1), (16, 2), (16, 4), (32, 1), (32, 2), (64, 1)) for n in (4, 8)]
+    with ClockSampler(local) as clocks:
+        for w, l, n, f in cases:
+            for rep in range(2):  # first launch warms up
+                cycles.zero_()
+                L.call("fd_probe_tmem_ld", w, l, n, f, iters, L.ptr(cycles), L.ptr(sink), L.stream_ptr(dev))
+                torch.cuda.synchronize()
+            cyc = cycles.view(nsm, 12)[:, :n].double()
+            per_sm = cyc.max(dim=1).values  # the slowest warp of each SM
+            bytes_sm = n * 32 * 128 * 4 * iters
+            rows.append({"width": w, "per_wait": l, "warps": n, "fma": bool(f),
+                         "bytes_per_clk_sm": bytes_sm / per_sm.median().item(),
+                         "cycles_per_128col_round": per_sm.median().item() / iters})
+    check_status()
+    if rank == 0:
+        best = max(rows, key=lambda r: r["bytes_per_clk_sm"])
+        print(json.dumps({"metric": "TMEM load throughput (B/clk/SM)", "value": best["bytes_per_clk_sm"],
+                          "unit": "B/clk/SM", "n_gpus": 1, "higher_is_better": True,
+                          "config": {"workload": "tmem_probe", "iters": iters,
+                                     "need": "FP8 GEMM promotion at the full MMA rate: 256 B/clk/SM"},
+                          "rows": rows, "clocks": clocks.summary()}), flush=True)
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default: 10 dit, 50 otherwise)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["dit", "video", "attention", "gemm", "packed", "block"], default="dit",
+    ap.add_argument("--workload", choices=["dit", "video", "attention", "gemm", "packed", "block", "tmem_probe"],
+                    default="dit",
                     help="dit = benchmark config 4 (headline); video = config 5 (Ulysses); "
                          "block = config 3 (one double-stream block); "
                          "attention = config 2; gemm = config 1; packed = the reference's packed "
@@ -1342,6 +1383,8 @@ def main(argv=None) -> int:
             if args.impl == "reference":
                 return run_packed_reference(args, world, rank)
             return run_packed(args, world, rank, local)
+        if args.workload == "tmem_probe":
+            return run_tmem_probe(args, world, rank, local)
         if args.impl == "reference":
             return run_reference(args, world, rank)
         if args.workload == "gemm":

@@ -59,6 +59,7 @@ _SIGS: dict[str, list] = {
     "fd_last_error": [],
     "fd_get_status": [ctypes.POINTER(ctypes.c_uint), _I],
     "fd_div_full_f32": [_P, _P, _P, _L, _P],
+    "fd_probe_tmem_ld": [_I, _I, _I, _I, _I, _P, _P, _P],
     "fd_fp8_act_quant": [_P, _I, _P, _P, _L, _L, _I, _P],
     "fd_fp8_weight_quant": [_P, _I, _P, _P, _L, _L, _I, _P],
     "fd_fp8_dequant_blockwise": [_P, _P, _P, _I, _L, _L, _I, _P],

@@ -510,6 +510,7 @@ extern "C" int fd_attn_quant(const void* q, const void* k, const void* v, int64_
                              float* workspace, void* stream) {
   FD_CHECK_ARG(BH > 0 && N > 0, "empty input");
   FD_CHECK_ARG(BH <= 65535, "BH too large");
+  FD_CHECK_ARG(N < (1ll << 30), "N too large");
   FD_CHECK_ARG(qk_kind == FD_QK_INT8 || qk_kind == FD_QK_FP8, "bad qk_kind");
   FD_CHECK_ARG((q_gran == FD_GRAN_TOKEN || q_gran == FD_GRAN_BLOCK) &&
                    (k_gran == FD_GRAN_TOKEN || k_gran == FD_GRAN_BLOCK),
@@ -560,14 +561,22 @@ extern "C" int fd_attn_quant(const void* q, const void* k, const void* v, int64_
 // paths where cudaMalloc's implicit synchronisation is not allowed.
 //
 // The host cannot use the array's name as a device address, so the address is
-// looked up once per device with cudaGetSymbolAddress, with that device
-// current, on the first call made on it; make that first call before any
-// stream capture.  The colstats launch writes every scratch element the
-// quantisation launch reads, so nothing needs clearing between calls; but all
-// calls share the one array, so calls that overlap on the GPU (different
-// streams, or different host threads, on one device) race on it.
+// looked up with cudaGetSymbolAddress, with the device current, on the first
+// call made in a CUDA context (the device's primary context, as torch and most
+// runtimes use, or a context the caller made current), and kept for that
+// context; make that first call before any stream capture.  The colstats
+// launch writes every scratch element the quantisation launch reads, so
+// nothing needs clearing between calls; but all calls in a context share the
+// one array, so calls that overlap on the GPU (different streams, or different
+// host threads, on one device) race on it.
 static std::mutex g_ws_mutex;
-static float* g_ws_addr[64] = {nullptr};
+struct WsSlot {
+  CUcontext ctx;
+  float* addr;
+};
+static WsSlot g_ws_slots[64][4] = {};  // per device: the last four contexts seen
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);  // cuCtxGetCurrent, through the runtime
+static CtxGetCurrentFn g_ctx_current = nullptr;
 
 static int noalloc_ws(float** out) {
   int dev = 0;
@@ -575,15 +584,36 @@ static int noalloc_ws(float** out) {
   if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "fd_attn_quant_noalloc: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return set_error(FD_ERR_ARG, "fd_attn_quant_noalloc: device index %d unsupported", dev);
   std::lock_guard<std::mutex> lock(g_ws_mutex);
-  if (!g_ws_addr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_attn_quant_ws);
-    if (e != cudaSuccess || p == nullptr)
-      return set_error(FD_ERR_CUDA, "fd_attn_quant_noalloc: cudaGetSymbolAddress failed: %s",
-                       cudaGetErrorString(e));
-    g_ws_addr[dev] = static_cast<float*>(p);
+  if (!g_ctx_current) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &fn, 4000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return set_error(FD_ERR_CUDA, "fd_attn_quant_noalloc: cuCtxGetCurrent unavailable");
+    g_ctx_current = reinterpret_cast<CtxGetCurrentFn>(fn);
   }
-  *out = g_ws_addr[dev];
+  CUcontext ctx = nullptr;
+  if (g_ctx_current(&ctx) != CUDA_SUCCESS)
+    return set_error(FD_ERR_CUDA, "fd_attn_quant_noalloc: cuCtxGetCurrent failed");
+  WsSlot* slots = g_ws_slots[dev];
+  for (int i = 0; ctx != nullptr && i < 4; ++i) {
+    if (slots[i].ctx == ctx && slots[i].addr) {
+      *out = slots[i].addr;
+      return FD_OK;
+    }
+  }
+  // first call in this context (with no context current yet, the runtime makes
+  // the device's primary context current here, and the launches use it too)
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_attn_quant_ws);
+  if (e != cudaSuccess || p == nullptr)
+    return set_error(FD_ERR_CUDA, "fd_attn_quant_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+  if (ctx == nullptr && (g_ctx_current(&ctx) != CUDA_SUCCESS || ctx == nullptr))
+    return set_error(FD_ERR_CUDA, "fd_attn_quant_noalloc: no current CUDA context");
+  // newest first; the oldest of four contexts is forgotten (looked up again if it returns)
+  for (int i = 3; i > 0; --i) slots[i] = slots[i - 1];
+  slots[0] = WsSlot{ctx, static_cast<float*>(p)};
+  *out = slots[0].addr;
   return FD_OK;
 }
 
@@ -595,6 +625,7 @@ extern "C" int fd_attn_quant_noalloc(const void* q, const void* k, const void* v
                                      float* q_desc, void* k_codes, float* k_desc, void* v_codes,
                                      float* v_desc, float* k_mean, void* stream) {
   FD_CHECK_ARG(BH > 0 && N > 0, "empty input");
+  FD_CHECK_ARG(BH <= 65535 && N < (1ll << 30), "BH or N too large");
   const int64_t need = fd_attn_quant_workspace_floats(BH, N);
   if (need > kNoAllocWsFloats)
     return set_error(FD_ERR_ARG,

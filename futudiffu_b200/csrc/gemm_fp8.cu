@@ -327,43 +327,68 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.f;
       const int nslices = p.kblocks + (LORA ? p.lora_slices : 0);
+      // The slice scales come from global memory; they are loaded two slices
+      // ahead so that no load latency sits between "slice ready" and the
+      // release of its TMEM buffer (the MMA issuer waits on that release).
+      // LoRA slices (the bf16 operands carry their scales) and rows past M use
+      // a_s = 1 / 0 as before; columns past the end of B read the last block's
+      // scale (they are never stored).
+      const int blo = min(n_lo / 128, p.nbs - 1), bhi = min(n_hi / 128, p.nbs - 1);
+      auto load_scales = [&](int kb, float& as, float& bl, float& bh) {
+        as = 1.0f;
+        bl = 1.0f;
+        bh = 1.0f;
+        if (kb >= p.kblocks) return;
+        if (BMODE == 1) {
+          bl = __ldg(p.b_s + (int64_t)kb * p.nbs + blo);
+          bh = __ldg(p.b_s + (int64_t)kb * p.nbs + bhi);
+        } else if (BMODE == 0) {
+          bl = __ldg(p.b_s + (int64_t)blo * p.kblocks + kb);
+          bh = __ldg(p.b_s + (int64_t)bhi * p.kblocks + kb);
+        }
+        as = row_ok ? __ldg(as_row + kb) : 0.f;
+      };
+      float as0, bl0, bh0, as1, bl1, bh1;
+      load_scales(0, as0, bl0, bh0);
+      load_scales(1, as1, bl1, bh1);
       for (int kb = 0; kb < nslices; ++kb, ++it) {
         const uint32_t tb = it % NTBUF, tph = (it / NTBUF) & 1;
-        const bool lora = LORA && kb >= p.kblocks;  // LoRA slices: the bf16 operands carry their scales
-        float sc_lo = 1.0f, sc_hi = 1.0f;
-        if (!lora) {
-          // (columns past the end of B read the last block's scale; they are never stored)
-          const int blo = min(n_lo / 128, p.nbs - 1), bhi = min(n_hi / 128, p.nbs - 1);
-          float bs_lo = 1.0f, bs_hi = 1.0f;
-          if (BMODE == 1) {
-            bs_lo = __ldg(p.b_s + (int64_t)kb * p.nbs + blo);
-            bs_hi = __ldg(p.b_s + (int64_t)kb * p.nbs + bhi);
-          } else if (BMODE == 0) {
-            bs_lo = __ldg(p.b_s + (int64_t)blo * p.kblocks + kb);
-            bs_hi = __ldg(p.b_s + (int64_t)bhi * p.kblocks + kb);
-          }
-          const float as = row_ok ? __ldg(as_row + kb) : 0.f;
-          sc_lo = as * bs_lo;
-          sc_hi = as * bs_hi;
-        }
+        float as2, bl2, bh2;
+        load_scales(kb + 2, as2, bl2, bh2);
+        // acc += partial * (a_s * b_s): the reference's (dot * a_s) * b_s rounded
+        // as one product of the two scales, as before
+        const float sc_lo = as0 * bl0, sc_hi = as0 * bh0;
+        as0 = as1; bl0 = bl1; bh0 = bh1;
+        as1 = as2; bl1 = bl2; bh1 = bh2;
         ok = ok && mbar_wait(&tfull[tb], tph, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) continue;
         tc_fence_after();
         const uint32_t taddr = tmem_base + lane_base + tb * BN;
+        // chunk c + 1 is loaded before chunk c is accumulated; the buffer is
+        // released as soon as the last chunk is in registers
+        uint32_t r0[16], r1[16];
+        tmem_ld16(taddr + col_lo, r0);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          uint32_t r0[16];
-          tmem_ld16(taddr + (c < 4 ? col_lo : col_hi) + (c & 3) * 16, r0);
+          uint32_t(&cur)[16] = (c & 1) ? r1 : r0;
+          uint32_t(&nxt)[16] = (c & 1) ? r0 : r1;
           tmem_wait_ld();
-          if (c == 7) {
+          if (c < 7) {
+            tmem_ld16(taddr + (c + 1 < 4 ? col_lo : col_hi) + ((c + 1) & 3) * 16, nxt);
+          } else {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[tb]);
           }
           const float sc = c < 4 ? sc_lo : sc_hi;
+          const uint64_t sc2 = pk(sc, sc);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) acc[16 * c + i] = fmaf(__uint_as_float(r0[i]), sc, acc[16 * c + i]);
+          for (int i = 0; i < 16; i += 2) {
+            uint64_t a2 = pk(acc[16 * c + i], acc[16 * c + i + 1]);
+            a2 = fma2(pk(__uint_as_float(cur[i]), __uint_as_float(cur[i + 1])), sc2, a2);
+            unpk(a2, acc[16 * c + i], acc[16 * c + i + 1]);
+          }
         }
       }
       if (BMODE == 2) {

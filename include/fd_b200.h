@@ -68,6 +68,17 @@ int fd_get_status(unsigned int* out, int clear);
  * Parity tests evaluate the CPU oracle's scale arithmetic with it. */
 int fd_div_full_f32(const float* a, const float* b, float* out, int64_t n, void* stream);
 
+/* TMEM load-throughput microbenchmark (no counterpart in the reference): one CTA
+ * per SM allocates the 512 TMEM columns; `warps` warps read them with tcgen05.ld
+ * 32x32b loads of `width` (16 / 32 / 64) columns, `per_wait` loads per
+ * tcgen05.wait::ld, `iters` rounds of 128 columns per warp; with `fma` != 0 every
+ * loaded value is accumulated as the FP8 GEMM's per-slice promotion does.
+ * cycles (num_SMs x 12) int64: each warp's clock64 duration (unused slots are not
+ * written).  Measures the bound of the GEMM's promotion (bench.py --workload
+ * tmem_probe). */
+int fd_probe_tmem_ld(int width, int per_wait, int warps, int fma, int iters, long long* cycles, float* sink,
+                     void* stream);
+
 /* G1 -- fp8_act_quant (src/futudiffu/fp8_kernels.py:54-90).
  * x (M, K) in x_dtype (bf16/f16/f32), K % block == 0, block == 128.
  * y (M, K) e4m3; s (M, K/block) f32 with s = max(amax/448, 1e-12),
@@ -291,10 +302,11 @@ int fd_attn_quant_kv(const void* k, const void* v, int64_t BH, int64_t N, int sm
  * device memory (hosts that pass only their planned input/output buffers, or
  * paths where cudaMalloc's synchronisation is not allowed).  Rejects shapes
  * whose scratch, 2 * BH * ceil(N/256) * 128 floats, exceeds the array
- * (FD_ERR_ARG).  The first call on a device looks up the array's device
- * address; make it before any stream capture.  Calls share the array: calls
- * that overlap on one GPU race.  fd_attn_quant_noalloc_max_floats() returns
- * the array size. */
+ * (FD_ERR_ARG), as it rejects N >= 2^30 or BH > 65535.  The first call in a
+ * CUDA context (the device's primary context, or one the caller made current)
+ * looks up the array's device address for that context; make it before any
+ * stream capture.  Calls share the array: calls that overlap on one GPU race.
+ * fd_attn_quant_noalloc_max_floats() returns the array size. */
 #define FD_NOALLOC_WS_FLOATS 1048576
 int64_t fd_attn_quant_noalloc_max_floats(void);
 int fd_attn_quant_noalloc(const void* q, const void* k, const void* v, int64_t BH, int64_t N,

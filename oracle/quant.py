@@ -31,11 +31,12 @@ def div_ieee(a, b) -> torch.Tensor:
 
 
 # The reference computes its quantisation scales in Triton, whose f32 `/`
-# compiles to the GPU's div.full.f32 (within 2 ulp of the correctly rounded
-# quotient; its exact results are a property of the hardware).  On the CPU the
-# oracle uses the correctly rounded quotient; parity tests on the GPU bind this
-# to the device's instruction (``division(futudiffu_b200._lib.device_divide)``)
-# so scale arithmetic is reproduced bit for bit.
+# compiles to a GPU divide instruction that is within 2 ulp of the correctly
+# rounded quotient (its exact results are a property of the hardware).  On the
+# CPU the oracle uses the correctly rounded quotient; parity tests on the GPU
+# evaluate the quotients with a Triton kernel (``division(tests.helpers.
+# triton_divide)``), i.e. the reference's own compiler path, so the scale
+# arithmetic is reproduced bit for bit without using the library under test.
 _TRITON_DIV = div_ieee
 
 

@@ -17,11 +17,11 @@ pytestmark = pytest.mark.gpu
 
 @pytest.fixture(autouse=True)
 def _triton_division():
-    """Evaluate the oracle's Triton-kernel quotients with the device's div.full.f32."""
-    from futudiffu_b200._lib import device_divide
+    """Evaluate the oracle's Triton-kernel quotients with Triton's own fp32 divide on the GPU."""
     from oracle import quant as _OQ
+    from tests.helpers import triton_divide
 
-    with _OQ.division(device_divide):
+    with _OQ.division(triton_divide):
         yield
 
 SM = 1.0 / math.sqrt(128)

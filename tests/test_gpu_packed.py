@@ -17,10 +17,10 @@ pytestmark = pytest.mark.gpu
 
 @pytest.fixture(autouse=True)
 def _triton_division():
-    from futudiffu_b200._lib import device_divide
     from oracle import quant as _OQ
+    from tests.helpers import triton_divide
 
-    with _OQ.division(device_divide):
+    with _OQ.division(triton_divide):
         yield
 
 

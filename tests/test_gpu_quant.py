@@ -14,11 +14,11 @@ pytestmark = pytest.mark.gpu
 
 @pytest.fixture(autouse=True)
 def _triton_division():
-    """Evaluate the oracle's Triton-kernel quotients with the device's div.full.f32."""
-    from futudiffu_b200._lib import device_divide
+    """Evaluate the oracle's Triton-kernel quotients with Triton's own fp32 divide on the GPU."""
     from oracle import quant as _OQ
+    from tests.helpers import triton_divide
 
-    with _OQ.division(device_divide):
+    with _OQ.division(triton_divide):
         yield
 
 
@@ -167,3 +167,16 @@ def test_device_divide_within_two_ulp_of_ieee(cuda_device):
     ulp = (got.view(torch.int32) - ref.view(torch.int32)).abs()
     assert ulp.max().item() <= 2
     assert (device_divide(torch.tensor([448.0]), torch.tensor([448.0])) == 1.0).all()
+
+
+def test_device_divide_equals_triton_divide(cuda_device):
+    """The library's f32 divide gives Triton's quotient bit for bit (the quantisers
+    use it for every scale; the reference's kernels use Triton's `/`)."""
+    from futudiffu_b200._lib import device_divide
+    from tests.helpers import triton_divide
+
+    g = gen(124)
+    a = torch.cat([torch.rand(1 << 20, generator=g) * 500, torch.full((4,), 448.0), torch.full((4,), 127.0)])
+    b = torch.cat([torch.rand(1 << 20, generator=g) * 20 + 1e-6, torch.tensor([448.0, 3.0, 1e-12, 7.0]),
+                   torch.tensor([127.0, 3.0, 1e-12, 0.1])])
+    assert torch.equal(device_divide(a, b).view(torch.int32), triton_divide(a, b).view(torch.int32))

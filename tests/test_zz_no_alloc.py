@@ -30,13 +30,14 @@ def _inputs(BH, N, seed):
     return q, k, v
 
 
-def _outputs(BH, N, gran):
+def _outputs(BH, N, gran, qk=0, pv=1):
     from futudiffu_b200.sage_attention import _desc_stride
 
     dev = "cuda"
+    code_dt = torch.int8 if qk == 0 else torch.float8_e4m3fn
     return {
-        "q_codes": torch.empty(BH, N, 128, dtype=torch.int8, device=dev),
-        "k_codes": torch.empty(BH, N, 128, dtype=torch.int8, device=dev),
+        "q_codes": torch.empty(BH, N, 128, dtype=code_dt, device=dev),
+        "k_codes": torch.empty(BH, N, 128, dtype=code_dt, device=dev),
         "q_desc": torch.empty(BH, _desc_stride(N, gran, 128), device=dev),
         "k_desc": torch.empty(BH, _desc_stride(N, gran, 64), device=dev),
         "v_codes": torch.empty(BH, N, 128, dtype=torch.float8_e4m3fn, device=dev),
@@ -45,12 +46,13 @@ def _outputs(BH, N, gran):
     }
 
 
-def _run(lib, name, q, k, v, BH, N, gran, out, ws=None):
+def _run(lib, name, q, k, v, BH, N, gran, out, ws=None, smooth=1, qk=0, pv=1):
     from futudiffu_b200 import _lib as L
 
-    args = [L.ptr(q), L.ptr(k), L.ptr(v), BH, N, 1, L.QK_INT8, gran, gran, L.PV_FP8, ctypes.c_float(SL2E),
+    fp8v = pv == L.PV_FP8
+    args = [L.ptr(q), L.ptr(k), L.ptr(v), BH, N, smooth, qk, gran, gran, pv, ctypes.c_float(SL2E),
             L.ptr(out["q_codes"]), L.ptr(out["q_desc"]), L.ptr(out["k_codes"]), L.ptr(out["k_desc"]),
-            L.ptr(out["v_codes"]), L.ptr(out["v_desc"]), L.ptr(out["k_mean"])]
+            L.ptr(out["v_codes"]) if fp8v else None, L.ptr(out["v_desc"]) if fp8v else None, L.ptr(out["k_mean"])]
     if ws is not None:
         args.append(L.ptr(ws))
     args.append(L.stream_ptr())
@@ -58,29 +60,40 @@ def _run(lib, name, q, k, v, BH, N, gran, out, ws=None):
     assert rc == L.FD_OK, lib.fd_last_error()
 
 
-def _same(a, b):
-    for key in a:
+def _same(a, b, keys):
+    for key in keys:
         x, y = a[key], b[key]
         if x.dtype == torch.float8_e4m3fn:
             x, y = x.view(torch.uint8), y.view(torch.uint8)
         assert torch.equal(x, y), key
 
 
-@pytest.mark.parametrize("gran", [0, 1])
-def test_noalloc_matches_allocating_entry_point(gran):
+# (granularity, smooth_k, qk kind, pv kind, N): both granularities with INT8 / FP8
+# Q/K codes and e4m3 or bf16 V, smoothing on and off, and a ragged N below one
+# 256-row scratch chunk
+CASES = [(0, 1, 0, 1, 1500), (1, 1, 0, 1, 1500), (0, 1, 1, 1, 1500), (1, 0, 0, 0, 1500), (0, 0, 1, 0, 1500),
+         (1, 1, 1, 0, 100), (0, 1, 0, 1, 100)]
+
+
+@pytest.mark.parametrize("gran,smooth,qk,pv,N", CASES)
+def test_noalloc_matches_allocating_entry_point(gran, smooth, qk, pv, N):
+    """Two calls in a row with different inputs: the second call's results cannot
+    come from scratch that the first call left behind."""
     from futudiffu_b200 import _lib as L
 
     lib = L.load()
-    BH, N = 6, 1500
-    for call, seed in enumerate((1, 2)):
-        q, k, v = _inputs(BH, N, seed)
-        ref = _outputs(BH, N, gran)
+    BH = 6
+    keys = ["q_codes", "q_desc", "k_codes", "k_desc"] + (["v_codes", "v_desc"] if pv == L.PV_FP8 else [])
+    keys += ["k_mean"] if smooth else []
+    for seed in (1, 2):
+        q, k, v = _inputs(BH, N, seed + 10 * N)
+        ref = _outputs(BH, N, gran, qk, pv)
         ws = torch.empty(int(lib.fd_attn_quant_workspace_floats(BH, N)), device="cuda")
-        _run(lib, "fd_attn_quant", q, k, v, BH, N, gran, ref, ws)
-        got = _outputs(BH, N, gran)
-        _run(lib, "fd_attn_quant_noalloc", q, k, v, BH, N, gran, got)
+        _run(lib, "fd_attn_quant", q, k, v, BH, N, gran, ref, ws, smooth, qk, pv)
+        got = _outputs(BH, N, gran, qk, pv)
+        _run(lib, "fd_attn_quant_noalloc", q, k, v, BH, N, gran, got, None, smooth, qk, pv)
         torch.cuda.synchronize()
-        _same(got, ref)
+        _same(got, ref, keys)
     L.check_status()
 
 
@@ -96,3 +109,8 @@ def test_noalloc_rejects_oversized_scratch():
                                    None, None, None, None, None, None, None, None)
     assert rc == L.FD_ERR_ARG
     assert b"maximum" in lib.fd_last_error()
+    # an N so large that the scratch size would wrap is rejected before it is computed
+    rc = lib.fd_attn_quant_noalloc(None, None, None, 1, 1 << 62, 1, 0, 0, 0, 1, ctypes.c_float(1.0),
+                                   None, None, None, None, None, None, None, None)
+    assert rc == L.FD_ERR_ARG
+    assert b"too large" in lib.fd_last_error()
