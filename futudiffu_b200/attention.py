@@ -81,29 +81,40 @@ def sdpa_attention(
 
 
 def rope_embed(pos: Tensor, dim: int, theta: float) -> Tensor:
-    """Flux/Lumina RoPE rotation matrices (..., n, dim/2, 2, 2) float32 (reference :124-136)."""
+    """RoPE rotations (Flux / Lumina form) for positions ``pos`` (..., n).
+
+    Channel pair i < dim / 2 turns by the angle a = pos * theta^(-2 i / dim); the
+    result holds the 2 x 2 rotation [[cos a, -sin a], [sin a, cos a]] per pair,
+    shape (..., n, dim / 2, 2, 2), float32.  The frequencies and angles are
+    evaluated in float64 and rounded once (reference src/futudiffu/attention.py:124-136;
+    the fused QKV post-process consumes this layout)."""
     assert dim % 2 == 0
-    device = pos.device
-    scale = torch.linspace(0, (dim - 2) / dim, steps=dim // 2, dtype=torch.float64, device=device)
-    omega = 1.0 / (theta ** scale)
-    out = torch.einsum("...n,d->...nd", pos.to(dtype=torch.float32, device=device), omega)
-    out = torch.stack([torch.cos(out), -torch.sin(out), torch.sin(out), torch.cos(out)], dim=-1)
-    out = out.reshape(*out.shape[:-1], 2, 2)
-    return out.to(dtype=torch.float32, device=device)
+    half = dim // 2
+    # exponents 2 i / dim, i = 0 .. half - 1, as evenly spaced float64 values
+    expo = torch.linspace(0.0, (dim - 2) / dim, steps=half, dtype=torch.float64, device=pos.device)
+    inv_freq = 1.0 / (theta ** expo)
+    ang = pos.to(torch.float32).to(torch.float64).unsqueeze(-1) * inv_freq
+    cos, sin = torch.cos(ang), torch.sin(ang)
+    rot = torch.stack((torch.stack((cos, -sin), dim=-1), torch.stack((sin, cos), dim=-1)), dim=-2)
+    return rot.to(torch.float32)
 
 
 def apply_rope_flux(xq: Tensor, xk: Tensor, freqs_cis: Tensor) -> tuple[Tensor, Tensor]:
+    """Rotate the channel pairs of Q and K by ``freqs_cis`` (rope_embed's layout)."""
     return _apply_rope1_flux(xq, freqs_cis), _apply_rope1_flux(xk, freqs_cis)
 
 
 def _apply_rope1_flux(x: Tensor, freqs_cis: Tensor) -> Tensor:
-    x_ = x.to(dtype=freqs_cis.dtype).reshape(*x.shape[:-1], -1, 1, 2)
-    x_out = freqs_cis[..., 0] * x_[..., 0]
-    x_out.addcmul_(freqs_cis[..., 1], x_[..., 1])
-    return x_out.reshape(*x.shape).type_as(x)
+    """(x_2i, x_2i+1) -> R_i (x_2i, x_2i+1) in freqs_cis' dtype, returned in x's dtype:
+    out = R[:, 0] x_2i + R[:, 1] x_2i+1 (each output channel a row of R)."""
+    pairs = x.to(freqs_cis.dtype).unflatten(-1, (-1, 1, 2))
+    out = torch.addcmul(freqs_cis[..., 0] * pairs[..., 0], freqs_cis[..., 1], pairs[..., 1])
+    return out.reshape(x.shape).type_as(x)
 
 
 def rms_norm(x: Tensor, weight: Tensor | None = None, eps: float = 1e-6) -> Tensor:
-    if weight is None:
-        return torch.nn.functional.rms_norm(x, (x.shape[-1],), eps=eps)
-    return torch.nn.functional.rms_norm(x, weight.shape, weight=weight.to(dtype=x.dtype, device=x.device), eps=eps)
+    """x / sqrt(mean(x^2) + eps) over the last dimension, times ``weight`` (cast to
+    x's dtype) when given: torch's fused RMSNorm."""
+    shape = (x.shape[-1],) if weight is None else tuple(weight.shape)
+    w = None if weight is None else weight.to(dtype=x.dtype, device=x.device)
+    return F.rms_norm(x, shape, weight=w, eps=eps)

@@ -39,12 +39,6 @@ NVCC_FLAGS = [
 ]
 
 
-# Per-file extra flags.  gelu_erf.cu: the reference's Triton kernels use
-# libdevice's flush-to-zero variants (erff among them); -ftz=true selects the
-# same variants, so fp8_gelu's codes and scales equal the reference's.
-FILE_FLAGS = {"gelu_erf.cu": ["-ftz=true"]}
-
-
 def nvcc() -> str:
     cand = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
     if not os.path.exists(cand):
@@ -65,7 +59,7 @@ def _compile(src: Path, verbose: bool, force: bool, hmtime: float) -> Path:
     obj = BUILD / (src.stem + ".o")
     if not force and obj.exists() and obj.stat().st_mtime >= max(src.stat().st_mtime, hmtime):
         return obj
-    cmd = [nvcc(), *ARCH, *NVCC_FLAGS, *FILE_FLAGS.get(src.name, []), "-c", str(src), "-o", str(obj)]
+    cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), flush=True)

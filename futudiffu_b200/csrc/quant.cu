@@ -1,6 +1,5 @@
 // Memory-bound FP8 quantisers: activation quant (1 x 128), weight quant
-// (128 x 128), blockwise dequant, SiLU-gate requant, GELU-tanh quant (the erf
-// GELU requantiser is in gelu_erf.cu).
+// (128 x 128), blockwise dequant, SiLU-gate requant, GELU requant.
 //
 // All of them move 16-byte vectors per thread and reduce each 128-element
 // group inside 16 consecutive lanes, so one warp covers two groups per
@@ -206,6 +205,34 @@ __global__ void __launch_bounds__(256) gelu_tanh_quant_kernel(const __nv_bfloat1
   }
 }
 
+// fp8_gelu_kernel, src/futudiffu/fp8_kernels.py:720-786 (erf GELU).
+__global__ void __launch_bounds__(256) gelu_requant_kernel(const uint8_t* __restrict__ x,
+                                                          const float* __restrict__ sx,
+                                                          uint8_t* __restrict__ y,
+                                                          float* __restrict__ sy,
+                                                          int64_t ngroups) {
+  const int64_t half_warps = (int64_t)gridDim.x * (blockDim.x >> 4);
+  const int sub = threadIdx.x & 15;
+  for (int64_t g = (int64_t)blockIdx.x * (blockDim.x >> 4) + (threadIdx.x >> 4); g < ngroups;
+       g += half_warps) {
+    const uint2 c = *reinterpret_cast<const uint2*>(x + g * 128 + sub * 8);
+    const uint32_t cw[2] = {c.x, c.y};
+    const float sc = sx[g];
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      __nv_fp8_e4m3 q;
+      q.__x = (cw[j / 4] >> ((j % 4) * 8)) & 0xFF;
+      const float a = float(q) * sc;
+      v[j] = a * 0.5f * (1.0f + erff(div_full(a, 1.41421356237f)));
+    }
+    const float amax = half_warp_max(amax8(v));
+    const float qm = quant_mult(amax);
+    *reinterpret_cast<uint2*>(y + g * 128 + sub * 8) = quant8(v, qm);
+    if (sub == 0) sy[g] = dequant_scale(amax);
+  }
+}
+
 }  // namespace fd
 
 using namespace fd;
@@ -322,3 +349,15 @@ extern "C" int fd_fp8_gelu_tanh_quant(const void* x, void* y, float* s, int64_t 
   return check_launch("gelu_tanh_quant");
 }
 
+extern "C" int fd_fp8_gelu_requant(const void* x, const float* sx, void* y, float* sy, int64_t M,
+                                   int64_t N, int block, void* stream) {
+  FD_CHECK_ARG(block == 128, "block_size must be 128");
+  FD_CHECK_ARG(M >= 0 && N > 0 && N % 128 == 0, "N must be a positive multiple of 128");
+  if (M == 0) return FD_OK;
+  FD_CHECK_ARG(x && sx && y && sy, "null pointer");
+  FD_CHECK_ARG(aligned8(x) && aligned8(y), "x and y must be 8-byte aligned");
+  const int64_t ng = M * (N / 128);
+  gelu_requant_kernel<<<grid_for(ng, 16), 256, 0, (cudaStream_t)stream>>>(
+      (const uint8_t*)x, sx, (uint8_t*)y, sy, ng);
+  return check_launch("gelu_requant");
+}

@@ -3,6 +3,8 @@ no-CPU-fallback guarantee, fake-tensor shapes of the custom ops (CPU only)."""
 
 from __future__ import annotations
 
+from pathlib import Path
+
 import pytest
 import torch
 
@@ -156,3 +158,19 @@ def test_lora_operand_padding():
     h, b, kp = lora_operands(torch.ones(3, 40), torch.ones(5, 40))
     assert kp == 64 and h.shape == (3, 64) and b.shape == (5, 64)
     assert h[:, 40:].abs().sum() == 0
+
+
+def test_rope_embed_equals_reference_fixture():
+    """rope_embed reproduces the reference's own rotations bit for bit
+    (tests/golden/fused_norms.pt: reference attention.rope_embed on Z-Image axes)."""
+    from futudiffu_b200.attention import rope_embed
+
+    d = torch.load(Path(__file__).parent / "golden" / "fused_norms.pt", weights_only=False)
+    B, S, hd = d["x"].shape[0], d["x"].shape[1], d["hd"]
+    pos = torch.zeros(S, 3)
+    pos[:, 0] = 1.0
+    pos[:, 1] = (torch.arange(S) % 7).float()
+    pos[:, 2] = (torch.arange(S) // 7).float()
+    freqs = torch.cat([rope_embed(pos[None, :, i], dd, 256.0) for i, dd in enumerate((32, 48, 48))], dim=-3)
+    freqs = freqs.expand(B, S, hd // 2, 2, 2).unsqueeze(2).contiguous()
+    assert torch.equal(freqs, d["freqs"])
