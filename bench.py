@@ -705,6 +705,10 @@ def run_dit(args, world, rank, local):
     check_status()
 
     subs = sub_entries(dev, world, local) if not args.no_sub else {}
+    if world >= 2 and not args.no_sub:
+        del graph
+        torch.cuda.empty_cache()
+        subs["video_config5"] = video_sub_entry(dev, world, rank, local)
     check_status()
 
     if rank == 0:
@@ -989,6 +993,51 @@ def run_video_reference(args, world, rank):
         "e2e": {"value": val, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
     return 0
+
+
+def video_sub_entry(dev, world: int, rank: int, local: int, steps: int = 3, warmup: int = 2) -> dict:
+    """Config 5 inside the default line at N >= 2 GPUs: one denoise step of the
+    14B-class video DiT with Ulysses sequence parallelism over all ranks (NCCL
+    all-to-all around every self-attention), device-timed, max over ranks."""
+    from futudiffu_b200 import check_status
+    from futudiffu_b200.dit import VideoDiT, VideoDiTConfig, sigmas, video_flops_per_step
+
+    cfg = VideoDiTConfig()
+    model = VideoDiT(cfg, seed=0, device=dev, group=None)
+    Ls = model.local_tokens
+    g = torch.Generator().manual_seed(200)
+    lat = torch.randn(1, cfg.tokens, cfg.patch_dim, generator=g).to(torch.bfloat16)
+    txt = torch.randn(1, cfg.txt_tokens, cfg.hidden, generator=g).to(torch.bfloat16).to(dev)
+    x = lat[:, rank * Ls:(rank + 1) * Ls].contiguous().to(dev)
+    sig = sigmas(28)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i, x):
+        t = torch.full((1,), sig[i % 28], device=dev)
+        v = model(x, txt, t)
+        return (x.float() + (sig[i % 28 + 1] - sig[i % 28]) * v.float()).to(x.dtype)
+
+    for i in range(warmup):
+        x = step(i, x)
+    torch.cuda.synchronize()
+    barrier(world)
+    with ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else local) as clocks:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            x = step(i, x)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world, dev)
+    check_status()
+    del model
+    torch.cuda.empty_cache()
+    fl = video_flops_per_step(cfg)
+    return {"metric": VIDEO_METRIC, "value": 1e3 / ms, "unit": "steps/s", "ms": ms, "steps": steps, "warmup": warmup,
+            "parallelism": f"Ulysses sequence parallel x{world} (NCCL all_to_all_single around each self-attention)",
+            "model_tflops": fl / (ms * 1e-3) / 1e12, "tokens": cfg.tokens, "blocks": cfg.n_blocks,
+            "clocks": clocks.summary()}
 
 
 def run_video(args, world, rank, local):
