@@ -37,7 +37,7 @@ class GemmProblem(ctypes.Structure):
                 ("M", ctypes.c_int64), ("N", ctypes.c_int64), ("K", ctypes.c_int64)]
 QK_INT8, QK_FP8 = 0, 1
 GRAN_TOKEN, GRAN_BLOCK = 0, 1
-PV_BF16, PV_FP8 = 0, 1
+PV_BF16, PV_FP8, PV_FP8_TILE = 0, 1, 2
 ACT_NONE, ACT_GELU_TANH, ACT_SILU_GATE = 0, 1, 2
 
 _DT_CODE = {
@@ -60,6 +60,7 @@ _SIGS: dict[str, list] = {
     "fd_get_status": [ctypes.POINTER(ctypes.c_uint), _I],
     "fd_div_full_f32": [_P, _P, _P, _L, _P],
     "fd_probe_tmem_ld": [_I, _I, _I, _I, _I, _P, _P, _P],
+    "fd_attn_quant_v_tile": [_P, _L, _L, _P, _P, _P],
     "fd_fp8_act_quant": [_P, _I, _P, _P, _L, _L, _I, _P],
     "fd_fp8_weight_quant": [_P, _I, _P, _P, _L, _L, _I, _P],
     "fd_fp8_dequant_blockwise": [_P, _P, _P, _I, _L, _L, _I, _P],

@@ -40,7 +40,7 @@ constexpr int BKV = 128;  // keys per KV tile
 constexpr int HD = 128;
 // K and V pipeline stages: 2 with e4m3 V (16 KiB per V tile); 1 with bf16 V
 // (32 KiB) so that two CTAs still fit on one SM.
-constexpr int kv_stages(int pv) { return pv == FD_PV_FP8 ? 2 : 1; }
+constexpr int kv_stages(int pv) { return pv == FD_PV_BF16 ? 1 : 2; }
 // Per-token K scale slots: tile i uses slot i % (stages + 2).  The K stage of tile
 // i is free once QK^T(i - stages) is done, which was issued after the softmax of
 // tile i - stages - 1 released S, i.e. after the softmax of tile i - stages - 2
@@ -82,21 +82,26 @@ FD_DEV float max_reduce64(const float* x) {
 
 template <int PV>
 struct Smem {
+  static constexpr bool PT = PV == FD_PV_FP8_TILE;
   static constexpr int KST = kv_stages(PV);
   static constexpr int KDS = kd_slots(PV);
   static constexpr uint32_t Q_BYTES = BQ * HD;                           // int8/e4m3 codes
   static constexpr uint32_t K_BYTES = BKV * HD;
-  static constexpr uint32_t V_BYTES = BKV * HD * (PV == FD_PV_FP8 ? 1 : 2);
-  static constexpr uint32_t P_BYTES = BQ * BKV * (PV == FD_PV_FP8 ? 1 : 2);
+  static constexpr uint32_t V_BYTES = BKV * HD * (PV == FD_PV_BF16 ? 2 : 1);
+  static constexpr uint32_t P_BYTES = BQ * BKV * (PV == FD_PV_BF16 ? 2 : 1);
   static constexpr uint32_t OFF_Q = 0;
   static constexpr uint32_t OFF_K = OFF_Q + Q_BYTES;
   static constexpr uint32_t OFF_V = OFF_K + KST * K_BYTES;
   static constexpr uint32_t OFF_P = OFF_V + KST * V_BYTES;
   static constexpr uint32_t OFF_KD = OFF_P + P_BYTES;                    // KDS x 128 f32 (per-token K)
   static constexpr uint32_t OFF_VD = OFF_KD + KDS * 512;                 // 128 f32
-  static constexpr uint32_t OFF_RED = OFF_VD + 512;                      // row max / sum exchange
+  static constexpr uint32_t OFF_VDT = OFF_VD + 512;                      // PT: KST x [2][128] f32 tile V scales
+  static constexpr uint32_t OFF_PX = OFF_VDT + (PT ? KST * 1024 : 0);    // PT: [2][2][128] f32 P descale / sum
+  static constexpr uint32_t OFF_RED = OFF_PX + (PT ? 2048 : 0);          // row max / sum exchange
   static constexpr uint32_t OFF_BAR = OFF_RED + (2 * 2 * 128 + 2 * 128) * 4;
-  static constexpr uint32_t TOTAL = OFF_BAR + 256 + 1024;               // + barriers, align slack
+  static constexpr uint32_t RAW = OFF_BAR + 256 + 1024;                 // + barriers, align slack
+  // PT: one CTA per SM (its 512 TMEM columns are the whole TMEM)
+  static constexpr uint32_t TOTAL = PT && RAW < 120 * 1024 ? 120 * 1024 : RAW;
 };
 
 struct Params {
@@ -273,13 +278,62 @@ FD_DEV float chunk_exp_store(const uint32_t (&r)[32], int col0, int N, bool half
   }
 }
 
-// QK: FD_QK_INT8 / FD_QK_FP8; KG: k granularity; PV: FD_PV_BF16 / FD_PV_FP8
+// PT mode: chunk_max over 32 keys (the scores as in chunk_max)
+template <int QK, int KG, bool FULL>
+FD_DEV float chunk_max32(const uint32_t (&r)[32], int col0, int N, bool half_ok, const float* kd) {
+  float m = -INFINITY;
+#pragma unroll
+  for (int e = 0; e < 32; e += 2) {
+    float x0 = __uint_as_float(r[e]), x1 = __uint_as_float(r[e + 1]);
+    if (KG == FD_GRAN_TOKEN) {
+      uint64_t v = pk(x0, x1);
+      if (QK == FD_QK_INT8) v = add2(v, pk(-S_BIAS, -S_BIAS));
+      unpk(mul2(v, pk(kd[e], kd[e + 1])), x0, x1);
+    }
+    if (!FULL) {
+      if (!(half_ok && col0 + e < N)) x0 = -INFINITY;
+      if (!(half_ok && col0 + e + 1 < N)) x1 = -INFINITY;
+    }
+    m = max3(m, x0, x1);
+  }
+  return m;
+}
+
+// PT mode: p = exp2(L + nb) of one 32-key chunk into p[32] (the arithmetic of
+// chunk_exp_store, without the store); keys out of range give 0.
+template <int QK, int KG, bool FULL>
+FD_DEV void chunk_p(const uint32_t (&r)[32], int col0, int N, bool half_ok, float qd, const float* kd, float c,
+                    float nb, float (&pout)[32]) {
+#pragma unroll
+  for (int e = 0; e < 32; e += 2) {
+    uint64_t v = pk(__uint_as_float(r[e]), __uint_as_float(r[e + 1]));
+    if (KG == FD_GRAN_BLOCK) {
+      v = fma2(v, pk(c, c), pk(nb, nb));
+    } else if (QK == FD_QK_INT8) {
+      const float nbq = -S_BIAS * qd;
+      v = fma2(fma2(v, pk(qd, qd), pk(nbq, nbq)), pk(kd[e], kd[e + 1]), pk(nb, nb));
+    } else {
+      v = fma2(mul2(v, pk(qd, qd)), pk(kd[e], kd[e + 1]), pk(nb, nb));
+    }
+    float a0, a1;
+    unpk(v, a0, a1);
+    if (!FULL) {
+      if (!(half_ok && col0 + e < N)) a0 = -INFINITY;
+      if (!(half_ok && col0 + e + 1 < N)) a1 = -INFINITY;
+    }
+    pout[e] = ex2_approx(a0);
+    pout[e + 1] = ex2_approx(a1);
+  }
+}
+
+// QK: FD_QK_INT8 / FD_QK_FP8; KG: k granularity; PV: FD_PV_BF16 / FD_PV_FP8 / FD_PV_FP8_TILE
 template <int QK, int KG, int PV>
-__global__ void __launch_bounds__(NUM_THREADS, 2)
+__global__ void __launch_bounds__(NUM_THREADS, PV == FD_PV_FP8_TILE ? 1 : 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const Params p) {
   using SM = Smem<PV>;
   constexpr int KST = SM::KST, KDS = SM::KDS;
+  constexpr uint32_t TMEM_COLS = PV == FD_PV_FP8_TILE ? 512 : 256;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + SM::OFF_Q;
@@ -314,7 +368,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       mbar_init(&bKfull[s], 1);
       mbar_init(&bVfull[s], 1);
       mbar_init(&bKempty[s], 1);
-      mbar_init(&bVempty[s], 1);
+      // PT: the V stage (codes and tile scales) is released by the softmax warps
+      // after they have promoted its PV; otherwise by the PV MMAs' commit
+      mbar_init(&bVempty[s], PV == FD_PV_FP8_TILE ? NUM_SOFTMAX_WARPS : 1);
     }
     for (int s = 0; s < KDS; ++s) mbar_init(&bKdfull[s], 1);
     mbar_init(bSfull, 1);
@@ -326,14 +382,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     fence_barrier_init();
   }
   if (warp == WARP_MMA) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // TMEM: S at [0, 128); O at [128, 256), or (PT) the two 64-key halves' PV
+  // products at [128, 256) and [256, 384) (O then lives in registers)
   const uint32_t tS = tmem_base, tO = tmem_base + 128;
+  const uint32_t tPV1 = tmem_base + 256;
 
   if (warp == WARP_TMA) {
     // ================================================================ producer
@@ -360,10 +419,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         ++i;
         issued = i;
         if (!mbar_wait(&bVempty[s], (use & 1) ^ 1, abort_flag)) break;
-        mbar_arrive_expect_tx(&bVfull[s], SM::V_BYTES);
-        if (PV == FD_PV_FP8) {
+        if (PV == FD_PV_FP8_TILE) {
+          // codes + the scales of the tile's one or two 64-row halves
+          const int nh = (2 * j + 1 < p.nkb64) ? 2 : 1;
+          mbar_arrive_expect_tx(&bVfull[s], SM::V_BYTES + nh * 512);
+          tma_load_3d(sV + s * SM::V_BYTES, &tmV, &bVfull[s], 0, j * BKV, bh);
+          bulk_load(reinterpret_cast<float*>(smem + SM::OFF_VDT) + s * 256,
+                    p.v_desc + ((int64_t)bh * p.nkb64 + 2 * j) * HD, nh * 512, &bVfull[s]);
+        } else if (PV == FD_PV_FP8) {
+          mbar_arrive_expect_tx(&bVfull[s], SM::V_BYTES);
           tma_load_3d(sV + s * SM::V_BYTES, &tmV, &bVfull[s], 0, j * BKV, bh);
         } else {
+          mbar_arrive_expect_tx(&bVfull[s], SM::V_BYTES);
           tma_load_3d(sV + s * SM::V_BYTES, &tmV, &bVfull[s], 0, j * BKV, bh);
           tma_load_3d(sV + s * SM::V_BYTES + BKV * 128, &tmV, &bVfull[s], 64, j * BKV, bh);
         }
@@ -390,8 +457,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
           QK == FD_QK_INT8 ? make_idesc(/*S32*/ 2, /*S8*/ 1, 1, 0, 0, BQ, BKV)
                            : make_idesc(/*F32*/ 1, /*E4M3*/ 0, 0, 0, 0, BQ, BKV);
       constexpr uint32_t idesc_pv =
-          PV == FD_PV_FP8 ? make_idesc(1, /*E4M3*/ 0, 0, /*A K-major*/ 0, /*B MN-major*/ 1, BQ, HD)
-                          : make_idesc(1, /*BF16*/ 1, 1, 0, 1, BQ, HD);
+          PV != FD_PV_BF16 ? make_idesc(1, /*E4M3*/ 0, 0, /*A K-major*/ 0, /*B MN-major*/ 1, BQ, HD)
+                           : make_idesc(1, /*BF16*/ 1, 1, 0, 1, BQ, HD);
       const uint32_t aQ = smem_u32(sQ);
       bool ok = mbar_wait(bQ, 0, abort_flag);
       // list of valid tiles is re-derived here in the same order as the producer
@@ -439,7 +506,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         tc_fence_after();
         const uint32_t aP = smem_u32(sP);
         const uint32_t bV = smem_u32(sV + s * SM::V_BYTES);
-        if (PV == FD_PV_FP8) {
+        if (PV == FD_PV_FP8_TILE) {
+          // each 64-key half into its own TMEM product (keys [64 h, 64 h + 64) of P
+          // and rows [64 h, 64 h + 64) of V), promoted by the softmax warps
+#pragma unroll
+          for (int k = 0; k < BKV / 32; ++k) {
+            const uint64_t ad = make_sdesc_sw128(aP + k * 32, 16, 1024);
+            const uint64_t bd = make_sdesc_sw128(bV + k * 32 * 128, 16, 1024);
+            mma_f8f6f4_ss(k < 2 ? tO : tPV1, ad, bd, idesc_pv, (k & 1) ? 1u : 0u);
+          }
+        } else if (PV == FD_PV_FP8) {
 #pragma unroll
           for (int k = 0; k < BKV / 32; ++k) {
             const uint64_t ad = make_sdesc_sw128(aP + k * 32, 16, 1024);
@@ -454,7 +530,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
             mma_f16_ss(tO, ad, bd, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
           }
         }
-        tc_commit(&bVempty[s]);
+        if (PV != FD_PV_FP8_TILE) tc_commit(&bVempty[s]);
         tc_commit(bOready);
         ++i;
         jcur = jn;
@@ -488,6 +564,182 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     const float qd = p.q_gran == FD_GRAN_TOKEN
                          ? p.q_desc[(int64_t)bh * p.q_desc_stride + (qrow < p.N ? qrow : 0)]
                          : p.q_desc[(int64_t)bh * p.q_desc_stride + qb];
+    if constexpr (PV == FD_PV_FP8_TILE) {
+    // ---------------------------------------------------------------- PT softmax
+    // The reference's FP8-PV update, 64 keys at a time (sage_kernels.py:1124-1158):
+    // thread h owns the 64-key half h of every 128-key tile, i.e. one reference
+    // tile.  Per half: m_new = max(m, rowmax), alpha = exp2(m - m_new),
+    // p = exp2(s - m_new), l = alpha l + sum p, P8 = e4m3(p * 448 / amax(p)),
+    // o = alpha o + (P8 V8 * amax(p) / 448) * v_desc[tile, d].  O stays in
+    // registers: thread h owns output columns [64 h, 64 h + 64).
+    float* px = reinterpret_cast<float*>(smem + SM::OFF_PX);  // [0][h][row] P descale, [1][h][row] sum p
+    const float* vdt = reinterpret_cast<const float*>(smem + SM::OFF_VDT);
+    float o[64];
+#pragma unroll
+    for (int e = 0; e < 64; ++e) o[e] = 0.f;
+    float m_run = -INFINITY, l = 0.f;
+    float pa1 = 0.f, pa2 = 0.f, ppd0 = 0.f, ppd1 = 0.f;  // the previous tile's update factors
+    bool ph1ok = false;
+    uint32_t pstage = 0;
+    // o = (o a1 + pv0 pd0 vd0) a2 + pv1 pd1 vd1 with the previous tile's products
+    auto promote = [&](uint32_t iprev) -> bool {
+      if (!mbar_wait(bOready, iprev & 1, abort_flag)) return false;
+      tc_fence_after();
+      const float* vd = vdt + pstage * 256 + cb;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        uint32_t r0[16], r1[16];
+        tmem_ld16(tO + lane_base + cb + 16 * cc, r0);
+        tmem_ld16(tPV1 + lane_base + cb + 16 * cc, r1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int c = 16 * cc + e;
+          float x = __fmul_rn(o[c], pa1);
+          x = __fadd_rn(x, __fmul_rn(__fmul_rn(__uint_as_float(r0[e]), ppd0), vd[c]));
+          x = __fmul_rn(x, pa2);
+          if (ph1ok) x = __fadd_rn(x, __fmul_rn(__fmul_rn(__uint_as_float(r1[e]), ppd1), vd[128 + c]));
+          o[c] = x;
+        }
+      }
+      // the tile's V codes and scales are used: release its V stage
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bVempty[pstage]);
+      return true;
+    };
+    uint32_t i = 0;
+    bool ok = true;
+    for (int j = 0; j < p.n_kv_tiles && ok; ++j) {
+      const int col0 = j * BKV + cb;
+      const bool half_ok = col0 < p.N;
+      const bool full = col0 + 64 <= p.N;
+      if (!mbar_wait(bSfull, i & 1, abort_flag)) { ok = false; break; }
+      if (KG == FD_GRAN_TOKEN) {
+        if (!mbar_wait(&bKdfull[i % KDS], (i / KDS) & 1, abort_flag)) { ok = false; break; }
+      }
+      tc_fence_after();
+      const float* kd = sKd + (i % KDS) * 128 + cb;
+      float c = 0.f;
+      if (KG == FD_GRAN_BLOCK) {
+        const int kb = 2 * j + h;
+        c = (kb < p.nkb64) ? p.k_desc[(int64_t)bh * p.k_desc_stride + kb] * qd : 0.f;
+      }
+      // ---- row maxima of the two halves
+      float mloc = -INFINITY;
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t r[32];
+        tmem_ld32(tS + lane_base + cb + 32 * cc, r);
+        tmem_wait_ld();
+        mloc = fmaxf(mloc, full ? chunk_max32<QK, KG, true>(r, col0 + 32 * cc, p.N, half_ok, kd + 32 * cc)
+                                : chunk_max32<QK, KG, false>(r, col0 + 32 * cc, p.N, half_ok, kd + 32 * cc));
+      }
+      if (KG == FD_GRAN_BLOCK) {
+        if (QK == FD_QK_INT8) mloc -= S_BIAS;
+        mloc = mloc == -INFINITY ? -INFINITY : mloc * c;
+      } else {
+        mloc = mloc == -INFINITY ? -INFINITY : mloc * qd;
+      }
+      float* rm = red_max + (i & 1) * 256;
+      rm[h * 128 + row] = mloc;
+      named_bar_sync(2 + quad, 64);
+      const float mx0 = h == 0 ? mloc : rm[row], mx1 = h == 1 ? mloc : rm[128 + row];
+      const float m1 = fmaxf(m_run, mx0), m2 = fmaxf(m1, mx1);
+      const float a1 = m_run == -INFINITY ? 0.f : ex2_approx(m_run - m1);
+      const float a2 = m1 == -INFINITY ? 0.f : ex2_approx(m1 - m2);
+      const float mh = h == 0 ? m1 : m2;
+      // ---- the previous tile's PV (frees P, the PV products and its V stage)
+      if (i > 0) {
+        if (!promote(i - 1)) { ok = false; break; }
+      }
+      // ---- p of this half: absmax and sum first, then the e4m3 codes (p recomputed)
+      const float nb0 = mh == -INFINITY ? 0.f : -mh;
+      const float nb = (KG == FD_GRAN_BLOCK && QK == FD_QK_INT8) ? fmaf(-S_BIAS, c, nb0) : nb0;
+      float pam = 0.f, psum = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t r[32];
+        float pv[32];
+        tmem_ld32(tS + lane_base + cb + 32 * cc, r);
+        tmem_wait_ld();
+        if (full) chunk_p<QK, KG, true>(r, col0 + 32 * cc, p.N, half_ok, qd, kd + 32 * cc, c, nb, pv);
+        else chunk_p<QK, KG, false>(r, col0 + 32 * cc, p.N, half_ok, qd, kd + 32 * cc, c, nb, pv);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          pam = fmaxf(pam, pv[e]);
+          psum += pv[e];
+        }
+      }
+      const float pinv = div_full(448.0f, fmaxf(pam, 1e-12f));
+      const float pd = div_full(pam, 448.0f);
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t r[32];
+        float pv[32];
+        tmem_ld32(tS + lane_base + cb + 32 * cc, r);
+        tmem_wait_ld();
+        if (QK == FD_QK_INT8) tmem_fill32(tS + lane_base + cb + 32 * cc, S_BIAS_BITS);
+        if (cc == 1) {
+          if (QK == FD_QK_INT8) tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bSfree);  // the tensor core may overwrite S now
+        }
+        if (full) chunk_p<QK, KG, true>(r, col0 + 32 * cc, p.N, half_ok, qd, kd + 32 * cc, c, nb, pv);
+        else chunk_p<QK, KG, false>(r, col0 + 32 * cc, p.N, half_ok, qd, kd + 32 * cc, c, nb, pv);
+        // 32 keys = two 16-byte chunks of the 128-byte e4m3 P row (chunk 4 h + 2 cc + k)
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          uint32_t w[4];
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const int e = 16 * k + 4 * q4;
+            w[q4] = f32x4_to_e4m3x4(__fmul_rn(pv[e], pinv), __fmul_rn(pv[e + 1], pinv),
+                                    __fmul_rn(pv[e + 2], pinv), __fmul_rn(pv[e + 3], pinv));
+          }
+          const int chunk = 4 * h + 2 * cc + k;
+          *reinterpret_cast<uint4*>(sP + row * 128 + ((chunk ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      px[h * 128 + row] = pd;
+      px[256 + h * 128 + row] = psum;
+      named_bar_sync(2 + quad, 64);
+      const float pd0 = px[row], pd1 = px[128 + row];
+      l = __fadd_rn(__fmul_rn(a2, __fadd_rn(__fmul_rn(a1, l), px[256 + row])), px[384 + row]);
+      m_run = m2;
+      pa1 = a1;
+      pa2 = a2;
+      ppd0 = pd0;
+      ppd1 = pd1;
+      ph1ok = 2 * j + 1 < p.nkb64;
+      pstage = i % KST;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bPfull);
+      ++i;
+    }
+    if (ok && i > 0) ok = promote(i - 1);
+    // ---- epilogue: out = o / l (bf16), LSE = m + log2(l)
+    const bool row_ok = qrow < p.N;
+    const float l_div = i > 0 ? l : 0.f;
+    if (ok && row_ok && h == 0 && p.lse) p.lse[(int64_t)bh * p.N + qrow] = i > 0 ? m_run + log2f(l) : -INFINITY;
+    if (ok && row_ok) {
+      __nv_bfloat16* orow = p.out + ((int64_t)bh * p.N + qrow) * HD + cb;
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) w[e] = pack_bf16x2(div_full(o[32 * cc + 2 * e], l_div), div_full(o[32 * cc + 2 * e + 1], l_div));
+        uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
+        dst[3] = make_uint4(w[12], w[13], w[14], w[15]);
+      }
+    }
+    } else {
     // l accumulates this thread's share of P in its stored scale (x PScale::SCALE)
     float m_ref = -INFINITY, l = 0.f;
     uint32_t i = 0;
@@ -685,12 +937,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         }
       }
     }
+    }  // PV != FD_PV_FP8_TILE
   }
 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == WARP_MMA) tmem_dealloc(tmem_base, 256);
+  if (warp == WARP_MMA) tmem_dealloc(tmem_base, TMEM_COLS);
 }
 
 template <int QK, int KG, int PV>
@@ -733,7 +986,11 @@ static int sage_attn_fwd_impl(const void* q_codes, const float* q_desc, const vo
   FD_CHECK_ARG(qk_kind == FD_QK_INT8 || qk_kind == FD_QK_FP8, "bad qk_kind");
   FD_CHECK_ARG(q_gran == FD_GRAN_TOKEN || q_gran == FD_GRAN_BLOCK, "bad q_gran");
   FD_CHECK_ARG(k_gran == FD_GRAN_TOKEN || k_gran == FD_GRAN_BLOCK, "bad k_gran");
-  FD_CHECK_ARG(pv_kind == FD_PV_BF16 || pv_kind == FD_PV_FP8, "bad pv_kind");
+  FD_CHECK_ARG(pv_kind == FD_PV_BF16 || pv_kind == FD_PV_FP8 || pv_kind == FD_PV_FP8_TILE, "bad pv_kind");
+  FD_CHECK_ARG(pv_kind != FD_PV_FP8_TILE || (q_gran == FD_GRAN_TOKEN && k_gran == FD_GRAN_TOKEN &&
+                                             block_mask == nullptr && out_heads == 0 && qo == nullptr && out),
+               "FD_PV_FP8_TILE: per-token Q/K, no block mask, (BH, N, 128) output");
+  FD_CHECK_ARG(pv_kind != FD_PV_FP8_TILE || aligned16(v_desc), "v_desc must be 16-byte aligned");
   FD_CHECK_ARG(q_codes && q_desc && k_codes && k_desc && v && (out || qo), "null pointer");
   FD_CHECK_ARG(pv_kind == FD_PV_BF16 || v_desc, "v_desc required for fp8 PV");
   FD_CHECK_ARG(aligned16(q_codes) && aligned16(k_codes) && aligned16(v) && (qo || aligned16(out)) &&
@@ -750,7 +1007,7 @@ static int sage_attn_fwd_impl(const void* q_codes, const float* q_desc, const vo
     rc = encode_tiled(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, k_codes, dims, strides, box,
                       CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    if (pv_kind == FD_PV_FP8) {
+    if (pv_kind != FD_PV_BF16) {
       rc = encode_tiled(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, v, dims, strides, box,
                         CU_TENSOR_MAP_SWIZZLE_128B);
     } else {
@@ -798,6 +1055,10 @@ static int sage_attn_fwd_impl(const void* q_codes, const float* q_desc, const vo
   p.k_desc_stride = fd_desc_stride(N, k_gran, 64);
   cudaStream_t st = (cudaStream_t)stream;
 #define FD_ATTN(QKV, KGV, PVV) return attn::launch<QKV, KGV, PVV>(tq, tk, tv, p, (int)BH, st)
+  if (pv_kind == FD_PV_FP8_TILE) {
+    if (qk_kind == FD_QK_INT8) FD_ATTN(FD_QK_INT8, FD_GRAN_TOKEN, FD_PV_FP8_TILE);
+    else FD_ATTN(FD_QK_FP8, FD_GRAN_TOKEN, FD_PV_FP8_TILE);
+  }
   if (qk_kind == FD_QK_INT8) {
     if (k_gran == FD_GRAN_TOKEN) {
       if (pv_kind == FD_PV_FP8) FD_ATTN(FD_QK_INT8, FD_GRAN_TOKEN, FD_PV_FP8);

@@ -552,6 +552,47 @@ extern "C" int fd_attn_quant(const void* q, const void* k, const void* v, int64_
 }
 
 // ---------------------------------------------------------------------------
+// V of the reference's FP8-PV kernel (_sage_attn_fwd_fp8qk_fp8pv_lse,
+// src/futudiffu/sage_kernels.py:1146-1152): per 64-row tile and column d,
+// amax over the tile's rows (rows past N count as 0), codes e4m3(v * (448 /
+// max(amax, 1e-12))) and descale amax / 448.  One CTA per (tile, bh), one
+// thread per column: every row read is one coalesced 256-byte line.
+namespace fd {
+__global__ void __launch_bounds__(128) v_tile_quant_kernel(const __nv_bfloat16* __restrict__ v, int64_t N,
+                                                          uint8_t* __restrict__ v_codes,
+                                                          float* __restrict__ v_desc) {
+  const int64_t t = blockIdx.x, bh = blockIdx.y, ntiles = gridDim.x;
+  const int c = threadIdx.x;
+  const int64_t r0 = t * 64;
+  const int rows = (int)min((int64_t)64, N - r0);
+  const __nv_bfloat16* src = v + (bh * N + r0) * 128 + c;
+  float x[64];
+  float am = 0.f;
+#pragma unroll
+  for (int r = 0; r < 64; ++r) {
+    x[r] = r < rows ? __bfloat162float(src[(int64_t)r * 128]) : 0.f;
+    am = fmaxf(am, fabsf(x[r]));
+  }
+  const float inv = div_full(448.0f, fmaxf(am, 1e-12f));
+  v_desc[(bh * ntiles + t) * 128 + c] = div_full(am, 448.0f);
+  uint8_t* dst = v_codes + (bh * N + r0) * 128 + c;
+#pragma unroll
+  for (int r = 0; r < 64; ++r)
+    if (r < rows) dst[(int64_t)r * 128] = (uint8_t)(f32x2_to_e4m3x2(__fmul_rn(x[r], inv), 0.f) & 0xFF);
+}
+}  // namespace fd
+
+extern "C" int fd_attn_quant_v_tile(const void* v, int64_t BH, int64_t N, void* v_codes, float* v_desc,
+                                    void* stream) {
+  FD_CHECK_ARG(BH > 0 && N > 0 && BH <= 65535 && N < (1ll << 30), "bad shape");
+  FD_CHECK_ARG(v && v_codes && v_desc, "null pointer");
+  const int64_t ntiles = (N + 63) / 64;
+  v_tile_quant_kernel<<<dim3((unsigned)ntiles, (unsigned)BH), 128, 0, (cudaStream_t)stream>>>(
+      (const __nv_bfloat16*)v, N, (uint8_t*)v_codes, v_desc);
+  return check_launch("attn_quant_v_tile");
+}
+
+// ---------------------------------------------------------------------------
 // fd_attn_quant_noalloc: fd_attn_quant with its scratch in g_attn_quant_ws.
 //
 // For callers that cannot allocate device memory themselves -- hosts that hand

@@ -98,31 +98,37 @@ def quantize_qkv(
 
     Layouts: codes (BH, N, 128); per-token descales (BH, round_up(N, 128)),
     per-block descales (BH, ceil(N/128)) for Q and (BH, ceil(N/64)) for K;
-    v_desc (BH, 128); k_mean (BH, 128) (bf16-rounded smoothing mean as f32).
+    v_desc (BH, 128) for pv_quant "fp8" (per channel), (BH, ceil(N/64), 128) for
+    "fp8_tile" (the reference's per-64-row-tile V scales); k_mean (BH, 128)
+    (bf16-rounded smoothing mean as f32).
     """
     BH, N, D = q.shape
     dev = q.device
     qk = L.QK_INT8 if qk_quant == "int8" else L.QK_FP8
     gran = L.GRAN_TOKEN if granularity == "per_token" else L.GRAN_BLOCK
-    pv = L.PV_FP8 if pv_quant == "fp8" else L.PV_BF16
+    pv = {"fp8": L.PV_FP8, "fp8_tile": L.PV_FP8_TILE}.get(pv_quant, L.PV_BF16)
     code_dt = torch.int8 if qk == L.QK_INT8 else torch.float8_e4m3fn
     q_codes = torch.empty(BH, N, D, dtype=code_dt, device=dev)
     k_codes = torch.empty(BH, N, D, dtype=code_dt, device=dev)
     q_desc = torch.empty(BH, _desc_stride(N, gran, 128), dtype=torch.float32, device=dev)
     k_desc = torch.empty(BH, _desc_stride(N, gran, 64), dtype=torch.float32, device=dev)
     k_mean = torch.empty(BH, D, dtype=torch.float32, device=dev)
-    if pv == L.PV_FP8:
+    v_codes = v_desc = None
+    if pv != L.PV_BF16:
         v_codes = torch.empty(BH, N, D, dtype=torch.float8_e4m3fn, device=dev)
-        v_desc = torch.empty(BH, D, dtype=torch.float32, device=dev)
-    else:
-        v_codes = None
-        v_desc = None
+        # per-channel: one scale per (bh, d); per tile: one per (bh, 64-row tile, d)
+        v_desc = torch.empty(BH, D, dtype=torch.float32, device=dev) if pv == L.PV_FP8 else \
+            torch.empty(BH, (N + 63) // 64, D, dtype=torch.float32, device=dev)
     ws = torch.empty(int(L.lib().fd_attn_quant_workspace_floats(BH, N)), dtype=torch.float32, device=dev)
+    pv_prologue = L.PV_FP8 if pv == L.PV_FP8 else L.PV_BF16
     L.call(
-        "fd_attn_quant", L.ptr(q), L.ptr(k), L.ptr(v), BH, N, int(bool(smooth_k)), qk, gran, gran, pv,
+        "fd_attn_quant", L.ptr(q), L.ptr(k), L.ptr(v), BH, N, int(bool(smooth_k)), qk, gran, gran, pv_prologue,
         float(sm_scale * _LOG2E), L.ptr(q_codes), L.ptr(q_desc), L.ptr(k_codes), L.ptr(k_desc),
-        L.ptr(v_codes), L.ptr(v_desc), L.ptr(k_mean), L.ptr(ws), L.stream_ptr(dev),
+        L.ptr(v_codes) if pv == L.PV_FP8 else None, L.ptr(v_desc) if pv == L.PV_FP8 else None,
+        L.ptr(k_mean), L.ptr(ws), L.stream_ptr(dev),
     )
+    if pv == L.PV_FP8_TILE:
+        L.call("fd_attn_quant_v_tile", L.ptr(v), BH, N, L.ptr(v_codes), L.ptr(v_desc), L.stream_ptr(dev))
     return {
         "q_codes": q_codes, "q_desc": q_desc, "k_codes": k_codes, "k_desc": k_desc,
         "v_codes": v_codes, "v_desc": v_desc, "k_mean": k_mean,
@@ -168,7 +174,7 @@ def _attn_forward(
                       granularity=granularity, pv_quant=pv_quant)
     out = torch.empty(B, N, H * D, dtype=q.dtype, device=q.device) if out_bnhd else torch.empty_like(qf)
     lse = torch.empty(BH, N, dtype=torch.float32, device=q.device) if want_lse else None
-    vsrc = qz["v_codes"] if qz["pv"] == L.PV_FP8 else vf
+    vsrc = qz["v_codes"] if qz["pv"] != L.PV_BF16 else vf
     common = (L.ptr(qz["q_codes"]), L.ptr(qz["q_desc"]), L.ptr(qz["k_codes"]), L.ptr(qz["k_desc"]),
               L.ptr(vsrc), L.ptr(qz["v_desc"]), L.ptr(bm), bm_stride, L.ptr(out), L.ptr(lse), BH, N)
     kinds = (qz["qk"], qz["gran"], qz["gran"], qz["pv"], L.stream_ptr(q.device))
@@ -298,7 +304,7 @@ def attn_forward_quant_out(
     vf = v.reshape(BH, N, D).contiguous()
     qz = quantize_qkv(qf, kf, vf, sm_scale, smooth_k=_SAGE_SMOOTH_K, qk_quant=qk_quant,
                       granularity=granularity, pv_quant=pv_quant)
-    vsrc = qz["v_codes"] if qz["pv"] == L.PV_FP8 else vf
+    vsrc = qz["v_codes"] if qz["pv"] != L.PV_BF16 else vf
     _quant_out_call(qz, vsrc, B, H, N, block_mask, regions, split, q.device)
 
 
@@ -332,7 +338,8 @@ def sage_attn_forward_with_lse(
     if _SAGE_QK_GRAN == "per_block":
         qk, pv = _SAGE_QK_QUANT, _SAGE_PV_QUANT
     elif _SAGE_PV_QUANT == "fp8":
-        qk, pv = "fp8", "fp8"
+        # the reference's FP8-QK / FP8-PV kernel: P and V scaled per 64-key tile
+        qk, pv = "fp8", "fp8_tile"
     else:
         qk, pv = _SAGE_QK_QUANT, "bf16"
     return _attn_forward(q, k, v, sm_scale, block_mask=None, qk_quant=qk, pv_quant=pv,

@@ -53,6 +53,10 @@ extern "C" {
 #define FD_GRAN_BLOCK 1 /* one scale per 128 Q rows / 64 K rows                      */
 #define FD_PV_BF16 0 /* bf16 P x bf16 V (sage_kernels.py:681-684)                     */
 #define FD_PV_FP8 1  /* e4m3 P (static scale) x e4m3 V (per-channel scale)            */
+/* FD_PV_FP8_TILE: the reference's FP8 PV (sage_kernels.py:1135-1154): per 64-key
+ * tile, e4m3 P per row (scaled by its absmax in the tile) and e4m3 V per column
+ * (scaled by its absmax over the tile's 64 rows, fd_attn_quant_v_tile).          */
+#define FD_PV_FP8_TILE 2
 
 /* Library version string and the last host-side error message (thread-local). */
 const char* fd_version(void);
@@ -294,6 +298,13 @@ int fd_qkv_postprocess_quant(const void* qkv, const float* qw, const float* kw, 
 int fd_attn_quant_kv(const void* k, const void* v, int64_t BH, int64_t N, int smooth_k, int qk_kind, int k_gran,
                      int pv_kind, void* k_codes, float* k_desc, void* v_codes, float* v_desc, float* k_mean,
                      float* workspace, void* stream);
+
+/* V for FD_PV_FP8_TILE (reference _sage_attn_fwd_fp8qk_fp8pv_lse,
+ * src/futudiffu/sage_kernels.py:1146-1152): v (BH, N, 128) bf16 -> v_codes
+ * (BH, N, 128) e4m3 and v_desc (BH, ceil(N/64), 128) f32, per 64-row tile and
+ * column: v_desc = amax / 448, code = e4m3(v * (448 / max(amax, 1e-12))); rows
+ * past N count as 0. */
+int fd_attn_quant_v_tile(const void* v, int64_t BH, int64_t N, void* v_codes, float* v_desc, void* stream);
 
 /* No counterpart in the reference.  fd_attn_quant with no workspace argument:
  * the scratch lives in a fixed device array inside the library (one per GPU

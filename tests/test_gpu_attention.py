@@ -88,13 +88,16 @@ MODES = [
     ("int8", "per_block", "bf16", "bf16", 0.9995),
     ("int8", "per_block", "fp8", "fp8_channel", 0.9995),
     ("fp8", "per_block", "fp8", "fp8_channel", 0.9995),
+    # the reference's FP8-PV kernel: P per row and V per column, per 64-key tile
+    ("fp8", "per_token", "fp8_tile", "fp8_tile", 0.9995),
+    ("int8", "per_token", "fp8_tile", "fp8_tile", 0.9995),
 ]
 
 
 def _run(q, k, v, dev, qk, gran, pv, mask=None, lse=True):
     from futudiffu_b200 import sage_attention as SA
 
-    SA.configure_sage(smooth_k=True, qk_quant=qk, pv_quant=pv, qk_granularity=gran)
+    SA.configure_sage(smooth_k=True, qk_quant=qk, pv_quant="fp8" if pv == "fp8_tile" else pv, qk_granularity=gran)
     d = lambda t: t.to(dev)  # noqa: E731
     B = 1
     q4, k4, v4 = (d(t).unsqueeze(0) for t in (q, k, v))
@@ -127,7 +130,8 @@ def test_attention_vs_oracle(cuda_device, mode, BH, N):
     out, lse = _run(q, k, v, cuda_device, qk, gran, pv)
     ref, rlse = OA.attention_forward(q, k, v, sm_scale=SM, qk_quant=qk, granularity=gran, pv_quant=opv)
     assert torch.isfinite(out.float()).all()
-    if opv == "bf16":
+    if opv in ("bf16", "fp8_tile"):
+        # bf16 P, or e4m3 P rounded exactly as the oracle (the reference's per-tile scales)
         c = cosine(out, ref)
         assert c >= tol, c
     else:
