@@ -566,7 +566,7 @@ __global__ void __launch_bounds__(NUM_THREADS, PV == FD_PV_FP8_TILE ? 1 : 2)
                          : p.q_desc[(int64_t)bh * p.q_desc_stride + qb];
     if constexpr (PV == FD_PV_FP8_TILE) {
     // ---------------------------------------------------------------- PT softmax
-    // The reference's FP8-PV update, 64 keys at a time (sage_kernels.py:1124-1158):
+    // The reference's FP8-PV update, 64 keys at a time (sage_kernels.py:1124-1154):
     // thread h owns the 64-key half h of every 128-key tile, i.e. one reference
     // tile.  Per half: m_new = max(m, rowmax), alpha = exp2(m - m_new),
     // p = exp2(s - m_new), l = alpha l + sum p, P8 = e4m3(p * 448 / amax(p)),

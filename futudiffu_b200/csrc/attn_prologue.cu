@@ -13,7 +13,7 @@
 //   _smooth_k          src/futudiffu/sage_attention.py:63-71 (bf16 mean, bf16 sub)
 //   INT8 Q/K per token src/futudiffu/sage_kernels.py:632-639, :656-663
 //   FP8 Q/K per token  src/futudiffu/sage_kernels.py:151-155, :176-179
-//   V e4m3 per channel src/futudiffu/sage_kernels.py:1146-1151 (here over the
+//   V e4m3 per channel src/futudiffu/sage_kernels.py:1142-1148 (here over the
 //                      whole sequence instead of one 64-row tile)
 #include <mutex>
 
@@ -553,7 +553,7 @@ extern "C" int fd_attn_quant(const void* q, const void* k, const void* v, int64_
 
 // ---------------------------------------------------------------------------
 // V of the reference's FP8-PV kernel (_sage_attn_fwd_fp8qk_fp8pv_lse,
-// src/futudiffu/sage_kernels.py:1146-1152): per 64-row tile and column d,
+// src/futudiffu/sage_kernels.py:1142-1148): per 64-row tile and column d,
 // amax over the tile's rows (rows past N count as 0), codes e4m3(v * (448 /
 // max(amax, 1e-12))) and descale amax / 448.  One CTA per (tile, bh), one
 // thread per column: every row read is one coalesced 256-byte line.

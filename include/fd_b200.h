@@ -300,7 +300,7 @@ int fd_attn_quant_kv(const void* k, const void* v, int64_t BH, int64_t N, int sm
                      float* workspace, void* stream);
 
 /* V for FD_PV_FP8_TILE (reference _sage_attn_fwd_fp8qk_fp8pv_lse,
- * src/futudiffu/sage_kernels.py:1146-1152): v (BH, N, 128) bf16 -> v_codes
+ * src/futudiffu/sage_kernels.py:1142-1148): v (BH, N, 128) bf16 -> v_codes
  * (BH, N, 128) e4m3 and v_desc (BH, ceil(N/64), 128) f32, per 64-row tile and
  * column: v_desc = amax / 448, code = e4m3(v * (448 / max(amax, 1e-12))); rows
  * past N count as 0. */
