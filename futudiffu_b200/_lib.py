@@ -94,6 +94,7 @@ _SIGS: dict[str, list] = {
                                    _P, _P, _L, _L, _P, _P, _L, _L, _L, _P],
     "fd_sage_attn_bwd_prepass": [_P, _P, _P, _L, _L, _P],
     "fd_sage_attn_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _P, _L, _L, _I, _F, _P],
+    "fd_sage_attn_bwd_tc": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _P, _L, _L, _I, _F, _P],
 }
 _RESTYPES = {
     "fd_version": ctypes.c_char_p,

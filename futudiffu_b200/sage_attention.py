@@ -371,9 +371,12 @@ def _per_token_descales(qz: dict, N: int) -> tuple[Tensor, Tensor]:
 
 
 def _attn_backward(q, k, v, out, lse, dout, sm_scale, block_mask, qk_quant, granularity):
+    """dQ, dK, dV on the tensor cores (fd_sage_attn_bwd_tc: a dK/dV kernel and a dQ
+    kernel, fp32 accumulation in TMEM, masked tiles skipped)."""
     B, H, N, D = q.shape
     BH = B * H
     L.require_cuda(q, k, v, out, lse, dout)
+    assert D == 128 and q.dtype == k.dtype == v.dtype == out.dtype == torch.bfloat16, "bf16 (B, H, N, 128) inputs"
     qf = q.reshape(BH, N, D).contiguous()
     kf = k.reshape(BH, N, D).contiguous()
     vf = v.reshape(BH, N, D).contiguous()
@@ -392,73 +395,16 @@ def _attn_backward(q, k, v, out, lse, dout, sm_scale, block_mask, qk_quant, gran
         ks = (kf - qz["k_mean"].to(torch.bfloat16).unsqueeze(1)).contiguous()
     else:
         ks = kf
-    if N % 8 == 0:
-        dq, dk, dv = _attn_backward_tc(qf, ks, vf, dof, lse, delta, qz, bm, bm_stride, float(sm_scale))
-        return dq.reshape(B, H, N, D), dk.reshape(B, H, N, D), dv.reshape(B, H, N, D)
     dq = torch.empty_like(qf)
     dk = torch.empty_like(qf)
     dv = torch.empty_like(qf)
     L.call(
-        "fd_sage_attn_bwd", L.ptr(qf), L.ptr(ks), L.ptr(vf), L.ptr(dof), L.ptr(lse), L.ptr(delta),
+        "fd_sage_attn_bwd_tc", L.ptr(qf), L.ptr(ks), L.ptr(vf), L.ptr(dof), L.ptr(lse), L.ptr(delta),
         L.ptr(qz["q_codes"]), L.ptr(qz["q_desc"]), L.ptr(qz["k_codes"]), L.ptr(qz["k_desc"]),
         L.ptr(bm), bm_stride, L.ptr(dq), L.ptr(dk), L.ptr(dv), BH, N, qz["qk"], float(sm_scale),
         L.stream_ptr(q.device),
     )
     return dq.reshape(B, H, N, D), dk.reshape(B, H, N, D), dv.reshape(B, H, N, D)
-
-
-# bytes of chunk scratch per (query row, key): S and dP fp32, P / dS*sm / dS bf16
-_BWD_BYTES_PER_PAIR = 14
-_BWD_CHUNK_BYTES = 3 << 30
-
-
-def _attn_backward_tc(qf, ks, vf, dof, lse, delta, qz, bm, bm_stride, sm_scale):
-    """Backward on the tensor cores: per chunk of heads and query rows, S = Qc Kc^T
-    (codes as bf16: exact for INT8) and dP = dO V^T as batched library GEMMs with
-    fp32 output, the elementwise kernel (P, dS and their bf16 roundings, block
-    mask), then dV += P^T dO, dK += (dS sm)^T Q, dQ = dS Ks sm, fp32-accumulated
-    and rounded to bf16 once.  Same per-element arithmetic as the CUDA-core
-    kernels (and the reference); only the accumulation order of the sums differs.
-    Scratch is bounded by _BWD_CHUNK_BYTES."""
-    BH, N, D = qf.shape
-    dev = qf.device
-    per_head = _BWD_BYTES_PER_PAIR * N * N
-    if per_head <= _BWD_CHUNK_BYTES:
-        HC, R = max(1, min(BH, _BWD_CHUNK_BYTES // per_head)), N
-    else:
-        HC, R = 1, max(128, (_BWD_CHUNK_BYTES // (_BWD_BYTES_PER_PAIR * N)) // 128 * 128)
-    f32, bf16 = torch.float32, torch.bfloat16
-    dq = torch.empty(BH, N, D, dtype=bf16, device=dev)
-    dk = torch.empty(BH, N, D, dtype=bf16, device=dev)
-    dv = torch.empty(BH, N, D, dtype=bf16, device=dev)
-    stream = L.stream_ptr(dev)
-    for h0 in range(0, BH, HC):
-        hc = min(HC, BH - h0)
-        hs = slice(h0, h0 + hc)
-        kc16 = qz["k_codes"][hs].to(bf16)
-        dk_acc = dv_acc = None
-        for r0 in range(0, N, R):
-            rr = min(R, N - r0)
-            rs = slice(r0, r0 + rr)
-            S = torch.bmm(qz["q_codes"][hs, rs].to(bf16), kc16.transpose(1, 2), out_dtype=f32)
-            dP = torch.bmm(dof[hs, rs], vf[hs].transpose(1, 2), out_dtype=f32)
-            P16, dSs16, dS16 = (torch.empty(hc, rr, N, dtype=bf16, device=dev) for _ in range(3))
-            L.call("fd_sage_attn_bwd_elementwise", L.ptr(S), L.ptr(dP), L.ptr(qz["q_desc"]), L.ptr(qz["k_desc"]),
-                   L.ptr(lse), L.ptr(delta), L.ptr(bm), bm_stride, L.ptr(P16), L.ptr(dSs16), L.ptr(dS16), hc, rr,
-                   r0, N, h0, sm_scale, stream)
-            del S, dP
-            dv_p = torch.bmm(P16.transpose(1, 2), dof[hs, rs], out_dtype=f32)
-            dk_p = torch.bmm(dSs16.transpose(1, 2), qf[hs, rs], out_dtype=f32)
-            dq_p = torch.bmm(dS16, ks[hs], out_dtype=f32)
-            dq[hs, rs] = (dq_p * sm_scale).to(bf16)
-            if dv_acc is None:
-                dv_acc, dk_acc = dv_p, dk_p
-            else:
-                dv_acc += dv_p
-                dk_acc += dk_p
-        dv[hs] = dv_acc.to(bf16)
-        dk[hs] = dk_acc.to(bf16)
-    return dq, dk, dv
 
 
 def sage_attn_backward(

@@ -381,6 +381,19 @@ int fd_sage_attn_bwd(const void* q, const void* k, const void* v, const void* do
                      const uint8_t* block_mask, int64_t mask_bh_stride, void* dq, void* dk,
                      void* dv, int64_t BH, int64_t N, int qk_kind, float sm_scale, void* stream);
 
+/* A7 -- the same backward on the tensor cores (tcgen05), any N: a dK / dV kernel
+ * (one CTA per 128-key tile over 64-query steps: S^T = Kc Qc^T on the codes,
+ * dP^T = V dO^T, dV += bf16(P)^T dO, dK += bf16(dS sm_scale)^T Q, accumulated in
+ * TMEM) and a dQ kernel (one CTA per 128-query tile over 64-key steps: S, dP,
+ * dQ += bf16(dS) Ks, times sm_scale at the end).  Same arguments and arithmetic
+ * as fd_sage_attn_bwd; masked (128 x 64) tiles are skipped.  All tensors 16-byte
+ * aligned. */
+int fd_sage_attn_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
+                        const float* lse, const float* delta, const void* q_codes,
+                        const float* q_desc, const void* k_codes, const float* k_desc,
+                        const uint8_t* block_mask, int64_t mask_bh_stride, void* dq, void* dk,
+                        void* dv, int64_t BH, int64_t N, int qk_kind, float sm_scale, void* stream);
+
 /* Elementwise step of the tensor-core backward (the products S = Qc Kc^T,
  * dP = dO V^T, dV = P^T dO, dK = dS^T Q, dQ = dS Ks run as batched library GEMMs
  * with fp32 output on a chunk of HC heads bh0 .. and query rows [r0, r0 + R)):

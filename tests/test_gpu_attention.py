@@ -247,11 +247,13 @@ def test_attention_status_clean(cuda_device):
 
 @pytest.mark.parametrize("gran", ["per_token", "per_block"])
 @pytest.mark.parametrize("qk", ["int8", "fp8"])
-@pytest.mark.parametrize("N,masked", [(256, False), (200, False), (201, False), (384, True)])
-def test_attention_backward_vs_oracle(cuda_device, qk, N, masked, gran):
-    """N % 8 == 0: the tensor-core backward (library GEMMs + elementwise kernel);
-    N = 201: the CUDA-core kernels.  Both granularities: the backward recomputes
-    P with the forward's Q/K scales (bf16 PV, so the forward is the oracle's)."""
+@pytest.mark.parametrize("N,docs", [(256, None), (200, None), (201, None), (65, None), (384, [128, 256]),
+                                    (448, [200, 248])])
+def test_attention_backward_vs_oracle(cuda_device, qk, N, docs, gran):
+    """The tcgen05 backward (dK/dV and dQ kernels) at aligned, ragged and masked
+    sizes (documents of 200 + 248 tokens leave half-masked 128-key tiles and
+    skipped steps).  Both granularities: the backward recomputes P with the
+    forward's Q/K scales (bf16 PV, so the forward is the oracle's)."""
     from futudiffu_b200 import sage_attention as SA
 
     BH = 2
@@ -259,8 +261,9 @@ def test_attention_backward_vs_oracle(cuda_device, qk, N, masked, gran):
     g = gen(77)
     dout = torch.randn(BH, N, 128, generator=g).to(torch.bfloat16)
     mask = None
+    masked = docs is not None
     if masked:
-        mask = torch.from_numpy(OB.build_block_mask([128, N - 128]))
+        mask = torch.from_numpy(OB.build_block_mask(docs))
     SA.configure_sage(smooth_k=True, qk_quant=qk, pv_quant="bf16", qk_granularity=gran)
     d = lambda t: t.to(cuda_device).unsqueeze(0)  # noqa: E731
     if masked:
@@ -381,26 +384,90 @@ def test_attention_quantised_output(cuda_device, masked):
 
 
 
-@pytest.mark.parametrize("masked", [False, True])
-def test_backward_chunking_invariant(cuda_device, masked, monkeypatch):
-    """The tensor-core backward gives the same gradients whether a head is done in
-    one chunk or in 128-row query blocks (dK / dV accumulated in fp32 across them)."""
+def _torch_backward_fp32(qf, kf, vf, dof, lse, delta, qz, ks, sm, mask=None):
+    """fp32 torch restatement on the GPU of the backward arithmetic, head by head:
+    S from the quantised codes, p = exp2((S q_desc) k_desc - lse) (0 on masked
+    128 x 64 tiles), dS = p (dO V^T - Delta), dV = bf16(p)^T dO, dK = bf16(dS sm)^T Q,
+    dQ = sm bf16(dS) Ks, each gradient rounded to bf16 once."""
+    BH, N, _ = qf.shape
+    f32, bf16 = torch.float32, torch.bfloat16
+    qd, kd = qz["q_desc"][:, :N], qz["k_desc"][:, :N]
+    dq, dk, dv = (torch.empty_like(qf) for _ in range(3))
+    for h in range(BH):
+        s = qz["q_codes"][h].to(f32) @ qz["k_codes"][h].to(f32).t()
+        p = torch.exp2((s * qd[h, :, None]) * kd[h, None, :] - lse[h, :, None])
+        if mask is not None:
+            m = mask[h if mask.shape[0] > 1 else 0].bool()
+            p = torch.where(m.repeat_interleave(128, 0)[:N].repeat_interleave(64, 1)[:, :N], p, 0.0)
+        dp = dof[h].float() @ vf[h].float().t()
+        ds = p * (dp - delta[h, :, None])
+        dv[h] = (p.to(bf16).float().t() @ dof[h].float()).to(bf16)
+        dk[h] = ((ds * sm).to(bf16).float().t() @ qf[h].float()).to(bf16)
+        dq[h] = ((ds.to(bf16).float() @ ks[h].float()) * sm).to(bf16)
+    return dq, dk, dv
+
+
+def _bwd_inputs(BH, N, seed, qk="int8", gran="per_token"):
+    from futudiffu_b200 import _lib as L
     from futudiffu_b200 import sage_attention as SA
 
-    BH, N = 3, 512
-    q, k, v = (t.to(cuda_device).unsqueeze(0) for t in qkv(BH, N, 41))
-    dout = torch.randn(1, BH, N, 128, generator=gen(42)).to(torch.bfloat16).to(cuda_device)
-    mask = torch.from_numpy(OB.build_block_mask([200, N - 200])).to(cuda_device) if masked else None
-    SA.configure_sage(smooth_k=True, qk_quant="int8", pv_quant="bf16")
+    dev = torch.device("cuda")
+    q, k, v = (t.to(dev) for t in qkv(BH, N, seed))
+    dof = torch.randn(BH, N, 128, generator=gen(seed + 1)).to(torch.bfloat16).to(dev)
+    SA.configure_sage(smooth_k=True, qk_quant=qk, pv_quant="bf16", qk_granularity=gran)
+    out, lse = SA.sage_attn_forward_with_lse(q.unsqueeze(0), k.unsqueeze(0), v.unsqueeze(0), SM)
+    qz = SA.quantize_qkv(q, k, v, SM, smooth_k=True, qk_quant=qk, granularity=gran, pv_quant="bf16")
+    qz["q_desc"], qz["k_desc"] = SA._per_token_descales(qz, N)
+    delta = (dof.float() * out[0].float()).sum(-1)
+    ks = (k - qz["k_mean"].to(torch.bfloat16).unsqueeze(1)).contiguous()
+    return q, k, v, out, lse, dof, qz, delta, ks
+
+
+@pytest.mark.parametrize("qk", ["int8", "fp8"])
+def test_backward_config2_vs_torch_fp32(cuda_device, qk):
+    """Benchmark config 2's shape (B 2, H 24, N 4096) against the fp32 torch
+    restatement of the same quantised arithmetic on the GPU."""
+    from futudiffu_b200 import sage_attention as SA
+
+    BH, N = 48, 4096
+    q, k, v, out, lse, dof, qz, delta, ks = _bwd_inputs(BH, N, 91, qk)
+    dq, dk, dv = SA.sage_attn_backward(q.unsqueeze(0), k.unsqueeze(0), v.unsqueeze(0), out, lse,
+                                       dof.unsqueeze(0), SM)
+    rq, rk, rv = _torch_backward_fp32(q, k, v, dof, lse, delta, qz, ks, SM)
+    for a, b in ((dq[0], rq), (dk[0], rk), (dv[0], rv)):
+        assert torch.isfinite(a.float()).all()
+        assert cosine(a.float().cpu(), b.float().cpu()) >= 0.9999
+    from futudiffu_b200 import check_status
+
+    check_status()
+
+
+@pytest.mark.parametrize("masked", [False, True])
+def test_backward_deterministic(cuda_device, masked):
+    """No atomics in the backward: two runs give the same bits, and a 3-D (per
+    head) mask with skipped steps matches the fp32 torch restatement."""
+    from futudiffu_b200 import sage_attention as SA
+
+    BH, N = 3, 704
+    q, k, v, out, lse, dof, qz, delta, ks = _bwd_inputs(BH, N, 41)
+    mask = None
     if masked:
-        out, lse = SA.sage_attn_forward_masked_with_lse(q, k, v, mask, SM)
-        run = lambda: SA.sage_attn_backward_masked(q, k, v, out, lse, dout, mask, SM)  # noqa: E731
+        mask = torch.stack([torch.from_numpy(OB.build_block_mask(d)) for d in ([200, 504], [704], [64, 320, 320])])
+        mask = mask.to(cuda_device)
+        out, lse = SA.sage_attn_forward_masked_with_lse(q.unsqueeze(0), k.unsqueeze(0), v.unsqueeze(0), mask, SM)
+        delta = (dof.float() * out[0].float()).sum(-1)
+        run = lambda: SA.sage_attn_backward_masked(q.unsqueeze(0), k.unsqueeze(0), v.unsqueeze(0), out, lse,  # noqa: E731
+                                                   dof.unsqueeze(0), mask, SM)
     else:
-        out, lse = SA.sage_attn_forward_with_lse(q, k, v, SM)
-        run = lambda: SA.sage_attn_backward(q, k, v, out, lse, dout, SM)  # noqa: E731
-    whole = run()
-    monkeypatch.setattr(SA, "_BWD_CHUNK_BYTES", SA._BWD_BYTES_PER_PAIR * N * 128)
-    blocks = run()
-    for a, b in zip(whole, blocks):
-        assert cosine(a.cpu(), b.cpu()) > 0.99999
-        assert (a.float() - b.float()).abs().max().item() <= 2 ** -6 * b.float().abs().max().item()
+        run = lambda: SA.sage_attn_backward(q.unsqueeze(0), k.unsqueeze(0), v.unsqueeze(0), out, lse,  # noqa: E731
+                                            dof.unsqueeze(0), SM)
+    a, b = run(), run()
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
+    ref = _torch_backward_fp32(q, k, v, dof, lse, delta, qz, ks, SM, mask)
+    for x, r in zip(a, ref):
+        assert torch.isfinite(x.float()).all()
+        assert cosine(x[0].float().cpu(), r.float().cpu()) >= 0.9999
+    from futudiffu_b200 import check_status
+
+    check_status()

@@ -60,6 +60,32 @@ def test_double_stream_block(cuda_device, B):
     _close(o_img, r_img)
 
 
+def test_double_stream_block_config3_full_size(cuda_device):
+    """Benchmark config 3 at its real shape (hidden 3072, 24 heads, 512 text + 4096
+    image tokens, batch 1) against the oracle composition.  The oracle runs its
+    linears as dequantised fp32 matmuls and its attention matmuls in fp32: the same
+    quantised operands and the same quantisers as the exact form, summed in another
+    order, which keeps the CPU side to seconds at this size."""
+    from futudiffu_b200.dit import DiTConfig, DoubleStreamBlock, batch_freqs, image_freqs, text_freqs
+
+    cfg = DiTConfig()
+    assert (cfg.hidden, cfg.heads, cfg.txt_tokens, cfg.img_tokens) == (3072, 24, 512, 4096)
+    g = torch.Generator(device=cuda_device).manual_seed(13)
+    blk = DoubleStreamBlock(cfg, g, cuda_device)
+    cg = gen(14)
+    x_txt = torch.randn(1, cfg.txt_tokens, cfg.hidden, generator=cg).to(torch.bfloat16)
+    x_img = torch.randn(1, cfg.img_tokens, cfg.hidden, generator=cg).to(torch.bfloat16)
+    vec = torch.randn(1, cfg.hidden, generator=cg).to(torch.bfloat16)
+    f_txt = batch_freqs(text_freqs(cfg, cuda_device), 1)
+    f_img = batch_freqs(image_freqs(cfg, cuda_device), 1)
+    with torch.no_grad():
+        o_txt, o_img = blk(x_txt.to(cuda_device), x_img.to(cuda_device), vec.to(cuda_device), f_txt, f_img)
+    with OD.eager_cpu_timing():
+        r_txt, r_img = OD.double_block(blk, x_txt, x_img, vec, f_txt.cpu(), f_img.cpu())
+    _close(o_txt, r_txt)
+    _close(o_img, r_img)
+
+
 def test_single_stream_block(cuda_device):
     from futudiffu_b200.dit import SingleStreamBlock, batch_freqs, image_freqs, text_freqs
 
