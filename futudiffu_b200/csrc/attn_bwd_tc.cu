@@ -12,18 +12,24 @@
 //
 // dK/dV kernel: CTA = one 128-key tile of one (b, h), looping over 64-query steps.
 //   resident: Kc (codes) and V (bf16) of the tile
-//   per step (3-stage ring): Qc, Q (bf16), dO (bf16) of 64 queries + q_desc /
+//   per step (4-stage ring): Qc, Q (bf16), dO (bf16) of 64 queries + q_desc /
 //   -lse / -Delta of those queries
 //   MMA:  S^T  = Kc Qc^T        (M 128 keys, N 64, kind::i8 onto the score bias, or f8f6f4)
 //         dP^T = V dO^T         (kind::f16, both K-major)
-//         dV  += P^T dO         (A = P^T in shared memory, B = the dO tile read MN-major)
-//         dK  += dSs^T Q        (B = the Q tile read MN-major)
+//         dV  += P^T dO         (A = P^T in TMEM, B = the dO tile read MN-major)
+//         dK  += dSs^T Q        (A = dSs^T in TMEM, B = the Q tile read MN-major)
 //   S^T / dP^T are double-buffered in TMEM, so the next step's products run on the
-//   tensor core while the compute warps turn this step's into P^T and dS^T.
-//   TMEM: dV [0,128), dK [128,256), S^T(b) [256+128b, +64), dP^T(b) [320+128b, +64).
+//   tensor core while the compute warps turn this step's into P^T and dS^T, which
+//   they write back as bf16 pairs over the dP^T columns they have read (the dV / dK
+//   products of step i are issued before step i + 2's S^T / dP^T, and tcgen05 MMAs
+//   of one thread run in issue order).
+//   TMEM: dV [0,128), dK [128,256), S^T(b) [256+128b, +64), dP^T(b) [320+128b, +64);
+//   the thread that read dP^T columns [32h, 32h+32) (queries 32h..32h+31) writes
+//   P^T of those queries over [32h, +16) and dSs^T over [32h+16, +16).
 // dQ kernel: CTA = one 128-query tile, looping over 64-key steps:
-//         S = Qc Kc^T, dP = dO V^T (double-buffered), dQ += dS Ks (B = Ks tile MN-major).
-//   TMEM: dQ [0,128), S(b) [128+128b, +64), dP(b) [192+128b, +64).
+//         S = Qc Kc^T, dP = dO V^T (double-buffered), dQ += dS Ks (A = dS in TMEM,
+//         B = the Ks tile read MN-major).
+//   TMEM: dQ [0,128), S(b) [128+64b, +64), dP(b) [256+64b, +64), dS(b) [384+32b, +32).
 // Warps 0-7 compute (TMEM lane quadrant w & 3, 32 of the step's 64 columns each),
 // warp 8 TMA producer, warp 9 MMA issuer.  Every wait is bounded (fd_common.cuh).
 #include "fd_common.cuh"
@@ -35,7 +41,7 @@ namespace attn_bwd_tc {
 constexpr int HD = 128;
 constexpr int BT = 128;  // rows of the resident tile
 constexpr int BS = 64;   // rows per step
-constexpr int NST = 3;   // stage ring depth
+constexpr int NST = 4;   // stage ring depth
 constexpr int NUM_COMPUTE_WARPS = 8;
 constexpr int WARP_TMA = 8, WARP_MMA = 9;
 constexpr int NUM_THREADS = 320;
@@ -55,18 +61,14 @@ struct SmemKV {  // dK / dV kernel
   static constexpr uint32_t Q_BYTES = BS * HD * 2;       // two panels of BS x 128 B
   static constexpr uint32_t DO_BYTES = BS * HD * 2;
   static constexpr uint32_t STAGE_BYTES = QC_BYTES + Q_BYTES + DO_BYTES;
-  static constexpr uint32_t PT_BYTES = BT * BS * 2;      // P^T / dS^T: 128 rows x 128 B
   static constexpr uint32_t OFF_KC = 0;
   static constexpr uint32_t OFF_V = OFF_KC + KC_BYTES;
   static constexpr uint32_t OFF_ST = OFF_V + V_BYTES;
   static constexpr uint32_t OFF_VEC = OFF_ST + NST * STAGE_BYTES;  // per stage: qd, nbq, nl, nd [4][64] f32
-  static constexpr uint32_t OFF_P = OFF_VEC + NST * 1024;
-  static constexpr uint32_t OFF_DS = OFF_P + PT_BYTES;
-  static constexpr uint32_t OFF_BAR = OFF_DS + PT_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_VEC + NST * 1024;
   static constexpr uint32_t TOTAL = OFF_BAR + 256 + 1024;  // + barriers, alignment slack
 };
-static_assert(SmemKV::OFF_ST % 1024 == 0 && SmemKV::STAGE_BYTES % 1024 == 0 && SmemKV::OFF_P % 1024 == 0 &&
-                  SmemKV::OFF_DS % 1024 == 0,
+static_assert(SmemKV::OFF_ST % 1024 == 0 && SmemKV::STAGE_BYTES % 1024 == 0,
               "swizzled tiles need 1024-byte alignment");
 static_assert(SmemKV::TOTAL <= 232448, "dK/dV shared memory");
 
@@ -77,17 +79,14 @@ struct SmemQ {  // dQ kernel
   static constexpr uint32_t V_BYTES = BS * HD * 2;
   static constexpr uint32_t KS_BYTES = BS * HD * 2;
   static constexpr uint32_t STAGE_BYTES = KC_BYTES + V_BYTES + KS_BYTES;
-  static constexpr uint32_t DS_BYTES = BT * BS * 2;
   static constexpr uint32_t OFF_QC = 0;
   static constexpr uint32_t OFF_DO = OFF_QC + QC_BYTES;
   static constexpr uint32_t OFF_ST = OFF_DO + DO_BYTES;
   static constexpr uint32_t OFF_KD = OFF_ST + NST * STAGE_BYTES;  // per stage 64 f32
-  static constexpr uint32_t OFF_DS = OFF_KD + 1024;               // two buffers
-  static constexpr uint32_t OFF_BAR = OFF_DS + 2 * DS_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_KD + 1024;
   static constexpr uint32_t TOTAL = OFF_BAR + 256 + 1024;
 };
-static_assert(SmemQ::OFF_ST % 1024 == 0 && SmemQ::STAGE_BYTES % 1024 == 0 && SmemQ::OFF_DS % 1024 == 0,
-              "swizzled tiles need 1024-byte alignment");
+static_assert(SmemQ::OFF_ST % 1024 == 0 && SmemQ::STAGE_BYTES % 1024 == 0, "swizzled tiles need 1024-byte alignment");
 static_assert(NST * 256 <= 1024, "dQ key-scale slots");
 static_assert(SmemQ::TOTAL <= 232448, "dQ shared memory");
 
@@ -129,16 +128,6 @@ FD_DEV bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) 
   return ok;
 }
 
-// 32 bf16 pairs of one row -> the row's 64-byte half (16-byte chunks 4h .. 4h+3)
-// of a 128-byte-swizzled K-major tile
-FD_DEV void store_row_half(uint8_t* tile, int row, int h, const uint32_t (&w)[16]) {
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const int ch = 4 * h + c;
-    *reinterpret_cast<uint4*>(tile + row * 128 + ((ch ^ (row & 7)) << 4)) =
-        make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
-  }
-}
 
 // 64 accumulator columns of this thread's row -> bf16 at dst (scaled by `scale`)
 FD_DEV void store_acc64(uint32_t taddr, bool any, bool row_ok, float scale, __nv_bfloat16* dst) {
@@ -185,8 +174,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sKc = smem + SM::OFF_KC;
   uint8_t* sV = smem + SM::OFF_V;
-  uint8_t* sP = smem + SM::OFF_P;
-  uint8_t* sDS = smem + SM::OFF_DS;
   float* sVec = reinterpret_cast<float*>(smem + SM::OFF_VEC);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::OFF_BAR);
   uint64_t* bRes = bars + 0;
@@ -194,9 +181,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* bEmpty = bFull + NST;           // [NST]
   uint64_t* bSdpFull = bEmpty + NST;        // [2]
   uint64_t* bSdpFree = bSdpFull + 2;        // [2]
-  uint64_t* bPsFull = bSdpFree + 2;
-  uint64_t* bPsEmpty = bPsFull + 1;
-  uint64_t* bAcc = bPsEmpty + 1;
+  uint64_t* bPsFull = bSdpFree + 2;        // [2]
+  uint64_t* bAcc = bPsFull + 2;
   uint64_t* bDrain = bAcc + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bDrain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -215,9 +201,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bSdpFull[b], 1);
       mbar_init(&bSdpFree[b], NUM_COMPUTE_WARPS);
+      mbar_init(&bPsFull[b], NUM_COMPUTE_WARPS);
     }
-    mbar_init(bPsFull, NUM_COMPUTE_WARPS);
-    mbar_init(bPsEmpty, 1);
     mbar_init(bAcc, 1);
     mbar_init(bDrain, 1);
     *abort_flag = 0;
@@ -248,24 +233,43 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tma_load_3d(sV, &tmV, bRes, 0, k0, bh);
       tma_load_3d(sV + BT * 128, &tmV, bRes, 64, k0, bh);
     }
+    // per-query constants of a step: q_desc, -S_BIAS q_desc (INT8), -lse (-inf past
+    // N, which zeroes those columns' P), -Delta; the next step's are loaded into
+    // registers while this step waits for its stage, so no global-load latency sits
+    // between a free stage and its refill
+    auto next_valid = [&](int from) {
+      for (int t = from; t < nsteps; ++t)
+        if (kv_step_valid(p, bh, kt, t)) return t;
+      return nsteps;
+    };
+    auto load_vec = [&](int t, float (&r)[6]) {
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int qi = t * BS + lane + 32 * u;
+        const bool ok = t < nsteps && qi < p.N;
+        r[3 * u] = ok ? p.q_desc[(int64_t)bh * p.dstride + qi] : 0.f;
+        r[3 * u + 1] = ok ? -p.lse[(int64_t)bh * p.N + qi] : -INFINITY;
+        r[3 * u + 2] = ok ? -p.delta[(int64_t)bh * p.N + qi] : 0.f;
+      }
+    };
     uint32_t i = 0;
-    for (int t = 0; t < nsteps; ++t) {
-      if (!kv_step_valid(p, bh, kt, t)) continue;
+    int t = next_valid(0);
+    float cur[6];
+    load_vec(t, cur);
+    for (; t < nsteps; ++i) {
+      const int tn = next_valid(t + 1);
+      float nxt[6];
+      load_vec(tn, nxt);
       const uint32_t s = i % NST, use = i / NST;
       if (!warp_wait(&bEmpty[s], (use & 1) ^ 1, abort_flag)) break;
-      // per-query constants of the step: q_desc, -S_BIAS q_desc (INT8), -lse
-      // (-inf past N, which zeroes those columns' P), -Delta
       float* v = sVec + s * 256;
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const int e = lane + 32 * u;
-        const int qi = t * BS + e;
-        const bool ok = qi < p.N;
-        const float qd = ok ? p.q_desc[(int64_t)bh * p.dstride + qi] : 0.f;
-        v[e] = qd;
-        v[64 + e] = QK == FD_QK_INT8 ? -S_BIAS * qd : 0.f;
-        v[128 + e] = ok ? -p.lse[(int64_t)bh * p.N + qi] : -INFINITY;
-        v[192 + e] = ok ? -p.delta[(int64_t)bh * p.N + qi] : 0.f;
+        v[e] = cur[3 * u];
+        v[64 + e] = QK == FD_QK_INT8 ? -S_BIAS * cur[3 * u] : 0.f;
+        v[128 + e] = cur[3 * u + 1];
+        v[192 + e] = cur[3 * u + 2];
       }
       __syncwarp();
       if (lane == 0) {
@@ -278,7 +282,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tma_load_3d(st + SM::QC_BYTES + SM::Q_BYTES + BS * 128, &tmDO, &bFull[s], 64, t * BS, bh);
       }
       __syncwarp();
-      ++i;
+#pragma unroll
+      for (int e = 0; e < 6; ++e) cur[e] = nxt[e];
+      t = tn;
     }
     if (lane == 0) {
       drain_wait(bRes, 0);
@@ -295,7 +301,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       constexpr uint32_t idesc_dp = make_idesc(1, /*BF16*/ 1, 1, 0, 0, BT, BS);
       constexpr uint32_t idesc_acc = make_idesc(1, 1, 1, /*A K-major*/ 0, /*B MN-major*/ 1, BT, HD);
       const uint32_t aKc = smem_u32(sKc), aV = smem_u32(sV);
-      const uint32_t aP = smem_u32(sP), aDS = smem_u32(sDS);
       bool ok = mbar_wait(bRes, 0, abort_flag);
       // the valid steps, in the producer's order
       auto next_valid = [&](int from) {
@@ -327,25 +332,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         return true;
       };
       auto issue_acc = [&](uint32_t i) -> bool {
-        const uint32_t s = i % NST;
-        if (!mbar_wait(bPsFull, i & 1, abort_flag)) return false;
+        const uint32_t s = i % NST, b = i & 1;
+        if (!mbar_wait(&bPsFull[b], (i >> 1) & 1, abort_flag)) return false;
         tc_fence_after();
         const uint32_t st = smem_u32(smem + SM::OFF_ST + s * SM::STAGE_BYTES);
         const uint32_t bQ = st + SM::QC_BYTES, bDO = st + SM::QC_BYTES + SM::Q_BYTES;
+        // queries [16 k, 16 k + 16): P^T at column 32 (k / 2) + 8 (k % 2), dSs^T 16 further
 #pragma unroll
         for (int k = 0; k < BS / 16; ++k) {
-          const uint64_t ad = make_sdesc_sw128(aP + k * 32, 16, 1024);
           const uint64_t bd = make_sdesc_sw128(bDO + k * 16 * 128, BS * 128, 1024);
-          mma_f16_ss(tdV, ad, bd, idesc_acc, (i > 0 || k > 0) ? 1u : 0u);
+          mma_f16_ts(tdV, tdP(b) + 32 * (k >> 1) + 8 * (k & 1), bd, idesc_acc, (i > 0 || k > 0) ? 1u : 0u);
         }
 #pragma unroll
         for (int k = 0; k < BS / 16; ++k) {
-          const uint64_t ad = make_sdesc_sw128(aDS + k * 32, 16, 1024);
           const uint64_t bd = make_sdesc_sw128(bQ + k * 16 * 128, BS * 128, 1024);
-          mma_f16_ss(tdK, ad, bd, idesc_acc, (i > 0 || k > 0) ? 1u : 0u);
+          mma_f16_ts(tdK, tdP(b) + 32 * (k >> 1) + 16 + 8 * (k & 1), bd, idesc_acc, (i > 0 || k > 0) ? 1u : 0u);
         }
         tc_commit(&bEmpty[s]);
-        tc_commit(bPsEmpty);
         return true;
       };
       // order: S/dP(0), S/dP(1), then acc(i), S/dP(i + 2), ...
@@ -432,14 +435,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           wd[c >> 1] = pack_bf16x2(d0, d1);
         }
       }
-      // the P^T / dS^T tiles are free once the previous step's dV / dK products are done
-      if (!mbar_wait(bPsEmpty, (i & 1) ^ 1, abort_flag)) { ok = false; break; }
-      store_row_half(sP, row, h, wp);
-      store_row_half(sDS, row, h, wd);
-      fence_proxy_async_smem();
+      // P^T and dSs^T over the 32 dP^T columns this thread has read: queries
+      // [32 h, 32 h + 32) as bf16 pairs, P^T at columns [32 h, +16), dSs^T at [32 h + 16, +16)
+      tmem_st16(tdP(b) + lane_base + cb, wp);
+      tmem_st16(tdP(b) + lane_base + cb + 16, wd);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bPsFull);
+      if (lane == 0) mbar_arrive(&bPsFull[b]);
       ++i;
     }
     // ---------------------------------------------------------------- epilogue
@@ -478,8 +481,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* bSdpFull = bEmpty + NST;   // [2]
   uint64_t* bSdpFree = bSdpFull + 2;   // [2]
   uint64_t* bDsFull = bSdpFree + 2;    // [2]
-  uint64_t* bDsEmpty = bDsFull + 2;    // [2]
-  uint64_t* bAcc = bDsEmpty + 2;
+  uint64_t* bAcc = bDsFull + 2;
   uint64_t* bDrain = bAcc + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bDrain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -500,7 +502,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&bSdpFull[b], 1);
       mbar_init(&bSdpFree[b], NUM_COMPUTE_WARPS);
       mbar_init(&bDsFull[b], NUM_COMPUTE_WARPS);
-      mbar_init(&bDsEmpty[b], 1);
     }
     mbar_init(bAcc, 1);
     mbar_init(bDrain, 1);
@@ -516,8 +517,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t tdQ = tmem_base;
-  auto tS = [&](uint32_t b) { return tmem_base + 128 + 128 * b; };
-  auto tdP = [&](uint32_t b) { return tmem_base + 192 + 128 * b; };
+  auto tS = [&](uint32_t b) { return tmem_base + 128 + 64 * b; };
+  auto tdP = [&](uint32_t b) { return tmem_base + 256 + 64 * b; };
+  auto tdS = [&](uint32_t b) { return tmem_base + 384 + 32 * b; };
 
   if (warp == WARP_TMA) {
     // ================================================================ producer
@@ -532,18 +534,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tma_load_3d(sDO, &tmDO, bRes, 0, q0, bh);
       tma_load_3d(sDO + BT * 128, &tmDO, bRes, 64, q0, bh);
     }
+    // per-key scales of a step, loaded one step ahead (as in the dK / dV producer)
+    auto next_valid = [&](int from) {
+      for (int j = from; j < nsteps; ++j)
+        if (step_valid(j)) return j;
+      return nsteps;
+    };
+    auto load_kd = [&](int j, float (&r)[2]) {
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int key = j * BS + lane + 32 * u;
+        r[u] = (j < nsteps && key < p.N) ? p.k_desc[(int64_t)bh * p.dstride + key] : 0.f;
+      }
+    };
     uint32_t i = 0;
-    for (int j = 0; j < nsteps; ++j) {
-      if (!step_valid(j)) continue;
+    int j = next_valid(0);
+    float cur[2];
+    load_kd(j, cur);
+    for (; j < nsteps; ++i) {
+      const int jn = next_valid(j + 1);
+      float nxt[2];
+      load_kd(jn, nxt);
       const uint32_t s = i % NST, use = i / NST;
       if (!warp_wait(&bEmpty[s], (use & 1) ^ 1, abort_flag)) break;
       float* kdv = sKd + s * 64;
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int e = lane + 32 * u;
-        const int key = j * BS + e;
-        kdv[e] = key < p.N ? p.k_desc[(int64_t)bh * p.dstride + key] : 0.f;
-      }
+      kdv[lane] = cur[0];
+      kdv[lane + 32] = cur[1];
       __syncwarp();
       if (lane == 0) {
         uint8_t* st = smem + SM::OFF_ST + s * SM::STAGE_BYTES;
@@ -555,7 +571,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tma_load_3d(st + SM::KC_BYTES + SM::V_BYTES + BS * 128, &tmKs, &bFull[s], 64, j * BS, bh);
       }
       __syncwarp();
-      ++i;
+      cur[0] = nxt[0];
+      cur[1] = nxt[1];
+      j = jn;
     }
     if (lane == 0) {
       drain_wait(bRes, 0);
@@ -602,15 +620,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         const uint32_t st = smem_u32(smem + SM::OFF_ST + s * SM::STAGE_BYTES);
         const uint32_t bKs = st + SM::KC_BYTES + SM::V_BYTES;
-        const uint32_t aDS = smem_u32(smem + SM::OFF_DS + b * SM::DS_BYTES);
 #pragma unroll
         for (int k = 0; k < BS / 16; ++k) {
-          const uint64_t ad = make_sdesc_sw128(aDS + k * 32, 16, 1024);
           const uint64_t bd = make_sdesc_sw128(bKs + k * 16 * 128, BS * 128, 1024);
-          mma_f16_ss(tdQ, ad, bd, idesc_acc, (i > 0 || k > 0) ? 1u : 0u);
+          mma_f16_ts(tdQ, tdS(b) + 8 * k, bd, idesc_acc, (i > 0 || k > 0) ? 1u : 0u);
         }
         tc_commit(&bEmpty[s]);
-        tc_commit(&bDsEmpty[b]);
         return true;
       };
       int nvalid = 0;
@@ -693,9 +708,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           wd[c >> 1] = pack_bf16x2(d0, d1);
         }
       }
-      if (!mbar_wait(&bDsEmpty[b], ((i >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
-      store_row_half(smem + SM::OFF_DS + b * SM::DS_BYTES, row, h, wd);
-      fence_proxy_async_smem();
+      // dS(b) is free: step i - 2's dQ product read it before S(i) / dP(i) (issued
+      // after it) completed
+      tmem_st16(tdS(b) + lane_base + 16 * h, wd);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bDsFull[b]);

@@ -211,6 +211,17 @@ FD_DEV void mma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T: A is M lanes x K, two bf16 / f16 per 32-bit
+// column (K = 16 per instruction = 8 columns), K-major by construction.
+FD_DEV void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Instruction descriptor (kind::f16 / f8f6f4 / i8), dense, no negation.
 //   c_fmt: 0 F16, 1 F32, 2 S32.  a_fmt/b_fmt: kind-specific code
 //   (f16: 0 F16, 1 BF16; f8f6f4: 0 E4M3, 1 E5M2; i8: 0 U8, 1 S8).
