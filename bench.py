@@ -322,7 +322,7 @@ def run_ours(args, world, rank, local):
 # ------------------------------------------------------------------ config 4: DiT denoise
 DIT_BATCH = 8
 DIT_METRIC = "DiT denoise steps/s (12B-class, 19 double + 38 single blocks, 4096+512 tokens, batch 8)"
-KERNELS_PER_CALL = {"fd_attn_quant": 3, "fd_attn_quant_noalloc": 3, "fd_attn_quant_kv": 2}
+KERNELS_PER_CALL = {"fd_attn_quant": 3, "fd_attn_quant_noalloc": 3, "fd_attn_quant_kv": 2, "fd_sage_attn_bwd": 2}
 
 
 class LaunchRecorder:
@@ -1391,13 +1391,63 @@ def run_tmem_probe(args, world, rank, local):
     return 0
 
 
+def run_attn_bwd(args, world, rank, local):
+    """Attention backward at the config-2 shape (B 2, H 24, N 4096, head dim 128):
+    one `sage_attn_backward` call per step (six launches: the forward's Q/K quantisation redone,
+    the Delta pre-pass, the tcgen05 dK/dV and dQ kernels), INT8 per-token QK as
+    configured by default.  Inputs (q, k, v, dO: 4 x 100 MB) exceed L2.  value =
+    TFLOP/s counted over the five products of the reference's formulation
+    (S, dP, dV, dK, dQ: 5 x 2 x B x H x N^2 x 128)."""
+    from futudiffu_b200 import check_status
+    from futudiffu_b200 import sage_attention as SA
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B, H, N = 2, 24, 4096
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    q, k, v, do = (torch.randn(B, H, N, 128, device=dev, generator=g).to(torch.bfloat16) for _ in range(4))
+    sm = 128 ** -0.5
+    SA.configure_sage(smooth_k=True, qk_quant="int8", pv_quant="bf16", qk_granularity="per_token")
+    out, lse = SA.sage_attn_forward_with_lse(q, k, v, sm)
+    for _ in range(args.warmup):
+        SA.sage_attn_backward(q, k, v, out, lse, do, sm)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for e0, e1 in ev:
+            e0.record()
+            SA.sage_attn_backward(q, k, v, out, lse, do, sm)
+            e1.record()
+        torch.cuda.synchronize()
+    ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in ev), world, dev)
+    check_status()
+    flops = 5 * 2.0 * B * H * N * N * 128
+    tf = flops / (ms * 1e-3) / 1e12
+    pk = peaks()
+    peak = pk["bf16_tflops"]
+    if rank == 0:
+        print(json.dumps({
+            "metric": "SageAttn backward TFLOPS (5 products)", "value": tf * world, "unit": "TFLOPS",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 QK recompute, bf16 dP / dV / dK / dQ operands, fp32 accumulation", "data": "synthetic",
+            "config": {"workload": "attn_bwd_config2", "B": B, "H": H, "N": N, "head_dim": 128,
+                       "qk": "int8 per-token", "l2": "inputs larger than L2"},
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
+                         "traffic": None, "peak_source": f"{pk['source']} bf16 dense (burst)"},
+            "gpu_launches": 6 * args.steps, "clocks": clocks.summary(),
+        }), flush=True)
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default: 10 dit, 50 otherwise)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["dit", "video", "attention", "gemm", "packed", "block", "tmem_probe"],
+    ap.add_argument("--workload", choices=["dit", "video", "attention", "attn_bwd", "gemm", "packed", "block",
+                                           "tmem_probe"],
                     default="dit",
                     help="dit = benchmark config 4 (headline); video = config 5 (Ulysses); "
                          "block = config 3 (one double-stream block); "
@@ -1434,6 +1484,8 @@ def main(argv=None) -> int:
             return run_packed(args, world, rank, local)
         if args.workload == "tmem_probe":
             return run_tmem_probe(args, world, rank, local)
+        if args.workload == "attn_bwd":
+            return run_attn_bwd(args, world, rank, local)
         if args.impl == "reference":
             return run_reference(args, world, rank)
         if args.workload == "gemm":

@@ -68,7 +68,6 @@ _SIGS: dict[str, list] = {
     "fd_fp8_gemm_quant": [_P, _P, _P, _P, _P, _I, _P, _P, _L, _L, _L, _I, _P],
     "fd_fp8_gemm_quant_ld": [_P, _P, _P, _P, _P, _I, _P, _P, _L, _L, _L, _I, _L, _L, _P],
     "fd_fp8_gemm_grouped2": [_P, _P, _I, _I, _P],
-    "fd_sage_attn_bwd_elementwise": [_P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _P, _L, _L, _L, _L, _L, _F, _P],
     "fd_fp8_gemm_blockwise_lora": [_P, _P, _P, _P, _P, _I, _P, _I, _L, _L, _L, _P, _P, _L, _P],
     "fd_fp8_silu_gate_quant": [_P, _P, _P, _L, _L, _I, _P],
     "fd_fp8_gelu_tanh_quant": [_P, _P, _P, _L, _L, _I, _P],
@@ -94,7 +93,6 @@ _SIGS: dict[str, list] = {
                                    _P, _P, _L, _L, _P, _P, _L, _L, _L, _P],
     "fd_sage_attn_bwd_prepass": [_P, _P, _P, _L, _L, _P],
     "fd_sage_attn_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _P, _L, _L, _I, _F, _P],
-    "fd_sage_attn_bwd_tc": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _L, _P, _P, _P, _L, _L, _I, _F, _P],
 }
 _RESTYPES = {
     "fd_version": ctypes.c_char_p,

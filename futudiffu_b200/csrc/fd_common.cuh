@@ -297,6 +297,21 @@ FD_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
       : "memory");
 }
 
+FD_DEV void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
+// Write the same 32-bit value into 16 consecutive columns of this thread's lane.
+FD_DEV void tmem_fill16(uint32_t taddr, uint32_t v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+      "r"(v)
+      : "memory");
+}
+
 // Write the same 32-bit value into 32 consecutive columns of this thread's lane.
 FD_DEV void tmem_fill32(uint32_t taddr, uint32_t v) {
   asm volatile(

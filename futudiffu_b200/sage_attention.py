@@ -371,7 +371,7 @@ def _per_token_descales(qz: dict, N: int) -> tuple[Tensor, Tensor]:
 
 
 def _attn_backward(q, k, v, out, lse, dout, sm_scale, block_mask, qk_quant, granularity):
-    """dQ, dK, dV on the tensor cores (fd_sage_attn_bwd_tc: a dK/dV kernel and a dQ
+    """dQ, dK, dV on the tensor cores (fd_sage_attn_bwd: a dK/dV kernel and a dQ
     kernel, fp32 accumulation in TMEM, masked tiles skipped)."""
     B, H, N, D = q.shape
     BH = B * H
@@ -399,7 +399,7 @@ def _attn_backward(q, k, v, out, lse, dout, sm_scale, block_mask, qk_quant, gran
     dk = torch.empty_like(qf)
     dv = torch.empty_like(qf)
     L.call(
-        "fd_sage_attn_bwd_tc", L.ptr(qf), L.ptr(ks), L.ptr(vf), L.ptr(dof), L.ptr(lse), L.ptr(delta),
+        "fd_sage_attn_bwd", L.ptr(qf), L.ptr(ks), L.ptr(vf), L.ptr(dof), L.ptr(lse), L.ptr(delta),
         L.ptr(qz["q_codes"]), L.ptr(qz["q_desc"]), L.ptr(qz["k_codes"]), L.ptr(qz["k_desc"]),
         L.ptr(bm), bm_stride, L.ptr(dq), L.ptr(dk), L.ptr(dv), BH, N, qz["qk"], float(sm_scale),
         L.stream_ptr(q.device),

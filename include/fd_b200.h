@@ -370,41 +370,20 @@ int fd_sage_attn_fwd_quant_out(const void* q_codes, const float* q_desc, const v
 int fd_sage_attn_bwd_prepass(const void* dout, const void* out, float* delta, int64_t BH,
                              int64_t N, void* stream);
 
-/* A7 -- attention backward (sage_kernels.py:805-1015 int8, :1491-1722 masked int8,
- * :356-567 fp8).  Recomputes P = exp2(S - lse) from the same per-token Q/K
- * codes the forward used, then dV = P^T dO, dS = P (dO V^T - delta),
- * dK = sm_scale dS^T Q, dQ = sm_scale dS K, all with bf16 operands and fp32
- * accumulation.  q, k (smoothed), v, dout: (BH, N, 128) bf16. */
+/* A7 -- attention backward on the tensor cores (sage_kernels.py:805-1015 int8,
+ * :1491-1722 masked int8, :356-567 fp8).  Recomputes P = exp2((S q_desc) k_desc - lse)
+ * from the same per-token Q/K codes the forward used (per-block scales expanded to
+ * per-token arrays, row stride round_up(N, 128)), then dV = P^T dO,
+ * dS = P (dO V^T - delta), dK = sm_scale dS^T Q, dQ = sm_scale dS K with bf16
+ * operands and fp32 accumulation in TMEM: a dK / dV kernel (one CTA per 128-key
+ * tile over 64-query steps) and a dQ kernel (one CTA per 128-query tile over
+ * 64-key steps); masked (128 x 64) tiles are skipped.  q, k (smoothed), v, dout,
+ * dq, dk, dv: (BH, N, 128) bf16, 16-byte aligned; any N. */
 int fd_sage_attn_bwd(const void* q, const void* k, const void* v, const void* dout,
                      const float* lse, const float* delta, const void* q_codes,
                      const float* q_desc, const void* k_codes, const float* k_desc,
                      const uint8_t* block_mask, int64_t mask_bh_stride, void* dq, void* dk,
                      void* dv, int64_t BH, int64_t N, int qk_kind, float sm_scale, void* stream);
-
-/* A7 -- the same backward on the tensor cores (tcgen05), any N: a dK / dV kernel
- * (one CTA per 128-key tile over 64-query steps: S^T = Kc Qc^T on the codes,
- * dP^T = V dO^T, dV += bf16(P)^T dO, dK += bf16(dS sm_scale)^T Q, accumulated in
- * TMEM) and a dQ kernel (one CTA per 128-query tile over 64-key steps: S, dP,
- * dQ += bf16(dS) Ks, times sm_scale at the end).  Same arguments and arithmetic
- * as fd_sage_attn_bwd; masked (128 x 64) tiles are skipped.  All tensors 16-byte
- * aligned. */
-int fd_sage_attn_bwd_tc(const void* q, const void* k, const void* v, const void* dout,
-                        const float* lse, const float* delta, const void* q_codes,
-                        const float* q_desc, const void* k_codes, const float* k_desc,
-                        const uint8_t* block_mask, int64_t mask_bh_stride, void* dq, void* dk,
-                        void* dv, int64_t BH, int64_t N, int qk_kind, float sm_scale, void* stream);
-
-/* Elementwise step of the tensor-core backward (the products S = Qc Kc^T,
- * dP = dO V^T, dV = P^T dO, dK = dS^T Q, dQ = dS Ks run as batched library GEMMs
- * with fp32 output on a chunk of HC heads bh0 .. and query rows [r0, r0 + R)):
- * S, dP (HC, R, N) fp32 -> P16 = bf16(p), dSs16 = bf16(dS * sm_scale),
- * dS16 = bf16(dS), with p = exp2((S q_desc) k_desc - lse) (0 on masked tiles) and
- * dS = p (dP - Delta), the per-element arithmetic of the reference's backward
- * (sage_kernels.py:896-907, :1007-1010).  N % 8 == 0. */
-int fd_sage_attn_bwd_elementwise(const float* S, const float* dP, const float* q_desc, const float* k_desc,
-                                 const float* lse, const float* delta, const uint8_t* block_mask,
-                                 int64_t mask_bh_stride, void* P16, void* dSs16, void* dS16, int64_t HC, int64_t R,
-                                 int64_t r0, int64_t N, int64_t bh0, float sm_scale, void* stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop
