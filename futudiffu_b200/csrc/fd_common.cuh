@@ -325,6 +325,19 @@ FD_DEV void tmem_fill32(uint32_t taddr, uint32_t v) {
 FD_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 FD_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// TMA tile store shared -> global (bulk-group completion).
+FD_DEV void tma_store_2d(const void* src, const CUtensorMap* map, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+FD_DEV void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// The shared-memory sources of every committed store have been read.
+FD_DEV void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Every committed store has completed.
+FD_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // ---------------------------------------------------------- conversions
 // fp32 -> e4m3, round-to-nearest-even, saturating to +-448 (the clamp every
 // reference quantizer applies before its cast makes saturation a no-op).

@@ -63,11 +63,17 @@ constexpr uint32_t STAGE_BYTES = BM * BK + BN * BK;  // 48 KiB
 
 enum { EPI_STORE = 0, EPI_QUANT = 1, EPI_GELU_TANH = 2, EPI_SILU_GATE = 3 };
 
+constexpr uint32_t STG_WARP = 32 * 128;  // output staging per epilogue warp: 32 rows x 128 B
+
 struct Layout {
-  static constexpr uint32_t OFF_RED = STAGES * STAGE_BYTES;  // [2][2][128] f32 (SiLU-gate max exchange)
-  static constexpr uint32_t OFF_BAR = OFF_RED + 2 * 2 * 128 * 4;
+  // TMA-store epilogues stage their rows here; the SiLU-gate epilogue (direct
+  // stores) uses the same bytes for its [2][2][128] f32 max exchange
+  static constexpr uint32_t OFF_STG = STAGES * STAGE_BYTES;
+  static constexpr uint32_t OFF_RED = OFF_STG;
+  static constexpr uint32_t OFF_BAR = OFF_STG + EPI_WARPS * STG_WARP;
   static constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 /*barriers*/ + 1024 /*align*/;
 };
+static_assert(Layout::SMEM_BYTES <= 232448, "shared memory per CTA");
 
 struct Params {
   const float* a_s;
@@ -122,6 +128,16 @@ FD_DEV void store_row64(void* c, int64_t row_off, int n_start, int N, const floa
   }
 }
 
+template <int CDT>
+FD_DEV uint32_t pack2(float a, float b) {
+  if constexpr (CDT == FD_DT_BF16) {
+    return pack_bf16x2(a, b);
+  } else {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
 template <int BDT>
 FD_DEV float load_bias(const void* bias, int n) {
   if constexpr (BDT == FD_DT_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(bias)[n]);
@@ -151,11 +167,19 @@ FD_DEV void named_bar_sync(int id, int nthreads) {
 // GROUPED: two independent problems (p0 with tmA / tmB, p1 with tmLA / tmLB) in one
 // persistent launch; tiles [0, p0.ntiles) belong to p0, the rest to p1, so a small
 // problem (a 512-row text stream) fills the SMs the large one leaves idle.
+// tmC0 / tmC1: the output of p0 / p1 for the epilogues that write through TMA
+// (bf16 / f16 stores and the 1 x 128 code epilogues except the SiLU gate).
 template <int BMODE, int CDT, int BDT, int EPI, bool LORA, bool GROUPED>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmLB,
+                    const __grid_constant__ CUtensorMap tmC0, const __grid_constant__ CUtensorMap tmC1,
                     const Params p0, const Params p1) {
+  // the epilogue's rows leave through a shared-memory staging buffer and one TMA
+  // store per warp and round, so the promotion warps start the next tile while
+  // the stores drain (direct 16-byte stores of 128 rows x 256 columns took
+  // thousands of cycles per tile, during which no TMEM buffer was released)
+  constexpr bool TMA_OUT = (EPI == EPI_STORE && CDT != FD_DT_F32) || EPI == EPI_QUANT || EPI == EPI_GELU_TANH;
   static_assert(!(LORA && GROUPED), "LoRA slices and grouped problems share the second tensor maps");
   const int total_tiles = p0.ntiles + (GROUPED ? p1.ntiles : 0);
   using LY = Layout;
@@ -406,7 +430,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (EPI == EPI_SILU_GATE || n < p.N) acc[i] += load_bias<BDT < 0 ? FD_DT_F32 : BDT>(p.bias, n);
         }
       }
-      if constexpr (EPI == EPI_STORE) {
+      // staging buffer, first output row and output map of this warp
+      uint8_t* stg = smem + LY::OFF_STG + (warp - 2) * STG_WARP;
+      const int row0 = mb * BM + q * 32;
+      const CUtensorMap* mC = g1 ? &tmC1 : &tmC0;
+      if constexpr (EPI == EPI_STORE && TMA_OUT) {
+        // two rounds of 64 columns: bf16 / f16 rows of 128 B in the 128-byte
+        // swizzle the output tensor map expects (granule g of row j at g ^ (j & 7))
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          if (lane == 0) bulk_wait_read_all();  // the previous store has read the buffer
+          __syncwarp();
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            const int i = 64 * j + 8 * g;
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((g ^ (lane & 7)) << 4)) =
+                make_uint4(pack2<CDT>(acc[i], acc[i + 1]), pack2<CDT>(acc[i + 2], acc[i + 3]),
+                           pack2<CDT>(acc[i + 4], acc[i + 5]), pack2<CDT>(acc[i + 6], acc[i + 7]));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          // rows past M and columns past N are clipped by the tensor map
+          if (lane == 0 && ok && row0 < p.M && n_lo + 64 * j < p.N) {
+            tma_store_2d(stg, mC, n_lo + 64 * j, row0);
+            bulk_commit_group();
+          }
+        }
+      } else if constexpr (EPI == EPI_STORE) {
         if (ok && row_ok) {
           store_row64<CDT>(p.c, (int64_t)m * p.ldc, n_lo, p.N, *reinterpret_cast<float(*)[64]>(acc));
           store_row64<CDT>(p.c, (int64_t)m * p.ldc, n_lo + 64, p.N, *reinterpret_cast<float(*)[64]>(acc + 64));
@@ -443,19 +493,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         float amax = 0.f;
 #pragma unroll
         for (int i = 0; i < 128; ++i) amax = fmaxf(amax, fabsf(acc[i]));
-        if (ok && row_ok && n_lo < p.N) {
-          const float qm = quant_mult(amax);
-          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.c) + (int64_t)m * p.ldc + n_lo);
+        // 128 codes per row (128 B, 128-byte swizzle) through the staging buffer
+        const float qm = quant_mult(amax);
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
 #pragma unroll
-          for (int k = 0; k < 8; ++k)
-            dst[k] = make_uint4(quant4(acc[16 * k], acc[16 * k + 1], acc[16 * k + 2], acc[16 * k + 3], qm),
-                                quant4(acc[16 * k + 4], acc[16 * k + 5], acc[16 * k + 6], acc[16 * k + 7], qm),
-                                quant4(acc[16 * k + 8], acc[16 * k + 9], acc[16 * k + 10], acc[16 * k + 11], qm),
-                                quant4(acc[16 * k + 12], acc[16 * k + 13], acc[16 * k + 14], acc[16 * k + 15], qm));
-          p.c_s[(int64_t)m * p.ldcs + n_lo / 128] = dequant_scale(amax);
+        for (int k = 0; k < 8; ++k)
+          *reinterpret_cast<uint4*>(stg + lane * 128 + ((k ^ (lane & 7)) << 4)) =
+              make_uint4(quant4(acc[16 * k], acc[16 * k + 1], acc[16 * k + 2], acc[16 * k + 3], qm),
+                         quant4(acc[16 * k + 4], acc[16 * k + 5], acc[16 * k + 6], acc[16 * k + 7], qm),
+                         quant4(acc[16 * k + 8], acc[16 * k + 9], acc[16 * k + 10], acc[16 * k + 11], qm),
+                         quant4(acc[16 * k + 12], acc[16 * k + 13], acc[16 * k + 14], acc[16 * k + 15], qm));
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && ok && row0 < p.M && n_lo < p.N) {
+          tma_store_2d(stg, mC, n_lo, row0);
+          bulk_commit_group();
         }
+        if (ok && row_ok && n_lo < p.N) p.c_s[(int64_t)m * p.ldcs + n_lo / 128] = dequant_scale(amax);
       }
     }
+    if (TMA_OUT && lane == 0) bulk_wait_all();  // every output store has completed
   }
 
   tc_fence_before();
@@ -465,8 +523,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 }
 
 template <int BMODE, int CDT, int BDT, int EPI = EPI_STORE, bool LORA = false, bool GROUPED = false>
-static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t st,
-                  const CUtensorMap* tla = nullptr, const CUtensorMap* tlb = nullptr, const Params* p1 = nullptr) {
+static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p,
+                  cudaStream_t st, const CUtensorMap* tla = nullptr, const CUtensorMap* tlb = nullptr,
+                  const Params* p1 = nullptr, const CUtensorMap* tc1 = nullptr) {
   auto kern = gemm_fp8_kernel<BMODE, CDT, BDT, EPI, LORA, GROUPED>;
   constexpr uint32_t smem_bytes = Layout::SMEM_BYTES;
   static bool attr_done = false;  // per instantiation
@@ -477,43 +536,64 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
   }
   const int total = p.ntiles + (GROUPED ? p1->ntiles : 0);
   const int grid = total < num_sms() ? total : num_sms();
-  kern<<<grid, NUM_THREADS, smem_bytes, st>>>(ta, tb, tla ? *tla : ta, tlb ? *tlb : tb, p, p1 ? *p1 : p);
+  kern<<<grid, NUM_THREADS, smem_bytes, st>>>(ta, tb, tla ? *tla : ta, tlb ? *tlb : tb, tc, tc1 ? *tc1 : tc, p,
+                                              p1 ? *p1 : p);
   return check_launch("fp8_gemm_blockwise");
 }
 
 template <int EPI>
-static int launch_quant(int bdt, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
-                        cudaStream_t st) {
-  if (!p.bias) return launch<0, -1, -1, EPI>(ta, tb, p, st);
+static int launch_quant(int bdt, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                        const Params& p, cudaStream_t st) {
+  if (!p.bias) return launch<0, -1, -1, EPI>(ta, tb, tc, p, st);
   switch (bdt) {
-    case FD_DT_BF16: return launch<0, -1, FD_DT_BF16, EPI>(ta, tb, p, st);
-    case FD_DT_F16: return launch<0, -1, FD_DT_F16, EPI>(ta, tb, p, st);
-    case FD_DT_F32: return launch<0, -1, FD_DT_F32, EPI>(ta, tb, p, st);
+    case FD_DT_BF16: return launch<0, -1, FD_DT_BF16, EPI>(ta, tb, tc, p, st);
+    case FD_DT_F16: return launch<0, -1, FD_DT_F16, EPI>(ta, tb, tc, p, st);
+    case FD_DT_F32: return launch<0, -1, FD_DT_F32, EPI>(ta, tb, tc, p, st);
     default: return set_error(FD_ERR_ARG, "unsupported bias dtype");
   }
 }
 
 template <int BMODE, int CDT, bool LORA = false>
-static int launch_bias(int bdt, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
+static int launch_bias(int bdt, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p,
                        cudaStream_t st, const CUtensorMap* tla = nullptr, const CUtensorMap* tlb = nullptr) {
-  if (!p.bias) return launch<BMODE, CDT, -1, EPI_STORE, LORA>(ta, tb, p, st, tla, tlb);
+  if (!p.bias) return launch<BMODE, CDT, -1, EPI_STORE, LORA>(ta, tb, tc, p, st, tla, tlb);
   switch (bdt) {
-    case FD_DT_BF16: return launch<BMODE, CDT, FD_DT_BF16, EPI_STORE, LORA>(ta, tb, p, st, tla, tlb);
-    case FD_DT_F16: return launch<BMODE, CDT, FD_DT_F16, EPI_STORE, LORA>(ta, tb, p, st, tla, tlb);
-    case FD_DT_F32: return launch<BMODE, CDT, FD_DT_F32, EPI_STORE, LORA>(ta, tb, p, st, tla, tlb);
+    case FD_DT_BF16: return launch<BMODE, CDT, FD_DT_BF16, EPI_STORE, LORA>(ta, tb, tc, p, st, tla, tlb);
+    case FD_DT_F16: return launch<BMODE, CDT, FD_DT_F16, EPI_STORE, LORA>(ta, tb, tc, p, st, tla, tlb);
+    case FD_DT_F32: return launch<BMODE, CDT, FD_DT_F32, EPI_STORE, LORA>(ta, tb, tc, p, st, tla, tlb);
     default: return set_error(FD_ERR_ARG, "unsupported bias dtype");
   }
 }
 
 template <int BMODE, bool LORA = false>
-static int launch_c(int cdt, int bdt, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
-                    cudaStream_t st, const CUtensorMap* tla = nullptr, const CUtensorMap* tlb = nullptr) {
+static int launch_c(int cdt, int bdt, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                    const Params& p, cudaStream_t st, const CUtensorMap* tla = nullptr,
+                    const CUtensorMap* tlb = nullptr) {
   switch (cdt) {
-    case FD_DT_BF16: return launch_bias<BMODE, FD_DT_BF16, LORA>(bdt, ta, tb, p, st, tla, tlb);
-    case FD_DT_F16: return launch_bias<BMODE, FD_DT_F16, LORA>(bdt, ta, tb, p, st, tla, tlb);
-    case FD_DT_F32: return launch_bias<BMODE, FD_DT_F32, LORA>(bdt, ta, tb, p, st, tla, tlb);
+    case FD_DT_BF16: return launch_bias<BMODE, FD_DT_BF16, LORA>(bdt, ta, tb, tc, p, st, tla, tlb);
+    case FD_DT_F16: return launch_bias<BMODE, FD_DT_F16, LORA>(bdt, ta, tb, tc, p, st, tla, tlb);
+    case FD_DT_F32: return launch_bias<BMODE, FD_DT_F32, LORA>(bdt, ta, tb, tc, p, st, tla, tlb);
     default: return set_error(FD_ERR_ARG, "unsupported output dtype");
   }
+}
+
+// Output tensor map of the TMA-store epilogues: rows of ldc elements, 32-row
+// boxes of 128 bytes (64 bf16 / f16 or 128 e4m3 codes), 128-byte swizzle.
+// kind: FD_DT_BF16 / FD_DT_F16 / FD_DT_E4M3; f32 outputs are stored directly
+// and get a placeholder map (never read).
+static int encode_out(CUtensorMap* m, void* c, int kind, int64_t M, int64_t N, int64_t ldc, const CUtensorMap& dummy) {
+  if (kind == FD_DT_F32 || kind < 0) {
+    *m = dummy;
+    return FD_OK;
+  }
+  const bool codes = kind == FD_DT_E4M3;
+  const uint64_t dims[2] = {(uint64_t)N, (uint64_t)M};
+  const uint64_t strides[1] = {(uint64_t)ldc * (codes ? 1 : 2)};
+  const uint32_t box[2] = {codes ? 128u : 64u, 32u};
+  return encode_tiled(m,
+                      codes ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                            : (kind == FD_DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16),
+                      2, c, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 }  // namespace gemm
@@ -576,9 +656,12 @@ extern "C" int fd_fp8_gemm_blockwise(const void* a, const float* a_s, const void
   p.ntiles = p.ntm * p.ntn;
   p.kblocks = (int)(K / 128);
   cudaStream_t st = (cudaStream_t)stream;
-  if (b_layout == 0) return gemm::launch_c<0>(c_dtype, bias_dtype, ta, tb, p, st);
-  if (b_layout == 1) return gemm::launch_c<1>(c_dtype, bias_dtype, ta, tb, p, st);
-  return gemm::launch_c<2>(c_dtype, bias_dtype, ta, tb, p, st);
+  CUtensorMap tc;
+  const int rc = gemm::encode_out(&tc, c, c_dtype, M, N, N, ta);
+  if (rc) return rc;
+  if (b_layout == 0) return gemm::launch_c<0>(c_dtype, bias_dtype, ta, tb, tc, p, st);
+  if (b_layout == 1) return gemm::launch_c<1>(c_dtype, bias_dtype, ta, tb, tc, p, st);
+  return gemm::launch_c<2>(c_dtype, bias_dtype, ta, tb, tc, p, st);
 }
 
 // GEMM with a quantising epilogue (see the header of this file): act 0 requantises
@@ -632,9 +715,12 @@ static int gemm_quant_impl(const void* a, const float* a_s, const void* b, const
   p.ntiles = p.ntm * p.ntn;
   p.kblocks = (int)(K / 128);
   cudaStream_t st = (cudaStream_t)stream;
-  if (act == FD_ACT_NONE) return gemm::launch_quant<gemm::EPI_QUANT>(bias_dtype, ta, tb, p, st);
-  if (act == FD_ACT_GELU_TANH) return gemm::launch_quant<gemm::EPI_GELU_TANH>(bias_dtype, ta, tb, p, st);
-  return gemm::launch_quant<gemm::EPI_SILU_GATE>(bias_dtype, ta, tb, p, st);
+  CUtensorMap tc;
+  const int rc = gemm::encode_out(&tc, c, act == FD_ACT_SILU_GATE ? -1 : FD_DT_E4M3, M, N, ldc, ta);
+  if (rc) return rc;
+  if (act == FD_ACT_NONE) return gemm::launch_quant<gemm::EPI_QUANT>(bias_dtype, ta, tb, tc, p, st);
+  if (act == FD_ACT_GELU_TANH) return gemm::launch_quant<gemm::EPI_GELU_TANH>(bias_dtype, ta, tb, tc, p, st);
+  return gemm::launch_quant<gemm::EPI_SILU_GATE>(bias_dtype, ta, tb, tc, p, st);
 }
 
 extern "C" int fd_fp8_gemm_quant(const void* a, const float* a_s, const void* b, const float* b_s,
@@ -723,7 +809,10 @@ extern "C" int fd_fp8_gemm_blockwise_lora(const void* a, const float* a_s, const
   p.lora_slices = (int)(lora_k / 64);
   p.ldc = N;
   p.ldcs = N / 128;
-  return gemm::launch_c<0, true>(c_dtype, bias_dtype, ta, tb, p, (cudaStream_t)stream, &tla, &tlb);
+  CUtensorMap tc;
+  const int rc = gemm::encode_out(&tc, c, c_dtype, M, N, N, tla);
+  if (rc) return rc;
+  return gemm::launch_c<0, true>(c_dtype, bias_dtype, ta, tb, tc, p, (cudaStream_t)stream, &tla, &tlb);
 }
 
 // ---------------------------------------------------------------------------
@@ -731,7 +820,8 @@ extern "C" int fd_fp8_gemm_blockwise_lora(const void* a, const float* a_s, const
 // double-stream block, same epilogue): act FD_GEMM_STORE_BF16 stores bf16
 // (+ bias), FD_ACT_* quantise as fd_fp8_gemm_quant.  B stored (N, K); bias
 // FD_DT_BF16 or none.
-static int grouped_problem(const fd_gemm_problem& q, int act, CUtensorMap& ta, CUtensorMap& tb, gemm::Params& p) {
+static int grouped_problem(const fd_gemm_problem& q, int act, CUtensorMap& ta, CUtensorMap& tb, CUtensorMap& tc,
+                           gemm::Params& p) {
   const bool quant = act != FD_GEMM_STORE_BF16;
   FD_CHECK_ARG(q.M > 0 && q.N > 0 && q.K > 0 && q.K % 128 == 0, "bad shape");
   FD_CHECK_ARG(quant ? q.N % 128 == 0 : q.N % 16 == 0, "bad N");
@@ -769,7 +859,8 @@ static int grouped_problem(const fd_gemm_problem& q, int act, CUtensorMap& ta, C
   p.lora_slices = 0;
   p.ldc = q.N;
   p.ldcs = q.N / 128;
-  return FD_OK;
+  return gemm::encode_out(&tc, q.c, act == FD_GEMM_STORE_BF16 ? FD_DT_BF16 : (act == FD_ACT_SILU_GATE ? -1 : FD_DT_E4M3),
+                          q.M, q.N, q.N, ta);
 }
 
 extern "C" int fd_fp8_gemm_grouped2(const fd_gemm_problem* q0, const fd_gemm_problem* q1, int bias_dtype, int act,
@@ -778,16 +869,16 @@ extern "C" int fd_fp8_gemm_grouped2(const fd_gemm_problem* q0, const fd_gemm_pro
   FD_CHECK_ARG(act == FD_GEMM_STORE_BF16 || (act >= FD_ACT_NONE && act <= FD_ACT_SILU_GATE), "bad act");
   FD_CHECK_ARG((q0->bias == nullptr) == (q1->bias == nullptr), "both problems or neither take a bias");
   FD_CHECK_ARG(q0->bias == nullptr || bias_dtype == FD_DT_BF16, "grouped GEMM bias must be bf16");
-  CUtensorMap ta0, tb0, ta1, tb1;
+  CUtensorMap ta0, tb0, tc0, ta1, tb1, tc1;
   gemm::Params p0, p1;
-  int rc = grouped_problem(*q0, act, ta0, tb0, p0);
+  int rc = grouped_problem(*q0, act, ta0, tb0, tc0, p0);
   if (rc) return rc;
-  rc = grouped_problem(*q1, act, ta1, tb1, p1);
+  rc = grouped_problem(*q1, act, ta1, tb1, tc1, p1);
   if (rc) return rc;
   cudaStream_t st = (cudaStream_t)stream;
   const bool bias = q0->bias != nullptr;
   using namespace gemm;
-#define FD_G2(CD, BD, E) return launch<0, CD, BD, E, false, true>(ta0, tb0, p0, st, &ta1, &tb1, &p1)
+#define FD_G2(CD, BD, E) return launch<0, CD, BD, E, false, true>(ta0, tb0, tc0, p0, st, &ta1, &tb1, &p1, &tc1)
   if (act == FD_GEMM_STORE_BF16) {
     if (bias) FD_G2(FD_DT_BF16, FD_DT_BF16, EPI_STORE);
     FD_G2(FD_DT_BF16, -1, EPI_STORE);
