@@ -145,6 +145,31 @@ FD_DEV float load_bias(const void* bias, int n) {
   else return reinterpret_cast<const float*>(bias)[n];
 }
 
+// bias[n .. n + 8) as floats; bias 16-byte aligned, n a multiple of 8
+template <int BDT>
+FD_DEV void load_bias8(const void* bias, int n, float (&b)[8]) {
+  if constexpr (BDT == FD_DT_F32) {
+    const float4 u = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(bias) + n));
+    const float4 v = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(bias) + n + 4));
+    b[0] = u.x; b[1] = u.y; b[2] = u.z; b[3] = u.w; b[4] = v.x; b[5] = v.y; b[6] = v.z; b[7] = v.w;
+  } else {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(bias) + n));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if constexpr (BDT == FD_DT_BF16) {
+        b[2 * j] = __uint_as_float(w[j] << 16);
+        b[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+      } else {
+        const __half2 h = *reinterpret_cast<const __half2*>(&w[j]);
+        const float2 f = __half22float2(h);
+        b[2 * j] = f.x;
+        b[2 * j + 1] = f.y;
+      }
+    }
+  }
+}
+
 // Wait that ignores the abort flag: used only to drain this thread's own
 // in-flight asynchronous work before the CTA exits.
 FD_DEV void drain_wait(uint64_t* bar, uint32_t parity) {
@@ -424,10 +449,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
       if (BDT >= 0 && p.bias) {
+        // eight columns per 16-byte load (32 bytes for f32); the scalar path covers
+        // a bias that is not 16-byte aligned and the columns of a partial last tile
+        constexpr int BT = BDT < 0 ? FD_DT_F32 : BDT;
+        const bool vec = (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0;
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          const int n = (i < 64 ? n_lo : n_hi) + (i & 63);
-          if (EPI == EPI_SILU_GATE || n < p.N) acc[i] += load_bias<BDT < 0 ? FD_DT_F32 : BDT>(p.bias, n);
+        for (int c8 = 0; c8 < 16; ++c8) {
+          const int n = (c8 < 8 ? n_lo : n_hi) + (c8 & 7) * 8;
+          float b[8];
+          if (vec && (EPI == EPI_SILU_GATE || n + 8 <= p.N)) {
+            load_bias8<BT>(p.bias, n, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) b[j] = (EPI == EPI_SILU_GATE || n + j < p.N) ? load_bias<BT>(p.bias, n + j) : 0.f;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[8 * c8 + j] += b[j];
         }
       }
       // staging buffer, first output row and output map of this warp
@@ -486,24 +523,49 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       } else {
         // EPI_QUANT / EPI_GELU_TANH: this thread's 128 columns are one whole output group
-        if (EPI == EPI_GELU_TANH) {
-#pragma unroll
-          for (int i = 0; i < 128; ++i) acc[i] = gelu_tanh(round_to_bf16(acc[i]));
-        }
-        float amax = 0.f;
-#pragma unroll
-        for (int i = 0; i < 128; ++i) amax = fmaxf(amax, fabsf(acc[i]));
         // 128 codes per row (128 B, 128-byte swizzle) through the staging buffer
-        const float qm = quant_mult(amax);
-        if (lane == 0) bulk_wait_read_all();
-        __syncwarp();
+        float amax = 0.f;
+        float qm;
+        if constexpr (EPI == EPI_GELU_TANH) {
+          // the GELU input is the accumulator rounded to bf16: packed two per
+          // register, the 64 freed registers let many GELUs run at once; the GELU
+          // is evaluated twice (absmax pass, then codes) instead of being kept
+          uint32_t xb[64];
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          *reinterpret_cast<uint4*>(stg + lane * 128 + ((k ^ (lane & 7)) << 4)) =
-              make_uint4(quant4(acc[16 * k], acc[16 * k + 1], acc[16 * k + 2], acc[16 * k + 3], qm),
-                         quant4(acc[16 * k + 4], acc[16 * k + 5], acc[16 * k + 6], acc[16 * k + 7], qm),
-                         quant4(acc[16 * k + 8], acc[16 * k + 9], acc[16 * k + 10], acc[16 * k + 11], qm),
-                         quant4(acc[16 * k + 12], acc[16 * k + 13], acc[16 * k + 14], acc[16 * k + 15], qm));
+          for (int i = 0; i < 64; ++i) xb[i] = pack_bf16x2(acc[2 * i], acc[2 * i + 1]);
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            amax = fmaxf(amax, fmaxf(fabsf(gelu_tanh(bf16_bits_to_f32(xb[i] & 0xffffu))),
+                                     fabsf(gelu_tanh(bf16_bits_to_f32(xb[i] >> 16)))));
+          qm = quant_mult(amax);
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            float g[16];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              g[2 * j] = gelu_tanh(bf16_bits_to_f32(xb[8 * k + j] & 0xffffu));
+              g[2 * j + 1] = gelu_tanh(bf16_bits_to_f32(xb[8 * k + j] >> 16));
+            }
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((k ^ (lane & 7)) << 4)) =
+                make_uint4(quant4(g[0], g[1], g[2], g[3], qm), quant4(g[4], g[5], g[6], g[7], qm),
+                           quant4(g[8], g[9], g[10], g[11], qm), quant4(g[12], g[13], g[14], g[15], qm));
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 128; ++i) amax = fmaxf(amax, fabsf(acc[i]));
+          qm = quant_mult(amax);
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((k ^ (lane & 7)) << 4)) =
+                make_uint4(quant4(acc[16 * k], acc[16 * k + 1], acc[16 * k + 2], acc[16 * k + 3], qm),
+                           quant4(acc[16 * k + 4], acc[16 * k + 5], acc[16 * k + 6], acc[16 * k + 7], qm),
+                           quant4(acc[16 * k + 8], acc[16 * k + 9], acc[16 * k + 10], acc[16 * k + 11], qm),
+                           quant4(acc[16 * k + 12], acc[16 * k + 13], acc[16 * k + 14], acc[16 * k + 15], qm));
+        }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0 && ok && row0 < p.M && n_lo < p.N) {
