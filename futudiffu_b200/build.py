@@ -55,11 +55,24 @@ def _headers_mtime() -> float:
     return max((h.stat().st_mtime for h in hs), default=0.0)
 
 
+# Files compiled as a whole program (no relocatable device code): ptxas applies
+# the per-warp register limits of setmaxnreg only there (the deferred-GELU FP8
+# GEMM gives its promotion warps 168 registers out of a 128-per-thread launch).
+# Such a file references no other file's device variables (FD_WHOLE_PROGRAM).
+WHOLE_PROGRAM = {"gemm_fp8.cu"}
+
+
+def _flags(src: Path) -> list[str]:
+    if src.name in WHOLE_PROGRAM:
+        return [f for f in NVCC_FLAGS if f != "-rdc=true"] + ["-DFD_WHOLE_PROGRAM"]
+    return NVCC_FLAGS
+
+
 def _compile(src: Path, verbose: bool, force: bool, hmtime: float) -> Path:
     obj = BUILD / (src.stem + ".o")
     if not force and obj.exists() and obj.stat().st_mtime >= max(src.stat().st_mtime, hmtime):
         return obj
-    cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
+    cmd = [nvcc(), *ARCH, *_flags(src), "-c", str(src), "-o", str(obj)]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), flush=True)

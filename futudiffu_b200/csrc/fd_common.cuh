@@ -28,8 +28,15 @@
 
 namespace fd {
 
-// Device-wide status word (bitwise OR of FD_STATUS_* flags).
+// Device-wide status word (bitwise OR of FD_STATUS_* flags).  A file compiled
+// as a whole program (no relocatable device code, FD_WHOLE_PROGRAM defined)
+// cannot reference another file's device variable, so it keeps its own word,
+// which fd_get_status() reads together with this one.
+#ifdef FD_WHOLE_PROGRAM
+static __device__ unsigned int g_status = 0;
+#else
 extern __device__ unsigned int g_status;
+#endif
 
 FD_DEV uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -25,6 +25,10 @@ int encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void*
                  const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                  CUtensorMapSwizzle swizzle);
 
+// Status word of the FP8 GEMM's translation unit (compiled as a whole program,
+// see fd_common.cuh): reads it into *out and clears it when `clear` is set.
+int gemm_status(unsigned int* out, int clear);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 inline bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; }
 inline bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3) == 0; }

@@ -54,9 +54,7 @@ namespace gemm {
 
 constexpr int BM = 128, BN = 256, BK = 128;  // BN: MMA / TMEM columns per tile
 constexpr int NTBUF = 2;                       // TMEM slice buffers (2 x 256 columns)
-constexpr int STAGES = 4;
-constexpr int NUM_THREADS = 320;
-constexpr int EPI_WARPS = 8;
+constexpr int EPI_WARPS = 8;                   // promotion warps
 constexpr int GROUP_M = 16;                    // row tiles per rasterisation group
 constexpr uint32_t A_BYTES = BM * BK;          // 16 KiB
 constexpr uint32_t STAGE_BYTES = BM * BK + BN * BK;  // 48 KiB
@@ -65,15 +63,78 @@ enum { EPI_STORE = 0, EPI_QUANT = 1, EPI_GELU_TANH = 2, EPI_SILU_GATE = 3 };
 
 constexpr uint32_t STG_WARP = 32 * 128;  // output staging per epilogue warp: 32 rows x 128 B
 
-struct Layout {
-  // TMA-store epilogues stage their rows here; the SiLU-gate epilogue (direct
-  // stores) uses the same bytes for its [2][2][128] f32 max exchange
+// Per-epilogue configuration.  Every epilogue but GELU-tanh runs on 10 warps:
+// warp 0 TMA producer, warp 1 MMA issuer, warps 2-9 promotion + epilogue, with
+// a 4-stage operand ring.  GELU-tanh (deferred): its epilogue costs about as
+// much issue time per tile as the promotion of all K slices, and on the
+// promotion warps it left the tensor core idle for that long, so it runs on
+// four more warps instead: the promotion warps (4-11) hand the bf16-rounded
+// tile to warps 12-15 through shared memory and go on with the next tile while
+// those evaluate GELU(tanh) and requantise.  The 64 KiB tile copy leaves room
+// for 3 operand stages.
+template <int EPI>
+struct Cfg {
+  static constexpr bool DEFER = EPI == EPI_GELU_TANH;
+  static constexpr int STAGES = DEFER ? 3 : 4;
+  static constexpr int THREADS = DEFER ? 512 : 320;
+  static constexpr int PROMO_WARP0 = DEFER ? 4 : 2;  // first promotion warp
+  static constexpr int GELU_WARP0 = 12;              // deferred GELU warps 12-15
+  // non-deferred: TMA-store staging (32 rows x 128 B per promotion warp), whose
+  // bytes the SiLU-gate epilogue uses for its [2][2][128] f32 max exchange;
+  // deferred: the bf16 tile copy, 128 rows x 256 values (512 B per row)
   static constexpr uint32_t OFF_STG = STAGES * STAGE_BYTES;
   static constexpr uint32_t OFF_RED = OFF_STG;
-  static constexpr uint32_t OFF_BAR = OFF_STG + EPI_WARPS * STG_WARP;
+  static constexpr uint32_t STG_BYTES = DEFER ? BM * BN * 2 : EPI_WARPS * STG_WARP;
+  static constexpr uint32_t OFF_BAR = OFF_STG + STG_BYTES;
   static constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 /*barriers*/ + 1024 /*align*/;
+  static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 };
-static_assert(Layout::SMEM_BYTES <= 232448, "shared memory per CTA");
+
+// Register split of the deferred-GELU kernel, launched with 128 registers per
+// thread x 512 threads (the whole register file): warps 0-3 (producer, MMA
+// issuer, two idle) keep 40, the eight promotion warps take 168 (their 128 fp32
+// accumulators), the four GELU warps keep 104:
+// 128 x 40 + 256 x 168 + 128 x 104 = 61440 registers, within the launch's
+// 65536 (and within 512 x 120, should the launch count ever be 120).
+template <int N>
+FD_DEV void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+FD_DEV void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// Maximum of the eight bf16 values packed in u.
+FD_DEV float max8_bf16(const uint4& u) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) m = fmaxf(m, fmaxf(bf16_bits_to_f32(w[j] & 0xffffu), bf16_bits_to_f32(w[j] >> 16)));
+  return m;
+}
+
+// |GELU(tanh)| maximum of the eight bf16 values packed in u (low half first).
+FD_DEV float gelu8_absmax(const uint4& u) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  float m = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    m = fmaxf(m, fmaxf(fabsf(gelu_tanh(bf16_bits_to_f32(w[j] & 0xffffu))), fabsf(gelu_tanh(bf16_bits_to_f32(w[j] >> 16)))));
+  return m;
+}
+
+// e4m3 codes of GELU(tanh) of the eight bf16 values in u, multiplied by qm.
+FD_DEV uint2 gelu8_codes(const uint4& u, float qm) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  float g[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    g[2 * j] = gelu_tanh(bf16_bits_to_f32(w[j] & 0xffffu));
+    g[2 * j + 1] = gelu_tanh(bf16_bits_to_f32(w[j] >> 16));
+  }
+  return make_uint2(quant4(g[0], g[1], g[2], g[3], qm), quant4(g[4], g[5], g[6], g[7], qm));
+}
 
 struct Params {
   const float* a_s;
@@ -195,7 +256,7 @@ FD_DEV void named_bar_sync(int id, int nthreads) {
 // tmC0 / tmC1: the output of p0 / p1 for the epilogues that write through TMA
 // (bf16 / f16 stores and the 1 x 128 code epilogues except the SiLU gate).
 template <int BMODE, int CDT, int BDT, int EPI, bool LORA, bool GROUPED>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(Cfg<EPI>::THREADS, 1)
     gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmLB,
                     const __grid_constant__ CUtensorMap tmC0, const __grid_constant__ CUtensorMap tmC1,
@@ -204,20 +265,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   // store per warp and round, so the promotion warps start the next tile while
   // the stores drain (direct 16-byte stores of 128 rows x 256 columns took
   // thousands of cycles per tile, during which no TMEM buffer was released)
-  constexpr bool TMA_OUT = (EPI == EPI_STORE && CDT != FD_DT_F32) || EPI == EPI_QUANT || EPI == EPI_GELU_TANH;
+  constexpr bool TMA_OUT = (EPI == EPI_STORE && CDT != FD_DT_F32) || EPI == EPI_QUANT;
+  using CF = Cfg<EPI>;
+  constexpr int STAGES = CF::STAGES;
   static_assert(!(LORA && GROUPED), "LoRA slices and grouped problems share the second tensor maps");
   const int total_tiles = p0.ntiles + (GROUPED ? p1.ntiles : 0);
-  using LY = Layout;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // stage s: A tile at s * STAGE_BYTES, B tile (256 rows) right after it
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::OFF_BAR);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + CF::OFF_BAR);
   uint64_t* full = bars;                   // [STAGES]
   uint64_t* empty = bars + STAGES;         // [STAGES]
   uint64_t* tfull = bars + 2 * STAGES;     // [NTBUF]
   uint64_t* tempty = tfull + NTBUF;        // [NTBUF]
   uint64_t* drain = tempty + NTBUF;        // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* hfull = drain + 1;             // deferred GELU: tile copy written
+  uint64_t* hempty = hfull + 1;            // deferred GELU: tile copy read
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(hempty + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   constexpr int B_MN = BMODE == 1 ? 1 : 0;
@@ -233,6 +297,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&tempty[i], EPI_WARPS);
     }
     mbar_init(drain, 1);
+    mbar_init(hfull, EPI_WARPS * 32);
+    mbar_init(hempty, 128);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -251,6 +317,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    if constexpr (CF::DEFER) reg_dealloc<40>();
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
@@ -303,6 +370,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    if constexpr (CF::DEFER) reg_dealloc<40>();
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc(/*c F32*/ 1, /*E4M3*/ 0, 0, /*a K-major*/ 0, B_MN, BM, BN);
       constexpr uint32_t idesc_lora = make_idesc(/*c F32*/ 1, /*BF16*/ 1, 1, 0, 0, BM, BN);
@@ -345,16 +413,71 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_commit(drain);
       drain_wait(drain, 0);
     }
+  } else if (CF::DEFER && warp >= CF::GELU_WARP0) {
+    // ------------------------------------------------------------ deferred GELU + requant
+    // Thread t owns row t of the tile: per tile it reads the promotion warps' bf16
+    // copy of its row (two 1 x 128 output groups) from shared memory and stores
+    // the e4m3 codes of GELU(tanh) and the group scale.  The group absmax needs
+    // no GELU per value: GELU(tanh) is increasing above x = -0.75 and |GELU| <=
+    // 0.17004 below it, so whenever GELU(max x) > 0.171 it is the absmax (the
+    // computed GELU of bf16 inputs keeps that order: neighbouring inputs differ by
+    // 2^-8 relative, far above fp32 rounding); otherwise every value is
+    // evaluated as before.  The codes then take one GELU per value.
+    reg_dealloc<104>();
+    const int t = (warp - CF::GELU_WARP0) * 32 + lane;
+    const uint8_t* hrow = smem + CF::OFF_STG + t * 512;
+    uint32_t nt = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++nt) {
+      const bool g1 = GROUPED && tile >= p0.ntiles;
+      const Params& p = g1 ? p1 : p0;
+      int mb, nb;
+      tile_coords(p, g1 ? tile - p0.ntiles : tile, mb, nb);
+      ok = ok && mbar_wait(hfull, nt & 1, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      const int m = mb * BM + t;
+      const bool row_ok = m < p.M;
+#pragma unroll 1
+      for (int g = 0; g < 2; ++g) {
+        const int n0 = nb * BN + g * 128;
+        if (!ok || n0 >= p.N) continue;
+        float xmax = -INFINITY;
+#pragma unroll 4
+        for (int j = 0; j < 16; ++j)
+          xmax = fmaxf(xmax, max8_bf16(*reinterpret_cast<const uint4*>(hrow + (((g * 16 + j) ^ (t & 7)) << 4))));
+        float amax = gelu_tanh(xmax);
+        if (!(amax > 0.171f)) {
+          amax = 0.f;
+#pragma unroll 2
+          for (int j = 0; j < 16; ++j)
+            amax = fmaxf(amax, gelu8_absmax(*reinterpret_cast<const uint4*>(hrow + (((g * 16 + j) ^ (t & 7)) << 4))));
+        }
+        const float qm = quant_mult(amax);
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.c) + (int64_t)m * p.ldc + n0);
+#pragma unroll 2
+        for (int j = 0; j < 16; j += 2) {
+          const uint2 lo = gelu8_codes(*reinterpret_cast<const uint4*>(hrow + (((g * 16 + j) ^ (t & 7)) << 4)), qm);
+          const uint2 hi = gelu8_codes(*reinterpret_cast<const uint4*>(hrow + (((g * 16 + j + 1) ^ (t & 7)) << 4)), qm);
+          if (row_ok) dst[j >> 1] = make_uint4(lo.x, lo.y, hi.x, hi.y);
+        }
+        if (row_ok) p.c_s[(int64_t)m * p.ldcs + n0 / 128] = dequant_scale(amax);
+      }
+      mbar_arrive(hempty);
+    }
+  } else if (CF::DEFER && warp < CF::PROMO_WARP0) {
+    // warps 2-3 of the deferred-GELU kernel have no role
+    reg_dealloc<40>();
   } else {
     // ------------------------------------------------------------ promotion + epilogue
     // Thread (q, h): row q * 32 + lane; TMEM columns [128 h, 128 h + 128) of the
     // 256-column accumulator (EPI_SILU_GATE: w1 columns [64 h, 64 h + 64) and the
     // matching w3 columns 128 + [64 h, 64 h + 64)).
+    if constexpr (CF::DEFER) reg_alloc<168>();
     const int q = warp & 3;             // TMEM lane quadrant this warp may access
-    const int h = (warp - 2) >> 2;      // column half
+    const int h = (warp - CF::PROMO_WARP0) >> 2;  // column half
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const int r = q * 32 + lane;        // row within the tile
-    float* red = reinterpret_cast<float*>(smem + LY::OFF_RED);  // [parity][half][128]
+    float* red = reinterpret_cast<float*>(smem + CF::OFF_RED);  // [parity][half][128]
     uint32_t it = 0, nt = 0;
     bool ok = true;
     // A thread whose wait timed out keeps walking the tiles (skipping the work)
@@ -468,10 +591,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
       // staging buffer, first output row and output map of this warp
-      uint8_t* stg = smem + LY::OFF_STG + (warp - 2) * STG_WARP;
+      uint8_t* stg = smem + CF::OFF_STG + (warp - CF::PROMO_WARP0) * STG_WARP;
       const int row0 = mb * BM + q * 32;
       const CUtensorMap* mC = g1 ? &tmC1 : &tmC0;
-      if constexpr (EPI == EPI_STORE && TMA_OUT) {
+      if constexpr (CF::DEFER) {
+        // the bf16-rounded tile (the GELU input) to the GELU warps: row r, this
+        // thread's 128 columns as 16-byte chunks h * 16 + j, chunk index XOR
+        // (r & 7) so that the 32 rows of a warp spread over the banks
+        const bool free = mbar_wait(hempty, (nt & 1) ^ 1, abort_flag);  // previous copy read
+        uint8_t* hrow = smem + CF::OFF_STG + r * 512;
+        if (ok && free) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int i = 8 * j;
+            *reinterpret_cast<uint4*>(hrow + (((h * 16 + j) ^ (r & 7)) << 4)) =
+                make_uint4(pack_bf16x2(acc[i], acc[i + 1]), pack_bf16x2(acc[i + 2], acc[i + 3]),
+                           pack_bf16x2(acc[i + 4], acc[i + 5]), pack_bf16x2(acc[i + 6], acc[i + 7]));
+          }
+        }
+        mbar_arrive(hfull);
+      } else if constexpr (EPI == EPI_STORE && TMA_OUT) {
         // two rounds of 64 columns: bf16 / f16 rows of 128 B in the 128-byte
         // swizzle the output tensor map expects (granule g of row j at g ^ (j & 7))
 #pragma unroll
@@ -522,50 +661,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (h == 0) p.c_s[(int64_t)m * p.ldcs + nb] = dequant_scale(amax);
         }
       } else {
-        // EPI_QUANT / EPI_GELU_TANH: this thread's 128 columns are one whole output group
-        // 128 codes per row (128 B, 128-byte swizzle) through the staging buffer
+        // EPI_QUANT: this thread's 128 columns are one whole output group, 128 codes per row (128 B, 128-byte swizzle) through the staging buffer
         float amax = 0.f;
-        float qm;
-        if constexpr (EPI == EPI_GELU_TANH) {
-          // the GELU input is the accumulator rounded to bf16: packed two per
-          // register, the 64 freed registers let many GELUs run at once; the GELU
-          // is evaluated twice (absmax pass, then codes) instead of being kept
-          uint32_t xb[64];
 #pragma unroll
-          for (int i = 0; i < 64; ++i) xb[i] = pack_bf16x2(acc[2 * i], acc[2 * i + 1]);
+        for (int i = 0; i < 128; ++i) amax = fmaxf(amax, fabsf(acc[i]));
+        const float qm = quant_mult(amax);
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
-            amax = fmaxf(amax, fmaxf(fabsf(gelu_tanh(bf16_bits_to_f32(xb[i] & 0xffffu))),
-                                     fabsf(gelu_tanh(bf16_bits_to_f32(xb[i] >> 16)))));
-          qm = quant_mult(amax);
-          if (lane == 0) bulk_wait_read_all();
-          __syncwarp();
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            float g[16];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              g[2 * j] = gelu_tanh(bf16_bits_to_f32(xb[8 * k + j] & 0xffffu));
-              g[2 * j + 1] = gelu_tanh(bf16_bits_to_f32(xb[8 * k + j] >> 16));
-            }
-            *reinterpret_cast<uint4*>(stg + lane * 128 + ((k ^ (lane & 7)) << 4)) =
-                make_uint4(quant4(g[0], g[1], g[2], g[3], qm), quant4(g[4], g[5], g[6], g[7], qm),
-                           quant4(g[8], g[9], g[10], g[11], qm), quant4(g[12], g[13], g[14], g[15], qm));
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 128; ++i) amax = fmaxf(amax, fabsf(acc[i]));
-          qm = quant_mult(amax);
-          if (lane == 0) bulk_wait_read_all();
-          __syncwarp();
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-            *reinterpret_cast<uint4*>(stg + lane * 128 + ((k ^ (lane & 7)) << 4)) =
-                make_uint4(quant4(acc[16 * k], acc[16 * k + 1], acc[16 * k + 2], acc[16 * k + 3], qm),
-                           quant4(acc[16 * k + 4], acc[16 * k + 5], acc[16 * k + 6], acc[16 * k + 7], qm),
-                           quant4(acc[16 * k + 8], acc[16 * k + 9], acc[16 * k + 10], acc[16 * k + 11], qm),
-                           quant4(acc[16 * k + 12], acc[16 * k + 13], acc[16 * k + 14], acc[16 * k + 15], qm));
-        }
+        for (int k = 0; k < 8; ++k)
+          *reinterpret_cast<uint4*>(stg + lane * 128 + ((k ^ (lane & 7)) << 4)) =
+              make_uint4(quant4(acc[16 * k], acc[16 * k + 1], acc[16 * k + 2], acc[16 * k + 3], qm),
+                         quant4(acc[16 * k + 4], acc[16 * k + 5], acc[16 * k + 6], acc[16 * k + 7], qm),
+                         quant4(acc[16 * k + 8], acc[16 * k + 9], acc[16 * k + 10], acc[16 * k + 11], qm),
+                         quant4(acc[16 * k + 12], acc[16 * k + 13], acc[16 * k + 14], acc[16 * k + 15], qm));
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0 && ok && row0 < p.M && n_lo < p.N) {
@@ -589,7 +698,7 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
                   cudaStream_t st, const CUtensorMap* tla = nullptr, const CUtensorMap* tlb = nullptr,
                   const Params* p1 = nullptr, const CUtensorMap* tc1 = nullptr) {
   auto kern = gemm_fp8_kernel<BMODE, CDT, BDT, EPI, LORA, GROUPED>;
-  constexpr uint32_t smem_bytes = Layout::SMEM_BYTES;
+  constexpr uint32_t smem_bytes = Cfg<EPI>::SMEM_BYTES;
   static bool attr_done = false;  // per instantiation
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
@@ -598,7 +707,7 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
   }
   const int total = p.ntiles + (GROUPED ? p1->ntiles : 0);
   const int grid = total < num_sms() ? total : num_sms();
-  kern<<<grid, NUM_THREADS, smem_bytes, st>>>(ta, tb, tla ? *tla : ta, tlb ? *tlb : tb, tc, tc1 ? *tc1 : tc, p,
+  kern<<<grid, Cfg<EPI>::THREADS, smem_bytes, st>>>(ta, tb, tla ? *tla : ta, tlb ? *tlb : tb, tc, tc1 ? *tc1 : tc, p,
                                               p1 ? *p1 : p);
   return check_launch("fp8_gemm_blockwise");
 }
@@ -659,6 +768,18 @@ static int encode_out(CUtensorMap* m, void* c, int kind, int64_t M, int64_t N, i
 }
 
 }  // namespace gemm
+
+int gemm_status(unsigned int* out, int clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_status, sizeof(*out));
+  if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "fd_get_status (gemm): %s", cudaGetErrorString(e));
+  if (clear) {
+    const unsigned int z = 0;
+    e = cudaMemcpyToSymbol(g_status, &z, sizeof(z));
+    if (e != cudaSuccess) return set_error(FD_ERR_CUDA, "fd_get_status (gemm): %s", cudaGetErrorString(e));
+  }
+  return FD_OK;
+}
+
 }  // namespace fd
 
 using namespace fd;

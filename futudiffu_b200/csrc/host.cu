@@ -104,6 +104,9 @@ extern "C" int fd_get_status(unsigned int* out, int clear) {
     e = cudaMemcpyToSymbol(fd::g_status, &z, sizeof(z));
     if (e != cudaSuccess) return fd::set_error(FD_ERR_CUDA, "fd_get_status: %s", cudaGetErrorString(e));
   }
-  *out = v;
+  unsigned int g = 0;
+  const int rc = fd::gemm_status(&g, clear);
+  if (rc) return rc;
+  *out = v | g;
   return FD_OK;
 }
