@@ -494,10 +494,12 @@ def run_dit_reference(args, world, rank):
     return 0
 
 
-def time_gemm(dev, shape: str, steps: int, warmup: int) -> list[float]:
+def time_gemm(dev, shape: str, steps: int, warmup: int, epilogue: str = "bf16") -> list[float]:
     """CUDA-event durations (ms) of ``steps`` FP8 block-GEMM launches at one of
-    GEMM_SHAPES (bf16 output), with a 256 MiB write between launches so that every
-    launch reads its operands from HBM (the operands are smaller than L2)."""
+    GEMM_SHAPES, with a 256 MiB write between launches so that every launch reads
+    its operands from HBM (the operands of the smaller shapes fit in L2).
+    ``epilogue``: "bf16" output, or "gelu" (GELU(tanh) + 1 x 128 e4m3 requant, the
+    MMDiT MLP-in epilogue)."""
     from futudiffu_b200 import _lib as L
     from futudiffu_b200.fp8 import quantize_fp8_blockwise_cuda
     from futudiffu_b200.fp8_kernels import fp8_act_quant
@@ -508,13 +510,21 @@ def time_gemm(dev, shape: str, steps: int, warmup: int) -> list[float]:
     w = (torch.randn(N, K, generator=g) * 0.02).to(dev)
     w8, ws = quantize_fp8_blockwise_cuda(w)
     a8, a_s = fp8_act_quant(x)
-    c = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    if epilogue == "gelu":
+        c = torch.empty(M, N, dtype=torch.uint8, device=dev)
+        c_s = torch.empty(M, N // 128, dtype=torch.float32, device=dev)
 
-    def gemm():
-        L.call("fd_fp8_gemm_blockwise", L.ptr(a8), L.ptr(a_s), L.ptr(w8), L.ptr(ws), None, 0, L.ptr(c),
-               L.DT_BF16, M, N, K, 0, L.stream_ptr(dev))
+        def gemm():
+            L.call("fd_fp8_gemm_quant", L.ptr(a8), L.ptr(a_s), L.ptr(w8), L.ptr(ws), None, 0, L.ptr(c), L.ptr(c_s),
+                   M, N, K, L.ACT_GELU_TANH, L.stream_ptr(dev))
+    else:
+        c = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+
+        def gemm():
+            L.call("fd_fp8_gemm_blockwise", L.ptr(a8), L.ptr(a_s), L.ptr(w8), L.ptr(ws), None, 0, L.ptr(c),
+                   L.DT_BF16, M, N, K, 0, L.stream_ptr(dev))
 
     for _ in range(warmup):
         gemm()
@@ -1130,7 +1140,10 @@ def run_video(args, world, rank, local):
     return 0
 
 
-GEMM_SHAPES = {"config1": (2048, 3072, 3072), "ref_qkv": (8576, 11520, 3840), "ref_w2": (8576, 3840, 10240)}
+# config 1, the reference benchmark's Z-Image QKV / FFN-out shapes, and the config-4
+# MLP-in linear at one sample (4608 tokens) and at the batch of 8
+GEMM_SHAPES = {"config1": (2048, 3072, 3072), "ref_qkv": (8576, 11520, 3840), "ref_w2": (8576, 3840, 10240),
+               "dit_mlp_in": (4608, 12288, 3072), "dit_mlp_in_b8": (36864, 12288, 3072)}
 
 
 PACKED_METRIC = "packed multi-image forward tokens/s (Z-Image-class blocks, 3840 hidden, 30 heads, 4288-token bin)"
@@ -1329,7 +1342,7 @@ def run_gemm(args, world, rank, local):
     torch.cuda.set_device(dev)
     M, N, K = GEMM_SHAPES[args.gemm_shape]
     with ClockSampler(local) as clocks:
-        times = time_gemm(dev, args.gemm_shape, args.steps, args.warmup)
+        times = time_gemm(dev, args.gemm_shape, args.steps, args.warmup, args.gemm_epilogue)
     ms = max_over_ranks(statistics.mean(times), world, dev)
     check_status()
     flops = 2.0 * M * N * K
@@ -1342,7 +1355,8 @@ def run_gemm(args, world, rank, local):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp8 e4m3 (1x128 / 128x128 f32 scales)",
             "data": "synthetic",
-            "config": {"workload": f"gemm_{args.gemm_shape}", "M": M, "N": N, "K": K, "l2": "flushed"},
+            "config": {"workload": f"gemm_{args.gemm_shape}", "M": M, "N": N, "K": K, "l2": "flushed",
+                       "epilogue": "GELU(tanh) + 1x128 e4m3 requant" if args.gemm_epilogue == "gelu" else "bf16"},
             "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
                          "frac": tf / peak, "traffic": GEMM_TRAFFIC_BYTES.get(args.gemm_shape),
                          "peak_source": f"2 x {pk['source']} bf16 dense: fp8 dense rate is twice bf16"},
@@ -1454,6 +1468,8 @@ def main(argv=None) -> int:
                          "attention = config 2; gemm = config 1; packed = the reference's packed "
                          "4288-token bin through Z-Image-class JointTransformerBlocks")
     ap.add_argument("--gemm-shape", choices=sorted(GEMM_SHAPES), default="config1")
+    ap.add_argument("--gemm-epilogue", choices=["bf16", "gelu"], default="bf16",
+                    help="gemm: bf16 output or the GELU(tanh) + 1x128 requant epilogue")
     ap.add_argument("--layers", type=int, default=30, help="packed: JointTransformerBlocks in the stack")
     ap.add_argument("--no-sub", action="store_true",
                     help="dit: skip the config-1 GEMM / config-2 attention sub-measurements")

@@ -266,3 +266,38 @@ def test_gemm_grouped2_equals_separate_launches(cuda_device, act):
             ref = FK.fp8_gemm_silu_gate_quant(a8, a_s, b8, bs)
         assert torch.equal(g[0].view(torch.uint8), ref[0].view(torch.uint8))
         assert torch.equal(g[1].reshape(ref[1].shape), ref[1])
+
+
+@pytest.mark.parametrize("grouped", [False, True])
+def test_gemm_gelu_absmax_shortcut_and_fallback(cuda_device, grouped):
+    """The GELU-tanh epilogue takes a group's absmax from GELU(max x) when that
+    exceeds 0.171 and evaluates every value otherwise.  Column groups are pushed
+    through a bias into every regime (all strongly negative, around the GELU
+    minimum at -0.75, tiny, mixed, large) and rows are scaled down to tiny
+    magnitudes, so both paths run; codes and scales equal the unfused pair."""
+    from futudiffu_b200 import _lib as L
+    from futudiffu_b200 import fp8_kernels as FK
+
+    M, N, K = 300, 1280, 256
+    g = gen(21)
+    x = torch.randn(M, K, generator=g)
+    x = x * torch.tensor([1e-4, 1e-2, 0.3, 1.0, 3.0]).repeat(M // 5 + 1)[:M, None]
+    w = torch.randn(N, K, generator=g) * 0.02
+    a8, a_s = (t.to(cuda_device) for t in OQ.act_quant(x.to(torch.bfloat16)))
+    b8, bs = (t.to(cuda_device) for t in OQ.weight_quant(w))
+    offsets = torch.tensor([-6.0, -0.75, 0.0, 0.02, -0.3, 0.25, 0.5, 4.0, -2.0, 1.0])
+    bias = offsets.repeat_interleave(128).to(torch.bfloat16).to(cuda_device)
+    if grouped:
+        out = FK.fp8_gemm_grouped2([(a8, a_s, b8, bs, bias), (a8[:129].contiguous(), a_s[:129].contiguous(), b8, bs, bias)],
+                                   act=L.ACT_GELU_TANH)
+        pairs = [(out[0], a8, a_s), (out[1], a8[:129].contiguous(), a_s[:129].contiguous())]
+    else:
+        pairs = [(FK.fp8_gemm_gelu_tanh_quant(a8, a_s, b8, bs, bias=bias), a8, a_s)]
+    for (c, c_s), aa, ss in pairs:
+        h = FK.fp8_addmm_blockwise(aa, ss, b8, bs, bias=bias, output_dtype=torch.bfloat16)
+        y, s = FK.fp8_gelu_tanh_quant(h)
+        assert torch.equal(_e4m3(c), _e4m3(y))
+        assert torch.equal(c_s.reshape(s.shape).cpu(), s.cpu())
+        # the regimes were reached: groups whose largest input stays below 0.25
+        hm = h.float().view(h.shape[0], -1, 128).amax(-1)
+        assert (hm < 0.25).any() and (hm > 0.25).any()
