@@ -35,6 +35,14 @@ class GemmProblem(ctypes.Structure):
     _fields_ = [("a", ctypes.c_void_p), ("a_s", ctypes.c_void_p), ("b", ctypes.c_void_p), ("b_s", ctypes.c_void_p),
                 ("bias", ctypes.c_void_p), ("c", ctypes.c_void_p), ("c_s", ctypes.c_void_p),
                 ("M", ctypes.c_int64), ("N", ctypes.c_int64), ("K", ctypes.c_int64)]
+
+
+class QkvStream(ctypes.Structure):
+    """fd_qkv_stream (include/fd_b200.h)."""
+    _fields_ = [("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p), ("freqs", ctypes.c_void_p),
+                ("S", ctypes.c_int64), ("s_off", ctypes.c_int64), ("eps", ctypes.c_float)]
+
+
 QK_INT8, QK_FP8 = 0, 1
 GRAN_TOKEN, GRAN_BLOCK = 0, 1
 PV_BF16, PV_FP8, PV_FP8_TILE = 0, 1, 2
@@ -68,6 +76,7 @@ _SIGS: dict[str, list] = {
     "fd_fp8_gemm_quant": [_P, _P, _P, _P, _P, _I, _P, _P, _L, _L, _L, _I, _P],
     "fd_fp8_gemm_quant_ld": [_P, _P, _P, _P, _P, _I, _P, _P, _L, _L, _L, _I, _L, _L, _P],
     "fd_fp8_gemm_grouped2": [_P, _P, _I, _I, _P],
+    "fd_fp8_gemm_qkv_quant": [_P, _P, _P, _P, _I, _L, _L, _L, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P],
     "fd_fp8_gemm_blockwise_lora": [_P, _P, _P, _P, _P, _I, _P, _I, _L, _L, _L, _P, _P, _L, _P],
     "fd_fp8_silu_gate_quant": [_P, _P, _P, _L, _L, _I, _P],
     "fd_fp8_gelu_tanh_quant": [_P, _P, _P, _L, _L, _I, _P],

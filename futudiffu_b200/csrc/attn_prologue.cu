@@ -19,6 +19,7 @@
 
 #include "fd_common.cuh"
 #include "fd_host.h"
+#include "fd_p3.cuh"
 
 namespace fd {
 
@@ -135,17 +136,6 @@ __global__ void __launch_bounds__(128) colstats_final_kernel(float* __restrict__
     for (; i < nchunks; ++i) am = fmaxf(am, ws_amax[base + (int64_t)i * 128]);
     ws_amax[base] = div_full(448.0f, fmaxf(am, 1e-12f));
     v_desc[bh * 128 + c] = div_full(am, 448.0f);
-  }
-}
-
-template <int QK>  // FD_QK_INT8 or FD_QK_FP8
-FD_DEV uint32_t quant_code(float x, float inv) {
-  const float y = x * inv;
-  if constexpr (QK == FD_QK_INT8) {
-    // .to(tl.int8) truncates toward zero (|y| <= 127 by construction)
-    return (uint32_t)(__float2int_rz(y) & 0xFF);
-  } else {
-    return f32x2_to_e4m3x2(y, 0.f) & 0xFF;
   }
 }
 
@@ -401,23 +391,16 @@ __global__ void __launch_bounds__(256, 3) qkv_quant_kernel(
                   bf16_bits_to_f32(uq.y & 0xFFFF), bf16_bits_to_f32(uq.y >> 16)};
     float k[4] = {bf16_bits_to_f32(uk.x & 0xFFFF), bf16_bits_to_f32(uk.x >> 16),
                   bf16_bits_to_f32(uk.y & 0xFFFF), bf16_bits_to_f32(uk.y >> 16)};
-    float sq = q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3];
-    float sk = k[0] * k[0] + k[1] * k[1] + k[2] * k[2] + k[3] * k[3];
-    sq = warp_sum(sq);
-    sk = warp_sum(sk);
-    const float rq = div_full(1.0f, sqrt_approx(div_full(sq, (float)HD) + eps));
-    const float rk = div_full(1.0f, sqrt_approx(div_full(sk, (float)HD) + eps));
+    const float rq = p3_rinv(warp_sum(p3_sumsq4(q)), eps);
+    const float rk = p3_rinv(warp_sum(p3_sumsq4(k)), eps);
     float qo[4], ko[4];
     const float4* fr = reinterpret_cast<const float4*>(freqs + row * 256) + lane * 2;
+    p3_rope4(q, rq, wqa, fr, qo);
+    p3_rope4(k, rk, wka, fr, ko);
 #pragma unroll
-    for (int pp = 0; pp < 2; ++pp) {
-      const float4 f = fr[pp];
-      const float qe = (q[2 * pp] * rq) * wqa[2 * pp], qd = (q[2 * pp + 1] * rq) * wqa[2 * pp + 1];
-      const float ke = (k[2 * pp] * rk) * wka[2 * pp], kd = (k[2 * pp + 1] * rk) * wka[2 * pp + 1];
-      qo[2 * pp] = round_to_bf16(f.x * qe + f.y * qd);
-      qo[2 * pp + 1] = round_to_bf16(f.z * qe + f.x * qd);
-      ko[2 * pp] = round_to_bf16(f.x * ke + f.y * kd);
-      ko[2 * pp + 1] = round_to_bf16(f.z * ke + f.x * kd);
+    for (int e = 0; e < 4; ++e) {
+      qo[e] = round_to_bf16(qo[e]);
+      ko[e] = round_to_bf16(ko[e]);
     }
     const int64_t o = (bh * N + n) * HD + lane * 4;
     *reinterpret_cast<uint2*>(k_out + o) = make_uint2(pack_bf16x2(ko[0], ko[1]), pack_bf16x2(ko[2], ko[3]));

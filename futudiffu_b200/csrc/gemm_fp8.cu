@@ -47,6 +47,7 @@
 // bf16, one tcgen05 kind::f16 MMA group per slice, promoted with scale 1, so
 // the delta is added to the fp32 accumulator before the single output rounding.
 #include "fd_act.cuh"
+#include "fd_p3.cuh"
 #include "fd_host.h"
 
 namespace fd {
@@ -59,7 +60,7 @@ constexpr int GROUP_M = 16;                    // row tiles per rasterisation gr
 constexpr uint32_t A_BYTES = BM * BK;          // 16 KiB
 constexpr uint32_t STAGE_BYTES = BM * BK + BN * BK;  // 48 KiB
 
-enum { EPI_STORE = 0, EPI_QUANT = 1, EPI_GELU_TANH = 2, EPI_SILU_GATE = 3 };
+enum { EPI_STORE = 0, EPI_QUANT = 1, EPI_GELU_TANH = 2, EPI_SILU_GATE = 3, EPI_QKV = 4 };
 
 constexpr uint32_t STG_WARP = 32 * 128;  // output staging per epilogue warp: 32 rows x 128 B
 
@@ -74,7 +75,7 @@ constexpr uint32_t STG_WARP = 32 * 128;  // output staging per epilogue warp: 32
 // for 3 operand stages.
 template <int EPI>
 struct Cfg {
-  static constexpr bool DEFER = EPI == EPI_GELU_TANH;
+  static constexpr bool DEFER = EPI == EPI_GELU_TANH || EPI == EPI_QKV;
   static constexpr int STAGES = DEFER ? 3 : 4;
   static constexpr int THREADS = DEFER ? 512 : 320;
   static constexpr int PROMO_WARP0 = DEFER ? 4 : 2;  // first promotion warp
@@ -85,7 +86,11 @@ struct Cfg {
   static constexpr uint32_t OFF_STG = STAGES * STAGE_BYTES;
   static constexpr uint32_t OFF_RED = OFF_STG;
   static constexpr uint32_t STG_BYTES = DEFER ? BM * BN * 2 : EPI_WARPS * STG_WARP;
-  static constexpr uint32_t OFF_BAR = OFF_STG + STG_BYTES;
+  // EPI_QKV: per-(virtual warp, column) K sums and V absmax, [8][128] f32 each, and
+  // the four epilogue warps' Q block maxima
+  static constexpr uint32_t OFF_QKV = OFF_STG + STG_BYTES;
+  static constexpr uint32_t QKV_BYTES = EPI == EPI_QKV ? 2 * 8 * 128 * 4 + 64 : 0;
+  static constexpr uint32_t OFF_BAR = OFF_QKV + QKV_BYTES;
   static constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 /*barriers*/ + 1024 /*align*/;
   static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 };
@@ -136,6 +141,27 @@ FD_DEV uint2 gelu8_codes(const uint4& u, float qm) {
   return make_uint2(quant4(g[0], g[1], g[2], g[3], qm), quant4(g[4], g[5], g[6], g[7], qm));
 }
 
+// EPI_QKV: the QKV linear of one stream of a joint attention with P3 (per-head
+// Q/K RMSNorm + RoPE) and the attention prologue's first pass in its epilogue
+// (the arithmetic of qkv_quant_kernel in attn_prologue.cu, shared through
+// fd_p3.cuh): Q as codes + descales, K and V in bf16, per-chunk K column sums and
+// V column absmax in the workspace.  GEMM rows are the stream's B x S tokens
+// (S a multiple of 128), GEMM columns [Q | K | V] x H heads x 128.
+struct QkvEpi {
+  const float* qw;      // (128,) Q norm weight
+  const float* kw;      // (128,) K norm weight
+  const float* freqs;   // (B S, 64, 2, 2) RoPE rotations of the stream's rows
+  uint8_t* q_codes;     // (B H, Nj, 128)
+  float* q_desc;        // (B H, q_desc_stride)
+  __nv_bfloat16* k_out; // (B H, Nj, 128)
+  __nv_bfloat16* v_out;
+  float* ws_sum;        // (B H, nchunks, 128)
+  float* ws_amax;
+  int64_t q_desc_stride;
+  float eps, sm_scale_log2e;
+  int S, H, Nj, s_off, q_gran, qk, nchunks, do_v;
+};
+
 struct Params {
   const float* a_s;
   const float* b_s;
@@ -149,6 +175,7 @@ struct Params {
   int lora_slices; // 64-column bf16 LoRA slices after the FP8 slices (EPI_STORE, BMODE 0)
   int64_t ldc;     // row stride of c in elements (N unless the output is a column window)
   int64_t ldcs;    // row stride of c_s in scales (N / 128 likewise)
+  QkvEpi qe;       // EPI_QKV only
 };
 
 // Tile t -> (row tile, column tile), GROUP_M row tiles at a time so that the
@@ -248,6 +275,139 @@ FD_DEV void drain_wait(uint64_t* bar, uint32_t parity) {
 //        2 -> B stored (N, K), per-row scales b_s (N,) applied after the K loop
 FD_DEV void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// AND of `pred` over the `nthreads` threads of named barrier `id` (all of them wait).
+FD_DEV bool named_bar_and(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
+constexpr int QKV_BAR = 6;  // named barrier of the four EPI_QKV epilogue warps
+
+// EPI_QKV epilogue of one 128 x 256 tile (two heads of Q, K or V) by the four
+// epilogue warps, from the promotion warps' bf16 copy of the tile (hbuf: row r at
+// r * 512, 16-byte chunk c of the row at c ^ (r & 7)).  The row / lane mapping and
+// every sum run in the order of qkv_quant_kernel (attn_prologue.cu): lane l holds
+// columns 4l .. 4l + 3 of a head, "virtual warp" v in 0..7 takes rows v + 8 i in
+// increasing i (real warp w4 plays v = w4 and v = w4 + 4), and the K sums of the
+// eight virtual warps are added in order, so the codes, descales, bf16 K / V and
+// workspace partials equal that kernel's bit for bit.
+template <int QK>
+FD_DEV void qkv_epilogue_tile(const Params& p, uint8_t* hbuf, float* red, int mb, int nb, int w4, int lane) {
+  const QkvEpi& e = p.qe;
+  const float qmax = (QK == FD_QK_INT8) ? 127.0f : 448.0f;
+  const int D = e.H * 128;
+  const int col0 = nb * BN;
+  const int part = col0 / D;  // 0 Q, 1 K, 2 V
+  const int h0 = (col0 - part * D) / 128;
+  const int row0 = mb * BM;
+  const int b = row0 / e.S, s0 = row0 - b * e.S;
+  const int chunk = (e.s_off + s0) / 128;
+  float* sh_k = red;          // [8][128]
+  float* sh_v = red + 1024;   // [8][128]
+  float* sh_q = red + 2048;   // [4]
+  const int t128 = w4 * 32 + lane;
+  const float4 w4v = reinterpret_cast<const float4*>(part == 0 ? e.qw : e.kw)[lane];
+  const float wv[4] = {w4v.x, w4v.y, w4v.z, w4v.w};
+#pragma unroll 1
+  for (int hh = 0; hh < 2; ++hh) {
+    const int64_t bh = (int64_t)b * e.H + h0 + hh;
+    float ks[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    float vm[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    float bmax = 0.f;
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i) {
+#pragma unroll
+      for (int v = 0; v < 2; ++v) {
+        const int r = w4 + 4 * v + 8 * i;
+        const int64_t n = e.s_off + s0 + r;
+        uint8_t* hp = hbuf + r * 512 + ((((hh * 16) + (lane >> 1)) ^ (r & 7)) << 4) + ((lane & 1) << 3);
+        const uint2 u = *reinterpret_cast<const uint2*>(hp);
+        const float x[4] = {bf16_bits_to_f32(u.x & 0xFFFF), bf16_bits_to_f32(u.x >> 16),
+                            bf16_bits_to_f32(u.y & 0xFFFF), bf16_bits_to_f32(u.y >> 16)};
+        const int64_t o = (bh * e.Nj + n) * 128 + lane * 4;
+        if (part == 2) {
+          *reinterpret_cast<uint2*>(e.v_out + o) = u;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) vm[v][k] = fmaxf(vm[v][k], fabsf(x[k]));
+          continue;
+        }
+        const float rr = p3_rinv(warp_sum(p3_sumsq4(x)), e.eps);
+        float y[4];
+        p3_rope4(x, rr, wv, reinterpret_cast<const float4*>(e.freqs + (int64_t)(row0 + r) * 256) + lane * 2, y);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) y[k] = round_to_bf16(y[k]);
+        const uint2 yb = make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
+        if (part == 1) {
+          *reinterpret_cast<uint2*>(e.k_out + o) = yb;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) ks[v][k] += y[k];
+          continue;
+        }
+        const float qa = fmaxf(fmaxf(fabsf(y[0]), fabsf(y[1])), fmaxf(fabsf(y[2]), fabsf(y[3])));
+        if (e.q_gran == FD_GRAN_TOKEN) {
+          const float am = warp_max(qa);
+          const float inv = div_full(qmax, fmaxf(am, 1e-12f));
+          *reinterpret_cast<uint32_t*>(e.q_codes + o) = quant_code<QK>(y[0], inv) | (quant_code<QK>(y[1], inv) << 8) |
+                                                       (quant_code<QK>(y[2], inv) << 16) |
+                                                       (quant_code<QK>(y[3], inv) << 24);
+          if (lane == 0) e.q_desc[bh * e.q_desc_stride + n] = div_full(am, qmax) * e.sm_scale_log2e;
+        } else {
+          bmax = fmaxf(bmax, qa);
+          *reinterpret_cast<uint2*>(hp) = yb;  // kept until the block's absmax is known
+        }
+      }
+    }
+    if (part != 0) {
+#pragma unroll
+      for (int v = 0; v < 2; ++v)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          sh_k[(w4 + 4 * v) * 128 + lane * 4 + k] = ks[v][k];
+          sh_v[(w4 + 4 * v) * 128 + lane * 4 + k] = vm[v][k];
+        }
+      named_bar_sync(QKV_BAR, 128);
+      const int c = t128;
+      float tsum = 0.f, amax = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        tsum += sh_k[w * 128 + c];
+        amax = fmaxf(amax, sh_v[w * 128 + c]);
+      }
+      if (part == 1) e.ws_sum[(bh * e.nchunks + chunk) * 128 + c] = tsum;
+      else if (e.do_v) e.ws_amax[(bh * e.nchunks + chunk) * 128 + c] = amax;
+      named_bar_sync(QKV_BAR, 128);
+    } else if (e.q_gran == FD_GRAN_BLOCK) {
+      bmax = warp_max(bmax);
+      if (lane == 0) sh_q[w4] = bmax;
+      named_bar_sync(QKV_BAR, 128);
+      const float mx = fmaxf(fmaxf(sh_q[0], sh_q[1]), fmaxf(sh_q[2], sh_q[3]));
+      if (t128 == 0) e.q_desc[bh * e.q_desc_stride + chunk] = div_full(mx, qmax) * e.sm_scale_log2e;
+      const float inv = div_full(qmax, fmaxf(mx, 1e-12f));
+#pragma unroll 4
+      for (int j = 0; j < 32; ++j) {
+        const int r = w4 + 4 * (j & 1) + 8 * (j >> 1);
+        const int64_t n = e.s_off + s0 + r;
+        const uint2 u = *reinterpret_cast<const uint2*>(hbuf + r * 512 + ((((hh * 16) + (lane >> 1)) ^ (r & 7)) << 4) +
+                                                         ((lane & 1) << 3));
+        const float y[4] = {bf16_bits_to_f32(u.x & 0xFFFF), bf16_bits_to_f32(u.x >> 16),
+                            bf16_bits_to_f32(u.y & 0xFFFF), bf16_bits_to_f32(u.y >> 16)};
+        *reinterpret_cast<uint32_t*>(e.q_codes + (bh * e.Nj + n) * 128 + lane * 4) =
+            quant_code<QK>(y[0], inv) | (quant_code<QK>(y[1], inv) << 8) | (quant_code<QK>(y[2], inv) << 16) |
+            (quant_code<QK>(y[3], inv) << 24);
+      }
+      named_bar_sync(QKV_BAR, 128);
+    }
+  }
 }
 
 // GROUPED: two independent problems (p0 with tmA / tmB, p1 with tmLA / tmLB) in one
@@ -414,7 +574,7 @@ __global__ void __launch_bounds__(Cfg<EPI>::THREADS, 1)
       drain_wait(drain, 0);
     }
   } else if (CF::DEFER && warp >= CF::GELU_WARP0) {
-    // ------------------------------------------------------------ deferred GELU + requant
+    // ------------------------------------------------------------ deferred GELU + requant / QKV prologue
     // Thread t owns row t of the tile: per tile it reads the promotion warps' bf16
     // copy of its row (two 1 x 128 output groups) from shared memory and stores
     // the e4m3 codes of GELU(tanh) and the group scale.  The group absmax needs
@@ -435,6 +595,18 @@ __global__ void __launch_bounds__(Cfg<EPI>::THREADS, 1)
       tile_coords(p, g1 ? tile - p0.ntiles : tile, mb, nb);
       ok = ok && mbar_wait(hfull, nt & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
+      if constexpr (EPI == EPI_QKV) {
+        // the four warps run the tile together (named barriers): all or none
+        ok = named_bar_and(QKV_BAR, 128, ok);
+        if (ok) {
+          uint8_t* hbuf = smem + CF::OFF_STG;
+          float* red = reinterpret_cast<float*>(smem + CF::OFF_QKV);
+          if (p.qe.qk == FD_QK_INT8) qkv_epilogue_tile<FD_QK_INT8>(p, hbuf, red, mb, nb, warp - CF::GELU_WARP0, lane);
+          else qkv_epilogue_tile<FD_QK_FP8>(p, hbuf, red, mb, nb, warp - CF::GELU_WARP0, lane);
+        }
+        mbar_arrive(hempty);
+        continue;
+      }
       const int m = mb * BM + t;
       const bool row_ok = m < p.M;
 #pragma unroll 1
@@ -1077,4 +1249,111 @@ extern "C" int fd_fp8_gemm_grouped2(const fd_gemm_problem* q0, const fd_gemm_pro
   if (bias) FD_G2(-1, FD_DT_BF16, EPI_SILU_GATE);
   FD_G2(-1, -1, EPI_SILU_GATE);
 #undef FD_G2
+}
+
+int64_t fd_desc_stride(int64_t N, int gran, int rows_per_block);  // attn_prologue.cu
+
+// ---------------------------------------------------------------------------
+// The QKV linear(s) of a joint attention with P3 and the attention prologue's
+// first pass in the GEMM epilogue (EPI_QKV); equals fd_fp8_gemm_blockwise (bf16)
+// followed by fd_qkv_postprocess_quant per stream.
+static int qkv_problem(const fd_gemm_problem& q, const fd_qkv_stream& st, int64_t B, int64_t H, int64_t N,
+                       int qk_kind, int q_gran, int pv_kind, float sm_scale_log2e, void* q_codes, float* q_desc,
+                       void* k_out, void* v_out, float* workspace, CUtensorMap& ta, CUtensorMap& tb,
+                       gemm::Params& p) {
+  FD_CHECK_ARG(q.M == B * st.S && q.N == 3 * H * 128 && q.K > 0 && q.K % 128 == 0, "bad shape");
+  FD_CHECK_ARG(st.S > 0 && st.S % 128 == 0 && st.s_off >= 0 && st.s_off % 128 == 0 && st.s_off + st.S <= N,
+               "S and s_off must be multiples of 128 inside N");
+  FD_CHECK_ARG(q.M < (1ll << 31) && q.K < (1ll << 31), "dimension too large");
+  FD_CHECK_ARG(q.a && q.a_s && q.b && q.b_s && st.q_norm && st.k_norm && st.freqs, "null pointer");
+  FD_CHECK_ARG(aligned16(q.a) && aligned16(q.b) && aligned16(st.q_norm) && aligned16(st.k_norm) &&
+                   aligned16(st.freqs),
+               "misaligned pointer");
+  {
+    const uint64_t dims[2] = {(uint64_t)q.K, (uint64_t)q.M};
+    const uint64_t strides[1] = {(uint64_t)q.K};
+    const uint32_t box[2] = {128, 128};
+    int rc = encode_tiled(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q.a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)q.K, (uint64_t)q.N};
+    const uint64_t strides[1] = {(uint64_t)q.K};
+    const uint32_t box[2] = {128, 256};
+    int rc = encode_tiled(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q.b, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  const int nchunks = (int)(N / 128);
+  p.a_s = q.a_s;
+  p.b_s = q.b_s;
+  p.bias = q.bias;
+  p.c = nullptr;
+  p.c_s = nullptr;
+  p.M = (int)q.M;
+  p.N = (int)q.N;
+  p.K = (int)q.K;
+  p.ntm = (int)(q.M / 128);
+  p.ntn = (int)(q.N / 256);
+  p.nbs = (int)(q.N / 128);
+  p.ntiles = p.ntm * p.ntn;
+  p.kblocks = (int)(q.K / 128);
+  p.lora_slices = 0;
+  p.ldc = q.N;
+  p.ldcs = 0;
+  gemm::QkvEpi& e = p.qe;
+  e.qw = st.q_norm;
+  e.kw = st.k_norm;
+  e.freqs = st.freqs;
+  e.q_codes = (uint8_t*)q_codes;
+  e.q_desc = q_desc;
+  e.k_out = (__nv_bfloat16*)k_out;
+  e.v_out = (__nv_bfloat16*)v_out;
+  e.ws_sum = workspace;
+  e.ws_amax = workspace + B * H * nchunks * 128;
+  e.q_desc_stride = fd_desc_stride(N, q_gran, 128);
+  e.eps = st.eps;
+  e.sm_scale_log2e = sm_scale_log2e;
+  e.S = (int)st.S;
+  e.H = (int)H;
+  e.Nj = (int)N;
+  e.s_off = (int)st.s_off;
+  e.q_gran = q_gran;
+  e.qk = qk_kind;
+  e.nchunks = nchunks;
+  e.do_v = pv_kind == FD_PV_FP8;
+  return FD_OK;
+}
+
+extern "C" int fd_fp8_gemm_qkv_quant(const fd_gemm_problem* p0, const fd_qkv_stream* s0, const fd_gemm_problem* p1,
+                                     const fd_qkv_stream* s1, int bias_dtype, int64_t B, int64_t H, int64_t N,
+                                     int qk_kind, int q_gran, int pv_kind, float sm_scale_log2e, void* q_codes,
+                                     float* q_desc, void* k_out, void* v_out, float* workspace, void* stream) {
+  FD_CHECK_ARG(p0 && s0 && (p1 == nullptr) == (s1 == nullptr), "a problem needs its stream description");
+  FD_CHECK_ARG(B > 0 && H > 0 && H % 2 == 0 && B * H <= 65535, "H must be even (two heads per 256-column tile)");
+  FD_CHECK_ARG(N > 0 && N % 128 == 0 && N < (1ll << 30), "N must be a positive multiple of 128");
+  FD_CHECK_ARG(qk_kind == FD_QK_INT8 || qk_kind == FD_QK_FP8, "bad qk_kind");
+  FD_CHECK_ARG(q_gran == FD_GRAN_TOKEN || q_gran == FD_GRAN_BLOCK, "bad q_gran");
+  FD_CHECK_ARG(pv_kind == FD_PV_BF16 || pv_kind == FD_PV_FP8, "bad pv_kind");
+  FD_CHECK_ARG(q_codes && q_desc && k_out && v_out && workspace, "null pointer");
+  FD_CHECK_ARG(aligned8(k_out) && aligned8(v_out) && (reinterpret_cast<uintptr_t>(q_codes) & 3) == 0,
+               "misaligned pointer");
+  FD_CHECK_ARG((p0->bias == nullptr || bias_dtype == FD_DT_BF16) && (p1 == nullptr || (p1->bias == nullptr) == (p0->bias == nullptr)),
+               "bias must be bf16, on both problems or neither");
+  CUtensorMap ta0, tb0, ta1, tb1;
+  gemm::Params q0p, q1p;
+  int rc = qkv_problem(*p0, *s0, B, H, N, qk_kind, q_gran, pv_kind, sm_scale_log2e, q_codes, q_desc, k_out, v_out,
+                       workspace, ta0, tb0, q0p);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  using namespace gemm;
+  const bool bias = p0->bias != nullptr;
+  if (p1) {
+    rc = qkv_problem(*p1, *s1, B, H, N, qk_kind, q_gran, pv_kind, sm_scale_log2e, q_codes, q_desc, k_out, v_out,
+                     workspace, ta1, tb1, q1p);
+    if (rc) return rc;
+    if (bias) return launch<0, -1, FD_DT_BF16, EPI_QKV, false, true>(ta0, tb0, ta0, q0p, st, &ta1, &tb1, &q1p, &ta1);
+    return launch<0, -1, -1, EPI_QKV, false, true>(ta0, tb0, ta0, q0p, st, &ta1, &tb1, &q1p, &ta1);
+  }
+  if (bias) return launch<0, -1, FD_DT_BF16, EPI_QKV>(ta0, tb0, ta0, q0p, st);
+  return launch<0, -1, -1, EPI_QKV>(ta0, tb0, ta0, q0p, st);
 }

@@ -16,6 +16,7 @@
 // tl.sqrt (sqrt.approx.f32), products evaluated left to right.
 #include "fd_act.cuh"
 #include "fd_host.h"
+#include "fd_p3.cuh"
 
 namespace fd {
 
@@ -300,27 +301,15 @@ __global__ void __launch_bounds__(256) qkv_post_kernel(const __nv_bfloat16* __re
                   bf16_bits_to_f32(uq.y & 0xFFFF), bf16_bits_to_f32(uq.y >> 16)};
     float k[4] = {bf16_bits_to_f32(uk.x & 0xFFFF), bf16_bits_to_f32(uk.x >> 16),
                   bf16_bits_to_f32(uk.y & 0xFFFF), bf16_bits_to_f32(uk.y >> 16)};
-    float sq = q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3];
-    float sk = k[0] * k[0] + k[1] * k[1] + k[2] * k[2] + k[3] * k[3];
-    sq = warp_sum(sq);
-    sk = warp_sum(sk);
-    const float rq = div_full(1.0f, sqrt_approx(div_full(sq, (float)HD) + eps));
-    const float rk = div_full(1.0f, sqrt_approx(div_full(sk, (float)HD) + eps));
+    const float rq = p3_rinv(warp_sum(p3_sumsq4(q)), eps);
+    const float rk = p3_rinv(warp_sum(p3_sumsq4(k)), eps);
     const float wqa[4] = {wq.x, wq.y, wq.z, wq.w};
     const float wka[4] = {wk.x, wk.y, wk.z, wk.w};
     float qo[4], ko[4];
     // freqs (rows, 64, 2, 2): pair p at row*256 + p*4: [cos, -sin, sin, cos]
     const float4* fr = reinterpret_cast<const float4*>(freqs + row * 256) + lane * 2;
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      const float4 f = fr[p];
-      const float qe = (q[2 * p] * rq) * wqa[2 * p], qd = (q[2 * p + 1] * rq) * wqa[2 * p + 1];
-      const float ke = (k[2 * p] * rk) * wka[2 * p], kd = (k[2 * p + 1] * rk) * wka[2 * p + 1];
-      qo[2 * p] = f.x * qe + f.y * qd;
-      qo[2 * p + 1] = f.z * qe + f.x * qd;
-      ko[2 * p] = f.x * ke + f.y * kd;
-      ko[2 * p + 1] = f.z * ke + f.x * kd;
-    }
+    p3_rope4(q, rq, wqa, fr, qo);
+    p3_rope4(k, rk, wka, fr, ko);
     const int64_t b = row / S, s = row % S;
     const int64_t o = ((b * H + h) * S_out + s_off + s) * HD + lane * 4;
     *reinterpret_cast<uint2*>(oq + o) = make_uint2(pack_bf16x2(qo[0], qo[1]), pack_bf16x2(qo[2], qo[3]));

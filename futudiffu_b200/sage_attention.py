@@ -19,6 +19,7 @@ entry point (the INT8-QK + FP8-PV combination of the B200 headline config).
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -248,6 +249,89 @@ def quantize_qkv_streams(
         "v_codes": v_codes, "v_desc": v_desc, "k_mean": k_mean, "qk": qk, "gran": gran, "pv": pv,
         "k": k, "v": v, "B": B, "H": H, "N": N,
     }
+
+
+def linear_prologue_ok(stream_lengths: list[int], H: int) -> bool:
+    """Streams qualify for the QKV linear fused with P3 and the prologue's first
+    pass (quantize_qkv_linear_streams) when every stream holds a multiple of 128
+    rows (a GEMM row tile is one 128-row block of one sample), there are at most
+    two, and the heads pair up into the GEMM's 256-column tiles."""
+    return len(stream_lengths) <= 2 and H % 2 == 0 and all(n % 128 == 0 for n in stream_lengths)
+
+
+def quantize_qkv_linear_streams(
+    streams: list[tuple], H: int, N: int, sm_scale: float | None, *, smooth_k: bool, qk_quant: str,
+    granularity: str, pv_quant: str,
+) -> dict:
+    """quantize_qkv_streams with the QKV linears in the same launch: the FP8 GEMM's
+    epilogue runs P3 and the Q quantisation (``fd_fp8_gemm_qkv_quant``), so the
+    bf16 Q/K/V never go to HBM before the prologue reads them.  ``streams``: one or
+    two (a8 (B, S, K) e4m3, a_s (B, S, K / 128) f32, w8 (3 H 128, K) e4m3, w_s
+    (3 H, K / 128) f32, bias (3 H 128,) bf16 or None, q_norm_w, k_norm_w, freqs
+    (B, S, [1,] 64, 2, 2), s_off, eps), rows [s_off, s_off + S) of the N joint rows
+    (see linear_prologue_ok).  Returns quantize_qkv_streams' dict, equal to it for
+    the bf16 outputs of the same linears."""
+    a0 = streams[0][0]
+    B, dev = a0.shape[0], a0.device
+    BH = B * H
+    D = 128
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    assert len(streams) in (1, 2) and linear_prologue_ok([st[0].shape[1] for st in streams], H)
+    qk = L.QK_INT8 if qk_quant == "int8" else L.QK_FP8
+    gran = L.GRAN_TOKEN if granularity == "per_token" else L.GRAN_BLOCK
+    pv = L.PV_FP8 if pv_quant == "fp8" else L.PV_BF16
+    code_dt = torch.int8 if qk == L.QK_INT8 else torch.float8_e4m3fn
+    q_codes = torch.empty(BH, N, D, dtype=code_dt, device=dev)
+    q_desc = torch.empty(BH, _desc_stride(N, gran, 128), dtype=torch.float32, device=dev)
+    k = torch.empty(BH, N, D, dtype=torch.bfloat16, device=dev)
+    v = torch.empty(BH, N, D, dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(int(L.lib().fd_qkv_quant_workspace_floats(BH, N)), dtype=torch.float32, device=dev)
+    probs, descs, keep = [], [], []
+    for a8, a_s, w8, w_s, bias, qw, kw, freqs, s_off, eps in streams:
+        Ba, S, K = a8.shape
+        assert Ba == B and a8.dtype == torch.float8_e4m3fn and a8.is_contiguous() and a_s.is_contiguous()
+        assert w8.shape == (3 * H * D, K) and w8.is_contiguous() and w_s.is_contiguous()
+        L.require_cuda(a8, a_s, w8, w_s, bias, qw, kw, freqs)
+        if bias is not None:
+            bias = bias.contiguous()
+            assert bias.dtype == torch.bfloat16
+        fr = _freqs_rows(freqs, B, S)
+        qw32, kw32 = qw.float().contiguous(), kw.float().contiguous()
+        keep += [bias, fr, qw32, kw32]
+        probs.append(L.GemmProblem(L.ptr(a8), L.ptr(a_s), L.ptr(w8), L.ptr(w_s), L.ptr(bias), None, None,
+                                   B * S, 3 * H * D, K))
+        descs.append(L.QkvStream(L.ptr(qw32), L.ptr(kw32), L.ptr(fr), S, s_off, float(eps)))
+    p1 = ctypes.addressof(probs[1]) if len(probs) == 2 else None
+    s1 = ctypes.addressof(descs[1]) if len(descs) == 2 else None
+    stream_ptr = L.stream_ptr(dev)
+    L.call("fd_fp8_gemm_qkv_quant", ctypes.addressof(probs[0]), ctypes.addressof(descs[0]), p1, s1, L.DT_BF16,
+           B, H, N, qk, gran, pv, float(sm_scale * _LOG2E), L.ptr(q_codes), L.ptr(q_desc), L.ptr(k), L.ptr(v),
+           L.ptr(ws), stream_ptr)
+    k_codes = torch.empty(BH, N, D, dtype=code_dt, device=dev)
+    k_desc = torch.empty(BH, _desc_stride(N, gran, 64), dtype=torch.float32, device=dev)
+    k_mean = torch.empty(BH, D, dtype=torch.float32, device=dev)
+    v_codes = torch.empty(BH, N, D, dtype=torch.float8_e4m3fn, device=dev) if pv == L.PV_FP8 else None
+    v_desc = torch.empty(BH, D, dtype=torch.float32, device=dev) if pv == L.PV_FP8 else None
+    L.call("fd_attn_quant_kv", L.ptr(k), L.ptr(v), BH, N, int(bool(smooth_k)), qk, gran, pv, L.ptr(k_codes),
+           L.ptr(k_desc), L.ptr(v_codes), L.ptr(v_desc), L.ptr(k_mean), L.ptr(ws), stream_ptr)
+    return {
+        "q_codes": q_codes, "q_desc": q_desc, "k_codes": k_codes, "k_desc": k_desc,
+        "v_codes": v_codes, "v_desc": v_desc, "k_mean": k_mean, "qk": qk, "gran": gran, "pv": pv,
+        "k": k, "v": v, "B": B, "H": H, "N": N,
+    }
+
+
+def attn_quant_out_from_linear(
+    streams: list[tuple], H: int, N: int, sm_scale: float | None, *, block_mask: Tensor | None, qk_quant: str,
+    pv_quant: str, granularity: str, regions: list[tuple[Tensor, Tensor]], split: int | None = None,
+) -> None:
+    """quantize_qkv_linear_streams + the quantised-output attention: from the QKV
+    linears' FP8 inputs to the output linears' 1 x 128 e4m3 inputs."""
+    qz = quantize_qkv_linear_streams(streams, H, N, sm_scale, smooth_k=_SAGE_SMOOTH_K, qk_quant=qk_quant,
+                                     granularity=granularity, pv_quant=pv_quant)
+    vsrc = qz["v_codes"] if qz["pv"] == L.PV_FP8 else qz["v"]
+    _quant_out_call(qz, vsrc, qz["B"], H, N, block_mask, regions, split, qz["k"].device)
 
 
 def _quant_out_call(qz: dict, vsrc: Tensor, B: int, H: int, N: int, block_mask: Tensor | None,

@@ -299,6 +299,30 @@ int fd_attn_quant_kv(const void* k, const void* v, int64_t BH, int64_t N, int sm
                      int pv_kind, void* k_codes, float* k_desc, void* v_codes, float* v_desc, float* k_mean,
                      float* workspace, void* stream);
 
+/* The QKV linear(s) of a joint attention with P3 and fd_qkv_postprocess_quant in
+ * the GEMM's epilogue: the bf16 Q/K/V never go to HBM before the prologue reads
+ * them.  No counterpart in the reference (fp8_gemm_blockwise, fused_qkv_postprocess
+ * and the attention kernels' quantisation, fp8_kernels.py:195-227,
+ * fused_kernels.py:270-471, sage_kernels.py:632-663).  Equal, code for code, to
+ * fd_fp8_gemm_blockwise (bf16 output) followed by fd_qkv_postprocess_quant for
+ * each stream; run fd_attn_quant_kv after it.  One problem per stream (p1 / s1
+ * NULL for a single stream, else the two run as one launch): a (B S, K) e4m3,
+ * b = the stream's QKV weight (3 H 128, K) e4m3 (rows [Q heads | K heads | V
+ * heads]), bias bf16 or NULL on both; c / c_s unused.  S and s_off multiples of
+ * 128, H even; outputs and workspace as fd_qkv_postprocess_quant's. */
+typedef struct fd_qkv_stream {
+  const float* q_norm;  /* (128,) f32 */
+  const float* k_norm;  /* (128,) f32 */
+  const float* freqs;   /* (B S, 64, 2, 2) f32 RoPE rotations of the stream's rows */
+  int64_t S;            /* rows per sample */
+  int64_t s_off;        /* first joint row of the stream */
+  float eps;
+} fd_qkv_stream;
+int fd_fp8_gemm_qkv_quant(const fd_gemm_problem* p0, const fd_qkv_stream* s0, const fd_gemm_problem* p1,
+                          const fd_qkv_stream* s1, int bias_dtype, int64_t B, int64_t H, int64_t N, int qk_kind,
+                          int q_gran, int pv_kind, float sm_scale_log2e, void* q_codes, float* q_desc, void* k_out,
+                          void* v_out, float* workspace, void* stream);
+
 /* V for FD_PV_FP8_TILE (reference _sage_attn_fwd_fp8qk_fp8pv_lse,
  * src/futudiffu/sage_kernels.py:1142-1148): v (BH, N, 128) bf16 -> v_codes
  * (BH, N, 128) e4m3 and v_desc (BH, ceil(N/64), 128) f32, per 64-row tile and

@@ -202,3 +202,58 @@ def test_fused_qkv_prologue_matches_unfused(cuda_device, qk, gran, pv):
     kc_g, kc_r = got["k_codes"].view(torch.uint8)[same], ref["k_codes"].view(torch.uint8)[same]
     assert torch.equal(kc_g, kc_r)
     assert torch.equal(got["k_desc"][same], ref["k_desc"][same])
+
+
+@pytest.mark.parametrize("qk,gran,pv,two,bias", [("int8", "per_block", "bf16", True, False),
+                                                 ("int8", "per_token", "fp8", True, True),
+                                                 ("fp8", "per_block", "fp8", False, False),
+                                                 ("fp8", "per_token", "bf16", False, True),
+                                                 ("int8", "per_block", "fp8", False, True)])
+def test_qkv_linear_fused_prologue_matches_unfused(cuda_device, qk, gran, pv, two, bias):
+    """The QKV linear with P3 and the prologue's first pass in its epilogue
+    (fd_fp8_gemm_qkv_quant, one or two streams in one launch) equals the bf16 GEMM
+    followed by the fused P3 + prologue, code for code: Q codes and descales, bf16
+    K / V, the K mean, K / V codes and descales."""
+    import math
+
+    from futudiffu_b200 import fp8_kernels as FK
+    from futudiffu_b200.attention import rope_embed
+    from futudiffu_b200.sage_attention import quantize_qkv_linear_streams, quantize_qkv_streams
+    from oracle import quant as OQ
+
+    g = gen(73)
+    B, H, K = 2, 4, 256
+    lens = (256, 384) if two else (512,)
+    N = sum(lens)
+    d = lambda t: t.to(cuda_device)  # noqa: E731
+    streams_lin, streams_bf16 = [], []
+    off = 0
+    for S in lens:
+        x = torch.randn(B, S, K, generator=g)
+        w = torch.randn(3 * H * 128, K, generator=g) * 0.05
+        w[H * 128:2 * H * 128] += 0.02  # a K offset for the smoothing to remove
+        a8, a_s = (d(t) for t in OQ.act_quant(x.to(torch.bfloat16)))
+        w8, ws = (d(t) for t in OQ.weight_quant(w))
+        bv = d((torch.randn(3 * H * 128, generator=g) * 0.1).to(torch.bfloat16)) if bias else None
+        pos = torch.arange(S).float()
+        f = torch.cat([rope_embed(pos, 64, 256.0), rope_embed(pos * 0.5, 64, 256.0)], dim=-3)
+        fr = d(f.unsqueeze(0).expand(B, S, 64, 2, 2).contiguous())
+        qw = d((1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16))
+        kw = d((1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16))
+        qkv = (FK.fp8_addmm_blockwise(a8, a_s, w8, ws, bias=bv, output_dtype=torch.bfloat16) if bias
+               else FK.fp8_gemm_blockwise(a8, a_s, w8, ws, output_dtype=torch.bfloat16))
+        streams_lin.append((a8, a_s, w8, ws, bv, qw, kw, fr, off, 1e-5))
+        streams_bf16.append((qkv, qw, kw, fr, off, 1e-5))
+        off += S
+    sm = 1 / math.sqrt(128)
+    kw_ = dict(smooth_k=True, qk_quant=qk, granularity=gran, pv_quant=pv)
+    got = quantize_qkv_linear_streams(streams_lin, H, N, sm, **kw_)
+    ref = quantize_qkv_streams(streams_bf16, H, N, sm, **kw_)
+    for key in ("k", "v", "q_codes", "q_desc", "k_mean", "k_codes", "k_desc", "v_codes", "v_desc"):
+        a, b = got[key], ref[key]
+        if a is None:
+            assert b is None
+            continue
+        if a.dtype in (torch.int8, torch.float8_e4m3fn):
+            a, b = a.view(torch.uint8), b.view(torch.uint8)
+        assert torch.equal(a, b), key
