@@ -354,6 +354,11 @@ class LaunchRecorder:
             probs = [self.L.GemmProblem.from_address(a) for a in args[:2]]
             mult = 2 if args[3] == self.L.ACT_SILU_GATE else 1
             kind, work = "gemm", sum(2.0 * q.M * q.N * q.K * mult for q in probs)
+        elif name == "fd_fp8_gemm_qkv_quant":
+            # the QKV linear(s) with the fused P3 + Q quantisation epilogue: GEMM work
+            # plus the prologue's first pass, kept apart from the plain GEMM rate
+            probs = [self.L.GemmProblem.from_address(a) for a in (args[0], args[2]) if a]
+            kind, work = "gemm_qkv", sum(2.0 * q.M * q.N * q.K for q in probs)
         elif name in ("fd_sage_attn_fwd", "fd_sage_attn_fwd_bnhd"):
             BH, N = args[10], args[11]
             kind, work = "attn", 4.0 * BH * N * N * 128
@@ -652,6 +657,7 @@ def run_dit(args, world, rank, local):
     rec.active = False
     torch.cuda.synchronize()
     gemm_work, gemm_ms, n_gemm = rec.summary("gemm")
+    qkv_work, qkv_ms, n_qkv = rec.summary("gemm_qkv")
     attn_work, attn_ms, n_attn = rec.summary("attn")
     launches_per_step = rec.launches // n_rec
     rec.close()
@@ -735,7 +741,14 @@ def run_dit(args, world, rank, local):
             "detail": {"model_tflop_per_step": step_flops / 1e12,
                        "model_tflops": step_flops / (ms * 1e-3) / 1e12,
                        "attention_kernel_tops": attn_work / (attn_ms * 1e-3) / 1e12 if attn_ms else None,
-                       "time_share": {"gemm": gemm_ms / n_rec / ms_local, "attention": attn_ms / n_rec / ms_local},
+                       "time_share": {"gemm": (gemm_ms + qkv_ms) / n_rec / ms_local,
+                                      "attention": attn_ms / n_rec / ms_local},
+                       "qkv_linear_fused_prologue": {
+                           "launches_per_step": n_qkv // n_rec,
+                           "share": qkv_ms / n_rec / ms_local,
+                           "gemm_tflops": qkv_work / (qkv_ms * 1e-3) / 1e12 if qkv_ms else None,
+                           "note": "the QKV linears with P3 + Q quantisation in the GEMM epilogue "
+                                   "(fd_fp8_gemm_qkv_quant); their time includes the prologue's first pass"},
                        "launch": f"each timed step replays the step's {launches_per_step} kernels as one "
                                  "captured CUDA graph",
                        "settle": f"{n_settle} untimed replays (3 s) before the timed steps"},
@@ -744,8 +757,10 @@ def run_dit(args, world, rank, local):
                                  "note": "step time x median SM clock under load; compare across N"},
             "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": peak, "unit": "TFLOP/s",
                          "frac": gemm_tf / peak, "traffic": None,
-                         "kernel": f"gemm_fp8_kernel (all {n_gemm // n_rec} GEMM launches of a step, "
-                                   "flop-weighted, CUDA events per launch over two eager steps)",
+                         "kernel": f"gemm_fp8_kernel ({n_gemm // n_rec} GEMM launches of a step: every FP8 "
+                                   "linear but the QKV linears with the fused prologue, see "
+                                   "detail.qkv_linear_fused_prologue; flop-weighted, CUDA events per launch "
+                                   "over two eager steps)",
                          "peak_source": f"2 x {pk['source']} sustained bf16 dense "
                                         f"({pk['bf16_tflops_sustained']} TF/s, kernels inside a long step): "
                                         "fp8 dense rate is twice bf16"},
@@ -855,6 +870,7 @@ def run_block(args, world, rank, local):
         rec.active = False
         torch.cuda.synchronize()
         gemm_work, gemm_ms, n_gemm = rec.summary("gemm")
+        qkv_work, qkv_ms, n_qkv = rec.summary("gemm_qkv")
         attn_work, attn_ms, _ = rec.summary("attn")
         launches_per_step = rec.launches // n_rec
         rec.close()
@@ -927,12 +943,14 @@ def run_block(args, world, rank, local):
             "detail": {"block_tflop": flops / 1e12,
                        "linears": "the two streams' linears as grouped launches",
                        "attention": "fused RMSNorm/RoPE/quant prologue, then the tcgen05 attention kernel",
-                       "time_share": {"gemm": gemm_ms / n_rec / ms_local, "attention": attn_ms / n_rec / ms_local},
+                       "time_share": {"gemm": (gemm_ms + qkv_ms) / n_rec / ms_local, "attention": attn_ms / n_rec / ms_local,
+                                      "qkv_linear_fused_prologue": qkv_ms / n_rec / ms_local},
                        "attention_kernel_tops": attn_work / (attn_ms * 1e-3) / 1e12 if attn_ms else None,
                        "launch": f"each step replays the block's {launches_per_step} kernels as one CUDA graph"},
             "roofline": {"bound": "tensor", "achieved": gemm_tf, "peak": peak, "unit": "TFLOP/s",
                          "frac": gemm_tf / peak, "traffic": None,
-                         "kernel": f"gemm_fp8_kernel (the {n_gemm // n_rec} GEMM launches of a block, flop-weighted, "
+                         "kernel": f"gemm_fp8_kernel (the {n_gemm // n_rec} GEMM launches of a block but the QKV linears with "
+                                   "the fused prologue, flop-weighted, "
                                    "CUDA events per launch over three eager forwards)",
                          "peak_source": f"2 x {pk['source']} burst bf16 dense ({pk['bf16_tflops']} TF/s): "
                                         "fp8 dense rate is twice bf16"},

@@ -86,21 +86,22 @@ struct Cfg {
   static constexpr uint32_t OFF_STG = STAGES * STAGE_BYTES;
   static constexpr uint32_t OFF_RED = OFF_STG;
   static constexpr uint32_t STG_BYTES = DEFER ? BM * BN * 2 : EPI_WARPS * STG_WARP;
-  // EPI_QKV: per-(virtual warp, column) K sums and V absmax, [8][128] f32 each, and
-  // the four epilogue warps' Q block maxima
+  // EPI_QKV: per-(virtual warp, column) K sums or V absmax, [8][128] f32, and the
+  // four epilogue warps' Q block maxima of the tile's two heads
   static constexpr uint32_t OFF_QKV = OFF_STG + STG_BYTES;
-  static constexpr uint32_t QKV_BYTES = EPI == EPI_QKV ? 2 * 8 * 128 * 4 + 64 : 0;
+  static constexpr uint32_t QKV_BYTES = EPI == EPI_QKV ? 8 * 128 * 4 + 64 : 0;
   static constexpr uint32_t OFF_BAR = OFF_QKV + QKV_BYTES;
   static constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 /*barriers*/ + 1024 /*align*/;
   static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 };
 
-// Register split of the deferred-GELU kernel, launched with 128 registers per
-// thread x 512 threads (the whole register file): warps 0-3 (producer, MMA
-// issuer, two idle) keep 40, the eight promotion warps take 168 (their 128 fp32
-// accumulators), the four GELU warps keep 104:
-// 128 x 40 + 256 x 168 + 128 x 104 = 61440 registers, within the launch's
-// 65536 (and within 512 x 120, should the launch count ever be 120).
+// Register split of the deferred-epilogue kernels, launched with 128 registers
+// per thread x 512 threads (the whole register file; ptxas reports 128 for
+// these instantiations): warps 0-3 (producer, MMA issuer, two idle) keep 40, the
+// eight promotion warps take 168 (their 128 fp32 accumulators), the four
+// epilogue warps keep 104 (GELU) or take 136 (EPI_QKV: eight row reductions in
+// flight): 128 x 40 + 256 x 168 + 128 x 104 = 61440 and 128 x 40 + 256 x 168 +
+// 128 x 136 = 65536 registers, within the launch's 65536.
 template <int N>
 FD_DEV void reg_alloc() {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
@@ -292,6 +293,10 @@ FD_DEV bool named_bar_and(int id, int nthreads, bool pred) {
 }
 
 constexpr int QKV_BAR = 6;  // named barrier of the four EPI_QKV epilogue warps
+#ifndef FD_QKV_ROWS
+#define FD_QKV_ROWS 2
+#endif
+constexpr int QG = FD_QKV_ROWS;  // EPI_QKV row items per step (even: virtual warps alternate)
 
 // EPI_QKV epilogue of one 128 x 256 tile (two heads of Q, K or V) by the four
 // epilogue warps, from the promotion warps' bf16 copy of the tile (hbuf: row r at
@@ -312,101 +317,196 @@ FD_DEV void qkv_epilogue_tile(const Params& p, uint8_t* hbuf, float* red, int mb
   const int row0 = mb * BM;
   const int b = row0 / e.S, s0 = row0 - b * e.S;
   const int chunk = (e.s_off + s0) / 128;
-  float* sh_k = red;          // [8][128]
-  float* sh_v = red + 1024;   // [8][128]
-  float* sh_q = red + 2048;   // [4]
+  float* sh_k = red;          // [8][128] per-virtual-warp K sums or V absmax
+  float* sh_q = red + 1024;   // [2][4] per-warp Q block maxima
   const int t128 = w4 * 32 + lane;
   const float4 w4v = reinterpret_cast<const float4*>(part == 0 ? e.qw : e.kw)[lane];
   const float wv[4] = {w4v.x, w4v.y, w4v.z, w4v.w};
+  const int64_t bh0 = (int64_t)b * e.H + h0;
+  // this warp's 32 rows: item j -> row w4 + 4 (j & 1) + 8 (j >> 1), i.e. virtual
+  // warp w4 + 4 (j & 1), its (j >> 1)-th row
+  auto row_of = [&](int j) { return w4 + 4 * (j & 1) + 8 * (j >> 1); };
+  auto rot = [&](int j) {
+    return reinterpret_cast<const float4*>(e.freqs + (int64_t)(row0 + row_of(j)) * 256) + lane * 2;
+  };
+  // [head][virtual warp][column]: K column sums on K tiles, V column absmax on V tiles
+  float cs[2][2][4];
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+    for (int v = 0; v < 2; ++v)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) cs[hh][v][k] = 0.f;
+  float bmax[2] = {0.f, 0.f};
+  // QG row items at a time (rows j .. j + QG - 1 of the warp, both heads: 2 QG
+  // independent reduce / divide chains in flight; the rotations of the four rows
+  // are loaded first, behind the row norms).  The K sums still accumulate each
+  // virtual warp's rows in increasing order.
+  const bool rope = part != 2;
 #pragma unroll 1
-  for (int hh = 0; hh < 2; ++hh) {
-    const int64_t bh = (int64_t)b * e.H + h0 + hh;
-    float ks[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    float vm[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    float bmax = 0.f;
-#pragma unroll 1
-    for (int i = 0; i < 16; ++i) {
+  for (int j = 0; j < 32; j += QG) {
+    float4 f[QG][2];
+    if (rope) {
 #pragma unroll
-      for (int v = 0; v < 2; ++v) {
-        const int r = w4 + 4 * v + 8 * i;
-        const int64_t n = e.s_off + s0 + r;
-        uint8_t* hp = hbuf + r * 512 + ((((hh * 16) + (lane >> 1)) ^ (r & 7)) << 4) + ((lane & 1) << 3);
-        const uint2 u = *reinterpret_cast<const uint2*>(hp);
-        const float x[4] = {bf16_bits_to_f32(u.x & 0xFFFF), bf16_bits_to_f32(u.x >> 16),
-                            bf16_bits_to_f32(u.y & 0xFFFF), bf16_bits_to_f32(u.y >> 16)};
-        const int64_t o = (bh * e.Nj + n) * 128 + lane * 4;
-        if (part == 2) {
-          *reinterpret_cast<uint2*>(e.v_out + o) = u;
+      for (int g = 0; g < QG; ++g) {
+        f[g][0] = __ldg(rot(j + g));
+        f[g][1] = __ldg(rot(j + g) + 1);
+      }
+    }
+    uint2 u[QG][2];
+    float x[QG][2][4];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) vm[v][k] = fmaxf(vm[v][k], fabsf(x[k]));
-          continue;
+    for (int g = 0; g < QG; ++g) {
+      const int r = row_of(j + g);
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        u[g][hh] = *reinterpret_cast<const uint2*>(hbuf + r * 512 + ((((hh * 16) + (lane >> 1)) ^ (r & 7)) << 4) +
+                                                  ((lane & 1) << 3));
+        x[g][hh][0] = bf16_bits_to_f32(u[g][hh].x & 0xFFFF);
+        x[g][hh][1] = bf16_bits_to_f32(u[g][hh].x >> 16);
+        x[g][hh][2] = bf16_bits_to_f32(u[g][hh].y & 0xFFFF);
+        x[g][hh][3] = bf16_bits_to_f32(u[g][hh].y >> 16);
+      }
+    }
+    if (part == 2) {
+#pragma unroll
+      for (int g = 0; g < QG; ++g) {
+        const int64_t n = e.s_off + s0 + row_of(j + g);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          *reinterpret_cast<uint2*>(e.v_out + ((bh0 + hh) * e.Nj + n) * 128 + lane * 4) = u[g][hh];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) cs[hh][g & 1][k] = fmaxf(cs[hh][g & 1][k], fabsf(x[g][hh][k]));
         }
-        const float rr = p3_rinv(warp_sum(p3_sumsq4(x)), e.eps);
-        float y[4];
-        p3_rope4(x, rr, wv, reinterpret_cast<const float4*>(e.freqs + (int64_t)(row0 + r) * 256) + lane * 2, y);
+      }
+      continue;
+    }
+    float ss[QG][2];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) y[k] = round_to_bf16(y[k]);
-        const uint2 yb = make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
-        if (part == 1) {
-          *reinterpret_cast<uint2*>(e.k_out + o) = yb;
+    for (int g = 0; g < QG; ++g)
 #pragma unroll
-          for (int k = 0; k < 4; ++k) ks[v][k] += y[k];
-          continue;
+      for (int hh = 0; hh < 2; ++hh) ss[g][hh] = p3_sumsq4(x[g][hh]);
+    // the butterfly of warp_sum, eight sums side by side
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int g = 0; g < QG; ++g)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) ss[g][hh] += __shfl_xor_sync(0xffffffffu, ss[g][hh], o);
+    float y[QG][2][4];
+#pragma unroll
+    for (int g = 0; g < QG; ++g)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        p3_rope4(x[g][hh], p3_rinv(ss[g][hh], e.eps), wv, f[g], y[g][hh]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) y[g][hh][k] = round_to_bf16(y[g][hh][k]);
+      }
+    if (part == 1) {
+#pragma unroll
+      for (int g = 0; g < QG; ++g) {
+        const int64_t n = e.s_off + s0 + row_of(j + g);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          *reinterpret_cast<uint2*>(e.k_out + ((bh0 + hh) * e.Nj + n) * 128 + lane * 4) =
+              make_uint2(pack_bf16x2(y[g][hh][0], y[g][hh][1]), pack_bf16x2(y[g][hh][2], y[g][hh][3]));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) cs[hh][g & 1][k] += y[g][hh][k];
         }
-        const float qa = fmaxf(fmaxf(fabsf(y[0]), fabsf(y[1])), fmaxf(fabsf(y[2]), fabsf(y[3])));
-        if (e.q_gran == FD_GRAN_TOKEN) {
-          const float am = warp_max(qa);
+      }
+      continue;
+    }
+    float qa[QG][2];
+#pragma unroll
+    for (int g = 0; g < QG; ++g)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+        qa[g][hh] = fmaxf(fmaxf(fabsf(y[g][hh][0]), fabsf(y[g][hh][1])), fmaxf(fabsf(y[g][hh][2]), fabsf(y[g][hh][3])));
+    if (e.q_gran == FD_GRAN_TOKEN) {
+      // warp_max's butterfly, eight maxima side by side
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int g = 0; g < QG; ++g)
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) qa[g][hh] = fmaxf(qa[g][hh], __shfl_xor_sync(0xffffffffu, qa[g][hh], o));
+#pragma unroll
+      for (int g = 0; g < QG; ++g) {
+        const int64_t n = e.s_off + s0 + row_of(j + g);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const float am = qa[g][hh];
           const float inv = div_full(qmax, fmaxf(am, 1e-12f));
-          *reinterpret_cast<uint32_t*>(e.q_codes + o) = quant_code<QK>(y[0], inv) | (quant_code<QK>(y[1], inv) << 8) |
-                                                       (quant_code<QK>(y[2], inv) << 16) |
-                                                       (quant_code<QK>(y[3], inv) << 24);
-          if (lane == 0) e.q_desc[bh * e.q_desc_stride + n] = div_full(am, qmax) * e.sm_scale_log2e;
-        } else {
-          bmax = fmaxf(bmax, qa);
-          *reinterpret_cast<uint2*>(hp) = yb;  // kept until the block's absmax is known
+          *reinterpret_cast<uint32_t*>(e.q_codes + ((bh0 + hh) * e.Nj + n) * 128 + lane * 4) =
+              quant_code<QK>(y[g][hh][0], inv) | (quant_code<QK>(y[g][hh][1], inv) << 8) |
+              (quant_code<QK>(y[g][hh][2], inv) << 16) | (quant_code<QK>(y[g][hh][3], inv) << 24);
+          if (lane == 0) e.q_desc[(bh0 + hh) * e.q_desc_stride + n] = div_full(am, qmax) * e.sm_scale_log2e;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int g = 0; g < QG; ++g) {
+        const int r = row_of(j + g);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          bmax[hh] = fmaxf(bmax[hh], qa[g][hh]);
+          // kept until the block's absmax is known
+          *reinterpret_cast<uint2*>(hbuf + r * 512 + ((((hh * 16) + (lane >> 1)) ^ (r & 7)) << 4) + ((lane & 1) << 3)) =
+              make_uint2(pack_bf16x2(y[g][hh][0], y[g][hh][1]), pack_bf16x2(y[g][hh][2], y[g][hh][3]));
         }
       }
     }
-    if (part != 0) {
+  }
+  if (part != 0) {
+#pragma unroll 1
+    for (int hh = 0; hh < 2; ++hh) {
+      const int64_t bh = bh0 + hh;
 #pragma unroll
       for (int v = 0; v < 2; ++v)
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          sh_k[(w4 + 4 * v) * 128 + lane * 4 + k] = ks[v][k];
-          sh_v[(w4 + 4 * v) * 128 + lane * 4 + k] = vm[v][k];
-        }
+        for (int k = 0; k < 4; ++k) sh_k[(w4 + 4 * v) * 128 + lane * 4 + k] = cs[hh][v][k];
       named_bar_sync(QKV_BAR, 128);
       const int c = t128;
       float tsum = 0.f, amax = 0.f;
 #pragma unroll
       for (int w = 0; w < 8; ++w) {
         tsum += sh_k[w * 128 + c];
-        amax = fmaxf(amax, sh_v[w * 128 + c]);
+        amax = fmaxf(amax, sh_k[w * 128 + c]);
       }
       if (part == 1) e.ws_sum[(bh * e.nchunks + chunk) * 128 + c] = tsum;
       else if (e.do_v) e.ws_amax[(bh * e.nchunks + chunk) * 128 + c] = amax;
       named_bar_sync(QKV_BAR, 128);
-    } else if (e.q_gran == FD_GRAN_BLOCK) {
-      bmax = warp_max(bmax);
-      if (lane == 0) sh_q[w4] = bmax;
-      named_bar_sync(QKV_BAR, 128);
-      const float mx = fmaxf(fmaxf(sh_q[0], sh_q[1]), fmaxf(sh_q[2], sh_q[3]));
-      if (t128 == 0) e.q_desc[bh * e.q_desc_stride + chunk] = div_full(mx, qmax) * e.sm_scale_log2e;
-      const float inv = div_full(qmax, fmaxf(mx, 1e-12f));
+    }
+  } else if (e.q_gran == FD_GRAN_BLOCK) {
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const float m = warp_max(bmax[hh]);
+      if (lane == 0) sh_q[hh * 4 + w4] = m;
+    }
+    named_bar_sync(QKV_BAR, 128);
+    float inv[2];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const float mx = fmaxf(fmaxf(sh_q[hh * 4], sh_q[hh * 4 + 1]), fmaxf(sh_q[hh * 4 + 2], sh_q[hh * 4 + 3]));
+      if (t128 == 0) e.q_desc[(bh0 + hh) * e.q_desc_stride + chunk] = div_full(mx, qmax) * e.sm_scale_log2e;
+      inv[hh] = div_full(qmax, fmaxf(mx, 1e-12f));
+    }
 #pragma unroll 4
-      for (int j = 0; j < 32; ++j) {
-        const int r = w4 + 4 * (j & 1) + 8 * (j >> 1);
-        const int64_t n = e.s_off + s0 + r;
+    for (int j = 0; j < 32; ++j) {
+      const int r = row_of(j);
+      const int64_t n = e.s_off + s0 + r;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
         const uint2 u = *reinterpret_cast<const uint2*>(hbuf + r * 512 + ((((hh * 16) + (lane >> 1)) ^ (r & 7)) << 4) +
                                                          ((lane & 1) << 3));
         const float y[4] = {bf16_bits_to_f32(u.x & 0xFFFF), bf16_bits_to_f32(u.x >> 16),
                             bf16_bits_to_f32(u.y & 0xFFFF), bf16_bits_to_f32(u.y >> 16)};
-        *reinterpret_cast<uint32_t*>(e.q_codes + (bh * e.Nj + n) * 128 + lane * 4) =
-            quant_code<QK>(y[0], inv) | (quant_code<QK>(y[1], inv) << 8) | (quant_code<QK>(y[2], inv) << 16) |
-            (quant_code<QK>(y[3], inv) << 24);
+        *reinterpret_cast<uint32_t*>(e.q_codes + ((bh0 + hh) * e.Nj + n) * 128 + lane * 4) =
+            quant_code<QK>(y[0], inv[hh]) | (quant_code<QK>(y[1], inv[hh]) << 8) |
+            (quant_code<QK>(y[2], inv[hh]) << 16) | (quant_code<QK>(y[3], inv[hh]) << 24);
       }
-      named_bar_sync(QKV_BAR, 128);
     }
+    named_bar_sync(QKV_BAR, 128);
   }
 }
 
@@ -583,7 +683,8 @@ __global__ void __launch_bounds__(Cfg<EPI>::THREADS, 1)
     // computed GELU of bf16 inputs keeps that order: neighbouring inputs differ by
     // 2^-8 relative, far above fp32 rounding); otherwise every value is
     // evaluated as before.  The codes then take one GELU per value.
-    reg_dealloc<104>();
+    if constexpr (EPI == EPI_QKV) reg_alloc<136>();
+    else reg_dealloc<104>();
     const int t = (warp - CF::GELU_WARP0) * 32 + lane;
     const uint8_t* hrow = smem + CF::OFF_STG + t * 512;
     uint32_t nt = 0;

@@ -51,7 +51,14 @@ from .fused_kernels import (
     fused_rms_norm_modulate_quant,
     qkv_postprocess_into,
 )
-from .sage_attention import _attn_forward, attn_forward_quant_out, attn_quant_out_from_streams, fused_prologue_ok
+from .sage_attention import (
+    _attn_forward,
+    attn_forward_quant_out,
+    attn_quant_out_from_linear,
+    attn_quant_out_from_streams,
+    fused_prologue_ok,
+    linear_prologue_ok,
+)
 
 HEAD_DIM = 128
 
@@ -236,15 +243,23 @@ class DoubleStreamBlock(nn.Module):
         # norm + 1 x 128 quant in one pass, straight into the QKV GEMMs
         hs = [fused_rms_norm_modulate_quant(x, st.norm_w[0], m[0].contiguous(), cfg.eps)
               for st, x, m in zip(sts, xs, mods)]
-        qkvs = both(lambda st: st.qkv, hs)
         # attention output as each stream's out-projection input: text rows to one
         # code buffer, image rows to the other (no split copy, no separate quantiser)
         dev, D = x_txt.device, cfg.hidden
         codes = [(torch.empty(B, n, D, dtype=torch.float8_e4m3fn, device=dev),
                   torch.empty(B, n, D // 128, dtype=torch.float32, device=dev)) for n in (Nt, N - Nt)]
-        streams = [(qkvs[0], self.txt.q_norm, self.txt.k_norm, freqs_txt, 0, cfg.eps),
-                   (qkvs[1], self.img.q_norm, self.img.k_norm, freqs_img, Nt, cfg.eps)]
-        joint_prologue_attention(streams, cfg, N, codes, split=Nt)
+        freqs = (freqs_txt, freqs_img)
+        if linear_prologue_ok([Nt, N - Nt], cfg.heads):
+            # both QKV linears in one launch, P3 and the Q quantisation in its epilogue
+            lin = [(h8, h_s, st.qkv.weight, st.qkv.weight_scale, st.qkv.bias, st.q_norm, st.k_norm, fr, off, cfg.eps)
+                   for st, (h8, h_s), fr, off in zip(sts, hs, freqs, (0, Nt))]
+            attn_quant_out_from_linear(lin, cfg.heads, N, None, block_mask=None, qk_quant=cfg.qk_quant,
+                                       pv_quant=cfg.pv_quant, granularity=cfg.granularity, regions=codes, split=Nt)
+        else:
+            qkvs = both(lambda st: st.qkv, hs)
+            streams = [(qkvs[0], self.txt.q_norm, self.txt.k_norm, freqs_txt, 0, cfg.eps),
+                       (qkvs[1], self.img.q_norm, self.img.k_norm, freqs_img, Nt, cfg.eps)]
+            joint_prologue_attention(streams, cfg, N, codes, split=Nt)
         attn = both(lambda st: st.proj, codes)
         xs = [fused_rms_norm_gate_residual(a, st.norm_w[1], m[1].contiguous(), x, cfg.eps)
               for st, a, x, m in zip(sts, attn, xs, mods)]
@@ -285,15 +300,21 @@ class SingleStreamBlock(nn.Module):
         a8, a_s = fused_rms_norm_modulate_quant(x, self.norm_w[0], scale.contiguous(), cfg.eps)
         w, ws = self.linear1.weight, self.linear1.weight_scale
         n_qkv = 3 * D
-        qkv = fp8_gemm_blockwise(a8, a_s, w[:n_qkv], ws[: n_qkv // 128], output_dtype=torch.bfloat16)
         # linear2's input [attention | MLP] as 1 x 128 codes: the GELU GEMM and the
         # attention write their halves of the same rows in place
         W = self.linear2.weight.shape[1]
         cat8 = torch.empty(B, N, W, dtype=torch.float8_e4m3fn, device=x.device)
         cat_s = torch.empty(B, N, W // 128, dtype=torch.float32, device=x.device)
         fp8_gemm_gelu_tanh_quant(a8, a_s, w[n_qkv:], ws[n_qkv // 128:], out=(cat8[..., D:], cat_s[..., D // 128:]))
-        joint_prologue_attention([(qkv, self.q_norm, self.k_norm, freqs, 0, cfg.eps)], cfg, N,
-                                 [(cat8[..., :D], cat_s[..., :D // 128])])
+        region = [(cat8[..., :D], cat_s[..., :D // 128])]
+        if linear_prologue_ok([N], cfg.heads):
+            # the QKV rows of linear1 with P3 and the Q quantisation in the GEMM epilogue
+            lin = [(a8, a_s, w[:n_qkv], ws[: n_qkv // 128], None, self.q_norm, self.k_norm, freqs, 0, cfg.eps)]
+            attn_quant_out_from_linear(lin, cfg.heads, N, None, block_mask=None, qk_quant=cfg.qk_quant,
+                                       pv_quant=cfg.pv_quant, granularity=cfg.granularity, regions=region)
+        else:
+            qkv = fp8_gemm_blockwise(a8, a_s, w[:n_qkv], ws[: n_qkv // 128], output_dtype=torch.bfloat16)
+            joint_prologue_attention([(qkv, self.q_norm, self.k_norm, freqs, 0, cfg.eps)], cfg, N, region)
         y = fp8_gemm_blockwise(cat8, cat_s, self.linear2.weight, self.linear2.weight_scale,
                                output_dtype=torch.bfloat16)
         return fused_rms_norm_gate_residual(y, self.norm_w[1], gate.contiguous(), x, cfg.eps)
