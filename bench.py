@@ -503,8 +503,10 @@ def time_gemm(dev, shape: str, steps: int, warmup: int, epilogue: str = "bf16") 
     """CUDA-event durations (ms) of ``steps`` FP8 block-GEMM launches at one of
     GEMM_SHAPES, with a 256 MiB write between launches so that every launch reads
     its operands from HBM (the operands of the smaller shapes fit in L2).
-    ``epilogue``: "bf16" output, or "gelu" (GELU(tanh) + 1 x 128 e4m3 requant, the
-    MMDiT MLP-in epilogue)."""
+    ``epilogue``: "bf16" output, "gelu" (GELU(tanh) + 1 x 128 e4m3 requant, the
+    MMDiT MLP-in epilogue) or "qkv" (the config-4 single-stream QKV linear, rows =
+    samples x 4608 tokens, N = 3 x 24 heads x 128, with P3 and the Q quantisation in
+    its epilogue: fd_fp8_gemm_qkv_quant, INT8 per-block Q, one launch)."""
     from futudiffu_b200 import _lib as L
     from futudiffu_b200.fp8 import quantize_fp8_blockwise_cuda
     from futudiffu_b200.fp8_kernels import fp8_act_quant
@@ -517,7 +519,27 @@ def time_gemm(dev, shape: str, steps: int, warmup: int, epilogue: str = "bf16") 
     a8, a_s = fp8_act_quant(x)
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
-    if epilogue == "gelu":
+    if epilogue == "qkv":
+        H, S = N // 384, 4608
+        assert N == 3 * H * 128 and M % S == 0
+        Bq = M // S
+        qn = torch.ones(128, dtype=torch.float32, device=dev)
+        fr = torch.zeros(M, 64, 2, 2, dtype=torch.float32, device=dev)
+        fr[:, :, 0, 0] = fr[:, :, 1, 1] = 1.0
+        q_codes = torch.empty(Bq * H, S, 128, dtype=torch.int8, device=dev)
+        q_desc = torch.empty(Bq * H, S // 128, dtype=torch.float32, device=dev)
+        k_out = torch.empty(Bq * H, S, 128, dtype=torch.bfloat16, device=dev)
+        v_out = torch.empty_like(k_out)
+        wsp = torch.empty(int(L.lib().fd_qkv_quant_workspace_floats(Bq * H, S)), dtype=torch.float32, device=dev)
+        prob = L.GemmProblem(L.ptr(a8), L.ptr(a_s), L.ptr(w8), L.ptr(ws), None, None, None, M, N, K)
+        desc = L.QkvStream(L.ptr(qn), L.ptr(qn), L.ptr(fr), S, 0, 1e-6)
+        import ctypes
+
+        def gemm():
+            L.call("fd_fp8_gemm_qkv_quant", ctypes.addressof(prob), ctypes.addressof(desc), None, None, L.DT_BF16,
+                   Bq, H, S, L.QK_INT8, L.GRAN_BLOCK, L.PV_BF16, 0.1275, L.ptr(q_codes), L.ptr(q_desc),
+                   L.ptr(k_out), L.ptr(v_out), L.ptr(wsp), L.stream_ptr(dev))
+    elif epilogue == "gelu":
         c = torch.empty(M, N, dtype=torch.uint8, device=dev)
         c_s = torch.empty(M, N // 128, dtype=torch.float32, device=dev)
 
@@ -1161,7 +1183,8 @@ def run_video(args, world, rank, local):
 # config 1, the reference benchmark's Z-Image QKV / FFN-out shapes, and the config-4
 # MLP-in linear at one sample (4608 tokens) and at the batch of 8
 GEMM_SHAPES = {"config1": (2048, 3072, 3072), "ref_qkv": (8576, 11520, 3840), "ref_w2": (8576, 3840, 10240),
-               "dit_mlp_in": (4608, 12288, 3072), "dit_mlp_in_b8": (36864, 12288, 3072)}
+               "dit_mlp_in": (4608, 12288, 3072), "dit_mlp_in_b8": (36864, 12288, 3072),
+               "dit_qkv": (4608, 9216, 3072), "dit_qkv_b8": (36864, 9216, 3072)}
 
 
 PACKED_METRIC = "packed multi-image forward tokens/s (Z-Image-class blocks, 3840 hidden, 30 heads, 4288-token bin)"
@@ -1374,7 +1397,9 @@ def run_gemm(args, world, rank, local):
             "scaling": "weak", "vs_baseline": None, "dtype": "fp8 e4m3 (1x128 / 128x128 f32 scales)",
             "data": "synthetic",
             "config": {"workload": f"gemm_{args.gemm_shape}", "M": M, "N": N, "K": K, "l2": "flushed",
-                       "epilogue": "GELU(tanh) + 1x128 e4m3 requant" if args.gemm_epilogue == "gelu" else "bf16"},
+                       "epilogue": {"gelu": "GELU(tanh) + 1x128 e4m3 requant",
+                                    "qkv": "P3 + INT8 per-block Q codes, bf16 K / V, K / V column statistics"}.get(
+                                        args.gemm_epilogue, "bf16")},
             "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
                          "frac": tf / peak, "traffic": GEMM_TRAFFIC_BYTES.get(args.gemm_shape),
                          "peak_source": f"2 x {pk['source']} bf16 dense: fp8 dense rate is twice bf16"},
@@ -1486,8 +1511,9 @@ def main(argv=None) -> int:
                          "attention = config 2; gemm = config 1; packed = the reference's packed "
                          "4288-token bin through Z-Image-class JointTransformerBlocks")
     ap.add_argument("--gemm-shape", choices=sorted(GEMM_SHAPES), default="config1")
-    ap.add_argument("--gemm-epilogue", choices=["bf16", "gelu"], default="bf16",
-                    help="gemm: bf16 output or the GELU(tanh) + 1x128 requant epilogue")
+    ap.add_argument("--gemm-epilogue", choices=["bf16", "gelu", "qkv"], default="bf16",
+                    help="gemm: bf16 output, the GELU(tanh) + 1x128 requant epilogue, or the QKV "
+                         "linear's fused P3 + Q-quantisation epilogue (--gemm-shape dit_qkv*)")
     ap.add_argument("--layers", type=int, default=30, help="packed: JointTransformerBlocks in the stack")
     ap.add_argument("--no-sub", action="store_true",
                     help="dit: skip the config-1 GEMM / config-2 attention sub-measurements")

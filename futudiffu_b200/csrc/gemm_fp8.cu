@@ -86,10 +86,10 @@ struct Cfg {
   static constexpr uint32_t OFF_STG = STAGES * STAGE_BYTES;
   static constexpr uint32_t OFF_RED = OFF_STG;
   static constexpr uint32_t STG_BYTES = DEFER ? BM * BN * 2 : EPI_WARPS * STG_WARP;
-  // EPI_QKV: per-(virtual warp, column) K sums or V absmax, [8][128] f32, and the
-  // four epilogue warps' Q block maxima of the tile's two heads
+  // EPI_QKV: per-(head, virtual warp, column) K sums or V absmax, [2][8][128] f32,
+  // and the Q block maxima per (head, virtual warp)
   static constexpr uint32_t OFF_QKV = OFF_STG + STG_BYTES;
-  static constexpr uint32_t QKV_BYTES = EPI == EPI_QKV ? 8 * 128 * 4 + 64 : 0;
+  static constexpr uint32_t QKV_BYTES = EPI == EPI_QKV ? 2 * 8 * 128 * 4 + 64 : 0;
   static constexpr uint32_t OFF_BAR = OFF_QKV + QKV_BYTES;
   static constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 /*barriers*/ + 1024 /*align*/;
   static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
@@ -99,8 +99,8 @@ struct Cfg {
 // per thread x 512 threads (the whole register file; ptxas reports 128 for
 // these instantiations): warps 0-3 (producer, MMA issuer, two idle) keep 40, the
 // eight promotion warps take 168 (their 128 fp32 accumulators), the four
-// epilogue warps keep 104 (GELU) or take 136 (EPI_QKV: eight row reductions in
-// flight): 128 x 40 + 256 x 168 + 128 x 104 = 61440 and 128 x 40 + 256 x 168 +
+// epilogue warps keep 104 (GELU) or take 136 (EPI_QKV: each lane holds 16 values
+// of a row and their rotations): 128 x 40 + 256 x 168 + 128 x 104 = 61440 and 128 x 40 + 256 x 168 +
 // 128 x 136 = 65536 registers, within the launch's 65536.
 template <int N>
 FD_DEV void reg_alloc() {
@@ -293,19 +293,19 @@ FD_DEV bool named_bar_and(int id, int nthreads, bool pred) {
 }
 
 constexpr int QKV_BAR = 6;  // named barrier of the four EPI_QKV epilogue warps
-#ifndef FD_QKV_ROWS
-#define FD_QKV_ROWS 2
-#endif
-constexpr int QG = FD_QKV_ROWS;  // EPI_QKV row items per step (even: virtual warps alternate)
 
 // EPI_QKV epilogue of one 128 x 256 tile (two heads of Q, K or V) by the four
 // epilogue warps, from the promotion warps' bf16 copy of the tile (hbuf: row r at
-// r * 512, 16-byte chunk c of the row at c ^ (r & 7)).  The row / lane mapping and
-// every sum run in the order of qkv_quant_kernel (attn_prologue.cu): lane l holds
-// columns 4l .. 4l + 3 of a head, "virtual warp" v in 0..7 takes rows v + 8 i in
-// increasing i (real warp w4 plays v = w4 and v = w4 + 4), and the K sums of the
-// eight virtual warps are added in order, so the codes, descales, bf16 K / V and
-// workspace partials equal that kernel's bit for bit.
+// r * 512, 16-byte chunk c of the row at c ^ (r & 7)).  Every value, sum and code
+// equals qkv_quant_kernel's (attn_prologue.cu) bit for bit.  That kernel gives a
+// (row, head) to a warp, lane L holding columns 4L .. 4L + 3, and its "virtual
+// warp" v in 0..7 takes rows v + 8 i in increasing i.  Here eight lanes share a
+// (row, head): lane l of a group plays lanes l, l + 8, l + 16 and l + 24, whose
+// partial sums of squares it adds as the xor-16 and xor-8 steps of the warp
+// butterfly would ((p0 + p2) + (p1 + p3)); the xor-4 / 2 / 1 steps stay inside the
+// group.  Group g of warp w4 is virtual warp 2 w4 + (g & 1) for head g >> 1, so
+// each K / V column sum still runs over a virtual warp's rows in increasing order
+// and over the eight virtual warps in order.
 template <int QK>
 FD_DEV void qkv_epilogue_tile(const Params& p, uint8_t* hbuf, float* red, int mb, int nb, int w4, int lane) {
   const QkvEpi& e = p.qe;
@@ -317,193 +317,147 @@ FD_DEV void qkv_epilogue_tile(const Params& p, uint8_t* hbuf, float* red, int mb
   const int row0 = mb * BM;
   const int b = row0 / e.S, s0 = row0 - b * e.S;
   const int chunk = (e.s_off + s0) / 128;
-  float* sh_k = red;          // [8][128] per-virtual-warp K sums or V absmax
-  float* sh_q = red + 1024;   // [2][4] per-warp Q block maxima
+  const int grp = lane >> 3, l8 = lane & 7;
+  const int vw = 2 * w4 + (grp & 1);  // virtual warp
+  const int hh = grp >> 1;            // head of the tile
+  const int64_t bh = (int64_t)b * e.H + h0 + hh;
+  float* sh_c = red;                  // [2 heads][8 virtual warps][128] K sums or V absmax
+  float* sh_q = red + 2048;           // [2 heads][8 virtual warps] Q block maxima
   const int t128 = w4 * 32 + lane;
-  const float4 w4v = reinterpret_cast<const float4*>(part == 0 ? e.qw : e.kw)[lane];
-  const float wv[4] = {w4v.x, w4v.y, w4v.z, w4v.w};
-  const int64_t bh0 = (int64_t)b * e.H + h0;
-  // this warp's 32 rows: item j -> row w4 + 4 (j & 1) + 8 (j >> 1), i.e. virtual
-  // warp w4 + 4 (j & 1), its (j >> 1)-th row
-  auto row_of = [&](int j) { return w4 + 4 * (j & 1) + 8 * (j >> 1); };
-  auto rot = [&](int j) {
-    return reinterpret_cast<const float4*>(e.freqs + (int64_t)(row0 + row_of(j)) * 256) + lane * 2;
+  // the norm weights (read at use from L1: registers go to the row's values)
+  const float4* wp = reinterpret_cast<const float4*>(part == 0 ? e.qw : e.kw);
+  float cs[4][4];  // K column sums / V column absmax of the four played lanes
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) cs[q][k] = 0.f;
+  float bmax = 0.f;
+  // smem address of played lane q's four values in row r
+  auto haddr = [&](int r, int q) {
+    return hbuf + r * 512 + ((((hh * 16) + 4 * q + (l8 >> 1)) ^ (r & 7)) << 4) + ((l8 & 1) << 3);
   };
-  // [head][virtual warp][column]: K column sums on K tiles, V column absmax on V tiles
-  float cs[2][2][4];
-#pragma unroll
-  for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-    for (int v = 0; v < 2; ++v)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) cs[hh][v][k] = 0.f;
-  float bmax[2] = {0.f, 0.f};
-  // QG row items at a time (rows j .. j + QG - 1 of the warp, both heads: 2 QG
-  // independent reduce / divide chains in flight; the rotations of the four rows
-  // are loaded first, behind the row norms).  The K sums still accumulate each
-  // virtual warp's rows in increasing order.
-  const bool rope = part != 2;
 #pragma unroll 1
-  for (int j = 0; j < 32; j += QG) {
-    float4 f[QG][2];
-    if (rope) {
+  for (int i = 0; i < 16; ++i) {
+    const int r = vw + 8 * i;
+    const int64_t n = e.s_off + s0 + r;
+    const int64_t obase = (bh * e.Nj + n) * 128 + 4 * l8;  // + 32 q: played lane l8 + 8 q
+    float4 f[4][2];
+    if (part != 2) {
+      const float4* fr = reinterpret_cast<const float4*>(e.freqs + (int64_t)(row0 + r) * 256);
 #pragma unroll
-      for (int g = 0; g < QG; ++g) {
-        f[g][0] = __ldg(rot(j + g));
-        f[g][1] = __ldg(rot(j + g) + 1);
+      for (int q = 0; q < 4; ++q) {
+        f[q][0] = __ldg(fr + 2 * (l8 + 8 * q));
+        f[q][1] = __ldg(fr + 2 * (l8 + 8 * q) + 1);
       }
     }
-    uint2 u[QG][2];
-    float x[QG][2][4];
+    uint2 u[4];
+    float x[4][4];
 #pragma unroll
-    for (int g = 0; g < QG; ++g) {
-      const int r = row_of(j + g);
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        u[g][hh] = *reinterpret_cast<const uint2*>(hbuf + r * 512 + ((((hh * 16) + (lane >> 1)) ^ (r & 7)) << 4) +
-                                                  ((lane & 1) << 3));
-        x[g][hh][0] = bf16_bits_to_f32(u[g][hh].x & 0xFFFF);
-        x[g][hh][1] = bf16_bits_to_f32(u[g][hh].x >> 16);
-        x[g][hh][2] = bf16_bits_to_f32(u[g][hh].y & 0xFFFF);
-        x[g][hh][3] = bf16_bits_to_f32(u[g][hh].y >> 16);
-      }
+    for (int q = 0; q < 4; ++q) {
+      u[q] = *reinterpret_cast<const uint2*>(haddr(r, q));
+      x[q][0] = bf16_bits_to_f32(u[q].x & 0xFFFF);
+      x[q][1] = bf16_bits_to_f32(u[q].x >> 16);
+      x[q][2] = bf16_bits_to_f32(u[q].y & 0xFFFF);
+      x[q][3] = bf16_bits_to_f32(u[q].y >> 16);
     }
     if (part == 2) {
 #pragma unroll
-      for (int g = 0; g < QG; ++g) {
-        const int64_t n = e.s_off + s0 + row_of(j + g);
+      for (int q = 0; q < 4; ++q) {
+        *reinterpret_cast<uint2*>(e.v_out + obase + 32 * q) = u[q];
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          *reinterpret_cast<uint2*>(e.v_out + ((bh0 + hh) * e.Nj + n) * 128 + lane * 4) = u[g][hh];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) cs[hh][g & 1][k] = fmaxf(cs[hh][g & 1][k], fabsf(x[g][hh][k]));
-        }
+        for (int k = 0; k < 4; ++k) cs[q][k] = fmaxf(cs[q][k], fabsf(x[q][k]));
       }
       continue;
     }
-    float ss[QG][2];
+    float ss = __fadd_rn(__fadd_rn(p3_sumsq4(x[0]), p3_sumsq4(x[2])), __fadd_rn(p3_sumsq4(x[1]), p3_sumsq4(x[3])));
 #pragma unroll
-    for (int g = 0; g < QG; ++g)
+    for (int o = 4; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rr = p3_rinv(ss, e.eps);
+    float y[4][4];
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) ss[g][hh] = p3_sumsq4(x[g][hh]);
-    // the butterfly of warp_sum, eight sums side by side
+    for (int q = 0; q < 4; ++q) {
+      const float4 t = __ldg(wp + l8 + 8 * q);
+      const float wq[4] = {t.x, t.y, t.z, t.w};
+      p3_rope4(x[q], rr, wq, f[q], y[q]);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int g = 0; g < QG; ++g)
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) ss[g][hh] += __shfl_xor_sync(0xffffffffu, ss[g][hh], o);
-    float y[QG][2][4];
-#pragma unroll
-    for (int g = 0; g < QG; ++g)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        p3_rope4(x[g][hh], p3_rinv(ss[g][hh], e.eps), wv, f[g], y[g][hh]);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) y[g][hh][k] = round_to_bf16(y[g][hh][k]);
-      }
+      for (int k = 0; k < 4; ++k) y[q][k] = round_to_bf16(y[q][k]);
+    }
     if (part == 1) {
 #pragma unroll
-      for (int g = 0; g < QG; ++g) {
-        const int64_t n = e.s_off + s0 + row_of(j + g);
+      for (int q = 0; q < 4; ++q) {
+        *reinterpret_cast<uint2*>(e.k_out + obase + 32 * q) =
+            make_uint2(pack_bf16x2(y[q][0], y[q][1]), pack_bf16x2(y[q][2], y[q][3]));
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          *reinterpret_cast<uint2*>(e.k_out + ((bh0 + hh) * e.Nj + n) * 128 + lane * 4) =
-              make_uint2(pack_bf16x2(y[g][hh][0], y[g][hh][1]), pack_bf16x2(y[g][hh][2], y[g][hh][3]));
-#pragma unroll
-          for (int k = 0; k < 4; ++k) cs[hh][g & 1][k] += y[g][hh][k];
-        }
+        for (int k = 0; k < 4; ++k) cs[q][k] += y[q][k];
       }
       continue;
     }
-    float qa[QG][2];
+    float qa = 0.f;
 #pragma unroll
-    for (int g = 0; g < QG; ++g)
+    for (int q = 0; q < 4; ++q)
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh)
-        qa[g][hh] = fmaxf(fmaxf(fabsf(y[g][hh][0]), fabsf(y[g][hh][1])), fmaxf(fabsf(y[g][hh][2]), fabsf(y[g][hh][3])));
+      for (int k = 0; k < 4; ++k) qa = fmaxf(qa, fabsf(y[q][k]));
     if (e.q_gran == FD_GRAN_TOKEN) {
-      // warp_max's butterfly, eight maxima side by side
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
+      for (int o = 4; o > 0; o >>= 1) qa = fmaxf(qa, __shfl_xor_sync(0xffffffffu, qa, o));
+      const float inv = div_full(qmax, fmaxf(qa, 1e-12f));
 #pragma unroll
-        for (int g = 0; g < QG; ++g)
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) qa[g][hh] = fmaxf(qa[g][hh], __shfl_xor_sync(0xffffffffu, qa[g][hh], o));
-#pragma unroll
-      for (int g = 0; g < QG; ++g) {
-        const int64_t n = e.s_off + s0 + row_of(j + g);
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const float am = qa[g][hh];
-          const float inv = div_full(qmax, fmaxf(am, 1e-12f));
-          *reinterpret_cast<uint32_t*>(e.q_codes + ((bh0 + hh) * e.Nj + n) * 128 + lane * 4) =
-              quant_code<QK>(y[g][hh][0], inv) | (quant_code<QK>(y[g][hh][1], inv) << 8) |
-              (quant_code<QK>(y[g][hh][2], inv) << 16) | (quant_code<QK>(y[g][hh][3], inv) << 24);
-          if (lane == 0) e.q_desc[(bh0 + hh) * e.q_desc_stride + n] = div_full(am, qmax) * e.sm_scale_log2e;
-        }
-      }
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<uint32_t*>(e.q_codes + obase + 32 * q) =
+            quant_code<QK>(y[q][0], inv) | (quant_code<QK>(y[q][1], inv) << 8) |
+            (quant_code<QK>(y[q][2], inv) << 16) | (quant_code<QK>(y[q][3], inv) << 24);
+      if (l8 == 0) e.q_desc[bh * e.q_desc_stride + n] = div_full(qa, qmax) * e.sm_scale_log2e;
     } else {
+      bmax = fmaxf(bmax, qa);
 #pragma unroll
-      for (int g = 0; g < QG; ++g) {
-        const int r = row_of(j + g);
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          bmax[hh] = fmaxf(bmax[hh], qa[g][hh]);
-          // kept until the block's absmax is known
-          *reinterpret_cast<uint2*>(hbuf + r * 512 + ((((hh * 16) + (lane >> 1)) ^ (r & 7)) << 4) + ((lane & 1) << 3)) =
-              make_uint2(pack_bf16x2(y[g][hh][0], y[g][hh][1]), pack_bf16x2(y[g][hh][2], y[g][hh][3]));
-        }
-      }
+      for (int q = 0; q < 4; ++q)  // kept until the block's absmax is known
+        *reinterpret_cast<uint2*>(haddr(r, q)) = make_uint2(pack_bf16x2(y[q][0], y[q][1]), pack_bf16x2(y[q][2], y[q][3]));
     }
   }
   if (part != 0) {
-#pragma unroll 1
-    for (int hh = 0; hh < 2; ++hh) {
-      const int64_t bh = bh0 + hh;
 #pragma unroll
-      for (int v = 0; v < 2; ++v)
+    for (int q = 0; q < 4; ++q)
 #pragma unroll
-        for (int k = 0; k < 4; ++k) sh_k[(w4 + 4 * v) * 128 + lane * 4 + k] = cs[hh][v][k];
-      named_bar_sync(QKV_BAR, 128);
-      const int c = t128;
+      for (int k = 0; k < 4; ++k) sh_c[(hh * 8 + vw) * 128 + 4 * (l8 + 8 * q) + k] = cs[q][k];
+    named_bar_sync(QKV_BAR, 128);
+    const int c = t128;
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const int64_t bh2 = (int64_t)b * e.H + h0 + h2;
       float tsum = 0.f, amax = 0.f;
 #pragma unroll
       for (int w = 0; w < 8; ++w) {
-        tsum += sh_k[w * 128 + c];
-        amax = fmaxf(amax, sh_k[w * 128 + c]);
+        const float t = sh_c[(h2 * 8 + w) * 128 + c];
+        tsum += t;
+        amax = fmaxf(amax, t);
       }
-      if (part == 1) e.ws_sum[(bh * e.nchunks + chunk) * 128 + c] = tsum;
-      else if (e.do_v) e.ws_amax[(bh * e.nchunks + chunk) * 128 + c] = amax;
-      named_bar_sync(QKV_BAR, 128);
-    }
-  } else if (e.q_gran == FD_GRAN_BLOCK) {
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const float m = warp_max(bmax[hh]);
-      if (lane == 0) sh_q[hh * 4 + w4] = m;
+      if (part == 1) e.ws_sum[(bh2 * e.nchunks + chunk) * 128 + c] = tsum;
+      else if (e.do_v) e.ws_amax[(bh2 * e.nchunks + chunk) * 128 + c] = amax;
     }
     named_bar_sync(QKV_BAR, 128);
-    float inv[2];
+  } else if (e.q_gran == FD_GRAN_BLOCK) {
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const float mx = fmaxf(fmaxf(sh_q[hh * 4], sh_q[hh * 4 + 1]), fmaxf(sh_q[hh * 4 + 2], sh_q[hh * 4 + 3]));
-      if (t128 == 0) e.q_desc[(bh0 + hh) * e.q_desc_stride + chunk] = div_full(mx, qmax) * e.sm_scale_log2e;
-      inv[hh] = div_full(qmax, fmaxf(mx, 1e-12f));
-    }
-#pragma unroll 4
-    for (int j = 0; j < 32; ++j) {
-      const int r = row_of(j);
-      const int64_t n = e.s_off + s0 + r;
+    for (int o = 4; o > 0; o >>= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
+    if (l8 == 0) sh_q[hh * 8 + vw] = bmax;
+    named_bar_sync(QKV_BAR, 128);
+    float mx = sh_q[hh * 8];
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const uint2 u = *reinterpret_cast<const uint2*>(hbuf + r * 512 + ((((hh * 16) + (lane >> 1)) ^ (r & 7)) << 4) +
-                                                         ((lane & 1) << 3));
-        const float y[4] = {bf16_bits_to_f32(u.x & 0xFFFF), bf16_bits_to_f32(u.x >> 16),
-                            bf16_bits_to_f32(u.y & 0xFFFF), bf16_bits_to_f32(u.y >> 16)};
-        *reinterpret_cast<uint32_t*>(e.q_codes + ((bh0 + hh) * e.Nj + n) * 128 + lane * 4) =
-            quant_code<QK>(y[0], inv[hh]) | (quant_code<QK>(y[1], inv[hh]) << 8) |
-            (quant_code<QK>(y[2], inv[hh]) << 16) | (quant_code<QK>(y[3], inv[hh]) << 24);
+    for (int w = 1; w < 8; ++w) mx = fmaxf(mx, sh_q[hh * 8 + w]);
+    if (vw == 0 && l8 == 0) e.q_desc[bh * e.q_desc_stride + chunk] = div_full(mx, qmax) * e.sm_scale_log2e;
+    const float inv = div_full(qmax, fmaxf(mx, 1e-12f));
+#pragma unroll 2
+    for (int i = 0; i < 16; ++i) {
+      const int r = vw + 8 * i;
+      const int64_t obase = (bh * e.Nj + e.s_off + s0 + r) * 128 + 4 * l8;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint2 u = *reinterpret_cast<const uint2*>(haddr(r, q));
+        const float y0 = bf16_bits_to_f32(u.x & 0xFFFF), y1 = bf16_bits_to_f32(u.x >> 16);
+        const float y2 = bf16_bits_to_f32(u.y & 0xFFFF), y3 = bf16_bits_to_f32(u.y >> 16);
+        *reinterpret_cast<uint32_t*>(e.q_codes + obase + 32 * q) = quant_code<QK>(y0, inv) |
+                                                                  (quant_code<QK>(y1, inv) << 8) |
+                                                                  (quant_code<QK>(y2, inv) << 16) |
+                                                                  (quant_code<QK>(y3, inv) << 24);
       }
     }
     named_bar_sync(QKV_BAR, 128);
