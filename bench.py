@@ -1045,6 +1045,37 @@ def run_video_reference(args, world, rank):
     return 0
 
 
+class ExchangeRecorder:
+    """CUDA events around every Ulysses all-to-all (``futudiffu_b200.ulysses``) while
+    active: the exchange's share of a video step and the bytes this rank sends."""
+
+    def __init__(self):
+        from futudiffu_b200 import ulysses as U
+
+        self.U = U
+        self.orig = U.dist.all_to_all_single
+        self.active = False
+        self.events, self.bytes = [], 0
+        U.dist.all_to_all_single = self._a2a
+
+    def _a2a(self, out, inp, *a, **kw):
+        if not self.active:
+            return self.orig(out, inp, *a, **kw)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        r = self.orig(out, inp, *a, **kw)
+        e1.record()
+        self.events.append((e0, e1))
+        self.bytes += inp.numel() * inp.element_size()
+        return r
+
+    def summary(self):
+        return sum(a.elapsed_time(b) for a, b in self.events), len(self.events), self.bytes
+
+    def close(self):
+        self.U.dist.all_to_all_single = self.orig
+
+
 def video_sub_entry(dev, world: int, rank: int, local: int, steps: int = 3, warmup: int = 2) -> dict:
     """Config 5 inside the default line at N >= 2 GPUs: one denoise step of the
     14B-class video DiT with Ulysses sequence parallelism over all ranks (NCCL
@@ -1079,13 +1110,28 @@ def video_sub_entry(dev, world: int, rank: int, local: int, steps: int = 3, warm
         e1.record(stream)
         torch.cuda.synchronize()
     barrier(world)
-    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world, dev)
+    ms_local = e0.elapsed_time(e1) / steps
+    ms = max_over_ranks(ms_local, world, dev)
+    # one more (untimed) step with CUDA events around every all-to-all
+    xr = ExchangeRecorder()
+    xr.active = True
+    x = step(0, x)
+    xr.active = False
+    torch.cuda.synchronize()
+    a2a_ms, n_a2a, a2a_bytes = xr.summary()
+    xr.close()
+    a2a_ms = max_over_ranks(a2a_ms, world, dev)
     check_status()
     del model
     torch.cuda.empty_cache()
     fl = video_flops_per_step(cfg)
     return {"metric": VIDEO_METRIC, "value": 1e3 / ms, "unit": "steps/s", "ms": ms, "steps": steps, "warmup": warmup,
             "parallelism": f"Ulysses sequence parallel x{world} (NCCL all_to_all_single around each self-attention)",
+            "nccl_ranks": world,
+            "all_to_all": {"calls_per_step": n_a2a, "ms_per_step": a2a_ms, "share_of_step": a2a_ms / ms,
+                           "bytes_sent_per_rank": a2a_bytes, "gb_s_per_rank": a2a_bytes / (a2a_ms * 1e6) if a2a_ms else None,
+                           "timed": "CUDA events around each all_to_all_single of one extra step, max over ranks; "
+                                    "Q, K, V cross as bf16, the attention output as 1x128 e4m3 codes + scales"},
             "model_tflops": fl / (ms * 1e-3) / 1e12, "tokens": cfg.tokens, "blocks": cfg.n_blocks,
             "clocks": clocks.summary()}
 
