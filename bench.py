@@ -142,9 +142,14 @@ def dist_setup():
         import torch.distributed as dist
 
         backend = "nccl" if torch.cuda.is_available() else "gloo"
+        opts = None
         if torch.cuda.is_available():
             torch.cuda.set_device(local)
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+            # NCCL kernels on a high-priority stream: the pipelined Ulysses exchange
+            # gets SMs as soon as attention CTAs retire
+            opts = dist.ProcessGroupNCCL.Options()
+            opts.is_high_priority_stream = True
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), pg_options=opts)
     return world, rank, local
 
 
@@ -1058,16 +1063,23 @@ class ExchangeRecorder:
         self.events, self.bytes = [], 0
         U.dist.all_to_all_single = self._a2a
 
+    class _Done:
+        def wait(self):
+            return True
+
     def _a2a(self, out, inp, *a, **kw):
         if not self.active:
             return self.orig(out, inp, *a, **kw)
+        # run each exchange alone (an asynchronous one synchronously) between two events:
+        # its own duration, not the part the pipelined schedule leaves exposed
+        pipelined = kw.pop("async_op", False)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         r = self.orig(out, inp, *a, **kw)
         e1.record()
         self.events.append((e0, e1))
         self.bytes += inp.numel() * inp.element_size()
-        return r
+        return self._Done() if pipelined else r
 
     def summary(self):
         return sum(a.elapsed_time(b) for a, b in self.events), len(self.events), self.bytes
@@ -1121,6 +1133,24 @@ def video_sub_entry(dev, world: int, rank: int, local: int, steps: int = 3, warm
     a2a_ms, n_a2a, a2a_bytes = xr.summary()
     xr.close()
     a2a_ms = max_over_ranks(a2a_ms, world, dev)
+    # the same steps with the exchange pipelined by head groups (the smallest group
+    # count > 1 that divides this rank's heads), for comparison with the default
+    Hp = cfg.heads // world
+    G = next((d for d in range(2, Hp + 1) if Hp % d == 0), None)
+    ms_pipe = None
+    if G is not None:
+        model.head_groups = G
+        x = step(0, x)
+        torch.cuda.synchronize()
+        barrier(world)
+        e0.record(stream)
+        for i in range(steps):
+            x = step(i, x)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        ms_pipe = max_over_ranks(e0.elapsed_time(e1) / steps, world, dev)
+        model.head_groups = 1
     check_status()
     del model
     torch.cuda.empty_cache()
@@ -1130,8 +1160,15 @@ def video_sub_entry(dev, world: int, rank: int, local: int, steps: int = 3, warm
             "nccl_ranks": world,
             "all_to_all": {"calls_per_step": n_a2a, "ms_per_step": a2a_ms, "share_of_step": a2a_ms / ms,
                            "bytes_sent_per_rank": a2a_bytes, "gb_s_per_rank": a2a_bytes / (a2a_ms * 1e6) if a2a_ms else None,
-                           "timed": "CUDA events around each all_to_all_single of one extra step, max over ranks; "
-                                    "Q, K, V cross as bf16, the attention output as 1x128 e4m3 codes + scales"},
+                           "timed": "CUDA events around each all_to_all_single of one extra step, each run alone "
+                                    "(not overlapped), max over ranks; Q, K, V cross as bf16, the attention output "
+                                    "as 1x128 e4m3 codes + scales",
+                           "pipelined": {"head_groups": G, "ms_step": ms_pipe,
+                                         "note": "the same step with heads in G groups: every group's Q/K/V "
+                                                 "exchange queued up front, groups attending alternately on two "
+                                                 "streams while NCCL moves the next group's inputs and the last "
+                                                 "group's output codes; the default step uses one exchange per "
+                                                 "tensor (G = 1)"}},
             "model_tflops": fl / (ms * 1e-3) / 1e12, "tokens": cfg.tokens, "blocks": cfg.n_blocks,
             "clocks": clocks.summary()}
 

@@ -518,8 +518,9 @@ class VideoBlock(nn.Module):
         self.ffn_in = random_fp8_linear(cfg.ffn, D, gen, device)
         self.ffn_out = random_fp8_linear(D, cfg.ffn, gen, device)
 
-    def forward(self, x: Tensor, vec: Tensor, txt: Tensor, freqs: Tensor, group=None) -> Tensor:
-        """x (1, L/P, D) bf16: this rank's tokens; vec (1, D); txt (1, 512, D); freqs (1, L/P, 64, 2, 2)."""
+    def forward(self, x: Tensor, vec: Tensor, txt: Tensor, freqs: Tensor, group=None, head_groups: int = 1) -> Tensor:
+        """x (1, L/P, D) bf16: this rank's tokens; vec (1, D); txt (1, 512, D); freqs (1, L/P, 64, 2, 2);
+        head_groups: how many head groups pipeline the Ulysses exchange with the attention."""
         from .ulysses import ulysses_attention_codes
 
         cfg = self.cfg
@@ -540,7 +541,7 @@ class VideoBlock(nn.Module):
                                    pv_quant=cfg.pv_quant, granularity=cfg.granularity, regions=[(c8, cs)])
             return c8, cs
 
-        o8, o_s = ulysses_attention_codes(q[0], k[0], v[0], attn_codes, group)   # (L/P, D), (L/P, D/128)
+        o8, o_s = ulysses_attention_codes(q[0], k[0], v[0], attn_codes, group, head_groups)  # (L/P, D), (L/P, D/128)
         a = gemm_bf16(o8.view(torch.float8_e4m3fn).unsqueeze(0), o_s.unsqueeze(0), self.proj)
         x = fused_rms_norm_gate_residual(a, self.norm_w[1], m[1], x, cfg.eps)
         # ---- cross-attention to the text (replicated on every rank; 512 keys, bf16 SDPA)
@@ -561,7 +562,9 @@ class VideoBlock(nn.Module):
 class VideoDiT(nn.Module):
     """14B-class video DiT, sequence-parallel over a process group (Ulysses)."""
 
-    def __init__(self, cfg: VideoDiTConfig, seed: int = 0, device="cuda", group=None):
+    def __init__(self, cfg: VideoDiTConfig, seed: int = 0, device="cuda", group=None, head_groups: int = 1):
+        """head_groups > 1 pipelines each Ulysses exchange with the attention by head
+        groups (``ulysses_attention_codes``); the output is the same for every value."""
         super().__init__()
         import torch.distributed as dist
 
@@ -578,6 +581,9 @@ class VideoDiT(nn.Module):
             raise ValueError(f"{cfg.tokens} tokens / {cfg.heads} heads do not split over {P} ranks")
         self.P, self.rank = P, rank
         self.local_tokens = cfg.tokens // P
+        if cfg.heads % (P * head_groups):
+            raise ValueError(f"{cfg.heads} heads do not split into {head_groups} groups over {P} ranks")
+        self.head_groups = head_groups
         self.img_in = nn.Linear(cfg.patch_dim, D, device=dev, dtype=torch.bfloat16)
         self.time_in1 = nn.Linear(cfg.time_dim, D, device=dev, dtype=torch.bfloat16)
         self.time_in2 = nn.Linear(D, D, device=dev, dtype=torch.bfloat16)
@@ -600,7 +606,7 @@ class VideoDiT(nn.Module):
             timestep_embedding(t, cfg.time_dim).to(torch.bfloat16))))
         x = self.img_in(x_local).contiguous()
         for blk in self.blocks:
-            x = blk(x, vec, txt, self.freqs_local, self.group)
+            x = blk(x, vec, txt, self.freqs_local, self.group, self.head_groups)
         scale = self.final_adaln(torch.nn.functional.silu(vec)).contiguous()
         return self.final_out(fused_rms_norm_modulate(x, self.final_norm, scale, cfg.eps))
 

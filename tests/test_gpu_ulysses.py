@@ -59,11 +59,20 @@ def _worker(rank, world, port, out):
         model = VideoDiT(cfg, seed=0, device=dev)
         assert model.P == world
         Ls = model.local_tokens
-        y = model(lat[:, rank * Ls:(rank + 1) * Ls].contiguous().to(dev), txt.to(dev), t)
+        xl = lat[:, rank * Ls:(rank + 1) * Ls].contiguous().to(dev)
+        model.head_groups = 1
+        y = model(xl, txt.to(dev), t)
+        # the pipelined exchange (head groups, async all-to-all) changes which rank
+        # attends which head, not any head's result: bit-identical output
+        same = []
+        for G in (2, 4):
+            model.head_groups = G
+            same.append(torch.equal(model(xl, txt.to(dev), t), y))
         parts = [torch.empty_like(y) for _ in range(world)]
         dist.all_gather(parts, y)
         torch.cuda.synchronize()
         check_status()
+        out[f"groups_equal_{rank}"] = all(same)
         if rank == 0:
             out["sharded"] = torch.cat(parts, 1).cpu()
         del model
@@ -86,6 +95,7 @@ def test_video_dit_two_ranks_equal_one():
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
     mp.start_processes(_worker, args=(2, _free_port(), out), nprocs=2, join=True, start_method="spawn")
+    assert out["groups_equal_0"] and out["groups_equal_1"]
     a, b = out["sharded"].float(), out["single"].float()
     assert torch.isfinite(a).all()
     assert cosine(a, b) >= 0.99999

@@ -72,3 +72,51 @@ def test_ulysses_single_rank_is_plain_attention():
     q, k, v = (torch.randn(3, 7, 8, generator=g) for _ in range(3))
     o = ulysses_attention(q, k, v, _exact)
     assert torch.allclose(o, _exact(q[None], k[None], v[None])[0].transpose(0, 1).reshape(7, 24), atol=1e-6)
+
+
+def _codes_fn(q, k, v):
+    """Stand-in for the attention kernel's quantised output: per-(token, head) scale
+    and uint8 codes, token-major (L, h * D) / (L, h), from exact attention."""
+    o = _exact(q, k, v)[0]                                   # (h, L, D)
+    s = o.abs().amax(-1).clamp_min(1e-6)                     # (h, L)
+    c = ((o / s[..., None]) * 127 + 128).round().clamp(0, 255).to(torch.uint8)
+    return c.transpose(0, 1).reshape(o.shape[1], -1), s.transpose(0, 1).contiguous()
+
+
+def _worker_groups(rank, world, port, H, L, D, groups, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from futudiffu_b200.ulysses import ulysses_attention_codes
+
+        g = torch.Generator().manual_seed(3)
+        q, k, v = (torch.randn(H, L, D, generator=g) for _ in range(3))
+        Ls = L // world
+        sl = slice(rank * Ls, (rank + 1) * Ls)
+        shards = [t[:, sl].contiguous() for t in (q, k, v)]
+        ref_c, ref_s = _codes_fn(q[None], k[None], v[None])
+        ref_c, ref_s = ref_c[sl], ref_s[sl]
+        res = {}
+        for G in (1,) + tuple(groups):
+            c, s = ulysses_attention_codes(*shards, _codes_fn, head_groups=G)
+            res[G] = (torch.equal(c, ref_c), float((s - ref_s).abs().max()))
+        out[rank] = res
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("H,L,groups", [(8, 12, (2, 4)), (12, 10, (2, 3, 6))])
+def test_ulysses_head_group_pipeline_world2(H, L, groups):
+    """The pipelined exchange (head groups, async all-to-all) returns the same codes
+    and scales as the one-shot exchange and as unsharded attention."""
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    mp.start_processes(_worker_groups, args=(2, _free_port(), H, L, 8, groups, out), nprocs=2, join=True,
+                       start_method="spawn")
+    assert len(out) == 2
+    for res in out.values():
+        for G, (codes_equal, scale_err) in res.items():
+            assert codes_equal, G
+            assert scale_err < 1e-6, G
+
