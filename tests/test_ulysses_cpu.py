@@ -1,5 +1,7 @@
-"""Ulysses sequence parallelism on CPU: world_size 2 over gloo, exact attention
-as the per-rank kernel; the sharded result must equal full attention."""
+"""Ulysses sequence parallelism on CPU: world sizes 2 and 4 over gloo, exact
+attention as the per-rank kernel; the sharded result must equal full attention.
+World size 4 with one head per rank and group is the layout of the 14B-class
+video workload at 8 GPUs (40 heads, 5 per rank, 5 head groups)."""
 
 from __future__ import annotations
 
@@ -54,7 +56,7 @@ def _worker(rank, world, port, H, L, D, out):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,H,L", [(2, 4, 12), (2, 6, 10)])
+@pytest.mark.parametrize("world,H,L", [(2, 4, 12), (2, 6, 10), (4, 8, 12)])
 def test_ulysses_attention_world2(world, H, L):
     ctx = mp.get_context("spawn")
     mgr = ctx.Manager()
@@ -106,15 +108,15 @@ def _worker_groups(rank, world, port, H, L, D, groups, out):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("H,L,groups", [(8, 12, (2, 4)), (12, 10, (2, 3, 6))])
-def test_ulysses_head_group_pipeline_world2(H, L, groups):
+@pytest.mark.parametrize("world,H,L,groups", [(2, 8, 12, (2, 4)), (2, 12, 10, (2, 3, 6)), (4, 20, 12, (5,))])
+def test_ulysses_head_group_pipeline_world2(world, H, L, groups):
     """The pipelined exchange (head groups, async all-to-all) returns the same codes
     and scales as the one-shot exchange and as unsharded attention."""
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
-    mp.start_processes(_worker_groups, args=(2, _free_port(), H, L, 8, groups, out), nprocs=2, join=True,
+    mp.start_processes(_worker_groups, args=(world, _free_port(), H, L, 8, groups, out), nprocs=world, join=True,
                        start_method="spawn")
-    assert len(out) == 2
+    assert len(out) == world
     for res in out.values():
         for G, (codes_equal, scale_err) in res.items():
             assert codes_equal, G
