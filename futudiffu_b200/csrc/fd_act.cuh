@@ -43,10 +43,39 @@ FD_DEV float silu_gate(float w1, float w3) {
 }
 
 // GELU, tanh approximation (torch F.gelu(approximate="tanh")):
-// 0.5 a (1 + tanh(sqrt(2/pi) (a + 0.044715 a^3))).
+// 0.5 a (1 + tanh(u)), u = sqrt(2/pi) (a + 0.044715 a^3), evaluated in the
+// logistic form of tanh, 0.5 (1 + tanh u) = 1 / (1 + e^(-2u)):
+//   GELU(a) = a / (1 + 2^z),  z = -2 log2(e) u = a (K1 + K3 a^2),
+// with K1 = -2 sqrt(2/pi) log2(e) and K3 = 0.044715 K1 rounded to f32 once.
+// One ex2.approx and one rcp.approx per value (relative error a few f32 ulp; the
+// denominator is >= 1, so nothing cancels), about a third of the issue slots of
+// an accurate tanhf.  Where 2^z >= 2^26 the factor is flushed to 0: that is
+// where 1 + tanh(u) rounds to exactly 0 in f32 (tanh(u) within half an ulp of
+// -1), so large negative inputs give -0 as the tanh form does.
+constexpr float GELU_K1 = -2.302208198144325f;
+constexpr float GELU_K3 = -0.1029432395800235f;
+
+FD_DEV float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+FD_DEV float gelu_factor(float e) { return e < 67108864.0f ? rcp_approx(__fadd_rn(1.0f, e)) : 0.0f; }
+
 FD_DEV float gelu_tanh(float a) {
-  const float inner = __fmul_rn(0.7978845608028654f, fmaf(__fmul_rn(0.044715f, a), __fmul_rn(a, a), a));
-  return __fmul_rn(__fmul_rn(0.5f, a), __fadd_rn(1.0f, tanhf(inner)));
+  const float z = __fmul_rn(a, fmaf(GELU_K3, __fmul_rn(a, a), GELU_K1));
+  return __fmul_rn(a, gelu_factor(ex2_approx(z)));
+}
+
+// Two values at once on the packed f32x2 pipes; bit for bit gelu_tanh of each
+// (fma.rn / mul.rn .f32x2 round every lane as the scalar instructions do).
+FD_DEV void gelu_tanh2(float& a0, float& a1) {
+  const uint64_t a = pk(a0, a1);
+  float z0, z1;
+  unpk(mul2(a, fma2(pk(GELU_K3, GELU_K3), mul2(a, a), pk(GELU_K1, GELU_K1))), z0, z1);
+  a0 = __fmul_rn(a0, gelu_factor(ex2_approx(z0)));
+  a1 = __fmul_rn(a1, gelu_factor(ex2_approx(z1)));
 }
 
 }  // namespace fd

@@ -136,8 +136,9 @@ FD_DEV uint2 gelu8_codes(const uint4& u, float qm) {
   float g[8];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    g[2 * j] = gelu_tanh(bf16_bits_to_f32(w[j] & 0xffffu));
-    g[2 * j + 1] = gelu_tanh(bf16_bits_to_f32(w[j] >> 16));
+    g[2 * j] = bf16_bits_to_f32(w[j] & 0xffffu);
+    g[2 * j + 1] = bf16_bits_to_f32(w[j] >> 16);
+    gelu_tanh2(g[2 * j], g[2 * j + 1]);
   }
   return make_uint2(quant4(g[0], g[1], g[2], g[3], qm), quant4(g[4], g[5], g[6], g[7], qm));
 }

@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(256) gelu_tanh_quant_kernel(const __nv_bfloat1
     float v[8];
     load8<__nv_bfloat16>(x + g * 128 + sub * 8, v);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = gelu_tanh(v[i]);
+    for (int i = 0; i < 8; i += 2) gelu_tanh2(v[i], v[i + 1]);
     const float amax = half_warp_max(amax8(v));
     const float qm = quant_mult(amax);
     *reinterpret_cast<uint2*>(y + g * 128 + sub * 8) = quant8(v, qm);
