@@ -226,13 +226,18 @@ class DoubleStreamBlock(nn.Module):
         self.img = _Stream(cfg, gen, device)
 
     def forward(self, x_txt: Tensor, x_img: Tensor, vec: Tensor, freqs_txt: Tensor,
-                freqs_img: Tensor) -> tuple[Tensor, Tensor]:
-        """x_* (B, L_*, D) bf16; vec (B, D); freqs_* (B, L_*, 64, 2, 2) fp32 (see batch_freqs)."""
+                freqs_img: Tensor, mods: Tensor | None = None) -> tuple[Tensor, Tensor]:
+        """x_* (B, L_*, D) bf16; vec (B, D); freqs_* (B, L_*, 64, 2, 2) fp32 (see batch_freqs);
+        mods: this block's modulation precomputed as (8, B, D) (text stream's four
+        chunks, then the image stream's; see DiT.modulations), else computed from vec."""
         cfg = self.cfg
         B, Nt = x_txt.shape[0], x_txt.shape[1]
         N = Nt + x_img.shape[1]
         sts, xs = (self.txt, self.img), [x_txt, x_img]
-        mods = [st.modulation(vec) for st in sts]
+        if mods is None:
+            mods = [st.modulation(vec) for st in sts]
+        else:
+            mods = [list(mods[:4]), list(mods[4:])]
 
         def both(lin_of, ins, act=None):
             # the two streams' linears as one grouped GEMM launch (the 512-row text
@@ -292,11 +297,15 @@ class SingleStreamBlock(nn.Module):
         self.linear1 = random_fp8_linear(3 * D + R * D, D, gen, device)
         self.linear2 = random_fp8_linear(D, D + R * D, gen, device)
 
-    def forward(self, x: Tensor, vec: Tensor, freqs: Tensor) -> Tensor:
-        """x (B, L, D) bf16; vec (B, D); freqs (B, L, 64, 2, 2) fp32."""
+    def forward(self, x: Tensor, vec: Tensor, freqs: Tensor, mods: Tensor | None = None) -> Tensor:
+        """x (B, L, D) bf16; vec (B, D); freqs (B, L, 64, 2, 2) fp32; mods: the
+        modulation (scale, gate) precomputed as (2, B, D), else computed from vec."""
         cfg = self.cfg
         B, N, D = x.shape
-        scale, gate = self.adaln(torch.nn.functional.silu(vec)).chunk(2, dim=-1)
+        if mods is None:
+            scale, gate = self.adaln(torch.nn.functional.silu(vec)).chunk(2, dim=-1)
+        else:
+            scale, gate = mods[0], mods[1]
         a8, a_s = fused_rms_norm_modulate_quant(x, self.norm_w[0], scale.contiguous(), cfg.eps)
         w, ws = self.linear1.weight, self.linear1.weight_scale
         n_qkv = 3 * D
@@ -355,6 +364,39 @@ class DiT(nn.Module):
         self.register_buffer("freqs_txt", text_freqs(cfg, dev), persistent=False)
         self.register_buffer("freqs_all", torch.cat([self.freqs_txt, self.freqs_img], dim=0), persistent=False)
         self._freqs_cache: dict[int, tuple[Tensor, Tensor, Tensor]] = {}
+        self._stack_modulation()
+
+    def _stack_modulation(self) -> None:
+        """Every block's adaLN linear as D x D chunks of one (C, D, D) weight stack
+        (and a (C, 1, D) bias stack): chunk order = per double-stream block the text
+        stream's four chunks then the image stream's, then per single-stream block
+        (scale, gate).  The blocks' own adaLN parameters become views of the stacks
+        (same values, no second copy), so ``modulations`` computes all of them with
+        one batched GEMM per forward instead of a SiLU, a GEMV and the chunk copies
+        per block (about 290 small launches of a 57-block step)."""
+        lins = [st.adaln for blk in self.double_blocks for st in (blk.txt, blk.img)]
+        lins += [blk.adaln for blk in self.single_blocks]
+        D = self.cfg.hidden
+        chunks = [lin.weight.shape[0] // D for lin in lins]
+        C = sum(chunks)
+        w = torch.empty(C, D, D, dtype=torch.bfloat16, device=self.freqs_img.device)
+        b = torch.empty(C, 1, D, dtype=torch.bfloat16, device=w.device)
+        c0 = 0
+        with torch.no_grad():
+            for lin, n in zip(lins, chunks):
+                w[c0:c0 + n].copy_(lin.weight.view(n, D, D))
+                b[c0:c0 + n].copy_(lin.bias.view(n, 1, D))
+                lin.weight = nn.Parameter(w[c0:c0 + n].view(n * D, D), requires_grad=False)
+                lin.bias = nn.Parameter(b[c0:c0 + n].view(n * D), requires_grad=False)
+                c0 += n
+        self.mod_w, self.mod_b = w, b
+
+    def modulations(self, vec: Tensor) -> Tensor:
+        """adaLN(SiLU(vec)) of every block at once: (C, B, D) bf16, chunk c of the
+        stacks of ``_stack_modulation`` (one batched GEMM with the bias as its C input)."""
+        C, D = self.mod_w.shape[0], self.cfg.hidden
+        s = torch.nn.functional.silu(vec).unsqueeze(0).expand(C, vec.shape[0], D)
+        return torch.baddbmm(self.mod_b, s, self.mod_w.transpose(1, 2))
 
     @torch.no_grad()
     def forward(self, img: Tensor, txt: Tensor, t: Tensor) -> Tensor:
@@ -368,11 +410,15 @@ class DiT(nn.Module):
         if B not in self._freqs_cache:
             self._freqs_cache[B] = tuple(batch_freqs(f, B) for f in (self.freqs_txt, self.freqs_img, self.freqs_all))
         f_txt, f_img, f_all = self._freqs_cache[B]
+        mods = self.modulations(vec)
+        c = 0
         for blk in self.double_blocks:
-            x_txt, x_img = blk(x_txt, x_img, vec, f_txt, f_img)
+            x_txt, x_img = blk(x_txt, x_img, vec, f_txt, f_img, mods=mods[c:c + 8])
+            c += 8
         x = torch.cat([x_txt, x_img], dim=1)
         for blk in self.single_blocks:
-            x = blk(x, vec, f_all)
+            x = blk(x, vec, f_all, mods=mods[c:c + 2])
+            c += 2
         x_img = x[:, cfg.txt_tokens:].contiguous()
         scale = self.final_adaln(torch.nn.functional.silu(vec)).contiguous()
         h = fused_rms_norm_modulate(x_img, self.final_norm, scale, cfg.eps)
