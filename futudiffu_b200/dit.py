@@ -109,6 +109,14 @@ def _rand(shape, gen, device, std, mean=0.0, dtype=torch.bfloat16) -> Tensor:
     return (torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std + mean).to(dtype)
 
 
+def _f32_norm_copies(m: nn.Module) -> None:
+    """f32 copies of a block's Q/K norm weights, made once: the P3 kernels read f32
+    weights, and handing them the bf16 parameters costs two conversion launches per
+    attention."""
+    m.register_buffer("q_norm32", m.q_norm.detach().float(), persistent=False)
+    m.register_buffer("k_norm32", m.k_norm.detach().float(), persistent=False)
+
+
 def image_freqs(cfg: DiTConfig, device) -> Tensor:
     """2-D RoPE rotations of the image tokens, (img_tokens, head_dim/2, 2, 2) fp32."""
     gh, gw = cfg.img_grid
@@ -206,6 +214,7 @@ class _Stream(nn.Module):
             [nn.Parameter(_rand((D,), gen, device, 0.05, 1.0), requires_grad=False) for _ in range(4)])
         self.q_norm = nn.Parameter(_rand((HEAD_DIM,), gen, device, 0.05, 1.0), requires_grad=False)
         self.k_norm = nn.Parameter(_rand((HEAD_DIM,), gen, device, 0.05, 1.0), requires_grad=False)
+        _f32_norm_copies(self)
         self.qkv = random_fp8_linear(3 * D, D, gen, device)
         self.proj = random_fp8_linear(D, D, gen, device)
         self.mlp_in = random_fp8_linear(cfg.mlp_ratio * D, D, gen, device)
@@ -256,14 +265,14 @@ class DoubleStreamBlock(nn.Module):
         freqs = (freqs_txt, freqs_img)
         if linear_prologue_ok([Nt, N - Nt], cfg.heads):
             # both QKV linears in one launch, P3 and the Q quantisation in its epilogue
-            lin = [(h8, h_s, st.qkv.weight, st.qkv.weight_scale, st.qkv.bias, st.q_norm, st.k_norm, fr, off, cfg.eps)
+            lin = [(h8, h_s, st.qkv.weight, st.qkv.weight_scale, st.qkv.bias, st.q_norm32, st.k_norm32, fr, off, cfg.eps)
                    for st, (h8, h_s), fr, off in zip(sts, hs, freqs, (0, Nt))]
             attn_quant_out_from_linear(lin, cfg.heads, N, None, block_mask=None, qk_quant=cfg.qk_quant,
                                        pv_quant=cfg.pv_quant, granularity=cfg.granularity, regions=codes, split=Nt)
         else:
             qkvs = both(lambda st: st.qkv, hs)
-            streams = [(qkvs[0], self.txt.q_norm, self.txt.k_norm, freqs_txt, 0, cfg.eps),
-                       (qkvs[1], self.img.q_norm, self.img.k_norm, freqs_img, Nt, cfg.eps)]
+            streams = [(qkvs[0], self.txt.q_norm32, self.txt.k_norm32, freqs_txt, 0, cfg.eps),
+                       (qkvs[1], self.img.q_norm32, self.img.k_norm32, freqs_img, Nt, cfg.eps)]
             joint_prologue_attention(streams, cfg, N, codes, split=Nt)
         attn = both(lambda st: st.proj, codes)
         xs = [fused_rms_norm_gate_residual(a, st.norm_w[1], m[1].contiguous(), x, cfg.eps)
@@ -293,6 +302,7 @@ class SingleStreamBlock(nn.Module):
             [nn.Parameter(_rand((D,), gen, device, 0.05, 1.0), requires_grad=False) for _ in range(2)])
         self.q_norm = nn.Parameter(_rand((HEAD_DIM,), gen, device, 0.05, 1.0), requires_grad=False)
         self.k_norm = nn.Parameter(_rand((HEAD_DIM,), gen, device, 0.05, 1.0), requires_grad=False)
+        _f32_norm_copies(self)
         # linear1 rows: [qkv (3D) | mlp_in (R D)]; linear2 columns: [attn (D) | mlp (R D)]
         self.linear1 = random_fp8_linear(3 * D + R * D, D, gen, device)
         self.linear2 = random_fp8_linear(D, D + R * D, gen, device)
@@ -318,12 +328,12 @@ class SingleStreamBlock(nn.Module):
         region = [(cat8[..., :D], cat_s[..., :D // 128])]
         if linear_prologue_ok([N], cfg.heads):
             # the QKV rows of linear1 with P3 and the Q quantisation in the GEMM epilogue
-            lin = [(a8, a_s, w[:n_qkv], ws[: n_qkv // 128], None, self.q_norm, self.k_norm, freqs, 0, cfg.eps)]
+            lin = [(a8, a_s, w[:n_qkv], ws[: n_qkv // 128], None, self.q_norm32, self.k_norm32, freqs, 0, cfg.eps)]
             attn_quant_out_from_linear(lin, cfg.heads, N, None, block_mask=None, qk_quant=cfg.qk_quant,
                                        pv_quant=cfg.pv_quant, granularity=cfg.granularity, regions=region)
         else:
             qkv = fp8_gemm_blockwise(a8, a_s, w[:n_qkv], ws[: n_qkv // 128], output_dtype=torch.bfloat16)
-            joint_prologue_attention([(qkv, self.q_norm, self.k_norm, freqs, 0, cfg.eps)], cfg, N, region)
+            joint_prologue_attention([(qkv, self.q_norm32, self.k_norm32, freqs, 0, cfg.eps)], cfg, N, region)
         y = fp8_gemm_blockwise(cat8, cat_s, self.linear2.weight, self.linear2.weight_scale,
                                output_dtype=torch.bfloat16)
         return fused_rms_norm_gate_residual(y, self.norm_w[1], gate.contiguous(), x, cfg.eps)
@@ -556,6 +566,7 @@ class VideoBlock(nn.Module):
         self.cross_gate = nn.Parameter(_rand((1, D), gen, device, 0.5), requires_grad=False)
         self.q_norm = nn.Parameter(_rand((HEAD_DIM,), gen, device, 0.05, 1.0), requires_grad=False)
         self.k_norm = nn.Parameter(_rand((HEAD_DIM,), gen, device, 0.05, 1.0), requires_grad=False)
+        _f32_norm_copies(self)
         self.qkv = random_fp8_linear(3 * D, D, gen, device)
         self.proj = random_fp8_linear(D, D, gen, device)
         self.cq = random_fp8_linear(D, D, gen, device)
@@ -576,7 +587,7 @@ class VideoBlock(nn.Module):
         # ---- self-attention (Ulysses: sequence -> head all-to-all around the kernel)
         h8, h_s = fused_rms_norm_modulate_quant(x, self.norm_w[0], m[0], cfg.eps)
         qkv = gemm_bf16(h8, h_s, self.qkv)
-        q, k, v = fused_qkv_postprocess(qkv, self.q_norm, self.k_norm, freqs, H, HEAD_DIM, cfg.eps)
+        q, k, v = fused_qkv_postprocess(qkv, self.q_norm32, self.k_norm32, freqs, H, HEAD_DIM, cfg.eps)
 
         def attn_codes(qh, kh, vh):
             # the output projection's 1 x 128 e4m3 input, written by the attention kernel
