@@ -42,6 +42,16 @@ FD_DEV float silu_gate(float w1, float w3) {
   return __fmul_rn(__fmul_rn(w1, sig), w3);
 }
 
+// quant4 with each pair's two multiplies in one packed f32x2 instruction
+// (mul.rn.f32x2 rounds every lane as __fmul_rn does): the same codes.
+FD_DEV uint32_t quant4p(float a, float b, float c, float d, float qm) {
+  const uint64_t q = pk(qm, qm);
+  float a2, b2, c2, d2;
+  unpk(mul2(pk(a, b), q), a2, b2);
+  unpk(mul2(pk(c, d), q), c2, d2);
+  return f32x2_to_e4m3x2(clamp448(a2), clamp448(b2)) | (f32x2_to_e4m3x2(clamp448(c2), clamp448(d2)) << 16);
+}
+
 // GELU, tanh approximation (torch F.gelu(approximate="tanh")):
 // 0.5 a (1 + tanh(u)), u = sqrt(2/pi) (a + 0.044715 a^3), evaluated in the
 // logistic form of tanh, 0.5 (1 + tanh u) = 1 / (1 + e^(-2u)):

@@ -66,6 +66,21 @@ FD_DEV void load8(const void* p, int64_t i, float (&v)[8]) {
   }
 }
 
+// n = (x rrms) w for the eight values of one vector, each pair's multiplies as
+// packed f32x2 instructions (mul.rn.f32x2 rounds every lane as a scalar
+// multiply does, so the products are those of the left-to-right scalar form).
+FD_DEV void normed8(const float (&x)[8], float rrms, const float (&w)[8], float (&n)[8]) {
+  const uint64_t r = pk(rrms, rrms);
+#pragma unroll
+  for (int e = 0; e < 8; e += 2) unpk(mul2(mul2(pk(x[e], x[e + 1]), r), pk(w[e], w[e + 1])), n[e], n[e + 1]);
+}
+
+// o = n f, pairs packed as in normed8.
+FD_DEV void times8(const float (&n)[8], const float (&f)[8], float (&o)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; e += 2) unpk(mul2(pk(n[e], n[e + 1]), pk(f[e], f[e + 1])), o[e], o[e + 1]);
+}
+
 // Max 8192 / (32 lanes * 8) = 32 vectors per lane.
 constexpr int kMaxVecPerLane = 32;
 
@@ -86,7 +101,7 @@ constexpr int kMaxVecPerLane = 32;
 // Registers: the row (NV 16-byte vectors per lane) dominates; rows of up to 3072
 // values (NV <= 12) fit three CTAs per SM, wider rows two.
 template <int MODE, int WDT, int SDT, int NV>
-__global__ void __launch_bounds__(256, (NV <= 12 ? 3 : 2)) rms_row_kernel(const __nv_bfloat16* __restrict__ x,
+__global__ void __launch_bounds__(256, (NV <= 12 && MODE != 2 ? 3 : 2)) rms_row_kernel(const __nv_bfloat16* __restrict__ x,
                                                      const void* __restrict__ w,
                                                      const void* __restrict__ sg,
                                                      const __nv_bfloat16* __restrict__ res,
@@ -168,10 +183,17 @@ __global__ void __launch_bounds__(256, (NV <= 12 ? 3 : 2)) rms_row_kernel(const 
           const float4 wa = w4[0], wb = w4[1], fa = f4[0], fb = f4[1];
           const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
           const float fv[8] = {fa.x, fa.y, fa.z, fa.w, fb.x, fb.y, fb.z, fb.w};
-          float xv[8];
+          float xv[8], nv[8], pv[8];
           unpack_bf16x8(xr[j], xv);
+          normed8(xv, rrms, wv, nv);
+          times8(nv, fv, pv);
+          // bf16 rounding two values per cvt, back to f32 as in unpack_bf16x8
 #pragma unroll
-          for (int e = 0; e < 8; ++e) o[e] = round_to_bf16(((xv[e] * rrms) * wv[e]) * fv[e]);
+          for (int e = 0; e < 8; e += 2) {
+            const uint32_t h = pack_bf16x2(pv[e], pv[e + 1]);
+            o[e] = __uint_as_float(h << 16);
+            o[e + 1] = __uint_as_float(h & 0xFFFF0000u);
+          }
         }
         float amax = 0.f;
 #pragma unroll
@@ -182,7 +204,7 @@ __global__ void __launch_bounds__(256, (NV <= 12 ? 3 : 2)) rms_row_kernel(const 
           const float qm = quant_mult(amax);
           uint8_t* codes = reinterpret_cast<uint8_t*>(out);
           *reinterpret_cast<uint2*>(codes + row * dim + c * 8) =
-              make_uint2(quant4(o[0], o[1], o[2], o[3], qm), quant4(o[4], o[5], o[6], o[7], qm));
+              make_uint2(quant4p(o[0], o[1], o[2], o[3], qm), quant4p(o[4], o[5], o[6], o[7], qm));
           if ((lane & 15) == 0) qs[row * (dim / 128) + c / 16] = dequant_scale(amax);
         }
       } else if (c < nvec) {
@@ -197,11 +219,13 @@ __global__ void __launch_bounds__(256, (NV <= 12 ? 3 : 2)) rms_row_kernel(const 
         const float fv[8] = {fa.x, fa.y, fa.z, fa.w, fb.x, fb.y, fb.z, fb.w};
         float xv[8];
         unpack_bf16x8(xr[j], xv);
+        if constexpr (MODE == 1) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float normed = (xv[e] * rrms) * wv[e];
-          if constexpr (MODE == 1) o[e] = r[e] + fv[e] * normed;
-          else o[e] = normed * fv[e];
+          for (int e = 0; e < 8; ++e) o[e] = r[e] + fv[e] * ((xv[e] * rrms) * wv[e]);
+        } else {
+          float nv[8];
+          normed8(xv, rrms, wv, nv);
+          times8(nv, fv, o);
         }
         reinterpret_cast<uint4*>(out + row * dim)[c] = pack_bf16x8(o);
       }
