@@ -98,8 +98,9 @@ constexpr int kMaxVecPerLane = 32;
 // come from parameter row rparam[b] of scale / gate (n_params rows), so a
 // packed sequence's per-image modulation is applied without materialising a
 // (tokens, dim) tensor.  Ranges or parameter rows out of bounds are skipped.
-// Registers: the row (NV 16-byte vectors per lane) dominates; rows of up to 3072
-// values (NV <= 12) fit three CTAs per SM, wider rows two.
+// Registers: the row (NV 16-byte vectors per lane) dominates; P1 and P2 rows of up
+// to 3072 values (NV <= 12) fit three CTAs per SM, wider rows two; P1 + G1 runs two
+// (at three its register cap of 85 spilled).
 template <int MODE, int WDT, int SDT, int NV>
 __global__ void __launch_bounds__(256, (NV <= 12 && MODE != 2 ? 3 : 2)) rms_row_kernel(const __nv_bfloat16* __restrict__ x,
                                                      const void* __restrict__ w,
