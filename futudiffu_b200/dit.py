@@ -109,12 +109,19 @@ def _rand(shape, gen, device, std, mean=0.0, dtype=torch.bfloat16) -> Tensor:
     return (torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std + mean).to(dtype)
 
 
-def _f32_norm_copies(m: nn.Module) -> None:
-    """f32 copies of a block's Q/K norm weights, made once: the P3 kernels read f32
-    weights, and handing them the bf16 parameters costs two conversion launches per
-    attention."""
-    m.register_buffer("q_norm32", m.q_norm.detach().float(), persistent=False)
-    m.register_buffer("k_norm32", m.k_norm.detach().float(), persistent=False)
+def f32_norms(m: nn.Module) -> tuple[Tensor, Tensor]:
+    """f32 copies of a block's Q/K norm weights for the P3 kernels (which read f32;
+    handing them the bf16 parameters costs two conversion launches per attention).
+    Made on first use and remade only when a parameter changes: the cache key is
+    each parameter's storage address and version counter, so a weight load (in
+    place or by assignment) or a move to another device is picked up."""
+    qn, kn = m.q_norm, m.k_norm
+    key = (qn.data_ptr(), qn._version, kn.data_ptr(), kn._version)
+    cache = m.__dict__.get("_norm32")
+    if cache is None or cache[0] != key:
+        cache = (key, qn.detach().float(), kn.detach().float())
+        m.__dict__["_norm32"] = cache
+    return cache[1], cache[2]
 
 
 def image_freqs(cfg: DiTConfig, device) -> Tensor:
@@ -214,7 +221,6 @@ class _Stream(nn.Module):
             [nn.Parameter(_rand((D,), gen, device, 0.05, 1.0), requires_grad=False) for _ in range(4)])
         self.q_norm = nn.Parameter(_rand((HEAD_DIM,), gen, device, 0.05, 1.0), requires_grad=False)
         self.k_norm = nn.Parameter(_rand((HEAD_DIM,), gen, device, 0.05, 1.0), requires_grad=False)
-        _f32_norm_copies(self)
         self.qkv = random_fp8_linear(3 * D, D, gen, device)
         self.proj = random_fp8_linear(D, D, gen, device)
         self.mlp_in = random_fp8_linear(cfg.mlp_ratio * D, D, gen, device)
@@ -265,14 +271,14 @@ class DoubleStreamBlock(nn.Module):
         freqs = (freqs_txt, freqs_img)
         if linear_prologue_ok([Nt, N - Nt], cfg.heads):
             # both QKV linears in one launch, P3 and the Q quantisation in its epilogue
-            lin = [(h8, h_s, st.qkv.weight, st.qkv.weight_scale, st.qkv.bias, st.q_norm32, st.k_norm32, fr, off, cfg.eps)
+            lin = [(h8, h_s, st.qkv.weight, st.qkv.weight_scale, st.qkv.bias, *f32_norms(st), fr, off, cfg.eps)
                    for st, (h8, h_s), fr, off in zip(sts, hs, freqs, (0, Nt))]
             attn_quant_out_from_linear(lin, cfg.heads, N, None, block_mask=None, qk_quant=cfg.qk_quant,
                                        pv_quant=cfg.pv_quant, granularity=cfg.granularity, regions=codes, split=Nt)
         else:
             qkvs = both(lambda st: st.qkv, hs)
-            streams = [(qkvs[0], self.txt.q_norm32, self.txt.k_norm32, freqs_txt, 0, cfg.eps),
-                       (qkvs[1], self.img.q_norm32, self.img.k_norm32, freqs_img, Nt, cfg.eps)]
+            streams = [(qkvs[0], *f32_norms(self.txt), freqs_txt, 0, cfg.eps),
+                       (qkvs[1], *f32_norms(self.img), freqs_img, Nt, cfg.eps)]
             joint_prologue_attention(streams, cfg, N, codes, split=Nt)
         attn = both(lambda st: st.proj, codes)
         xs = [fused_rms_norm_gate_residual(a, st.norm_w[1], m[1].contiguous(), x, cfg.eps)
@@ -302,7 +308,6 @@ class SingleStreamBlock(nn.Module):
             [nn.Parameter(_rand((D,), gen, device, 0.05, 1.0), requires_grad=False) for _ in range(2)])
         self.q_norm = nn.Parameter(_rand((HEAD_DIM,), gen, device, 0.05, 1.0), requires_grad=False)
         self.k_norm = nn.Parameter(_rand((HEAD_DIM,), gen, device, 0.05, 1.0), requires_grad=False)
-        _f32_norm_copies(self)
         # linear1 rows: [qkv (3D) | mlp_in (R D)]; linear2 columns: [attn (D) | mlp (R D)]
         self.linear1 = random_fp8_linear(3 * D + R * D, D, gen, device)
         self.linear2 = random_fp8_linear(D, D + R * D, gen, device)
@@ -328,12 +333,12 @@ class SingleStreamBlock(nn.Module):
         region = [(cat8[..., :D], cat_s[..., :D // 128])]
         if linear_prologue_ok([N], cfg.heads):
             # the QKV rows of linear1 with P3 and the Q quantisation in the GEMM epilogue
-            lin = [(a8, a_s, w[:n_qkv], ws[: n_qkv // 128], None, self.q_norm32, self.k_norm32, freqs, 0, cfg.eps)]
+            lin = [(a8, a_s, w[:n_qkv], ws[: n_qkv // 128], None, *f32_norms(self), freqs, 0, cfg.eps)]
             attn_quant_out_from_linear(lin, cfg.heads, N, None, block_mask=None, qk_quant=cfg.qk_quant,
                                        pv_quant=cfg.pv_quant, granularity=cfg.granularity, regions=region)
         else:
             qkv = fp8_gemm_blockwise(a8, a_s, w[:n_qkv], ws[: n_qkv // 128], output_dtype=torch.bfloat16)
-            joint_prologue_attention([(qkv, self.q_norm32, self.k_norm32, freqs, 0, cfg.eps)], cfg, N, region)
+            joint_prologue_attention([(qkv, *f32_norms(self), freqs, 0, cfg.eps)], cfg, N, region)
         y = fp8_gemm_blockwise(cat8, cat_s, self.linear2.weight, self.linear2.weight_scale,
                                output_dtype=torch.bfloat16)
         return fused_rms_norm_gate_residual(y, self.norm_w[1], gate.contiguous(), x, cfg.eps)
@@ -383,14 +388,18 @@ class DiT(nn.Module):
         (scale, gate).  The blocks' own adaLN parameters become views of the stacks
         (same values, no second copy), so ``modulations`` computes all of them with
         one batched GEMM per forward instead of a SiLU, a GEMV and the chunk copies
-        per block (about 290 small launches of a 57-block step)."""
+        per block (about 290 small launches of a 57-block step).  Weights loaded in
+        place land in the stacks through the views; parameters that are replaced or
+        moved (``load_state_dict(..., assign=True)``, ``.to()``) no longer view them,
+        which ``modulations`` detects by address and restacks."""
         lins = [st.adaln for blk in self.double_blocks for st in (blk.txt, blk.img)]
         lins += [blk.adaln for blk in self.single_blocks]
         D = self.cfg.hidden
         chunks = [lin.weight.shape[0] // D for lin in lins]
         C = sum(chunks)
-        w = torch.empty(C, D, D, dtype=torch.bfloat16, device=self.freqs_img.device)
-        b = torch.empty(C, 1, D, dtype=torch.bfloat16, device=w.device)
+        dev = lins[0].weight.device if lins else self.freqs_img.device
+        w = torch.empty(C, D, D, dtype=torch.bfloat16, device=dev)
+        b = torch.empty(C, 1, D, dtype=torch.bfloat16, device=dev)
         c0 = 0
         with torch.no_grad():
             for lin, n in zip(lins, chunks):
@@ -400,10 +409,17 @@ class DiT(nn.Module):
                 lin.bias = nn.Parameter(b[c0:c0 + n].view(n * D), requires_grad=False)
                 c0 += n
         self.mod_w, self.mod_b = w, b
+        self._mod_lins = lins
+        self._mod_key = self._modulation_key()
+
+    def _modulation_key(self) -> list[tuple[int, int]]:
+        return [(lin.weight.data_ptr(), lin.bias.data_ptr()) for lin in self._mod_lins]
 
     def modulations(self, vec: Tensor) -> Tensor:
         """adaLN(SiLU(vec)) of every block at once: (C, B, D) bf16, chunk c of the
         stacks of ``_stack_modulation`` (one batched GEMM with the bias as its C input)."""
+        if self._modulation_key() != self._mod_key:
+            self._stack_modulation()
         C, D = self.mod_w.shape[0], self.cfg.hidden
         s = torch.nn.functional.silu(vec).unsqueeze(0).expand(C, vec.shape[0], D)
         return torch.baddbmm(self.mod_b, s, self.mod_w.transpose(1, 2))
@@ -566,7 +582,6 @@ class VideoBlock(nn.Module):
         self.cross_gate = nn.Parameter(_rand((1, D), gen, device, 0.5), requires_grad=False)
         self.q_norm = nn.Parameter(_rand((HEAD_DIM,), gen, device, 0.05, 1.0), requires_grad=False)
         self.k_norm = nn.Parameter(_rand((HEAD_DIM,), gen, device, 0.05, 1.0), requires_grad=False)
-        _f32_norm_copies(self)
         self.qkv = random_fp8_linear(3 * D, D, gen, device)
         self.proj = random_fp8_linear(D, D, gen, device)
         self.cq = random_fp8_linear(D, D, gen, device)
@@ -587,7 +602,7 @@ class VideoBlock(nn.Module):
         # ---- self-attention (Ulysses: sequence -> head all-to-all around the kernel)
         h8, h_s = fused_rms_norm_modulate_quant(x, self.norm_w[0], m[0], cfg.eps)
         qkv = gemm_bf16(h8, h_s, self.qkv)
-        q, k, v = fused_qkv_postprocess(qkv, self.q_norm32, self.k_norm32, freqs, H, HEAD_DIM, cfg.eps)
+        q, k, v = fused_qkv_postprocess(qkv, *f32_norms(self), freqs, H, HEAD_DIM, cfg.eps)
 
         def attn_codes(qh, kh, vh):
             # the output projection's 1 x 128 e4m3 input, written by the attention kernel

@@ -60,8 +60,40 @@ def test_block_adaln_parameters_view_the_stack(monkeypatch):
         assert m.mod_b[0, 0, 5].item() == -3.0
 
 
-def test_f32_norm_copies(monkeypatch):
+def test_modulations_follow_replaced_parameters(monkeypatch):
+    """load_state_dict(assign=True) replaces the adaLN parameters, so they stop
+    viewing the stack: the next modulations() restacks and uses the new weights."""
+    m = _tiny_dit(monkeypatch)
+    vec = torch.randn(2, 256, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16)
+    sd = {k: v.clone() for k, v in m.state_dict().items()}
+    key = "single_blocks.1.adaln.weight"
+    sd[key] = torch.randn(sd[key].shape, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16)
+    m.load_state_dict(sd, strict=False, assign=True)
+    mods = m.modulations(vec)
+    blk = m.single_blocks[1]
+    assert torch.equal(blk.adaln.weight, sd[key])
+    assert blk.adaln.weight.data_ptr() == m.mod_w[16 + 2].data_ptr()   # a view of the new stack
+    for k, ref in enumerate(blk.adaln(torch.nn.functional.silu(vec)).chunk(2, dim=-1)):
+        assert torch.equal(mods[16 + 2 + k], ref)
+    # in place: no restack needed, the views carry the values
+    with torch.no_grad():
+        m.double_blocks[0].img.adaln.bias.add_(1.0)
+    ref = m.double_blocks[0].img.modulation(vec)
+    mods = m.modulations(vec)
+    assert all(torch.equal(mods[4 + k], ref[k]) for k in range(4))
+
+
+def test_f32_norm_copies_follow_the_parameters(monkeypatch):
+    import futudiffu_b200.dit as D
+
     m = _tiny_dit(monkeypatch)
     for st in (m.double_blocks[0].txt, m.double_blocks[1].img, m.single_blocks[2]):
-        assert st.q_norm32.dtype == torch.float32 and torch.equal(st.q_norm32, st.q_norm.float())
-        assert torch.equal(st.k_norm32, st.k_norm.float())
+        q32, k32 = D.f32_norms(st)
+        assert q32.dtype == torch.float32 and torch.equal(q32, st.q_norm.float())
+        assert torch.equal(k32, st.k_norm.float())
+        assert D.f32_norms(st)[0] is q32                     # cached while unchanged
+        with torch.no_grad():
+            st.q_norm.mul_(2.0)                              # in place: version counter moves
+        assert torch.equal(D.f32_norms(st)[0], st.q_norm.float())
+        st.k_norm = torch.nn.Parameter(st.k_norm.detach() + 1, requires_grad=False)   # replaced
+        assert torch.equal(D.f32_norms(st)[1], st.k_norm.float())
